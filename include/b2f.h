@@ -1,0 +1,176 @@
+/*
+ * b2f.h -- C ABI of libb200flash.so, the B200 (sm_100a) kernels behind
+ * MLX-Flash's quantized-weight / quantized-KV-cache hot path.
+ *
+ * Conventions (every entry point):
+ *   - plain device pointers, int64 sizes, and an opaque `stream`
+ *     (a cudaStream_t passed as void*; NULL means the legacy default stream);
+ *   - returns an int status: B2F_OK (0) or a negative B2F_ERR_* code; a CUDA
+ *     launch error is reported as B2F_ERR_CUDA and its cudaError_t text is
+ *     available from b2f_last_error_string();
+ *   - the library never allocates: outputs and workspaces are owned by the
+ *     caller (the Python layer allocates them as torch tensors);
+ *   - entry points are stream-ordered and hold no global mutable state, so
+ *     different threads may drive different streams concurrently.
+ *
+ * Data formats:
+ *   AFFINE (weights): W[rows, K] -> wq uint32[rows, K*bits/32] packed
+ *     least-significant field first (element k at bit bits*(k%(32/bits)) of
+ *     word k/(32/bits)); scales/biases [rows, K/group_size] in the weight dtype;
+ *     w = q*scale + bias.
+ *   KV-SYM (reference KV format, quantized_kv_cache.py:68-234): per row of D
+ *     values, groups of gs=min(group_size,D); scale=absmax/(2^(bits-1)-1) in
+ *     float32; codes offset by max_int into uint8; 4-bit byte = c[2i]<<4|c[2i+1];
+ *     2-bit byte = c0<<6|c1<<4|c2<<2|c3.
+ */
+#ifndef B2F_H_
+#define B2F_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define B2F_OK 0
+#define B2F_ERR_INVALID (-1)      /* bad pointer / shape / stride argument */
+#define B2F_ERR_UNSUPPORTED (-2)  /* bits / group_size / dtype / size not supported */
+#define B2F_ERR_ALIGN (-3)        /* pointer or stride alignment violated */
+#define B2F_ERR_CUDA (-4)         /* CUDA launch/runtime error */
+#define B2F_ERR_TIMEOUT (-5)      /* a bounded device wait gave up */
+#define B2F_ERR_WORKSPACE (-6)    /* workspace missing or too small */
+
+/* element dtypes */
+#define B2F_BF16 0
+#define B2F_F16 1
+#define B2F_F32 2
+
+/* ---- library info --------------------------------------------------- */
+const char* b2f_version(void);
+const char* b2f_status_string(int status);
+/* text of the last CUDA error seen by this thread (or "") */
+const char* b2f_last_error_string(void);
+
+/* ---- (a) affine quantize / (a') dequantize ---------------------------- */
+
+/* mx.quantize(w, group_size, bits) as called through
+ * nn.QuantizedLinear.from_linear (mlx_flash_compress/layer_quantization.py:254)
+ * and nn.quantize (mlx_flash_compress/dflash_model.py:300).
+ * w: [rows, K] of `dtype`; wq: uint32 [rows, K*bits/32]; scales, biases:
+ * [rows, K/group_size] of `dtype`.  bits in {2,4,8}; group_size in {32,64,128}. */
+int b2f_quantize_affine(const void* w, int dtype, int64_t rows, int64_t K, int bits,
+                        int group_size, uint32_t* wq, void* scales, void* biases,
+                        void* stream);
+
+/* mx.dequantize (the unpack restated at mlx_flash_compress/mixed_precision.py:150-171).
+ * If row_index is non-NULL, output row i is source row row_index[i] (an
+ * embedding-style gather); otherwise out_rows must equal the source rows. */
+int b2f_dequantize_affine(const uint32_t* wq, const void* scales, const void* biases,
+                          int dtype, int64_t out_rows, int64_t K, int bits,
+                          int group_size, const int32_t* row_index, void* out,
+                          void* stream);
+
+/* ---- (b) dequant-GEMV, dense ----------------------------------------- */
+
+/* mx.quantized_matmul(x, wq, scales, biases, transpose=True, group_size, bits),
+ * the forward of nn.QuantizedLinear swapped in at layer_quantization.py:254.
+ * x bf16 [M, K] (row stride ldx elements); wq [N, K*bits/32]; scales/biases
+ * bf16 [N, K/group_size]; y bf16 [M, N] (row stride ldy).  If residual is
+ * non-NULL (bf16 [M, N], stride ldy) y = residual + x.W^T.
+ * bits in {4,8}; group_size in {32,64,128}; K % group_size == 0; K <= 64*group_size. */
+int b2f_qgemv_affine(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                     const void* scales, const void* biases, int64_t N, int64_t K,
+                     int bits, int group_size, const void* residual, void* y,
+                     int64_t ldy, void* stream);
+
+/* ---- (b) grouped dequant-GEMV (routed experts) ------------------------ */
+
+/* Workspace bytes needed by b2f_moe_plan for A assignments over E experts
+ * with token tiles of `tile` rows. */
+int64_t b2f_moe_plan_workspace_bytes(int64_t A, int64_t E, int tile);
+
+/* Upper bound on the number of (expert, token-tile) slots the plan can emit. */
+int64_t b2f_moe_plan_max_slots(int64_t A, int64_t E, int tile);
+
+/* Groups the A assignments by expert (counting sort on the GPU) and cuts each
+ * expert's list into tiles of at most `tile` assignments.  expert_of[a] is the
+ * expert of assignment a (the rhs_indices of mx.gather_qmm at
+ * expert_streaming.py:230-241, after the lookup remap at :228).  The plan lives
+ * in `workspace` (b2f_moe_plan_workspace_bytes) and is consumed by
+ * b2f_gather_qgemv_affine.  Out-of-range expert ids make the call fail with
+ * B2F_ERR_INVALID reported through `status_out` (device int32, may be NULL). */
+int b2f_moe_plan(const int32_t* expert_of, int64_t A, int64_t E, int tile,
+                 void* workspace, int64_t workspace_bytes, int32_t* status_out,
+                 void* stream);
+
+/* mx.gather_qmm(x, w, scales, biases, rhs_indices=..., transpose=True,
+ * group_size, bits) -- expert_streaming.py:230-241.
+ * For every assignment a: out[a, :] = x[x_row[a], :] . W[expert_of[a]]^T,
+ * where x_row[a] = x_row_index ? x_row_index[a] : a / x_row_div.
+ * w_gate: stacked [E, N, K*bits/32] (+ scales/biases [E, N, K/gs]).
+ * If w_up is non-NULL the call computes the SwitchGLU front half instead:
+ * out[a, :] = silu(x.Wgate^T) * (x.Wup^T)  (kernels/ops.py:48-108 fused in).
+ * The plan must come from b2f_moe_plan with the same expert_of and `tile`. */
+int b2f_gather_qgemv_affine(const void* x, int64_t ldx, const int32_t* x_row_index,
+                            int64_t x_row_div, int64_t A, int64_t E,
+                            const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                            const uint32_t* w_up, const void* s_up, const void* b_up,
+                            int64_t N, int64_t K, int bits, int group_size, int tile,
+                            const void* plan_workspace, int64_t plan_workspace_bytes,
+                            void* out, int64_t ldo, void* stream);
+
+/* ---- (a-kv) reference KV quantizer ------------------------------------ */
+
+/* Packed bytes per row and groups per row for a last axis of length D. */
+int64_t b2f_kv_packed_len(int64_t D, int bits, int group_size);
+int64_t b2f_kv_num_groups(int64_t D, int group_size);
+
+/* quantize_tensor(x, bits, group_size) -- quantized_kv_cache.py:68-156.
+ * x: [rows, D] of `dtype` (bf16/f16/f32: arithmetic follows the dtype, like
+ * MLX does).  Row r is written to packed row dst_row[r] (or r if dst_row is
+ * NULL) of `packed` (row stride packed_ld bytes) and scales row dst_row[r]
+ * (stride scales_ld floats); zeros (same layout as scales) may be NULL. */
+int b2f_kv_quantize_sym(const void* x, int dtype, int64_t rows, int64_t D, int bits,
+                        int group_size, const int64_t* dst_row, uint8_t* packed,
+                        int64_t packed_ld, float* scales, float* zeros,
+                        int64_t scales_ld, void* stream);
+
+/* dequantize_tensor(...) -- quantized_kv_cache.py:159-234; float32 output
+ * [rows, D].  Row r is read from src_row[r] (or r) of packed/scales. */
+int b2f_kv_dequantize_sym(const uint8_t* packed, int64_t packed_ld, const float* scales,
+                          int64_t scales_ld, const int64_t* src_row, int64_t rows,
+                          int64_t D, int bits, int group_size, float* out, void* stream);
+
+/* ---- (d) paged decode attention over packed K/V ----------------------- */
+
+/* Workspace bytes for b2f_qkv_decode_attn with the given split count. */
+int64_t b2f_qkv_decode_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int n_splits);
+
+/* Decode attention for 1 query token per sequence over a paged KV cache in
+ * the reference KV format (the fp32 SDPA the caller of
+ * quantized_kv_cache.py:311-358 performs, without materialising fp32 K/V).
+ * q: bf16 [B, Hq, D]; out: bf16 [B, Hq, D].
+ * A page holds Hkv*page_size rows of packed_len(D) code bytes (and D/64 f32
+ * scales); the row of (head h, slot s) in page P is
+ *   P*Hkv*page_size + h*head_stride + s*slot_stride,
+ * head-major pages: head_stride=page_size, slot_stride=1
+ * token-major pages (the reference's [S, H, D] chunk order): head_stride=1,
+ * slot_stride=Hkv.
+ * block_table: int32 [B, max_pages]; seq_lens: int32 [B].
+ * Hq % Hkv == 0, Hq/Hkv <= 16; D in {64,128,256}; bits in {4,8}; gs=64 (or D
+ * if D<64); page_size % 16 == 0.  n_splits >= 1 splits each sequence. */
+int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_scales,
+                        const uint8_t* v_pages, const float* v_scales,
+                        const int32_t* block_table, int64_t max_pages,
+                        const int32_t* seq_lens, int64_t B, int64_t Hq, int64_t Hkv,
+                        int64_t D, int64_t page_size, int64_t head_stride,
+                        int64_t slot_stride, int bits, int group_size,
+                        float softmax_scale, int n_splits, void* workspace,
+                        int64_t workspace_bytes, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2F_H_ */

@@ -1,0 +1,218 @@
+"""MLX quantized-array ops with MLX's signatures, on CUDA torch tensors.
+
+These replace the ``mx.*`` calls the reference makes on its hot path:
+
+* ``quantize``          <- ``mx.quantize`` via ``nn.QuantizedLinear.from_linear``
+                           (``mlx_flash_compress/layer_quantization.py:254``)
+* ``dequantize``        <- ``mx.dequantize`` (unpack restated at
+                           ``mlx_flash_compress/mixed_precision.py:150-171``)
+* ``quantized_matmul``  <- the ``nn.QuantizedLinear`` forward
+* ``gather_qmm``        <- ``mx.gather_qmm`` in ``CachedSwitchLinear.__call__``
+                           (``mlx_flash_compress/expert_streaming.py:230-241``)
+
+Format: affine groups along the last axis; ``wq`` uint32 packed least
+significant field first; ``scales``/``biases`` in the weight dtype;
+``w = q*scale + bias``.  Every call runs a libb200flash kernel on the tensors'
+device; CPU tensors are rejected.
+"""
+
+import torch
+
+from . import _capi
+from ._capi import DTYPE_CODES, call, ptr, require_cuda, stream_of
+
+SUPPORTED_BITS = (2, 4, 8)
+MATMUL_BITS = (4, 8)
+GROUP_SIZES = (32, 64, 128)
+
+
+def _check_format(bits, group_size, allowed=SUPPORTED_BITS):
+    if bits not in allowed:
+        raise ValueError(f"bits must be one of {allowed}, got {bits}")
+    if group_size not in GROUP_SIZES:
+        raise ValueError(f"group_size must be one of {GROUP_SIZES}, got {group_size}")
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"):
+    """Affine-quantize ``w[..., K]`` -> ``(wq uint32[..., K*bits/32], scales, biases)``."""
+    if mode != "affine":
+        raise ValueError(f"only mode='affine' is supported, got {mode!r}")
+    _check_format(bits, group_size)
+    if w.dtype not in DTYPE_CODES:
+        raise ValueError(f"unsupported dtype {w.dtype}")
+    if w.dim() < 1 or w.shape[-1] % group_size:
+        raise ValueError(f"last dimension {tuple(w.shape)[-1:]} must be divisible by group_size {group_size}")
+    dev = require_cuda(w)
+    K = w.shape[-1]
+    lead = tuple(w.shape[:-1])
+    rows = w.numel() // K if K else 0
+    wc = _capi.aligned_contiguous(w)
+    wq = torch.empty(*lead, K * bits // 32, dtype=torch.uint32, device=dev)
+    scales = torch.empty(*lead, K // group_size, dtype=w.dtype, device=dev)
+    biases = torch.empty_like(scales)
+    call("b2f_quantize_affine", ptr(wc), DTYPE_CODES[w.dtype], rows, K, bits, group_size, ptr(wq),
+         ptr(scales), ptr(biases), stream_of(dev))
+    return wq, scales, biases
+
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64,
+               bits: int = 4, mode: str = "affine", row_index: torch.Tensor = None) -> torch.Tensor:
+    """Inverse of :func:`quantize`; result dtype is the scales' dtype.
+
+    ``row_index`` (int32, optional) gathers rows (embedding lookup).
+    """
+    if mode != "affine":
+        raise ValueError(f"only mode='affine' is supported, got {mode!r}")
+    _check_format(bits, group_size)
+    if scales.dtype not in DTYPE_CODES:
+        raise ValueError(f"unsupported scale dtype {scales.dtype}")
+    dev = require_cuda(w, scales, biases, row_index)
+    K = w.shape[-1] * 32 // bits
+    if scales.shape[-1] * group_size != K or biases.shape != scales.shape:
+        raise ValueError("scales/biases do not match the packed weight shape")
+    w = w.contiguous()
+    scales = scales.contiguous()
+    biases = biases.contiguous()
+    if row_index is not None:
+        row_index = row_index.to(torch.int32).contiguous()
+        out_lead = tuple(row_index.shape)
+    else:
+        out_lead = tuple(w.shape[:-1])
+    rows = 1
+    for d in out_lead:
+        rows *= d
+    out = torch.empty(*out_lead, K, dtype=scales.dtype, device=dev)
+    call("b2f_dequantize_affine", ptr(w), ptr(scales), ptr(biases), DTYPE_CODES[scales.dtype], rows, K,
+         bits, group_size, ptr(row_index), ptr(out), stream_of(dev))
+    return out
+
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                     transpose: bool = True, group_size: int = 64, bits: int = 4,
+                     mode: str = "affine", residual: torch.Tensor = None) -> torch.Tensor:
+    """``x @ dequantize(w).T`` for ``x[..., K]`` (bf16) -> ``[..., N]`` bf16.
+
+    ``residual`` (optional, ``[..., N]`` bf16) is added in the same kernel.
+    """
+    if not transpose:
+        raise ValueError("only transpose=True is supported on this path")
+    if mode != "affine":
+        raise ValueError(f"only mode='affine' is supported, got {mode!r}")
+    _check_format(bits, group_size, MATMUL_BITS)
+    if x.dtype != torch.bfloat16 or scales.dtype != torch.bfloat16:
+        raise ValueError("quantized_matmul takes bf16 activations and bf16 scales/biases")
+    dev = require_cuda(x, w, scales, biases, residual)
+    N = w.shape[-2]
+    K = w.shape[-1] * 32 // bits
+    if x.shape[-1] != K:
+        raise ValueError(f"x last dim {x.shape[-1]} != K {K}")
+    if w.dim() != 2 or tuple(scales.shape) != (N, K // group_size) or biases.shape != scales.shape:
+        raise ValueError("w must be [N, K*bits/32] with scales/biases [N, K/group_size]")
+    lead = tuple(x.shape[:-1])
+    M = x.numel() // K
+    xc = _capi.aligned_contiguous(x.reshape(M, K))
+    out = torch.empty(*lead, N, dtype=torch.bfloat16, device=dev)
+    res = None
+    if residual is not None:
+        res = residual.reshape(M, N).contiguous()
+    call("b2f_qgemv_affine", ptr(xc), K, M, ptr(w.contiguous()), ptr(scales.contiguous()),
+         ptr(biases.contiguous()), N, K, bits, group_size, ptr(res), ptr(out), N, stream_of(dev))
+    return out
+
+
+def _moe_tile(K, group_size):
+    return 16 if K // group_size <= 32 else 8
+
+
+class MoEPlan:
+    """Device-side grouping of assignments by expert (output of ``b2f_moe_plan``)."""
+
+    def __init__(self, expert_of: torch.Tensor, num_experts: int, tile: int):
+        dev = require_cuda(expert_of)
+        self.expert_of = expert_of.to(torch.int32).contiguous().reshape(-1)
+        self.A = self.expert_of.numel()
+        self.E = int(num_experts)
+        self.tile = int(tile)
+        nbytes = _capi.lib().b2f_moe_plan_workspace_bytes(self.A, self.E, self.tile)
+        self.workspace = torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        call("b2f_moe_plan", ptr(self.expert_of), self.A, self.E, self.tile, ptr(self.workspace),
+             self.workspace.numel(), ptr(self.status), stream_of(dev))
+
+    def check(self):
+        """Synchronising check that every expert id was in range."""
+        rc = int(self.status.item())
+        if rc:
+            raise IndexError("expert index out of range in rhs_indices")
+
+
+def gather_qmv_planned(x_rows: torch.Tensor, plan: MoEPlan, w, scales, biases, group_size, bits,
+                       x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None) -> torch.Tensor:
+    """Grouped GEMV over a prepared plan: ``out[a] = x_rows[row(a)] . W[e(a)]^T``.
+
+    ``up=(w_up, s_up, b_up)`` switches to the fused SwitchGLU front half
+    ``silu(x.Wg^T) * (x.Wu^T)``.
+    """
+    dev = require_cuda(x_rows, w, scales, biases, x_row_index)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    if x_rows.shape[-1] != K:
+        raise ValueError(f"x last dim {x_rows.shape[-1]} != K {K}")
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
+    wu = su = bu = None
+    if up is not None:
+        wu, su, bu = (t.contiguous() for t in up)
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_gather_qgemv_affine", ptr(xc), K, ptr(xri), int(x_row_div), plan.A, E, ptr(w.contiguous()),
+         ptr(scales.contiguous()), ptr(biases.contiguous()), ptr(wu), ptr(su), ptr(bu), N, K, bits,
+         group_size, plan.tile, ptr(plan.workspace), plan.workspace.numel(), ptr(out), N, stream_of(dev))
+    return out
+
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+               lhs_indices: torch.Tensor = None, rhs_indices: torch.Tensor = None, transpose: bool = True,
+               group_size: int = 64, bits: int = 4, mode: str = "affine",
+               sorted_indices: bool = False) -> torch.Tensor:
+    """``mx.gather_qmm``: per batch element ``x[lhs] @ dequantize(w[rhs]).T``.
+
+    ``x``: ``[..., M, K]`` bf16; ``w``: ``[E, N, K*bits/32]``; result
+    ``[*broadcast(batch), M, N]`` bf16.  ``sorted_indices`` is accepted for
+    signature compatibility; the kernel always groups rows by expert itself.
+    """
+    if not transpose:
+        raise ValueError("only transpose=True is supported on this path")
+    if mode != "affine":
+        raise ValueError(f"only mode='affine' is supported, got {mode!r}")
+    _check_format(bits, group_size, MATMUL_BITS)
+    if x.dtype != torch.bfloat16 or scales.dtype != torch.bfloat16:
+        raise ValueError("gather_qmm takes bf16 activations and bf16 scales/biases")
+    dev = require_cuda(x, w, scales, biases, lhs_indices, rhs_indices)
+    if w.dim() != 3:
+        raise ValueError("w must be stacked [E, N, K*bits/32]")
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    if x.dim() < 2 or x.shape[-1] != K:
+        raise ValueError(f"x must be [..., M, {K}]")
+    M = x.shape[-2]
+    xb = tuple(x.shape[:-2])
+    nx = 1
+    for d in xb:
+        nx *= d
+    lhs = (torch.arange(nx, device=dev).reshape(xb) if lhs_indices is None else lhs_indices.to(dev).long())
+    rhs = (torch.arange(E, device=dev) if rhs_indices is None else rhs_indices.to(dev).long())
+    if rhs_indices is None and lhs_indices is None:
+        rhs = rhs.reshape(E, *([1] * 0))
+    lhs_b, rhs_b = torch.broadcast_tensors(lhs, rhs)
+    batch = tuple(lhs_b.shape)
+    lhs_f = lhs_b.reshape(-1)
+    rhs_f = rhs_b.reshape(-1)
+    # assignment a = (batch element, m): x row = lhs*M + m, expert = rhs
+    m_idx = torch.arange(M, device=dev)
+    x_row = (lhs_f[:, None] * M + m_idx[None, :]).reshape(-1).to(torch.int32)
+    expert_of = rhs_f[:, None].expand(-1, M).reshape(-1).to(torch.int32)
+    tile = _moe_tile(K, group_size)
+    plan = MoEPlan(expert_of, E, tile)
+    out = gather_qmv_planned(x.reshape(nx * M, K), plan, w, scales, biases, group_size, bits,
+                             x_row_index=x_row)
+    return out.reshape(*batch, M, N)

@@ -1,0 +1,455 @@
+// (d) paged decode attention that reads the reference KV format directly
+// (uint8 codes + float32 per-64 scales, quantized_kv_cache.py:68-156): one
+// query token per sequence, grouped-query heads sharing each KV head.
+//
+// Layout in HBM (per layer):
+//   K/V codes  uint8 [num_pages][Hkv][page][D*bits/8]   (one reference row per token)
+//   K/V scales f32   [num_pages][Hkv][page][D/64]
+//   block_table int32 [B][max_pages], seq_lens int32 [B]
+// A CTA = (split of the context, kv head, sequence); 4 warps walk 16-token
+// sub-tiles of the split.  Per sub-tile:
+//   S = Q.K^T   warp MMA m16n8k16 (fp16 in, fp32 acc): rows = the G query
+//               heads of this KV head, k = head_dim, n = 8 tokens.  K codes
+//               become fp16 1024+code with one prmt/lop3 per two values;
+//               per 64-wide group: s += kscale*(acc - (1024+max_int)*sum(q))
+//   online softmax in base 2 (q is pre-scaled by softmax_scale*log2(e))
+//   O += P.V    P from the S accumulators (FA2 register reuse), V codes
+//               decoded to fp16 (code-max_int)*vscale in registers.
+// Splits write (m, l, O) partials; a combine kernel merges them.
+#include "common.cuh"
+
+namespace b2f {
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  const uint8_t* kp;
+  const float* ks;
+  const uint8_t* vp;
+  const float* vs;
+  const int32_t* block_table;
+  int64_t max_pages;
+  const int32_t* seq_lens;
+  int B, Hq, Hkv, G, PS, n_splits;
+  int64_t head_stride, slot_stride;  // rows between heads / between slots of a page
+  float qscale;
+  float* o_part;
+  float* ml_part;
+  __nv_bfloat16* out;
+};
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+
+template <int BITS, int D>
+__global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p) {
+  constexpr int DG = D / 64;      // quantization groups per row
+  constexpr int KSTEPS = D / 16;  // MMA k-steps for Q.K^T
+  constexpr int NTD = D / 8;      // 8-wide output column tiles
+  constexpr int RB = D * BITS / 8;
+  constexpr float MI = BITS == 8 ? 127.f : 7.f;
+  constexpr float KOFF = 1024.f + MI;
+  constexpr int KW = BITS == 8 ? 4 : 2;  // K words per thread per group per token
+  constexpr int VW = BITS == 8 ? 2 : 1;  // V words per thread per group per token
+
+  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int G = p.G;
+  const int len = p.seq_lens[b];
+  const int n_sub = (len + 15) / 16;
+  const int per_split = (n_sub + p.n_splits - 1) / p.n_splits;
+  const int sub_begin = split * per_split;
+  const int sub_end = min(n_sub, sub_begin + per_split);
+
+  // ---- Q fragments (fp16, pre-scaled) and per-group sums of q -----------
+  uint32_t qa[KSTEPS][4];
+  float qg[2][DG];
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    const int head = r + 8 * h2;
+    const bool hv = head < G;
+    const __nv_bfloat16* qrow = p.q + (int64_t(b) * p.Hq + int64_t(hkv) * G + head) * D;
+#pragma unroll
+    for (int g = 0; g < DG; ++g) {
+      float v[16];
+      if (hv) {
+        const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * g + 16 * c);
+        const uint4 a = src[0], bb = src[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+          v[2 * i] = round_f16(__low2float(h) * p.qscale);
+          v[2 * i + 1] = round_f16(__high2float(h) * p.qscale);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      }
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) part += v[i];
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      qg[h2][g] = part;
+      if constexpr (BITS == 8) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          qa[g * 4 + s][h2] = pack_f16x2(v[4 * s], v[4 * s + 1]);
+          qa[g * 4 + s][2 + h2] = pack_f16x2(v[4 * s + 2], v[4 * s + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int wi = 0; wi < 2; ++wi) {
+          const int sA = g * 4 + 2 * wi;
+          const float* e = &v[8 * wi];
+          qa[sA][h2] = pack_f16x2(e[0], e[4]);
+          qa[sA][2 + h2] = pack_f16x2(e[1], e[5]);
+          qa[sA + 1][h2] = pack_f16x2(e[2], e[6]);
+          qa[sA + 1][2 + h2] = pack_f16x2(e[3], e[7]);
+        }
+      }
+    }
+  }
+
+  float oacc[NTD][4];
+#pragma unroll
+  for (int j = 0; j < NTD; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oacc[j][i] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+
+  for (int sub = sub_begin + warp; sub < sub_end; sub += 4) {
+    const int t0 = sub * 16;
+    const int page = p.block_table[int64_t(b) * p.max_pages + t0 / p.PS];
+    // row of token t0; token t0+i is at rowbase + i*slot_stride
+    const int64_t rowbase = int64_t(page) * p.Hkv * p.PS + hkv * p.head_stride + (t0 % p.PS) * p.slot_stride;
+    const int64_t ss = p.slot_stride;
+
+    // ---- loads: K for tokens r and 8+r, V for tokens 2c,2c+1,8+2c,9+2c --
+    uint32_t kw[2][DG][KW];
+    float ksc[2][2][DG];
+    uint32_t vw[4][DG][VW];
+    float vsc[4][DG];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const uint8_t* krow = p.kp + (rowbase + (nt * 8 + r) * ss) * RB;
+#pragma unroll
+      for (int g = 0; g < DG; ++g) {
+        if constexpr (BITS == 8) {
+          const uint4 q = *reinterpret_cast<const uint4*>(krow + 64 * g + 16 * c);
+          kw[nt][g][0] = q.x;
+          kw[nt][g][1] = q.y;
+          kw[nt][g][2] = q.z;
+          kw[nt][g][3] = q.w;
+        } else {
+          const uint2 q = *reinterpret_cast<const uint2*>(krow + 32 * g + 8 * c);
+          kw[nt][g][0] = q.x;
+          kw[nt][g][1] = q.y;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tok = nt * 8 + 2 * c + e;
+        const bool tv = t0 + tok < len;
+#pragma unroll
+        for (int g = 0; g < DG; ++g) ksc[nt][e][g] = tv ? p.ks[(rowbase + tok * ss) * DG + g] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int tok = (t >> 1) * 8 + 2 * c + (t & 1);
+      const bool tv = t0 + tok < len;
+      const uint8_t* vrow = p.vp + (rowbase + tok * ss) * RB;
+#pragma unroll
+      for (int g = 0; g < DG; ++g) {
+        if constexpr (BITS == 8) {
+          const uint2 q = *reinterpret_cast<const uint2*>(vrow + 64 * g + 8 * r);
+          vw[t][g][0] = q.x;
+          vw[t][g][1] = q.y;
+        } else {
+          vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vrow + 32 * g + 4 * r);
+        }
+        vsc[t][g] = tv ? p.vs[(rowbase + tok * ss) * DG + g] : 0.f;
+      }
+    }
+
+    // ---- S = Q.K^T -------------------------------------------------------
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      float sacc[DG][4];
+#pragma unroll
+      for (int g = 0; g < DG; ++g) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sacc[g][i] = 0.f;
+        if constexpr (BITS == 8) {
+#pragma unroll
+          for (int st = 0; st < 4; ++st) {
+            const uint32_t w = kw[nt][g][st];
+            const uint32_t bf[2] = {prmt(w, 0x64646464u, 0x4140u), prmt(w, 0x64646464u, 0x4342u)};
+            mma_f16_16816(sacc[g], qa[g * 4 + st], bf);
+          }
+        } else {
+#pragma unroll
+          for (int wi = 0; wi < 2; ++wi) {
+            const uint32_t w = kw[nt][g][wi];
+            const uint32_t e15 = and_or(w, 0x000F000Fu, 0x64006400u);
+            const uint32_t e04 = and_or(w >> 4, 0x000F000Fu, 0x64006400u);
+            const uint32_t e37 = and_or(w >> 8, 0x000F000Fu, 0x64006400u);
+            const uint32_t e26 = and_or(w >> 12, 0x000F000Fu, 0x64006400u);
+            const uint32_t bA[2] = {e04, e15};
+            const uint32_t bB[2] = {e26, e37};
+            mma_f16_16816(sacc[g], qa[g * 4 + 2 * wi], bA);
+            mma_f16_16816(sacc[g], qa[g * 4 + 2 * wi + 1], bB);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = i >> 1, e = i & 1;
+        float v = 0.f;
+#pragma unroll
+        for (int g = 0; g < DG; ++g) v += ksc[nt][e][g] * (sacc[g][i] - KOFF * qg[row][g]);
+        const int tok = nt * 8 + 2 * c + e;
+        s[nt][i] = (t0 + tok < len) ? v : -INFINITY;
+      }
+    }
+
+    // ---- online softmax (rows r and r+8) --------------------------------
+    float pr[2][4];
+#pragma unroll
+    for (int row = 0; row < 2; ++row) {
+      float mt = fmaxf(fmaxf(s[0][2 * row], s[0][2 * row + 1]), fmaxf(s[1][2 * row], s[1][2 * row + 1]));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float mnew = fmaxf(m_run[row], mt);
+      const bool none = (mnew == -INFINITY);
+      const float alpha = none ? 1.f : exp2f(m_run[row] - mnew);
+      float lsum = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float pv = none ? 0.f : exp2f(s[nt][2 * row + e] - mnew);
+          pr[nt][2 * row + e] = pv;
+          lsum += pv;
+        }
+      l_run[row] = l_run[row] * alpha + lsum;
+      m_run[row] = mnew;
+#pragma unroll
+      for (int j = 0; j < NTD; ++j) {
+        oacc[j][2 * row] *= alpha;
+        oacc[j][2 * row + 1] *= alpha;
+      }
+    }
+
+    // ---- O += P.V --------------------------------------------------------
+    const uint32_t pa[4] = {pack_f16x2(pr[0][0], pr[0][1]), pack_f16x2(pr[0][2], pr[0][3]),
+                            pack_f16x2(pr[1][0], pr[1][1]), pack_f16x2(pr[1][2], pr[1][3])};
+    uint32_t vs01[DG], vs23[DG];
+#pragma unroll
+    for (int g = 0; g < DG; ++g) {
+      vs01[g] = pack_f16x2(vsc[0][g], vsc[1][g]);
+      vs23[g] = pack_f16x2(vsc[2][g], vsc[3][g]);
+    }
+    const uint32_t off2 = pack_f16x2(KOFF, KOFF);
+#pragma unroll
+    for (int j = 0; j < NTD; ++j) {
+      const int gj = j >> 3, jj = j & 7;
+      uint32_t x01, x23;
+      if constexpr (BITS == 8) {
+        const int wsel = jj >> 2, k = jj & 3;
+        const uint32_t sel = uint32_t(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
+        x01 = and_or(prmt(vw[0][gj][wsel], vw[1][gj][wsel], sel), 0x00FF00FFu, 0x64006400u);
+        x23 = and_or(prmt(vw[2][gj][wsel], vw[3][gj][wsel], sel), 0x00FF00FFu, 0x64006400u);
+      } else {
+        const int k = jj >> 1;
+        const uint32_t sel = uint32_t(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
+        uint32_t y01 = prmt(vw[0][gj][0], vw[1][gj][0], sel);
+        uint32_t y23 = prmt(vw[2][gj][0], vw[3][gj][0], sel);
+        if ((jj & 1) == 0) {
+          y01 >>= 4;
+          y23 >>= 4;
+        }
+        x01 = and_or(y01, 0x000F000Fu, 0x64006400u);
+        x23 = and_or(y23, 0x000F000Fu, 0x64006400u);
+      }
+      const uint32_t bfr[2] = {hmul2_u(hsub2_u(x01, off2), vs01[gj]), hmul2_u(hsub2_u(x23, off2), vs23[gj])};
+      mma_f16_16816(oacc[j], pa, bfr);
+    }
+  }
+
+  // ---- merge the 4 warps through shared memory -----------------------------
+  extern __shared__ float sm[];
+  float* sm_o = sm;                      // [4][G][D]
+  float* sm_ml = sm + 4 * G * D;         // [4][G][2]
+#pragma unroll
+  for (int row = 0; row < 2; ++row) {
+    float l = l_run[row];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    const int head = r + 8 * row;
+    if (head < G) {
+      if (c == 0) {
+        sm_ml[(warp * G + head) * 2 + 0] = m_run[row];
+        sm_ml[(warp * G + head) * 2 + 1] = l;
+      }
+#pragma unroll
+      for (int j = 0; j < NTD; ++j) {
+        const int gj = j >> 3, jj = j & 7;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int d = 64 * gj + 8 * (2 * c + e) + jj;
+          sm_o[(warp * G + head) * D + d] = oacc[j][2 * row + e];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int hq0 = hkv * G;
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int head = idx / D, d = idx % D;
+    float mstar = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mstar = fmaxf(mstar, sm_ml[(w * G + head) * 2]);
+    float o = 0.f, l = 0.f;
+    if (mstar != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm_ml[(w * G + head) * 2] - mstar);
+        o += f * sm_o[(w * G + head) * D + d];
+        l += f * sm_ml[(w * G + head) * 2 + 1];
+      }
+    }
+    const int64_t bh = int64_t(b) * p.Hq + hq0 + head;
+    if (p.n_splits == 1) {
+      p.out[bh * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+    } else {
+      p.o_part[(bh * p.n_splits + split) * D + d] = o;
+      if (d == 0) {
+        p.ml_part[(bh * p.n_splits + split) * 2 + 0] = mstar;
+        p.ml_part[(bh * p.n_splits + split) * 2 + 1] = l;
+      }
+    }
+  }
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part,
+                                    int n_splits, int D, __nv_bfloat16* __restrict__ out) {
+  const int64_t bh = blockIdx.x;
+  const float* ml = ml_part + bh * n_splits * 2;
+  float mstar = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) mstar = fmaxf(mstar, ml[2 * s]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float o = 0.f, l = 0.f;
+    if (mstar != -INFINITY) {
+      for (int s = 0; s < n_splits; ++s) {
+        const float f = exp2f(ml[2 * s] - mstar);
+        o += f * o_part[(bh * n_splits + s) * D + d];
+        l += f * ml[2 * s + 1];
+      }
+    }
+    out[bh * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+  }
+}
+
+template <int BITS, int D>
+static int launch_attn(const AttnParams& p, cudaStream_t st) {
+  const int smem = (4 * p.G * D + 4 * p.G * 2) * int(sizeof(float));
+  auto kern = qkv_decode_attn_kernel<BITS, D>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return B2F_ERR_CUDA;
+    }
+  }
+  const dim3 grid{unsigned(p.n_splits), unsigned(p.Hkv), unsigned(p.B)};
+  kern<<<grid, 128, smem, st>>>(p);
+  int rc = check_launch();
+  if (rc != B2F_OK || p.n_splits == 1) return rc;
+  attn_combine_kernel<<<unsigned(int64_t(p.B) * p.Hq), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, D, p.out);
+  return check_launch();
+}
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" {
+
+int64_t b2f_qkv_decode_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t D, int n_splits) {
+  if (B <= 0 || Hq <= 0 || D <= 0 || n_splits <= 1) return 0;
+  return B * Hq * n_splits * (D + 2) * int64_t(sizeof(float));
+}
+
+int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_scales,
+                        const uint8_t* v_pages, const float* v_scales, const int32_t* block_table,
+                        int64_t max_pages, const int32_t* seq_lens, int64_t B, int64_t Hq,
+                        int64_t Hkv, int64_t D, int64_t page_size, int64_t head_stride,
+                        int64_t slot_stride, int bits, int group_size, float softmax_scale,
+                        int n_splits, void* workspace, int64_t workspace_bytes, void* out,
+                        void* stream) {
+  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(D == 64 || D == 128 || D == 256) || group_size != 64) return B2F_ERR_UNSUPPORTED;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) return B2F_ERR_INVALID;
+  if (Hq / Hkv > 16) return B2F_ERR_UNSUPPORTED;
+  if (page_size <= 0 || page_size % 16 != 0 || max_pages <= 0 || n_splits < 1) return B2F_ERR_INVALID;
+  // the Hkv*page_size rows of a page must be covered exactly once
+  const bool head_major = head_stride == page_size && slot_stride == 1;
+  const bool token_major = head_stride == 1 && slot_stride == Hkv;
+  if (!head_major && !token_major) return B2F_ERR_INVALID;
+  if (B == 0) return B2F_OK;
+  if (B > 65535 || Hkv > 65535 || n_splits > 65535) return B2F_ERR_UNSUPPORTED;
+  if (!q || !k_pages || !k_scales || !v_pages || !v_scales || !block_table || !seq_lens || !out)
+    return B2F_ERR_INVALID;
+  if (!aligned(q, 16) || !aligned(k_pages, 16) || !aligned(v_pages, 16) || !aligned(k_scales, 4) ||
+      !aligned(v_scales, 4))
+    return B2F_ERR_ALIGN;
+  AttnParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.kp = k_pages;
+  p.ks = k_scales;
+  p.vp = v_pages;
+  p.vs = v_scales;
+  p.block_table = block_table;
+  p.max_pages = max_pages;
+  p.seq_lens = seq_lens;
+  p.B = int(B);
+  p.Hq = int(Hq);
+  p.Hkv = int(Hkv);
+  p.G = int(Hq / Hkv);
+  p.PS = int(page_size);
+  p.head_stride = head_stride;
+  p.slot_stride = slot_stride;
+  p.n_splits = n_splits;
+  p.qscale = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  if (n_splits > 1) {
+    const int64_t need = b2f_qkv_decode_attn_workspace_bytes(B, Hq, D, n_splits);
+    if (!workspace || workspace_bytes < need) return B2F_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return B2F_ERR_ALIGN;
+    p.o_part = static_cast<float*>(workspace);
+    p.ml_part = p.o_part + B * Hq * n_splits * D;
+  }
+  cudaStream_t st = as_stream(stream);
+  if (bits == 8) {
+    if (D == 64) return launch_attn<8, 64>(p, st);
+    if (D == 128) return launch_attn<8, 128>(p, st);
+    return launch_attn<8, 256>(p, st);
+  }
+  if (D == 64) return launch_attn<4, 64>(p, st);
+  if (D == 128) return launch_attn<4, 128>(p, st);
+  return launch_attn<4, 256>(p, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,434 @@
+// (a) affine group quantizer/packer, (a') unpacker, (a-kv) reference-format
+// symmetric KV quantizer and dequantizer.  All HBM-bound byte/integer work:
+// one pass over the input, 16-byte vector loads, warp-shuffle group reductions.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace b2f {
+
+static thread_local std::string g_last_error;
+void set_last_cuda_error(cudaError_t e) { g_last_error = cudaGetErrorString(e); }
+
+// ------------------------------------------------------------------------
+// (a) affine quantize.  One thread owns EPT consecutive elements of one
+// group; TPG = GS/EPT neighbouring lanes reduce min/max with shuffles.
+// Rounding follows oracle/affine.py: range = max-min (f32), scale =
+// round_T(range / n_bins), q = clip(rint((w - min) / scale), 0, n_bins),
+// q = 0 for a group whose rounded scale is 0.
+// ------------------------------------------------------------------------
+template <class Tag, int BITS, int GS>
+__global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag::T* __restrict__ w,
+                                                              int64_t n_threads,
+                                                              uint32_t* __restrict__ wq,
+                                                              typename Tag::T* __restrict__ scales,
+                                                              typename Tag::T* __restrict__ biases) {
+  using T = typename Tag::T;
+  constexpr int EPT = (BITS == 2) ? 16 : 8;
+  constexpr int TPG = GS / EPT;
+  constexpr int WPT = EPT * BITS / 32;
+  constexpr int PER = 32 / BITS;
+  constexpr float NBINS = float((1 << BITS) - 1);
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t iters = (n_threads + stride - 1) / stride;
+  int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t it = 0; it < iters; ++it, t += stride) {
+    const bool valid = t < n_threads;
+    float v[EPT];
+    if (valid) {
+      const T* src = w + t * EPT;
+      constexpr int VEC = (EPT * int(sizeof(T))) / 16;
+      uint4 raw[VEC];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) raw[i] = reinterpret_cast<const uint4*>(src)[i];
+      const T* vals = reinterpret_cast<const T*>(raw);
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) v[i] = Tag::to_f(vals[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPT; ++i) v[i] = 0.f;
+    }
+    float mx = v[0], mn = v[0];
+#pragma unroll
+    for (int i = 1; i < EPT; ++i) {
+      mx = fmaxf(mx, v[i]);
+      mn = fminf(mn, v[i]);
+    }
+    mx = warp_max<TPG>(mx);
+    mn = warp_min<TPG>(mn);
+    const float scale = Tag::round(__fdiv_rn(__fsub_rn(mx, mn), NBINS));
+    uint32_t words[WPT];
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) words[j] = 0u;
+#pragma unroll
+    for (int i = 0; i < EPT; ++i) {
+      uint32_t q = 0u;
+      if (scale != 0.f) {
+        float r = rintf(__fdiv_rn(__fsub_rn(v[i], mn), scale));
+        r = fminf(fmaxf(r, 0.f), NBINS);
+        q = uint32_t(r);
+      }
+      words[i / PER] |= q << (BITS * (i % PER));
+    }
+    if (valid) {
+      uint32_t* dst = wq + t * WPT;
+      if constexpr (WPT == 2) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
+      } else {
+        dst[0] = words[0];
+      }
+      if ((threadIdx.x % TPG) == 0) {
+        const int64_t g = (t * EPT) / GS;
+        scales[g] = Tag::from_f(scale);
+        biases[g] = Tag::from_f(mn);
+      }
+    }
+  }
+}
+
+template <class Tag, int BITS>
+static int launch_quantize_bits(const void* w, int64_t rows, int64_t K, int gs, uint32_t* wq,
+                                void* s, void* b, cudaStream_t st) {
+  using T = typename Tag::T;
+  constexpr int EPT = (BITS == 2) ? 16 : 8;
+  const int64_t n_threads = rows * K / EPT;
+  if (n_threads == 0) return B2F_OK;
+  const int block = 256;
+  int64_t grid = (n_threads + block - 1) / block;
+  if (grid > 148 * 64) grid = 148 * 64;
+  auto W = static_cast<const T*>(w);
+  auto S = static_cast<T*>(s);
+  auto Bi = static_cast<T*>(b);
+  switch (gs) {
+    case 32:
+      quantize_affine_kernel<Tag, BITS, 32><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      break;
+    case 64:
+      quantize_affine_kernel<Tag, BITS, 64><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      break;
+    case 128:
+      quantize_affine_kernel<Tag, BITS, 128><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      break;
+    default:
+      return B2F_ERR_UNSUPPORTED;
+  }
+  return check_launch();
+}
+
+template <class Tag>
+static int launch_quantize(const void* w, int64_t rows, int64_t K, int bits, int gs, uint32_t* wq,
+                           void* s, void* b, cudaStream_t st) {
+  switch (bits) {
+    case 2: return launch_quantize_bits<Tag, 2>(w, rows, K, gs, wq, s, b, st);
+    case 4: return launch_quantize_bits<Tag, 4>(w, rows, K, gs, wq, s, b, st);
+    case 8: return launch_quantize_bits<Tag, 8>(w, rows, K, gs, wq, s, b, st);
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+}
+
+// ------------------------------------------------------------------------
+// (a') affine dequantize: one thread per packed word; optional row gather.
+// w = round_T(q*scale + bias) with an f32 multiply then an f32 add.
+// ------------------------------------------------------------------------
+template <class Tag, int BITS>
+__global__ void __launch_bounds__(256) dequantize_affine_kernel(
+    const uint32_t* __restrict__ wq, const typename Tag::T* __restrict__ scales,
+    const typename Tag::T* __restrict__ biases, int64_t out_rows, int64_t K, int gs,
+    const int32_t* __restrict__ row_index, typename Tag::T* __restrict__ out) {
+  using T = typename Tag::T;
+  constexpr int PER = 32 / BITS;
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
+  const int64_t wpr = K / PER;
+  const int64_t n = out_rows * wpr;
+  const int64_t groups = K / gs;
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = t / wpr, j = t - r * wpr;
+    const int64_t src = row_index ? int64_t(row_index[r]) : r;
+    const uint32_t word = wq[src * wpr + j];
+    const int64_t g = (j * PER) / gs;
+    const float s = Tag::to_f(scales[src * groups + g]);
+    const float b = Tag::to_f(biases[src * groups + g]);
+    T vals[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const float q = float((word >> (BITS * i)) & MASK);
+      vals[i] = Tag::from_f(__fadd_rn(__fmul_rn(q, s), b));
+    }
+    T* dst = out + r * K + j * PER;
+    constexpr int BYTES = PER * int(sizeof(T));
+    if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+      for (int i = 0; i < BYTES / 16; ++i)
+        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(vals)[i];
+    } else if constexpr (BYTES == 8) {
+      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(vals);
+    } else {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) dst[i] = vals[i];
+    }
+  }
+}
+
+template <class Tag>
+static int launch_dequantize(const uint32_t* wq, const void* s, const void* b, int64_t rows,
+                             int64_t K, int bits, int gs, const int32_t* ridx, void* out,
+                             cudaStream_t st) {
+  using T = typename Tag::T;
+  const int64_t n = rows * K * bits / 32;
+  if (n == 0) return B2F_OK;
+  const int block = 256;
+  int64_t grid = (n + block - 1) / block;
+  if (grid > 148 * 64) grid = 148 * 64;
+  auto S = static_cast<const T*>(s);
+  auto Bi = static_cast<const T*>(b);
+  auto O = static_cast<T*>(out);
+  switch (bits) {
+    case 2: dequantize_affine_kernel<Tag, 2><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
+    case 4: dequantize_affine_kernel<Tag, 4><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
+    case 8: dequantize_affine_kernel<Tag, 8><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+  return check_launch();
+}
+
+// ------------------------------------------------------------------------
+// (a-kv) reference KV quantizer.  One warp per row: per group an absmax
+// shuffle reduction, then the codes go to a per-warp shared buffer, then the
+// bytes are packed (high nibble first / MSB crumb first).  Each arithmetic
+// step rounds into the input dtype exactly like the reference's MLX ops.
+// ------------------------------------------------------------------------
+struct KvGeom {
+  int64_t D, dp, ng, pl;
+  int gs, bits, max_int;
+};
+
+static KvGeom kv_geom(int64_t D, int bits, int group_size) {
+  KvGeom g;
+  g.D = D;
+  g.gs = int(D < group_size ? D : group_size);
+  g.dp = (D % g.gs == 0) ? D : D + g.gs - D % g.gs;
+  g.ng = g.dp / g.gs;
+  g.pl = bits == 8 ? g.dp : (bits == 4 ? (g.dp + 1) / 2 : (g.dp + 3) / 4);
+  g.bits = bits;
+  g.max_int = (1 << (bits - 1)) - 1;
+  return g;
+}
+
+template <class Tag>
+__global__ void kv_quantize_kernel(const typename Tag::T* __restrict__ x, int64_t rows, KvGeom g,
+                                   const int64_t* __restrict__ dst_row, uint8_t* __restrict__ packed,
+                                   int64_t packed_ld, float* __restrict__ scales,
+                                   float* __restrict__ zeros, int64_t scales_ld) {
+  extern __shared__ uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int wpb = blockDim.x >> 5;
+  const int64_t buf_bytes = (g.dp + 15) & ~int64_t(15);
+  uint8_t* codes = smem + warp * buf_bytes;
+  const float mi = float(g.max_int);
+  for (int64_t row = int64_t(blockIdx.x) * wpb + warp; row < rows; row += int64_t(gridDim.x) * wpb) {
+    const typename Tag::T* xr = x + row * g.D;
+    const int64_t orow = dst_row ? dst_row[row] : row;
+    for (int64_t grp = 0; grp < g.ng; ++grp) {
+      const int64_t base = grp * g.gs;
+      float m = 0.f;
+      for (int j = lane; j < g.gs; j += 32) {
+        const int64_t e = base + j;
+        const float v = e < g.D ? Tag::to_f(xr[e]) : 0.f;
+        m = fmaxf(m, fabsf(v));
+      }
+      m = warp_max<32>(m);
+      float scale = Tag::round(__fdiv_rn(m, mi));
+      if (scale == 0.f) scale = 1.f;
+      for (int j = lane; j < g.gs; j += 32) {
+        const int64_t e = base + j;
+        const float v = e < g.D ? Tag::to_f(xr[e]) : 0.f;
+        float xs = Tag::round(__fdiv_rn(v, scale));
+        float xq = Tag::round(rintf(xs));
+        xq = fminf(fmaxf(xq, -mi), mi);
+        codes[e] = uint8_t(int(Tag::round(xq + mi)));
+      }
+      if (lane == 0) {
+        scales[orow * scales_ld + grp] = scale;
+        if (zeros) zeros[orow * scales_ld + grp] = 0.f;
+      }
+    }
+    __syncwarp();
+    uint8_t* pr = packed + orow * packed_ld;
+    for (int64_t ob = lane; ob < g.pl; ob += 32) {
+      uint8_t byte;
+      if (g.bits == 8) {
+        byte = codes[ob];
+      } else if (g.bits == 4) {
+        const int64_t e = 2 * ob;
+        const uint8_t c0 = codes[e];
+        const uint8_t c1 = (e + 1 < g.dp) ? codes[e + 1] : 0;
+        byte = uint8_t((c0 << 4) | (c1 & 0x0F));
+      } else {
+        const int64_t e = 4 * ob;
+        uint8_t c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = (e + i < g.dp) ? codes[e + i] : 0;
+        byte = uint8_t((c[0] << 6) | ((c[1] & 3) << 4) | ((c[2] & 3) << 2) | (c[3] & 3));
+      }
+      pr[ob] = byte;
+    }
+    __syncwarp();
+  }
+}
+
+__global__ void kv_dequantize_kernel(const uint8_t* __restrict__ packed, int64_t packed_ld,
+                                     const float* __restrict__ scales, int64_t scales_ld,
+                                     const int64_t* __restrict__ src_row, int64_t rows, KvGeom g,
+                                     float* __restrict__ out) {
+  const int64_t n = rows * g.D;
+  const float mi = float(g.max_int);
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
+       t += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = t / g.D, j = t - r * g.D;
+    const int64_t sr = src_row ? src_row[r] : r;
+    const uint8_t* pr = packed + sr * packed_ld;
+    uint32_t code;
+    if (g.bits == 8) {
+      code = pr[j];
+    } else if (g.bits == 4) {
+      const uint8_t b = pr[j >> 1];
+      code = (j & 1) ? (b & 0x0F) : (b >> 4);
+    } else {
+      const uint8_t b = pr[j >> 2];
+      code = (b >> (6 - 2 * (j & 3))) & 3u;
+    }
+    out[t] = __fmul_rn(float(code) - mi, scales[sr * scales_ld + j / g.gs]);
+  }
+}
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" {
+
+const char* b2f_version(void) { return "b200flash 0.1.0 (sm_100a)"; }
+
+const char* b2f_status_string(int s) {
+  switch (s) {
+    case B2F_OK: return "ok";
+    case B2F_ERR_INVALID: return "invalid argument";
+    case B2F_ERR_UNSUPPORTED: return "unsupported bits/group_size/dtype/size";
+    case B2F_ERR_ALIGN: return "misaligned pointer or stride";
+    case B2F_ERR_CUDA: return "CUDA error";
+    case B2F_ERR_TIMEOUT: return "device wait timed out";
+    case B2F_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown status";
+  }
+}
+
+const char* b2f_last_error_string(void) { return g_last_error.c_str(); }
+
+int b2f_quantize_affine(const void* w, int dtype, int64_t rows, int64_t K, int bits,
+                        int group_size, uint32_t* wq, void* scales, void* biases, void* stream) {
+  if (rows < 0 || K < 0) return B2F_ERR_INVALID;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(group_size == 32 || group_size == 64 || group_size == 128)) return B2F_ERR_UNSUPPORTED;
+  if (K % group_size != 0) return B2F_ERR_INVALID;
+  if (rows * K == 0) return B2F_OK;
+  if (!w || !wq || !scales || !biases) return B2F_ERR_INVALID;
+  if (!aligned(w, 16) || !aligned(wq, 8)) return B2F_ERR_ALIGN;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case B2F_BF16: return launch_quantize<TagBF16>(w, rows, K, bits, group_size, wq, scales, biases, st);
+    case B2F_F16: return launch_quantize<TagF16>(w, rows, K, bits, group_size, wq, scales, biases, st);
+    case B2F_F32: return launch_quantize<TagF32>(w, rows, K, bits, group_size, wq, scales, biases, st);
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+}
+
+int b2f_dequantize_affine(const uint32_t* wq, const void* scales, const void* biases, int dtype,
+                          int64_t out_rows, int64_t K, int bits, int group_size,
+                          const int32_t* row_index, void* out, void* stream) {
+  if (out_rows < 0 || K < 0) return B2F_ERR_INVALID;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(group_size == 32 || group_size == 64 || group_size == 128)) return B2F_ERR_UNSUPPORTED;
+  if (K % group_size != 0) return B2F_ERR_INVALID;
+  if (out_rows * K == 0) return B2F_OK;
+  if (!wq || !scales || !biases || !out) return B2F_ERR_INVALID;
+  if (!aligned(out, 16)) return B2F_ERR_ALIGN;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case B2F_BF16: return launch_dequantize<TagBF16>(wq, scales, biases, out_rows, K, bits, group_size, row_index, out, st);
+    case B2F_F16: return launch_dequantize<TagF16>(wq, scales, biases, out_rows, K, bits, group_size, row_index, out, st);
+    case B2F_F32: return launch_dequantize<TagF32>(wq, scales, biases, out_rows, K, bits, group_size, row_index, out, st);
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+}
+
+int64_t b2f_kv_packed_len(int64_t D, int bits, int group_size) {
+  if (D <= 0 || group_size <= 0 || !(bits == 2 || bits == 4 || bits == 8)) return 0;
+  return kv_geom(D, bits, group_size).pl;
+}
+
+int64_t b2f_kv_num_groups(int64_t D, int group_size) {
+  if (D <= 0 || group_size <= 0) return 0;
+  return kv_geom(D, 8, group_size).ng;
+}
+
+int b2f_kv_quantize_sym(const void* x, int dtype, int64_t rows, int64_t D, int bits,
+                        int group_size, const int64_t* dst_row, uint8_t* packed,
+                        int64_t packed_ld, float* scales, float* zeros, int64_t scales_ld,
+                        void* stream) {
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (group_size <= 0 || rows < 0 || D < 0) return B2F_ERR_INVALID;
+  if (rows == 0 || D == 0) return B2F_OK;
+  if (!x || !packed || !scales) return B2F_ERR_INVALID;
+  KvGeom g = kv_geom(D, bits, group_size);
+  if (packed_ld < g.pl || scales_ld < g.ng) return B2F_ERR_INVALID;
+  const int64_t buf = (g.dp + 15) & ~int64_t(15);
+  if (buf > 200 * 1024) return B2F_ERR_UNSUPPORTED;
+  int wpb = int(buf <= 48 * 1024 / 8 ? 8 : (48 * 1024 / buf > 0 ? 48 * 1024 / buf : 1));
+  const int64_t smem = buf * wpb;
+  int64_t grid = (rows + wpb - 1) / wpb;
+  if (grid > 148 * 32) grid = 148 * 32;
+  cudaStream_t st = as_stream(stream);
+  auto launch = [&](auto tag) -> int {
+    using Tag = decltype(tag);
+    if (smem > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kv_quantize_kernel<Tag>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return B2F_ERR_CUDA;
+      }
+    }
+    kv_quantize_kernel<Tag><<<grid, wpb * 32, smem, st>>>(
+        static_cast<const typename Tag::T*>(x), rows, g, dst_row, packed, packed_ld, scales, zeros,
+        scales_ld);
+    return check_launch();
+  };
+  switch (dtype) {
+    case B2F_BF16: return launch(TagBF16{});
+    case B2F_F16: return launch(TagF16{});
+    case B2F_F32: return launch(TagF32{});
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+}
+
+int b2f_kv_dequantize_sym(const uint8_t* packed, int64_t packed_ld, const float* scales,
+                          int64_t scales_ld, const int64_t* src_row, int64_t rows, int64_t D,
+                          int bits, int group_size, float* out, void* stream) {
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (group_size <= 0 || rows < 0 || D < 0) return B2F_ERR_INVALID;
+  if (rows == 0 || D == 0) return B2F_OK;
+  if (!packed || !scales || !out) return B2F_ERR_INVALID;
+  KvGeom g = kv_geom(D, bits, group_size);
+  if (packed_ld < g.pl || scales_ld < g.ng) return B2F_ERR_INVALID;
+  const int64_t n = rows * D;
+  int64_t grid = (n + 255) / 256;
+  if (grid > 148 * 64) grid = 148 * 64;
+  kv_dequantize_kernel<<<grid, 256, 0, as_stream(stream)>>>(packed, packed_ld, scales, scales_ld,
+                                                            src_row, rows, g, out);
+  return check_launch();
+}
+
+}  // extern "C"

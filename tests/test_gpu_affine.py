@@ -1,0 +1,102 @@
+"""GPU parity: affine quantize / dequantize / quantized_matmul vs the oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from b200flash import mx_compat
+from oracle import affine
+from oracle.fp import round_to
+
+from helpers import assert_close, to_dev, to_np, u32_to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def test_quantize_matches_golden_bit_exact(golden, dev):
+    z = golden("affine.npz")
+    for bits in (2, 4, 8):
+        for gs in (32, 64, 128):
+            k = f"b{bits}_g{gs}"
+            wq, s, b = mx_compat.quantize(to_dev(z[f"{k}/w"], "bf16", dev), gs, bits)
+            assert wq.dtype == torch.uint32
+            assert np.array_equal(to_np(wq), z[f"{k}/wq"]), k
+            assert np.array_equal(to_np(s), z[f"{k}/scales"]), k
+            assert np.array_equal(to_np(b), z[f"{k}/biases"]), k
+            d = mx_compat.dequantize(wq, s, b, gs, bits)
+            assert np.array_equal(to_np(d), z[f"{k}/deq"]), k
+    for dt in ("f16", "f32"):
+        wq, s, b = mx_compat.quantize(to_dev(z[f"{dt}/w"], dt, dev), 64, 4)
+        assert np.array_equal(to_np(wq), z[f"{dt}/wq"]) and np.array_equal(to_np(s), z[f"{dt}/scales"])
+        assert np.array_equal(to_np(mx_compat.dequantize(wq, s, b, 64, 4)), z[f"{dt}/deq"])
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantize_config1_full_size_bit_exact(dev, bits):
+    """W[4096, 4096] ~ N(0, 0.02) bf16, group 64: packed words, scales, biases bit-exact."""
+    rng = np.random.default_rng(0)
+    w = round_to(rng.normal(0, 0.02, (4096, 4096)).astype(np.float32), "bf16")
+    wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits)
+    owq, os_, ob = affine.quantize(w, 64, bits)
+    assert np.array_equal(to_np(wq), owq)
+    assert np.array_equal(to_np(s), os_) and np.array_equal(to_np(b), ob)
+    d = to_np(mx_compat.dequantize(wq, s, b, 64, bits))
+    assert np.array_equal(d, affine.dequantize(owq, os_, ob, 64, bits))
+
+
+def test_quantize_edge_groups(dev):
+    w = np.zeros((4, 128), np.float32)
+    w[1] = 3.0                      # constant group
+    w[2, :64] = np.linspace(-1, 1, 64)
+    w[3] = round_to(np.float32(1e-30) * np.arange(128), "bf16")  # tiny range
+    w = round_to(w, "bf16")
+    for bits in (2, 4, 8):
+        wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits)
+        owq, os_, ob = affine.quantize(w, 64, bits)
+        assert np.array_equal(to_np(wq), owq) and np.array_equal(to_np(s), os_) and np.array_equal(to_np(b), ob)
+
+
+def test_dequantize_row_gather(dev):
+    rng = np.random.default_rng(3)
+    w = round_to(rng.normal(0, 0.02, (64, 256)).astype(np.float32), "bf16")
+    wq, s, b = affine.quantize(w, 64, 4)
+    idx = np.array([5, 0, 63, 5, 17], np.int32)
+    out = mx_compat.dequantize(u32_to_dev(wq, dev), to_dev(s, "bf16", dev), to_dev(b, "bf16", dev), 64, 4,
+                               row_index=torch.from_numpy(idx).to(dev))
+    assert np.array_equal(to_np(out), affine.dequantize(wq[idx], s[idx], b[idx], 64, 4))
+
+
+def _qmm_case(dev, M, N, K, bits, gs, seed=0, resid=False):
+    rng = np.random.default_rng(seed)
+    w = round_to(rng.normal(0, 0.02, (N, K)).astype(np.float32), "bf16")
+    x = round_to(rng.standard_normal((M, K)).astype(np.float32), "bf16")
+    wq, s, b = affine.quantize(w, gs, bits)
+    r = round_to(rng.standard_normal((M, N)).astype(np.float32), "bf16") if resid else None
+    y = mx_compat.quantized_matmul(to_dev(x, "bf16", dev), u32_to_dev(wq, dev), to_dev(s, "bf16", dev),
+                                   to_dev(b, "bf16", dev), True, gs, bits,
+                                   residual=None if r is None else to_dev(r, "bf16", dev))
+    want = affine.quantized_matmul(x, wq, s, b, True, gs, bits, out_dtype="f32")
+    if r is not None:
+        want = want + r
+    assert_close(to_np(y), want, what=f"qmm M={M} N={N} K={K} bits={bits} gs={gs}")
+
+
+def test_qmm_config1(dev):
+    """x[8, 4096] . W[4096, 4096]^T, 4-bit g64 (rel 1e-2 / abs 2e-2 in bf16)."""
+    _qmm_case(dev, 8, 4096, 4096, 4, 64)
+    _qmm_case(dev, 8, 4096, 4096, 8, 64)
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 40])
+def test_qmm_token_counts(dev, M):
+    _qmm_case(dev, M, 512, 2048, 4, 64, seed=M)
+
+
+@pytest.mark.parametrize("bits,gs,K,N", [(4, 32, 256, 100), (4, 128, 768, 64), (8, 32, 512, 48),
+                                         (8, 128, 2048, 32), (4, 64, 768, 2048), (8, 64, 64, 16)])
+def test_qmm_shapes(dev, bits, gs, K, N):
+    _qmm_case(dev, 5, N, K, bits, gs, seed=K + N)
+
+
+def test_qmm_residual(dev):
+    _qmm_case(dev, 4, 256, 1024, 4, 64, resid=True)

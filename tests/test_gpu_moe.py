@@ -1,0 +1,91 @@
+"""GPU parity: gather_qmm (routed experts) and the fused SwitchGLU front half."""
+
+import numpy as np
+import pytest
+import torch
+
+from b200flash import mx_compat
+from oracle import affine, moe
+from oracle.fp import round_to
+
+from helpers import assert_close, to_dev, to_np, u32_to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _experts(rng, E, N, K, bits, gs):
+    w = round_to(rng.normal(0, 0.02, (E, N, K)).astype(np.float32), "bf16")
+    return affine.quantize(w, gs, bits)
+
+
+def _dev3(t, dev):
+    wq, s, b = t
+    return u32_to_dev(wq, dev), to_dev(s, "bf16", dev), to_dev(b, "bf16", dev)
+
+
+@pytest.mark.parametrize("T,k,E", [(1, 8, 16), (5, 2, 4), (33, 4, 16), (64, 8, 32)])
+def test_gather_qmm_switch_layout(dev, T, k, E):
+    """x[T,1,1,K] with rhs_indices[T,k] -> [T,k,1,N] (expert_streaming.py:230-241 layout)."""
+    rng = np.random.default_rng(T * 100 + E)
+    N, K = 96, 256
+    wq, s, b = _experts(rng, E, N, K, 4, 64)
+    x = round_to(rng.standard_normal((T, 1, 1, K)).astype(np.float32), "bf16")
+    inds = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    out = mx_compat.gather_qmm(to_dev(x, "bf16", dev), *_dev3((wq, s, b), dev),
+                               rhs_indices=torch.from_numpy(inds).to(dev), transpose=True, group_size=64, bits=4)
+    assert tuple(out.shape) == (T, k, 1, N)
+    want = affine.gather_qmm(x, wq, s, b, rhs_indices=inds, group_size=64, bits=4, out_dtype="f32")
+    assert_close(to_np(out), want, what="gather_qmm")
+
+
+def test_gather_qmm_down_proj_layout_8bit(dev):
+    """x[T,k,1,I] per assignment (the down projection) with 8-bit experts."""
+    rng = np.random.default_rng(9)
+    T, k, E, N, K = 7, 3, 6, 64, 768
+    wq, s, b = _experts(rng, E, N, K, 8, 64)
+    x = round_to(rng.standard_normal((T, k, 1, K)).astype(np.float32), "bf16")
+    inds = rng.integers(0, E, (T, k)).astype(np.int32)
+    out = mx_compat.gather_qmm(to_dev(x, "bf16", dev), *_dev3((wq, s, b), dev),
+                               rhs_indices=torch.from_numpy(inds).to(dev), group_size=64, bits=8)
+    want = affine.gather_qmm(x, wq, s, b, rhs_indices=inds, group_size=64, bits=8, out_dtype="f32")
+    assert_close(to_np(out), want, what="gather_qmm 8-bit")
+
+
+def test_gather_qmm_skewed_routing_and_empty_experts(dev):
+    """Most assignments on one expert (several token tiles), many experts unused."""
+    rng = np.random.default_rng(11)
+    T, k, E, N, K = 70, 2, 64, 48, 512
+    wq, s, b = _experts(rng, E, N, K, 4, 64)
+    x = round_to(rng.standard_normal((T, 1, 1, K)).astype(np.float32), "bf16")
+    inds = np.stack([np.zeros(T, np.int32), rng.integers(1, 4, T).astype(np.int32)], axis=1)
+    out = mx_compat.gather_qmm(to_dev(x, "bf16", dev), *_dev3((wq, s, b), dev),
+                               rhs_indices=torch.from_numpy(inds).to(dev), group_size=64, bits=4)
+    want = affine.gather_qmm(x, wq, s, b, rhs_indices=inds, group_size=64, bits=4, out_dtype="f32")
+    assert_close(to_np(out), want, what="skewed gather_qmm")
+
+
+def test_moe_plan_rejects_out_of_range_expert(dev):
+    plan = mx_compat.MoEPlan(torch.tensor([0, 1, 9], dtype=torch.int32, device=dev), 4, 16)
+    with pytest.raises(IndexError):
+        plan.check()
+
+
+def test_fused_switchglu_front_half(dev):
+    """silu(x.Wg^T)*(x.Wu^T) in one grouped kernel, Qwen3-MoE expert shape (I=768, H=2048)."""
+    rng = np.random.default_rng(5)
+    T, k, E, H, I = 6, 8, 16, 2048, 768
+    g = _experts(rng, E, I, H, 4, 64)
+    u = _experts(rng, E, I, H, 4, 64)
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    inds = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    plan = mx_compat.MoEPlan(torch.from_numpy(inds.reshape(-1)).to(dev), E, 16)
+    h = mx_compat.gather_qmv_planned(to_dev(x, "bf16", dev), plan, *_dev3(g, dev), 64, 4, x_row_div=k,
+                                     up=_dev3(u, dev))
+    gw = [affine.dequantize_f32(*(a[e] for a in g), 64, 4).astype(np.float64) for e in range(E)]
+    uw = [affine.dequantize_f32(*(a[e] for a in u), 64, 4).astype(np.float64) for e in range(E)]
+    want = np.zeros((T * k, I))
+    for t in range(T):
+        for j in range(k):
+            e = inds[t, j]
+            want[t * k + j] = moe.silu(gw[e] @ x[t]) * (uw[e] @ x[t])
+    assert_close(to_np(h), want, what="fused swiglu")

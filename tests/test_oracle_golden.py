@@ -1,0 +1,104 @@
+"""The CPU oracle against the golden vectors generated from the reference's own code."""
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import affine, kv_sym, mixed
+from oracle.fp import round_bf16, round_f16
+
+from conftest import GOLDEN
+
+
+def _kv_cases(golden):
+    z = golden("kv_sym.npz")
+    for entry in z["__cases__"]:
+        name, bits, gs, dtype = str(entry).split("|")
+        yield z, name, int(bits), int(gs), dtype
+
+
+def test_kv_oracle_matches_reference_outputs(golden):
+    n = 0
+    for z, name, bits, gs, dtype in _kv_cases(golden):
+        x = z[f"{name}/x"]
+        p, s, zr = kv_sym.quantize_tensor(x, bits, gs, dtype)
+        assert np.array_equal(p, z[f"{name}/packed"]), name
+        assert np.array_equal(s.view(np.uint32), z[f"{name}/scales"].view(np.uint32)), name
+        assert not zr.any()
+        r = kv_sym.dequantize_tensor(p, s, zr, bits, x.shape, gs)
+        assert np.array_equal(r.view(np.uint32), z[f"{name}/restored"].view(np.uint32)), name
+        n += 1
+    assert n >= 100
+
+
+def test_kv_oracle_reference_thresholds():
+    """The reference's own roundtrip MSE bounds (tests/test_quantized_kv_cache.py:46-119)."""
+    rng = np.random.default_rng(42)
+    x = rng.standard_normal(128).astype(np.float32)
+    for bits, bound in ((4, 0.02), (8, 0.001), (2, 0.6)):
+        p, s, z = kv_sym.quantize_tensor(x, bits, 64)
+        r = kv_sym.dequantize_tensor(p, s, z, bits, x.shape, 64)
+        assert float(np.mean((x - r) ** 2)) < bound
+    zz = np.zeros(64, np.float32)
+    p, s, z = kv_sym.quantize_tensor(zz, 4, 64)
+    assert not kv_sym.dequantize_tensor(p, s, z, 4, zz.shape, 64).any()
+
+
+def test_kv_oracle_sizes_and_errors():
+    for bits, n in ((4, 64), (2, 32), (8, 128)):
+        p, _, _ = kv_sym.quantize_tensor(np.ones(128, np.float32), bits, 64)
+        assert p.shape[-1] == n
+        assert kv_sym.packed_len(128, bits, 64) == n
+    with pytest.raises(ValueError, match="bits must be 2, 4, or 8"):
+        kv_sym.quantize_tensor(np.ones(3, np.float32), 3)
+    with pytest.raises(ValueError, match="bits must be 2, 4, or 8"):
+        kv_sym.dequantize_tensor(np.ones(3), np.ones(3), np.ones(3), 5, (3,))
+    p, s, z = kv_sym.quantize_tensor(np.zeros((0,), np.float32), 4)
+    assert p.shape == (0,) and s.shape == (0,)
+
+
+def test_mixed_precision_oracle_matches_reference(golden):
+    z = golden("mixed2bit.npz")
+    for i in range(3):
+        rows, K, gs = (int(v) for v in z[f"c{i}/meta"])
+        p, s, b = mixed.requantize_4bit_to_2bit(z[f"c{i}/wq"], z[f"c{i}/scales"], z[f"c{i}/biases"], gs)
+        assert np.array_equal(p, z[f"c{i}/packed2"])
+        assert np.array_equal(s.view(np.uint16), z[f"c{i}/scales2"].view(np.uint16))
+        assert np.array_equal(b.view(np.uint16), z[f"c{i}/biases2"].view(np.uint16))
+        d = mixed.dequantize_2bit(p, s, b, K)
+        assert np.array_equal(d.view(np.uint32), z[f"c{i}/deq2"].view(np.uint32))
+
+
+def test_affine_oracle_vectors(golden):
+    z = golden("affine.npz")
+    for bits in (2, 4, 8):
+        for gs in (32, 64, 128):
+            k = f"b{bits}_g{gs}"
+            wq, s, b = affine.quantize(z[f"{k}/w"], gs, bits)
+            assert np.array_equal(wq, z[f"{k}/wq"])
+            assert np.array_equal(s, z[f"{k}/scales"]) and np.array_equal(b, z[f"{k}/biases"])
+            assert np.array_equal(affine.dequantize(wq, s, b, gs, bits), z[f"{k}/deq"])
+            # constant group: scale 0, exact reconstruction
+            assert s[3, 0] == 0 and np.all(affine.dequantize(wq, s, b, gs, bits)[3, :gs] == 0.015625)
+            y = affine.quantized_matmul(z[f"{k}/x"], wq, s, b, True, gs, bits)
+            assert np.array_equal(y, z[f"{k}/y"])
+
+
+def test_affine_unpack_order_and_roundtrip():
+    # element k sits at bits 4*(k%8) of word k//8 (mixed_precision.py:150-171)
+    words = affine.unpack(np.array([[0x76543210, 0xFEDCBA98]], np.uint32), 4)
+    assert words.tolist() == [list(range(16))]
+    rng = np.random.default_rng(1)
+    w = round_bf16(rng.normal(0, 0.02, (8, 128)).astype(np.float32))
+    for bits in (4, 8):
+        wq, s, b = affine.quantize(w, 64, bits)
+        err = np.abs(affine.dequantize(wq, s, b, 64, bits) - w)
+        assert np.all(err <= (s.repeat(64, axis=1) * 0.5 + 1e-6) * 1.01 + np.abs(w) * 2 ** -8)
+
+
+def test_round_helpers():
+    assert round_bf16(np.float32(1.0 + 2 ** -8)) == 1.0  # tie -> even
+    assert round_bf16(np.float32(1.0 + 3 * 2 ** -8)) == np.float32(1.0 + 2 ** -6)
+    assert round_f16(np.float32(65519.0)) == 65504.0
