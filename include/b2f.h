@@ -169,6 +169,41 @@ int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_sc
                         float softmax_scale, int n_splits, void* workspace,
                         int64_t workspace_bytes, void* out, void* stream);
 
+/* ---- decode-step glue around the hot path (Qwen3-MoE-shaped decoder) ----- */
+
+/* MoE combine + residual + RMSNorm in one pass (expert_streaming.py:464-470
+ * `y = (y * scores[..., None]).sum(-2)` and the shared-expert add, then the
+ * next RMSNorm):  h = resid + sum_j scores[m,j] * y[m*k+j];  resid_out =
+ * bf16(h); norm_out = bf16(weight * h * rsqrt(mean(h^2) + eps)).  y may be
+ * NULL (plain RMSNorm).  resid_out may alias resid.  H <= 4096. */
+int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M,
+                        int64_t k, const void* weight, float eps, int64_t H, void* resid_out,
+                        void* norm_out, void* stream);
+
+/* Per token: q heads RMSNorm(q_norm)+RoPE -> q_out [B,Hq,D]; k heads
+ * RMSNorm(k_norm)+RoPE then the reference KV quantizer (bf16 arithmetic,
+ * group 64) into head-major page slot positions[b]; v heads quantized as is.
+ * qkv: bf16 [B, (Hq+2*Hkv)*D].  D = 128; bits in {4,8}.  This is the append
+ * path of QuantizedKVEntry.append (quantized_kv_cache.py:284-309) fused with
+ * the attention prologue. */
+int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                               const void* q_norm, const void* k_norm, float eps,
+                               float rope_theta, const int32_t* positions, void* q_out,
+                               uint8_t* k_codes, float* k_scales, uint8_t* v_codes,
+                               float* v_scales, const int32_t* block_table, int64_t max_pages,
+                               int64_t page_size, int bits, void* stream);
+
+/* Router of the MoE block (expert_streaming.py:439-472): gates =
+ * softmax(x.wr^T + bias), top-k (ties to the lower id), scores = gates of the
+ * top-k, renormalised to sum 1 if renorm.  x bf16 [T,H]; wr bf16 [E,H];
+ * bias f32 [E] or NULL; inds int32 [T,k]; scores f32 [T,k]. */
+int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
+                       int64_t E, int64_t k, int renorm, int32_t* inds, float* scores,
+                       void* stream);
+
+/* Greedy next token: out[m] = argmax_v x[m, v] (ties to the lower index). */
+int b2f_argmax_rows(const void* x, int64_t M, int64_t V, int32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,246 @@
+"""Qwen3-MoE-shaped decoder driven entirely by libb200flash kernels.
+
+This is the decode loop the reference runs through mlx-lm
+(``serve.py:347-353`` -> model forward -> ``CachedSwitchLinear`` /
+``QuantizedKVCacheManager``), rebuilt around the quantized hot path:
+
+per layer (B sequences, one new token each)
+  qkv   = quantized_matmul(xn, Wqkv)                    b2f_qgemv_affine
+  q     = RoPE(RMSNorm(q)); K,V -> 8-bit pages          b2f_qk_norm_rope_kv_append
+  a     = attention over packed K/V                     b2f_qkv_decode_attn
+  h    += quantized_matmul(a, Wo)                       b2f_qgemv_affine (residual fused)
+  xn    = RMSNorm(h)                                    b2f_combine_rmsnorm
+  top-k = softmax router                                b2f_moe_route_topk
+  plan  = group assignments by expert                   b2f_moe_plan
+  hh    = silu(gather_qmm(xn, Wg)) * gather_qmm(xn, Wu) b2f_gather_qgemv_affine (fused)
+  y     = gather_qmm(hh, Wd)                            b2f_gather_qgemv_affine
+  h    += sum_k score_k y_k ; xn = RMSNorm(h)           b2f_combine_rmsnorm
+then logits = quantized_matmul(xn, lm_head), next = argmax.
+
+Every buffer is allocated once, so ``step()`` can be captured in a CUDA graph.
+Weights are random (N(0, 0.02) before 4-bit quantization) with the model's
+shapes; the router adds a per-expert logit bias log(p_e) with p Zipf(s) so
+expert popularity is skewed like real traffic.
+"""
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _capi
+from ._capi import call, ptr
+from .quantized_kv_cache import packed_len, pick_splits
+
+
+@dataclass
+class Qwen3MoeShape:
+    hidden: int = 2048
+    layers: int = 48
+    n_heads: int = 32
+    n_kv_heads: int = 4
+    head_dim: int = 128
+    moe_inter: int = 768
+    n_experts: int = 128
+    top_k: int = 8
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    bits: int = 4
+    group_size: int = 64
+    kv_bits: int = 8
+    norm_topk: bool = True
+    zipf_s: float = 1.1
+
+
+class QWeight:
+    """An affine-quantized weight ``[*lead, N, K]`` (wq uint32, bf16 scales/biases)."""
+
+    def __init__(self, wq, scales, biases, bits, group_size):
+        self.wq, self.scales, self.biases = wq, scales, biases
+        self.bits, self.group_size = bits, group_size
+        self.N = wq.shape[-2]
+        self.K = wq.shape[-1] * 32 // bits
+
+    @property
+    def nbytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.wq, self.scales, self.biases))
+
+
+def random_qweight(shape, bits, gs, dev, gen, std=0.02, chunk_rows=1 << 16):
+    """N(0, std) bf16 weights quantized on the device in row chunks (bounded temp memory)."""
+    *lead, N, K = shape
+    rows = N
+    for d in lead:
+        rows *= d
+    wq = torch.empty(rows, K * bits // 32, dtype=torch.uint32, device=dev)
+    sc = torch.empty(rows, K // gs, dtype=torch.bfloat16, device=dev)
+    bi = torch.empty_like(sc)
+    st = _capi.stream_of(dev)
+    for r0 in range(0, rows, chunk_rows):
+        r1 = min(rows, r0 + chunk_rows)
+        w = (torch.randn(r1 - r0, K, device=dev, generator=gen) * std).to(torch.bfloat16)
+        call("b2f_quantize_affine", ptr(w), 0, r1 - r0, K, bits, gs, ptr(wq[r0]), ptr(sc[r0]), ptr(bi[r0]), st)
+        del w
+    return QWeight(wq.reshape(*lead, N, -1), sc.reshape(*lead, N, -1), bi.reshape(*lead, N, -1), bits, gs)
+
+
+class Qwen3MoeDecoder:
+    """Random-weight Qwen3-MoE-shaped decoder with a paged 8-bit KV cache."""
+
+    def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
+                 device="cuda:0", seed: int = 0, layers=None):
+        self.s = s = shape
+        self.dev = dev = torch.device(device)
+        self.B = max_batch
+        self.page = page_size
+        self.L = s.layers if layers is None else layers
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        H, D, Hq, Hkv, E, I = s.hidden, s.head_dim, s.n_heads, s.n_kv_heads, s.n_experts, s.moe_inter
+        bits, gs = s.bits, s.group_size
+        self.qkv_rows = (Hq + 2 * Hkv) * D
+
+        def norm_w(n):
+            return (1.0 + 0.1 * torch.randn(n, device=dev, generator=gen)).to(torch.bfloat16)
+
+        self.embed = random_qweight((s.vocab, H), bits, gs, dev, gen, std=1.0)
+        self.layers = []
+        ranks = torch.arange(1, E + 1, dtype=torch.float64, device=dev)
+        zipf = ranks ** (-s.zipf_s)
+        zipf = (zipf / zipf.sum()).log().to(torch.float32)
+        for _ in range(self.L):
+            perm = torch.randperm(E, device=dev, generator=gen)
+            self.layers.append({
+                "in_norm": norm_w(H), "post_norm": norm_w(H), "q_norm": norm_w(D), "k_norm": norm_w(D),
+                "wqkv": random_qweight((self.qkv_rows, H), bits, gs, dev, gen),
+                "wo": random_qweight((H, Hq * D), bits, gs, dev, gen),
+                "wr": (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16),
+                "rbias": zipf[perm].contiguous(),
+                "gate": random_qweight((E, I, H), bits, gs, dev, gen),
+                "up": random_qweight((E, I, H), bits, gs, dev, gen),
+                "down": random_qweight((E, H, I), bits, gs, dev, gen),
+            })
+        self.final_norm = norm_w(H)
+        self.lm_head = random_qweight((s.vocab, H), bits, gs, dev, gen)
+
+        # paged KV pool (head-major pages), one block table row per sequence
+        self.max_pages = (max_context + page_size - 1) // page_size + 1
+        self.num_pages = self.B * self.max_pages
+        self.rb = packed_len(D, s.kv_bits, 64)
+        self.kv = []
+        for _ in range(self.L):
+            self.kv.append({
+                "kc": torch.zeros(self.num_pages, Hkv, page_size, self.rb, dtype=torch.uint8, device=dev),
+                "ks": torch.zeros(self.num_pages, Hkv, page_size, D // 64, dtype=torch.float32, device=dev),
+                "vc": torch.zeros(self.num_pages, Hkv, page_size, self.rb, dtype=torch.uint8, device=dev),
+                "vs": torch.zeros(self.num_pages, Hkv, page_size, D // 64, dtype=torch.float32, device=dev),
+            })
+        self.block_table = torch.arange(self.num_pages, dtype=torch.int32, device=dev).reshape(self.B, self.max_pages)
+
+        # step buffers
+        B, A = self.B, self.B * s.top_k
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.positions = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.seq_lens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.h = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+        self.xn = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.empty(B, self.qkv_rows, dtype=torch.bfloat16, device=dev)
+        self.q = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+        self.inds = torch.empty(B, s.top_k, dtype=torch.int32, device=dev)
+        self.scores = torch.empty(B, s.top_k, dtype=torch.float32, device=dev)
+        self.tile = 16
+        self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
+        self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
+        self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.hh = torch.empty(A, I, dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+        self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
+        self.next_tokens = torch.empty(B, dtype=torch.int32, device=dev)
+        self.n_splits = pick_splits(B, Hkv, max_context)
+        wsb = int(_capi.lib().b2f_qkv_decode_attn_workspace_bytes(B, Hq, D, self.n_splits))
+        self.attn_ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+        self.attn_ws_bytes = wsb
+        self.softmax_scale = 1.0 / math.sqrt(D)
+
+    # ------------------------------------------------------------------
+    def weight_bytes(self) -> int:
+        n = self.embed.nbytes + self.lm_head.nbytes
+        for ly in self.layers:
+            n += sum(ly[k].nbytes for k in ("wqkv", "wo", "gate", "up", "down"))
+            n += ly["wr"].numel() * 2
+        return n
+
+    def fill_random_context(self, ctx_len: int, seed: int = 1):
+        """Synthetic prefilled context: every sequence holds ctx_len random
+        8-bit KV rows (codes uniform, scales like N(0,1) data) in every layer."""
+        g = torch.Generator(device=self.dev)
+        g.manual_seed(seed)
+        npg = (ctx_len + self.page - 1) // self.page
+        for kv in self.kv:
+            for key in ("kc", "vc"):
+                kv[key].random_(0, 255, generator=g)
+            for key in ("ks", "vs"):
+                kv[key].uniform_(0.015, 0.03, generator=g)
+        assert npg < self.max_pages
+        self.positions.fill_(ctx_len)
+        self.tokens.random_(0, self.s.vocab, generator=g)
+
+    # ------------------------------------------------------------------
+    def step(self):
+        """One decode step for all B sequences (graph-capturable)."""
+        s, B = self.s, self.B
+        H, D, Hq, Hkv, E, I = s.hidden, s.head_dim, s.n_heads, s.n_kv_heads, s.n_experts, s.moe_inter
+        A = B * s.top_k
+        st = _capi.stream_of(self.dev)
+        # embedding gather (dequantize selected rows) and first norm
+        e = self.embed
+        call("b2f_dequantize_affine", ptr(e.wq), ptr(e.scales), ptr(e.biases), 0, B, H, e.bits, e.group_size,
+             ptr(self.tokens), ptr(self.h), st)
+        torch.add(self.positions, 1, out=self.seq_lens)
+        call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(self.layers[0]["in_norm"]), s.rms_eps, H,
+             0, ptr(self.xn), st)
+        for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
+            w = ly["wqkv"]
+            call("b2f_qgemv_affine", ptr(self.xn), H, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K, w.bits,
+                 w.group_size, 0, ptr(self.qkv), w.N, st)
+            call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]), ptr(ly["k_norm"]),
+                 s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]), ptr(kv["ks"]),
+                 ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page, s.kv_bits, st)
+            call("b2f_qkv_decode_attn", ptr(self.q), ptr(kv["kc"]), ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]),
+                 ptr(self.block_table), self.max_pages, ptr(self.seq_lens), B, Hq, Hkv, D, self.page, self.page, 1,
+                 s.kv_bits, 64, self.softmax_scale, self.n_splits, ptr(self.attn_ws), self.attn_ws_bytes,
+                 ptr(self.attn), st)
+            w = ly["wo"]
+            call("b2f_qgemv_affine", ptr(self.attn), Hq * D, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K,
+                 w.bits, w.group_size, ptr(self.h), ptr(self.h), H, st)
+            call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
+                 ptr(self.xn), st)
+            call("b2f_moe_route_topk", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
+                 int(s.norm_topk), ptr(self.inds), ptr(self.scores), st)
+            call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
+                 ptr(self.plan_status), st)
+            g, u, d = ly["gate"], ly["up"], ly["down"]
+            call("b2f_gather_qgemv_affine", ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
+                 ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
+                 ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, st)
+            call("b2f_gather_qgemv_affine", ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
+                 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y),
+                 H, st)
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm
+            call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.y), ptr(self.scores), B, s.top_k, ptr(nxt),
+                 s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
+        w = self.lm_head
+        call("b2f_qgemv_affine", ptr(self.xn), H, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K, w.bits,
+             w.group_size, 0, ptr(self.logits), w.N, st)
+        call("b2f_argmax_rows", ptr(self.logits), B, s.vocab, ptr(self.next_tokens), st)
+        # feed back: next input token and position
+        self.tokens.copy_(self.next_tokens)
+        self.positions.add_(1)
+
+    def launches_per_step(self) -> int:
+        """libb200flash kernel launches in one step (attention counts its combine pass)."""
+        attn = 2 if self.n_splits > 1 else 1
+        per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 1 + 1 + 1
+        return 2 + self.L * per_layer + 2
