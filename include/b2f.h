@@ -169,6 +169,34 @@ int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_sc
                         float softmax_scale, int n_splits, void* workspace,
                         int64_t workspace_bytes, void* out, void* stream);
 
+/* Allocation-free form of b2f_qkv_decode_attn (no counterpart in the
+ * reference): the split-K partial results go to a fixed device array inside
+ * the library instead of a caller workspace, for callers that cannot allocate
+ * device memory (a C/cgo/JNI host without a device allocator, a process whose
+ * GPU memory is owned by another framework's pool, or a path where a
+ * synchronising cudaMalloc is not acceptable).
+ *   - capacity: B2F_ATTN_NOALLOC_SCRATCH_BYTES; a call whose workspace
+ *     (b2f_qkv_decode_attn_workspace_bytes) would exceed it returns
+ *     B2F_ERR_WORKSPACE without launching anything;
+ *   - the array is part of the loaded library: every GPU that loads it holds
+ *     4 MiB until the process exits;
+ *   - the first call on a device (that device must be current) looks up the
+ *     array's device address with cudaGetSymbolAddress and caches it; make that
+ *     first call before any stream capture;
+ *   - all calls on a device share the array and it keeps the last call's
+ *     contents (nothing needs clearing: every byte read is written first);
+ *     calls that overlap on the GPU race on it, so serialise them.
+ * Arguments and results are those of b2f_qkv_decode_attn without the
+ * workspace pair.  It allocates nothing. */
+#define B2F_ATTN_NOALLOC_SCRATCH_BYTES (4 << 20)
+int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const float* k_scales,
+                                const uint8_t* v_pages, const float* v_scales,
+                                const int32_t* block_table, int64_t max_pages,
+                                const int32_t* seq_lens, int64_t B, int64_t Hq, int64_t Hkv,
+                                int64_t D, int64_t page_size, int64_t head_stride,
+                                int64_t slot_stride, int bits, int group_size,
+                                float softmax_scale, int n_splits, void* out, void* stream);
+
 /* ---- decode-step glue around the hot path (Qwen3-MoE-shaped decoder) ----- */
 
 /* MoE combine + residual + RMSNorm in one pass (expert_streaming.py:464-470

@@ -47,6 +47,8 @@ SIGNATURES = {
     "b2f_qkv_decode_attn_workspace_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "b2f_qkv_decode_attn": (_I, [_P, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I, _I, _F, _I, _P, _I64, _P, _P]),
+    "b2f_qkv_decode_attn_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                         _I64, _I, _I, _F, _I, _P, _P]),
     "b2f_combine_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _P, _F, _I64, _P, _P, _P]),
     "b2f_qk_norm_rope_kv_append": (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P,
                                         _P, _I64, _I64, _I, _P]),

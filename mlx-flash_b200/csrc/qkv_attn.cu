@@ -453,3 +453,81 @@ int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_sc
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of b2f_qkv_decode_attn.
+//
+// Some callers cannot allocate device memory at the point where they run
+// decode attention: a host binding (cgo / JNI / a plain C program) that has no
+// device allocator of its own, a serving loop whose GPU memory is already
+// fully owned by another framework's pool, or a latency-critical path where a
+// cudaMalloc (which can synchronise the whole device) is not acceptable.  For
+// them the split-K partial results live in the fixed device array below
+// instead of a caller-provided workspace.
+//
+// The array is B2F_ATTN_NOALLOC_SCRATCH_BYTES (4 MiB) and is part of the
+// library image: every GPU that loads the library holds it until the process
+// exits.  All calls on a device share it and it keeps the previous call's
+// contents; the kernels overwrite every byte they later read, so nothing has
+// to be cleared between calls.  Calls that overlap on the GPU (different
+// streams, or different host threads on the same device) race on it.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace b2f {
+
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[B2F_ATTN_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the scratch array for the current device.  The host-side
+// symbol is only a stand-in, so the address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+static int attn_noalloc_scratch(void** out) {
+  constexpr int kMaxDevices = 64;
+  static void* cache[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) return B2F_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_last_cuda_error(e);
+      return B2F_ERR_CUDA;
+    }
+    cache[dev] = p;
+  }
+  *out = cache[dev];
+  return B2F_OK;
+}
+
+}  // namespace b2f
+
+extern "C" int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const float* k_scales,
+                                           const uint8_t* v_pages, const float* v_scales,
+                                           const int32_t* block_table, int64_t max_pages,
+                                           const int32_t* seq_lens, int64_t B, int64_t Hq, int64_t Hkv,
+                                           int64_t D, int64_t page_size, int64_t head_stride,
+                                           int64_t slot_stride, int bits, int group_size,
+                                           float softmax_scale, int n_splits, void* out, void* stream) {
+  if (B <= 0 || Hq <= 0 || D <= 0 || n_splits < 1) {
+    return b2f_qkv_decode_attn(q, k_pages, k_scales, v_pages, v_scales, block_table, max_pages, seq_lens, B,
+                               Hq, Hkv, D, page_size, head_stride, slot_stride, bits, group_size,
+                               softmax_scale, n_splits, nullptr, 0, out, stream);
+  }
+  const int64_t need = b2f_qkv_decode_attn_workspace_bytes(B, Hq, D, n_splits);
+  if (need > int64_t(B2F_ATTN_NOALLOC_SCRATCH_BYTES)) return B2F_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = b2f::attn_noalloc_scratch(&scratch);
+    if (rc != B2F_OK) return rc;
+  }
+  return b2f_qkv_decode_attn(q, k_pages, k_scales, v_pages, v_scales, block_table, max_pages, seq_lens, B, Hq,
+                             Hkv, D, page_size, head_stride, slot_stride, bits, group_size, softmax_scale,
+                             n_splits, scratch, need, out, stream);
+}
