@@ -203,7 +203,7 @@ int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const flo
  * `y = (y * scores[..., None]).sum(-2)` and the shared-expert add, then the
  * next RMSNorm):  h = resid + sum_j scores[m,j] * y[m*k+j];  resid_out =
  * bf16(h); norm_out = bf16(weight * h * rsqrt(mean(h^2) + eps)).  y may be
- * NULL (plain RMSNorm).  resid_out may alias resid.  H <= 4096. */
+ * NULL (plain RMSNorm).  resid_out may alias resid.  H % 8 == 0, H <= 8192. */
 int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M,
                         int64_t k, const void* weight, float eps, int64_t H, void* resid_out,
                         void* norm_out, void* stream);
@@ -223,11 +223,12 @@ int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t H
 
 /* Router of the MoE block (expert_streaming.py:439-472): gates =
  * softmax(x.wr^T + bias), top-k (ties to the lower id), scores = gates of the
- * top-k, renormalised to sum 1 if renorm.  x bf16 [T,H]; wr bf16 [E,H];
- * bias f32 [E] or NULL; inds int32 [T,k]; scores f32 [T,k]. */
+ * top-k, renormalised to sum 1 if renorm.  x bf16 [T,H] (H % 8 == 0); wr bf16
+ * [E,H]; bias f32 [E] or NULL; logits_ws f32 [T,E] caller workspace (holds the
+ * gates afterwards); inds int32 [T,k]; scores f32 [T,k]. */
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
-                       int64_t E, int64_t k, int renorm, int32_t* inds, float* scores,
-                       void* stream);
+                       int64_t E, int64_t k, int renorm, float* logits_ws, int32_t* inds,
+                       float* scores, void* stream);
 
 /* Greedy next token: out[m] = argmax_v x[m, v] (ties to the lower index). */
 int b2f_argmax_rows(const void* x, int64_t M, int64_t V, int32_t* out, void* stream);

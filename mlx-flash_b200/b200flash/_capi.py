@@ -52,7 +52,7 @@ SIGNATURES = {
     "b2f_combine_rmsnorm": (_I, [_P, _P, _P, _I64, _I64, _P, _F, _I64, _P, _P, _P]),
     "b2f_qk_norm_rope_kv_append": (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P,
                                         _P, _I64, _I64, _I, _P]),
-    "b2f_moe_route_topk": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P, _P]),
+    "b2f_moe_route_topk": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),
     "b2f_argmax_rows": (_I, [_P, _I64, _I64, _P, _P]),
 }
 

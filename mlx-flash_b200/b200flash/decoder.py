@@ -150,6 +150,7 @@ class Qwen3MoeDecoder:
         self.attn = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
         self.inds = torch.empty(B, s.top_k, dtype=torch.int32, device=dev)
         self.scores = torch.empty(B, s.top_k, dtype=torch.float32, device=dev)
+        self.gates = torch.empty(B, E, dtype=torch.float32, device=dev)
         self.tile = 16
         self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
         self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
@@ -218,7 +219,7 @@ class Qwen3MoeDecoder:
             call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
                  ptr(self.xn), st)
             call("b2f_moe_route_topk", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
-                 int(s.norm_topk), ptr(self.inds), ptr(self.scores), st)
+                 int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), st)
             call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
                  ptr(self.plan_status), st)
             g, u, d = ly["gate"], ly["up"], ly["down"]
@@ -242,5 +243,5 @@ class Qwen3MoeDecoder:
     def launches_per_step(self) -> int:
         """libb200flash kernel launches in one step (attention counts its combine pass)."""
         attn = 2 if self.n_splits > 1 else 1
-        per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 1 + 1 + 1
+        per_layer = 1 + 1 + attn + 1 + 1 + 2 + 1 + 1 + 1 + 1
         return 2 + self.L * per_layer + 2

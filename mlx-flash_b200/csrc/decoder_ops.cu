@@ -14,39 +14,72 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
   if (lane == 0) sh[warp] = v;
   __syncthreads();
   float t = 0.f;
-#pragma unroll
-  for (int w = 0; w < NW; ++w) t += sh[w];
+  const int nw = int(blockDim.x + 31) >> 5;
+  for (int w = 0; w < nw && w < NW; ++w) t += sh[w];
   __syncthreads();
   return t;
 }
 
 // h = resid + sum_j score[m, j] * y[m*k + j]  (y may be null -> h = resid)
 // resid_out = bf16(h); norm_out = bf16(w * h_bf16 * rsqrt(mean(h_bf16^2) + eps))
+// One CTA per row; a thread owns chunks of 8 contiguous elements (16-byte loads).
+constexpr int CMB_CHUNKS = 4;
+
 __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ y,
     const float* __restrict__ scores, int k, const __nv_bfloat16* __restrict__ w, float eps, int H,
     __nv_bfloat16* __restrict__ resid_out, __nv_bfloat16* __restrict__ norm_out) {
   __shared__ float sh[8];
   const int64_t m = blockIdx.x;
-  float hv[16];
+  const int nvec = H / 8;
+  float hv[CMB_CHUNKS][8];
   float ss = 0.f;
-  int n = 0;
-  for (int i = threadIdx.x; i < H; i += blockDim.x, ++n) {
-    float h = __bfloat162float(resid[m * H + i]);
-    if (y) {
-      for (int j = 0; j < k; ++j) h += scores[m * k + j] * __bfloat162float(y[(m * k + j) * H + i]);
+#pragma unroll
+  for (int q = 0; q < CMB_CHUNKS; ++q) {
+    const int v = threadIdx.x + q * blockDim.x;
+    if (v >= nvec) break;
+    const uint4 rr = reinterpret_cast<const uint4*>(resid + m * H)[v];
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[2 * i] = __low2float(r2[i]);
+      h[2 * i + 1] = __high2float(r2[i]);
     }
-    const float hb = __bfloat162float(__float2bfloat16_rn(h));
-    if (n < 16) hv[n] = hb;
-    ss += hb * hb;
+    if (y) {
+      for (int j = 0; j < k; ++j) {
+        const float sc = scores[m * k + j];
+        const uint4 yy = reinterpret_cast<const uint4*>(y + (m * k + j) * H)[v];
+        const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&yy);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          h[2 * i] += sc * __low2float(y2[i]);
+          h[2 * i + 1] += sc * __high2float(y2[i]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      hv[q][i] = __bfloat162float(__float2bfloat16_rn(h[i]));
+      ss += hv[q][i] * hv[q][i];
+    }
   }
   const float tot = block_sum<8>(ss, sh);
-  const float r = rsqrtf(tot / float(H) + eps);
-  n = 0;
-  for (int i = threadIdx.x; i < H; i += blockDim.x, ++n) {
-    const float hb = hv[n];
-    if (resid_out) resid_out[m * H + i] = __float2bfloat16_rn(hb);
-    norm_out[m * H + i] = __float2bfloat16_rn(__bfloat162float(w[i]) * hb * r);
+  const float rs = rsqrtf(tot / float(H) + eps);
+#pragma unroll
+  for (int q = 0; q < CMB_CHUNKS; ++q) {
+    const int v = threadIdx.x + q * blockDim.x;
+    if (v >= nvec) break;
+    const uint4 ww = reinterpret_cast<const uint4*>(w)[v];
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&ww);
+    uint32_t o[4], ro[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      o[i] = pack_bf16x2(__low2float(w2[i]) * hv[q][2 * i] * rs, __high2float(w2[i]) * hv[q][2 * i + 1] * rs);
+      ro[i] = pack_bf16x2(hv[q][2 * i], hv[q][2 * i + 1]);
+    }
+    if (resid_out) reinterpret_cast<uint4*>(resid_out + m * H)[v] = make_uint4(ro[0], ro[1], ro[2], ro[3]);
+    reinterpret_cast<uint4*>(norm_out + m * H)[v] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -81,6 +114,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
   const int slot = pos % p.PS;
   const __nv_bfloat16* row = p.qkv + int64_t(b) * NH * D;
   const float mi = p.bits == 8 ? 127.f : 7.f;
+  // rotary angles of this token: one sincosf per frequency, shared by all heads
+  __shared__ float rope_c[D / 2], rope_s[D / 2];
+  if (threadIdx.x < D / 2) {
+    const float inv = exp2f(-(2.f * float(threadIdx.x) / float(D)) * log2f(p.theta));
+    sincosf(float(pos) * inv, &rope_s[threadIdx.x], &rope_c[threadIdx.x]);
+  }
+  __syncthreads();
   for (int h = warp; h < NH; h += nw) {
     float v[4];
 #pragma unroll
@@ -98,9 +138,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int d = lane + 32 * i;  // frequency index < 64
-        const float inv = exp2f(-(2.f * float(d) / float(D)) * log2f(p.theta));
-        float sn, cs;
-        sincosf(float(pos) * inv, &sn, &cs);
+        const float sn = rope_s[d], cs = rope_c[d];
         const float x1 = v[i], x2 = v[i + 2];
         v[i] = __bfloat162float(__float2bfloat16_rn(x1 * cs - x2 * sn));
         v[i + 2] = __bfloat162float(__float2bfloat16_rn(x2 * cs + x1 * sn));
@@ -148,99 +186,132 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
   }
 }
 
-// logits[t, e] = x[t].wr[e] (+ bias[e]); gates = softmax; top-k by value
-// (ties -> lower id); scores optionally renormalised over the top-k.
-// CTA = 4 tokens x 8 warps; x rows staged in shared memory.
-constexpr int ROUTE_TOK = 4;
-
-__global__ void __launch_bounds__(256) route_topk_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
-                                                         const __nv_bfloat16* __restrict__ wr,
-                                                         const float* __restrict__ bias, int E, int k,
-                                                         int renorm, int32_t* __restrict__ inds,
-                                                         float* __restrict__ scores) {
-  extern __shared__ float sm[];
-  float* xs = sm;                      // [ROUTE_TOK][H]
-  float* lg = sm + ROUTE_TOK * H;      // [ROUTE_TOK][E]
-  const int t0 = blockIdx.x * ROUTE_TOK;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int i = threadIdx.x; i < ROUTE_TOK * H; i += blockDim.x) {
-    const int t = i / H, d = i % H;
-    xs[i] = (t0 + t < T) ? __bfloat162float(x[int64_t(t0 + t) * H + d]) : 0.f;
-  }
-  __syncthreads();
-  for (int e = warp; e < E; e += nw) {
-    float acc[ROUTE_TOK] = {0.f, 0.f, 0.f, 0.f};
-    const __nv_bfloat16* wrow = wr + int64_t(e) * H;
-    for (int d = lane * 2; d < H; d += 64) {
-      const __nv_bfloat162 w2 = *reinterpret_cast<const __nv_bfloat162*>(wrow + d);
-      const float w0 = __low2float(w2), w1 = __high2float(w2);
+// logits[t, e] = x[t].wr[e] (+ bias[e]): CTA = 8 experts x 8 tokens, one warp
+// per expert, 16-byte loads of the router row and the (L1-shared) token rows.
+__global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                           const __nv_bfloat16* __restrict__ wr,
+                                                           const float* __restrict__ bias, int E,
+                                                           float* __restrict__ logits) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x * 8 + warp;
+  const int t0 = blockIdx.y * 8;
+  if (e >= E) return;
+  float acc[8];
 #pragma unroll
-      for (int t = 0; t < ROUTE_TOK; ++t) acc[t] += w0 * xs[t * H + d] + w1 * xs[t * H + d + 1];
+  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+  const __nv_bfloat16* wrow = wr + int64_t(e) * H;
+  for (int h = lane * 8; h < H; h += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(wrow + h);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    float wf[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      wf[2 * i] = __low2float(w2[i]);
+      wf[2 * i + 1] = __high2float(w2[i]);
     }
 #pragma unroll
-    for (int t = 0; t < ROUTE_TOK; ++t) {
-      const float s = warp_sum<32>(acc[t]);
-      if (lane == 0) lg[t * E + e] = s + (bias ? bias[e] : 0.f);
+    for (int t = 0; t < 8; ++t) {
+      if (t0 + t < T) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(x + int64_t(t0 + t) * H + h);
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[t] += wf[2 * i] * __low2float(x2[i]) + wf[2 * i + 1] * __high2float(x2[i]);
+      }
     }
   }
-  __syncthreads();
-  if (warp < ROUTE_TOK && t0 + warp < T) {
-    const int t = warp;
-    float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[t * E + e]);
-    mx = warp_max<32>(mx);
-    float sum = 0.f;
-    for (int e = lane; e < E; e += 32) {
-      const float g = expf(lg[t * E + e] - mx);
-      lg[t * E + e] = g;
-      sum += g;
-    }
-    sum = warp_sum<32>(sum);
-    float picked = 0.f;
-    int64_t base = int64_t(t0 + t) * k;
-    for (int j = 0; j < k; ++j) {
-      float bv = -1.f;
-      int bi = 0x7fffffff;
-      for (int e = lane; e < E; e += 32) {
-        const float g = lg[t * E + e];
-        if (g > bv || (g == bv && e < bi)) {
-          bv = g;
-          bi = e;
-        }
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == 0) {
-        inds[base + j] = bi;
-        scores[base + j] = bv / sum;
-        lg[t * E + bi] = -2.f;  // remove from the candidates
-      }
-      picked += bv / sum;
-      __syncwarp();
-    }
-    if (renorm && lane < k) scores[base + lane] = scores[base + lane] / picked;
+  for (int t = 0; t < 8; ++t) {
+    const float v = warp_sum<32>(acc[t]);
+    if (lane == 0 && t0 + t < T) logits[int64_t(t0 + t) * E + e] = v + (bias ? bias[e] : 0.f);
   }
 }
 
-__global__ void __launch_bounds__(256) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
-                                                          int32_t* __restrict__ out) {
-  __shared__ float sv[8];
-  __shared__ int si[8];
+// gates = softmax(logits[t]); top-k by value (ties -> lower id); scores are the
+// gates of the top-k, optionally renormalised to sum 1.  One warp per token.
+__global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
+                                                         int renorm, int32_t* __restrict__ inds,
+                                                         float* __restrict__ scores) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  float* lg = logits + int64_t(t) * E;
+  float mx = -INFINITY;
+  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+  mx = warp_max<32>(mx);
+  float sum = 0.f;
+  for (int e = lane; e < E; e += 32) {
+    const float g = expf(lg[e] - mx);
+    lg[e] = g;
+    sum += g;
+  }
+  sum = warp_sum<32>(sum);
+  __syncwarp();
+  float picked = 0.f, my_score = 0.f;
+  const int64_t base = int64_t(t) * k;
+  for (int j = 0; j < k; ++j) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      const float g = lg[e];
+      if (g > bv || (g == bv && e < bi)) {
+        bv = g;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    const float sc = bv / sum;
+    if (lane == j) my_score = sc;
+    if (lane == 0) {
+      inds[base + j] = bi;
+      lg[bi] = -2.f;  // remove from the candidates
+    }
+    picked += sc;
+    __syncwarp();
+  }
+  if (lane < k) scores[base + lane] = renorm ? my_score / picked : my_score;
+}
+
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
+                                                           int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
   const int64_t m = blockIdx.x;
+  const __nv_bfloat16* row = x + m * V;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = __bfloat162float(x[m * V + i]);
-    if (v > bv) {
-      bv = v;
-      bi = int(i);
+  const bool vec = (V % 8) == 0 && (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+  if (vec) {
+    for (int64_t v = threadIdx.x; v < V / 8; v += blockDim.x) {
+      const uint4 q = reinterpret_cast<const uint4*>(row)[v];
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = __low2float(q2[i]), b = __high2float(q2[i]);
+        if (a > bv) {
+          bv = a;
+          bi = int(8 * v + 2 * i);
+        }
+        if (b > bv) {
+          bv = b;
+          bi = int(8 * v + 2 * i + 1);
+        }
+      }
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = __bfloat162float(row[i]);
+      if (v > bv) {
+        bv = v;
+        bi = int(i);
+      }
     }
   }
 #pragma unroll
@@ -277,10 +348,15 @@ extern "C" {
 int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M, int64_t k,
                         const void* weight, float eps, int64_t H, void* resid_out, void* norm_out,
                         void* stream) {
-  if (M < 0 || H <= 0 || H > 16 * 256 || (y && (k <= 0 || !scores))) return B2F_ERR_INVALID;
+  if (M < 0 || H <= 0 || (y && (k <= 0 || !scores))) return B2F_ERR_INVALID;
+  if (H % 8 != 0 || H > CMB_CHUNKS * 8 * 256) return B2F_ERR_UNSUPPORTED;
   if (M == 0) return B2F_OK;
   if (!resid || !weight || !norm_out) return B2F_ERR_INVALID;
-  combine_rmsnorm_kernel<<<unsigned(M), 256, 0, as_stream(stream)>>>(
+  if (!aligned(resid, 16) || !aligned(weight, 16) || !aligned(norm_out, 16) || (y && !aligned(y, 16)) ||
+      (resid_out && !aligned(resid_out, 16)))
+    return B2F_ERR_ALIGN;
+  const int threads = int(H / 8) < 256 ? int(((H / 8) + 31) / 32 * 32) : 256;
+  combine_rmsnorm_kernel<<<unsigned(M), threads, 0, as_stream(stream)>>>(
       static_cast<const __nv_bfloat16*>(resid), static_cast<const __nv_bfloat16*>(y), scores, int(k),
       static_cast<const __nv_bfloat16*>(weight), eps, int(H), static_cast<__nv_bfloat16*>(resid_out),
       static_cast<__nv_bfloat16*>(norm_out));
@@ -322,23 +398,19 @@ int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t H
 }
 
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
-                       int64_t k, int renorm, int32_t* inds, float* scores, void* stream) {
-  if (T < 0 || H <= 0 || H % 2 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, void* stream) {
+  if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+  if (H % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (T == 0) return B2F_OK;
-  if (!x || !wr || !inds || !scores) return B2F_ERR_INVALID;
-  const int64_t smem = (ROUTE_TOK * H + ROUTE_TOK * E) * int64_t(sizeof(float));
-  if (smem > 200 * 1024) return B2F_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return B2F_ERR_CUDA;
-    }
-  }
-  const unsigned grid = unsigned((T + ROUTE_TOK - 1) / ROUTE_TOK);
-  route_topk_kernel<<<grid, 256, smem, as_stream(stream)>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-                                                            static_cast<const __nv_bfloat16*>(wr), bias, int(E),
-                                                            int(k), renorm, inds, scores);
+  if (!x || !wr || !logits_ws || !inds || !scores) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
+  cudaStream_t st = as_stream(stream);
+  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + 7) / 8), 1u};
+  route_logits_kernel<<<g1, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+                                           static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits_ws);
+  int rc = check_launch();
+  if (rc != B2F_OK) return rc;
+  route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds, scores);
   return check_launch();
 }
 
@@ -346,7 +418,7 @@ int b2f_argmax_rows(const void* x, int64_t M, int64_t V, int32_t* out, void* str
   if (M < 0 || V <= 0 || V > 0x7fffffff) return B2F_ERR_INVALID;
   if (M == 0) return B2F_OK;
   if (!x || !out) return B2F_ERR_INVALID;
-  argmax_rows_kernel<<<unsigned(M), 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16*>(x), V, out);
+  argmax_rows_kernel<<<unsigned(M), 1024, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16*>(x), V, out);
   return check_launch();
 }
 

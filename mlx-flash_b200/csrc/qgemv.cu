@@ -1,24 +1,27 @@
 // (b) dequant-fused GEMV for the MLX affine format, dense and grouped
 // (routed experts), with the SwitchGLU gate/up pair fused.
 //
-// Memory-bound design (decode: M <= 16..32 tokens per weight tile):
-//  * A CTA owns a run of 16-row blocks of one weight matrix (one expert) and
-//    one tile of <= 8*NT tokens.  Its NW warps split K: warp w owns GW
-//    consecutive quantization groups.  The tile's activations for those
-//    groups are loaded ONCE into registers as bf16 MMA B-fragments and stay
-//    there while the weight rows stream past ("activations stationary").
-//  * Weights are read with 8/16-byte vector loads of packed words and
-//    unpacked in registers straight into bf16 A-fragments with one lop3 per
-//    two values: (0x4300 | q) is the bf16 number 128+q.  For 8-bit words the
-//    high nibble goes through (0x4500 | hi) = 2048 + 16*hi, so both halves
-//    accumulate into the same fp32 accumulator.
-//  * Each MMA k-step stays inside one quantization group, so the group's
-//    scale and bias are applied once per group to the fp32 partial:
+// Memory-bound design (decode: <= 16 tokens per weight pass):
+//  * Work is the flattened sequence (token tile, 16-row block), split into
+//    equal contiguous ranges, one per CTA (stream-K balance).
+//  * A producer warp streams each 16-row block of packed words (plus its
+//    scales/biases) into a STAGES-deep shared-memory ring with TMA bulk
+//    copies (cp.async.bulk, completion on an mbarrier's transaction count)
+//    and refills a stage once every consumer warp released it.
+//  * Consumer warps split K by quantization group.  Each keeps the tile's
+//    activations for its groups in registers as MMA B-fragments, reloaded
+//    only when the token tile changes ("activations stationary").
+//  * Packed words are unpacked in registers straight into bf16 A-fragments:
+//    (0x4300 | q) is the bf16 number 128+q; the high nibble of an 8-bit code
+//    goes through (0x4500 | hi) = 2048 + 16*hi.  Legacy warp MMAs
+//    (mma.sync m16n8k16, fp32 accumulate) do the dot products.
+//  * Each MMA k-step stays inside one quantization group, so scale and bias
+//    are applied once per group to the fp32 partial:
 //        y += s * sum_k x_k*(OFF + q_k) + (b - OFF*s) * sum_k x_k
-//    (OFF = 128 for 4-bit, 2176 for 8-bit), i.e. exactly q*s+b with fp32
-//    accumulation -- the same factorisation MLX's qmv uses.
-//  * The per-warp partial tiles are reduced across warps through shared
-//    memory in a fixed order (deterministic), then written as bf16.
+//    (OFF = 128 for 4-bit, 2176 for 8-bit) -- exactly q*s+b with fp32
+//    accumulation, the factorisation MLX's qmv uses.
+//  * Per-warp partial tiles are reduced across warps through a padded,
+//    double-buffered shared-memory tile in a fixed order (deterministic).
 #include "common.cuh"
 
 namespace b2f {
@@ -42,177 +45,243 @@ struct GemvParams {
   const int4* slots;
   const int32_t* sorted;
   int tile;
-  int rb_per_chunk;
+  int32_t* err;  // optional: set to B2F_ERR_TIMEOUT if a bounded wait gave up
 };
 
-template <int BITS>
-struct WordFrag;
+// Shared-memory plan of one launch (host-computed).
+struct SmemPlan {
+  int pitch;      // bytes per staged weight row (row_bytes padded against bank conflicts)
+  int row_bytes;  // K*BITS/8
+  int off_w[2], off_s[2], off_b[2];
+  int stage_bytes, stages, red_off, red_buf_floats, flag_off, mbar_off;
+};
+
+constexpr int RED_PITCH = 20;  // floats per output column of a partial tile (16 rows; 20 = 4 mod 16)
 
 // 4-bit: a word holds 8 consecutive k.  R_i = (e_i, e_{i+4}) as bf16 128+q.
-template <>
-struct WordFrag<4> {
-  static __device__ __forceinline__ void unpack(uint32_t w, uint32_t (&R)[4]) {
-    R[0] = and_or(w, 0x000F000Fu, 0x43004300u);
-    R[1] = and_or(w >> 4, 0x000F000Fu, 0x43004300u);
-    R[2] = and_or(w >> 8, 0x000F000Fu, 0x43004300u);
-    R[3] = and_or(w >> 12, 0x000F000Fu, 0x43004300u);
-  }
-};
+__device__ __forceinline__ void unpack4(uint32_t w, uint32_t (&R)[4]) {
+  R[0] = and_or(w, 0x000F000Fu, 0x43004300u);
+  R[1] = and_or(w >> 4, 0x000F000Fu, 0x43004300u);
+  R[2] = and_or(w >> 8, 0x000F000Fu, 0x43004300u);
+  R[3] = and_or(w >> 12, 0x000F000Fu, 0x43004300u);
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
 
 template <int BITS, int GS, int NT, int GW, int MAT>
-__global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(288, 1) qgemv_kernel(const GemvParams p, const SmemPlan L) {
   constexpr int STEPS = GS / 16;           // MMA k-steps per group
   constexpr int CHUNK_K = GS / 4;          // k values per thread per group
   constexpr int CW = CHUNK_K * BITS / 32;  // packed words per thread per group per row
   constexpr int XV = CHUNK_K / 8;          // 16-byte activation loads per thread per group
+  constexpr int GROUP_BYTES = GS * BITS / 8;
   constexpr float OFF = BITS == 4 ? 128.f : 2176.f;
   constexpr int TILE_COLS = 8 * NT;
+  constexpr int OUTS = 16 * TILE_COLS;  // outputs per row block
+  constexpr int MAX_OPT = 8;            // outputs per consumer thread (>= OUTS / 32)
 
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int NW = blockDim.x >> 5;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int NW = int(blockDim.x >> 5) - 1;  // consumer warps; warp NW produces
+  const int NC = NW * 32;
   const int r = lane >> 2, c = lane & 3;
   const int G = int(p.K / GS);
-  const int64_t words_per_row = p.K * BITS / 32;
-
-  int expert = 0, tok_begin, n_tok;
-  if (p.slots) {
-    if (int(blockIdx.y) >= *p.slot_count) return;
-    const int4 sl = p.slots[blockIdx.y];
-    expert = sl.x;
-    tok_begin = sl.y;
-    n_tok = sl.z;
-  } else {
-    tok_begin = int(blockIdx.y) * p.tile;
-    n_tok = int(min(int64_t(p.tile), p.M - tok_begin));
-  }
-
-  // ---- activation B-fragments and per-group activation sums -----------
-  uint32_t bfr[GW][NT][STEPS][2];
-  float xsum[GW][NT][2];
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const int ti = nt * 8 + r;
-    const bool tvalid = ti < n_tok;
-    int64_t xrow = 0;
-    if (tvalid) {
-      if (p.slots) {
-        const int a = p.sorted[tok_begin + ti];
-        xrow = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
-      } else {
-        xrow = tok_begin + ti;
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < GW; ++j) {
-      const int g = warp * GW + j;
-      const bool valid = tvalid && g < G;
-      uint32_t xr[XV * 4];
-      if (valid) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.x + xrow * p.ldx + int64_t(g) * GS + c * CHUNK_K);
-#pragma unroll
-        for (int v = 0; v < XV; ++v) {
-          const uint4 q = src[v];
-          xr[4 * v + 0] = q.x;
-          xr[4 * v + 1] = q.y;
-          xr[4 * v + 2] = q.z;
-          xr[4 * v + 3] = q.w;
-        }
-      } else {
-#pragma unroll
-        for (int v = 0; v < XV * 4; ++v) xr[v] = 0u;
-      }
-      float part = 0.f;
-#pragma unroll
-      for (int v = 0; v < XV * 4; ++v) {
-        const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&xr[v]);
-        part += __low2float(h) + __high2float(h);
-      }
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      xsum[j][nt][0] = __shfl_sync(0xffffffffu, part, 8 * c);
-      xsum[j][nt][1] = __shfl_sync(0xffffffffu, part, 8 * c + 4);
-      if constexpr (BITS == 4) {
-        // word wi covers 8 k: regs X01,X23,X45,X67 = xr[4wi .. 4wi+3]
-#pragma unroll
-        for (int s = 0; s < STEPS; ++s) {
-          const int wi = s >> 1;
-          const uint32_t* xw = &xr[4 * wi];
-          if ((s & 1) == 0) {
-            bfr[j][nt][s][0] = prmt(xw[0], xw[2], 0x5410u);  // (x0, x4)
-            bfr[j][nt][s][1] = prmt(xw[0], xw[2], 0x7632u);  // (x1, x5)
-          } else {
-            bfr[j][nt][s][0] = prmt(xw[1], xw[3], 0x5410u);  // (x2, x6)
-            bfr[j][nt][s][1] = prmt(xw[1], xw[3], 0x7632u);  // (x3, x7)
-          }
-        }
-      } else {
-        // word s covers 4 k: regs X01, X23 = xr[2s], xr[2s+1]
-#pragma unroll
-        for (int s = 0; s < STEPS; ++s) {
-          bfr[j][nt][s][0] = prmt(xr[2 * s], xr[2 * s + 1], 0x5410u);  // (x0, x2)
-          bfr[j][nt][s][1] = prmt(xr[2 * s], xr[2 * s + 1], 0x7632u);  // (x1, x3)
-        }
-      }
-    }
-  }
-
-  // ---- stream the weight rows ------------------------------------------
-  extern __shared__ float red[];  // [NW][MAT][16][TILE_COLS]
   const int64_t n_rb = (p.N + 15) / 16;
-  const int64_t rb_begin = int64_t(blockIdx.x) * p.rb_per_chunk;
-  const int64_t rb_end = min(rb_begin + p.rb_per_chunk, n_rb);
+  const int n_slots = p.slots ? *p.slot_count : int((p.M + p.tile - 1) / p.tile);
+  const int64_t W = int64_t(n_slots) * n_rb;
+  const int64_t per = (W + gridDim.x - 1) / gridDim.x;
+  const int64_t w_begin = int64_t(blockIdx.x) * per;
+  const int64_t w_end = min(W, w_begin + per);
+  if (w_begin >= w_end) return;
+  const int n_iter = int(w_end - w_begin);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.mbar_off);
+  uint64_t* empty = full + L.stages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.flag_off);
+  float* red = reinterpret_cast<float*>(smem + L.red_off);
 
-  // sv packs (scale, bias) of one row/group as a bf16x2 (scale in the low half)
-  uint32_t wcur[MAT][GW][2][CW], wnext[MAT][GW][2][CW];
-  uint32_t scur[MAT][GW][2], snext[MAT][GW][2];
-
-  auto load_rb = [&](int64_t rb, uint32_t (&wv)[MAT][GW][2][CW], uint32_t (&sv)[MAT][GW][2]) {
-#pragma unroll
-    for (int m = 0; m < MAT; ++m) {
-      const uint32_t* wbase = p.w[m] + int64_t(expert) * p.w_estride;
-      const uint16_t* sbase = reinterpret_cast<const uint16_t*>(p.s[m]) + int64_t(expert) * p.sb_estride;
-      const uint16_t* bbase = reinterpret_cast<const uint16_t*>(p.b[m]) + int64_t(expert) * p.sb_estride;
-#pragma unroll
-      for (int j = 0; j < GW; ++j) {
-        const int g = warp * GW + j;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int64_t row = rb * 16 + r + 8 * h;
-          if (g < G && row < p.N) {
-            const uint32_t* src = wbase + row * words_per_row + int64_t(g) * (GS * BITS / 32) + c * CW;
-            if constexpr (CW == 1) {
-              wv[m][j][h][0] = src[0];
-            } else if constexpr (CW == 2) {
-              const uint2 q = *reinterpret_cast<const uint2*>(src);
-              wv[m][j][h][0] = q.x;
-              wv[m][j][h][1] = q.y;
-            } else {
-#pragma unroll
-              for (int v = 0; v < CW / 4; ++v) {
-                const uint4 q = reinterpret_cast<const uint4*>(src)[v];
-                wv[m][j][h][4 * v + 0] = q.x;
-                wv[m][j][h][4 * v + 1] = q.y;
-                wv[m][j][h][4 * v + 2] = q.z;
-                wv[m][j][h][4 * v + 3] = q.w;
-              }
-            }
-            sv[m][j][h] = uint32_t(sbase[row * G + g]) | (uint32_t(bbase[row * G + g]) << 16);
-          } else {
-#pragma unroll
-            for (int v = 0; v < CW; ++v) wv[m][j][h][v] = 0u;
-            sv[m][j][h] = 0u;
-          }
-        }
-      }
+  auto slot_info = [&](int slot, int& expert, int& tok_begin, int& n_tok) {
+    if (p.slots) {
+      const int4 sl = p.slots[slot];
+      expert = sl.x;
+      tok_begin = sl.y;
+      n_tok = sl.z;
+    } else {
+      expert = 0;
+      tok_begin = slot * p.tile;
+      n_tok = int(min(int64_t(p.tile), p.M - tok_begin));
     }
   };
+  // scales/biases of a block go through TMA when the copy is 16-byte shaped
+  auto sb_tma_ok = [&](int64_t e0, int rows) {
+    return ((rows * G * 2) % 16) == 0 && aligned16(p.s[0] + e0) && aligned16(p.b[0] + e0) &&
+           (MAT == 1 || (aligned16(p.s[1] + e0) && aligned16(p.b[1] + e0)));
+  };
 
-  if (rb_begin < rb_end) load_rb(rb_begin, wcur, scur);
-  for (int64_t rb = rb_begin; rb < rb_end; ++rb) {
-    if (rb + 1 < rb_end) load_rb(rb + 1, wnext, snext);
+  if (tid == 0) {
+    for (int s = 0; s < L.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  // =========================== producer warp ================================
+  if (warp == NW) {
+    if (lane == 0) {
+      for (int it = 0; it < n_iter; ++it) {
+        const int s = it % L.stages;
+        if (it >= L.stages) {
+          if (*abort_flag || !mbar_wait_bounded(&empty[s], uint32_t(((it / L.stages) - 1) & 1))) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+        const int64_t widx = w_begin + it;
+        const int slot = int(widx / n_rb);
+        const int64_t rb = widx - int64_t(slot) * n_rb;
+        int expert, tb, nt_;
+        slot_info(slot, expert, tb, nt_);
+        const int rows = int(min(int64_t(16), p.N - rb * 16));
+        uint8_t* st = smem + s * L.stage_bytes;
+        const int sbr = rows * G * 2;
+        const int64_t e0 = int64_t(expert) * p.sb_estride + rb * 16 * G;
+        const bool sb_tma = sb_tma_ok(e0, rows);
+        const uint32_t bytes = uint32_t(MAT * rows * L.row_bytes + (sb_tma ? MAT * 2 * sbr : 0));
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&full[s], bytes);
+#pragma unroll
+        for (int m = 0; m < MAT; ++m) {
+          const uint8_t* wb = reinterpret_cast<const uint8_t*>(p.w[m] + int64_t(expert) * p.w_estride) +
+                              rb * 16 * int64_t(L.row_bytes);
+          for (int rr = 0; rr < rows; ++rr)
+            bulk_g2s(st + L.off_w[m] + rr * L.pitch, wb + int64_t(rr) * L.row_bytes, uint32_t(L.row_bytes),
+                     &full[s]);
+          if (sb_tma) {
+            bulk_g2s(st + L.off_s[m], p.s[m] + e0, uint32_t(sbr), &full[s]);
+            bulk_g2s(st + L.off_b[m], p.b[m] + e0, uint32_t(sbr), &full[s]);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // =========================== consumer warps ===============================
+  uint32_t bfr[GW][NT][STEPS][2];
+  float xsum[GW][NT][2];
+  int64_t my_orow[MAX_OPT];
+  int cur_slot = -1, expert = 0, tok_begin = 0, n_tok = 0;
+  bool timed_out = false;
+
+  for (int it = 0; it < n_iter; ++it) {
+    const int64_t widx = w_begin + it;
+    const int slot = int(widx / n_rb);
+    const int64_t rb = widx - int64_t(slot) * n_rb;
+    if (slot != cur_slot) {
+      // (re)load this token tile's activations as register B-fragments
+      cur_slot = slot;
+      slot_info(slot, expert, tok_begin, n_tok);
+#pragma unroll
+      for (int k = 0; k < MAX_OPT; ++k) {
+        const int idx = tid + k * NC;
+        const int col = idx >> 4;
+        my_orow[k] = -1;
+        if (idx < OUTS && col < n_tok)
+          my_orow[k] = p.slots ? int64_t(p.sorted[tok_begin + col]) : int64_t(tok_begin + col);
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int ti = nt * 8 + r;
+        const bool tvalid = ti < n_tok;
+        int64_t xrow = 0;
+        if (tvalid) {
+          if (p.slots) {
+            const int a = p.sorted[tok_begin + ti];
+            xrow = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
+          } else {
+            xrow = tok_begin + ti;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < GW; ++j) {
+          const int g = warp * GW + j;
+          const bool valid = tvalid && g < G;
+          uint32_t xr[XV * 4];
+          if (valid) {
+            const uint4* src =
+                reinterpret_cast<const uint4*>(p.x + xrow * p.ldx + int64_t(g) * GS + c * CHUNK_K);
+#pragma unroll
+            for (int v = 0; v < XV; ++v) {
+              const uint4 q = src[v];
+              xr[4 * v + 0] = q.x;
+              xr[4 * v + 1] = q.y;
+              xr[4 * v + 2] = q.z;
+              xr[4 * v + 3] = q.w;
+            }
+          } else {
+#pragma unroll
+            for (int v = 0; v < XV * 4; ++v) xr[v] = 0u;
+          }
+          float part = 0.f;
+#pragma unroll
+          for (int v = 0; v < XV * 4; ++v) {
+            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&xr[v]);
+            part += __low2float(h) + __high2float(h);
+          }
+          part += __shfl_xor_sync(0xffffffffu, part, 1);
+          part += __shfl_xor_sync(0xffffffffu, part, 2);
+          xsum[j][nt][0] = __shfl_sync(0xffffffffu, part, 8 * c);
+          xsum[j][nt][1] = __shfl_sync(0xffffffffu, part, 8 * c + 4);
+          if constexpr (BITS == 4) {
+#pragma unroll
+            for (int s = 0; s < STEPS; ++s) {
+              const uint32_t* xw = &xr[4 * (s >> 1)];
+              if ((s & 1) == 0) {
+                bfr[j][nt][s][0] = prmt(xw[0], xw[2], 0x5410u);  // (x0, x4)
+                bfr[j][nt][s][1] = prmt(xw[0], xw[2], 0x7632u);  // (x1, x5)
+              } else {
+                bfr[j][nt][s][0] = prmt(xw[1], xw[3], 0x5410u);  // (x2, x6)
+                bfr[j][nt][s][1] = prmt(xw[1], xw[3], 0x7632u);  // (x3, x7)
+              }
+            }
+          } else {
+#pragma unroll
+            for (int s = 0; s < STEPS; ++s) {
+              bfr[j][nt][s][0] = prmt(xr[2 * s], xr[2 * s + 1], 0x5410u);  // (x0, x2)
+              bfr[j][nt][s][1] = prmt(xr[2 * s], xr[2 * s + 1], 0x7632u);  // (x1, x3)
+            }
+          }
+        }
+      }
+    }
+
+    // residual of this block's outputs, fetched before the math
+    float resid[MAX_OPT];
+#pragma unroll
+    for (int k = 0; k < MAX_OPT; ++k) {
+      resid[k] = 0.f;
+      const int64_t n = rb * 16 + ((tid + k * NC) & 15);
+      if (p.residual && my_orow[k] >= 0 && n < p.N)
+        resid[k] = __bfloat162float(p.residual[my_orow[k] * p.ldo + n]);
+    }
+
+    const int s_idx = it % L.stages;
+    if (!timed_out) {
+      if (*abort_flag || !mbar_wait_bounded(&full[s_idx], uint32_t((it / L.stages) & 1))) {
+        timed_out = true;
+        *abort_flag = 1;
+      }
+    }
+    const uint8_t* st = smem + s_idx * L.stage_bytes;
+    const int rows = int(min(int64_t(16), p.N - rb * 16));
+    const int64_t sb0 = int64_t(expert) * p.sb_estride + rb * 16 * G;
+    const bool sb_tma = sb_tma_ok(sb0, rows);
 
     float acc[MAT][NT][4];
 #pragma unroll
@@ -224,9 +293,44 @@ __global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
 
 #pragma unroll
     for (int j = 0; j < GW; ++j) {
-      if (warp * GW + j >= G) continue;
+      const int g = warp * GW + j;
+      if (g >= G) continue;
 #pragma unroll
       for (int m = 0; m < MAT; ++m) {
+        uint32_t wv[2][CW];
+        float sc[2], bi[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = r + 8 * h;
+          const uint8_t* src = st + L.off_w[m] + row * L.pitch + g * GROUP_BYTES + c * CW * 4;
+          if constexpr (CW == 1) {
+            wv[h][0] = *reinterpret_cast<const uint32_t*>(src);
+          } else if constexpr (CW == 2) {
+            const uint2 q = *reinterpret_cast<const uint2*>(src);
+            wv[h][0] = q.x;
+            wv[h][1] = q.y;
+          } else {
+#pragma unroll
+            for (int v = 0; v < CW / 4; ++v) {
+              const uint4 q = reinterpret_cast<const uint4*>(src)[v];
+              wv[h][4 * v + 0] = q.x;
+              wv[h][4 * v + 1] = q.y;
+              wv[h][4 * v + 2] = q.z;
+              wv[h][4 * v + 3] = q.w;
+            }
+          }
+          if (sb_tma) {
+            sc[h] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L.off_s[m])[row * G + g]);
+            bi[h] = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(st + L.off_b[m])[row * G + g]);
+          } else if (row < rows) {
+            const int64_t e0 = sb0 + int64_t(row) * G + g;
+            sc[h] = __bfloat162float(p.s[m][e0]);
+            bi[h] = __bfloat162float(p.b[m][e0]);
+          } else {
+            sc[h] = 0.f;
+            bi[h] = 0.f;
+          }
+        }
         float ag[NT][4];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -236,8 +340,8 @@ __global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
 #pragma unroll
           for (int wi = 0; wi < CW; ++wi) {
             uint32_t R0[4], R1[4];
-            WordFrag<4>::unpack(wcur[m][j][0][wi], R0);
-            WordFrag<4>::unpack(wcur[m][j][1][wi], R1);
+            unpack4(wv[0][wi], R0);
+            unpack4(wv[1][wi], R1);
 #pragma unroll
             for (int hs = 0; hs < 2; ++hs) {
               const int s = 2 * wi + hs;
@@ -249,7 +353,7 @@ __global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
         } else {
 #pragma unroll
           for (int s = 0; s < STEPS; ++s) {
-            const uint32_t w0 = wcur[m][j][0][s], w1 = wcur[m][j][1][s];
+            const uint32_t w0 = wv[0][s], w1 = wv[1][s];
             const uint32_t lo[4] = {and_or(w0, 0x000F000Fu, 0x43004300u), and_or(w1, 0x000F000Fu, 0x43004300u),
                                     and_or(w0 >> 8, 0x000F000Fu, 0x43004300u),
                                     and_or(w1 >> 8, 0x000F000Fu, 0x43004300u)};
@@ -265,21 +369,23 @@ __global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
           }
         }
         // group epilogue: y += s*acc + (b - OFF*s) * sum(x)
-        const float s0 = __uint_as_float(scur[m][j][0] << 16);
-        const float s1 = __uint_as_float(scur[m][j][1] << 16);
-        const float c0 = __uint_as_float(scur[m][j][0] & 0xFFFF0000u) - OFF * s0;
-        const float c1 = __uint_as_float(scur[m][j][1] & 0xFFFF0000u) - OFF * s1;
+        const float c0 = bi[0] - OFF * sc[0];
+        const float c1 = bi[1] - OFF * sc[1];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          acc[m][nt][0] += s0 * ag[nt][0] + c0 * xsum[j][nt][0];
-          acc[m][nt][1] += s0 * ag[nt][1] + c0 * xsum[j][nt][1];
-          acc[m][nt][2] += s1 * ag[nt][2] + c1 * xsum[j][nt][0];
-          acc[m][nt][3] += s1 * ag[nt][3] + c1 * xsum[j][nt][1];
+          acc[m][nt][0] += sc[0] * ag[nt][0] + c0 * xsum[j][nt][0];
+          acc[m][nt][1] += sc[0] * ag[nt][1] + c0 * xsum[j][nt][1];
+          acc[m][nt][2] += sc[1] * ag[nt][2] + c1 * xsum[j][nt][0];
+          acc[m][nt][3] += sc[1] * ag[nt][3] + c1 * xsum[j][nt][1];
         }
       }
     }
+    // this warp is done reading stage s_idx
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s_idx]);
 
-    // ---- cross-warp reduction (fixed order) and store -----------------
+    // ---- cross-warp reduction (fixed order), double-buffered partials ------
+    float* rbuf = red + (it & 1) * L.red_buf_floats;
 #pragma unroll
     for (int m = 0; m < MAT; ++m)
 #pragma unroll
@@ -288,36 +394,28 @@ __global__ void __launch_bounds__(512, 1) qgemv_kernel(const GemvParams p) {
         for (int i = 0; i < 4; ++i) {
           const int row = r + 8 * (i >> 1);
           const int col = nt * 8 + 2 * c + (i & 1);
-          red[((warp * MAT + m) * 16 + row) * TILE_COLS + col] = acc[m][nt][i];
+          rbuf[((warp * MAT + m) * TILE_COLS + col) * RED_PITCH + row] = acc[m][nt][i];
         }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < 16 * TILE_COLS; idx += blockDim.x) {
+    named_sync(NC);
+#pragma unroll
+    for (int k = 0; k < MAX_OPT; ++k) {
+      const int idx = tid + k * NC;
+      if (idx >= OUTS) break;
       const int col = idx >> 4, row = idx & 15;
       const int64_t n = rb * 16 + row;
-      if (col < n_tok && n < p.N) {
+      if (my_orow[k] >= 0 && n < p.N) {
         float v0 = 0.f, v1 = 0.f;
         for (int w = 0; w < NW; ++w) {
-          v0 += red[((w * MAT + 0) * 16 + row) * TILE_COLS + col];
-          if constexpr (MAT == 2) v1 += red[((w * MAT + 1) * 16 + row) * TILE_COLS + col];
+          v0 += rbuf[((w * MAT + 0) * TILE_COLS + col) * RED_PITCH + row];
+          if constexpr (MAT == 2) v1 += rbuf[((w * MAT + 1) * TILE_COLS + col) * RED_PITCH + row];
         }
-        const int64_t orow = p.slots ? int64_t(p.sorted[tok_begin + col]) : int64_t(tok_begin + col);
         float v = (MAT == 2) ? silu_mul(v0, v1) : v0;
-        if (p.residual) v += __bfloat162float(p.residual[orow * p.ldo + n]);
-        p.out[orow * p.ldo + n] = __float2bfloat16_rn(v);
+        v += resid[k];
+        p.out[my_orow[k] * p.ldo + n] = __float2bfloat16_rn(v);
       }
     }
-    __syncthreads();
-#pragma unroll
-    for (int m = 0; m < MAT; ++m)
-#pragma unroll
-      for (int j = 0; j < GW; ++j)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-#pragma unroll
-          for (int v = 0; v < CW; ++v) wcur[m][j][h][v] = wnext[m][j][h][v];
-          scur[m][j][h] = snext[m][j][h];
-        }
   }
+  if (timed_out && lane == 0 && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
 }
 
 // ---- MoE plan: counting sort of assignments by expert, cut into tiles ----
@@ -452,68 +550,113 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* __restric
 }
 
 // ---- launcher ------------------------------------------------------------
-template <int BITS, int GS, int NT, int GW, int MAT>
-static int launch_gemv_cfg(const GemvParams& p, int64_t slots_grid, int NW, cudaStream_t st) {
-  const int64_t n_rb = (p.N + 15) / 16;
-  const int64_t chunks = (n_rb + p.rb_per_chunk - 1) / p.rb_per_chunk;
-  if (chunks > 0x7fffffff || slots_grid > 65535) return B2F_ERR_UNSUPPORTED;
-  const int smem = NW * MAT * 16 * 8 * NT * int(sizeof(float));
-  const dim3 grid{unsigned(chunks), unsigned(slots_grid), 1u};
-  auto kern = qgemv_kernel<BITS, GS, NT, GW, MAT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) {
-      set_last_cuda_error(e);
-      return B2F_ERR_CUDA;
-    }
+static int g_num_sms = 0;
+
+static int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      g_num_sms = n;
+    else
+      g_num_sms = 148;
   }
-  kern<<<grid, NW * 32, smem, st>>>(p);
+  return g_num_sms;
+}
+
+template <int BITS, int GS, int NT, int GW, int MAT>
+static int launch_gemv_cfg(const GemvParams& p, int64_t max_work, int NW, cudaStream_t st) {
+  constexpr int CW = (GS / 4) * BITS / 32;
+  SmemPlan L{};
+  L.row_bytes = int(p.K * BITS / 8);
+  // consecutive staged rows start 8 (32-bit loads: 4) or 16 banks apart
+  const int extra = CW * 16 < 64 ? CW * 16 : 64;
+  L.pitch = int(align_up(L.row_bytes, 128)) + extra;
+  const int G = int(p.K / GS);
+  const int sb = int(align_up(16 * G * 2, 16));
+  int o = 0;
+  for (int m = 0; m < MAT; ++m) {
+    L.off_w[m] = o;
+    o += 16 * L.pitch;
+    L.off_s[m] = o;
+    o += sb;
+    L.off_b[m] = o;
+    o += sb;
+  }
+  L.stage_bytes = int(align_up(o, 128));
+  L.red_buf_floats = NW * MAT * 8 * NT * RED_PITCH;
+  const int red_bytes = 2 * L.red_buf_floats * int(sizeof(float));
+  const int budget = 220 * 1024;
+  int stages = (budget - red_bytes - 512) / L.stage_bytes;
+  if (stages > 8) stages = 8;
+  if (stages < 2) return B2F_ERR_UNSUPPORTED;
+  L.stages = stages;
+  L.red_off = stages * L.stage_bytes;
+  L.flag_off = int(align_up(L.red_off + red_bytes, 16));
+  L.mbar_off = L.flag_off + 16;
+  const int smem = L.mbar_off + 16 * stages;
+  auto kern = qgemv_kernel<BITS, GS, NT, GW, MAT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  const int threads = (NW + 1) * 32;  // + one producer warp
+  int per_sm = 1;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  int64_t grid = int64_t(num_sms()) * per_sm;
+  if (grid > max_work) grid = max_work;
+  if (grid < 1) grid = 1;
+  kern<<<unsigned(grid), threads, smem, st>>>(p, L);
   return check_launch();
 }
 
+// Groups per warp: the smallest GW that keeps <= 8 consumer warps while the
+// activation fragments (GW*NT*GS/8 registers) stay <= 64 registers.
 template <int BITS, int GS, int NT, int MAT>
-static int launch_gemv_gw(const GemvParams& p, int64_t slots_grid, cudaStream_t st) {
+static int launch_gemv_gw(const GemvParams& p, int64_t max_work, cudaStream_t st) {
   const int G = int(p.K / GS);
-  if (G <= 16) return launch_gemv_cfg<BITS, GS, NT, 1, MAT>(p, slots_grid, G, st);
-  if (G <= 32) return launch_gemv_cfg<BITS, GS, NT, 2, MAT>(p, slots_grid, (G + 1) / 2, st);
-  if constexpr (NT == 1 && GS <= 64) {
-    if (G <= 64) return launch_gemv_cfg<BITS, GS, NT, 4, MAT>(p, slots_grid, (G + 3) / 4, st);
+  constexpr int MAXGW = (8 * 64 / GS) / NT;  // GW*NT*GS/8 <= 64
+  if (G <= 8) return launch_gemv_cfg<BITS, GS, NT, 1, MAT>(p, max_work, G, st);
+  if constexpr (MAXGW >= 2) {
+    if (G <= 16) return launch_gemv_cfg<BITS, GS, NT, 2, MAT>(p, max_work, (G + 1) / 2, st);
   }
+  if constexpr (MAXGW >= 4) {
+    if (G <= 32) return launch_gemv_cfg<BITS, GS, NT, 4, MAT>(p, max_work, (G + 3) / 4, st);
+  }
+  if constexpr (MAXGW >= 8) {
+    if (G <= 64) return launch_gemv_cfg<BITS, GS, NT, 8, MAT>(p, max_work, (G + 7) / 8, st);
+  }
+  // otherwise more warps with fewer groups each (<= 8 consumer warps still)
   return B2F_ERR_UNSUPPORTED;
 }
 
 template <int NT, int MAT>
-static int launch_gemv_nt(const GemvParams& p, int bits, int gs, int64_t slots_grid, cudaStream_t st) {
+static int launch_gemv_nt(const GemvParams& p, int bits, int gs, int64_t max_work, cudaStream_t st) {
   if (bits == 4) {
-    if (gs == 32) return launch_gemv_gw<4, 32, NT, MAT>(p, slots_grid, st);
-    if (gs == 64) return launch_gemv_gw<4, 64, NT, MAT>(p, slots_grid, st);
-    if (gs == 128) return launch_gemv_gw<4, 128, NT, MAT>(p, slots_grid, st);
+    if (gs == 32) return launch_gemv_gw<4, 32, NT, MAT>(p, max_work, st);
+    if (gs == 64) return launch_gemv_gw<4, 64, NT, MAT>(p, max_work, st);
+    if (gs == 128) return launch_gemv_gw<4, 128, NT, MAT>(p, max_work, st);
   } else if (bits == 8) {
-    if (gs == 32) return launch_gemv_gw<8, 32, NT, MAT>(p, slots_grid, st);
-    if (gs == 64) return launch_gemv_gw<8, 64, NT, MAT>(p, slots_grid, st);
-    if (gs == 128) return launch_gemv_gw<8, 128, NT, MAT>(p, slots_grid, st);
+    if (gs == 32) return launch_gemv_gw<8, 32, NT, MAT>(p, max_work, st);
+    if (gs == 64) return launch_gemv_gw<8, 64, NT, MAT>(p, max_work, st);
+    if (gs == 128) return launch_gemv_gw<8, 128, NT, MAT>(p, max_work, st);
   }
   return B2F_ERR_UNSUPPORTED;
 }
 
-static int launch_gemv(const GemvParams& p, int bits, int gs, int nt, int mat, int64_t slots_grid,
+// max_work: an upper bound on (token tiles x row blocks), used to cap the grid.
+static int launch_gemv(const GemvParams& p, int bits, int gs, int nt, int mat, int64_t max_work,
                        cudaStream_t st) {
   if (mat == 1) {
-    if (nt == 1) return launch_gemv_nt<1, 1>(p, bits, gs, slots_grid, st);
-    if (nt == 2) return launch_gemv_nt<2, 1>(p, bits, gs, slots_grid, st);
+    if (nt == 1) return launch_gemv_nt<1, 1>(p, bits, gs, max_work, st);
+    if (nt == 2) return launch_gemv_nt<2, 1>(p, bits, gs, max_work, st);
   } else {
-    if (nt == 1) return launch_gemv_nt<1, 2>(p, bits, gs, slots_grid, st);
-    if (nt == 2) return launch_gemv_nt<2, 2>(p, bits, gs, slots_grid, st);
+    if (nt == 1) return launch_gemv_nt<1, 2>(p, bits, gs, max_work, st);
+    if (nt == 2) return launch_gemv_nt<2, 2>(p, bits, gs, max_work, st);
   }
   return B2F_ERR_UNSUPPORTED;
-}
-
-// Row-blocks per CTA so that the grid has roughly `target` CTAs.
-static int pick_rb_per_chunk(int64_t n_rb, int64_t slots, int64_t target) {
-  int64_t want = (n_rb * slots + target - 1) / target;
-  if (want < 1) want = 1;
-  if (want > n_rb) want = n_rb;
-  return int(want);
 }
 
 static int check_gemv_shape(int64_t N, int64_t K, int bits, int gs) {
@@ -557,8 +700,7 @@ int b2f_qgemv_affine(const void* x, int64_t ldx, int64_t M, const uint32_t* wq, 
   p.tile = 8 * nt;
   const int64_t slots = (M + p.tile - 1) / p.tile;
   const int64_t n_rb = (N + 15) / 16;
-  p.rb_per_chunk = pick_rb_per_chunk(n_rb, slots, 148 * 2);
-  return launch_gemv(p, bits, group_size, nt, 1, slots, as_stream(stream));
+  return launch_gemv(p, bits, group_size, nt, 1, slots * n_rb, as_stream(stream));
 }
 
 int64_t b2f_moe_plan_workspace_bytes(int64_t A, int64_t E, int tile) {
@@ -628,9 +770,7 @@ int b2f_gather_qgemv_affine(const void* x, int64_t ldx, const int32_t* x_row_ind
   p.tile = tile;
   const int64_t max_slots = plan_max_slots(A, E, tile);
   const int64_t n_rb = (N + 15) / 16;
-  const int64_t exp_slots = (A < E ? A : E);
-  p.rb_per_chunk = pick_rb_per_chunk(n_rb, exp_slots, 148 * 3);
-  return launch_gemv(p, bits, group_size, tile / 8, w_up ? 2 : 1, max_slots, as_stream(stream));
+  return launch_gemv(p, bits, group_size, tile / 8, w_up ? 2 : 1, max_slots * n_rb, as_stream(stream));
 }
 
 }  // extern "C"

@@ -89,3 +89,48 @@ def test_fused_switchglu_front_half(dev):
             e = inds[t, j]
             want[t * k + j] = moe.silu(gw[e] @ x[t]) * (uw[e] @ x[t])
     assert_close(to_np(h), want, what="fused swiglu")
+
+
+@pytest.mark.parametrize("T,E,k,renorm", [(1, 128, 8, True), (64, 128, 8, True), (37, 64, 4, False)])
+def test_router_topk_matches_oracle(dev, T, E, k, renorm):
+    """softmax(x.Wr + bias) top-k with renormalisation (expert_streaming.py:439-472)."""
+    from b200flash.moe import route_topk
+
+    rng = np.random.default_rng(T + E)
+    H = 2048
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    wr = round_to(rng.normal(0, 0.02, (E, H)).astype(np.float32), "bf16")
+    bias = (-1.1 * np.log(np.arange(1, E + 1))).astype(np.float32)
+    inds, scores = route_topk(to_dev(x, "bf16", dev), to_dev(wr, "bf16", dev), k,
+                              torch.from_numpy(bias).to(dev), renorm)
+    logits = x.astype(np.float64) @ wr.T.astype(np.float64) + bias
+    g = np.exp(logits - logits.max(-1, keepdims=True))
+    g /= g.sum(-1, keepdims=True)
+    order = np.argsort(-g, axis=-1, kind="stable")[:, :k]
+    ws = np.take_along_axis(g, order, -1)
+    if renorm:
+        ws = ws / ws.sum(-1, keepdims=True)
+    gi = to_np(inds)
+    # same expert sets (order within a token by descending gate)
+    assert np.array_equal(gi, order), (gi[:2], order[:2])
+    assert_close(to_np(scores), ws, rtol=1e-4, atol=1e-5, what="router scores")
+
+
+def test_moe_block_matches_oracle(dev):
+    """Router + SwiGLU experts + weighted combine + residual vs the oracle MoE."""
+    from b200flash.moe import moe_block
+
+    rng = np.random.default_rng(21)
+    T, E, H, I, k = 9, 16, 256, 128, 4
+    g = _experts(rng, E, I, H, 4, 64)
+    u = _experts(rng, E, I, H, 4, 64)
+    d = _experts(rng, E, H, I, 4, 64)
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    wr = round_to(rng.normal(0, 0.05, (E, H)).astype(np.float32), "bf16")
+    res = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    out, inds, scores = moe_block(to_dev(x, "bf16", dev), to_dev(wr, "bf16", dev), _dev3(g, dev), _dev3(u, dev),
+                                  _dev3(d, dev), k, residual=to_dev(res, "bf16", dev))
+    oi, os_ = moe.route(x, wr.T, k)
+    assert np.array_equal(to_np(inds), oi)
+    y, _, _ = moe.expert_mlp(x, oi, os_, g, u, d)
+    assert_close(to_np(out), y + res, what="moe block")
