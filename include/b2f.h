@@ -120,6 +120,31 @@ int b2f_gather_qgemv_affine(const void* x, int64_t ldx, const int32_t* x_row_ind
                             const void* plan_workspace, int64_t plan_workspace_bytes,
                             void* out, int64_t ldo, void* stream);
 
+/* ---- (c) tcgen05/TMEM grouped GEMM (prefill and large decode tiles) ----- */
+
+/* Same contract as b2f_qgemv_affine, computed on the 5th-generation tensor
+ * cores: 128 weight rows x `tile` tokens per CTA (tile a multiple of 16,
+ * <= 256), weights dequantized to bf16 in shared memory, fp32 accumulators in
+ * tensor memory.  group_size must be 64; bits in {4,8}; K % 64 == 0.  This is
+ * mx.quantized_matmul for many tokens (prefill of QuantizedLinear,
+ * layer_quantization.py:254). */
+int b2f_qgemm_affine_tcgen05(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                             const void* scales, const void* biases, int64_t N, int64_t K,
+                             int bits, int group_size, const void* residual, void* y,
+                             int64_t ldy, int tile, void* stream);
+
+/* mx.gather_qmm on the tensor cores (expert_streaming.py:230-241 at prefill
+ * sizes): same arguments and plan as b2f_gather_qgemv_affine, with the plan
+ * built by b2f_moe_plan for the same `tile` (16..256, multiple of 16). */
+int b2f_gather_qgemm_affine_tcgen05(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                    int64_t x_row_div, int64_t A, int64_t E,
+                                    const uint32_t* w_gate, const void* s_gate,
+                                    const void* b_gate, const uint32_t* w_up, const void* s_up,
+                                    const void* b_up, int64_t N, int64_t K, int bits,
+                                    int group_size, int tile, const void* plan_workspace,
+                                    int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                    void* stream);
+
 /* ---- (a-kv) reference KV quantizer ------------------------------------ */
 
 /* Packed bytes per row and groups per row for a last axis of length D. */

@@ -40,6 +40,9 @@ SIGNATURES = {
     "b2f_moe_plan": (_I, [_P, _I64, _I64, _I, _P, _I64, _P, _P]),
     "b2f_gather_qgemv_affine": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64,
                                      _I64, _I, _I, _I, _P, _I64, _P, _I64, _P]),
+    "b2f_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I, _P, _P, _I64, _I, _P]),
+    "b2f_gather_qgemm_affine_tcgen05": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64,
+                                             _I64, _I, _I, _I, _P, _I64, _P, _I64, _P]),
     "b2f_kv_packed_len": (_I64, [_I64, _I, _I]),
     "b2f_kv_num_groups": (_I64, [_I64, _I]),
     "b2f_kv_quantize_sym": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _I64, _P, _P, _I64, _P]),

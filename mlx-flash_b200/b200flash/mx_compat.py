@@ -124,6 +124,52 @@ def _moe_tile(K, group_size):
     return 16 if K // group_size <= 32 else 8
 
 
+def tc_supported(K, group_size, bits):
+    """Shapes the tcgen05 grouped GEMM takes (group 64, K % 64 == 0)."""
+    return group_size == 64 and K % 64 == 0 and bits in (4, 8)
+
+
+def quantized_matmul_tc(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                        group_size: int = 64, bits: int = 4, residual: torch.Tensor = None,
+                        tile: int = 128) -> torch.Tensor:
+    """``x @ dequantize(w).T`` on the tcgen05 tensor cores (prefill-sized M)."""
+    dev = require_cuda(x, w, scales, biases, residual)
+    if x.dtype != torch.bfloat16 or scales.dtype != torch.bfloat16:
+        raise ValueError("bf16 activations and bf16 scales/biases required")
+    N = w.shape[-2]
+    K = w.shape[-1] * 32 // bits
+    if not tc_supported(K, group_size, bits):
+        raise ValueError("tcgen05 path needs group_size 64 and K % 64 == 0")
+    lead = tuple(x.shape[:-1])
+    M = x.numel() // K
+    xc = _capi.aligned_contiguous(x.reshape(M, K))
+    out = torch.empty(*lead, N, dtype=torch.bfloat16, device=dev)
+    res = None if residual is None else residual.reshape(M, N).contiguous()
+    call("b2f_qgemm_affine_tcgen05", ptr(xc), K, M, ptr(w.contiguous()), ptr(scales.contiguous()),
+         ptr(biases.contiguous()), N, K, bits, group_size, ptr(res), ptr(out), N, int(tile), stream_of(dev))
+    return out
+
+
+def gather_qmm_tc_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size, bits,
+                          x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None) -> torch.Tensor:
+    """Grouped GEMM over a prepared plan on the tcgen05 tensor cores (plan tile 16..256)."""
+    dev = require_cuda(x_rows, w, scales, biases, x_row_index)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    if not tc_supported(K, group_size, bits):
+        raise ValueError("tcgen05 path needs group_size 64 and K % 64 == 0")
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
+    wu = su = bu = None
+    if up is not None:
+        wu, su, bu = (t.contiguous() for t in up)
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_gather_qgemm_affine_tcgen05", ptr(xc), K, ptr(xri), int(x_row_div), plan.A, E, ptr(w.contiguous()),
+         ptr(scales.contiguous()), ptr(biases.contiguous()), ptr(wu), ptr(su), ptr(bu), N, K, bits, group_size,
+         plan.tile, ptr(plan.workspace), plan.workspace.numel(), ptr(out), N, stream_of(dev))
+    return out
+
+
 class MoEPlan:
     """Device-side grouping of assignments by expert (output of ``b2f_moe_plan``)."""
 

@@ -451,6 +451,9 @@ static PlanLayout plan_layout(int64_t A, int64_t E, int tile) {
   return L;
 }
 
+int64_t plan_slots_offset(int64_t A, int64_t E, int tile) { return plan_layout(A, E, tile).off_slots; }
+int64_t plan_sorted_offset(int64_t A, int64_t E, int tile) { return plan_layout(A, E, tile).off_sorted; }
+
 // Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
 __device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -715,7 +718,7 @@ int64_t b2f_moe_plan_max_slots(int64_t A, int64_t E, int tile) {
 
 int b2f_moe_plan(const int32_t* expert_of, int64_t A, int64_t E, int tile, void* workspace,
                  int64_t workspace_bytes, int32_t* status_out, void* stream) {
-  if (A < 0 || E <= 0 || !(tile == 8 || tile == 16 || tile == 32)) return B2F_ERR_INVALID;
+  if (A < 0 || E <= 0 || tile < 8 || tile > 256 || tile % 8 != 0) return B2F_ERR_INVALID;
   if (A > 0x3fffffff || E > 65535) return B2F_ERR_UNSUPPORTED;
   PlanLayout L = plan_layout(A, E, tile);
   if (!workspace || workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
