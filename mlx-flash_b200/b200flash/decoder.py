@@ -89,7 +89,7 @@ class Qwen3MoeDecoder:
     """Random-weight Qwen3-MoE-shaped decoder with a paged 8-bit KV cache."""
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
-                 device="cuda:0", seed: int = 0, layers=None):
+                 device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto"):
         self.s = s = shape
         self.dev = dev = torch.device(device)
         self.B = max_batch
@@ -151,7 +151,12 @@ class Qwen3MoeDecoder:
         self.inds = torch.empty(B, s.top_k, dtype=torch.int32, device=dev)
         self.scores = torch.empty(B, s.top_k, dtype=torch.float32, device=dev)
         self.gates = torch.empty(B, E, dtype=torch.float32, device=dev)
-        self.tile = 16
+        # routed experts: tcgen05 grouped GEMM once experts see >= 1 token on
+        # average, else the register-fragment GEMV (tiles of 16 tokens)
+        if moe_engine == "auto":
+            moe_engine = "tc" if A >= E else "gemv"
+        self.moe_engine = moe_engine
+        self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine == "tc" else 16
         self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
         self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
         self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -223,10 +228,11 @@ class Qwen3MoeDecoder:
             call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
                  ptr(self.plan_status), st)
             g, u, d = ly["gate"], ly["up"], ly["down"]
-            call("b2f_gather_qgemv_affine", ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
+            fn = "b2f_gather_qgemm_affine_tcgen05" if self.moe_engine == "tc" else "b2f_gather_qgemv_affine"
+            call(fn, ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
                  ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
                  ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, st)
-            call("b2f_gather_qgemv_affine", ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
+            call(fn, ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
                  0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y),
                  H, st)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm

@@ -9,9 +9,11 @@
 //   warp 0     TMA producer: 2-D tensor-map loads of the packed words of the
 //              128 rows for the chunk (32B/64B-swizzled) into a ring.
 //   warps 1-4  converters: dequantize row t of the chunk, w = q*s + b as one
-//              bf16 rounding, into a 128B-swizzled K-major A tile; gather the
-//              tile's token rows of x into the B tile (same K permutation);
-//              afterwards the epilogue (TMEM -> registers -> bf16 stores).
+//              bf16 rounding, into a 128B-swizzled K-major A tile (scales and
+//              biases fetched one chunk ahead); afterwards the epilogue
+//              (TMEM -> registers -> bf16 stores).
+//   warps 6-7  x loaders (alternate chunks): gather the tile's token rows of x
+//              for a chunk into the B tile (same K permutation), ahead of the math.
 //   warp 5     MMA issuer (one thread): tcgen05.mma kind::f16, bf16 x bf16 ->
 //              fp32 in TMEM, 4 x K16 per chunk per matrix; tcgen05.commit
 //              frees the A/B stage and finally signals the accumulators.
@@ -108,7 +110,7 @@ __device__ __forceinline__ float silu_mul_tc(float g, float u) { return g / (1.f
 __device__ __forceinline__ int sw128_off(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
 
 template <int BITS, int MAT, int TILE_N>
-__global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tm0,
+__global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tm0,
                                                          const __grid_constant__ CUtensorMap tm1) {
   constexpr int PKB = TC_KC * BITS / 8;         // packed bytes per row per chunk (32 or 64)
   constexpr int PK_TILE = TC_M * PKB;           // per matrix
@@ -161,7 +163,7 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const TcParams p, cons
       mbar_init(&pk_empty[s], 4);
     }
     for (int s = 0; s < AS; ++s) {
-      mbar_init(&ab_full[s], 4);
+      mbar_init(&ab_full[s], 5);  // 4 converter warps + the x loader warp of that chunk
       mbar_init(&ab_empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -237,12 +239,74 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const TcParams p, cons
       }
       tc_commit(acc_full);
     }
+  } else if (warp >= 6) {
+    // =========================== x loaders (warps 6, 7: alternate chunks) =====
+    // B tile: token rows of x for a chunk, K order (0,4,1,5,2,6,3,7) per 8.
+    for (int c = warp - 6; c < n_chunks; c += 2) {
+      const int s2 = c % AS;
+      if (*abort_flag) break;
+      if (c >= AS && !mbar_wait_bounded(&ab_empty[s2], uint32_t(((c / AS) - 1) & 1))) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t* brow = ab + s2 * ab_stride + MAT * A_TILE;
+      // batches of 8 16-byte vectors per lane: loads first, then permuted stores
+      for (int base = 0; base < n_pad * 8; base += 256) {
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int idx = base + lane + 32 * i;
+          const int n = idx >> 3, j = idx & 7;
+          v[i] = make_uint4(0u, 0u, 0u, 0u);
+          if (n < n_tok) v[i] = *reinterpret_cast<const uint4*>(p.x + xrow[n] * p.ldx + int64_t(c) * TC_KC + 8 * j);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int idx = base + lane + 32 * i;
+          const int n = idx >> 3, j = idx & 7;
+          if (n < n_pad) {
+            const uint4 xv = v[i];
+            *reinterpret_cast<uint4*>(brow + sw128_off(n, j)) =
+                make_uint4(prmt(xv.x, xv.z, 0x5410u), prmt(xv.x, xv.z, 0x7632u), prmt(xv.y, xv.w, 0x5410u),
+                           prmt(xv.y, xv.w, 0x7632u));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ab_full[s2]);
+    }
   } else {
     // =========================== converters (warps 1-4) ========================
     const int t = tid - 32;  // weight row within the tile (0..127)
     const int64_t grow = m0 + t;
     const bool row_ok = grow < p.N;
+    const int64_t sb_row = int64_t(expert) * p.sb_estride + grow * (p.K / 64);
+    // scales/biases fetched two chunks ahead (raw bf16 bits)
+    uint16_t sq[3][MAT], bq[3][MAT];
+    const uint16_t* sp[MAT];
+    const uint16_t* bp[MAT];
+#pragma unroll
+    for (int m = 0; m < MAT; ++m) {
+      sp[m] = reinterpret_cast<const uint16_t*>(p.s[m]) + sb_row;
+      bp[m] = reinterpret_cast<const uint16_t*>(p.b[m]) + sb_row;
+#pragma unroll
+      for (int d = 0; d < 2; ++d) {
+        sq[d][m] = (row_ok && d < n_chunks) ? sp[m][d] : uint16_t(0);
+        bq[d][m] = (row_ok && d < n_chunks) ? bp[m][d] : uint16_t(0);
+      }
+    }
     for (int c = 0; c < n_chunks; ++c) {
+      float csc[MAT], cbi[MAT];
+#pragma unroll
+      for (int m = 0; m < MAT; ++m) {
+        csc[m] = __uint_as_float(uint32_t(sq[0][m]) << 16);
+        cbi[m] = __uint_as_float(uint32_t(bq[0][m]) << 16);
+        sq[0][m] = sq[1][m];
+        bq[0][m] = bq[1][m];
+        sq[1][m] = (row_ok && c + 2 < n_chunks) ? sp[m][c + 2] : uint16_t(0);
+        bq[1][m] = (row_ok && c + 2 < n_chunks) ? bp[m][c + 2] : uint16_t(0);
+      }
       const int s1 = c % PS, s2 = c % AS;
       if (*abort_flag) break;
       if (!mbar_wait_bounded(&pk_full[s1], uint32_t((c / PS) & 1)) ||
@@ -253,12 +317,7 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const TcParams p, cons
       uint8_t* st = ab + s2 * ab_stride;
 #pragma unroll
       for (int m = 0; m < MAT; ++m) {
-        float sc = 0.f, bi = 0.f;
-        if (row_ok) {
-          const int64_t e0 = int64_t(expert) * p.sb_estride + grow * (p.K / 64) + c;
-          sc = __bfloat162float(p.s[m][e0]);
-          bi = __bfloat162float(p.b[m][e0]);
-        }
+        const float sc = csc[m], bi = cbi[m];
         const uint32_t s2v = pack_bf16x2(sc, sc), b2v = pack_bf16x2(bi, bi);
         const uint8_t* prow = pk + (s1 * MAT + m) * PK_TILE + t * PKB;
         const int sw = (t * PKB >> 7) & PK_SW_MASK;  // TMA swizzle of this row
@@ -301,18 +360,6 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const TcParams p, cons
             }
           }
         }
-      }
-      // B tile: token rows of x for this chunk, K order (0,4,1,5,2,6,3,7) per 8
-      uint8_t* brow = st + MAT * A_TILE;
-      for (int idx = t; idx < n_pad * 8; idx += 128) {
-        const int n = idx >> 3, j = idx & 7;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (n < n_tok) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(p.x + xrow[n] * p.ldx + int64_t(c) * TC_KC + 8 * j);
-          v = make_uint4(prmt(xv.x, xv.z, 0x5410u), prmt(xv.x, xv.z, 0x7632u), prmt(xv.y, xv.w, 0x5410u),
-                         prmt(xv.y, xv.w, 0x7632u));
-        }
-        *reinterpret_cast<uint4*>(brow + sw128_off(n, j)) = v;
       }
       fence_proxy_async_smem();  // generic-proxy stores -> tensor-core reads
       __syncwarp();
@@ -398,10 +445,12 @@ static int launch_tc_cfg(TcParams p, const CUtensorMap& m0, const CUtensorMap& m
   constexpr int PK_TILE = TC_M * TC_KC * BITS / 8;
   constexpr int A_TILE = TC_M * TC_KC * 2;
   constexpr int B_TILE = TILE_N * TC_KC * 2;
-  const int budget = 200 * 1024;
+  // two CTAs per SM when the tiles allow it (each ~110 KB), else one larger CTA
   const int ab_stride = MAT * A_TILE + B_TILE;
-  int AS = 3, PS = 4;
-  while (AS > 2 && PS * MAT * PK_TILE + AS * ab_stride > budget) --AS;
+  int budget = 108 * 1024;
+  if (4 * MAT * PK_TILE + 2 * ab_stride > budget) budget = 200 * 1024;
+  int AS = 3, PS = 12;
+  while (AS > 2 && 4 * MAT * PK_TILE + AS * ab_stride > budget) --AS;
   while (PS > 2 && PS * MAT * PK_TILE + AS * ab_stride > budget) --PS;
   p.ab_stages = AS;
   p.pk_stages = PS;
@@ -414,7 +463,7 @@ static int launch_tc_cfg(TcParams p, const CUtensorMap& m0, const CUtensorMap& m
     return B2F_ERR_CUDA;
   }
   const dim3 grid{unsigned((p.N + TC_M - 1) / TC_M), unsigned(slots_grid), 1u};
-  kern<<<grid, 192, smem, st>>>(p, m0, m1);
+  kern<<<grid, 256, smem, st>>>(p, m0, m1);
   return check_launch();
 }
 
