@@ -249,7 +249,7 @@ int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t H
 /* Router of the MoE block (expert_streaming.py:439-472): gates =
  * softmax(x.wr^T + bias), top-k (ties to the lower id), scores = gates of the
  * top-k, renormalised to sum 1 if renorm.  x bf16 [T,H] (H % 8 == 0); wr bf16
- * [E,H]; bias f32 [E] or NULL; logits_ws f32 [T,E] caller workspace (holds the
+ * [E,H] (E <= 256); bias f32 [E] or NULL; logits_ws f32 [T,E] caller workspace (holds the
  * gates afterwards); inds int32 [T,k]; scores f32 [T,k]. */
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
                        int64_t E, int64_t k, int renorm, float* logits_ws, int32_t* inds,

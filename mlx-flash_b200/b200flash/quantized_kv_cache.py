@@ -141,11 +141,12 @@ def decode_attention(q: torch.Tensor, k_pages: torch.Tensor, k_scales: torch.Ten
 
 
 def pick_splits(B: int, Hkv: int, max_len: int, sms: int = 148) -> int:
-    """Context splits so that B*Hkv*splits CTAs cover the SMs ~4 times over."""
+    """Context splits: about two CTAs per SM, at least 1024 tokens per split
+    (longer per-warp streams beat more, shorter CTAs on B200)."""
     if max_len <= 0:
         return 1
-    want = max(1, (4 * sms + B * Hkv - 1) // max(1, B * Hkv))
-    cap = max(1, (max_len + 255) // 256)  # keep >= 256 tokens per split
+    want = max(1, (2 * sms + B * Hkv - 1) // max(1, B * Hkv))
+    cap = max(1, max_len // 1024)
     return int(min(want, cap, 64))
 
 

@@ -200,6 +200,7 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* 
 #pragma unroll
   for (int t = 0; t < 8; ++t) acc[t] = 0.f;
   const __nv_bfloat16* wrow = wr + int64_t(e) * H;
+#pragma unroll 4
   for (int h = lane * 8; h < H; h += 256) {
     const uint4 wv = *reinterpret_cast<const uint4*>(wrow + h);
     const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
@@ -227,7 +228,10 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* 
 }
 
 // gates = softmax(logits[t]); top-k by value (ties -> lower id); scores are the
-// gates of the top-k, optionally renormalised to sum 1.  One warp per token.
+// gates of the top-k, optionally renormalised to sum 1.  One warp per token;
+// the E <= 256 logits live in registers (8 per lane).
+constexpr int TOPK_PER_LANE = 8;
+
 __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
                                                          int renorm, int32_t* __restrict__ inds,
                                                          float* __restrict__ scores) {
@@ -235,26 +239,38 @@ __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ log
   const int t = blockIdx.x * 8 + warp;
   if (t >= T) return;
   float* lg = logits + int64_t(t) * E;
+  float v[TOPK_PER_LANE];
   float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+  for (int i = 0; i < TOPK_PER_LANE; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, v[i]);
+  }
   mx = warp_max<32>(mx);
   float sum = 0.f;
-  for (int e = lane; e < E; e += 32) {
-    const float g = expf(lg[e] - mx);
-    lg[e] = g;
-    sum += g;
+#pragma unroll
+  for (int i = 0; i < TOPK_PER_LANE; ++i) {
+    const int e = lane + 32 * i;
+    v[i] = e < E ? expf(v[i] - mx) : -1.f;
+    sum += e < E ? v[i] : 0.f;
   }
   sum = warp_sum<32>(sum);
-  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < TOPK_PER_LANE; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) lg[e] = v[i] / sum;  // leave the gates in the workspace
+  }
   float picked = 0.f, my_score = 0.f;
-  const int64_t base = int64_t(t) * k;
+  int my_ind = 0;
   for (int j = 0; j < k; ++j) {
     float bv = -1.f;
     int bi = 0x7fffffff;
-    for (int e = lane; e < E; e += 32) {
-      const float g = lg[e];
-      if (g > bv || (g == bv && e < bi)) {
-        bv = g;
+#pragma unroll
+    for (int i = 0; i < TOPK_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      if (v[i] > bv || (v[i] == bv && e < bi)) {
+        bv = v[i];
         bi = e;
       }
     }
@@ -268,15 +284,22 @@ __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ log
       }
     }
     const float sc = bv / sum;
-    if (lane == j) my_score = sc;
-    if (lane == 0) {
-      inds[base + j] = bi;
-      lg[bi] = -2.f;  // remove from the candidates
+    if (lane == j) {
+      my_score = sc;
+      my_ind = bi;
+    }
+    // the owner lane drops the winner from its candidates
+    if ((bi & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < TOPK_PER_LANE; ++i)
+        if (lane + 32 * i == bi) v[i] = -2.f;
     }
     picked += sc;
-    __syncwarp();
   }
-  if (lane < k) scores[base + lane] = renorm ? my_score / picked : my_score;
+  if (lane < k) {
+    inds[int64_t(t) * k + lane] = my_ind;
+    scores[int64_t(t) * k + lane] = renorm ? my_score / picked : my_score;
+  }
 }
 
 __global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
@@ -400,6 +423,7 @@ int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t H
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
                        int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, void* stream) {
   if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+  if (E > 32 * TOPK_PER_LANE) return B2F_ERR_UNSUPPORTED;
   if (H % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (T == 0) return B2F_OK;
   if (!x || !wr || !logits_ws || !inds || !scores) return B2F_ERR_INVALID;

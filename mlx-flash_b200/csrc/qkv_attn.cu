@@ -127,18 +127,19 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
 
-  for (int sub = sub_begin + warp; sub < sub_end; sub += 4) {
+  // K for tokens r and 8+r, V for tokens 2c,2c+1,8+2c,9+2c of one sub-tile
+  struct Tile {
+    uint32_t kw[2][DG][KW];
+    float ksc[2][2][DG];
+    uint32_t vw[4][DG][VW];
+    float vsc[4][DG];
+  };
+  auto load_tile = [&](int sub, Tile& T) {
     const int t0 = sub * 16;
     const int page = p.block_table[int64_t(b) * p.max_pages + t0 / p.PS];
     // row of token t0; token t0+i is at rowbase + i*slot_stride
     const int64_t rowbase = int64_t(page) * p.Hkv * p.PS + hkv * p.head_stride + (t0 % p.PS) * p.slot_stride;
     const int64_t ss = p.slot_stride;
-
-    // ---- loads: K for tokens r and 8+r, V for tokens 2c,2c+1,8+2c,9+2c --
-    uint32_t kw[2][DG][KW];
-    float ksc[2][2][DG];
-    uint32_t vw[4][DG][VW];
-    float vsc[4][DG];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       const uint8_t* krow = p.kp + (rowbase + (nt * 8 + r) * ss) * RB;
@@ -146,14 +147,14 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
       for (int g = 0; g < DG; ++g) {
         if constexpr (BITS == 8) {
           const uint4 q = *reinterpret_cast<const uint4*>(krow + 64 * g + 16 * c);
-          kw[nt][g][0] = q.x;
-          kw[nt][g][1] = q.y;
-          kw[nt][g][2] = q.z;
-          kw[nt][g][3] = q.w;
+          T.kw[nt][g][0] = q.x;
+          T.kw[nt][g][1] = q.y;
+          T.kw[nt][g][2] = q.z;
+          T.kw[nt][g][3] = q.w;
         } else {
           const uint2 q = *reinterpret_cast<const uint2*>(krow + 32 * g + 8 * c);
-          kw[nt][g][0] = q.x;
-          kw[nt][g][1] = q.y;
+          T.kw[nt][g][0] = q.x;
+          T.kw[nt][g][1] = q.y;
         }
       }
 #pragma unroll
@@ -161,7 +162,7 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
         const int tok = nt * 8 + 2 * c + e;
         const bool tv = t0 + tok < len;
 #pragma unroll
-        for (int g = 0; g < DG; ++g) ksc[nt][e][g] = tv ? p.ks[(rowbase + tok * ss) * DG + g] : 0.f;
+        for (int g = 0; g < DG; ++g) T.ksc[nt][e][g] = tv ? p.ks[(rowbase + tok * ss) * DG + g] : 0.f;
       }
     }
 #pragma unroll
@@ -173,14 +174,26 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
       for (int g = 0; g < DG; ++g) {
         if constexpr (BITS == 8) {
           const uint2 q = *reinterpret_cast<const uint2*>(vrow + 64 * g + 8 * r);
-          vw[t][g][0] = q.x;
-          vw[t][g][1] = q.y;
+          T.vw[t][g][0] = q.x;
+          T.vw[t][g][1] = q.y;
         } else {
-          vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vrow + 32 * g + 4 * r);
+          T.vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vrow + 32 * g + 4 * r);
         }
-        vsc[t][g] = tv ? p.vs[(rowbase + tok * ss) * DG + g] : 0.f;
+        T.vsc[t][g] = tv ? p.vs[(rowbase + tok * ss) * DG + g] : 0.f;
       }
     }
+  };
+
+  Tile nxt;
+  if (sub_begin + warp < sub_end) load_tile(sub_begin + warp, nxt);
+  for (int sub = sub_begin + warp; sub < sub_end; sub += 4) {
+    const int t0 = sub * 16;
+    const Tile cur = nxt;  // this sub-tile; the next one is loaded while it is computed
+    if (sub + 4 < sub_end) load_tile(sub + 4, nxt);
+    const auto& kw = cur.kw;
+    const auto& ksc = cur.ksc;
+    const auto& vw = cur.vw;
+    const auto& vsc = cur.vsc;
 
     // ---- S = Q.K^T -------------------------------------------------------
     float s[2][4];
