@@ -145,7 +145,7 @@ def pick_splits(B: int, Hkv: int, max_len: int, sms: int = 148) -> int:
     (longer per-warp streams beat more, shorter CTAs on B200)."""
     if max_len <= 0:
         return 1
-    want = max(1, (2 * sms + B * Hkv - 1) // max(1, B * Hkv))
+    want = max(1, (2 * sms) // max(1, B * Hkv))
     cap = max(1, max_len // 1024)
     return int(min(want, cap, 64))
 
