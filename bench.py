@@ -43,16 +43,17 @@ def load_peaks():
 
 
 def workload_name(args):
-    return (f"Qwen3-30B-A3B-shaped decoder decode step: 48 layers, 32q/4kv heads d128, 128 experts top-8 "
+    return (f"Qwen3-30B-A3B-shaped decoder decode step: {args.layers} layers, 32q/4kv heads d128, 128 experts top-8 "
             f"(H 2048, I 768), 4-bit g64 weights, 8-bit g64 KV, batch {args.batch}, context {args.ctx}")
 
 
 def config_dict(args, world):
     return {"workload": workload_name(args), "batch_per_gpu": args.batch, "global_batch": args.batch * world,
-            "context": args.ctx, "layers": 48, "weights": "4-bit affine g64 (N(0,0.02) random init)",
+            "context": args.ctx, "layers": args.layers, "weights": "4-bit affine g64 (N(0,0.02) random init)",
             "kv_cache": "8-bit sym g64, paged (64-token pages)", "routing": "softmax top-8, Zipf(1.1) popularity",
             "l2_policy": "inputs larger than L2 (weights ~17 GB, KV ~7 GB), no flush",
-            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"}
+            "parallelism": (f"ep{world} experts (NCCL all-gather dispatch / reduce-scatter combine), "
+                            f"dp{world} attention") if world > 1 else "1 GPU"}
 
 
 # ---------------------------------------------------------------------------
@@ -153,18 +154,26 @@ def profile_kernels(dec, torch):
 
         def route_and_keep(name, *args):
             rc = orig_route(name, *args)
-            if name == "b2f_moe_route_topk":
+            if name == "b2f_moe_route_topk" and dec.ep is None:
                 routed.append(dec.inds.clone())
+            elif name == "b2f_ep_plan":
+                loc = dec.ep.local.clone()
+                routed.append(loc[loc >= 0])
             return rc
 
+        import b200flash.ep as epmod
+
         dmod.call = route_and_keep
+        epmod.call = route_and_keep
         dec.step()
     finally:
         dmod.call = orig_call
+        epmod.call = orig_call
     torch.cuda.synchronize()
     for tag, e0, e1 in pending:
         timings[tag].append(e0.elapsed_time(e1) * 1e-3)
-    distinct = [int(torch.unique(r).numel()) for r in routed]
+    # per layer: distinct experts this rank computes, and its assignments
+    distinct = [(int(torch.unique(r).numel()), int(r.numel())) for r in routed]
     return timings, distinct
 
 
@@ -190,11 +199,15 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     from b200flash.decoder import Qwen3MoeDecoder, Qwen3MoeShape
+    from b200flash.ep import EPExchange
 
     shape = Qwen3MoeShape()
     max_ctx = args.ctx + args.warmup * 3 + args.steps * 3 + 8
+    # N > 1: experts sharded expert-parallel (ExpertShard blocks), attention,
+    # router and lm_head data-parallel over each rank's own batch
+    exchange = EPExchange() if world > 1 else None
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
-                          seed=1234 + rank)
+                          seed=1234, layers=args.layers, exchange=exchange)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -221,11 +234,15 @@ def run_ours(args):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        if args.profile_window:
+            torch.cuda.profiler.start()
         e0.record()
         for _ in range(args.steps):
             graph.replay()
         e1.record()
         torch.cuda.synchronize()
+        if args.profile_window:
+            torch.cuda.profiler.stop()
     barrier()
     t = e0.elapsed_time(e1) * 1e-3
     t_max = t
@@ -262,9 +279,8 @@ def run_ours(args):
     timings, distinct = profile_kernels(dec, torch)
     peak, peak_kind = load_peaks()
     per_exp = moe_bytes_per_expert(shape)
-    A = args.batch * shape.top_k
-    gu_bytes = [2 * u * per_exp + args.batch * shape.hidden * 2 + A * shape.moe_inter * 2 for u in distinct]
-    dn_bytes = [u * per_exp + A * shape.moe_inter * 2 + A * shape.hidden * 2 for u in distinct]
+    gu_bytes = [2 * u * per_exp + a * shape.hidden * 2 + a * shape.moe_inter * 2 for u, a in distinct]
+    dn_bytes = [u * per_exp + a * shape.moe_inter * 2 + a * shape.hidden * 2 for u, a in distinct]
     ctx_now = int(dec.positions[0].item())
     at_bytes = attention_bytes(dec, ctx_now)
     kernels = {}
@@ -280,7 +296,8 @@ def run_ours(args):
     roofline = {"kernel": dom, "bound": "hbm", "achieved": round(d["gbs"], 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
                 "traffic": None, "bytes_per_launch": int(d["bytes_per_launch"]),
-                "avg_launch_us": round(d["avg_us"], 2), "distinct_experts_per_layer": round(sum(distinct) / len(distinct), 1)}
+                "avg_launch_us": round(d["avg_us"], 2),
+                "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / len(distinct), 1)}
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * t_max / args.steps, 4), "higher_is_better": True,
@@ -422,6 +439,11 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=48,
+                    help="decoder depth; anything but 48 is a profiling case, not a bench line")
+    ap.add_argument("--profile-window", action="store_true",
+                    help="bracket the timed replays with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

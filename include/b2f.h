@@ -222,13 +222,45 @@ int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const flo
                                 int64_t slot_stride, int bits, int group_size,
                                 float softmax_scale, int n_splits, void* out, void* stream);
 
+/* ---- (e) expert parallelism: device halves of dispatch / combine -------- */
+
+/* Replaces the expert-to-rank routing of distributed_experts.py:36-80
+ * (ExpertShard.owner_of / DistributedExpertManager) for HBM-resident
+ * experts.  `recv` holds W gathered routing segments of seg_bytes each (one
+ * per rank, in rank order; the output of an all-gather).  Segment r: T
+ * bf16 rows of the normalised hidden state, row pitch row_bytes, at byte 0;
+ * int32 top-k expert ids [T, k] at inds_off; float32 scores [T, k] at
+ * scores_off.  Assignment a = (r*T + t)*k + j.  This rank owns the global
+ * experts [e_begin, e_begin + e_count) of e_total.  Writes a plan over the
+ * local experts (same workspace format and size as b2f_moe_plan with
+ * A = W*T*k, E = e_count) plus, per assignment: x_row[a] = the assignment's
+ * row in `recv` viewed as bf16 [W*seg_bytes/row_bytes, row_bytes/2];
+ * wts[a] = its score, or 0 if another rank owns the expert; local[a] = its
+ * local expert id, or -1.  Ids outside [0, e_total) set B2F_ERR_INVALID in
+ * status_out (device int32, may be NULL). */
+int b2f_ep_plan(const void* recv, int64_t seg_bytes, int64_t row_bytes, int64_t inds_off,
+                int64_t scores_off, int64_t W, int64_t T, int64_t k, int64_t e_begin,
+                int64_t e_count, int64_t e_total, int tile, int32_t* x_row, float* wts,
+                int32_t* local, void* workspace, int64_t workspace_bytes,
+                int32_t* status_out, void* stream);
+
+/* Per gathered token g < G: out[g, :] = bf16(sum_j wts[g*k+j] * y[g*k+j, :])
+ * over the j with local[g*k+j] >= 0 (this rank's share of the weighted
+ * expert sum at expert_streaming.py:464-470; 0 where the token has no local
+ * expert).  A sum over ranks of `out` (a reduce-scatter) completes the MoE
+ * output.  bf16 y [G*k, ldy], out [G, ldo]; H % 8 == 0. */
+int b2f_ep_combine_partial(const void* y, int64_t ldy, const float* wts, const int32_t* local,
+                           int64_t G, int64_t k, int64_t H, void* out, int64_t ldo, void* stream);
+
 /* ---- decode-step glue around the hot path (Qwen3-MoE-shaped decoder) ----- */
 
 /* MoE combine + residual + RMSNorm in one pass (expert_streaming.py:464-470
  * `y = (y * scores[..., None]).sum(-2)` and the shared-expert add, then the
  * next RMSNorm):  h = resid + sum_j scores[m,j] * y[m*k+j];  resid_out =
  * bf16(h); norm_out = bf16(weight * h * rsqrt(mean(h^2) + eps)).  y may be
- * NULL (plain RMSNorm).  resid_out may alias resid.  H % 8 == 0, H <= 8192. */
+ * NULL (plain RMSNorm); scores may be NULL (every score 1, e.g. k = 1 for an
+ * already combined expert-parallel output).  resid_out may alias resid.
+ * H % 8 == 0, H <= 8192. */
 int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M,
                         int64_t k, const void* weight, float eps, int64_t H, void* resid_out,
                         void* norm_out, void* stream);

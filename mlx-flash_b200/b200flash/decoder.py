@@ -17,6 +17,13 @@ per layer (B sequences, one new token each)
   h    += sum_k score_k y_k ; xn = RMSNorm(h)           b2f_combine_rmsnorm
 then logits = quantized_matmul(xn, lm_head), next = argmax.
 
+With an ``EPExchange`` over W > 1 ranks the routed experts are sharded
+expert-parallel (``b200flash.ep``): each rank holds the ExpertShard block of
+every layer's experts, runs attention, router and lm_head for its own B
+sequences, and the plan/experts/combine lines above become all-gather of
+the routing segments -> b2f_ep_plan -> local experts ->
+b2f_ep_combine_partial -> reduce-scatter -> b2f_combine_rmsnorm (k = 1).
+
 Every buffer is allocated once, so ``step()`` can be captured in a CUDA graph.
 Weights are random (N(0, 0.02) before 4-bit quantization) with the model's
 shapes; the router adds a per-expert logit bias log(p_e) with p Zipf(s) so
@@ -30,6 +37,8 @@ import torch
 
 from . import _capi
 from ._capi import call, ptr
+from .distributed_experts import ExpertShard
+from .ep import ExpertParallelMoE
 from .quantized_kv_cache import packed_len, pick_splits
 
 
@@ -89,7 +98,7 @@ class Qwen3MoeDecoder:
     """Random-weight Qwen3-MoE-shaped decoder with a paged 8-bit KV cache."""
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
-                 device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto"):
+                 device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None):
         self.s = s = shape
         self.dev = dev = torch.device(device)
         self.B = max_batch
@@ -98,6 +107,15 @@ class Qwen3MoeDecoder:
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
         H, D, Hq, Hkv, E, I = s.hidden, s.head_dim, s.n_heads, s.n_kv_heads, s.n_experts, s.moe_inter
+        # expert parallelism: this rank's block of every layer's experts
+        self.world = 1 if exchange is None else exchange.world
+        self.shard = ExpertShard(rank=0 if exchange is None else exchange.rank, world_size=self.world,
+                                 total_experts=E)
+        E_loc = len(self.shard.owned_experts)
+        egen = gen
+        if self.world > 1:
+            egen = torch.Generator(device=dev)
+            egen.manual_seed(seed + 1000003 * (self.shard.rank + 1))
         bits, gs = s.bits, s.group_size
         self.qkv_rows = (Hq + 2 * Hkv) * D
 
@@ -117,9 +135,9 @@ class Qwen3MoeDecoder:
                 "wo": random_qweight((H, Hq * D), bits, gs, dev, gen),
                 "wr": (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16),
                 "rbias": zipf[perm].contiguous(),
-                "gate": random_qweight((E, I, H), bits, gs, dev, gen),
-                "up": random_qweight((E, I, H), bits, gs, dev, gen),
-                "down": random_qweight((E, H, I), bits, gs, dev, gen),
+                "gate": random_qweight((E_loc, I, H), bits, gs, dev, egen),
+                "up": random_qweight((E_loc, I, H), bits, gs, dev, egen),
+                "down": random_qweight((E_loc, H, I), bits, gs, dev, egen),
             })
         self.final_norm = norm_w(H)
         self.lm_head = random_qweight((s.vocab, H), bits, gs, dev, gen)
@@ -144,24 +162,35 @@ class Qwen3MoeDecoder:
         self.positions = torch.zeros(B, dtype=torch.int32, device=dev)
         self.seq_lens = torch.zeros(B, dtype=torch.int32, device=dev)
         self.h = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
-        self.xn = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
+        self.ep = None
+        if self.world > 1:
+            self.ep = ExpertParallelMoE(self.shard, B, H, I, s.top_k, dev, bits, gs, exchange,
+                                        engine=moe_engine)
+            self.moe_engine = self.ep.engine
+        self.xn = torch.empty(B, H, dtype=torch.bfloat16, device=dev) if self.ep is None else self.ep.x
         self.qkv = torch.empty(B, self.qkv_rows, dtype=torch.bfloat16, device=dev)
         self.q = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
         self.attn = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
-        self.inds = torch.empty(B, s.top_k, dtype=torch.int32, device=dev)
-        self.scores = torch.empty(B, s.top_k, dtype=torch.float32, device=dev)
+        if self.ep is None:
+            self.inds = torch.empty(B, s.top_k, dtype=torch.int32, device=dev)
+            self.scores = torch.empty(B, s.top_k, dtype=torch.float32, device=dev)
+        else:
+            self.inds, self.scores = self.ep.inds, self.ep.scores
         self.gates = torch.empty(B, E, dtype=torch.float32, device=dev)
         # routed experts: tcgen05 grouped GEMM once experts see >= 1 token on
         # average, else the register-fragment GEMV (tiles of 16 tokens)
-        if moe_engine == "auto":
-            moe_engine = "tc" if A >= E else "gemv"
-        self.moe_engine = moe_engine
-        self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine == "tc" else 16
-        self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
-        self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
-        self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.hh = torch.empty(A, I, dtype=torch.bfloat16, device=dev)
-        self.y = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+        if self.ep is None:
+            if moe_engine == "auto":
+                moe_engine = "tc" if A >= E else "gemv"
+            self.moe_engine = moe_engine
+            self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine == "tc" else 16
+            self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
+            self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
+            self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.hh = torch.empty(A, I, dtype=torch.bfloat16, device=dev)
+            self.y = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+        else:
+            self.tile = self.ep.tile
         self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
         self.next_tokens = torch.empty(B, dtype=torch.int32, device=dev)
         self.n_splits = pick_splits(B, Hkv, max_context)
@@ -223,11 +252,19 @@ class Qwen3MoeDecoder:
                  w.bits, w.group_size, ptr(self.h), ptr(self.h), H, st)
             call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
                  ptr(self.xn), st)
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm
+            g, u, d = ly["gate"], ly["up"], ly["down"]
+            if self.ep is not None:
+                self.ep.route(ly["wr"], ly["rbias"], s.norm_topk)
+                y = self.ep.forward((g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases),
+                                    (d.wq, d.scales, d.biases))
+                call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), 0, B, 1, ptr(nxt), s.rms_eps, H, ptr(self.h),
+                     ptr(self.xn), st)
+                continue
             call("b2f_moe_route_topk", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), st)
             call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
                  ptr(self.plan_status), st)
-            g, u, d = ly["gate"], ly["up"], ly["down"]
             fn = "b2f_gather_qgemm_affine_tcgen05" if self.moe_engine == "tc" else "b2f_gather_qgemv_affine"
             call(fn, ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
                  ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
@@ -235,7 +272,6 @@ class Qwen3MoeDecoder:
             call(fn, ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
                  0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y),
                  H, st)
-            nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm
             call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.y), ptr(self.scores), B, s.top_k, ptr(nxt),
                  s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
         w = self.lm_head
@@ -249,5 +285,8 @@ class Qwen3MoeDecoder:
     def launches_per_step(self) -> int:
         """libb200flash kernel launches in one step (attention counts its combine pass)."""
         attn = 2 if self.n_splits > 1 else 1
-        per_layer = 1 + 1 + attn + 1 + 1 + 2 + 1 + 1 + 1 + 1
+        # qkv, rope+append, attention, o_proj, norm, router, plan, gate/up, down, combine
+        per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 2 + 1
+        if self.ep is not None:
+            per_layer += 1  # the partial-sum kernel before the reduce-scatter
         return 2 + self.L * per_layer + 2

@@ -1,0 +1,220 @@
+"""Expert-parallel routed MoE over NCCL (one process per GPU).
+
+Replaces the reference's distributed-expert plan
+(``mlx_flash_compress/distributed_experts.py:36-150``: contiguous expert
+blocks per rank, ``owner_of``) and the expert-streaming tiers
+(``expert_streaming.py``) for the case where every expert is resident in some
+GPU's HBM.  Ownership follows ``ExpertShard`` exactly.
+
+Per MoE block, on every rank (T tokens each, attention and router run on the
+rank's own tokens):
+
+1. the rank's *routing segment* -- its normalised hidden rows, top-k expert
+   ids and scores, laid out back to back in one byte buffer -- is gathered
+   onto every rank (``all_gather_into_tensor``: one NCCL call);
+2. ``b2f_ep_plan`` sorts the ``W*T*k`` gathered assignments by local expert
+   (experts of other ranks skipped) and records each assignment's x row in
+   the gathered buffer;
+3. the grouped expert kernels (tcgen05 GEMM or register GEMV) run on the
+   local expert shard, reading x rows in place from the gathered segments;
+4. ``b2f_ep_combine_partial`` forms every gathered token's score-weighted sum
+   over its local experts;
+5. ``reduce_scatter_tensor`` (sum) returns to each rank the sum over ranks of
+   its own tokens' partials -- the complete MoE output.
+
+All buffers are allocated once, so the block (collectives included) can be
+captured in a CUDA graph.  No TMA multicast is used anywhere on this path.
+"""
+
+import torch
+import torch.distributed as dist
+
+from . import _capi
+from ._capi import call, ptr, require_cuda, stream_of
+from .distributed_experts import ExpertShard
+
+
+def _align(v: int, a: int) -> int:
+    return (v + a - 1) // a * a
+
+
+class RoutingSegment:
+    """Byte layout of one rank's routing segment (T tokens, hidden H, top-k).
+
+    ``[0, T*2H)``: bf16 x rows (row pitch ``2H`` bytes); ``inds_off``: int32
+    ``[T, k]`` expert ids; ``scores_off``: float32 ``[T, k]``.  The segment is
+    padded to a whole number of x rows so gathered segments stay one bf16
+    matrix of ``W * seg_rows`` rows.
+    """
+
+    def __init__(self, T: int, H: int, k: int):
+        if H % 8:
+            raise ValueError("hidden size must be a multiple of 8")
+        self.T, self.H, self.k = T, H, k
+        self.row_bytes = 2 * H
+        self.inds_off = T * self.row_bytes
+        self.scores_off = self.inds_off + 4 * T * k
+        self.seg_bytes = _align(self.scores_off + 4 * T * k, self.row_bytes)
+        self.seg_rows = self.seg_bytes // self.row_bytes
+
+    def views(self, buf: torch.Tensor, r: int = 0):
+        """(x bf16 [T,H], inds int32 [T,k], scores f32 [T,k]) views of segment r of ``buf``."""
+        base = r * self.seg_bytes
+        T, H, k = self.T, self.H, self.k
+        x = buf[base: base + T * self.row_bytes].view(torch.bfloat16).view(T, H)
+        inds = buf[base + self.inds_off: base + self.inds_off + 4 * T * k].view(torch.int32).view(T, k)
+        scores = buf[base + self.scores_off: base + self.scores_off + 4 * T * k].view(torch.float32).view(T, k)
+        return x, inds, scores
+
+
+class EPExchange:
+    """The two collectives of the expert-parallel MoE over a process group.
+
+    NCCL groups use ``all_gather_into_tensor`` / ``reduce_scatter_tensor``
+    directly.  Gloo has no reduce-scatter, so on a CPU group the combine is an
+    ``all_reduce`` followed by taking this rank's slice (same result).
+    """
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.backend = dist.get_backend(group)
+
+    def all_gather(self, recv: torch.Tensor, send: torch.Tensor):
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+
+    def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor):
+        if self.backend == "nccl":
+            dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            tmp = inp.clone()
+            dist.all_reduce(tmp, op=dist.ReduceOp.SUM, group=self.group)
+            out.copy_(tmp.view(self.world, *out.shape)[self.rank])
+
+
+class ExpertParallelMoE:
+    """Buffers and launches of the expert-parallel MoE block for one rank.
+
+    ``shard``: this rank's ``ExpertShard``.  ``T``: tokens per rank per call
+    (fixed; the buffers are sized for it).  The caller writes the normalised
+    hidden state into ``self.x`` (a view into the send segment), calls
+    :meth:`route`, then :meth:`forward` with the layer's local expert weights
+    ``(wq, scales, biases)`` stacked over the ``len(shard.owned_experts)``
+    local experts; the result lands in ``self.out`` (bf16 ``[T, H]``).
+    """
+
+    def __init__(self, shard: ExpertShard, T: int, hidden: int, inter: int, top_k: int, device,
+                 bits: int = 4, group_size: int = 64, exchange: EPExchange = None, engine: str = "auto",
+                 tile: int = None):
+        self.shard = shard
+        self.W = shard.world_size
+        self.rank = shard.rank
+        owned = shard.owned_experts
+        if not owned or owned != list(range(owned[0], owned[0] + len(owned))):
+            raise ValueError("expert parallelism needs a non-empty contiguous expert block per rank")
+        self.e_begin, self.e_count, self.e_total = owned[0], len(owned), shard.total_experts
+        self.T, self.H, self.I, self.k = T, hidden, inter, top_k
+        self.bits, self.gs = bits, group_size
+        self.dev = dev = torch.device(device)
+        if dev.type != "cuda":
+            raise RuntimeError("ExpertParallelMoE runs on CUDA devices only")
+        if exchange is not None and exchange.world != self.W:
+            raise ValueError("exchange world size differs from the shard's")
+        self.exchange = exchange
+        self.seg = seg = RoutingSegment(T, hidden, top_k)
+        self.send = torch.zeros(seg.seg_bytes, dtype=torch.uint8, device=dev)
+        self.recv = self.send if self.W == 1 else torch.zeros(self.W * seg.seg_bytes, dtype=torch.uint8,
+                                                              device=dev)
+        self.x, self.inds, self.scores = seg.views(self.send)
+        self.G = self.W * T
+        self.A = self.G * top_k
+        A = self.A
+        self.x_row = torch.zeros(A, dtype=torch.int32, device=dev)
+        self.wts = torch.zeros(A, dtype=torch.float32, device=dev)
+        self.local = torch.full((A,), -1, dtype=torch.int32, device=dev)
+        if engine == "auto":
+            engine = "tc" if T * top_k >= self.e_count and group_size == 64 else "gemv"
+        if engine not in ("tc", "gemv"):
+            raise ValueError(f"unknown expert engine {engine!r}")
+        self.engine = engine
+        if tile is None:
+            tile = min(256, max(16, (T + 15) // 16 * 16)) if engine == "tc" else 16
+        self.tile = tile
+        self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, self.e_count, tile))
+        self.plan_ws = torch.empty(max(self.plan_bytes, 16), dtype=torch.uint8, device=dev)
+        self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.gates = torch.empty(T, self.e_total, dtype=torch.float32, device=dev)
+        self.hh = torch.empty(A, inter, dtype=torch.bfloat16, device=dev)
+        self.y = torch.empty(A, hidden, dtype=torch.bfloat16, device=dev)
+        self.part = torch.empty(self.G, hidden, dtype=torch.bfloat16, device=dev)
+        self.out = self.part if self.W == 1 else torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
+
+    # -- phases (the single-GPU multi-rank emulation in the tests drives them one by one)
+    def route(self, wr: torch.Tensor, bias: torch.Tensor = None, renorm: bool = True):
+        """Softmax top-k routing of ``self.x`` into the send segment."""
+        call("b2f_moe_route_topk", ptr(self.x), self.T, self.H, ptr(wr), ptr(bias), self.e_total, self.k,
+             int(renorm), ptr(self.gates), ptr(self.inds), ptr(self.scores), stream_of(self.dev))
+
+    def dispatch(self):
+        if self.W > 1:
+            self.exchange.all_gather(self.recv, self.send)
+
+    def compute(self, gate, up, down):
+        """Plan over the gathered assignments, local experts, weighted partial sums."""
+        seg, st = self.seg, stream_of(self.dev)
+        call("b2f_ep_plan", ptr(self.recv), seg.seg_bytes, seg.row_bytes, seg.inds_off, seg.scores_off, self.W,
+             self.T, self.k, self.e_begin, self.e_count, self.e_total, self.tile, ptr(self.x_row), ptr(self.wts),
+             ptr(self.local), ptr(self.plan_ws), self.plan_bytes, ptr(self.plan_status), st)
+        fn = "b2f_gather_qgemm_affine_tcgen05" if self.engine == "tc" else "b2f_gather_qgemv_affine"
+        gw, gs_, gb = gate
+        uw, us, ub = up
+        dw, ds, db = down
+        call(fn, ptr(self.recv), self.H, ptr(self.x_row), 1, self.A, self.e_count, ptr(gw), ptr(gs_), ptr(gb),
+             ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile, ptr(self.plan_ws),
+             self.plan_bytes, ptr(self.hh), self.I, st)
+        call(fn, ptr(self.hh), self.I, 0, 1, self.A, self.e_count, ptr(dw), ptr(ds), ptr(db), 0, 0, 0, self.H,
+             self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), self.H, st)
+        call("b2f_ep_combine_partial", ptr(self.y), self.H, ptr(self.wts), ptr(self.local), self.G, self.k,
+             self.H, ptr(self.part), self.H, st)
+
+    def combine(self):
+        if self.W > 1:
+            self.exchange.reduce_scatter(self.out, self.part)
+
+    def forward(self, gate, up, down) -> torch.Tensor:
+        self.dispatch()
+        self.compute(gate, up, down)
+        self.combine()
+        return self.out
+
+    def check(self):
+        """Synchronising check that every gathered expert id was in range."""
+        if int(self.plan_status.item()):
+            raise IndexError("expert index out of range in the gathered routing")
+
+    launches_per_block = 5  # route, plan, gate/up, down, partial (collectives are NCCL's)
+
+
+def local_expert_slice(w: torch.Tensor, shard: ExpertShard) -> torch.Tensor:
+    """Rows of a stacked ``[E, ...]`` expert tensor that ``shard`` owns."""
+    owned = shard.owned_experts
+    return w[owned[0]: owned[-1] + 1]
+
+
+def ep_moe_block(x: torch.Tensor, wr: torch.Tensor, gate, up, down, top_k: int, shard: ExpertShard,
+                 exchange: EPExchange = None, bias=None, renorm=True, group_size: int = 64, bits: int = 4):
+    """One-shot expert-parallel MoE block: ``sum_k score_k * expert_k(x)`` for this rank's tokens.
+
+    ``gate``/``up``/``down``: ``(wq, scales, biases)`` of this rank's local
+    experts only.  Builds the buffers on every call; a decode loop keeps one
+    :class:`ExpertParallelMoE` instead.
+    """
+    dev = require_cuda(x, wr)
+    T, H = x.shape
+    inter = gate[0].shape[1]
+    moe = ExpertParallelMoE(shard, T, H, inter, top_k, dev, bits, group_size, exchange)
+    moe.x.copy_(x)
+    moe.route(wr.contiguous(), None if bias is None else bias.to(torch.float32).contiguous(), renorm)
+    out = moe.forward(gate, up, down)
+    return out.clone(), moe.inds.clone(), moe.scores.clone()

@@ -20,7 +20,8 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
   return t;
 }
 
-// h = resid + sum_j score[m, j] * y[m*k + j]  (y may be null -> h = resid)
+// h = resid + sum_j score[m, j] * y[m*k + j]  (y may be null -> h = resid;
+// scores may be null -> every score is 1)
 // resid_out = bf16(h); norm_out = bf16(w * h_bf16 * rsqrt(mean(h_bf16^2) + eps))
 // One CTA per row; a thread owns chunks of 8 contiguous elements (16-byte loads).
 constexpr int CMB_CHUNKS = 4;
@@ -48,7 +49,7 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     }
     if (y) {
       for (int j = 0; j < k; ++j) {
-        const float sc = scores[m * k + j];
+        const float sc = scores ? scores[m * k + j] : 1.0f;
         const uint4 yy = reinterpret_cast<const uint4*>(y + (m * k + j) * H)[v];
         const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&yy);
 #pragma unroll
@@ -371,7 +372,7 @@ extern "C" {
 int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M, int64_t k,
                         const void* weight, float eps, int64_t H, void* resid_out, void* norm_out,
                         void* stream) {
-  if (M < 0 || H <= 0 || (y && (k <= 0 || !scores))) return B2F_ERR_INVALID;
+  if (M < 0 || H <= 0 || (y && k <= 0)) return B2F_ERR_INVALID;
   if (H % 8 != 0 || H > CMB_CHUNKS * 8 * 256) return B2F_ERR_UNSUPPORTED;
   if (M == 0) return B2F_OK;
   if (!resid || !weight || !norm_out) return B2F_ERR_INVALID;

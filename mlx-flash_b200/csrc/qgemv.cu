@@ -23,6 +23,7 @@
 //  * Per-warp partial tiles are reduced across warps through a padded,
 //    double-buffered shared-memory tile in a fixed order (deterministic).
 #include "common.cuh"
+#include "plan.cuh"
 
 namespace b2f {
 
@@ -418,139 +419,8 @@ __global__ void __launch_bounds__(288, 1) qgemv_kernel(const GemvParams p, const
   if (timed_out && lane == 0 && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
 }
 
-// ---- MoE plan: counting sort of assignments by expert, cut into tiles ----
-struct PlanLayout {
-  int64_t off_hdr, off_counts, off_offsets, off_cursor, off_soff, off_sorted, off_slots, total;
-};
-
-static int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
-
-static int64_t plan_max_slots(int64_t A, int64_t E, int tile) {
-  const int64_t ne = A < E ? A : E;
-  return ne + A / tile + 1;
-}
-
-static PlanLayout plan_layout(int64_t A, int64_t E, int tile) {
-  PlanLayout L;
-  int64_t o = 0;
-  L.off_hdr = o;
-  o += 64;
-  L.off_counts = o;
-  o = align_up(o + 4 * E, 16);
-  L.off_offsets = o;
-  o = align_up(o + 4 * (E + 1), 16);
-  L.off_cursor = o;
-  o = align_up(o + 4 * E, 16);
-  L.off_soff = o;
-  o = align_up(o + 4 * (E + 1), 16);
-  L.off_sorted = o;
-  o = align_up(o + 4 * (A > 0 ? A : 1), 16);
-  L.off_slots = o;
-  o = align_up(o + 16 * plan_max_slots(A, E, tile), 256);
-  L.total = o;
-  return L;
-}
-
 int64_t plan_slots_offset(int64_t A, int64_t E, int tile) { return plan_layout(A, E, tile).off_slots; }
 int64_t plan_sorted_offset(int64_t A, int64_t E, int tile) { return plan_layout(A, E, tile).off_sorted; }
-
-// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
-__device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int inc = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += n;
-  }
-  if (lane == 31) warp_tot[warp] = inc;
-  __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    int t = lane < nw ? warp_tot[lane] : 0;
-    int ti = t;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, ti, o);
-      if (lane >= o) ti += n;
-    }
-    if (lane < nw) warp_tot[lane] = ti - t;
-    if (lane == nw - 1) *total = ti;
-  }
-  __syncthreads();
-  const int r = inc - v + warp_tot[warp];
-  __syncthreads();
-  return r;
-}
-
-__global__ void __launch_bounds__(1024) moe_plan_kernel(const int32_t* __restrict__ expert_of, int A, int E,
-                                                        int tile, char* ws, PlanLayout L,
-                                                        int32_t* status_out) {
-  int32_t* hdr = reinterpret_cast<int32_t*>(ws + L.off_hdr);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.off_offsets);
-  int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.off_cursor);
-  int32_t* soff = reinterpret_cast<int32_t*>(ws + L.off_soff);
-  int32_t* sorted = reinterpret_cast<int32_t*>(ws + L.off_sorted);
-  int4* slots = reinterpret_cast<int4*>(ws + L.off_slots);
-  __shared__ int warp_tot[32];
-  __shared__ int total;
-  __shared__ int bad;
-  if (threadIdx.x == 0) bad = 0;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    counts[e] = 0;
-    cursor[e] = 0;
-  }
-  __syncthreads();
-  for (int a = threadIdx.x; a < A; a += blockDim.x) {
-    const int e = expert_of[a];
-    if (e < 0 || e >= E) {
-      bad = 1;
-    } else {
-      atomicAdd(&counts[e], 1);
-    }
-  }
-  __syncthreads();
-  // exclusive scans over experts (chunks of blockDim.x)
-  int run = 0, srun = 0;
-  for (int base = 0; base < E; base += blockDim.x) {
-    const int e = base + threadIdx.x;
-    const int cnt = e < E ? counts[e] : 0;
-    const int ns = (cnt + tile - 1) / tile;
-    const int ex = block_exclusive_scan(cnt, warp_tot, &total);
-    const int t1 = total;
-    __syncthreads();
-    const int sx = block_exclusive_scan(ns, warp_tot, &total);
-    const int t2 = total;
-    if (e < E) {
-      offsets[e] = run + ex;
-      soff[e] = srun + sx;
-    }
-    run += t1;
-    srun += t2;
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    offsets[E] = run;
-    soff[E] = srun;
-    hdr[0] = srun;
-    hdr[1] = bad ? B2F_ERR_INVALID : B2F_OK;
-    if (status_out) *status_out = hdr[1];
-  }
-  __syncthreads();
-  for (int a = threadIdx.x; a < A; a += blockDim.x) {
-    const int e = expert_of[a];
-    if (e >= 0 && e < E) {
-      const int pos = offsets[e] + atomicAdd(&cursor[e], 1);
-      sorted[pos] = a;
-    }
-  }
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int cnt = counts[e];
-    for (int j = 0, s = soff[e]; j * tile < cnt; ++j, ++s)
-      slots[s] = make_int4(e, offsets[e] + j * tile, min(tile, cnt - j * tile), 0);
-  }
-}
 
 // ---- launcher ------------------------------------------------------------
 static int g_num_sms = 0;
@@ -724,7 +594,7 @@ int b2f_moe_plan(const int32_t* expert_of, int64_t A, int64_t E, int tile, void*
   if (!workspace || workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
   if (A > 0 && !expert_of) return B2F_ERR_INVALID;
   if (!aligned(workspace, 16)) return B2F_ERR_ALIGN;
-  moe_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(expert_of, int(A), int(E), tile,
+  moe_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(DenseExperts{expert_of}, int(A), int(E), tile,
                                                      static_cast<char*>(workspace), L, status_out);
   return check_launch();
 }

@@ -1,0 +1,114 @@
+"""Host side of the expert-parallel MoE on CPU: the routing-segment layout,
+the two collectives over a 2-rank gloo group, and the exactness of the
+dispatch/combine decomposition (sum over ranks of owner-masked partials
+equals the single-process MoE), with the oracle standing in for the expert
+kernels on each rank."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from b200flash.distributed_experts import ExpertShard
+from b200flash.ep import RoutingSegment
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_routing_segment_layout():
+    seg = RoutingSegment(T=64, H=2048, k=8)
+    assert seg.row_bytes == 4096
+    assert seg.inds_off == 64 * 4096
+    assert seg.scores_off == seg.inds_off + 64 * 8 * 4
+    assert seg.seg_bytes % seg.row_bytes == 0 and seg.seg_bytes >= seg.scores_off + 64 * 8 * 4
+    assert seg.seg_rows == 65
+    buf = torch.zeros(3 * seg.seg_bytes, dtype=torch.uint8)
+    for r in range(3):
+        x, inds, sc = seg.views(buf, r)
+        x.fill_(r + 1)
+        inds.fill_(10 + r)
+        sc.fill_(0.5 * r)
+    rows = buf.view(torch.bfloat16).view(3 * seg.seg_rows, 2048)
+    for r in range(3):
+        x, inds, sc = seg.views(buf, r)
+        assert torch.equal(rows[r * seg.seg_rows: r * seg.seg_rows + 64], x)
+        assert int(inds[5, 3]) == 10 + r and float(sc[63, 7]) == 0.5 * r
+    with pytest.raises(ValueError):
+        RoutingSegment(T=4, H=100, k=2)
+
+
+def _rank_main(rank, world, port, out_path):
+    import torch.distributed as dist
+
+    from b200flash.ep import EPExchange
+    from oracle import affine, moe
+    from oracle.fp import round_to
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}")
+    try:
+        ex = EPExchange()
+        T, H, I, k, E = 5, 128, 64, 3, 7
+        rng = np.random.default_rng(0)
+
+        def experts(N, K):
+            return affine.quantize(round_to(rng.normal(0, 0.02, (E, N, K)).astype(np.float32), "bf16"), 64, 4)
+
+        g, u, d = experts(I, H), experts(I, H), experts(H, I)
+        wr = round_to(rng.normal(0, 0.05, (H, E)).astype(np.float32), "bf16")
+        xs = [round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16") for _ in range(world)]
+        seg = RoutingSegment(T, H, k)
+        send = torch.zeros(seg.seg_bytes, dtype=torch.uint8)
+        x, inds, scores = seg.views(send)
+        x.copy_(torch.from_numpy(xs[rank]).to(torch.bfloat16))
+        oi, osc = moe.route(xs[rank], wr, k)
+        inds.copy_(torch.from_numpy(oi))
+        scores.copy_(torch.from_numpy(osc.astype(np.float32)))
+        recv = torch.empty(world * seg.seg_bytes, dtype=torch.uint8)
+        ex.all_gather(recv, send)
+        shard = ExpertShard(rank=rank, world_size=world, total_experts=E)
+        part = torch.zeros(world * T, H, dtype=torch.float32)
+        for r in range(world):
+            xr, ir, sr = seg.views(recv, r)
+            xr = xr.float().numpy()
+            ir = ir.numpy()
+            sr = sr.numpy().astype(np.float64)
+            _, _, yk = moe.expert_mlp(xr, ir, sr, g, u, d)
+            mask = np.vectorize(shard.is_local)(ir)
+            part[r * T:(r + 1) * T] = torch.from_numpy((yk * (sr * mask)[..., None]).sum(1))
+        out = torch.empty(T, H, dtype=torch.float32)
+        ex.reduce_scatter(out, part)
+        want, _, _ = moe.expert_mlp(xs[rank], oi, osc, g, u, d)
+        err = float(np.abs(out.numpy() - want).max())
+        owners = sorted(set(shard.owner_of(int(e)) for e in oi.reshape(-1)))
+        with open(out_path, "w") as f:
+            f.write(f"{err} {len(owners)}\n")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_decomposition_over_gloo(tmp_path):
+    import torch.multiprocessing as mp
+
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    outs = [str(tmp_path / f"rank{r}.txt") for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r])) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert [p.exitcode for p in procs] == [0] * world
+    for o in outs:
+        err, n_owners = open(o).read().split()
+        assert float(err) < 1e-5, err
+        assert int(n_owners) >= 1
