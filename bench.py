@@ -177,6 +177,16 @@ def profile_kernels(dec, torch):
     return timings, distinct
 
 
+# DRAM bytes moved per algorithmic byte, from ncu captures of each kernel on
+# the 2-layer copy of this decode step (dram__bytes_read.sum +
+# dram__bytes_write.sum over the launch's algorithmic bytes; see
+# profiles/qgemm_tc_moe_b64_2layer.txt and
+# profiles/qkv_decode_attn_b64_ctx2048.txt).  The per-layer shapes are those
+# of the 48-layer step, so traffic scales with the units a launch processes.
+NCU_TRAFFIC_RATIO = {"moe_gate_up": 95.547392 / 73.596928, "moe_down": 46.04288 / 39.15776,
+                     "attention": 148.952064 / 144.142336}
+
+
 def attention_bytes(dec, ctx):
     s = dec.s
     per_tok = s.n_kv_heads * 2 * (dec.rb + 4 * (s.head_dim // 64))
@@ -295,7 +305,10 @@ def run_ours(args):
     d = kernels[dom]
     roofline = {"kernel": dom, "bound": "hbm", "achieved": round(d["gbs"], 1), "peak": peak,
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
-                "traffic": None, "bytes_per_launch": int(d["bytes_per_launch"]),
+                "traffic": (int(d["bytes_per_launch"] * NCU_TRAFFIC_RATIO[dom]) if dom in NCU_TRAFFIC_RATIO
+                            else None),
+                "traffic_source": "ncu DRAM bytes / algorithmic bytes on the 2-layer capture, times this launch's bytes",
+                "bytes_per_launch": int(d["bytes_per_launch"]),
                 "avg_launch_us": round(d["avg_us"], 2),
                 "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / len(distinct), 1)}
     result = {

@@ -252,6 +252,56 @@ int b2f_ep_plan(const void* recv, int64_t seg_bytes, int64_t row_bytes, int64_t 
 int b2f_ep_combine_partial(const void* y, int64_t ldy, const float* wts, const int32_t* local,
                            int64_t G, int64_t k, int64_t H, void* out, int64_t ldo, void* stream);
 
+/* ---- smaller ops: Q4_0 GEMV, kernels/ops.py drop-ins, 2-bit requant,
+ *      sensitivity fake quantization ------------------------------------- */
+
+/* flash_dequant_gemv_q4 (kernels/flash_dequant.metal:19-49), for nvec input
+ * vectors: y[b, m] = sum_n (code(m,n) - 8) * scales[m, n/group_size] * x[b, n].
+ * weights uint8 [M, N/2], code 2i in the low nibble of byte i, 2i+1 in the
+ * high nibble; scales fp16 [M, N/group_size]; x fp32 [nvec, N]; y fp32
+ * [nvec, M]; fp32 accumulation.  group_size a multiple of 32; weights
+ * 16-byte aligned. */
+int b2f_q4_0_gemv(const uint8_t* weights, const void* scales, const float* x, float* y,
+                  int64_t M, int64_t N, int group_size, int64_t nvec, void* stream);
+
+/* kernels/ops.py:48-108 swiglu(gate, up): out = silu(gate) * up computed in
+ * fp32, stored in `dtype` (B2F_BF16, B2F_F16 or B2F_F32), n elements. */
+int b2f_swiglu(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream);
+
+/* kernels/ops.py:111-148 moe_dispatch for T tokens: out[t, :] =
+ * sum_j expert_outputs_t[selected_ids[t, j], :] * routing_weights[t, j],
+ * expert_outputs_t = expert_outputs + t * eo_token_stride elements, each
+ * [E, H] of `dtype`; ids int32 [T, k]; weights fp32 [T, k]; out [T, H] of
+ * `dtype`; fp32 accumulation.  eo_token_stride 0 shares one [E, H] block. */
+int b2f_moe_dispatch(const void* expert_outputs, int64_t eo_token_stride, int64_t E, int64_t H,
+                     const int32_t* selected_ids, const float* routing_weights, int64_t T,
+                     int64_t k, int dtype, void* out, void* stream);
+
+/* requantize_4bit_to_2bit (mixed_precision.py:130-216), bit-exact: wq uint32
+ * [rows, cols_u32] (8 LSB-first nibbles per word), scales/biases [rows,
+ * n_groups] of `dtype`; per group of wpg = 8*cols_u32/n_groups codes
+ * (a power of two, 4..1024): v = nib*s + b, crumb = clip(rint((v-min)/range*3),
+ * 0, 3) with range = max-min (1e-10 if smaller); packed uint8 [rows,
+ * 2*cols_u32], crumb j at bits 2*(j%4) of byte j/4; scales2 = fp16(range/3),
+ * biases2 = fp16(min), both [rows, n_groups]. */
+int b2f_requant_4to2(const uint32_t* wq, int64_t rows, int64_t cols_u32, const void* scales,
+                     const void* biases, int dtype, int64_t n_groups, uint8_t* packed,
+                     void* scales2, void* biases2, void* stream);
+
+/* dequantize_2bit (mixed_precision.py:219-245): out fp32 [rows,
+ * n_values_per_row] = crumb * scale2 + bias2 (fp16 scale/bias [rows, n_groups]). */
+int b2f_dequant_2bit(const uint8_t* packed, int64_t packed_ld, const void* scales2,
+                     const void* biases2, int64_t n_groups, int64_t rows,
+                     int64_t n_values_per_row, float* out, void* stream);
+
+/* _quantize_linears_inplace (layer_quantization.py:461-494) for one tensor of
+ * n elements: scale = max(dtype(absmax/qmax), 1e-10), out fp32 =
+ * clip(rint(w/scale), qmin, qmax) * scale with (qmin, qmax) = (-8, 7) for
+ * bits 4 and (-128, 127) for bits 8.  absmax_out: device fp32, receives
+ * max|w|. */
+int b2f_fake_quant_sym(const void* w, int dtype, int64_t n, int bits, float* out,
+                       float* absmax_out, void* stream);
+
 /* ---- decode-step glue around the hot path (Qwen3-MoE-shaped decoder) ----- */
 
 /* MoE combine + residual + RMSNorm in one pass (expert_streaming.py:464-470

@@ -41,6 +41,12 @@ SIGNATURES = {
     "b2f_ep_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
                          _I64, _P, _P]),
     "b2f_ep_combine_partial": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P]),
+    "b2f_q4_0_gemv": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _P]),
+    "b2f_swiglu": (_I, [_P, _P, _P, _I64, _I, _P]),
+    "b2f_moe_dispatch": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P]),
+    "b2f_requant_4to2": (_I, [_P, _I64, _I64, _P, _P, _I, _I64, _P, _P, _P, _P]),
+    "b2f_dequant_2bit": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "b2f_fake_quant_sym": (_I, [_P, _I, _I64, _I, _P, _P, _P]),
     "b2f_gather_qgemv_affine": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64,
                                      _I64, _I, _I, _I, _P, _I64, _P, _I64, _P]),
     "b2f_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I, _P, _P, _I64, _I, _P]),

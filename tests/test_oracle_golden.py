@@ -102,3 +102,34 @@ def test_round_helpers():
     assert round_bf16(np.float32(1.0 + 2 ** -8)) == 1.0  # tie -> even
     assert round_bf16(np.float32(1.0 + 3 * 2 ** -8)) == np.float32(1.0 + 2 ** -6)
     assert round_f16(np.float32(65519.0)) == 65504.0
+
+
+def test_q4_0_c_restatement_against_float64():
+    """The C restatement of the Q4_0 shader agrees with an order-free float64 sum."""
+    from oracle import q4_0
+
+    rng = np.random.default_rng(0)
+    for M, N, gs in ((3, 64, 32), (17, 512, 32), (5, 256, 64)):
+        w = rng.integers(0, 256, (M, N // 2), dtype=np.uint8)
+        s = (rng.random((M, N // gs)) * 0.1).astype(np.float16)
+        x = rng.standard_normal(N).astype(np.float32)
+        got = q4_0.gemv(w, s, x, gs)
+        want = q4_0.gemv_numpy(w, s, x, gs)
+        assert np.allclose(got, want, rtol=1e-4, atol=1e-4)
+    # hand case: code 9 (v=1) low nibble, code 0 (v=-8) high nibble; scale 0.5
+    w = np.array([[0x09] * 16], np.uint8)
+    s = np.array([[0.5]], np.float16)
+    x = np.arange(32, dtype=np.float32)
+    assert q4_0.gemv(w, s, x, 32)[0] == np.float32(sum(0.5 * x[0::2]) - sum(4.0 * x[1::2]))
+
+
+def test_fake_quant_oracle_rules():
+    from oracle import sensitivity
+
+    w = np.array([0.7, -0.35, 0.1, 0.0], np.float32)
+    out, amax = sensitivity.fake_quantize_sym(w, 4, "f32")
+    assert amax == np.float32(0.7)
+    scale = np.float32(0.7) / np.float32(7.0)
+    assert np.array_equal(out, (np.clip(np.rint(w / scale), -8, 7) * scale).astype(np.float32))
+    z, za = sensitivity.fake_quantize_sym(np.zeros(4, np.float32), 8, "bf16")
+    assert za == 0 and not z.any()
