@@ -222,6 +222,82 @@ int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const flo
                                 int64_t slot_stride, int bits, int group_size,
                                 float softmax_scale, int n_splits, void* out, void* stream);
 
+/* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
+
+/* Copies the planned assignments' activation rows into plan order:
+ * out[i, :] = x[x_row(sorted[i]), :] for i < (planned count), x_row(a) =
+ * x_row_index ? x_row_index[a] : a / x_row_div, with every group of 8
+ * columns stored in the order (0,4,1,5,2,6,3,7).  The plan (b2f_moe_plan or
+ * b2f_ep_plan) must use the same A, E and tile.  Rows >= the planned count
+ * are not written.  bf16 x [*, ldx], out [A, ldo]; K % 8 == 0. */
+int b2f_moe_gather_rows(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div,
+                        int64_t A, int64_t E, int tile, const void* plan_workspace,
+                        int64_t plan_workspace_bytes, int64_t K, void* out, int64_t ldo,
+                        void* stream);
+
+/* mx.gather_qmm over expert-sorted rows (expert_streaming.py:224-241 with
+ * sorted_indices=True) on tcgen05/TMEM: persistent CTAs walk the plan's
+ * (slot, 128-row block) units; x tiles arrive by TMA from x_sorted (the
+ * layout b2f_moe_gather_rows writes: plan order, permuted column groups).
+ * w_up non-NULL fuses silu(x.Wg^T) * (x.Wu^T).  out_sorted = 0: out[a, n] for
+ * assignment a, natural columns (the layout of b2f_gather_qgemm_affine_*);
+ * out_sorted = 1: out[i, perm(n)] in plan order -- the x_sorted layout of a
+ * following call (N % 8 == 0).  group_size 64, bits 4 or 8, K % 128 == 0. */
+int b2f_sorted_qgemm_affine_tcgen05(const void* x_sorted, int64_t ldx, int64_t A, int64_t E,
+                                    const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                    const uint32_t* w_up, const void* s_up, const void* b_up,
+                                    int64_t N, int64_t K, int bits, int group_size, int tile,
+                                    const void* plan_workspace, int64_t plan_workspace_bytes,
+                                    void* out, int64_t ldo, int out_sorted, void* stream);
+
+/* ---- KV eviction: attention-guided (H2O / ScissorHands) and sink + window - */
+
+/* kv_compression.py:84-141 record_attention: per-token importance = mean over
+ * the H heads of one attention row.  attn points at head 0's row; head h's
+ * row starts head_stride elements later (head_stride = S_q * S for the last
+ * query row of an [H, S_q, S] tensor).  mode 0: out[s] = v; 1: out[s] += v
+ * (H2O accumulation); 2: out[s] = decay*out[s] + (1-decay)*v (ScissorHands
+ * EMA).  out2 (may be NULL): out2[s] += v (H2O cross-layer total).  fp32
+ * outputs; attn in `dtype`. */
+int b2f_attn_row_head_mean(const void* attn, int dtype, int64_t H, int64_t head_stride, int64_t S,
+                           int mode, float decay, float* out, float* out2, void* stream);
+
+/* Workspace bytes of b2f_qkv_head_mean_probs. */
+int64_t b2f_qkv_head_mean_probs_workspace_bytes(int64_t B, int64_t Hq, int n_splits);
+
+/* The same importance on the paged quantized decode path (no attention
+ * matrix is formed): for every sequence b and token t < seq_lens[b],
+ * v = mean over the Hq query heads of softmax_t(scale * q[b,h] . K[b,t]),
+ * K dequantized from the reference KV format pages exactly as
+ * b2f_qkv_decode_attn reads them (same page/stride arguments); written to
+ * out[b*out_ld + t] by `mode` as in b2f_attn_row_head_mean.  max_len >= every
+ * seq_len; Hq/Hkv <= 16; D % 64 == 0, D <= 256. */
+int b2f_qkv_head_mean_probs(const void* q, const uint8_t* k_pages, const float* k_scales,
+                            const int32_t* block_table, int64_t max_pages, const int32_t* seq_lens,
+                            int64_t max_len, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                            int64_t page_size, int64_t head_stride, int64_t slot_stride, int bits,
+                            int group_size, float softmax_scale, int n_splits, void* workspace,
+                            int64_t workspace_bytes, float* out, int64_t out_ld, int mode,
+                            float decay, void* stream);
+
+/* kv_compression.py:293-364 _compress_layer keep list for one layer of S
+ * tokens: if S > budget and the middle [sink, S-window) holds more than
+ * budget - sink - window tokens, keep = sink tokens, the most important
+ * middle tokens (importance[t] descending, ties to the lower position;
+ * importance NULL or importance_len < S scores every token 1) in position
+ * order, then the recent window; else keep = 0..S-1.  keep: int32 [S]
+ * (device); count: device int32, the number kept.  One CTA. */
+int b2f_evict_keep_indices(const float* importance, int64_t importance_len, int64_t S, int64_t sink,
+                           int64_t window, int64_t budget, int32_t* keep, int32_t* count,
+                           void* stream);
+
+/* dst[o, i, :] = src[o, keep[i], :] for o < outer, i < n_keep; rows of
+ * row_bytes bytes, src [outer, S_src, row], dst [outer, n_keep, row] (the
+ * reindexing of [H, S, D] keys/values, streaming_llm.py:129-160 and
+ * kv_compression.py:349-355, and of per-token score arrays). */
+int b2f_gather_tokens(const void* src, void* dst, int64_t outer, int64_t S_src, int64_t row_bytes,
+                      const int32_t* keep, int64_t n_keep, void* stream);
+
 /* ---- (e) expert parallelism: device halves of dispatch / combine -------- */
 
 /* Replaces the expert-to-rank routing of distributed_experts.py:36-80

@@ -41,6 +41,15 @@ SIGNATURES = {
     "b2f_ep_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P,
                          _I64, _P, _P]),
     "b2f_ep_combine_partial": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _P]),
+    "b2f_moe_gather_rows": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _I64, _P]),
+    "b2f_sorted_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I,
+                                             _P, _I64, _P, _I64, _I, _P]),
+    "b2f_attn_row_head_mean": (_I, [_P, _I, _I64, _I64, _I64, _I, ctypes.c_float, _P, _P, _P]),
+    "b2f_qkv_head_mean_probs_workspace_bytes": (_I64, [_I64, _I64, _I]),
+    "b2f_qkv_head_mean_probs": (_I, [_P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I,
+                                     _I, ctypes.c_float, _I, _P, _I64, _P, _I64, _I, ctypes.c_float, _P]),
+    "b2f_evict_keep_indices": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "b2f_gather_tokens": (_I, [_P, _P, _I64, _I64, _I64, _P, _I64, _P]),
     "b2f_q4_0_gemv": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _P]),
     "b2f_swiglu": (_I, [_P, _P, _P, _I64, _I, _P]),
     "b2f_moe_dispatch": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P]),

@@ -182,13 +182,19 @@ class Qwen3MoeDecoder:
         if self.ep is None:
             if moe_engine == "auto":
                 moe_engine = "tc" if A >= E else "gemv"
+            if moe_engine not in ("tc", "tc_gather", "gemv"):
+                raise ValueError(f"unknown expert engine {moe_engine!r}")
+            if moe_engine == "tc" and ((H // 64) % 2 or (I // 64) % 2):
+                moe_engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
             self.moe_engine = moe_engine
-            self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine == "tc" else 16
+            self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine != "gemv" else 16
             self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
             self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
             self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
             self.hh = torch.empty(A, I, dtype=torch.bfloat16, device=dev)
             self.y = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+            # "tc": activations gathered into expert-sorted rows once per layer
+            self.xs = torch.empty(A, H, dtype=torch.bfloat16, device=dev) if moe_engine == "tc" else None
         else:
             self.tile = self.ep.tile
         self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
@@ -265,13 +271,23 @@ class Qwen3MoeDecoder:
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), st)
             call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
                  ptr(self.plan_status), st)
-            fn = "b2f_gather_qgemm_affine_tcgen05" if self.moe_engine == "tc" else "b2f_gather_qgemv_affine"
-            call(fn, ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
-                 ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
-                 ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, st)
-            call(fn, ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
-                 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y),
-                 H, st)
+            if self.moe_engine == "tc":
+                call("b2f_moe_gather_rows", ptr(self.xn), H, 0, s.top_k, A, E, self.tile, ptr(self.plan_ws),
+                     self.plan_bytes, H, ptr(self.xs), H, st)
+                call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.xs), H, A, E, ptr(g.wq), ptr(g.scales),
+                     ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
+                     ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, 1, st)
+                call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.hh), I, A, E, ptr(d.wq), ptr(d.scales),
+                     ptr(d.biases), 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws),
+                     self.plan_bytes, ptr(self.y), H, 0, st)
+            else:
+                fn = "b2f_gather_qgemm_affine_tcgen05" if self.moe_engine == "tc_gather" else "b2f_gather_qgemv_affine"
+                call(fn, ptr(self.xn), H, 0, s.top_k, A, E, ptr(g.wq), ptr(g.scales),
+                     ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
+                     ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, st)
+                call(fn, ptr(self.hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
+                     0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes,
+                     ptr(self.y), H, st)
             call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.y), ptr(self.scores), B, s.top_k, ptr(nxt),
                  s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
         w = self.lm_head
@@ -287,6 +303,8 @@ class Qwen3MoeDecoder:
         attn = 2 if self.n_splits > 1 else 1
         # qkv, rope+append, attention, o_proj, norm, router, plan, gate/up, down, combine
         per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 2 + 1
+        if self.moe_engine == "tc":
+            per_layer += 1  # the row gather into expert-sorted order
         if self.ep is not None:
             per_layer += 1  # the partial-sum kernel before the reduce-scatter
         return 2 + self.L * per_layer + 2

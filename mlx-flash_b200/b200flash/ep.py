@@ -15,8 +15,10 @@ rank's own tokens):
 2. ``b2f_ep_plan`` sorts the ``W*T*k`` gathered assignments by local expert
    (experts of other ranks skipped) and records each assignment's x row in
    the gathered buffer;
-3. the grouped expert kernels (tcgen05 GEMM or register GEMV) run on the
-   local expert shard, reading x rows in place from the gathered segments;
+3. the grouped expert kernels run on the local expert shard: the rows are
+   copied from the gathered segments into expert-sorted order
+   (``b2f_moe_gather_rows``) for the tcgen05 GEMM, or read in place through
+   the x-row index by the register GEMV;
 4. ``b2f_ep_combine_partial`` forms every gathered token's score-weighted sum
    over its local experts;
 5. ``reduce_scatter_tensor`` (sum) returns to each rank the sum over ranks of
@@ -135,17 +137,20 @@ class ExpertParallelMoE:
         self.local = torch.full((A,), -1, dtype=torch.int32, device=dev)
         if engine == "auto":
             engine = "tc" if T * top_k >= self.e_count and group_size == 64 else "gemv"
-        if engine not in ("tc", "gemv"):
+        if engine not in ("tc", "tc_gather", "gemv"):
             raise ValueError(f"unknown expert engine {engine!r}")
+        if engine == "tc" and ((hidden // 64) % 2 or (inter // 64) % 2):
+            engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
         self.engine = engine
         if tile is None:
-            tile = min(256, max(16, (T + 15) // 16 * 16)) if engine == "tc" else 16
+            tile = min(256, max(16, (T + 15) // 16 * 16)) if engine != "gemv" else 16
         self.tile = tile
         self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, self.e_count, tile))
         self.plan_ws = torch.empty(max(self.plan_bytes, 16), dtype=torch.uint8, device=dev)
         self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)
         self.gates = torch.empty(T, self.e_total, dtype=torch.float32, device=dev)
         self.hh = torch.empty(A, inter, dtype=torch.bfloat16, device=dev)
+        self.xs = torch.empty(A, hidden, dtype=torch.bfloat16, device=dev) if engine == "tc" else None
         self.y = torch.empty(A, hidden, dtype=torch.bfloat16, device=dev)
         self.part = torch.empty(self.G, hidden, dtype=torch.bfloat16, device=dev)
         self.out = self.part if self.W == 1 else torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
@@ -166,15 +171,25 @@ class ExpertParallelMoE:
         call("b2f_ep_plan", ptr(self.recv), seg.seg_bytes, seg.row_bytes, seg.inds_off, seg.scores_off, self.W,
              self.T, self.k, self.e_begin, self.e_count, self.e_total, self.tile, ptr(self.x_row), ptr(self.wts),
              ptr(self.local), ptr(self.plan_ws), self.plan_bytes, ptr(self.plan_status), st)
-        fn = "b2f_gather_qgemm_affine_tcgen05" if self.engine == "tc" else "b2f_gather_qgemv_affine"
         gw, gs_, gb = gate
         uw, us, ub = up
         dw, ds, db = down
-        call(fn, ptr(self.recv), self.H, ptr(self.x_row), 1, self.A, self.e_count, ptr(gw), ptr(gs_), ptr(gb),
-             ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile, ptr(self.plan_ws),
-             self.plan_bytes, ptr(self.hh), self.I, st)
-        call(fn, ptr(self.hh), self.I, 0, 1, self.A, self.e_count, ptr(dw), ptr(ds), ptr(db), 0, 0, 0, self.H,
-             self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), self.H, st)
+        if self.engine == "tc":
+            call("b2f_moe_gather_rows", ptr(self.recv), self.H, ptr(self.x_row), 1, self.A, self.e_count, self.tile,
+                 ptr(self.plan_ws), self.plan_bytes, self.H, ptr(self.xs), self.H, st)
+            call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.xs), self.H, self.A, self.e_count, ptr(gw), ptr(gs_),
+                 ptr(gb), ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile,
+                 ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), self.I, 1, st)
+            call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.hh), self.I, self.A, self.e_count, ptr(dw), ptr(ds),
+                 ptr(db), 0, 0, 0, self.H, self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws),
+                 self.plan_bytes, ptr(self.y), self.H, 0, st)
+        else:
+            fn = "b2f_gather_qgemm_affine_tcgen05" if self.engine == "tc_gather" else "b2f_gather_qgemv_affine"
+            call(fn, ptr(self.recv), self.H, ptr(self.x_row), 1, self.A, self.e_count, ptr(gw), ptr(gs_), ptr(gb),
+                 ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile, ptr(self.plan_ws),
+                 self.plan_bytes, ptr(self.hh), self.I, st)
+            call(fn, ptr(self.hh), self.I, 0, 1, self.A, self.e_count, ptr(dw), ptr(ds), ptr(db), 0, 0, 0, self.H,
+                 self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), self.H, st)
         call("b2f_ep_combine_partial", ptr(self.y), self.H, ptr(self.wts), ptr(self.local), self.G, self.k,
              self.H, ptr(self.part), self.H, st)
 
@@ -193,7 +208,10 @@ class ExpertParallelMoE:
         if int(self.plan_status.item()):
             raise IndexError("expert index out of range in the gathered routing")
 
-    launches_per_block = 5  # route, plan, gate/up, down, partial (collectives are NCCL's)
+    @property
+    def launches_per_block(self) -> int:
+        """route, plan, (row gather), gate/up, down, partial; the collectives are NCCL's."""
+        return 6 if self.engine == "tc" else 5
 
 
 def local_expert_slice(w: torch.Tensor, shard: ExpertShard) -> torch.Tensor:

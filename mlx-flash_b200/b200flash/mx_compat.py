@@ -170,6 +170,43 @@ def gather_qmm_tc_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bias
     return out
 
 
+def moe_gather_rows(x_rows: torch.Tensor, plan: "MoEPlan", x_row_index: torch.Tensor = None,
+                    x_row_div: int = 1) -> torch.Tensor:
+    """Activation rows in the plan's expert-sorted order (``[A, K]``; rows past
+    the planned count are left unwritten), each group of 8 columns in the
+    order (0,4,1,5,2,6,3,7) that ``sorted_qmm_tc`` consumes."""
+    dev = require_cuda(x_rows, x_row_index)
+    K = x_rows.shape[-1]
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    out = torch.empty(plan.A, K, dtype=torch.bfloat16, device=dev)
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_moe_gather_rows", ptr(xc), K, ptr(xri), int(x_row_div), plan.A, plan.E, plan.tile,
+         ptr(plan.workspace), plan.workspace.numel(), K, ptr(out), K, stream_of(dev))
+    return out
+
+
+def sorted_qmm_tc(x_sorted: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size: int, bits: int,
+                  up=None, out_sorted: bool = False) -> torch.Tensor:
+    """Grouped tcgen05 GEMM over expert-sorted rows (``moe_gather_rows`` layout).
+
+    ``out_sorted=False``: ``out[a] = x[row(a)] . W[e(a)]^T`` for assignment
+    ``a`` (natural columns).  ``out_sorted=True``: rows stay in sorted order
+    with permuted columns -- the input layout of the next ``sorted_qmm_tc``.
+    ``up=(w_up, s_up, b_up)`` fuses the SwitchGLU front half.
+    """
+    dev = require_cuda(x_sorted, w, scales, biases)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
+    wu = su = bu = None
+    if up is not None:
+        wu, su, bu = (t.contiguous() for t in up)
+    call("b2f_sorted_qgemm_affine_tcgen05", ptr(x_sorted), x_sorted.shape[-1], plan.A, E, ptr(w.contiguous()),
+         ptr(scales.contiguous()), ptr(biases.contiguous()), ptr(wu), ptr(su), ptr(bu), N, K, bits, group_size,
+         plan.tile, ptr(plan.workspace), plan.workspace.numel(), ptr(out), N, int(out_sorted), stream_of(dev))
+    return out
+
+
 class MoEPlan:
     """Device-side grouping of assignments by expert (output of ``b2f_moe_plan``)."""
 

@@ -188,43 +188,65 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
 }
 
 // logits[t, e] = x[t].wr[e] (+ bias[e]): CTA = 8 experts x 8 tokens, one warp
-// per expert, 16-byte loads of the router row and the (L1-shared) token rows.
+// per expert.  The CTA's 8 token rows are staged in shared memory with
+// coalesced 16-byte loads; each warp first issues all of its router-row
+// loads (RL_MAXV 16-byte vectors per lane, H <= 8192), then reads x from
+// shared memory, so one memory latency covers the whole dot product.
+constexpr int RL_TOK = 8;
+constexpr int RL_MAXV = 4;  // router-row vectors per lane per pass (1024 elements per warp pass)
+
 __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                            const __nv_bfloat16* __restrict__ wr,
                                                            const float* __restrict__ bias, int E,
                                                            float* __restrict__ logits) {
+  extern __shared__ __align__(16) uint4 xs[];  // [RL_TOK][H/8]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x * 8 + warp;
-  const int t0 = blockIdx.y * 8;
+  const int t0 = blockIdx.y * RL_TOK;
+  const int nt = min(RL_TOK, T - t0);
+  const int hv = H / 8;
+  for (int i = threadIdx.x; i < RL_TOK * hv; i += blockDim.x) {
+    const int t = i / hv, v = i - t * hv;
+    xs[i] = t < nt ? reinterpret_cast<const uint4*>(x + int64_t(t0 + t) * H)[v] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  __syncthreads();
   if (e >= E) return;
-  float acc[8];
+  float acc[RL_TOK];
 #pragma unroll
-  for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-  const __nv_bfloat16* wrow = wr + int64_t(e) * H;
-#pragma unroll 4
-  for (int h = lane * 8; h < H; h += 256) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(wrow + h);
-    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
-    float wf[8];
+  for (int t = 0; t < RL_TOK; ++t) acc[t] = 0.f;
+  const uint4* wrow = reinterpret_cast<const uint4*>(wr + int64_t(e) * H);
+  for (int v0 = 0; v0 < hv; v0 += 32 * RL_MAXV) {
+    uint4 wv[RL_MAXV];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      wf[2 * i] = __low2float(w2[i]);
-      wf[2 * i + 1] = __high2float(w2[i]);
+    for (int j = 0; j < RL_MAXV; ++j) {
+      const int v = v0 + lane + 32 * j;
+      wv[j] = v < hv ? wrow[v] : make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (t0 + t < T) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(x + int64_t(t0 + t) * H + h);
+    for (int j = 0; j < RL_MAXV; ++j) {
+      const int v = v0 + lane + 32 * j;
+      if (v >= hv) break;
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[j]);
+      float wf[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        wf[2 * i] = __low2float(w2[i]);
+        wf[2 * i + 1] = __high2float(w2[i]);
+      }
+#pragma unroll
+      for (int t = 0; t < RL_TOK; ++t) {
+        const uint4 xv = xs[t * hv + v];
         const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[t] += wf[2 * i] * __low2float(x2[i]) + wf[2 * i + 1] * __high2float(x2[i]);
+        for (int i = 0; i < 4; ++i)
+          acc[t] = fmaf(wf[2 * i], __low2float(x2[i]), fmaf(wf[2 * i + 1], __high2float(x2[i]), acc[t]));
       }
     }
   }
 #pragma unroll
-  for (int t = 0; t < 8; ++t) {
+  for (int t = 0; t < RL_TOK; ++t) {
     const float v = warp_sum<32>(acc[t]);
-    if (lane == 0 && t0 + t < T) logits[int64_t(t0 + t) * E + e] = v + (bias ? bias[e] : 0.f);
+    if (lane == 0 && t < nt) logits[int64_t(t0 + t) * E + e] = v + (bias ? bias[e] : 0.f);
   }
 }
 
@@ -430,8 +452,14 @@ int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, cons
   if (!x || !wr || !logits_ws || !inds || !scores) return B2F_ERR_INVALID;
   if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
   cudaStream_t st = as_stream(stream);
-  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + 7) / 8), 1u};
-  route_logits_kernel<<<g1, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+  if (H > 8192) return B2F_ERR_UNSUPPORTED;
+  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
+  const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+          cudaSuccess)
+    return check_launch();
+  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
                                            static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits_ws);
   int rc = check_launch();
   if (rc != B2F_OK) return rc;

@@ -28,11 +28,9 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace b2f {
-
-constexpr int TC_M = 128;
-constexpr int TC_KC = 64;  // K per chunk (= quantization group)
 
 struct TcParams {
   const __nv_bfloat16* x;
@@ -54,60 +52,6 @@ struct TcParams {
   int32_t* err;
   int pk_stages, ab_stages;
 };
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, 128B-swizzled shared-memory matrix descriptor (8-row atoms of
-// 128 B stacked every 1024 B).
-__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
-  const uint64_t start = (smem_u32(tile) >> 4) & 0x3FFFu;
-  return start | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ uint32_t hsub2_bf(uint32_t a, uint32_t b) {
-  __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t hfma2_bf(uint32_t a, uint32_t b, uint32_t c) {
-  __nv_bfloat162 r = __hfma2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b),
-                             *reinterpret_cast<__nv_bfloat162*>(&c));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-
-__device__ __forceinline__ float silu_mul_tc(float g, float u) { return g / (1.f + __expf(-g)) * u; }
-
-// Byte offset of the 16-byte chunk `j` (8 K values) of row `r` in a K-major
-// 128B-swizzled tile.
-__device__ __forceinline__ int sw128_off(int r, int j) { return (r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4); }
 
 template <int BITS, int MAT, int TILE_N>
 __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tm0,
@@ -407,10 +351,10 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
 }
 
 // ---- host side -------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 static std::mutex g_encode_mu;
 
-static int get_encoder() {
+int get_encoder() {
   std::lock_guard<std::mutex> lock(g_encode_mu);
   if (g_encode) return B2F_OK;
   void* fn = nullptr;
@@ -426,7 +370,7 @@ static int get_encoder() {
 
 // Packed weights of all experts as a 2-D uint32 tensor [E*N rows, K*bits/32
 // words]; box = 128 rows x one chunk (8 or 16 words), 32B/64B swizzle.
-static int make_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int bits) {
+int make_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int bits) {
   const cuuint64_t words = cuuint64_t(K * bits / 32);
   const cuuint64_t dims[2] = {words, cuuint64_t(rows)};
   const cuuint64_t strides[1] = {words * 4};

@@ -1,0 +1,528 @@
+// (c) grouped expert GEMM on tcgen05/TMEM over expert-sorted token rows.
+//
+// The MoE plan (plan.cuh) orders the routed assignments by expert.  With
+// the activations copied into that order once per layer (b2f_moe_gather_rows,
+// which also applies the K order the weight unpack produces), every token
+// tile of an expert is a run of consecutive rows, so the tile's x block for a
+// K-chunk is one 2-D TMA load straight into the 128B-swizzled MMA layout.
+// The gate/up call writes its output rows in the same sorted, K-permuted
+// layout, so the down projection reads them the same way; the down call
+// writes rows back in assignment order for the weighted combine.
+//
+// Persistent CTAs (one per SM) walk the work units (slot, 128-row block) of
+// the plan; the pipeline runs across unit boundaries:
+//   warp 0      producer: per K-chunk one TMA load of the x tile and one of
+//               the packed words per matrix into a PS-deep ring; per 8
+//               chunks the rows' scales and biases with 4-byte cp.async
+//               into a 2-deep ring (no 16-byte row alignment needed).
+//   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, bf16 x bf16
+//               -> fp32 TMEM accumulators; tcgen05.commit frees stages.
+//   warps 2-9   converters: thread (row, K half) dequantizes 32 values of its
+//               row, w = q*s + b in one bf16 rounding, into the AS-deep A
+//               ring; then the epilogue (TMEM -> registers -> bf16 rows).
+// Every wait is bounded: on a timeout the kernel records B2F_ERR_TIMEOUT,
+// drains its own copies and MMAs (bounded), frees TMEM and returns.
+#include "common.cuh"
+#include "plan.cuh"
+#include "tc_common.cuh"
+
+namespace b2f {
+
+constexpr int TC2_THREADS = 320;
+constexpr int TC2_CONV_WARPS = 8;
+constexpr int TC2_SB_CHUNKS = 8;  // chunks per scale/bias block
+
+struct Tc2Params {
+  const int32_t* slot_count;
+  const int4* slots;
+  const int32_t* sorted;
+  const __nv_bfloat16* s[2];
+  const __nv_bfloat16* b[2];
+  int64_t sb_estride;  // scale elements per expert matrix (N * K/64)
+  int64_t N, K;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int out_sorted;
+  int n_rb;
+  int max_slots;
+  int32_t* err;
+  int PS, AS;
+};
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Position of K index k inside its group of 8 in the permuted layout
+// (0,4,1,5,2,6,3,7): the order the nibble unpack emits pairs in.
+__device__ __forceinline__ int64_t kperm_col(int64_t k) { return (k & ~int64_t(7)) | ((k & 3) << 1) | ((k >> 2) & 1); }
+
+template <int BITS, int MAT, int TILE_N>
+__global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Params p,
+                                                                  const __grid_constant__ CUtensorMap tmx,
+                                                                  const __grid_constant__ CUtensorMap tm0,
+                                                                  const __grid_constant__ CUtensorMap tm1) {
+  constexpr int PKB = TC_KC * BITS / 8;  // packed bytes per row per chunk
+  constexpr int PK_TILE = TC_M * PKB;
+  constexpr int A_TILE = TC_M * TC_KC * 2;
+  constexpr int B_TILE = TILE_N * TC_KC * 2;
+  constexpr int STAGE = B_TILE + MAT * PK_TILE;
+  constexpr int SB_BYTES = MAT * 2 * TC_M * TC2_SB_CHUNKS * 2;  // [MAT][s|b][128 rows][8 groups] bf16
+  constexpr uint32_t TMEM_COLS = (MAT * TILE_N <= 32) ? 32 : (MAT * TILE_N <= 64) ? 64 : (MAT * TILE_N <= 128) ? 128
+                                 : (MAT * TILE_N <= 256) ? 256 : 512;
+  constexpr int PK_SW_MASK = PKB / 16 - 1;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int PS = p.PS, AS = p.AS;
+
+  uint8_t* stages = smem;                              // [PS][B tile | MAT pk tiles]
+  uint8_t* atiles = stages + PS * STAGE;               // [AS][MAT][A_TILE]
+  uint8_t* sbuf = atiles + AS * MAT * A_TILE;          // [2][SB_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * SB_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = full + PS;
+  uint64_t* a_full = empty + PS;
+  uint64_t* a_empty = a_full + AS;
+  uint64_t* sb_full = a_empty + AS;
+  uint64_t* sb_empty = sb_full + 2;
+  uint64_t* acc_full = sb_empty + 2;
+  uint64_t* drain = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if (tid == 0) {
+    for (int s = 0; s < PS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < AS; ++s) {
+      mbar_init(&a_full[s], TC2_CONV_WARPS);
+      mbar_init(&a_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sb_full[s], 32);
+      mbar_init(&sb_empty[s], TC2_CONV_WARPS);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int n_slots = *p.slot_count;
+  if (n_slots > p.max_slots) n_slots = p.max_slots;
+  const int n_units = n_slots * p.n_rb;
+  const int n_chunks = int(p.K / TC_KC);
+  const int64_t ngroups = p.K / TC_KC;
+
+  if (warp == 0) {
+    // =============================== producer ===================================
+    // Control flow stays warp-uniform: lane 0 waits, the verdict is broadcast.
+    int g = 0, gb = 0;
+    bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+    for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+      const int4 sl = p.slots[u / p.n_rb];
+      const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
+      const int row0 = int(int64_t(sl.x) * p.N + m0);
+      for (int c = 0; c < n_chunks; ++c) {
+        if (c % TC2_SB_CHUNKS == 0) {
+          const int sbs = gb & 1;
+          int ok = 1;
+          if (lane == 0) ok = !*abort_flag && (gb < 2 || mbar_wait_bounded(&sb_empty[sbs], uint32_t(((gb >> 1) - 1) & 1)));
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          __syncwarp();
+          if (!ok) {
+            stop = true;
+            break;
+          }
+          uint8_t* dst = sbuf + sbs * SB_BYTES;
+          // items (m, s|b, row, group pair): 4-byte copies of two bf16 groups
+          for (int i = lane; i < MAT * 2 * TC_M * 4; i += 32) {
+            const int q = i & 3, r = (i >> 2) & (TC_M - 1), kind = (i >> 9) & 1, m = i >> 10;
+            const int64_t gg = c + 2 * q;
+            if (m0 + r < p.N && gg < ngroups) {
+              const __nv_bfloat16* base = kind ? (m ? p.b[1] : p.b[0]) : (m ? p.s[1] : p.s[0]);
+              const __nv_bfloat16* src = base + int64_t(sl.x) * p.sb_estride + (m0 + r) * ngroups + gg;
+              cp_async4(dst + ((m * 2 + kind) * TC_M + r) * 16 + q * 4, src);
+            }
+          }
+          cp_async_arrive_noinc(&sb_full[sbs]);
+          ++gb;
+        }
+        int ok = 1;
+        if (lane == 0) {
+          const int s = g % PS;
+          ok = !*abort_flag && (g < PS || mbar_wait_bounded(&empty[s], uint32_t(((g / PS) - 1) & 1)));
+          if (ok) {
+            uint8_t* st = stages + s * STAGE;
+            mbar_arrive_expect_tx(&full[s], uint32_t(STAGE));
+            tma_load_2d(st, &tmx, c * TC_KC, sl.y, &full[s]);
+            tma_load_2d(st + B_TILE, &tm0, c * (PKB / 4), row0, &full[s]);
+            if constexpr (MAT == 2) tma_load_2d(st + B_TILE + PK_TILE, &tm1, c * (PKB / 4), row0, &full[s]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          stop = true;
+          break;
+        }
+        ++g;
+      }
+    }
+    if (stop && lane == 0) *abort_flag = 1;
+    cp_async_wait_all();
+    if (lane == 0 && stop) {
+      // let the TMA loads already issued land before the CTA goes away
+      for (int k = 1; k <= PS && g - k >= 0; ++k) {
+        const int gi = g - k;
+        mbar_wait_bounded(&full[gi % PS], uint32_t((gi / PS) & 1), 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // =============================== MMA issuer =================================
+    if (lane == 0) {
+      int g = 0;
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+        const int4 sl = p.slots[u / p.n_rb];
+        const int n_pad = (sl.z + 15) & ~15;
+        const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n_pad >> 3) << 17) |
+                               (uint32_t(TC_M >> 4) << 24);
+        for (int c = 0; c < n_chunks; ++c, ++g) {
+          const int s = g % PS, sa = g % AS;
+          if (!mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) ||
+              !mbar_wait_bounded(&a_full[sa], uint32_t((g / AS) & 1))) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t bdesc = sw128_desc(stages + s * STAGE);
+#pragma unroll
+          for (int m = 0; m < MAT; ++m) {
+            const uint64_t adesc = sw128_desc(atiles + (sa * MAT + m) * A_TILE);
+#pragma unroll
+            for (int ks = 0; ks < TC_KC / 16; ++ks)
+              tc_mma(tmem + uint32_t(m * TILE_N), adesc + 2 * ks, bdesc + 2 * ks, idesc,
+                     (c > 0 || ks > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&a_empty[sa]);
+          if (c == n_chunks - 1) tc_commit(acc_full);
+        }
+      }
+      // all MMAs issued by this thread complete before TMEM is released
+      tc_commit(drain);
+      mbar_wait_bounded(drain, 0u, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // =============================== converters / epilogue ========================
+    const int tc = tid - 64;          // 0..255
+    const int t = tc & (TC_M - 1);    // row within the block
+    const int h = tc >> 7;            // K half of the chunk
+    const int sw = (t * PKB >> 7) & PK_SW_MASK;  // TMA swizzle of this packed row
+    // Every lane waits on the barriers; the verdict is made warp-uniform
+    // (__all_sync) so the .sync.aligned TMEM loads and __syncwarp never diverge.
+    int g = 0, gb = 0, it = 0;
+    bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
+    for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x, ++it) {
+      const int4 sl = p.slots[u / p.n_rb];
+      const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
+      for (int c = 0; c < n_chunks; ++c, ++g) {
+        const int s = g % PS, sa = g % AS, sbs = gb & 1;
+        const bool ok = !(*abort_flag) &&
+                        (c % TC2_SB_CHUNKS != 0 || mbar_wait_bounded(&sb_full[sbs], uint32_t((gb >> 1) & 1))) &&
+                        mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) &&
+                        (g < AS || mbar_wait_bounded(&a_empty[sa], uint32_t(((g / AS) - 1) & 1)));
+        if (!__all_sync(0xffffffffu, ok)) {
+          stop = true;
+          break;
+        }
+        const uint8_t* sbb = sbuf + sbs * SB_BYTES;
+#pragma unroll
+        for (int m = 0; m < MAT; ++m) {
+          const uint16_t sraw = *reinterpret_cast<const uint16_t*>(sbb + ((m * 2 + 0) * TC_M + t) * 16 +
+                                                                   (c % TC2_SB_CHUNKS) * 2);
+          const uint16_t braw = *reinterpret_cast<const uint16_t*>(sbb + ((m * 2 + 1) * TC_M + t) * 16 +
+                                                                   (c % TC2_SB_CHUNKS) * 2);
+          const uint32_t s2v = uint32_t(sraw) | (uint32_t(sraw) << 16);
+          const uint32_t b2v = uint32_t(braw) | (uint32_t(braw) << 16);
+          const uint8_t* prow = stages + s * STAGE + B_TILE + m * PK_TILE + t * PKB;
+          uint8_t* arow = atiles + (sa * MAT + m) * A_TILE;
+          if constexpr (BITS == 4) {
+            // this thread's 16 B = 4 words = K values 32h .. 32h+31
+            const uint4 q = *reinterpret_cast<const uint4*>(prow + ((h ^ sw) << 4));
+            const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t w = wds[i];
+              uint32_t o[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t qv = hsub2_bf(and_or(w >> (4 * j), 0x000F000Fu, 0x43004300u), 0x43004300u);
+                o[j] = hfma2_bf(qv, s2v, b2v);  // (k j, k j+4)
+              }
+              *reinterpret_cast<uint4*>(arow + sw128_off(t, 4 * h + i)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          } else {
+            // 32 B = two 16-byte pieces 2h, 2h+1; words (2i, 2i+1) -> A chunk i
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int piece = 2 * h + hh;
+              const uint4 q = *reinterpret_cast<const uint4*>(prow + ((piece ^ sw) << 4));
+              const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int ii = 0; ii < 2; ++ii) {
+                const uint32_t wa = wds[2 * ii], wb = wds[2 * ii + 1];
+                uint32_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float qa = float((wa >> (8 * j)) & 0xFFu), qb = float((wb >> (8 * j)) & 0xFFu);
+                  o[j] = hfma2_bf(pack_bf16x2(qa, qb), s2v, b2v);
+                }
+                *reinterpret_cast<uint4*>(arow + sw128_off(t, 2 * piece + ii)) = make_uint4(o[0], o[1], o[2], o[3]);
+              }
+            }
+          }
+        }
+        fence_proxy_async_smem();  // generic stores -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          if (c % TC2_SB_CHUNKS == TC2_SB_CHUNKS - 1 || c == n_chunks - 1) mbar_arrive(&sb_empty[sbs]);
+        }
+        if (c % TC2_SB_CHUNKS == TC2_SB_CHUNKS - 1 || c == n_chunks - 1) ++gb;
+      }
+      if (stop) break;
+      // ---- epilogue: TMEM -> registers -> bf16 ---------------------------------
+      if (!__all_sync(0xffffffffu, !(*abort_flag) && mbar_wait_bounded(acc_full, uint32_t(it & 1)))) {
+        stop = true;
+        break;
+      }
+      tc_fence_after();
+      const int qd = warp & 3;           // TMEM lane quarter this warp may read
+      const int ch = (warp - 2) >> 2;    // which 16-column blocks
+      const int row = 32 * qd + lane;
+      const int64_t gr = m0 + row;
+      const int n_tok = sl.z, n_pad = (n_tok + 15) & ~15;
+      const int64_t col = p.out_sorted ? kperm_col(gr) : gr;
+      for (int n0 = 16 * ch; n0 < n_pad; n0 += 32) {
+        uint32_t gv[16], uv[16];
+        tmem_ld16(tmem + (uint32_t(32 * qd) << 16) + uint32_t(n0), gv);
+        if constexpr (MAT == 2) tmem_ld16(tmem + (uint32_t(32 * qd) << 16) + uint32_t(TILE_N + n0), uv);
+        if (gr < p.N) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = n0 + i;
+            if (n < n_tok) {
+              float v = __uint_as_float(gv[i]);
+              if constexpr (MAT == 2) v = silu_mul_tc(v, __uint_as_float(uv[i]));
+              const int64_t o = p.out_sorted ? int64_t(sl.y + n) : int64_t(p.sorted[sl.y + n]);
+              p.out[o * p.ldo + col] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+      tc_fence_before();  // TMEM reads ordered before the next unit's MMAs
+    }
+    if (stop && lane == 0) *abort_flag = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+  if (tid == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+}
+
+// out[i, :] = x[row(sorted[i]), :] for every planned assignment i, each group
+// of 8 columns permuted to (0,4,1,5,2,6,3,7).
+__global__ void __launch_bounds__(256) moe_gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                              const int32_t* __restrict__ x_row_index,
+                                                              int64_t x_row_div, const int32_t* __restrict__ sorted,
+                                                              const int32_t* __restrict__ total_ptr, int64_t K,
+                                                              __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                              int64_t A) {
+  const int64_t total = min(int64_t(*total_ptr), A);
+  const int64_t vpr = K / 8;
+  for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total * vpr;
+       idx += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t i = idx / vpr, v = idx - i * vpr;
+    const int a = sorted[i];
+    const int64_t xr = x_row_index ? int64_t(x_row_index[a]) : int64_t(a) / x_row_div;
+    const uint4 xv = *reinterpret_cast<const uint4*>(x + xr * ldx + 8 * v);
+    *reinterpret_cast<uint4*>(out + i * ldo + 8 * v) =
+        make_uint4(prmt(xv.x, xv.z, 0x5410u), prmt(xv.x, xv.z, 0x7632u), prmt(xv.y, xv.w, 0x5410u),
+                   prmt(xv.y, xv.w, 0x7632u));
+  }
+}
+
+static int make_rows_map(CUtensorMap* map, const void* x, int64_t rows, int64_t K, int64_t ldx, int box_rows) {
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(TC_KC), cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
+}
+
+static int g_sms_tc2 = 0;
+
+template <int BITS, int MAT, int TILE_N>
+static int launch_tc2_cfg(Tc2Params p, const CUtensorMap& mx, const CUtensorMap& m0, const CUtensorMap& m1,
+                          cudaStream_t st) {
+  constexpr int PK_TILE = TC_M * TC_KC * BITS / 8;
+  constexpr int A_TILE = TC_M * TC_KC * 2;
+  constexpr int B_TILE = TILE_N * TC_KC * 2;
+  constexpr int STAGE = B_TILE + MAT * PK_TILE;
+  constexpr int SB_BYTES = MAT * 2 * TC_M * TC2_SB_CHUNKS * 2;
+  const int budget = 220 * 1024;
+  int AS = 3;
+  if (MAT * A_TILE * AS + 2 * SB_BYTES + 3 * STAGE > budget) AS = 2;
+  int PS = (budget - AS * MAT * A_TILE - 2 * SB_BYTES - 1024 - 256) / STAGE;
+  if (PS > 10) PS = 10;
+  if (PS < 2) return B2F_ERR_UNSUPPORTED;
+  p.PS = PS;
+  p.AS = AS;
+  const int smem = 1024 + PS * STAGE + AS * MAT * A_TILE + 2 * SB_BYTES + 8 * (2 * PS + 2 * AS + 6) + 16;
+  if (smem > 227 * 1024) return B2F_ERR_UNSUPPORTED;
+  auto kern = qgemm_tc2_kernel<BITS, MAT, TILE_N>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  if (g_sms_tc2 == 0) {
+    int dev = 0, n = 0;
+    g_sms_tc2 = (cudaGetDevice(&dev) == cudaSuccess &&
+                 cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+                    ? n
+                    : 148;
+  }
+  const int64_t max_units = int64_t(p.max_slots) * p.n_rb;
+  const int grid = int(max_units < g_sms_tc2 ? max_units : g_sms_tc2);
+  kern<<<grid < 1 ? 1 : grid, TC2_THREADS, smem, st>>>(p, mx, m0, m1);
+  return check_launch();
+}
+
+template <int BITS, int MAT>
+static int launch_tc2_bits(const Tc2Params& p, const CUtensorMap& mx, const CUtensorMap& m0, const CUtensorMap& m1,
+                           int tile, cudaStream_t st) {
+  if (tile <= 16) return launch_tc2_cfg<BITS, MAT, 16>(p, mx, m0, m1, st);
+  if (tile <= 32) return launch_tc2_cfg<BITS, MAT, 32>(p, mx, m0, m1, st);
+  if (tile <= 64) return launch_tc2_cfg<BITS, MAT, 64>(p, mx, m0, m1, st);
+  if (tile <= 128) return launch_tc2_cfg<BITS, MAT, 128>(p, mx, m0, m1, st);
+  return launch_tc2_cfg<BITS, MAT, 256>(p, mx, m0, m1, st);
+}
+
+static int tile_rows(int tile) { return tile <= 16 ? 16 : tile <= 32 ? 32 : tile <= 64 ? 64 : tile <= 128 ? 128 : 256; }
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" {
+
+int b2f_moe_gather_rows(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div, int64_t A,
+                        int64_t E, int tile, const void* plan_workspace, int64_t plan_workspace_bytes, int64_t K,
+                        void* out, int64_t ldo, void* stream) {
+  if (A < 0 || E <= 0 || K <= 0 || K % 8 != 0 || ldx < K || ldo < K) return B2F_ERR_INVALID;
+  if (!x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x || !out || !plan_workspace) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(out, 16) || ldx % 8 || ldo % 8) return B2F_ERR_ALIGN;
+  const PlanLayout L = plan_layout(A, E, tile);
+  if (plan_workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
+  const char* ws = static_cast<const char*>(plan_workspace);
+  const int32_t* offsets = reinterpret_cast<const int32_t*>(ws + L.off_offsets);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t work = A * (K / 8);
+  const int64_t blocks = (work + 255) / 256;
+  const int grid = int(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8);
+  moe_gather_rows_kernel<<<grid, 256, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, x_row_index, x_row_div > 0 ? x_row_div : 1,
+      reinterpret_cast<const int32_t*>(ws + L.off_sorted), offsets + E, K, static_cast<__nv_bfloat16*>(out), ldo, A);
+  return check_launch();
+}
+
+int b2f_sorted_qgemm_affine_tcgen05(const void* x_sorted, int64_t ldx, int64_t A, int64_t E, const uint32_t* w_gate,
+                                    const void* s_gate, const void* b_gate, const uint32_t* w_up, const void* s_up,
+                                    const void* b_up, int64_t N, int64_t K, int bits, int group_size, int tile,
+                                    const void* plan_workspace, int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                    int out_sorted, void* stream) {
+  if (!(bits == 4 || bits == 8) || group_size != 64) return B2F_ERR_UNSUPPORTED;
+  if (N <= 0 || K <= 0 || K % 64 != 0) return B2F_ERR_INVALID;
+  if ((K / 64) % 2 != 0) return B2F_ERR_UNSUPPORTED;  // 4-byte scale copies cover two groups
+  if (A < 0 || E <= 0 || tile < 16 || tile > 256 || tile % 16) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x_sorted || !w_gate || !s_gate || !b_gate || !out || !plan_workspace) return B2F_ERR_INVALID;
+  if (out_sorted && N % 8 != 0) return B2F_ERR_INVALID;  // permuted columns stay inside the row
+  if (w_up && (!s_up || !b_up)) return B2F_ERR_INVALID;
+  if (ldx < K || ldo < N) return B2F_ERR_INVALID;
+  if (!aligned(x_sorted, 16) || ldx % 8 || !aligned(w_gate, 16) || (w_up && !aligned(w_up, 16)))
+    return B2F_ERR_ALIGN;
+  if (!aligned(s_gate, 4) || !aligned(b_gate, 4) || (w_up && (!aligned(s_up, 4) || !aligned(b_up, 4))))
+    return B2F_ERR_ALIGN;
+  const PlanLayout L = plan_layout(A, E, tile);
+  if (plan_workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
+  const int64_t max_slots = plan_max_slots(A, E, tile);
+  const int64_t n_rb = (N + TC_M - 1) / TC_M;
+  if (max_slots * n_rb > 0x7fffffff || E * N > 0x7fffffff || A > 0x7fffffff) return B2F_ERR_UNSUPPORTED;
+  const char* ws = static_cast<const char*>(plan_workspace);
+  Tc2Params p{};
+  p.slot_count = reinterpret_cast<const int32_t*>(ws + L.off_hdr);
+  p.slots = reinterpret_cast<const int4*>(ws + L.off_slots);
+  p.sorted = reinterpret_cast<const int32_t*>(ws + L.off_sorted);
+  p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
+  p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
+  p.s[1] = static_cast<const __nv_bfloat16*>(w_up ? s_up : s_gate);
+  p.b[1] = static_cast<const __nv_bfloat16*>(w_up ? b_up : b_gate);
+  p.sb_estride = N * (K / 64);
+  p.N = N;
+  p.K = K;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.out_sorted = out_sorted ? 1 : 0;
+  p.n_rb = int(n_rb);
+  p.max_slots = int(max_slots);
+  int rc = get_encoder();
+  if (rc != B2F_OK) return rc;
+  CUtensorMap mx, m0, m1;
+  rc = make_rows_map(&mx, x_sorted, A, K, ldx, tile_rows(tile));
+  if (rc != B2F_OK) return rc;
+  rc = make_weight_map(&m0, w_gate, E * N, K, bits);
+  if (rc != B2F_OK) return rc;
+  if (w_up) {
+    rc = make_weight_map(&m1, w_up, E * N, K, bits);
+    if (rc != B2F_OK) return rc;
+  } else {
+    m1 = m0;
+  }
+  cudaStream_t st = as_stream(stream);
+  if (bits == 4)
+    return w_up ? launch_tc2_bits<4, 2>(p, mx, m0, m1, tile, st) : launch_tc2_bits<4, 1>(p, mx, m0, m1, tile, st);
+  return w_up ? launch_tc2_bits<8, 2>(p, mx, m0, m1, tile, st) : launch_tc2_bits<8, 1>(p, mx, m0, m1, tile, st);
+}
+
+}  // extern "C"

@@ -230,3 +230,45 @@ def round(a, decimals=0):  # noqa: A001
 
 def clip(a, a_min, a_max):
     return array(_fit(np.clip(a._a, a_min, a_max), a.dtype), a.dtype)
+
+
+# -- additions used by kv_compression.py / streaming_llm.py ---------------------
+def _arr_tolist(self):
+    return self._a.tolist()
+
+
+array.tolist = _arr_tolist
+
+
+def ones(shape, dtype=float32):
+    return array(np.ones(shape, dtype=np.float32 if dtype.is_float else dtype.np), dtype)
+
+
+def arange(start, stop=None, step=1, dtype=None):
+    if stop is None:
+        start, stop = 0, start
+    return array(np.arange(start, stop, step).astype(np.int32), dtype or int32)
+
+
+def argsort(a, axis=-1):
+    # stable order for equal keys (lower position first)
+    return array(np.argsort(a._a, axis=axis, kind="stable").astype(np.int32), int32)
+
+
+def sort(a, axis=-1):
+    return array(np.sort(a._a, axis=axis, kind="stable"), a.dtype)
+
+
+def _getitem_ext(self, idx):
+    if isinstance(idx, array):
+        idx = idx._a
+    elif isinstance(idx, tuple):
+        idx = tuple(i._a if isinstance(i, array) else i for i in idx)
+    return array(self._a[idx], self.dtype)
+
+
+array.__getitem__ = _getitem_ext
+
+
+def eval(*args):  # noqa: A001 - MLX's lazy-evaluation barrier; NumPy is eager
+    return None

@@ -22,6 +22,11 @@ What each fixture pins:
 * ``ep_shard.json`` -- ``ExpertShard`` ownership and ``owner_of`` from
   ``mlx_flash_compress/distributed_experts.py:36-80`` executed unmodified.
 * ``moe_dispatch.npz`` -- ``moe_dispatch_numpy`` (``kernels/ops.py:138-148``).
+* ``kv_evict.npz`` -- the reference's own ``CompressedKVCache`` (H2O and
+  ScissorHands scoring, ``kv_compression.py``) and ``StreamingLLMCache``
+  (``streaming_llm.py``) executed with the NumPy ``mlx.core`` stand-in on
+  seeded update sequences: every step's inputs, the cache contents after the
+  step, and the tracked importance arrays.
 """
 
 import importlib.util
@@ -203,6 +208,64 @@ def gen_dispatch(out):
     np.savez_compressed(os.path.join(out, "moe_dispatch.npz"), **arrays)
 
 
+def _softmax_rows(rng, H, Sq, S):
+    z = rng.standard_normal((H, Sq, S)).astype(np.float32) * 2.0
+    z = np.exp(z - z.max(axis=-1, keepdims=True))
+    return (z / z.sum(axis=-1, keepdims=True)).astype(np.float32)
+
+
+def gen_evict(out):
+    sys.path.insert(0, os.path.join(HERE, "_mlx_standin"))
+    import mlx.core as mx
+
+    kvc = _load_ref_module("ref_kv_compression", "mlx_flash_compress/kv_compression.py")
+    sll = _load_ref_module("ref_streaming_llm", "mlx_flash_compress/streaming_llm.py")
+    arrays = {}
+    L, H, D = 2, 4, 8
+    for scoring in ("h2o", "scissorhands"):
+        rng = np.random.default_rng(7 if scoring == "h2o" else 8)
+        cfg = kvc.KVCompressionConfig(budget_ratio=0.8, sink_tokens=2, recent_window=6, scoring=scoring)
+        cache = kvc.CompressedKVCache(cfg, L, H, D)
+        lens = [0] * L
+        steps = [40] + [1] * 6 + [7, 1, 1, 1]
+        for si, n in enumerate(steps):
+            for li in range(L):
+                k = rng.standard_normal((H, n, D)).astype(np.float32)
+                v = rng.standard_normal((H, n, D)).astype(np.float32)
+                S = lens[li] + n
+                a = _softmax_rows(rng, H, n, S)
+                ko, vo = cache.update(li, mx.array(k), mx.array(v), mx.array(a))
+                lens[li] = ko.shape[1]
+                key = f"{scoring}/s{si}/l{li}"
+                arrays[f"{key}/k"], arrays[f"{key}/v"], arrays[f"{key}/attn"] = k, v, a
+                arrays[f"{key}/k_out"] = np.asarray(ko, np.float32)
+                arrays[f"{key}/v_out"] = np.asarray(vo, np.float32)
+                imp = cache.tracker._importance[li]
+                arrays[f"{key}/imp"] = np.asarray(imp, np.float32) if imp is not None else np.zeros(0, np.float32)
+                gi = cache.tracker._global_importance
+                arrays[f"{key}/gimp"] = np.asarray(gi, np.float32) if gi is not None else np.zeros(0, np.float32)
+        arrays[f"{scoring}/steps"] = np.array(steps)
+        arrays[f"{scoring}/stats"] = np.array([cache.get_stats()["compression_count"],
+                                               cache.get_stats()["total_evicted"]])
+    rng = np.random.default_rng(9)
+    cache = sll.StreamingLLMCache(sll.StreamingLLMConfig(num_sink_tokens=4, window_size=16), L, H, D)
+    steps = [10, 3, 3, 3, 3, 1, 1, 20, 1]
+    for si, n in enumerate(steps):
+        for li in range(L):
+            k = rng.standard_normal((H, n, D)).astype(np.float32)
+            v = rng.standard_normal((H, n, D)).astype(np.float32)
+            ko, vo = cache.update(li, mx.array(k), mx.array(v))
+            key = f"stream/s{si}/l{li}"
+            arrays[f"{key}/k"], arrays[f"{key}/v"] = k, v
+            arrays[f"{key}/k_out"] = np.asarray(ko, np.float32)
+            arrays[f"{key}/v_out"] = np.asarray(vo, np.float32)
+            arrays[f"{key}/pos"] = np.asarray(cache.get_positions(li)).astype(np.int32)
+    arrays["stream/steps"] = np.array(steps)
+    st = cache.get_stats()
+    arrays["stream/stats"] = np.array([st["eviction_count"], st["total_evicted_tokens"], st["current_length"]])
+    np.savez_compressed(os.path.join(out, "kv_evict.npz"), **arrays)
+
+
 def main():
     out = HERE
     n = gen_kv(out)
@@ -210,7 +273,8 @@ def main():
     gen_affine(out)
     gen_ep(out)
     gen_dispatch(out)
-    print(f"golden vectors written: {n} KV cases + mixed/affine/ep/dispatch")
+    gen_evict(out)
+    print(f"golden vectors written: {n} KV cases + mixed/affine/ep/dispatch/evict")
 
 
 if __name__ == "__main__":

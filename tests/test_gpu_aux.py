@@ -141,7 +141,7 @@ def test_quantized_linear_from_linear(dev):
     assert np.array_equal(to_np(ql.weight), wq)
     for M in (3, 96):
         x = torch.randn(M, 512, device=dev).to(torch.bfloat16)
-        want = affine.quantized_matmul(to_np(x), wq, s, b, True, 64, 4) + to_np(lin.bias.to(torch.bfloat16))
+        want = affine.quantized_matmul(to_np(x), wq, s, b, True, 64, 4) + to_np(lin.bias.detach().to(torch.bfloat16))
         assert_close(to_np(ql(x)), want, what=f"QuantizedLinear M={M}")
 
 

@@ -133,3 +133,58 @@ def test_fake_quant_oracle_rules():
     assert np.array_equal(out, (np.clip(np.rint(w / scale), -8, 7) * scale).astype(np.float32))
     z, za = sensitivity.fake_quantize_sym(np.zeros(4, np.float32), 8, "bf16")
     assert za == 0 and not z.any()
+
+
+def _replay_compressed(z, scoring):
+    """Run the oracle's eviction over the recorded update sequence."""
+    from oracle import kv_evict
+
+    steps = z[f"{scoring}/steps"]
+    L = 2
+    tr = kv_evict.Tracker(L, scoring)
+    keys = [None] * L
+    for si, n in enumerate(steps):
+        for li in range(L):
+            key = f"{scoring}/s{si}/l{li}"
+            k = z[f"{key}/k"]
+            keys[li] = k if keys[li] is None else np.concatenate([keys[li], k], axis=1)
+            tr.record(li, z[f"{key}/attn"])
+            S = keys[li].shape[1]
+            budget = max(2 + 6, max(1, int(S * 0.8)))
+            if S > budget:
+                keep = kv_evict.keep_indices(tr.importance(li), S, 2, 6, budget)
+                if len(keep) != S:
+                    keys[li] = keys[li][:, keep, :]
+                    tr.truncate(keep)
+            yield key, keys[li], tr
+
+
+@pytest.mark.parametrize("scoring", ["h2o", "scissorhands"])
+def test_eviction_oracle_matches_reference_goldens(golden, scoring):
+    z = golden("kv_evict.npz")
+    for key, keys, tr in _replay_compressed(z, scoring):
+        li = int(key[-1])
+        assert np.array_equal(keys, z[f"{key}/k_out"]), key
+        imp = tr.imp[li] if tr.imp[li] is not None else np.zeros(0, np.float32)
+        assert np.allclose(imp, z[f"{key}/imp"], rtol=1e-6, atol=1e-7), key
+        if scoring == "h2o":
+            assert np.allclose(tr.glob, z[f"{key}/gimp"], rtol=1e-6, atol=1e-7), key
+
+
+def test_streaming_oracle_matches_reference_goldens(golden):
+    from oracle import kv_evict
+
+    z = golden("kv_evict.npz")
+    keys, pos, nxt = [None, None], [None, None], [0, 0]
+    for si, n in enumerate(z["stream/steps"]):
+        for li in range(2):
+            key = f"stream/s{si}/l{li}"
+            k = z[f"{key}/k"]
+            p = np.arange(nxt[li], nxt[li] + n, dtype=np.int32)
+            nxt[li] += n
+            keys[li] = k if keys[li] is None else np.concatenate([keys[li], k], axis=1)
+            pos[li] = p if pos[li] is None else np.concatenate([pos[li], p])
+            keep = kv_evict.streaming_keep(keys[li].shape[1], 4, 16)
+            keys[li], pos[li] = keys[li][:, keep, :], pos[li][keep]
+            assert np.array_equal(keys[li], z[f"{key}/k_out"]), key
+            assert np.array_equal(pos[li], z[f"{key}/pos"]), key
