@@ -127,7 +127,7 @@ def profile_kernels(dec, torch):
 
     def timed_call(name, *args):
         tag = None
-        if name in ("b2f_gather_qgemv_affine", "b2f_gather_qgemm_affine_tcgen05"):
+        if name in ("b2f_gather_qgemv_affine", "b2f_gather_qgemm_affine_tcgen05", "b2f_sorted_qgemm_affine_tcgen05"):
             tag = "moe_gate_up" if state["gather"] % 2 == 0 else "moe_down"
             state["gather"] += 1
         elif name == "b2f_qkv_decode_attn":

@@ -12,14 +12,15 @@
 // Persistent CTAs (one per SM) walk the work units (slot, 128-row block) of
 // the plan; the pipeline runs across unit boundaries:
 //   warp 0      producer: per K-chunk one TMA load of the x tile and one of
-//               the packed words per matrix into a PS-deep ring; per 8
-//               chunks the rows' scales and biases with 4-byte cp.async
-//               into a 2-deep ring (no 16-byte row alignment needed).
+//               the packed words per matrix into a PS-deep ring.
 //   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, bf16 x bf16
 //               -> fp32 TMEM accumulators; tcgen05.commit frees stages.
 //   warps 2-9   converters: thread (row, K half) dequantizes 32 values of its
 //               row, w = q*s + b in one bf16 rounding, into the AS-deep A
 //               ring; then the epilogue (TMEM -> registers -> bf16 rows).
+//               Scales and biases come in blocks of 8 groups (4-byte loads
+//               into registers), one block ahead in the CTA's unit order,
+//               so their memory latency hides behind 8 chunks of work.
 // Every wait is bounded: on a timeout the kernel records B2F_ERR_TIMEOUT,
 // drains its own copies and MMAs (bounded), frees TMEM and returns.
 #include "common.cuh"
@@ -30,7 +31,7 @@ namespace b2f {
 
 constexpr int TC2_THREADS = 320;
 constexpr int TC2_CONV_WARPS = 8;
-constexpr int TC2_SB_CHUNKS = 8;  // chunks per scale/bias block
+constexpr int TC2_SB_CHUNKS = 8;  // chunks per scale/bias register block
 
 struct Tc2Params {
   const int32_t* slot_count;
@@ -49,14 +50,6 @@ struct Tc2Params {
   int PS, AS;
 };
 
-__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
 // Position of K index k inside its group of 8 in the permuted layout
 // (0,4,1,5,2,6,3,7): the order the nibble unpack emits pairs in.
 __device__ __forceinline__ int64_t kperm_col(int64_t k) { return (k & ~int64_t(7)) | ((k & 3) << 1) | ((k >> 2) & 1); }
@@ -71,7 +64,6 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
   constexpr int A_TILE = TC_M * TC_KC * 2;
   constexpr int B_TILE = TILE_N * TC_KC * 2;
   constexpr int STAGE = B_TILE + MAT * PK_TILE;
-  constexpr int SB_BYTES = MAT * 2 * TC_M * TC2_SB_CHUNKS * 2;  // [MAT][s|b][128 rows][8 groups] bf16
   constexpr uint32_t TMEM_COLS = (MAT * TILE_N <= 32) ? 32 : (MAT * TILE_N <= 64) ? 64 : (MAT * TILE_N <= 128) ? 128
                                  : (MAT * TILE_N <= 256) ? 256 : 512;
   constexpr int PK_SW_MASK = PKB / 16 - 1;
@@ -83,15 +75,12 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
 
   uint8_t* stages = smem;                              // [PS][B tile | MAT pk tiles]
   uint8_t* atiles = stages + PS * STAGE;               // [AS][MAT][A_TILE]
-  uint8_t* sbuf = atiles + AS * MAT * A_TILE;          // [2][SB_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * SB_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(atiles + AS * MAT * A_TILE);
   uint64_t* full = bars;
   uint64_t* empty = full + PS;
   uint64_t* a_full = empty + PS;
   uint64_t* a_empty = a_full + AS;
-  uint64_t* sb_full = a_empty + AS;
-  uint64_t* sb_empty = sb_full + 2;
-  uint64_t* acc_full = sb_empty + 2;
+  uint64_t* acc_full = a_empty + AS;
   uint64_t* drain = acc_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -104,10 +93,6 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     for (int s = 0; s < AS; ++s) {
       mbar_init(&a_full[s], TC2_CONV_WARPS);
       mbar_init(&a_empty[s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sb_full[s], 32);
-      mbar_init(&sb_empty[s], TC2_CONV_WARPS);
     }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
@@ -134,37 +119,13 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
   if (warp == 0) {
     // =============================== producer ===================================
     // Control flow stays warp-uniform: lane 0 waits, the verdict is broadcast.
-    int g = 0, gb = 0;
+    int g = 0;
     bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
     for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
       const int4 sl = p.slots[u / p.n_rb];
       const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
       const int row0 = int(int64_t(sl.x) * p.N + m0);
       for (int c = 0; c < n_chunks; ++c) {
-        if (c % TC2_SB_CHUNKS == 0) {
-          const int sbs = gb & 1;
-          int ok = 1;
-          if (lane == 0) ok = !*abort_flag && (gb < 2 || mbar_wait_bounded(&sb_empty[sbs], uint32_t(((gb >> 1) - 1) & 1)));
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          __syncwarp();
-          if (!ok) {
-            stop = true;
-            break;
-          }
-          uint8_t* dst = sbuf + sbs * SB_BYTES;
-          // items (m, s|b, row, group pair): 4-byte copies of two bf16 groups
-          for (int i = lane; i < MAT * 2 * TC_M * 4; i += 32) {
-            const int q = i & 3, r = (i >> 2) & (TC_M - 1), kind = (i >> 9) & 1, m = i >> 10;
-            const int64_t gg = c + 2 * q;
-            if (m0 + r < p.N && gg < ngroups) {
-              const __nv_bfloat16* base = kind ? (m ? p.b[1] : p.b[0]) : (m ? p.s[1] : p.s[0]);
-              const __nv_bfloat16* src = base + int64_t(sl.x) * p.sb_estride + (m0 + r) * ngroups + gg;
-              cp_async4(dst + ((m * 2 + kind) * TC_M + r) * 16 + q * 4, src);
-            }
-          }
-          cp_async_arrive_noinc(&sb_full[sbs]);
-          ++gb;
-        }
         int ok = 1;
         if (lane == 0) {
           const int s = g % PS;
@@ -186,7 +147,6 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
       }
     }
     if (stop && lane == 0) *abort_flag = 1;
-    cp_async_wait_all();
     if (lane == 0 && stop) {
       // let the TMA loads already issued land before the CTA goes away
       for (int k = 1; k <= PS && g - k >= 0; ++k) {
@@ -239,30 +199,70 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     const int sw = (t * PKB >> 7) & PK_SW_MASK;  // TMA swizzle of this packed row
     // Every lane waits on the barriers; the verdict is made warp-uniform
     // (__all_sync) so the .sync.aligned TMEM loads and __syncwarp never diverge.
-    int g = 0, gb = 0, it = 0;
+    // scale/bias register blocks: [m][s|b][4 words = 8 groups]; `nxt` is
+    // loaded one block ahead along this CTA's (unit, block) sequence
+    const int nblk = (n_chunks + TC2_SB_CHUNKS - 1) / TC2_SB_CHUNKS;
+    uint32_t cur[MAT][2][4], nxt[MAT][2][4];
+    int pu = blockIdx.x, pj = 0;
+    auto load_block = [&](uint32_t (&dst)[MAT][2][4]) {
+      const bool live = pu < n_units;
+      int64_t base = 0;
+      int64_t row = TC_M;
+      if (live) {
+        const int4 su = p.slots[pu / p.n_rb];
+        row = int64_t(pu % p.n_rb) * TC_M + t;
+        base = int64_t(su.x) * p.sb_estride + row * ngroups + int64_t(pj) * TC2_SB_CHUNKS;
+      }
+#pragma unroll
+      for (int m = 0; m < MAT; ++m)
+#pragma unroll
+        for (int kind = 0; kind < 2; ++kind) {
+          const __nv_bfloat16* src = kind ? (m ? p.b[1] : p.b[0]) : (m ? p.s[1] : p.s[0]);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int64_t gg = int64_t(pj) * TC2_SB_CHUNKS + 2 * i;
+            dst[m][kind][i] = (live && row < p.N && gg < ngroups)
+                                  ? __ldg(reinterpret_cast<const uint32_t*>(src + base + 2 * i))
+                                  : 0u;
+          }
+        }
+      if (++pj == nblk) {
+        pj = 0;
+        pu += gridDim.x;
+      }
+    };
+    load_block(cur);
+    load_block(nxt);
+    int g = 0, it = 0;
     bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
     for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x, ++it) {
       const int4 sl = p.slots[u / p.n_rb];
       const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
       for (int c = 0; c < n_chunks; ++c, ++g) {
-        const int s = g % PS, sa = g % AS, sbs = gb & 1;
-        const bool ok = !(*abort_flag) &&
-                        (c % TC2_SB_CHUNKS != 0 || mbar_wait_bounded(&sb_full[sbs], uint32_t((gb >> 1) & 1))) &&
-                        mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) &&
+        const int s = g % PS, sa = g % AS;
+        if (c % TC2_SB_CHUNKS == 0 && g > 0) {
+#pragma unroll
+          for (int m = 0; m < MAT; ++m)
+#pragma unroll
+            for (int kind = 0; kind < 2; ++kind)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) cur[m][kind][i] = nxt[m][kind][i];
+          load_block(nxt);
+        }
+        const bool ok = !(*abort_flag) && mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) &&
                         (g < AS || mbar_wait_bounded(&a_empty[sa], uint32_t(((g / AS) - 1) & 1)));
         if (!__all_sync(0xffffffffu, ok)) {
           stop = true;
           break;
         }
-        const uint8_t* sbb = sbuf + sbs * SB_BYTES;
+        const int cw = (c % TC2_SB_CHUNKS) >> 1, chi = c & 1;  // word and half of this chunk's group
 #pragma unroll
         for (int m = 0; m < MAT; ++m) {
-          const uint16_t sraw = *reinterpret_cast<const uint16_t*>(sbb + ((m * 2 + 0) * TC_M + t) * 16 +
-                                                                   (c % TC2_SB_CHUNKS) * 2);
-          const uint16_t braw = *reinterpret_cast<const uint16_t*>(sbb + ((m * 2 + 1) * TC_M + t) * 16 +
-                                                                   (c % TC2_SB_CHUNKS) * 2);
-          const uint32_t s2v = uint32_t(sraw) | (uint32_t(sraw) << 16);
-          const uint32_t b2v = uint32_t(braw) | (uint32_t(braw) << 16);
+          const uint32_t sw4 = cw == 0 ? cur[m][0][0] : cw == 1 ? cur[m][0][1] : cw == 2 ? cur[m][0][2] : cur[m][0][3];
+          const uint32_t bw4 = cw == 0 ? cur[m][1][0] : cw == 1 ? cur[m][1][1] : cw == 2 ? cur[m][1][2] : cur[m][1][3];
+          // broadcast the chunk's bf16 (low half = even group) to both halves
+          const uint32_t s2v = prmt(sw4, 0u, chi ? 0x3232u : 0x1010u);
+          const uint32_t b2v = prmt(bw4, 0u, chi ? 0x3232u : 0x1010u);
           const uint8_t* prow = stages + s * STAGE + B_TILE + m * PK_TILE + t * PKB;
           uint8_t* arow = atiles + (sa * MAT + m) * A_TILE;
           if constexpr (BITS == 4) {
@@ -303,11 +303,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
         }
         fence_proxy_async_smem();  // generic stores -> tensor-core reads
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&a_full[sa]);
-          if (c % TC2_SB_CHUNKS == TC2_SB_CHUNKS - 1 || c == n_chunks - 1) mbar_arrive(&sb_empty[sbs]);
-        }
-        if (c % TC2_SB_CHUNKS == TC2_SB_CHUNKS - 1 || c == n_chunks - 1) ++gb;
+        if (lane == 0) mbar_arrive(&a_full[sa]);
       }
       if (stop) break;
       // ---- epilogue: TMEM -> registers -> bf16 ---------------------------------
@@ -395,16 +391,15 @@ static int launch_tc2_cfg(Tc2Params p, const CUtensorMap& mx, const CUtensorMap&
   constexpr int A_TILE = TC_M * TC_KC * 2;
   constexpr int B_TILE = TILE_N * TC_KC * 2;
   constexpr int STAGE = B_TILE + MAT * PK_TILE;
-  constexpr int SB_BYTES = MAT * 2 * TC_M * TC2_SB_CHUNKS * 2;
   const int budget = 220 * 1024;
   int AS = 3;
-  if (MAT * A_TILE * AS + 2 * SB_BYTES + 3 * STAGE > budget) AS = 2;
-  int PS = (budget - AS * MAT * A_TILE - 2 * SB_BYTES - 1024 - 256) / STAGE;
+  if (MAT * A_TILE * AS + 3 * STAGE > budget) AS = 2;
+  int PS = (budget - AS * MAT * A_TILE - 1024 - 256) / STAGE;
   if (PS > 10) PS = 10;
   if (PS < 2) return B2F_ERR_UNSUPPORTED;
   p.PS = PS;
   p.AS = AS;
-  const int smem = 1024 + PS * STAGE + AS * MAT * A_TILE + 2 * SB_BYTES + 8 * (2 * PS + 2 * AS + 6) + 16;
+  const int smem = 1024 + PS * STAGE + AS * MAT * A_TILE + 8 * (2 * PS + 2 * AS + 2) + 16;
   if (smem > 227 * 1024) return B2F_ERR_UNSUPPORTED;
   auto kern = qgemm_tc2_kernel<BITS, MAT, TILE_N>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -473,7 +468,7 @@ int b2f_sorted_qgemm_affine_tcgen05(const void* x_sorted, int64_t ldx, int64_t A
                                     int out_sorted, void* stream) {
   if (!(bits == 4 || bits == 8) || group_size != 64) return B2F_ERR_UNSUPPORTED;
   if (N <= 0 || K <= 0 || K % 64 != 0) return B2F_ERR_INVALID;
-  if ((K / 64) % 2 != 0) return B2F_ERR_UNSUPPORTED;  // 4-byte scale copies cover two groups
+  if ((K / 64) % 2 != 0) return B2F_ERR_UNSUPPORTED;  // 4-byte scale loads cover two groups
   if (A < 0 || E <= 0 || tile < 16 || tile > 256 || tile % 16) return B2F_ERR_INVALID;
   if (A == 0) return B2F_OK;
   if (!x_sorted || !w_gate || !s_gate || !b_gate || !out || !plan_workspace) return B2F_ERR_INVALID;
