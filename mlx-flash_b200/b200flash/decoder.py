@@ -181,7 +181,7 @@ class Qwen3MoeDecoder:
         # average, else the register-fragment GEMV (tiles of 16 tokens)
         if self.ep is None:
             if moe_engine == "auto":
-                moe_engine = "tc" if A >= E else "gemv"
+                moe_engine = "tc_gather" if A >= E else "gemv"
             if moe_engine not in ("tc", "tc_gather", "gemv"):
                 raise ValueError(f"unknown expert engine {moe_engine!r}")
             if moe_engine == "tc" and ((H // 64) % 2 or (I // 64) % 2):

@@ -136,7 +136,7 @@ class ExpertParallelMoE:
         self.wts = torch.zeros(A, dtype=torch.float32, device=dev)
         self.local = torch.full((A,), -1, dtype=torch.int32, device=dev)
         if engine == "auto":
-            engine = "tc" if T * top_k >= self.e_count and group_size == 64 else "gemv"
+            engine = "tc_gather" if T * top_k >= self.e_count and group_size == 64 else "gemv"
         if engine not in ("tc", "tc_gather", "gemv"):
             raise ValueError(f"unknown expert engine {engine!r}")
         if engine == "tc" and ((hidden // 64) % 2 or (inter // 64) % 2):

@@ -11,8 +11,11 @@
 //
 // Persistent CTAs (one per SM) walk the work units (slot, 128-row block) of
 // the plan; the pipeline runs across unit boundaries:
-//   warp 0      producer: per K-chunk one TMA load of the x tile and one of
-//               the packed words per matrix into a PS-deep ring.
+//   warp 0      producer: per stage of SC K-chunks one TMA load of the
+//               packed words per matrix (SC*32 or SC*64 bytes per row, so a
+//               stage moves whole 128-byte row segments) and the x tiles of
+//               those chunks, 16 token rows per load and only as many rows
+//               as the slot has, into a PS-deep ring.
 //   warp 1      MMA issuer (one thread): tcgen05.mma kind::f16, bf16 x bf16
 //               -> fp32 TMEM accumulators; tcgen05.commit frees stages.
 //   warps 2-9   converters: thread (row, K half) dequantizes 32 values of its
@@ -54,26 +57,27 @@ struct Tc2Params {
 // (0,4,1,5,2,6,3,7): the order the nibble unpack emits pairs in.
 __device__ __forceinline__ int64_t kperm_col(int64_t k) { return (k & ~int64_t(7)) | ((k & 3) << 1) | ((k >> 2) & 1); }
 
-template <int BITS, int MAT, int TILE_N>
+template <int BITS, int MAT, int TILE_N, int SC>
 __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Params p,
                                                                   const __grid_constant__ CUtensorMap tmx,
                                                                   const __grid_constant__ CUtensorMap tm0,
                                                                   const __grid_constant__ CUtensorMap tm1) {
   constexpr int PKB = TC_KC * BITS / 8;  // packed bytes per row per chunk
-  constexpr int PK_TILE = TC_M * PKB;
+  constexpr int PITCH = SC * PKB;        // packed bytes per row per stage
+  constexpr int PK_TILE = TC_M * PITCH;  // per matrix per stage
   constexpr int A_TILE = TC_M * TC_KC * 2;
-  constexpr int B_TILE = TILE_N * TC_KC * 2;
-  constexpr int STAGE = B_TILE + MAT * PK_TILE;
+  constexpr int B_TILE = TILE_N * TC_KC * 2;  // per chunk
+  constexpr int STAGE = SC * B_TILE + MAT * PK_TILE;
   constexpr uint32_t TMEM_COLS = (MAT * TILE_N <= 32) ? 32 : (MAT * TILE_N <= 64) ? 64 : (MAT * TILE_N <= 128) ? 128
                                  : (MAT * TILE_N <= 256) ? 256 : 512;
-  constexpr int PK_SW_MASK = PKB / 16 - 1;
+  constexpr int PK_SW_MASK = PITCH / 16 - 1;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int PS = p.PS, AS = p.AS;
 
-  uint8_t* stages = smem;                              // [PS][B tile | MAT pk tiles]
+  uint8_t* stages = smem;                              // [PS][SC B tiles | MAT pk tiles]
   uint8_t* atiles = stages + PS * STAGE;               // [AS][MAT][A_TILE]
   uint64_t* bars = reinterpret_cast<uint64_t*>(atiles + AS * MAT * A_TILE);
   uint64_t* full = bars;
@@ -119,23 +123,27 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
   if (warp == 0) {
     // =============================== producer ===================================
     // Control flow stays warp-uniform: lane 0 waits, the verdict is broadcast.
-    int g = 0;
+    int gsx = 0;  // stage sequence number
     bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
     for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
       const int4 sl = p.slots[u / p.n_rb];
       const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
       const int row0 = int(int64_t(sl.x) * p.N + m0);
-      for (int c = 0; c < n_chunks; ++c) {
+      const int n16 = (sl.z + 15) >> 4;  // 16-row x boxes per chunk
+      for (int c0 = 0; c0 < n_chunks; c0 += SC) {
         int ok = 1;
         if (lane == 0) {
-          const int s = g % PS;
-          ok = !*abort_flag && (g < PS || mbar_wait_bounded(&empty[s], uint32_t(((g / PS) - 1) & 1)));
+          const int s = gsx % PS;
+          ok = !*abort_flag && (gsx < PS || mbar_wait_bounded(&empty[s], uint32_t(((gsx / PS) - 1) & 1)));
           if (ok) {
+            const int nsub = min(SC, n_chunks - c0);
             uint8_t* st = stages + s * STAGE;
-            mbar_arrive_expect_tx(&full[s], uint32_t(STAGE));
-            tma_load_2d(st, &tmx, c * TC_KC, sl.y, &full[s]);
-            tma_load_2d(st + B_TILE, &tm0, c * (PKB / 4), row0, &full[s]);
-            if constexpr (MAT == 2) tma_load_2d(st + B_TILE + PK_TILE, &tm1, c * (PKB / 4), row0, &full[s]);
+            mbar_arrive_expect_tx(&full[s], uint32_t(MAT * PK_TILE + nsub * n16 * 16 * TC_KC * 2));
+            tma_load_2d(st + SC * B_TILE, &tm0, (c0 / SC) * (PITCH / 4), row0, &full[s]);
+            if constexpr (MAT == 2) tma_load_2d(st + SC * B_TILE + PK_TILE, &tm1, (c0 / SC) * (PITCH / 4), row0, &full[s]);
+            for (int cc = 0; cc < nsub; ++cc)
+              for (int r = 0; r < n16; ++r)
+                tma_load_2d(st + cc * B_TILE + r * 16 * TC_KC * 2, &tmx, (c0 + cc) * TC_KC, sl.y + 16 * r, &full[s]);
           }
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -143,14 +151,14 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
           stop = true;
           break;
         }
-        ++g;
+        ++gsx;
       }
     }
     if (stop && lane == 0) *abort_flag = 1;
     if (lane == 0 && stop) {
       // let the TMA loads already issued land before the CTA goes away
-      for (int k = 1; k <= PS && g - k >= 0; ++k) {
-        const int gi = g - k;
+      for (int k = 1; k <= PS && gsx - k >= 0; ++k) {
+        const int gi = gsx - k;
         mbar_wait_bounded(&full[gi % PS], uint32_t((gi / PS) & 1), 100000000ull);
       }
     }
@@ -158,21 +166,21 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
   } else if (warp == 1) {
     // =============================== MMA issuer =================================
     if (lane == 0) {
-      int g = 0;
+      int g = 0, gsx = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int4 sl = p.slots[u / p.n_rb];
         const int n_pad = (sl.z + 15) & ~15;
         const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n_pad >> 3) << 17) |
                                (uint32_t(TC_M >> 4) << 24);
         for (int c = 0; c < n_chunks; ++c, ++g) {
-          const int s = g % PS, sa = g % AS;
-          if (!mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) ||
+          const int s = gsx % PS, sa = g % AS, cc = c % SC;
+          if (!mbar_wait_bounded(&full[s], uint32_t((gsx / PS) & 1)) ||
               !mbar_wait_bounded(&a_full[sa], uint32_t((g / AS) & 1))) {
             *abort_flag = 1;
             break;
           }
           tc_fence_after();
-          const uint64_t bdesc = sw128_desc(stages + s * STAGE);
+          const uint64_t bdesc = sw128_desc(stages + s * STAGE + cc * B_TILE);
 #pragma unroll
           for (int m = 0; m < MAT; ++m) {
             const uint64_t adesc = sw128_desc(atiles + (sa * MAT + m) * A_TILE);
@@ -181,8 +189,11 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
               tc_mma(tmem + uint32_t(m * TILE_N), adesc + 2 * ks, bdesc + 2 * ks, idesc,
                      (c > 0 || ks > 0) ? 1u : 0u);
           }
-          tc_commit(&empty[s]);
           tc_commit(&a_empty[sa]);
+          if (cc == SC - 1 || c == n_chunks - 1) {
+            tc_commit(&empty[s]);
+            ++gsx;
+          }
           if (c == n_chunks - 1) tc_commit(acc_full);
         }
       }
@@ -196,7 +207,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     const int tc = tid - 64;          // 0..255
     const int t = tc & (TC_M - 1);    // row within the block
     const int h = tc >> 7;            // K half of the chunk
-    const int sw = (t * PKB >> 7) & PK_SW_MASK;  // TMA swizzle of this packed row
+    const int sw = (t * PITCH >> 7) & PK_SW_MASK;  // TMA swizzle of this packed row
     // Every lane waits on the barriers; the verdict is made warp-uniform
     // (__all_sync) so the .sync.aligned TMEM loads and __syncwarp never diverge.
     // scale/bias register blocks: [m][s|b][4 words = 8 groups]; `nxt` is
@@ -233,13 +244,13 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     };
     load_block(cur);
     load_block(nxt);
-    int g = 0, it = 0;
+    int g = 0, it = 0, gsx = 0;
     bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
     for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x, ++it) {
       const int4 sl = p.slots[u / p.n_rb];
       const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
       for (int c = 0; c < n_chunks; ++c, ++g) {
-        const int s = g % PS, sa = g % AS;
+        const int s = gsx % PS, sa = g % AS, cc = c % SC;
         if (c % TC2_SB_CHUNKS == 0 && g > 0) {
 #pragma unroll
           for (int m = 0; m < MAT; ++m)
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
               for (int i = 0; i < 4; ++i) cur[m][kind][i] = nxt[m][kind][i];
           load_block(nxt);
         }
-        const bool ok = !(*abort_flag) && mbar_wait_bounded(&full[s], uint32_t((g / PS) & 1)) &&
+        const bool ok = !(*abort_flag) && mbar_wait_bounded(&full[s], uint32_t((gsx / PS) & 1)) &&
                         (g < AS || mbar_wait_bounded(&a_empty[sa], uint32_t(((g / AS) - 1) & 1)));
         if (!__all_sync(0xffffffffu, ok)) {
           stop = true;
@@ -263,11 +274,11 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
           // broadcast the chunk's bf16 (low half = even group) to both halves
           const uint32_t s2v = prmt(sw4, 0u, chi ? 0x3232u : 0x1010u);
           const uint32_t b2v = prmt(bw4, 0u, chi ? 0x3232u : 0x1010u);
-          const uint8_t* prow = stages + s * STAGE + B_TILE + m * PK_TILE + t * PKB;
+          const uint8_t* prow = stages + s * STAGE + SC * B_TILE + m * PK_TILE + t * PITCH;
           uint8_t* arow = atiles + (sa * MAT + m) * A_TILE;
           if constexpr (BITS == 4) {
             // this thread's 16 B = 4 words = K values 32h .. 32h+31
-            const uint4 q = *reinterpret_cast<const uint4*>(prow + ((h ^ sw) << 4));
+            const uint4 q = *reinterpret_cast<const uint4*>(prow + (((2 * cc + h) ^ sw) << 4));
             const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -285,7 +296,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               const int piece = 2 * h + hh;
-              const uint4 q = *reinterpret_cast<const uint4*>(prow + ((piece ^ sw) << 4));
+              const uint4 q = *reinterpret_cast<const uint4*>(prow + (((4 * cc + piece) ^ sw) << 4));
               const uint32_t wds[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
               for (int ii = 0; ii < 2; ++ii) {
@@ -304,6 +315,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
         fence_proxy_async_smem();  // generic stores -> tensor-core reads
         __syncwarp();
         if (lane == 0) mbar_arrive(&a_full[sa]);
+        if (cc == SC - 1 || c == n_chunks - 1) ++gsx;
       }
       if (stop) break;
       // ---- epilogue: TMEM -> registers -> bf16 ---------------------------------
@@ -384,24 +396,70 @@ static int make_rows_map(CUtensorMap* map, const void* x, int64_t rows, int64_t 
 
 static int g_sms_tc2 = 0;
 
-template <int BITS, int MAT, int TILE_N>
-static int launch_tc2_cfg(Tc2Params p, const CUtensorMap& mx, const CUtensorMap& m0, const CUtensorMap& m1,
-                          cudaStream_t st) {
-  constexpr int PK_TILE = TC_M * TC_KC * BITS / 8;
+// Packed weights as a 2-D uint32 tensor [rows, K*bits/32 words]; box = 128
+// rows x `pitch` bytes (SC chunks), swizzle matching the pitch.
+static int make_weight_map_pitch(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int bits,
+                                 int pitch) {
+  const cuuint64_t words = cuuint64_t(K * bits / 32);
+  const cuuint64_t dims[2] = {words, cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {words * 4};
+  const cuuint32_t box[2] = {cuuint32_t(pitch / 4), cuuint32_t(TC_M)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = pitch == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : pitch == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
+}
+
+struct Tc2Maps {
+  const void* x;
+  int64_t x_rows, ldx;
+  const uint32_t* w0;
+  const uint32_t* w1;
+  int64_t w_rows;
+};
+
+// Stages and A-ring depth for a configuration; false if PS < 2.
+template <int BITS, int MAT, int TILE_N, int SC>
+static bool tc2_plan(int* PS_out, int* AS_out, int* smem_out) {
+  constexpr int PITCH = SC * TC_KC * BITS / 8;
+  constexpr int PK_TILE = TC_M * PITCH;
   constexpr int A_TILE = TC_M * TC_KC * 2;
   constexpr int B_TILE = TILE_N * TC_KC * 2;
-  constexpr int STAGE = B_TILE + MAT * PK_TILE;
+  constexpr int STAGE = SC * B_TILE + MAT * PK_TILE;
   const int budget = 220 * 1024;
   int AS = 3;
   if (MAT * A_TILE * AS + 3 * STAGE > budget) AS = 2;
   int PS = (budget - AS * MAT * A_TILE - 1024 - 256) / STAGE;
-  if (PS > 10) PS = 10;
-  if (PS < 2) return B2F_ERR_UNSUPPORTED;
+  if (PS > 8) PS = 8;
+  *PS_out = PS;
+  *AS_out = AS;
+  *smem_out = 1024 + PS * STAGE + AS * MAT * A_TILE + 8 * (2 * PS + 2 * AS + 2) + 16;
+  return PS >= 2 && *smem_out <= 227 * 1024;
+}
+
+template <int BITS, int MAT, int TILE_N, int SC>
+static int launch_tc2_cfg(Tc2Params p, const Tc2Maps& maps, cudaStream_t st) {
+  int PS, AS, smem;
+  if (!tc2_plan<BITS, MAT, TILE_N, SC>(&PS, &AS, &smem)) return B2F_ERR_UNSUPPORTED;
   p.PS = PS;
   p.AS = AS;
-  const int smem = 1024 + PS * STAGE + AS * MAT * A_TILE + 8 * (2 * PS + 2 * AS + 2) + 16;
-  if (smem > 227 * 1024) return B2F_ERR_UNSUPPORTED;
-  auto kern = qgemm_tc2_kernel<BITS, MAT, TILE_N>;
+  CUtensorMap mx, m0, m1;
+  int rc = make_rows_map(&mx, maps.x, maps.x_rows, p.K, maps.ldx, 16);
+  if (rc != B2F_OK) return rc;
+  constexpr int PITCH = SC * TC_KC * BITS / 8;
+  rc = make_weight_map_pitch(&m0, maps.w0, maps.w_rows, p.K, BITS, PITCH);
+  if (rc != B2F_OK) return rc;
+  if (maps.w1) {
+    rc = make_weight_map_pitch(&m1, maps.w1, maps.w_rows, p.K, BITS, PITCH);
+    if (rc != B2F_OK) return rc;
+  } else {
+    m1 = m0;
+  }
+  auto kern = qgemm_tc2_kernel<BITS, MAT, TILE_N, SC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -420,17 +478,31 @@ static int launch_tc2_cfg(Tc2Params p, const CUtensorMap& mx, const CUtensorMap&
   return check_launch();
 }
 
-template <int BITS, int MAT>
-static int launch_tc2_bits(const Tc2Params& p, const CUtensorMap& mx, const CUtensorMap& m0, const CUtensorMap& m1,
-                           int tile, cudaStream_t st) {
-  if (tile <= 16) return launch_tc2_cfg<BITS, MAT, 16>(p, mx, m0, m1, st);
-  if (tile <= 32) return launch_tc2_cfg<BITS, MAT, 32>(p, mx, m0, m1, st);
-  if (tile <= 64) return launch_tc2_cfg<BITS, MAT, 64>(p, mx, m0, m1, st);
-  if (tile <= 128) return launch_tc2_cfg<BITS, MAT, 128>(p, mx, m0, m1, st);
-  return launch_tc2_cfg<BITS, MAT, 256>(p, mx, m0, m1, st);
+// Widest stage (most chunks per weight load) that still leaves >= 3 stages,
+// else the widest with >= 2.
+template <int BITS, int MAT, int TILE_N>
+static int launch_tc2_tile(const Tc2Params& p, const Tc2Maps& maps, cudaStream_t st) {
+  int PS, AS, smem;
+  if constexpr (BITS == 4) {
+    if (tc2_plan<4, MAT, TILE_N, 4>(&PS, &AS, &smem) && PS >= 3) return launch_tc2_cfg<4, MAT, TILE_N, 4>(p, maps, st);
+  }
+  if (tc2_plan<BITS, MAT, TILE_N, 2>(&PS, &AS, &smem) && PS >= 3) return launch_tc2_cfg<BITS, MAT, TILE_N, 2>(p, maps, st);
+  if (tc2_plan<BITS, MAT, TILE_N, 1>(&PS, &AS, &smem) && PS >= 3) return launch_tc2_cfg<BITS, MAT, TILE_N, 1>(p, maps, st);
+  if constexpr (BITS == 4) {
+    if (tc2_plan<4, MAT, TILE_N, 4>(&PS, &AS, &smem)) return launch_tc2_cfg<4, MAT, TILE_N, 4>(p, maps, st);
+  }
+  if (tc2_plan<BITS, MAT, TILE_N, 2>(&PS, &AS, &smem)) return launch_tc2_cfg<BITS, MAT, TILE_N, 2>(p, maps, st);
+  return launch_tc2_cfg<BITS, MAT, TILE_N, 1>(p, maps, st);
 }
 
-static int tile_rows(int tile) { return tile <= 16 ? 16 : tile <= 32 ? 32 : tile <= 64 ? 64 : tile <= 128 ? 128 : 256; }
+template <int BITS, int MAT>
+static int launch_tc2_bits(const Tc2Params& p, const Tc2Maps& maps, int tile, cudaStream_t st) {
+  if (tile <= 16) return launch_tc2_tile<BITS, MAT, 16>(p, maps, st);
+  if (tile <= 32) return launch_tc2_tile<BITS, MAT, 32>(p, maps, st);
+  if (tile <= 64) return launch_tc2_tile<BITS, MAT, 64>(p, maps, st);
+  if (tile <= 128) return launch_tc2_tile<BITS, MAT, 128>(p, maps, st);
+  return launch_tc2_tile<BITS, MAT, 256>(p, maps, st);
+}
 
 }  // namespace b2f
 
@@ -503,21 +575,10 @@ int b2f_sorted_qgemm_affine_tcgen05(const void* x_sorted, int64_t ldx, int64_t A
   p.max_slots = int(max_slots);
   int rc = get_encoder();
   if (rc != B2F_OK) return rc;
-  CUtensorMap mx, m0, m1;
-  rc = make_rows_map(&mx, x_sorted, A, K, ldx, tile_rows(tile));
-  if (rc != B2F_OK) return rc;
-  rc = make_weight_map(&m0, w_gate, E * N, K, bits);
-  if (rc != B2F_OK) return rc;
-  if (w_up) {
-    rc = make_weight_map(&m1, w_up, E * N, K, bits);
-    if (rc != B2F_OK) return rc;
-  } else {
-    m1 = m0;
-  }
+  Tc2Maps maps{x_sorted, A, ldx, w_gate, w_up, E * N};
   cudaStream_t st = as_stream(stream);
-  if (bits == 4)
-    return w_up ? launch_tc2_bits<4, 2>(p, mx, m0, m1, tile, st) : launch_tc2_bits<4, 1>(p, mx, m0, m1, tile, st);
-  return w_up ? launch_tc2_bits<8, 2>(p, mx, m0, m1, tile, st) : launch_tc2_bits<8, 1>(p, mx, m0, m1, tile, st);
+  if (bits == 4) return w_up ? launch_tc2_bits<4, 2>(p, maps, tile, st) : launch_tc2_bits<4, 1>(p, maps, tile, st);
+  return w_up ? launch_tc2_bits<8, 2>(p, maps, tile, st) : launch_tc2_bits<8, 1>(p, maps, tile, st);
 }
 
 }  // extern "C"
