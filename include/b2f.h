@@ -222,6 +222,20 @@ int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const flo
                                 int64_t slot_stride, int bits, int group_size,
                                 float softmax_scale, int n_splits, void* out, void* stream);
 
+/* Workspace bytes of b2f_qgemm_affine_tcgen05_splitk (fp32 partials). */
+int64_t b2f_qgemm_splitk_workspace_bytes(int64_t M, int64_t N, int ksplit);
+
+/* b2f_qgemm_affine_tcgen05 with K cut into `ksplit` ranges so that few
+ * 128-row blocks (decode-sized M, e.g. the q/k/v and o projections at 64
+ * tokens) still fill every SM: each range writes fp32 partials into
+ * `workspace`, a second kernel sums them (+ residual) into bf16 y.
+ * ksplit 1..64; ksplit == 1 is b2f_qgemm_affine_tcgen05. */
+int b2f_qgemm_affine_tcgen05_splitk(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                                    const void* scales, const void* biases, int64_t N, int64_t K,
+                                    int bits, int group_size, const void* residual, void* y,
+                                    int64_t ldy, int tile, int ksplit, void* workspace,
+                                    int64_t workspace_bytes, void* stream);
+
 /* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
 
 /* Copies the planned assignments' activation rows into plan order:

@@ -98,7 +98,8 @@ class Qwen3MoeDecoder:
     """Random-weight Qwen3-MoE-shaped decoder with a paged 8-bit KV cache."""
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
-                 device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None):
+                 device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
+                 dense_engine: str = "auto"):
         self.s = s = shape
         self.dev = dev = torch.device(device)
         self.B = max_batch
@@ -204,6 +205,33 @@ class Qwen3MoeDecoder:
         self.attn_ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
         self.attn_ws_bytes = wsb
         self.softmax_scale = 1.0 / math.sqrt(D)
+        # dense projections: register GEMV for a few tokens, tcgen05 (split-K
+        # where the matrix has few 128-row blocks) for larger batches
+        if dense_engine == "auto":
+            dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
+        if dense_engine not in ("tc", "gemv"):
+            raise ValueError(f"unknown dense engine {dense_engine!r}")
+        self.dense_engine = dense_engine
+        self.dense_tile = min(256, max(16, (B + 15) // 16 * 16))
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+        def ksplit_for(N, K):
+            blocks = (N + 127) // 128
+            chunks = K // 64
+            ks = 1
+            while blocks * ks * 2 <= 2 * sms and ks * 2 <= chunks // 4:
+                ks *= 2
+            return ks
+
+        self.ks_qkv = ksplit_for(self.qkv_rows, H)
+        self.ks_o = ksplit_for(H, Hq * D)
+        ws = 0
+        if dense_engine == "tc":
+            lib = _capi.lib()
+            ws = max(int(lib.b2f_qgemm_splitk_workspace_bytes(B, self.qkv_rows, self.ks_qkv)) if self.ks_qkv > 1 else 0,
+                     int(lib.b2f_qgemm_splitk_workspace_bytes(B, H, self.ks_o)) if self.ks_o > 1 else 0)
+        self.dense_ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        self.dense_ws_bytes = ws
 
     # ------------------------------------------------------------------
     def weight_bytes(self) -> int:
@@ -244,8 +272,7 @@ class Qwen3MoeDecoder:
              0, ptr(self.xn), st)
         for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
             w = ly["wqkv"]
-            call("b2f_qgemv_affine", ptr(self.xn), H, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K, w.bits,
-                 w.group_size, 0, ptr(self.qkv), w.N, st)
+            self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
             call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]), ptr(ly["k_norm"]),
                  s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]), ptr(kv["ks"]),
                  ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page, s.kv_bits, st)
@@ -254,8 +281,7 @@ class Qwen3MoeDecoder:
                  s.kv_bits, 64, self.softmax_scale, self.n_splits, ptr(self.attn_ws), self.attn_ws_bytes,
                  ptr(self.attn), st)
             w = ly["wo"]
-            call("b2f_qgemv_affine", ptr(self.attn), Hq * D, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K,
-                 w.bits, w.group_size, ptr(self.h), ptr(self.h), H, st)
+            self._dense(self.attn, Hq * D, w, self.h, self.h, self.ks_o, st)
             call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
                  ptr(self.xn), st)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm
@@ -290,19 +316,30 @@ class Qwen3MoeDecoder:
                      ptr(self.y), H, st)
             call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.y), ptr(self.scores), B, s.top_k, ptr(nxt),
                  s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
-        w = self.lm_head
-        call("b2f_qgemv_affine", ptr(self.xn), H, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K, w.bits,
-             w.group_size, 0, ptr(self.logits), w.N, st)
+        self._dense(self.xn, H, self.lm_head, 0, self.logits, 1, st)
         call("b2f_argmax_rows", ptr(self.logits), B, s.vocab, ptr(self.next_tokens), st)
         # feed back: next input token and position
         self.tokens.copy_(self.next_tokens)
         self.positions.add_(1)
+
+    def _dense(self, x, ldx, w, residual, out, ksplit, st):
+        """out = x . W^T (+ residual): register GEMV or tcgen05 (split-K)."""
+        B = self.B
+        if self.dense_engine == "gemv":
+            call("b2f_qgemv_affine", ptr(x), ldx, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K, w.bits,
+                 w.group_size, ptr(residual) if isinstance(residual, torch.Tensor) else 0, ptr(out), w.N, st)
+        else:
+            call("b2f_qgemm_affine_tcgen05_splitk", ptr(x), ldx, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K,
+                 w.bits, w.group_size, ptr(residual) if isinstance(residual, torch.Tensor) else 0, ptr(out), w.N,
+                 self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
 
     def launches_per_step(self) -> int:
         """libb200flash kernel launches in one step (attention counts its combine pass)."""
         attn = 2 if self.n_splits > 1 else 1
         # qkv, rope+append, attention, o_proj, norm, router, plan, gate/up, down, combine
         per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 2 + 1
+        if self.dense_engine == "tc":
+            per_layer += int(self.ks_qkv > 1) + int(self.ks_o > 1)  # split-K sums
         if self.moe_engine == "tc":
             per_layer += 1  # the row gather into expert-sorted order
         if self.ep is not None:

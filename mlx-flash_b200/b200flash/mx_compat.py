@@ -131,8 +131,11 @@ def tc_supported(K, group_size, bits):
 
 def quantized_matmul_tc(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                         group_size: int = 64, bits: int = 4, residual: torch.Tensor = None,
-                        tile: int = 128) -> torch.Tensor:
-    """``x @ dequantize(w).T`` on the tcgen05 tensor cores (prefill-sized M)."""
+                        tile: int = 128, ksplit: int = 1) -> torch.Tensor:
+    """``x @ dequantize(w).T`` on the tcgen05 tensor cores (prefill-sized M).
+
+    ``ksplit > 1`` cuts K into ranges whose fp32 partials are summed by a
+    second kernel (decode-sized M with few 128-row blocks)."""
     dev = require_cuda(x, w, scales, biases, residual)
     if x.dtype != torch.bfloat16 or scales.dtype != torch.bfloat16:
         raise ValueError("bf16 activations and bf16 scales/biases required")
@@ -145,6 +148,13 @@ def quantized_matmul_tc(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, 
     xc = _capi.aligned_contiguous(x.reshape(M, K))
     out = torch.empty(*lead, N, dtype=torch.bfloat16, device=dev)
     res = None if residual is None else residual.reshape(M, N).contiguous()
+    if ksplit > 1:
+        nb = int(_capi.lib().b2f_qgemm_splitk_workspace_bytes(M, N, int(ksplit)))
+        ws = torch.empty(max(nb, 16), dtype=torch.uint8, device=dev)
+        call("b2f_qgemm_affine_tcgen05_splitk", ptr(xc), K, M, ptr(w.contiguous()), ptr(scales.contiguous()),
+             ptr(biases.contiguous()), N, K, bits, group_size, ptr(res), ptr(out), N, int(tile), int(ksplit),
+             ptr(ws), nb, stream_of(dev))
+        return out
     call("b2f_qgemm_affine_tcgen05", ptr(xc), K, M, ptr(w.contiguous()), ptr(scales.contiguous()),
          ptr(biases.contiguous()), N, K, bits, group_size, ptr(res), ptr(out), N, int(tile), stream_of(dev))
     return out

@@ -51,6 +51,8 @@ struct TcParams {
   int tile;  // tokens per slot (<= TILE_N)
   int32_t* err;
   int pk_stages, ab_stages;
+  int ksplit;      // dense mode: K is cut into ksplit ranges (grid z)
+  float* partial;  // ksplit > 1: fp32 partials [ksplit][M][N]
 };
 
 template <int BITS, int MAT, int TILE_N>
@@ -84,7 +86,12 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
   }
   const int n_pad = (n_tok + 15) & ~15;
   const int64_t m0 = int64_t(blockIdx.x) * TC_M;
-  const int n_chunks = int(p.K / TC_KC);
+  // this CTA's K range (split-K in dense mode): chunks [c_base, c_base + n_chunks)
+  const int all_chunks = int(p.K / TC_KC);
+  const int cps = (all_chunks + p.ksplit - 1) / p.ksplit;
+  const int c_base = int(blockIdx.z) * cps;
+  const int n_chunks = min(cps, all_chunks - c_base);
+  if (n_chunks <= 0) return;
 
   // ---- shared memory carve-up (all tiles 1024-B aligned) ---------------------
   uint8_t* pk = smem;                                  // [PS][MAT][PK_TILE]
@@ -152,8 +159,9 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
         }
         if (*abort_flag) break;
         mbar_arrive_expect_tx(&pk_full[s], uint32_t(MAT * PK_TILE));
-        tma_load_2d(pk + (s * MAT + 0) * PK_TILE, &tm0, c * (PKB / 4), row0, &pk_full[s]);
-        if constexpr (MAT == 2) tma_load_2d(pk + (s * MAT + 1) * PK_TILE, &tm1, c * (PKB / 4), row0, &pk_full[s]);
+        tma_load_2d(pk + (s * MAT + 0) * PK_TILE, &tm0, (c_base + c) * (PKB / 4), row0, &pk_full[s]);
+        if constexpr (MAT == 2)
+          tma_load_2d(pk + (s * MAT + 1) * PK_TILE, &tm1, (c_base + c) * (PKB / 4), row0, &pk_full[s]);
       }
     }
   } else if (warp == 5) {
@@ -202,7 +210,8 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
           const int idx = base + lane + 32 * i;
           const int n = idx >> 3, j = idx & 7;
           v[i] = make_uint4(0u, 0u, 0u, 0u);
-          if (n < n_tok) v[i] = *reinterpret_cast<const uint4*>(p.x + xrow[n] * p.ldx + int64_t(c) * TC_KC + 8 * j);
+          if (n < n_tok)
+            v[i] = *reinterpret_cast<const uint4*>(p.x + xrow[n] * p.ldx + int64_t(c_base + c) * TC_KC + 8 * j);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
     const int t = tid - 32;  // weight row within the tile (0..127)
     const int64_t grow = m0 + t;
     const bool row_ok = grow < p.N;
-    const int64_t sb_row = int64_t(expert) * p.sb_estride + grow * (p.K / 64);
+    const int64_t sb_row = int64_t(expert) * p.sb_estride + grow * (p.K / 64) + c_base;
     // scales/biases fetched two chunks ahead (raw bf16 bits)
     uint16_t sq[3][MAT], bq[3][MAT];
     const uint16_t* sp[MAT];
@@ -332,8 +341,12 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
               float v = __uint_as_float(g[i]);
               if constexpr (MAT == 2) v = silu_mul_tc(v, __uint_as_float(u[i]));
               const int64_t o = orow[n];
-              if (p.residual) v += __bfloat162float(p.residual[o * p.ldo + gr]);
-              p.out[o * p.ldo + gr] = __float2bfloat16_rn(v);
+              if (p.partial) {
+                p.partial[(int64_t(blockIdx.z) * p.M + o) * p.N + gr] = v;
+              } else {
+                if (p.residual) v += __bfloat162float(p.residual[o * p.ldo + gr]);
+                p.out[o * p.ldo + gr] = __float2bfloat16_rn(v);
+              }
             }
           }
         }
@@ -348,6 +361,20 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
   if (tid == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+}
+
+// split-K: out[m, n] = bf16(sum_k partial[k, m, n] + residual[m, n])
+__global__ void __launch_bounds__(256) splitk_finalize_kernel(const float* __restrict__ partial, int ksplit, int64_t M,
+                                                              int64_t N, const __nv_bfloat16* __restrict__ residual,
+                                                              __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int64_t total = M * N;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float v = 0.f;
+    for (int k = 0; k < ksplit; ++k) v += partial[int64_t(k) * total + i];
+    if (residual) v += __bfloat162float(residual[m * ldo + n]);
+    out[m * ldo + n] = __float2bfloat16_rn(v);
+  }
 }
 
 // ---- host side -------------------------------------------------------------------
@@ -406,7 +433,7 @@ static int launch_tc_cfg(TcParams p, const CUtensorMap& m0, const CUtensorMap& m
     set_last_cuda_error(e);
     return B2F_ERR_CUDA;
   }
-  const dim3 grid{unsigned((p.N + TC_M - 1) / TC_M), unsigned(slots_grid), 1u};
+  const dim3 grid{unsigned((p.N + TC_M - 1) / TC_M), unsigned(slots_grid), unsigned(p.ksplit)};
   kern<<<grid, 256, smem, st>>>(p, m0, m1);
   return check_launch();
 }
@@ -476,9 +503,62 @@ int b2f_qgemm_affine_tcgen05(const void* x, int64_t ldx, int64_t M, const uint32
   p.out = static_cast<__nv_bfloat16*>(y);
   p.ldo = ldy;
   p.tile = tile;
+  p.ksplit = 1;
   const int64_t slots = (M + tile - 1) / tile;
   if (slots > 65535) return B2F_ERR_UNSUPPORTED;
   return launch_tc(p, wq, nullptr, 1, bits, tile, slots, as_stream(stream));
+}
+
+int64_t b2f_qgemm_splitk_workspace_bytes(int64_t M, int64_t N, int ksplit) {
+  if (M <= 0 || N <= 0 || ksplit <= 0) return 0;
+  return int64_t(ksplit) * M * N * int64_t(sizeof(float));
+}
+
+int b2f_qgemm_affine_tcgen05_splitk(const void* x, int64_t ldx, int64_t M, const uint32_t* wq, const void* scales,
+                                    const void* biases, int64_t N, int64_t K, int bits, int group_size,
+                                    const void* residual, void* y, int64_t ldy, int tile, int ksplit,
+                                    void* workspace, int64_t workspace_bytes, void* stream) {
+  if (ksplit == 1)
+    return b2f_qgemm_affine_tcgen05(x, ldx, M, wq, scales, biases, N, K, bits, group_size, residual, y, ldy, tile,
+                                    stream);
+  int rc = check_tc_shape(N, K, bits, group_size);
+  if (rc != B2F_OK) return rc;
+  if (M < 0 || tile < 16 || tile > 256 || tile % 16 || ksplit < 1 || ksplit > 64) return B2F_ERR_INVALID;
+  if (M == 0) return B2F_OK;
+  if (!x || !wq || !scales || !biases || !y) return B2F_ERR_INVALID;
+  if (ldx < K || ldy < N) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || (ldx % 8) != 0 || !aligned(wq, 16)) return B2F_ERR_ALIGN;
+  if (!workspace || workspace_bytes < b2f_qgemm_splitk_workspace_bytes(M, N, ksplit)) return B2F_ERR_WORKSPACE;
+  if (!aligned(workspace, 16)) return B2F_ERR_ALIGN;
+  // every K range non-empty: ksplit ranges of ceil(chunks / ksplit) chunks
+  const int chunks = int(K / 64);
+  const int cps = (chunks + ksplit - 1) / ksplit;
+  ksplit = (chunks + cps - 1) / cps;
+  TcParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.M = M;
+  p.s[0] = static_cast<const __nv_bfloat16*>(scales);
+  p.b[0] = static_cast<const __nv_bfloat16*>(biases);
+  p.N = N;
+  p.K = K;
+  p.out = static_cast<__nv_bfloat16*>(y);
+  p.ldo = ldy;
+  p.tile = tile;
+  p.ksplit = ksplit;
+  p.partial = static_cast<float*>(workspace);
+  const int64_t slots = (M + tile - 1) / tile;
+  if (slots > 65535) return B2F_ERR_UNSUPPORTED;
+  cudaStream_t st = as_stream(stream);
+  rc = launch_tc(p, wq, nullptr, 1, bits, tile, slots, st);
+  if (rc != B2F_OK) return rc;
+  const int64_t total = M * N;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t blocks = (total + 255) / 256;
+  splitk_finalize_kernel<<<unsigned(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8), 256, 0, st>>>(
+      p.partial, ksplit, M, N, static_cast<const __nv_bfloat16*>(residual), p.out, ldy);
+  return check_launch();
 }
 
 int b2f_gather_qgemm_affine_tcgen05(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div,
@@ -505,6 +585,7 @@ int b2f_gather_qgemm_affine_tcgen05(const void* x, int64_t ldx, const int32_t* x
   p.ldx = ldx;
   p.x_row_index = x_row_index;
   p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  p.ksplit = 1;
   p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
   p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
   p.s[1] = static_cast<const __nv_bfloat16*>(s_up);

@@ -46,6 +46,20 @@ def test_tc_dense_residual(dev):
     assert_close(to_np(y), affine.quantized_matmul(x, wq, s, b, True, 64, 4, out_dtype="f32") + r, what="residual")
 
 
+@pytest.mark.parametrize("M,N,K,bits,tile,ksplit", [(64, 5120, 2048, 4, 64, 4), (64, 2048, 4096, 4, 64, 8),
+                                                    (37, 300, 768, 8, 64, 3), (16, 256, 512, 4, 16, 5)])
+def test_tc_dense_splitk(dev, M, N, K, bits, tile, ksplit):
+    """Split-K: fp32 partials per K range, summed with the residual by a second kernel."""
+    rng = np.random.default_rng(M + N + ksplit)
+    wq, s, b = _w(rng, (N, K), bits)
+    x = round_to(rng.standard_normal((M, K)).astype(np.float32), "bf16")
+    r = round_to(rng.standard_normal((M, N)).astype(np.float32), "bf16")
+    y = mx_compat.quantized_matmul_tc(to_dev(x, "bf16", dev), *_dev3((wq, s, b), dev), 64, bits,
+                                      residual=to_dev(r, "bf16", dev), tile=tile, ksplit=ksplit)
+    want = affine.quantized_matmul(x, wq, s, b, True, 64, bits, out_dtype="f32") + r
+    assert_close(to_np(y), want, what=f"split-K M={M} N={N} K={K} ks={ksplit}")
+
+
 @pytest.mark.parametrize("T,k,E,tile", [(64, 8, 32, 64), (512, 8, 128, 128), (7, 2, 4, 16)])
 def test_tc_grouped_swiglu_and_down(dev, T, k, E, tile):
     """Qwen3-MoE expert shapes (H 2048, I 768): SwitchGLU front half then down."""
