@@ -236,6 +236,16 @@ int b2f_qgemm_affine_tcgen05_splitk(const void* x, int64_t ldx, int64_t M, const
                                     int64_t ldy, int tile, int ksplit, void* workspace,
                                     int64_t workspace_bytes, void* stream);
 
+/* b2f_moe_route_topk followed by b2f_moe_plan on its ids, in two launches
+ * (router logits; then top-k per token with the counting sort run by the
+ * last thread block to finish): expert_streaming.py:439-472 routing plus the
+ * sort-by-expert of gather_qmm(sorted_indices=True).  Same outputs as the
+ * two calls; plan workspace as for b2f_moe_plan(A = T*k, E, tile).  H <= 8192. */
+int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
+                       int64_t E, int64_t k, int renorm, float* logits_ws, int32_t* inds,
+                       float* scores, int tile, void* plan_workspace, int64_t plan_workspace_bytes,
+                       int32_t* status_out, void* stream);
+
 /* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
 
 /* Copies the planned assignments' activation rows into plan order:

@@ -293,10 +293,9 @@ class Qwen3MoeDecoder:
                 call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), 0, B, 1, ptr(nxt), s.rms_eps, H, ptr(self.h),
                      ptr(self.xn), st)
                 continue
-            call("b2f_moe_route_topk", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
-                 int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), st)
-            call("b2f_moe_plan", ptr(self.inds), A, E, self.tile, ptr(self.plan_ws), self.plan_bytes,
-                 ptr(self.plan_status), st)
+            call("b2f_moe_route_plan", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
+                 int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
+                 self.plan_bytes, ptr(self.plan_status), st)
             if self.moe_engine == "tc":
                 call("b2f_moe_gather_rows", ptr(self.xn), H, 0, s.top_k, A, E, self.tile, ptr(self.plan_ws),
                      self.plan_bytes, H, ptr(self.xs), H, st)
@@ -336,8 +335,8 @@ class Qwen3MoeDecoder:
     def launches_per_step(self) -> int:
         """libb200flash kernel launches in one step (attention counts its combine pass)."""
         attn = 2 if self.n_splits > 1 else 1
-        # qkv, rope+append, attention, o_proj, norm, router, plan, gate/up, down, combine
-        per_layer = 1 + 1 + attn + 1 + 1 + 1 + 1 + 2 + 1
+        # qkv, rope+append, attention, o_proj, norm, router (logits + top-k/plan), gate/up, down, combine
+        per_layer = 1 + 1 + attn + 1 + 1 + 2 + 2 + 1
         if self.dense_engine == "tc":
             per_layer += int(self.ks_qkv > 1) + int(self.ks_o > 1)  # split-K sums
         if self.moe_engine == "tc":

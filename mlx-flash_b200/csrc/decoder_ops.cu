@@ -4,6 +4,7 @@
 // paged cache, softmax top-k routing, and a row argmax.  All are
 // bandwidth/latency-bound; one CTA per token row.
 #include "common.cuh"
+#include "plan.cuh"
 
 namespace b2f {
 
@@ -255,12 +256,10 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* 
 // the E <= 256 logits live in registers (8 per lane).
 constexpr int TOPK_PER_LANE = 8;
 
-__global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
-                                                         int renorm, int32_t* __restrict__ inds,
-                                                         float* __restrict__ scores) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.x * 8 + warp;
-  if (t >= T) return;
+// One warp: softmax and top-k of token t's logits.
+__device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int t, int E, int k, int renorm,
+                                                 int32_t* __restrict__ inds, float* __restrict__ scores) {
+  const int lane = threadIdx.x & 31;
   float* lg = logits + int64_t(t) * E;
   float v[TOPK_PER_LANE];
   float mx = -INFINITY;
@@ -323,6 +322,35 @@ __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ log
     inds[int64_t(t) * k + lane] = my_ind;
     scores[int64_t(t) * k + lane] = renorm ? my_score / picked : my_score;
   }
+}
+
+__global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
+                                                         int renorm, int32_t* __restrict__ inds,
+                                                         float* __restrict__ scores) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < T) route_topk_token(logits, t, E, k, renorm, inds, scores);
+}
+
+// Top-k of every token, then -- in the last thread block to finish, found
+// with an arrival counter -- the counting sort of the T*k assignments by
+// expert (the MoE plan), so routing and planning take one launch.
+__global__ void __launch_bounds__(256) route_topk_plan_kernel(float* __restrict__ logits, int T, int E, int k,
+                                                              int renorm, int32_t* __restrict__ inds,
+                                                              float* __restrict__ scores, int tile, char* ws,
+                                                              PlanLayout L, int32_t* status_out) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < T) route_topk_token(logits, t, E, k, renorm, inds, scores);
+  __shared__ int is_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this block's ids visible before it is counted
+    int32_t* counter = reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2;
+    is_last = atomicAdd(counter, 1) == int(gridDim.x) - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  moe_plan_block(DenseExperts{inds}, T * k, E, tile, ws, L, status_out);
 }
 
 __global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
@@ -464,6 +492,37 @@ int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, cons
   int rc = check_launch();
   if (rc != B2F_OK) return rc;
   route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds, scores);
+  return check_launch();
+}
+
+int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, int tile,
+                       void* plan_workspace, int64_t plan_workspace_bytes, int32_t* status_out, void* stream) {
+  if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+  if (E > 32 * TOPK_PER_LANE || H % 8 != 0 || H > 8192) return B2F_ERR_UNSUPPORTED;
+  if (tile < 8 || tile > 256 || tile % 8 != 0) return B2F_ERR_INVALID;
+  if (T * k > 0x3fffffff) return B2F_ERR_UNSUPPORTED;
+  if (T == 0) return B2F_OK;
+  if (!x || !wr || !logits_ws || !inds || !scores || !plan_workspace) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(wr, 16) || !aligned(plan_workspace, 16)) return B2F_ERR_ALIGN;
+  const PlanLayout L = plan_layout(T * k, E, tile);
+  if (plan_workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
+  cudaStream_t st = as_stream(stream);
+  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
+  const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+          cudaSuccess)
+    return check_launch();
+  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+                                               static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits_ws);
+  int rc = check_launch();
+  if (rc != B2F_OK) return rc;
+  char* ws = static_cast<char*>(plan_workspace);
+  if (cudaMemsetAsync(reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2, 0, sizeof(int32_t), st) != cudaSuccess)
+    return check_launch();
+  route_topk_plan_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds,
+                                                                scores, tile, ws, L, status_out);
   return check_launch();
 }
 

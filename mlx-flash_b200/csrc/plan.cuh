@@ -7,7 +7,8 @@
 // of assignments per step, so the sort is a few microseconds.
 //
 // Workspace layout (PlanLayout):
-//   hdr     int32[16]   hdr[0] = number of slots, hdr[1] = status
+//   hdr     int32[16]   hdr[0] = number of slots, hdr[1] = status,
+//                       hdr[2] = arrival counter of the fused top-k + plan kernel
 //   counts  int32[E]    assignments per expert
 //   offsets int32[E+1]  exclusive scan of counts
 //   cursor  int32[E]    scatter cursors
@@ -122,9 +123,10 @@ struct GatheredExperts {
   }
 };
 
+// The counting sort, run by one whole thread block (any blockDim <= 1024).
 template <class Src>
-__global__ void __launch_bounds__(1024) moe_plan_kernel(const Src src, int A, int E, int tile, char* ws,
-                                                        PlanLayout L, int32_t* status_out) {
+__device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int tile, char* ws, PlanLayout L,
+                                               int32_t* status_out) {
   int32_t* hdr = reinterpret_cast<int32_t*>(ws + L.off_hdr);
   int32_t* counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
   int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.off_offsets);
@@ -187,6 +189,12 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(const Src src, int A, in
     for (int j = 0, s = soff[e]; j * tile < cnt; ++j, ++s)
       slots[s] = make_int4(e, offsets[e] + j * tile, min(tile, cnt - j * tile), 0);
   }
+}
+
+template <class Src>
+__global__ void __launch_bounds__(1024) moe_plan_kernel(const Src src, int A, int E, int tile, char* ws,
+                                                        PlanLayout L, int32_t* status_out) {
+  moe_plan_block(src, A, E, tile, ws, L, status_out);
 }
 
 }  // namespace b2f

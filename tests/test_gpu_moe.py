@@ -134,3 +134,41 @@ def test_moe_block_matches_oracle(dev):
     assert np.array_equal(to_np(inds), oi)
     y, _, _ = moe.expert_mlp(x, oi, os_, g, u, d)
     assert_close(to_np(out), y + res, what="moe block")
+
+
+@pytest.mark.parametrize("T,E,k,tile", [(64, 128, 8, 64), (5, 16, 4, 16), (300, 64, 6, 32)])
+def test_fused_route_plan_matches_separate_calls(dev, T, E, k, tile):
+    """b2f_moe_route_plan (top-k + counting sort in the last block) == route_topk then moe_plan."""
+    from b200flash import _capi
+    from b200flash.moe import route_topk
+
+    rng = np.random.default_rng(T + E)
+    H, N = 256, 64
+    x = to_dev(round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16"), "bf16", dev)
+    wr = to_dev(round_to(rng.normal(0, 0.05, (E, H)).astype(np.float32), "bf16"), "bf16", dev)
+    bias = torch.from_numpy(rng.normal(0, 0.5, E).astype(np.float32)).to(dev)
+    inds_ref, scores_ref = route_topk(x, wr, k, bias)
+    A = T * k
+    nb = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, tile))
+    ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+    gates = torch.empty(T, E, dtype=torch.float32, device=dev)
+    inds = torch.empty(T, k, dtype=torch.int32, device=dev)
+    scores = torch.empty(T, k, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(2):  # the arrival counter must reset between calls
+        _capi.call("b2f_moe_route_plan", x.data_ptr(), T, H, wr.data_ptr(), bias.data_ptr(), E, k, 1,
+                   gates.data_ptr(), inds.data_ptr(), scores.data_ptr(), tile, ws.data_ptr(), nb,
+                   status.data_ptr(), _capi.stream_of(dev))
+        torch.cuda.synchronize()
+        assert torch.equal(inds, inds_ref) and torch.equal(scores, scores_ref)
+        assert int(status.item()) == 0
+        # the plan drives the grouped GEMM exactly like one built by b2f_moe_plan
+        wq, s, b = _experts(rng, E, N, H, 4, 64)
+        wd = _dev3((wq, s, b), dev)
+        out = torch.empty(A, N, dtype=torch.bfloat16, device=dev)
+        _capi.call("b2f_gather_qgemm_affine_tcgen05", x.data_ptr(), H, 0, k, A, E, wd[0].data_ptr(), wd[1].data_ptr(),
+                   wd[2].data_ptr(), 0, 0, 0, N, H, 4, 64, tile, ws.data_ptr(), nb, out.data_ptr(), N,
+                   _capi.stream_of(dev))
+        want = affine.gather_qmm(to_np(x)[:, None, None, :], wq, s, b, rhs_indices=to_np(inds),
+                                 group_size=64, bits=4, out_dtype="f32")
+        assert_close(to_np(out).reshape(want.shape), want, what="grouped GEMM over the fused plan")
