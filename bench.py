@@ -154,7 +154,7 @@ def profile_kernels(dec, torch):
 
         def route_and_keep(name, *args):
             rc = orig_route(name, *args)
-            if name == "b2f_moe_route_topk" and dec.ep is None:
+            if name in ("b2f_moe_route_topk", "b2f_moe_route_plan") and dec.ep is None:
                 routed.append(dec.inds.clone())
             elif name == "b2f_ep_plan":
                 loc = dec.ep.local.clone()
@@ -310,7 +310,7 @@ def run_ours(args):
                 "traffic_source": "ncu DRAM bytes / algorithmic bytes on the 2-layer capture, times this launch's bytes",
                 "bytes_per_launch": int(d["bytes_per_launch"]),
                 "avg_launch_us": round(d["avg_us"], 2),
-                "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / len(distinct), 1)}
+                "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / max(1, len(distinct)), 1)}
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1e3 * t_max / args.steps, 4), "higher_is_better": True,

@@ -17,6 +17,7 @@
 //               decoded to fp16 (code-max_int)*vscale in registers.
 // Splits write (m, l, O) partials; a combine kernel merges them.
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace b2f {
 
@@ -35,7 +36,20 @@ struct AttnParams {
   float* o_part;
   float* ml_part;
   __nv_bfloat16* out;
+  int ring_bytes;  // ring path: shared-memory bytes of the page ring (the merge area follows)
+  int slot_bytes;  // ring path: bytes of one ring slot
 };
+
+constexpr int ATTN_RING = 4;  // pages in flight per CTA on the ring path
+
+// Byte offset of `byte` of K/V code row `row` inside a TMA tile of rows of
+// RB bytes written with the swizzle matching RB (128B / 64B / 32B).
+template <int RB>
+__device__ __forceinline__ int swz_off(int row, int byte) {
+  constexpr int MASK = RB / 16 - 1;
+  const int sw = ((row * RB) >> 7) & MASK;
+  return row * RB + ((((byte >> 4) ^ sw)) << 4) + (byte & 15);
+}
 
 __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
   __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
@@ -47,8 +61,10 @@ __device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
 }
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
-template <int BITS, int D>
-__global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p) {
+template <int BITS, int D, bool RING>
+__global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const AttnParams p,
+                                                                         const __grid_constant__ CUtensorMap tmk,
+                                                                         const __grid_constant__ CUtensorMap tmv) {
   constexpr int DG = D / 64;      // quantization groups per row
   constexpr int KSTEPS = D / 16;  // MMA k-steps for Q.K^T
   constexpr int NTD = D / 8;      // 8-wide output column tiles
@@ -184,12 +200,8 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
     }
   };
 
-  Tile nxt;
-  if (sub_begin + warp < sub_end) load_tile(sub_begin + warp, nxt);
-  for (int sub = sub_begin + warp; sub < sub_end; sub += 4) {
-    const int t0 = sub * 16;
-    const Tile cur = nxt;  // this sub-tile; the next one is loaded while it is computed
-    if (sub + 4 < sub_end) load_tile(sub + 4, nxt);
+  // S = Q.K^T, online softmax and O += P.V for one 16-token sub-tile
+  auto process = [&](const Tile& cur, int t0) {
     const auto& kw = cur.kw;
     const auto& ksc = cur.ksc;
     const auto& vw = cur.vw;
@@ -299,10 +311,132 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
       const uint32_t bfr[2] = {hmul2_u(hsub2_u(x01, off2), vs01[gj]), hmul2_u(hsub2_u(x23, off2), vs23[gj])};
       mma_f16_16816(oacc[j], pa, bfr);
     }
+  };
+
+  extern __shared__ __align__(1024) uint8_t attn_smem[];
+  bool aborted = false;
+  if constexpr (!RING) {
+    Tile nxt;
+    if (sub_begin + warp < sub_end) load_tile(sub_begin + warp, nxt);
+    for (int sub = sub_begin + warp; sub < sub_end; sub += 4) {
+      const Tile cur = nxt;  // this sub-tile; the next one is loaded while it is computed
+      if (sub + 4 < sub_end) load_tile(sub + 4, nxt);
+      process(cur, sub * 16);
+    }
+  } else {
+    // ---- page ring: warp 4 streams whole pages (TMA tiles of K/V codes, bulk
+    // copies of their scales) into ATTN_RING slots; warps 0-3 compute from them
+    uint64_t* full = reinterpret_cast<uint64_t*>(attn_smem + p.ring_bytes - 128);
+    uint64_t* empty = full + ATTN_RING;
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + ATTN_RING);
+    if (threadIdx.x == 0) {
+      for (int i = 0; i < ATTN_RING; ++i) {
+        mbar_init(&full[i], 1);
+        mbar_init(&empty[i], 4);
+      }
+      *abort_flag = 0;
+      fence_mbarrier_init();
+    }
+    __syncthreads();
+    const int spp = p.PS / 16;
+    const int pg0 = sub_begin / spp;
+    const int npg = sub_end > sub_begin ? (sub_end + spp - 1) / spp - pg0 : 0;
+    constexpr int RB_ = D * BITS / 8;
+    const int code_bytes = p.PS * RB_, sc_bytes = p.PS * DG * 4;
+    if (warp == 4) {
+      if (lane == 0) {
+        int jj = 0;
+        for (; jj < npg; ++jj) {
+          const int slot = jj % ATTN_RING;
+          if (jj >= ATTN_RING && !mbar_wait_bounded(&empty[slot], uint32_t(((jj / ATTN_RING) - 1) & 1))) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          const int page = p.block_table[int64_t(b) * p.max_pages + pg0 + jj];
+          const int64_t rowbase = (int64_t(page) * p.Hkv + hkv) * p.PS;
+          uint8_t* sb = attn_smem + slot * p.slot_bytes;
+          mbar_arrive_expect_tx(&full[slot], uint32_t(2 * code_bytes + 2 * sc_bytes));
+          tma_load_2d(sb, &tmk, 0, int(rowbase), &full[slot]);
+          tma_load_2d(sb + code_bytes, &tmv, 0, int(rowbase), &full[slot]);
+          bulk_g2s(sb + 2 * code_bytes, p.ks + rowbase * DG, uint32_t(sc_bytes), &full[slot]);
+          bulk_g2s(sb + 2 * code_bytes + sc_bytes, p.vs + rowbase * DG, uint32_t(sc_bytes), &full[slot]);
+        }
+        // copies already issued land before the CTA goes away
+        for (int k = 1; k <= ATTN_RING && jj - k >= 0; ++k)
+          mbar_wait_bounded(&full[(jj - k) % ATTN_RING], uint32_t(((jj - k) / ATTN_RING) & 1), 100000000ull);
+      }
+      __syncwarp();
+    } else {
+      for (int jj = 0; jj < npg; ++jj) {
+        const int slot = jj % ATTN_RING;
+        const bool ok = !*abort_flag && mbar_wait_bounded(&full[slot], uint32_t((jj / ATTN_RING) & 1));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) *abort_flag = 1;
+          aborted = true;
+          break;
+        }
+        const uint8_t* kb = attn_smem + slot * p.slot_bytes;
+        const uint8_t* vb = kb + code_bytes;
+        const float* ksb = reinterpret_cast<const float*>(kb + 2 * code_bytes);
+        const float* vsb = ksb + p.PS * DG;
+        const int s_lo = max(sub_begin, (pg0 + jj) * spp), s_hi = min(sub_end, (pg0 + jj + 1) * spp);
+        for (int sub = s_lo; sub < s_hi; ++sub) {
+          if (((sub - sub_begin) & 3) != warp) continue;
+          const int t0 = sub * 16;
+          const int lr = t0 % p.PS;  // first row of the sub-tile in the page
+          Tile T;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int row = lr + nt * 8 + r;
+#pragma unroll
+            for (int g = 0; g < DG; ++g) {
+              if constexpr (BITS == 8) {
+                const uint4 q = *reinterpret_cast<const uint4*>(kb + swz_off<RB_>(row, 64 * g + 16 * c));
+                T.kw[nt][g][0] = q.x;
+                T.kw[nt][g][1] = q.y;
+                T.kw[nt][g][2] = q.z;
+                T.kw[nt][g][3] = q.w;
+              } else {
+                const uint2 q = *reinterpret_cast<const uint2*>(kb + swz_off<RB_>(row, 32 * g + 8 * c));
+                T.kw[nt][g][0] = q.x;
+                T.kw[nt][g][1] = q.y;
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int tok = nt * 8 + 2 * c + e;
+              const bool tv = t0 + tok < len;
+#pragma unroll
+              for (int g = 0; g < DG; ++g) T.ksc[nt][e][g] = tv ? ksb[(lr + tok) * DG + g] : 0.f;
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int tok = (t >> 1) * 8 + 2 * c + (t & 1);
+            const bool tv = t0 + tok < len;
+#pragma unroll
+            for (int g = 0; g < DG; ++g) {
+              if constexpr (BITS == 8) {
+                const uint2 q = *reinterpret_cast<const uint2*>(vb + swz_off<RB_>(lr + tok, 64 * g + 8 * r));
+                T.vw[t][g][0] = q.x;
+                T.vw[t][g][1] = q.y;
+              } else {
+                T.vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vb + swz_off<RB_>(lr + tok, 32 * g + 4 * r));
+              }
+              T.vsc[t][g] = tv ? vsb[(lr + tok) * DG + g] : 0.f;
+            }
+          }
+          process(T, t0);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    }
   }
 
   // ---- merge the 4 warps through shared memory -----------------------------
-  extern __shared__ float sm[];
+  float* sm = reinterpret_cast<float*>(attn_smem + (RING ? p.ring_bytes : 0));
   float* sm_o = sm;                      // [4][G][D]
   float* sm_ml = sm + 4 * G * D;         // [4][G][2]
 #pragma unroll
@@ -311,7 +445,7 @@ __global__ void __launch_bounds__(128) qkv_decode_attn_kernel(const AttnParams p
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
     const int head = r + 8 * row;
-    if (head < G) {
+    if (head < G && warp < 4) {
       if (c == 0) {
         sm_ml[(warp * G + head) * 2 + 0] = m_run[row];
         sm_ml[(warp * G + head) * 2 + 1] = l;
@@ -375,10 +509,47 @@ __global__ void attn_combine_kernel(const float* __restrict__ o_part, const floa
   }
 }
 
+// K or V code pages as a 2-D uint8 tensor of rows of RB bytes (one row per
+// token and KV head); box = one page of one head (page_size rows), swizzled
+// so the warps' fragment reads hit distinct banks.  The row count is not
+// known here; only rows named by the block table are ever addressed.
+static int make_kv_map(CUtensorMap* map, const uint8_t* base, int RB, int PS) {
+  const cuuint64_t dims[2] = {cuuint64_t(RB), cuuint64_t(1) << 31};
+  const cuuint64_t strides[1] = {cuuint64_t(RB)};
+  const cuuint32_t box[2] = {cuuint32_t(RB), cuuint32_t(PS)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                           : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
+}
+
 template <int BITS, int D>
-static int launch_attn(const AttnParams& p, cudaStream_t st) {
-  const int smem = (4 * p.G * D + 4 * p.G * 2) * int(sizeof(float));
-  auto kern = qkv_decode_attn_kernel<BITS, D>;
+static int launch_attn(AttnParams p, cudaStream_t st) {
+  constexpr int RB = D * BITS / 8;
+  constexpr int DG = D / 64;
+  const int merge = (4 * p.G * D + 4 * p.G * 2) * int(sizeof(float));
+  // page ring: head-major pages whose code rows fit one swizzled TMA box row
+  constexpr bool RING_OK = D <= 128 && RB <= 128 && RB % 32 == 0;  // D = 256 would spill registers
+  const bool ring = RING_OK && p.head_stride == p.PS && p.slot_stride == 1 && p.PS <= 256 && aligned(p.ks, 16) &&
+                    aligned(p.vs, 16) && get_encoder() == B2F_OK;
+  CUtensorMap mk{}, mv{};
+  int smem = merge;
+  if (ring) {
+    if (make_kv_map(&mk, p.kp, RB, p.PS) != B2F_OK || make_kv_map(&mv, p.vp, RB, p.PS) != B2F_OK)
+      return B2F_ERR_INVALID;
+    const int raw = 2 * p.PS * RB + 2 * p.PS * DG * 4;
+    p.slot_bytes = (raw + 1023) / 1024 * 1024;
+    p.ring_bytes = ATTN_RING * p.slot_bytes + 128;
+    smem = p.ring_bytes + merge;
+  }
+  auto kern = qkv_decode_attn_kernel<BITS, D, false>;
+  if constexpr (RING_OK) {
+    if (ring) kern = qkv_decode_attn_kernel<BITS, D, true>;
+  }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
@@ -387,7 +558,7 @@ static int launch_attn(const AttnParams& p, cudaStream_t st) {
     }
   }
   const dim3 grid{unsigned(p.n_splits), unsigned(p.Hkv), unsigned(p.B)};
-  kern<<<grid, 128, smem, st>>>(p);
+  kern<<<grid, ring ? 160 : 128, smem, st>>>(p, mk, mv);
   int rc = check_launch();
   if (rc != B2F_OK || p.n_splits == 1) return rc;
   attn_combine_kernel<<<unsigned(int64_t(p.B) * p.Hq), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, D, p.out);
