@@ -188,7 +188,12 @@ class Qwen3MoeDecoder:
             if moe_engine == "tc" and ((H // 64) % 2 or (I // 64) % 2):
                 moe_engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
             self.moe_engine = moe_engine
-            self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine != "gemv" else 16
+            # per-slot tcgen05 kernel: 32-token tiles measured best from 16 to 512
+            # tokens (two CTAs per SM fit; hot experts take several slots)
+            if moe_engine == "tc_gather":
+                self.tile = 32
+            else:
+                self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine != "gemv" else 16
             self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
             self.plan_ws = torch.empty(self.plan_bytes, dtype=torch.uint8, device=dev)
             self.plan_status = torch.zeros(1, dtype=torch.int32, device=dev)

@@ -143,7 +143,10 @@ class ExpertParallelMoE:
             engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
         self.engine = engine
         if tile is None:
-            tile = min(256, max(16, (T + 15) // 16 * 16)) if engine != "gemv" else 16
+            if engine == "tc_gather":
+                tile = 32
+            else:
+                tile = min(256, max(16, (T + 15) // 16 * 16)) if engine != "gemv" else 16
         self.tile = tile
         self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, self.e_count, tile))
         self.plan_ws = torch.empty(max(self.plan_bytes, 16), dtype=torch.uint8, device=dev)
