@@ -132,7 +132,8 @@ def profile_kernels(dec, torch):
             state["gather"] += 1
         elif name == "b2f_qkv_decode_attn":
             tag = "attention"
-        elif name in ("b2f_qgemv_affine", "b2f_qgemm_affine_tcgen05_splitk") and args[6] == dec.qkv_rows:
+        elif name in ("b2f_qgemv_affine", "b2f_qgemm_affine_tcgen05_splitk", "b2f_qgemm_affine_tcgen05_partials") \
+                and args[6] == dec.qkv_rows:
             tag = "qkv_proj"
         if tag is None:
             return orig_call(name, *args)

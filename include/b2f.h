@@ -225,6 +225,19 @@ int b2f_qkv_decode_attn_noalloc(const void* q, const uint8_t* k_pages, const flo
 /* Workspace bytes of b2f_qgemm_affine_tcgen05_splitk (fp32 partials). */
 int64_t b2f_qgemm_splitk_workspace_bytes(int64_t M, int64_t N, int ksplit);
 
+/* Number of non-empty K ranges the split-K entry points use for `ksplit`
+ * (ranges of ceil((K/64)/ksplit) 64-wide chunks); 0 for invalid K. */
+int b2f_qgemm_splitk_ranges(int64_t K, int ksplit);
+
+/* The first half of b2f_qgemm_affine_tcgen05_splitk: fp32 partials
+ * partial[r][M][N] for r < b2f_qgemm_splitk_ranges(K, ksplit), to be summed
+ * by the consumer (b2f_combine_rmsnorm_partials,
+ * b2f_qk_norm_rope_kv_append_partials) instead of a separate pass. */
+int b2f_qgemm_affine_tcgen05_partials(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                                      const void* scales, const void* biases, int64_t N, int64_t K,
+                                      int bits, int group_size, int tile, int ksplit, float* partial,
+                                      int64_t partial_bytes, void* stream);
+
 /* b2f_qgemm_affine_tcgen05 with K cut into `ksplit` ranges so that few
  * 128-row blocks (decode-sized M, e.g. the q/k/v and o projections at 64
  * tokens) still fill every SM: each range writes fp32 partials into
@@ -411,6 +424,24 @@ int b2f_fake_quant_sym(const void* w, int dtype, int64_t n, int bits, float* out
  * NULL (plain RMSNorm); scores may be NULL (every score 1, e.g. k = 1 for an
  * already combined expert-parallel output).  resid_out may alias resid.
  * H % 8 == 0, H <= 8192. */
+/* b2f_combine_rmsnorm with the residual update taken from split-K partials:
+ * h = resid + sum_r partial[r][m][:] (nsplit fp32 planes [M, H], 16-byte
+ * aligned); resid_out = bf16(h); norm_out = RMSNorm(h). */
+int b2f_combine_rmsnorm_partials(const void* resid, const float* partial, int nsplit, int64_t M,
+                                 const void* weight, float eps, int64_t H, void* resid_out,
+                                 void* norm_out, void* stream);
+
+/* b2f_qk_norm_rope_kv_append reading the q/k/v projection as split-K partials
+ * (nsplit fp32 planes [B, (Hq+2Hkv)*D]): the row is bf16(sum of the planes),
+ * the value the projection's bf16 output would hold. */
+int b2f_qk_norm_rope_kv_append_partials(const float* qkv_partial, int nsplit, int64_t B, int64_t Hq,
+                                        int64_t Hkv, int64_t D, const void* q_norm,
+                                        const void* k_norm, float eps, float rope_theta,
+                                        const int32_t* positions, void* q_out, uint8_t* k_codes,
+                                        float* k_scales, uint8_t* v_codes, float* v_scales,
+                                        const int32_t* block_table, int64_t max_pages,
+                                        int64_t page_size, int bits, void* stream);
+
 int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, int64_t M,
                         int64_t k, const void* weight, float eps, int64_t H, void* resid_out,
                         void* norm_out, void* stream);

@@ -228,13 +228,15 @@ class Qwen3MoeDecoder:
                 ks *= 2
             return ks
 
-        self.ks_qkv = ksplit_for(self.qkv_rows, H)
-        self.ks_o = ksplit_for(H, Hq * D)
+        lib = _capi.lib()
+        # K ranges actually used (every range non-empty); 1 = no split
+        self.ks_qkv = int(lib.b2f_qgemm_splitk_ranges(H, ksplit_for(self.qkv_rows, H)))
+        self.ks_o = int(lib.b2f_qgemm_splitk_ranges(Hq * D, ksplit_for(H, Hq * D)))
         ws = 0
         if dense_engine == "tc":
-            lib = _capi.lib()
             ws = max(int(lib.b2f_qgemm_splitk_workspace_bytes(B, self.qkv_rows, self.ks_qkv)) if self.ks_qkv > 1 else 0,
                      int(lib.b2f_qgemm_splitk_workspace_bytes(B, H, self.ks_o)) if self.ks_o > 1 else 0)
+        # fp32 split-K partials, consumed by the RoPE/KV-append and residual+norm kernels
         self.dense_ws = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
         self.dense_ws_bytes = ws
 
@@ -277,18 +279,31 @@ class Qwen3MoeDecoder:
              0, ptr(self.xn), st)
         for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
             w = ly["wqkv"]
-            self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
-            call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]), ptr(ly["k_norm"]),
-                 s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]), ptr(kv["ks"]),
-                 ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page, s.kv_bits, st)
+            if self.dense_engine == "tc" and self.ks_qkv > 1:
+                self._partials(self.xn, H, w, self.ks_qkv, st)
+                call("b2f_qk_norm_rope_kv_append_partials", ptr(self.dense_ws), self.ks_qkv, B, Hq, Hkv, D,
+                     ptr(ly["q_norm"]), ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q),
+                     ptr(kv["kc"]), ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table),
+                     self.max_pages, self.page, s.kv_bits, st)
+            else:
+                self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
+                call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]),
+                     ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]),
+                     ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page,
+                     s.kv_bits, st)
             call("b2f_qkv_decode_attn", ptr(self.q), ptr(kv["kc"]), ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]),
                  ptr(self.block_table), self.max_pages, ptr(self.seq_lens), B, Hq, Hkv, D, self.page, self.page, 1,
                  s.kv_bits, 64, self.softmax_scale, self.n_splits, ptr(self.attn_ws), self.attn_ws_bytes,
                  ptr(self.attn), st)
             w = ly["wo"]
-            self._dense(self.attn, Hq * D, w, self.h, self.h, self.ks_o, st)
-            call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
-                 ptr(self.xn), st)
+            if self.dense_engine == "tc" and self.ks_o > 1:
+                self._partials(self.attn, Hq * D, w, self.ks_o, st)
+                call("b2f_combine_rmsnorm_partials", ptr(self.h), ptr(self.dense_ws), self.ks_o, B,
+                     ptr(ly["post_norm"]), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
+            else:
+                self._dense(self.attn, Hq * D, w, self.h, self.h, self.ks_o, st)
+                call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
+                     ptr(self.xn), st)
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < self.L else self.final_norm
             g, u, d = ly["gate"], ly["up"], ly["down"]
             if self.ep is not None:
@@ -337,13 +352,17 @@ class Qwen3MoeDecoder:
                  w.bits, w.group_size, ptr(residual) if isinstance(residual, torch.Tensor) else 0, ptr(out), w.N,
                  self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
 
+    def _partials(self, x, ldx, w, ksplit, st):
+        """fp32 split-K partials of x . W^T into the dense workspace."""
+        call("b2f_qgemm_affine_tcgen05_partials", ptr(x), ldx, self.B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N,
+             w.K, w.bits, w.group_size, self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
+
     def launches_per_step(self) -> int:
         """libb200flash kernel launches in one step (attention counts its combine pass)."""
         attn = 2 if self.n_splits > 1 else 1
         # qkv, rope+append, attention, o_proj, norm, router (logits + top-k/plan), gate/up, down, combine
         per_layer = 1 + 1 + attn + 1 + 1 + 2 + 2 + 1
-        if self.dense_engine == "tc":
-            per_layer += int(self.ks_qkv > 1) + int(self.ks_o > 1)  # split-K sums
+
         if self.moe_engine == "tc":
             per_layer += 1  # the row gather into expert-sorted order
         if self.ep is not None:

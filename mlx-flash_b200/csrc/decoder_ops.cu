@@ -30,7 +30,8 @@ constexpr int CMB_CHUNKS = 4;
 __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ y,
     const float* __restrict__ scores, int k, const __nv_bfloat16* __restrict__ w, float eps, int H,
-    __nv_bfloat16* __restrict__ resid_out, __nv_bfloat16* __restrict__ norm_out) {
+    __nv_bfloat16* __restrict__ resid_out, __nv_bfloat16* __restrict__ norm_out,
+    const float* __restrict__ partial = nullptr, int nsplit = 0, int64_t M = 0) {
   __shared__ float sh[8];
   const int64_t m = blockIdx.x;
   const int nvec = H / 8;
@@ -47,6 +48,20 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     for (int i = 0; i < 4; ++i) {
       h[2 * i] = __low2float(r2[i]);
       h[2 * i + 1] = __high2float(r2[i]);
+    }
+    if (partial) {  // split-K fp32 partials of a projection added to the residual
+      for (int j = 0; j < nsplit; ++j) {
+        const float4* pp = reinterpret_cast<const float4*>(partial + (int64_t(j) * M + m) * H) + 2 * v;
+        const float4 a = pp[0], c = pp[1];
+        h[0] += a.x;
+        h[1] += a.y;
+        h[2] += a.z;
+        h[3] += a.w;
+        h[4] += c.x;
+        h[5] += c.y;
+        h[6] += c.z;
+        h[7] += c.w;
+      }
     }
     if (y) {
       for (int j = 0; j < k; ++j) {
@@ -92,6 +107,8 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
 // d = lane + 32*i, so d and d+64 sit in the same lane).
 struct RopeKvParams {
   const __nv_bfloat16* qkv;
+  const float* qkv_partial;  // split-K fp32 partials [nsplit][B][NH*D] (replaces qkv when set)
+  int nsplit;
   const __nv_bfloat16* q_norm;
   const __nv_bfloat16* k_norm;
   float eps, theta;
@@ -125,8 +142,19 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
   __syncthreads();
   for (int h = warp; h < NH; h += nw) {
     float v[4];
+    if (p.qkv_partial) {
+      // the projection's bf16 output, formed here from its split-K partials
+      const int64_t plane = int64_t(gridDim.x) * NH * D;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(row[h * D + lane + 32 * i]);
+      for (int i = 0; i < 4; ++i) {
+        float a = 0.f;
+        for (int j = 0; j < p.nsplit; ++j) a += p.qkv_partial[j * plane + int64_t(b) * NH * D + h * D + lane + 32 * i];
+        v[i] = __bfloat162float(__float2bfloat16_rn(a));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(row[h * D + lane + 32 * i]);
+    }
     const bool is_q = h < p.Hq, is_k = !is_q && h < p.Hq + p.Hkv;
     if (is_q || is_k) {
       const __nv_bfloat16* nw_ = is_q ? p.q_norm : p.k_norm;
@@ -413,6 +441,43 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* 
   }
 }
 
+static int qk_norm_rope_impl(const void* qkv, const float* qkv_partial, int nsplit, int64_t B, int64_t Hq,
+                             int64_t Hkv, int64_t D, const void* q_norm, const void* k_norm, float eps,
+                             float rope_theta, const int32_t* positions, void* q_out, uint8_t* k_codes,
+                             float* k_scales, uint8_t* v_codes, float* v_scales, const int32_t* block_table,
+                             int64_t max_pages, int64_t page_size, int bits, void* stream) {
+  if (D != 128) return B2F_ERR_UNSUPPORTED;
+  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || page_size <= 0 || max_pages <= 0) return B2F_ERR_INVALID;
+  if (B == 0) return B2F_OK;
+  if (B > 0x7fffffff) return B2F_ERR_UNSUPPORTED;
+  if (!q_norm || !k_norm || !positions || !q_out || !k_codes || !k_scales || !v_codes || !v_scales ||
+      !block_table)
+    return B2F_ERR_INVALID;
+  RopeKvParams p{};
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.qkv_partial = qkv_partial;
+  p.nsplit = nsplit;
+  p.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
+  p.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
+  p.eps = eps;
+  p.theta = rope_theta;
+  p.positions = positions;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_codes = k_codes;
+  p.k_scales = k_scales;
+  p.v_codes = v_codes;
+  p.v_scales = v_scales;
+  p.block_table = block_table;
+  p.max_pages = max_pages;
+  p.Hq = int(Hq);
+  p.Hkv = int(Hkv);
+  p.PS = int(page_size);
+  p.bits = bits;
+  qk_norm_rope_kv_kernel<<<unsigned(B), 256, 0, as_stream(stream)>>>(p);
+  return check_launch();
+}
+
 }  // namespace b2f
 
 using namespace b2f;
@@ -437,38 +502,43 @@ int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, i
   return check_launch();
 }
 
+int b2f_combine_rmsnorm_partials(const void* resid, const float* partial, int nsplit, int64_t M,
+                                 const void* weight, float eps, int64_t H, void* resid_out, void* norm_out,
+                                 void* stream) {
+  if (M < 0 || H <= 0 || nsplit < 1) return B2F_ERR_INVALID;
+  if (H % 8 != 0 || H > CMB_CHUNKS * 8 * 256) return B2F_ERR_UNSUPPORTED;
+  if (M == 0) return B2F_OK;
+  if (!resid || !partial || !weight || !norm_out) return B2F_ERR_INVALID;
+  if (!aligned(resid, 16) || !aligned(partial, 16) || !aligned(weight, 16) || !aligned(norm_out, 16) ||
+      (resid_out && !aligned(resid_out, 16)))
+    return B2F_ERR_ALIGN;
+  const int threads = int(H / 8) < 256 ? int(((H / 8) + 31) / 32 * 32) : 256;
+  combine_rmsnorm_kernel<<<unsigned(M), threads, 0, as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(resid), nullptr, nullptr, 0, static_cast<const __nv_bfloat16*>(weight),
+      eps, int(H), static_cast<__nv_bfloat16*>(resid_out), static_cast<__nv_bfloat16*>(norm_out), partial, nsplit, M);
+  return check_launch();
+}
+
+int b2f_qk_norm_rope_kv_append_partials(const float* qkv_partial, int nsplit, int64_t B, int64_t Hq, int64_t Hkv,
+                                        int64_t D, const void* q_norm, const void* k_norm, float eps,
+                                        float rope_theta, const int32_t* positions, void* q_out, uint8_t* k_codes,
+                                        float* k_scales, uint8_t* v_codes, float* v_scales,
+                                        const int32_t* block_table, int64_t max_pages, int64_t page_size, int bits,
+                                        void* stream) {
+  if (nsplit < 1 || (!qkv_partial && B > 0)) return B2F_ERR_INVALID;
+  return qk_norm_rope_impl(nullptr, qkv_partial, nsplit, B, Hq, Hkv, D, q_norm, k_norm, eps, rope_theta, positions,
+                           q_out, k_codes, k_scales, v_codes, v_scales, block_table, max_pages, page_size, bits,
+                           stream);
+}
+
 int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                                const void* q_norm, const void* k_norm, float eps, float rope_theta,
                                const int32_t* positions, void* q_out, uint8_t* k_codes, float* k_scales,
                                uint8_t* v_codes, float* v_scales, const int32_t* block_table,
                                int64_t max_pages, int64_t page_size, int bits, void* stream) {
-  if (D != 128) return B2F_ERR_UNSUPPORTED;
-  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
-  if (B < 0 || Hq <= 0 || Hkv <= 0 || page_size <= 0 || max_pages <= 0) return B2F_ERR_INVALID;
-  if (B == 0) return B2F_OK;
-  if (!qkv || !q_norm || !k_norm || !positions || !q_out || !k_codes || !k_scales || !v_codes ||
-      !v_scales || !block_table)
-    return B2F_ERR_INVALID;
-  RopeKvParams p{};
-  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
-  p.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
-  p.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
-  p.eps = eps;
-  p.theta = rope_theta;
-  p.positions = positions;
-  p.q_out = static_cast<__nv_bfloat16*>(q_out);
-  p.k_codes = k_codes;
-  p.k_scales = k_scales;
-  p.v_codes = v_codes;
-  p.v_scales = v_scales;
-  p.block_table = block_table;
-  p.max_pages = max_pages;
-  p.Hq = int(Hq);
-  p.Hkv = int(Hkv);
-  p.PS = int(page_size);
-  p.bits = bits;
-  qk_norm_rope_kv_kernel<<<unsigned(B), 256, 0, as_stream(stream)>>>(p);
-  return check_launch();
+  if (!qkv && B > 0) return B2F_ERR_INVALID;
+  return qk_norm_rope_impl(qkv, nullptr, 0, B, Hq, Hkv, D, q_norm, k_norm, eps, rope_theta, positions, q_out,
+                           k_codes, k_scales, v_codes, v_scales, block_table, max_pages, page_size, bits, stream);
 }
 
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,

@@ -514,6 +514,43 @@ int64_t b2f_qgemm_splitk_workspace_bytes(int64_t M, int64_t N, int ksplit) {
   return int64_t(ksplit) * M * N * int64_t(sizeof(float));
 }
 
+int b2f_qgemm_splitk_ranges(int64_t K, int ksplit) {
+  if (K <= 0 || K % 64 != 0 || ksplit < 1) return 0;
+  const int chunks = int(K / 64);
+  const int cps = (chunks + ksplit - 1) / ksplit;
+  return (chunks + cps - 1) / cps;
+}
+
+int b2f_qgemm_affine_tcgen05_partials(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                                      const void* scales, const void* biases, int64_t N, int64_t K, int bits,
+                                      int group_size, int tile, int ksplit, float* partial,
+                                      int64_t partial_bytes, void* stream) {
+  int rc = check_tc_shape(N, K, bits, group_size);
+  if (rc != B2F_OK) return rc;
+  if (M < 0 || tile < 16 || tile > 256 || tile % 16 || ksplit < 1 || ksplit > 64) return B2F_ERR_INVALID;
+  if (M == 0) return B2F_OK;
+  if (!x || !wq || !scales || !biases || !partial) return B2F_ERR_INVALID;
+  if (ldx < K) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || (ldx % 8) != 0 || !aligned(wq, 16) || !aligned(partial, 16)) return B2F_ERR_ALIGN;
+  ksplit = b2f_qgemm_splitk_ranges(K, ksplit);
+  if (partial_bytes < b2f_qgemm_splitk_workspace_bytes(M, N, ksplit)) return B2F_ERR_WORKSPACE;
+  TcParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.M = M;
+  p.s[0] = static_cast<const __nv_bfloat16*>(scales);
+  p.b[0] = static_cast<const __nv_bfloat16*>(biases);
+  p.N = N;
+  p.K = K;
+  p.ldo = N;
+  p.tile = tile;
+  p.ksplit = ksplit;
+  p.partial = partial;
+  const int64_t slots = (M + tile - 1) / tile;
+  if (slots > 65535) return B2F_ERR_UNSUPPORTED;
+  return launch_tc(p, wq, nullptr, 1, bits, tile, slots, as_stream(stream));
+}
+
 int b2f_qgemm_affine_tcgen05_splitk(const void* x, int64_t ldx, int64_t M, const uint32_t* wq, const void* scales,
                                     const void* biases, int64_t N, int64_t K, int bits, int group_size,
                                     const void* residual, void* y, int64_t ldy, int tile, int ksplit,

@@ -47,12 +47,17 @@ def _export_cache(dec, ctx):
     return out
 
 
-@pytest.mark.parametrize("kv_bits,engine", [(8, "gemv"), (4, "gemv"), (8, "tc")])
-def test_decode_step_matches_oracle(dev, kv_bits, engine):
-    shape = Qwen3MoeShape(hidden=256, layers=2, n_heads=8, n_kv_heads=2, head_dim=128, moe_inter=128,
+@pytest.mark.parametrize("kv_bits,engine,dense,hidden", [(8, "gemv", "gemv", 256), (4, "gemv", "gemv", 256),
+                                                         (8, "tc", "gemv", 256), (8, "tc_gather", "tc", 256),
+                                                         (8, "tc_gather", "tc", 1024), (4, "gemv", "tc", 1024)])
+def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
+    """dense="tc" runs q/k/v and o through split-K partials summed inside the
+    RoPE/KV-append and residual+RMSNorm kernels (K = 1024 splits both)."""
+    shape = Qwen3MoeShape(hidden=hidden, layers=2, n_heads=8, n_kv_heads=2, head_dim=128, moe_inter=128,
                           n_experts=8, top_k=2, vocab=1000, kv_bits=kv_bits)
     B, ctx = 3, 40
-    dec = Qwen3MoeDecoder(shape, max_batch=B, max_context=128, page_size=16, device=dev, seed=7, moe_engine=engine)
+    dec = Qwen3MoeDecoder(shape, max_batch=B, max_context=128, page_size=16, device=dev, seed=7, moe_engine=engine,
+                          dense_engine=dense)
     dec.fill_random_context(ctx)
     if kv_bits == 4:
         for kv in dec.kv:  # valid 4-bit codes are 0..14 in each nibble
