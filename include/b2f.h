@@ -183,7 +183,7 @@ int64_t b2f_qkv_decode_attn_workspace_bytes(int64_t B, int64_t Hq, int64_t D, in
  * token-major pages (the reference's [S, H, D] chunk order): head_stride=1,
  * slot_stride=Hkv.
  * block_table: int32 [B, max_pages]; seq_lens: int32 [B].
- * Hq % Hkv == 0, Hq/Hkv <= 16; D in {64,128,256}; bits in {4,8}; gs=64 (or D
+ * Hq % Hkv == 0, Hq/Hkv <= 16; D in {64,128,256}; bits in {2,4,8}; gs=64 (or D
  * if D<64); page_size % 16 == 0.  n_splits >= 1 splits each sequence. */
 int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_scales,
                         const uint8_t* v_pages, const float* v_scales,
@@ -335,6 +335,21 @@ int b2f_evict_keep_indices(const float* importance, int64_t importance_len, int6
 int b2f_gather_tokens(const void* src, void* dst, int64_t outer, int64_t S_src, int64_t row_bytes,
                       const int32_t* keep, int64_t n_keep, void* stream);
 
+/* Compaction of a paged quantized KV cache (head-major pages [page][Hkv][PS]
+ * of D*bits/8 code bytes + D/64 fp32 scales per row) after an eviction
+ * decision: for sequence b and i < n_keep[b], token keep[b*keep_ld + i] of
+ * the pages named by block_table_src moves to position i of the pages named
+ * by block_table_dst (K and V codes and scales, every KV head).  Source and
+ * destination pages must be distinct.  The eviction policies of
+ * streaming_llm.py:129-160 and kv_compression.py:293-364 applied to the
+ * quantized cache instead of full-precision [H, S, D] arrays. */
+int b2f_kv_pages_gather(const uint8_t* k_pages, const float* k_scales, const uint8_t* v_pages,
+                        const float* v_scales, const int32_t* block_table_src, const int32_t* keep,
+                        int64_t keep_ld, const int32_t* n_keep, int64_t max_keep,
+                        uint8_t* k_pages_out, float* k_scales_out, uint8_t* v_pages_out,
+                        float* v_scales_out, const int32_t* block_table_dst, int64_t max_pages,
+                        int64_t B, int64_t Hkv, int64_t D, int64_t page_size, int bits, void* stream);
+
 /* ---- (e) expert parallelism: device halves of dispatch / combine -------- */
 
 /* Replaces the expert-to-rank routing of distributed_experts.py:36-80
@@ -449,7 +464,7 @@ int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, i
 /* Per token: q heads RMSNorm(q_norm)+RoPE -> q_out [B,Hq,D]; k heads
  * RMSNorm(k_norm)+RoPE then the reference KV quantizer (bf16 arithmetic,
  * group 64) into head-major page slot positions[b]; v heads quantized as is.
- * qkv: bf16 [B, (Hq+2*Hkv)*D].  D = 128; bits in {4,8}.  This is the append
+ * qkv: bf16 [B, (Hq+2*Hkv)*D].  D = 128; bits in {2,4,8}.  This is the append
  * path of QuantizedKVEntry.append (quantized_kv_cache.py:284-309) fused with
  * the attention prologue. */
 int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,

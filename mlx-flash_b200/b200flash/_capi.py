@@ -59,6 +59,8 @@ SIGNATURES = {
     "b2f_qkv_head_mean_probs": (_I, [_P, _P, _P, _P, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I,
                                      _I, ctypes.c_float, _I, _P, _I64, _P, _I64, _I, ctypes.c_float, _P]),
     "b2f_evict_keep_indices": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "b2f_kv_pages_gather": (_I, [_P, _P, _P, _P, _P, _P, _I64, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                 _I64, _I, _P]),
     "b2f_gather_tokens": (_I, [_P, _P, _I64, _I64, _I64, _P, _I64, _P]),
     "b2f_q4_0_gemv": (_I, [_P, _P, _P, _P, _I64, _I64, _I, _I64, _P]),
     "b2f_swiglu": (_I, [_P, _P, _P, _I64, _I, _P]),

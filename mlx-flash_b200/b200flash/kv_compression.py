@@ -66,6 +66,38 @@ def evict_keep_indices(importance, S: int, sink: int, window: int, budget: int, 
     return keep, int(count.item())
 
 
+def compact_pages(k_pages, k_scales, v_pages, v_scales, block_table_src, keep, n_keep, block_table_dst,
+                  num_kv_heads: int, head_dim: int, bits: int, page_size: int, out=None):
+    """Apply per-sequence keep lists to a paged quantized cache (kernel ``b2f_kv_pages_gather``).
+
+    ``keep``: int32 ``[B, max_keep]`` token positions (ascending, as
+    ``evict_keep_indices`` returns them); ``n_keep``: int32 ``[B]``.  Kept
+    token ``i`` of sequence ``b`` lands at slot ``i`` of the pages named by
+    ``block_table_dst[b]``.  Head-major pages; ``out`` = optional
+    ``(k_pages, k_scales, v_pages, v_scales)`` destination pools (default: the
+    source pools, which then must hold ``block_table_dst``'s pages distinct
+    from the source pages).  Returns the destination pools.
+    """
+    dev = require_cuda(k_pages, k_scales, v_pages, v_scales, block_table_src, keep, n_keep, block_table_dst)
+    if out is None:
+        out = (k_pages, k_scales, v_pages, v_scales)
+    bts = block_table_src.to(torch.int32).contiguous()
+    btd = block_table_dst.to(torch.int32).contiguous()
+    if bts.shape != btd.shape:
+        raise ValueError("source and destination block tables must have the same shape")
+    kp = keep.to(torch.int32).contiguous()
+    if kp.dim() == 1:
+        kp = kp.reshape(1, -1)
+    nk = n_keep.to(torch.int32).contiguous().reshape(-1)
+    B = bts.shape[0]
+    if kp.shape[0] != B or nk.numel() != B:
+        raise ValueError("keep / n_keep must have one row per sequence")
+    call("b2f_kv_pages_gather", ptr(k_pages), ptr(k_scales), ptr(v_pages), ptr(v_scales), ptr(bts), ptr(kp),
+         kp.shape[1], ptr(nk), kp.shape[1], ptr(out[0]), ptr(out[1]), ptr(out[2]), ptr(out[3]), ptr(btd),
+         bts.shape[1], B, num_kv_heads, head_dim, page_size, bits, stream_of(dev))
+    return out
+
+
 class AttentionScoreTracker:
     """Per-token importance per layer (and H2O's cross-layer total)."""
 

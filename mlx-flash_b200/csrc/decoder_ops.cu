@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
   const int page = p.block_table[int64_t(b) * p.max_pages + pos / p.PS];
   const int slot = pos % p.PS;
   const __nv_bfloat16* row = p.qkv + int64_t(b) * NH * D;
-  const float mi = p.bits == 8 ? 127.f : 7.f;
+  const float mi = p.bits == 8 ? 127.f : p.bits == 4 ? 7.f : 1.f;
   // rotary angles of this token: one sincosf per frequency, shared by all heads
   __shared__ float rope_c[D / 2], rope_s[D / 2];
   if (threadIdx.x < D / 2) {
@@ -206,6 +206,16 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
     if (p.bits == 8) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = uint8_t(c[i]);
+    } else if (p.bits == 2) {
+      // four codes per byte, the first in the top two bits
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t c1 = __shfl_down_sync(0xffffffffu, c[i], 1);
+        const uint32_t c2 = __shfl_down_sync(0xffffffffu, c[i], 2);
+        const uint32_t c3 = __shfl_down_sync(0xffffffffu, c[i], 3);
+        if ((lane & 3) == 0)
+          dst[(lane + 32 * i) >> 2] = uint8_t((c[i] << 6) | ((c1 & 3u) << 4) | ((c2 & 3u) << 2) | (c3 & 3u));
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -447,7 +457,7 @@ static int qk_norm_rope_impl(const void* qkv, const float* qkv_partial, int nspl
                              float* k_scales, uint8_t* v_codes, float* v_scales, const int32_t* block_table,
                              int64_t max_pages, int64_t page_size, int bits, void* stream) {
   if (D != 128) return B2F_ERR_UNSUPPORTED;
-  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || page_size <= 0 || max_pages <= 0) return B2F_ERR_INVALID;
   if (B == 0) return B2F_OK;
   if (B > 0x7fffffff) return B2F_ERR_UNSUPPORTED;

@@ -71,7 +71,7 @@ __device__ __forceinline__ void hm_scores(const HmParams& p, int b, int hkv, int
   const int RB = p.D * BITS / 8, DG = p.D / 64;
   const uint8_t* kr = p.kp + row * RB;
   const float* ksr = p.ks + row * DG;
-  constexpr float MI = BITS == 8 ? 127.f : 7.f;
+  constexpr float MI = BITS == 8 ? 127.f : BITS == 4 ? 7.f : 1.f;
   float kv[HM_MAXD / 32];
 #pragma unroll
   for (int i = 0; i < HM_MAXD / 32; ++i) {
@@ -81,9 +81,11 @@ __device__ __forceinline__ void hm_scores(const HmParams& p, int b, int hkv, int
       uint32_t code;
       if constexpr (BITS == 8) {
         code = kr[d];
-      } else {
+      } else if constexpr (BITS == 4) {
         const uint8_t byte = kr[d >> 1];
         code = (d & 1) ? (byte & 0xFu) : (byte >> 4);
+      } else {
+        code = (kr[d >> 2] >> (6 - 2 * (d & 3))) & 0x3u;
       }
       v = (float(code) - MI) * ksr[d >> 6];
     }
@@ -404,7 +406,7 @@ int b2f_qkv_head_mean_probs(const void* q, const uint8_t* k_pages, const float* 
                             int64_t Hkv, int64_t D, int64_t page_size, int64_t head_stride, int64_t slot_stride,
                             int bits, int group_size, float softmax_scale, int n_splits, void* workspace,
                             int64_t workspace_bytes, float* out, int64_t out_ld, int mode, float decay, void* stream) {
-  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
   if (group_size != 64 || D % 64 != 0 || D > HM_MAXD) return B2F_ERR_UNSUPPORTED;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Hq / Hkv > HM_MAXG || Hq > 256) return B2F_ERR_UNSUPPORTED;
   if (page_size <= 0 || max_pages <= 0 || max_len < 0 || out_ld < max_len || n_splits <= 0 || mode < 0 || mode > 2)
@@ -444,6 +446,9 @@ int b2f_qkv_head_mean_probs(const void* q, const uint8_t* k_pages, const float* 
   if (bits == 8) {
     hm_pass1_kernel<8><<<g1, 128, 0, st>>>(p);
     hm_pass2_kernel<8><<<g2, 128, 0, st>>>(p);
+  } else if (bits == 2) {
+    hm_pass1_kernel<2><<<g1, 128, 0, st>>>(p);
+    hm_pass2_kernel<2><<<g2, 128, 0, st>>>(p);
   } else {
     hm_pass1_kernel<4><<<g1, 128, 0, st>>>(p);
     hm_pass2_kernel<4><<<g2, 128, 0, st>>>(p);
@@ -480,3 +485,67 @@ int b2f_gather_tokens(const void* src, void* dst, int64_t outer, int64_t S_src, 
 }
 
 }  // extern "C"
+
+// ---- compaction of a paged quantized cache ----------------------------------
+// For sequence b and kept position i < n_keep[b]: token keep[b][i] of the
+// source pages (block table bt_src) moves to position i of the destination
+// pages (bt_dst), for every KV head: codes (RB bytes) and scales (DG floats)
+// of K and V.  Head-major pages [page][Hkv][PS]; one warp per (b, i, head).
+namespace b2f {
+__global__ void __launch_bounds__(256) kv_pages_gather_kernel(
+    const uint8_t* __restrict__ kp, const float* __restrict__ ks, const uint8_t* __restrict__ vp,
+    const float* __restrict__ vs, const int32_t* __restrict__ bt_src, const int32_t* __restrict__ keep,
+    int64_t keep_ld, const int32_t* __restrict__ n_keep, uint8_t* __restrict__ kp_out, float* __restrict__ ks_out,
+    uint8_t* __restrict__ vp_out, float* __restrict__ vs_out, const int32_t* __restrict__ bt_dst, int64_t max_pages,
+    int B, int Hkv, int PS, int RB, int DG, int64_t max_keep) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t total = int64_t(B) * max_keep * Hkv;
+  if (wid >= total) return;
+  const int h = int(wid % Hkv);
+  const int64_t rest = wid / Hkv;
+  const int64_t i = rest % max_keep;
+  const int b = int(rest / max_keep);
+  if (i >= n_keep[b]) return;
+  const int t = keep[int64_t(b) * keep_ld + i];
+  if (t < 0 || t / PS >= max_pages || i / PS >= max_pages) return;  // keep entry outside the block table
+  const int64_t src = (int64_t(bt_src[int64_t(b) * max_pages + t / PS]) * Hkv + h) * PS + t % PS;
+  const int64_t dst = (int64_t(bt_dst[int64_t(b) * max_pages + i / PS]) * Hkv + h) * PS + i % PS;
+  for (int o = lane * 4; o < RB; o += 128) {
+    *reinterpret_cast<uint32_t*>(kp_out + dst * RB + o) = *reinterpret_cast<const uint32_t*>(kp + src * RB + o);
+    *reinterpret_cast<uint32_t*>(vp_out + dst * RB + o) = *reinterpret_cast<const uint32_t*>(vp + src * RB + o);
+  }
+  if (lane < DG) {
+    ks_out[dst * DG + lane] = ks[src * DG + lane];
+    vs_out[dst * DG + lane] = vs[src * DG + lane];
+  }
+}
+}  // namespace b2f
+
+extern "C" int b2f_kv_pages_gather(const uint8_t* k_pages, const float* k_scales, const uint8_t* v_pages,
+                                   const float* v_scales, const int32_t* block_table_src, const int32_t* keep,
+                                   int64_t keep_ld, const int32_t* n_keep, int64_t max_keep, uint8_t* k_pages_out,
+                                   float* k_scales_out, uint8_t* v_pages_out, float* v_scales_out,
+                                   const int32_t* block_table_dst, int64_t max_pages, int64_t B, int64_t Hkv,
+                                   int64_t D, int64_t page_size, int bits, void* stream) {
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (B < 0 || Hkv <= 0 || D <= 0 || D % 64 != 0 || page_size <= 0 || max_pages <= 0 || max_keep < 0 ||
+      keep_ld < max_keep)
+    return B2F_ERR_INVALID;
+  const int RB = int(D * bits / 8);
+  if (RB % 4 != 0) return B2F_ERR_UNSUPPORTED;
+  if (B == 0 || max_keep == 0) return B2F_OK;
+  if (!k_pages || !k_scales || !v_pages || !v_scales || !block_table_src || !keep || !n_keep || !k_pages_out ||
+      !k_scales_out || !v_pages_out || !v_scales_out || !block_table_dst)
+    return B2F_ERR_INVALID;
+  if (!aligned(k_pages, 4) || !aligned(v_pages, 4) || !aligned(k_pages_out, 4) || !aligned(v_pages_out, 4))
+    return B2F_ERR_ALIGN;
+  const int64_t warps = B * max_keep * Hkv;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  if (blocks > 0x7fffffff) return B2F_ERR_UNSUPPORTED;
+  kv_pages_gather_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(
+      k_pages, k_scales, v_pages, v_scales, block_table_src, keep, keep_ld, n_keep, k_pages_out, k_scales_out,
+      v_pages_out, v_scales_out, block_table_dst, max_pages, int(B), int(Hkv), int(page_size), RB, int(D / 64),
+      max_keep);
+  return check_launch();
+}

@@ -69,10 +69,10 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
   constexpr int KSTEPS = D / 16;  // MMA k-steps for Q.K^T
   constexpr int NTD = D / 8;      // 8-wide output column tiles
   constexpr int RB = D * BITS / 8;
-  constexpr float MI = BITS == 8 ? 127.f : 7.f;
+  constexpr float MI = BITS == 8 ? 127.f : BITS == 4 ? 7.f : 1.f;
   constexpr float KOFF = 1024.f + MI;
-  constexpr int KW = BITS == 8 ? 4 : 2;  // K words per thread per group per token
-  constexpr int VW = BITS == 8 ? 2 : 1;  // V words per thread per group per token
+  constexpr int KW = BITS == 8 ? 4 : BITS == 4 ? 2 : 1;  // K words per thread per group per token
+  constexpr int VW = BITS == 8 ? 2 : 1;                  // V words per thread per group per token
 
   const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -121,6 +121,15 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
           qa[g * 4 + s][h2] = pack_f16x2(v[4 * s], v[4 * s + 1]);
           qa[g * 4 + s][2 + h2] = pack_f16x2(v[4 * s + 2], v[4 * s + 3]);
         }
+      } else if constexpr (BITS == 2) {
+        // k-step st takes the crumb pairs at shifts 4st and 4st+2 of the word
+        // (elements lo, lo+8 with lo = 3,2 | 1,0 | 7,6 | 5,4)
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          const int lo0 = (st & 1) ? 1 : 3, base = (st >> 1) * 4;
+          qa[g * 4 + st][h2] = pack_f16x2(v[base + lo0], v[base + lo0 + 8]);
+          qa[g * 4 + st][2 + h2] = pack_f16x2(v[base + lo0 - 1], v[base + lo0 + 7]);
+        }
       } else {
 #pragma unroll
         for (int wi = 0; wi < 2; ++wi) {
@@ -167,6 +176,8 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
           T.kw[nt][g][1] = q.y;
           T.kw[nt][g][2] = q.z;
           T.kw[nt][g][3] = q.w;
+        } else if constexpr (BITS == 2) {
+          T.kw[nt][g][0] = *reinterpret_cast<const uint32_t*>(krow + 16 * g + 4 * c);
         } else {
           const uint2 q = *reinterpret_cast<const uint2*>(krow + 32 * g + 8 * c);
           T.kw[nt][g][0] = q.x;
@@ -192,6 +203,8 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
           const uint2 q = *reinterpret_cast<const uint2*>(vrow + 64 * g + 8 * r);
           T.vw[t][g][0] = q.x;
           T.vw[t][g][1] = q.y;
+        } else if constexpr (BITS == 2) {
+          T.vw[t][g][0] = *reinterpret_cast<const uint16_t*>(vrow + 16 * g + 2 * r);
         } else {
           T.vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vrow + 32 * g + 4 * r);
         }
@@ -221,6 +234,14 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
           for (int st = 0; st < 4; ++st) {
             const uint32_t w = kw[nt][g][st];
             const uint32_t bf[2] = {prmt(w, 0x64646464u, 0x4140u), prmt(w, 0x64646464u, 0x4342u)};
+            mma_f16_16816(sacc[g], qa[g * 4 + st], bf);
+          }
+        } else if constexpr (BITS == 2) {
+          const uint32_t w = kw[nt][g][0];
+#pragma unroll
+          for (int st = 0; st < 4; ++st) {
+            const uint32_t bf[2] = {and_or(w >> (4 * st), 0x00030003u, 0x64006400u),
+                                    and_or(w >> (4 * st + 2), 0x00030003u, 0x64006400u)};
             mma_f16_16816(sacc[g], qa[g * 4 + st], bf);
           }
         } else {
@@ -296,6 +317,12 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
         const uint32_t sel = uint32_t(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
         x01 = and_or(prmt(vw[0][gj][wsel], vw[1][gj][wsel], sel), 0x00FF00FFu, 0x64006400u);
         x23 = and_or(prmt(vw[2][gj][wsel], vw[3][gj][wsel], sel), 0x00FF00FFu, 0x64006400u);
+      } else if constexpr (BITS == 2) {
+        // element 8r+jj: byte jj/4 of the two loaded, crumb jj%4 (most significant first)
+        const int k = jj >> 2, sh = 6 - 2 * (jj & 3);
+        const uint32_t sel = uint32_t(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
+        x01 = and_or(prmt(vw[0][gj][0], vw[1][gj][0], sel) >> sh, 0x00030003u, 0x64006400u);
+        x23 = and_or(prmt(vw[2][gj][0], vw[3][gj][0], sel) >> sh, 0x00030003u, 0x64006400u);
       } else {
         const int k = jj >> 1;
         const uint32_t sel = uint32_t(k | (k << 4) | ((4 + k) << 8) | ((4 + k) << 12));
@@ -397,6 +424,8 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
                 T.kw[nt][g][1] = q.y;
                 T.kw[nt][g][2] = q.z;
                 T.kw[nt][g][3] = q.w;
+              } else if constexpr (BITS == 2) {
+                T.kw[nt][g][0] = *reinterpret_cast<const uint32_t*>(kb + swz_off<RB_>(row, 16 * g + 4 * c));
               } else {
                 const uint2 q = *reinterpret_cast<const uint2*>(kb + swz_off<RB_>(row, 32 * g + 8 * c));
                 T.kw[nt][g][0] = q.x;
@@ -421,6 +450,8 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
                 const uint2 q = *reinterpret_cast<const uint2*>(vb + swz_off<RB_>(lr + tok, 64 * g + 8 * r));
                 T.vw[t][g][0] = q.x;
                 T.vw[t][g][1] = q.y;
+              } else if constexpr (BITS == 2) {
+                T.vw[t][g][0] = *reinterpret_cast<const uint16_t*>(vb + swz_off<RB_>(lr + tok, 16 * g + 2 * r));
               } else {
                 T.vw[t][g][0] = *reinterpret_cast<const uint32_t*>(vb + swz_off<RB_>(lr + tok, 32 * g + 4 * r));
               }
@@ -583,7 +614,7 @@ int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_sc
                         int64_t slot_stride, int bits, int group_size, float softmax_scale,
                         int n_splits, void* workspace, int64_t workspace_bytes, void* out,
                         void* stream) {
-  if (!(bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
   if (!(D == 64 || D == 128 || D == 256) || group_size != 64) return B2F_ERR_UNSUPPORTED;
   if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) return B2F_ERR_INVALID;
   if (Hq / Hkv > 16) return B2F_ERR_UNSUPPORTED;
@@ -630,6 +661,11 @@ int b2f_qkv_decode_attn(const void* q, const uint8_t* k_pages, const float* k_sc
     if (D == 64) return launch_attn<8, 64>(p, st);
     if (D == 128) return launch_attn<8, 128>(p, st);
     return launch_attn<8, 256>(p, st);
+  }
+  if (bits == 2) {
+    if (D == 64) return launch_attn<2, 64>(p, st);
+    if (D == 128) return launch_attn<2, 128>(p, st);
+    return launch_attn<2, 256>(p, st);
   }
   if (D == 64) return launch_attn<4, 64>(p, st);
   if (D == 128) return launch_attn<4, 128>(p, st);

@@ -49,7 +49,8 @@ def _export_cache(dec, ctx):
 
 @pytest.mark.parametrize("kv_bits,engine,dense,hidden", [(8, "gemv", "gemv", 256), (4, "gemv", "gemv", 256),
                                                          (8, "tc", "gemv", 256), (8, "tc_gather", "tc", 256),
-                                                         (8, "tc_gather", "tc", 1024), (4, "gemv", "tc", 1024)])
+                                                         (8, "tc_gather", "tc", 1024), (4, "gemv", "tc", 1024),
+                                                         (2, "tc_gather", "gemv", 256)])
 def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
     """dense="tc" runs q/k/v and o through split-K partials summed inside the
     RoPE/KV-append and residual+RMSNorm kernels (K = 1024 splits both)."""
@@ -63,6 +64,12 @@ def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
         for kv in dec.kv:  # valid 4-bit codes are 0..14 in each nibble
             for k in ("kc", "vc"):
                 kv[k].copy_(((kv[k] % 15) << 4) | (kv[k] // 16 % 15))
+    if kv_bits == 2:
+        for kv in dec.kv:  # valid 2-bit codes are 0..2 in each crumb
+            for k in ("kc", "vc"):
+                c = kv[k]
+                kv[k].copy_((((c >> 6) % 3) << 6) | ((((c >> 4) & 3) % 3) << 4) | ((((c >> 2) & 3) % 3) << 2)
+                            | ((c & 3) % 3))
     model = _export(dec)
     cache = _export_cache(dec, ctx)
     tokens = to_np(dec.tokens).astype(np.int64)

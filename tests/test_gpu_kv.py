@@ -32,7 +32,7 @@ def test_quantize_tensor_matches_reference_vectors(golden, dev):
     assert n >= 100
 
 
-@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("bits", [2, 4, 8])
 def test_pack_512_token_chunk_config2(dev, bits):
     """The 512-token prefill chunk of 16 sequences x 8 KV heads x 128 (bf16): byte-exact."""
     rng = np.random.default_rng(bits)
@@ -145,7 +145,7 @@ def _paged_case(dev, rng, B, lens, Hq, Hkv, D, bits, page):
     return (to_dev(q, "bf16", dev), T(kp), T(ks), T(vp), T(vs), T(bt), T(np.array(lens, np.int32))), (q, keys, vals)
 
 
-@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("bits", [2, 4, 8])
 @pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (32, 4, 128), (8, 8, 64), (16, 2, 256)])
 def test_decode_attention_paged(dev, bits, Hq, Hkv, D):
     rng = np.random.default_rng(bits * 1000 + Hq + D)
@@ -158,9 +158,9 @@ def test_decode_attention_paged(dev, bits, Hq, Hkv, D):
 
 
 def test_decode_attention_config2_shape(dev):
-    """Llama-3-8B heads (32q/8kv, d128), batch 16, context 8192, 8-bit and 4-bit KV."""
+    """Llama-3-8B heads (32q/8kv, d128), batch 16, context 8192, 8-, 4- and 2-bit KV."""
     rng = np.random.default_rng(2)
-    for bits in (8, 4):
+    for bits in (8, 4, 2):
         args, (q, keys, vals) = _paged_case(dev, rng, 16, [8192] * 16, 32, 8, 128, bits, 128)
         out = to_np(decode_attention(*args, bits=bits, page_size=128, num_kv_heads=8))
         sel = [0, 7, 15]

@@ -9,7 +9,8 @@ import torch
 
 from b200flash import _capi
 from b200flash.kv_compression import (AttentionScoreTracker, CompressedKVCache, KVCompressionConfig,
-                                      evict_keep_indices)
+                                      compact_pages, evict_keep_indices)
+from b200flash.quantized_kv_cache import decode_attention
 from b200flash.streaming_llm import StreamingLLMCache, StreamingLLMConfig
 from oracle import attn, kv_evict
 
@@ -74,6 +75,7 @@ def test_keep_indices_long_context(dev, S, sink, window, budget, kind):
 
 
 @pytest.mark.parametrize("bits,Hq,Hkv,D,splits", [(8, 32, 8, 128, 4), (4, 32, 4, 128, 1), (8, 8, 8, 64, 3),
+                                                  (2, 32, 8, 128, 2),
                                                   (4, 16, 2, 256, 2)])
 def test_head_mean_probs_from_packed_pages(dev, bits, Hq, Hkv, D, splits):
     rng = np.random.default_rng(bits * 100 + Hq)
@@ -105,3 +107,45 @@ def test_tracker_record_decode_accumulates(dev):
     _, means = attn.decode_attention(q, keys, vals)
     assert np.allclose(to_np(tr._importance[0]), 2 * means[0], rtol=2e-3, atol=1e-6)
     assert np.allclose(to_np(tr._global_importance), 3 * means[0], rtol=2e-3, atol=1e-6)
+
+
+@pytest.mark.parametrize("bits,Hq,Hkv,D", [(8, 32, 8, 128), (4, 32, 4, 128), (4, 16, 2, 256), (2, 8, 8, 64)])
+def test_compact_pages_then_decode(dev, bits, Hq, Hkv, D):
+    """H2O keep lists applied to a paged quantized cache: every kept row's codes
+    and scales move bit-exactly, and decode attention over the compacted pages
+    equals the oracle's attention over the kept tokens only."""
+    rng = np.random.default_rng(bits * 7 + D)
+    lens = [5, 300, 1000, 64]
+    page = 64
+    args, (q, keys, vals) = _paged_case(dev, rng, len(lens), lens, Hq, Hkv, D, bits, page)
+    qd, kp, ks, vp, vs, bt, sl = args
+    _, means = attn.decode_attention(q, keys, vals)
+    keeps = [kv_evict.keep_indices(means[b], L, 4, 32, max(40, L // 4)) for b, L in enumerate(lens)]
+    max_keep = max(len(k) for k in keeps)
+    keep = np.zeros((len(lens), max_keep), np.int32)
+    for b, k in enumerate(keeps):
+        keep[b, :len(k)] = k
+    n_keep = np.array([len(k) for k in keeps], np.int32)
+    # destination pages: a fresh pool, pages in reverse order
+    total = kp.shape[0]
+    btd = np.zeros(tuple(bt.shape), np.int32)
+    nxt = total - 1
+    for b, k in enumerate(keeps):
+        for j in range((len(k) + page - 1) // page):
+            btd[b, j] = nxt
+            nxt -= 1
+    outs = tuple(torch.zeros_like(t) for t in (kp, ks, vp, vs))
+    T = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    compact_pages(kp, ks, vp, vs, bt, T(keep), T(n_keep), T(btd), Hkv, D, bits, page, out=outs)
+    torch.cuda.synchronize()
+    src = [to_np(t) for t in (kp, ks, vp, vs)]
+    got = [to_np(t) for t in outs]
+    btn = to_np(bt)
+    for b, k in enumerate(keeps):
+        for i, t in enumerate(k):
+            for s_arr, g_arr in zip(src, got):
+                assert np.array_equal(g_arr[btd[b, i // page], :, i % page], s_arr[btn[b, t // page], :, t % page])
+    out = decode_attention(qd, outs[0], outs[1], outs[2], outs[3], T(btd), T(n_keep), bits, page, Hkv)
+    ref, _ = attn.decode_attention(q, [keys[b][k] for b, k in enumerate(keeps)],
+                                   [vals[b][k] for b, k in enumerate(keeps)])
+    assert np.allclose(to_np(out.float()), ref, rtol=1e-2, atol=2e-2)
