@@ -259,6 +259,35 @@ int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, cons
                        float* scores, int tile, void* plan_workspace, int64_t plan_workspace_bytes,
                        int32_t* status_out, void* stream);
 
+/* ---- (c) grouped GEMM for decode-sized expert tiles (register dequant) -- */
+
+/* mx.gather_qmm (expert_streaming.py:230-241; SwitchGLU front half of
+ * kernels/ops.py:48-108 fused when w_up is non-NULL) for decode-sized expert
+ * tiles: the 4-bit codes are TMA-staged in shared memory, unpacked in
+ * registers and fed to warp-level tensor-core MMA (mma.sync m16n8k16 bf16,
+ * 16 weight rows x 8 tokens), each 64-wide group folded as
+ * s*sum(q x) + b*sum(x) in fp32 (the order MLX's quantized kernels use).
+ * Plan from b2f_moe_plan / b2f_moe_route_plan / b2f_ep_plan with tile = 16;
+ * same weight format as b2f_gather_qgemm_affine_tcgen05; bits 4,
+ * group_size 64, K % 128 == 0, N % 8 == 0.
+ * x_plan_order = 0: x row of assignment a is x_row_index[a] (or a/x_row_div),
+ *   natural column order.
+ * x_plan_order = 1: x row i belongs to sorted position i of the plan and each
+ *   group of 8 columns is stored in the order (0,4,1,5,2,6,3,7) (what
+ *   b2f_moe_gather_rows writes, or this call with out_plan_order = 1).
+ * out_plan_order = 0: out[a, :] for assignment a, natural column order.
+ * out_plan_order = 1: out row i = sorted position i, columns permuted as above
+ *   (the input of the down projection with x_plan_order = 1).
+ * A device wait that gives up records B2F_ERR_TIMEOUT in the plan's status
+ * word (int32 at byte 4 of the plan workspace). */
+int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
+                                const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                const uint32_t* w_up, const void* s_up, const void* b_up,
+                                int64_t N, int64_t K, int bits, int group_size, int tile,
+                                void* plan_workspace, int64_t plan_workspace_bytes, void* out,
+                                int64_t ldo, int out_plan_order, void* stream);
+
 /* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
 
 /* Copies the planned assignments' activation rows into plan order:

@@ -51,6 +51,8 @@ SIGNATURES = {
     "b2f_qk_norm_rope_kv_append_partials": (_I, [_P, _I, _I64, _I64, _I64, _I64, _P, _P, _F, _F, _P, _P, _P, _P,
                                                  _P, _P, _P, _I64, _I64, _I, _P]),
     "b2f_moe_route_plan": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P, _P, _I, _P, _I64, _P, _P]),
+    "b2f_gather_qgemm_affine_mma": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64,
+                                         _I, _I, _I, _P, _I64, _P, _I64, _I, _P]),
     "b2f_moe_gather_rows": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _I64, _P]),
     "b2f_sorted_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I,
                                              _P, _I64, _P, _I64, _I, _P]),

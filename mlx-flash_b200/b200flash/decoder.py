@@ -178,20 +178,26 @@ class Qwen3MoeDecoder:
         else:
             self.inds, self.scores = self.ep.inds, self.ep.scores
         self.gates = torch.empty(B, E, dtype=torch.float32, device=dev)
-        # routed experts: tcgen05 grouped GEMM once experts see >= 1 token on
-        # average, else the register-fragment GEMV (tiles of 16 tokens)
         if self.ep is None:
             if moe_engine == "auto":
-                moe_engine = "tc_gather" if A >= E else "gemv"
-            if moe_engine not in ("tc", "tc_gather", "gemv"):
+                # 4-bit / group 64 / 128-wide K: register-unpack warp MMA (decode
+                # tiles of <= 16 tokens); else tcgen05 once experts see >= 1 token
+                # on average, the register GEMV below that
+                mma_ok = bits == 4 and gs == 64 and H % 128 == 0 and I % 128 == 0
+                moe_engine = "mma" if mma_ok else ("tc_gather" if A >= E else "gemv")
+            if moe_engine not in ("tc", "tc_gather", "gemv", "mma"):
                 raise ValueError(f"unknown expert engine {moe_engine!r}")
             if moe_engine == "tc" and ((H // 64) % 2 or (I // 64) % 2):
                 moe_engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
+            if moe_engine == "mma" and (bits != 4 or gs != 64 or H % 128 or I % 128):
+                moe_engine = "tc_gather"  # register-dequant MMA: 4-bit, group 64, 128-wide K chunks
             self.moe_engine = moe_engine
             # per-slot tcgen05 kernel: 32-token tiles measured best from 16 to 512
             # tokens (two CTAs per SM fit; hot experts take several slots)
             if moe_engine == "tc_gather":
                 self.tile = 32
+            elif moe_engine == "mma":
+                self.tile = 16
             else:
                 self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine != "gemv" else 16
             self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))
@@ -316,7 +322,15 @@ class Qwen3MoeDecoder:
             call("b2f_moe_route_plan", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
                  self.plan_bytes, ptr(self.plan_status), st)
-            if self.moe_engine == "tc":
+            if self.moe_engine == "mma":
+                # gate/up rows land in plan order (the down GEMM's input layout)
+                call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(g.wq), ptr(g.scales),
+                     ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,
+                     ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, 1, st)
+                call("b2f_gather_qgemm_affine_mma", ptr(self.hh), I, 0, 1, 1, A, E, ptr(d.wq), ptr(d.scales),
+                     ptr(d.biases), 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws),
+                     self.plan_bytes, ptr(self.y), H, 0, st)
+            elif self.moe_engine == "tc":
                 call("b2f_moe_gather_rows", ptr(self.xn), H, 0, s.top_k, A, E, self.tile, ptr(self.plan_ws),
                      self.plan_bytes, H, ptr(self.xs), H, st)
                 call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.xs), H, A, E, ptr(g.wq), ptr(g.scales),

@@ -136,15 +136,22 @@ class ExpertParallelMoE:
         self.wts = torch.zeros(A, dtype=torch.float32, device=dev)
         self.local = torch.full((A,), -1, dtype=torch.int32, device=dev)
         if engine == "auto":
-            engine = "tc_gather" if T * top_k >= self.e_count and group_size == 64 else "gemv"
-        if engine not in ("tc", "tc_gather", "gemv"):
+            if bits == 4 and group_size == 64 and hidden % 128 == 0 and inter % 128 == 0:
+                engine = "mma"
+            else:
+                engine = "tc_gather" if T * top_k >= self.e_count and group_size == 64 else "gemv"
+        if engine not in ("tc", "tc_gather", "gemv", "mma"):
             raise ValueError(f"unknown expert engine {engine!r}")
         if engine == "tc" and ((hidden // 64) % 2 or (inter // 64) % 2):
             engine = "tc_gather"  # the sorted-row kernel copies scales two groups at a time
+        if engine == "mma" and (bits != 4 or group_size != 64 or hidden % 128 or inter % 128):
+            engine = "tc_gather"  # register-dequant MMA: 4-bit, group 64, 128-wide K chunks
         self.engine = engine
         if tile is None:
             if engine == "tc_gather":
                 tile = 32
+            elif engine == "mma":
+                tile = 16
             else:
                 tile = min(256, max(16, (T + 15) // 16 * 16)) if engine != "gemv" else 16
         self.tile = tile
@@ -177,7 +184,14 @@ class ExpertParallelMoE:
         gw, gs_, gb = gate
         uw, us, ub = up
         dw, ds, db = down
-        if self.engine == "tc":
+        if self.engine == "mma":
+            call("b2f_gather_qgemm_affine_mma", ptr(self.recv), self.H, ptr(self.x_row), 1, 0, self.A, self.e_count,
+                 ptr(gw), ptr(gs_), ptr(gb), ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile,
+                 ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), self.I, 1, st)
+            call("b2f_gather_qgemm_affine_mma", ptr(self.hh), self.I, 0, 1, 1, self.A, self.e_count, ptr(dw),
+                 ptr(ds), ptr(db), 0, 0, 0, self.H, self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws),
+                 self.plan_bytes, ptr(self.y), self.H, 0, st)
+        elif self.engine == "tc":
             call("b2f_moe_gather_rows", ptr(self.recv), self.H, ptr(self.x_row), 1, self.A, self.e_count, self.tile,
                  ptr(self.plan_ws), self.plan_bytes, self.H, ptr(self.xs), self.H, st)
             call("b2f_sorted_qgemm_affine_tcgen05", ptr(self.xs), self.H, self.A, self.e_count, ptr(gw), ptr(gs_),

@@ -180,6 +180,34 @@ def gather_qmm_tc_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bias
     return out
 
 
+def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size, bits,
+                           x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None,
+                           x_plan_order: bool = False, out_plan_order: bool = False) -> torch.Tensor:
+    """Grouped GEMM over a prepared plan (tile 16) on warp-level tensor-core MMA
+    with the 4-bit codes unpacked in registers (decode-sized expert tiles).
+
+    ``x_plan_order``: ``x_rows`` is in plan order with permuted columns (the
+    ``moe_gather_rows`` layout, or this function's ``out_plan_order`` output).
+    ``out_plan_order``: the result keeps that layout (input of the down projection).
+    """
+    dev = require_cuda(x_rows, w, scales, biases, x_row_index)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    if bits != 4 or group_size != 64 or K % 128 or N % 8 or plan.tile != 16:
+        raise ValueError("the register-dequant MMA path needs 4-bit, group 64, K % 128 == 0, N % 8 == 0, tile 16")
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
+    wu = su = bu = None
+    if up is not None:
+        wu, su, bu = (t.contiguous() for t in up)
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_gather_qgemm_affine_mma", ptr(xc), K, ptr(xri), int(x_row_div), int(x_plan_order), plan.A, E,
+         ptr(w.contiguous()), ptr(scales.contiguous()), ptr(biases.contiguous()), ptr(wu), ptr(su), ptr(bu), N, K,
+         bits, group_size, plan.tile, ptr(plan.workspace), plan.workspace.numel(), ptr(out), N, int(out_plan_order),
+         stream_of(dev))
+    return out
+
+
 def moe_gather_rows(x_rows: torch.Tensor, plan: "MoEPlan", x_row_index: torch.Tensor = None,
                     x_row_div: int = 1) -> torch.Tensor:
     """Activation rows in the plan's expert-sorted order (``[A, K]``; rows past

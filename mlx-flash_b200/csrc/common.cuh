@@ -168,6 +168,21 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   return true;
 }
+// mbar_wait_bounded for a thread that has nothing else to do while it waits
+// (a producer whose ring is full): backs off between polls so the spinning
+// thread leaves the issue slots to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_t parity,
+                                                          uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  uint32_t ns = 32;
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > limit_ns) return false;
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+  }
+  return true;
+}
 // named barrier over the first `nthreads` threads of the CTA (id 1)
 __device__ __forceinline__ void named_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");

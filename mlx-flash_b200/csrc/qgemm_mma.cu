@@ -1,0 +1,457 @@
+// (c) grouped dequant GEMM for decode-sized expert tiles: warp-level tensor-core
+// MMA (mma.sync m16n8k16, bf16 in, fp32 accumulate) on 4-bit codes unpacked in
+// registers.  Same contract as b2f_gather_qgemm_affine_tcgen05
+// (mx.gather_qmm, expert_streaming.py:230-241, with the SwitchGLU front half of
+// kernels/ops.py:48-108 fused when w_up is given).
+//
+// Why this path exists next to the tcgen05 kernels: at decode a routed expert
+// sees a handful of tokens (typically 1-16).  tcgen05.mma costs a fixed ~55
+// cycles per M=128,K=16 instruction for every N <= 64 on B200 (measured), at
+// most ~37 weights per cycle per SM against the ~44 weights per cycle per SM at
+// which 4-bit weights stream from HBM, and its operands pass through shared
+// memory as dequantized bf16.  mma.sync measures 554 TFLOP/s (bf16) on B200;
+// with 16 weight rows as its M side and up to 8 tokens as its N side, each code
+// is read once from shared memory and consumed from registers.
+//
+// Arithmetic (the order MLX's own quantized kernels use): per 64-wide group g
+//   y[t, n] += s[n,g] * sum_k q[n,k] x[t,k] + b[n,g] * sum_k x[t,k]
+// The codes enter the MMA as the exact bf16 values 128+q (one lop3 per pair),
+// so the group sum is T = sum (128+q) x and y += s*T + (b - 128 s)*X with
+// X = sum x, itself one MMA against an all-ones operand; everything after the
+// bf16 products is fp32.
+//
+// CTA = 4 consumer warps + 1 producer warp.  Per 128-wide K chunk the producer
+// TMA-loads the CTA's weight rows (64 bytes of codes per row, 64B-swizzled) and
+// bulk-copies the slot's token rows (256 bytes each, stored 320 bytes apart so
+// the consumers' 16-byte reads hit distinct banks) into a ring of S stages.
+// Each consumer warp owns 64 weight rows (gate/up: 32 rows of each matrix).
+//
+// K mapping inside a chunk: lane (r = lane/4, c = lane%4), code word j (0..3)
+// of a row covers k in [8c + 32j, 8c + 32j + 8); nibble i is k + i (MLX's
+// LSB-first order).  MMA k-step 2j takes the nibble pairs (0,4) and (1,5) of
+// word j, k-step 2j+1 the pairs (2,6) and (3,7), and the token fragments the
+// same pairs; words 0-1 are group 2h of chunk h, words 2-3 group 2h+1.
+#include "common.cuh"
+#include "tc_common.cuh"
+
+namespace b2f {
+
+constexpr int MMA_CW = 4;         // consumer warps per CTA
+constexpr int MMA_XSTRIDE = 320;  // bytes between token rows of a staged x chunk
+constexpr int MMA_TOK = 16;       // tokens per plan slot (two 8-token MMA n-tiles)
+#ifndef B2F_MMA_WROWS
+#define B2F_MMA_WROWS 64
+#endif
+constexpr int MMA_WROWS = B2F_MMA_WROWS;  // weight rows per consumer warp
+#ifndef B2F_MMA_CTAS_PER_SM
+#define B2F_MMA_CTAS_PER_SM 3
+#endif
+constexpr int MMA_CTAS_PER_SM = B2F_MMA_CTAS_PER_SM;  // resident CTAs per SM the registers are sized for
+
+struct MmaParams {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  const int32_t* x_row_index;
+  int64_t x_row_div;
+  const __nv_bfloat16* s[2];
+  const __nv_bfloat16* b[2];
+  int64_t N, K;
+  int G;  // quantization groups per row (K / 64)
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int out_plan;  // 1: output rows in plan order, columns permuted (0,4,1,5,2,6,3,7) per 8
+  const int32_t* slot_count;
+  const int4* slots;
+  const int32_t* sorted;
+  int32_t* err;
+  int stages;
+};
+
+__device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(0.f));
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// The consumer side of one CTA for slots of up to 8*NTA tokens.
+//   MAT 2: rows [wr0, wr0+32) of gate and of up (SwiGLU epilogue); MAT 1: rows
+//   [wr0, wr0+64) of one matrix.  MT = row tiles of 16 per matrix.
+template <int MAT, int NTA, bool XPLAN>
+__device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
+                                            uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
+                                            int begin, int cnt, int64_t row_base, int HC, int warp, int lane) {
+  constexpr int MT = MMA_WROWS / 16 / MAT;
+  const int S = p.stages;
+  const int r = lane >> 2, c = lane & 3;
+  const int sw = (r >> 1) & 3;  // 64B swizzle phase of this lane's rows (r and r+8 share it)
+  const int wr0 = warp * (MMA_WROWS / MAT);
+  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+
+  float acc[MAT][MT][NTA][4];
+#pragma unroll
+  for (int m = 0; m < MAT; ++m)
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int nt = 0; nt < NTA; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[m][i][nt][e] = 0.f;
+
+  // (s, b) pairs of both groups of a chunk for rows R and R+8 of each tile
+  uint32_t sr[MAT][MT][2], br[MAT][MT][2];
+  const int64_t srow0 = int64_t(expert) * p.N + row_base + wr0 + r;
+  auto load_sb = [&](int h) {
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const bool rv = row_base + wr0 + 16 * i + 8 * hf + r < p.N;
+        const int64_t o = (srow0 + 16 * i + 8 * hf) * p.G + 2 * h;
+#pragma unroll
+        for (int m = 0; m < MAT; ++m) {
+          const __nv_bfloat16* sp = m == 0 ? p.s[0] : p.s[1];
+          const __nv_bfloat16* bp = m == 0 ? p.b[0] : p.b[1];
+          sr[m][i][hf] = rv ? *reinterpret_cast<const uint32_t*>(sp + o) : 0u;
+          br[m][i][hf] = rv ? *reinterpret_cast<const uint32_t*>(bp + o) : 0u;
+        }
+      }
+  };
+  load_sb(0);
+
+  int s = 0;
+  uint32_t phase = 0;
+  for (int h = 0; h < HC; ++h) {
+    const bool ok = !*abort_flag && mbar_wait_bounded(&full[s], phase);
+    if (!__all_sync(0xffffffffu, ok)) {
+      if (lane == 0) *abort_flag = 1;
+      break;
+    }
+    const uint8_t* wst = smem + s * STAGE;
+    const uint8_t* xst = wst + W_BYTES;
+#pragma unroll
+    for (int grp = 0; grp < 2; ++grp) {
+      float t[MAT][MT][NTA][4];  // sum over the group of (128+q) x
+      float xs[NTA][4];          // sum over the group of x (rows all equal)
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * grp + jj;
+        // token fragments: token 8nt + r, pairs (0,4) (1,5) | (2,6) (3,7)
+        uint32_t bx[NTA][2][2];
+#pragma unroll
+        for (int nt = 0; nt < NTA; ++nt) {
+          const uint4 u = *reinterpret_cast<const uint4*>(xst + (8 * nt + r) * MMA_XSTRIDE + 16 * c + 64 * j);
+          if constexpr (XPLAN) {  // stored as (0,4,1,5,2,6,3,7): the pairs already
+            bx[nt][0][0] = u.x;
+            bx[nt][0][1] = u.y;
+            bx[nt][1][0] = u.z;
+            bx[nt][1][1] = u.w;
+          } else {
+            bx[nt][0][0] = prmt(u.x, u.z, 0x5410u);
+            bx[nt][0][1] = prmt(u.x, u.z, 0x7632u);
+            bx[nt][1][0] = prmt(u.y, u.w, 0x5410u);
+            bx[nt][1][1] = prmt(u.y, u.w, 0x7632u);
+          }
+          if (jj == 0) {
+            mma_bf16_16816_zero(xs[nt], ones, bx[nt][0]);
+          } else {
+            mma_bf16_16816(xs[nt], ones, bx[nt][0]);
+          }
+          mma_bf16_16816(xs[nt], ones, bx[nt][1]);
+        }
+#pragma unroll
+        for (int m = 0; m < MAT; ++m) {
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            const uint8_t* rowp = wst + m * CTA_ROWS * 64 + (wr0 + 16 * i + r) * 64 + 16 * (j ^ sw) + 4 * c;
+            const uint32_t wl = *reinterpret_cast<const uint32_t*>(rowp);
+            const uint32_t wh = *reinterpret_cast<const uint32_t*>(rowp + 8 * 64);
+            const uint32_t a0[4] = {and_or(wl, 0x000F000Fu, 0x43004300u), and_or(wh, 0x000F000Fu, 0x43004300u),
+                                    and_or(wl >> 4, 0x000F000Fu, 0x43004300u),
+                                    and_or(wh >> 4, 0x000F000Fu, 0x43004300u)};
+            const uint32_t a1[4] = {and_or(wl >> 8, 0x000F000Fu, 0x43004300u),
+                                    and_or(wh >> 8, 0x000F000Fu, 0x43004300u),
+                                    and_or(wl >> 12, 0x000F000Fu, 0x43004300u),
+                                    and_or(wh >> 12, 0x000F000Fu, 0x43004300u)};
+#pragma unroll
+            for (int nt = 0; nt < NTA; ++nt) {
+              if (jj == 0) {
+                mma_bf16_16816_zero(t[m][i][nt], a0, bx[nt][0]);
+              } else {
+                mma_bf16_16816(t[m][i][nt], a0, bx[nt][0]);
+              }
+              mma_bf16_16816(t[m][i][nt], a1, bx[nt][1]);
+            }
+          }
+        }
+      }
+      // fold the group: y += s*T + (b - 128 s)*X   (rows R: e 0,1; R+8: e 2,3)
+#pragma unroll
+      for (int m = 0; m < MAT; ++m)
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          const float s0 = grp ? bf_hi(sr[m][i][0]) : bf_lo(sr[m][i][0]);
+          const float s1 = grp ? bf_hi(sr[m][i][1]) : bf_lo(sr[m][i][1]);
+          const float c0 = fmaf(-128.f, s0, grp ? bf_hi(br[m][i][0]) : bf_lo(br[m][i][0]));
+          const float c1 = fmaf(-128.f, s1, grp ? bf_hi(br[m][i][1]) : bf_lo(br[m][i][1]));
+#pragma unroll
+          for (int nt = 0; nt < NTA; ++nt) {
+            acc[m][i][nt][0] = fmaf(s0, t[m][i][nt][0], fmaf(c0, xs[nt][0], acc[m][i][nt][0]));
+            acc[m][i][nt][1] = fmaf(s0, t[m][i][nt][1], fmaf(c0, xs[nt][1], acc[m][i][nt][1]));
+            acc[m][i][nt][2] = fmaf(s1, t[m][i][nt][2], fmaf(c1, xs[nt][0], acc[m][i][nt][2]));
+            acc[m][i][nt][3] = fmaf(s1, t[m][i][nt][3], fmaf(c1, xs[nt][1], acc[m][i][nt][3]));
+          }
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (h + 1 < HC) load_sb(h + 1);
+    if (++s == S) {
+      s = 0;
+      phase ^= 1u;
+    }
+  }
+  if (*abort_flag) return;
+
+  // ---- epilogue: values (row R or R+8, tokens 2c and 2c+1) -> bf16 rows ------
+#pragma unroll
+  for (int nt = 0; nt < NTA; ++nt) {
+    const int t0 = 8 * nt + 2 * c;
+    int64_t orow0 = 0, orow1 = 0;
+    if (t0 < cnt) orow0 = p.out_plan ? int64_t(begin + t0) : int64_t(p.sorted[begin + t0]);
+    if (t0 + 1 < cnt) orow1 = p.out_plan ? int64_t(begin + t0 + 1) : int64_t(p.sorted[begin + t0 + 1]);
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float v0 = acc[0][i][nt][2 * hf], v1 = acc[0][i][nt][2 * hf + 1];
+        if constexpr (MAT == 2) {
+          v0 = silu_mul_tc(v0, acc[1][i][nt][2 * hf]);
+          v1 = silu_mul_tc(v1, acc[1][i][nt][2 * hf + 1]);
+        }
+        const int64_t row8 = row_base + wr0 + 16 * i + 8 * hf;  // first row of this lane's 8-row group
+        if (!p.out_plan) {
+          // lanes r and r^1 trade so each holds two adjacent rows of one token
+          const float recv = __shfl_xor_sync(0xffffffffu, (r & 1) ? v0 : v1, 4);
+          const bool odd = r & 1;
+          const int tok = odd ? t0 + 1 : t0;
+          const int64_t col = row8 + (r & ~1);
+          if (tok < cnt && col < p.N)
+            *reinterpret_cast<uint32_t*>(p.out + (odd ? orow1 : orow0) * p.ldo + col) =
+                odd ? pack_bf16x2(recv, v1) : pack_bf16x2(v0, recv);
+        } else {
+          // (0,4,1,5,2,6,3,7) order: lanes r and r^4 trade, positions 2(r&3), 2(r&3)+1
+          const bool up = r >= 4;
+          const float recv = __shfl_xor_sync(0xffffffffu, up ? v0 : v1, 16);
+          const int tok = up ? t0 + 1 : t0;
+          if (tok < cnt && row8 < p.N)
+            *reinterpret_cast<uint32_t*>(p.out + (up ? orow1 : orow0) * p.ldo + row8 + 2 * (r & 3)) =
+                up ? pack_bf16x2(recv, v1) : pack_bf16x2(v0, recv);
+        }
+      }
+  }
+}
+
+template <int MAT, bool XPLAN>
+__global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
+                                                         const __grid_constant__ CUtensorMap tm1) {
+  constexpr int CTA_ROWS = MMA_CW * MMA_WROWS / MAT;  // weight rows per matrix
+  constexpr int W_BYTES = MAT * CTA_ROWS * 64;
+  constexpr int STAGE = W_BYTES + MMA_TOK * MMA_XSTRIDE;
+  static_assert(STAGE % 1024 == 0, "ring stages must stay 1024-byte aligned for the swizzled TMA tiles");
+
+  extern __shared__ __align__(1024) uint8_t mma_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mma_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+
+  if (int(blockIdx.y) >= *p.slot_count) return;
+  const int4 sl = p.slots[blockIdx.y];
+  const int expert = sl.x, begin = sl.y, cnt = min(sl.z, MMA_TOK);
+  const int64_t row_base = int64_t(blockIdx.x) * CTA_ROWS;
+  if (row_base >= p.N || cnt <= 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int HC = int(p.K >> 7);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], MMA_CW);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  if (warp == MMA_CW) {
+    // ---- producer: weight tiles by TMA, one token row per lane by bulk copy ----
+    const __nv_bfloat16* xrow = nullptr;
+    if (lane < cnt) {
+      const int pos = begin + lane;
+      int64_t row;
+      if constexpr (XPLAN) {
+        row = pos;
+      } else {
+        const int a = p.sorted[pos];
+        row = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
+      }
+      xrow = p.x + row * p.ldx;
+    }
+    const int wrow = int(int64_t(expert) * p.N + row_base);
+    int h = 0, s = 0;
+    uint32_t phase = 0;
+    for (; h < HC; ++h) {
+      int ok = 1;
+      if (lane == 0) {
+        if (h >= S && !mbar_wait_bounded_backoff(&empty[s], phase ^ 1u)) ok = 0;
+        if (*abort_flag) ok = 0;
+        if (ok) {
+          mbar_arrive_expect_tx(&full[s], uint32_t(W_BYTES + cnt * 256));
+        } else {
+          *abort_flag = 1;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      uint8_t* st = smem + s * STAGE;
+      if (lane == 0) {
+        tma_load_2d(st, &tm0, h * 16, wrow, &full[s]);
+        if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * 64, &tm1, h * 16, wrow, &full[s]);
+      }
+      if (lane < cnt) bulk_g2s(st + W_BYTES + lane * MMA_XSTRIDE, xrow + int64_t(h) * 128, 256u, &full[s]);
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
+    }
+    // copies already issued land before the CTA goes away
+    if (lane == 0)
+      for (int k = 1; k <= S && h - k >= 0; ++k)
+        mbar_wait_bounded(&full[(h - k) % S], uint32_t(((h - k) / S) & 1), 100000000ull);
+    return;
+  }
+
+  if (cnt <= 8) {
+    mma_consume<MAT, 1, XPLAN>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert, begin, cnt,
+                               row_base, HC, warp, lane);
+  } else {
+    mma_consume<MAT, 2, XPLAN>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert, begin, cnt,
+                               row_base, HC, warp, lane);
+  }
+  if (lane == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+}
+
+// 4-bit code rows as a 2-D uint32 tensor [rows, K/8]; box = one 128-wide K
+// chunk (16 words = 64 bytes) of `box_rows` rows, 64B-swizzled.
+static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int box_rows) {
+  const cuuint64_t words = cuuint64_t(K / 8);
+  const cuuint64_t dims[2] = {words, cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {words * 4};
+  const cuuint32_t box[2] = {16u, cuuint32_t(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
+}
+
+template <int MAT, bool XPLAN>
+static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, int64_t E, int64_t slots_grid,
+                          cudaStream_t st) {
+  constexpr int CTA_ROWS = MMA_CW * MMA_WROWS / MAT;
+  constexpr int STAGE = MAT * CTA_ROWS * 64 + MMA_TOK * MMA_XSTRIDE;
+  // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
+  // of it reserved per CTA)
+  int S = 8;
+  while (S > 2 && MMA_CTAS_PER_SM * (S * STAGE + 1024 + 256 + 1024) > 228 * 1024) --S;
+  p.stages = S;
+  const int smem = S * STAGE + 1024 + 256;
+  CUtensorMap m0{}, m1{};
+  int rc = make_mma_weight_map(&m0, w0, E * p.N, p.K, CTA_ROWS);
+  if (rc != B2F_OK) return rc;
+  if (w1) {
+    rc = make_mma_weight_map(&m1, w1, E * p.N, p.K, CTA_ROWS);
+    if (rc != B2F_OK) return rc;
+  } else {
+    m1 = m0;
+  }
+  auto kern = qgemm_mma_kernel<MAT, XPLAN>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  const dim3 grid{unsigned((p.N + CTA_ROWS - 1) / CTA_ROWS), unsigned(slots_grid), 1u};
+  kern<<<grid, 160, smem, st>>>(p, m0, m1);
+  return check_launch();
+}
+
+// plan layout helpers live in qgemv.cu
+int64_t plan_slots_offset(int64_t A, int64_t E, int tile);
+int64_t plan_sorted_offset(int64_t A, int64_t E, int tile);
+
+}  // namespace b2f
+
+using namespace b2f;
+
+extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                           int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
+                                           const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                           const uint32_t* w_up, const void* s_up, const void* b_up, int64_t N,
+                                           int64_t K, int bits, int group_size, int tile, void* plan_workspace,
+                                           int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                           int out_plan_order, void* stream) {
+  if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
+  if (tile != MMA_TOK) return B2F_ERR_UNSUPPORTED;
+  if (A < 0 || E <= 0) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x || !w_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
+  if (w_up && (!s_up || !b_up)) return B2F_ERR_INVALID;
+  if (!x_plan_order && !x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
+  if (ldx < K || ldo < N) return B2F_ERR_INVALID;
+  if (E * N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w_gate, 16) || (w_up && !aligned(w_up, 16)) || !aligned(out, 4) ||
+      ldo % 2 != 0 || !aligned(s_gate, 4) || !aligned(b_gate, 4) || (w_up && (!aligned(s_up, 4) || !aligned(b_up, 4))))
+    return B2F_ERR_ALIGN;
+  const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
+  if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
+  const int64_t max_slots = b2f_moe_plan_max_slots(A, E, tile);
+  if (max_slots > 65535) return B2F_ERR_UNSUPPORTED;
+  int rc = get_encoder();
+  if (rc != B2F_OK) return rc;
+  char* ws = static_cast<char*>(plan_workspace);
+  MmaParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.x_row_index = x_row_index;
+  p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
+  p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
+  p.s[1] = static_cast<const __nv_bfloat16*>(s_up);
+  p.b[1] = static_cast<const __nv_bfloat16*>(b_up);
+  p.N = N;
+  p.K = K;
+  p.G = int(K / 64);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.out_plan = out_plan_order ? 1 : 0;
+  p.slot_count = reinterpret_cast<const int32_t*>(ws);
+  p.err = reinterpret_cast<int32_t*>(ws) + 1;  // the plan header's status word
+  p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
+  p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
+  cudaStream_t st = as_stream(stream);
+  const bool xp = x_plan_order != 0;
+  if (w_up) {
+    return xp ? launch_mma_cfg<2, true>(p, w_gate, w_up, E, max_slots, st)
+              : launch_mma_cfg<2, false>(p, w_gate, w_up, E, max_slots, st);
+  }
+  return xp ? launch_mma_cfg<1, true>(p, w_gate, nullptr, E, max_slots, st)
+            : launch_mma_cfg<1, false>(p, w_gate, nullptr, E, max_slots, st);
+}

@@ -68,6 +68,8 @@ def _emulate(dev, W, T, E, k, H, I, bits, engine, seed):
     (4, 16, 32, 8, 512, 256, 4, "tc"),
     (2, 12, 8, 2, 256, 192, 8, "tc"),
     (8, 4, 16, 8, 256, 128, 4, "gemv"),
+    (4, 16, 32, 8, 512, 256, 4, "mma"),
+    (3, 7, 16, 4, 256, 128, 4, "mma"),
 ])
 def test_ep_block_matches_oracle(dev, W, T, E, k, H, I, bits, engine):
     ranks, shards, xs, wr, (g, u, d), total = _emulate(dev, W, T, E, k, H, I, bits, engine, seed=W * 100 + T)

@@ -1,0 +1,96 @@
+"""GPU parity: the register-dequant warp-MMA grouped GEMM (decode-sized expert
+tiles) vs the oracle, and its plan-order chaining (gate/up output consumed by
+the down projection without a gather)."""
+
+import numpy as np
+import pytest
+import torch
+
+from b200flash import mx_compat
+from oracle import affine, moe
+from oracle.fp import round_to
+
+from helpers import assert_close, to_dev, to_np, u32_to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _w(rng, shape, bits=4):
+    w = round_to(rng.normal(0, 0.02, shape).astype(np.float32), "bf16")
+    return affine.quantize(w, 64, bits)
+
+
+def _dev3(t, dev):
+    wq, s, b = t
+    return u32_to_dev(wq, dev), to_dev(s, "bf16", dev), to_dev(b, "bf16", dev)
+
+
+def _routing(rng, T, k, E):
+    p = np.arange(1, E + 1) ** -1.1
+    p /= p.sum()
+    return np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+
+
+@pytest.mark.parametrize("T,k,E,H,I", [(64, 8, 128, 2048, 768), (64, 8, 32, 2048, 768), (7, 2, 4, 640, 384),
+                                       (512, 8, 128, 2048, 768), (33, 4, 16, 1024, 512), (3, 1, 4, 256, 128)])
+def test_mma_swiglu_then_down(dev, T, k, E, H, I):
+    """SwitchGLU front half then down projection (Qwen3-MoE expert shapes and
+    ragged ones: H = 640 leaves a partial CTA and idle warps in the down GEMM;
+    512 tokens put up to ~200 tokens on one expert, i.e. many slots; slots of
+    1-8 tokens take the one-n-tile path, 9-16 the two-n-tile path)."""
+    rng = np.random.default_rng(T * 3 + E + H)
+    tile = 16
+    g, u, d = _w(rng, (E, I, H)), _w(rng, (E, I, H)), _w(rng, (E, H, I))
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    inds = _routing(rng, T, k, E)
+    plan = mx_compat.MoEPlan(torch.from_numpy(inds.reshape(-1)).to(dev), E, tile)
+    h = mx_compat.gather_qmm_mma_planned(to_dev(x, "bf16", dev), plan, *_dev3(g, dev), 64, 4, x_row_div=k,
+                                         up=_dev3(u, dev))
+    y = mx_compat.gather_qmm_mma_planned(h, plan, *_dev3(d, dev), 64, 4, x_row_div=1)
+    plan.check()
+    _, hw, _ = moe.expert_mlp(x, inds, np.ones_like(inds, np.float64), g, u, d)
+    assert_close(to_np(h), hw.reshape(T * k, I), what="mma swiglu")
+    hh = to_np(h).astype(np.float64)
+    want = np.zeros((T * k, H))
+    for a in range(T * k):
+        e = inds.reshape(-1)[a]
+        want[a] = affine.dequantize_f32(d[0][e], d[1][e], d[2][e], 64, 4).astype(np.float64) @ hh[a]
+    assert_close(to_np(y), want, what="mma down")
+
+
+def test_mma_plan_order_chain_is_exact(dev):
+    """gate/up written in plan order with permuted columns equals the gathered,
+    permuted natural-order output bit for bit, and the down projection reading
+    it gives bit-identical rows to the natural-order chain."""
+    rng = np.random.default_rng(11)
+    T, k, E, H, I, tile = 64, 8, 64, 1024, 768, 16
+    g, u, d = _w(rng, (E, I, H)), _w(rng, (E, I, H)), _w(rng, (E, H, I))
+    x = to_dev(round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16"), "bf16", dev)
+    inds = _routing(rng, T, k, E)
+    plan = mx_compat.MoEPlan(torch.from_numpy(inds.reshape(-1)).to(dev), E, tile)
+    gu = dict(up=_dev3(u, dev))
+    h_nat = mx_compat.gather_qmm_mma_planned(x, plan, *_dev3(g, dev), 64, 4, x_row_div=k, **gu)
+    h_pln = mx_compat.gather_qmm_mma_planned(x, plan, *_dev3(g, dev), 64, 4, x_row_div=k, out_plan_order=True, **gu)
+    gathered = mx_compat.moe_gather_rows(h_nat, plan, x_row_div=1)
+    assert torch.equal(h_pln.view(torch.int16), gathered.view(torch.int16))
+    y_nat = mx_compat.gather_qmm_mma_planned(h_nat, plan, *_dev3(d, dev), 64, 4, x_row_div=1)
+    y_pln = mx_compat.gather_qmm_mma_planned(h_pln, plan, *_dev3(d, dev), 64, 4, x_plan_order=True)
+    assert torch.equal(y_nat.view(torch.int16), y_pln.view(torch.int16))
+
+
+def test_mma_single_matrix_with_row_index(dev):
+    """Plain gather_qmm (no fused up) with an explicit x_row_index, vs the oracle."""
+    rng = np.random.default_rng(5)
+    A, E, N, K, R = 300, 24, 1000, 1280, 90
+    w = _w(rng, (E, N, K))
+    x = round_to(rng.standard_normal((R, K)).astype(np.float32), "bf16")
+    xrow = rng.integers(0, R, A).astype(np.int32)
+    eid = rng.integers(0, E, A).astype(np.int32)
+    plan = mx_compat.MoEPlan(torch.from_numpy(eid).to(dev), E, 16)
+    y = mx_compat.gather_qmm_mma_planned(to_dev(x, "bf16", dev), plan, *_dev3(w, dev), 64, 4,
+                                         x_row_index=torch.from_numpy(xrow).to(dev))
+    want = np.zeros((A, N))
+    deq = [affine.dequantize_f32(w[0][e], w[1][e], w[2][e], 64, 4).astype(np.float64) for e in range(E)]
+    for a in range(A):
+        want[a] = deq[eid[a]] @ x[xrow[a]].astype(np.float64)
+    assert_close(to_np(y), want, what="mma gather_qmm")
