@@ -127,8 +127,11 @@ def profile_kernels(dec, torch):
 
     def timed_call(name, *args):
         tag = None
-        if name in ("b2f_gather_qgemv_affine", "b2f_gather_qgemm_affine_tcgen05", "b2f_sorted_qgemm_affine_tcgen05",
-                    "b2f_gather_qgemm_affine_mma"):
+        if name == "b2f_gather_qgemm_affine_mma" and args[6] == 1:
+            # one-expert plan: the dense q/k/v (or o) projection of the batch
+            tag = "qkv_proj" if args[13] == dec.qkv_rows else None
+        elif name in ("b2f_gather_qgemv_affine", "b2f_gather_qgemm_affine_tcgen05", "b2f_sorted_qgemm_affine_tcgen05",
+                      "b2f_gather_qgemm_affine_mma"):
             tag = "moe_gate_up" if state["gather"] % 2 == 0 else "moe_down"
             state["gather"] += 1
         elif name == "b2f_qkv_decode_attn":
@@ -219,7 +222,8 @@ def run_ours(args):
     # router and lm_head data-parallel over each rank's own batch
     exchange = EPExchange() if world > 1 else None
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
-                          seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine)
+                          seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
+                          dense_engine=args.dense_engine)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -456,6 +460,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--moe-engine", default="auto", choices=["auto", "mma", "tc_gather", "tc", "gemv"],
                     help="routed-expert GEMM engine (auto: the decoder's choice for this batch)")
+    ap.add_argument("--dense-engine", default="auto", choices=["auto", "mma", "tc", "gemv"],
+                    help="q/k/v and o projection engine (auto: the decoder's choice for this batch)")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")
     ap.add_argument("--profile-window", action="store_true",

@@ -267,7 +267,9 @@ int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, cons
  * registers and fed to warp-level tensor-core MMA (mma.sync m16n8k16 bf16,
  * 16 weight rows x 8 tokens), each 64-wide group folded as
  * s*sum(q x) + b*sum(x) in fp32 (the order MLX's quantized kernels use).
- * Plan from b2f_moe_plan / b2f_moe_route_plan / b2f_ep_plan with tile = 16;
+ * Plan from b2f_moe_plan / b2f_moe_route_plan / b2f_ep_plan with tile = 16
+ * (expert tiles), or tile = 64 without w_up (wide tiles: a dense projection
+ * of up to 64 decode tokens is b2f_moe_plan over all-zero expert ids, E = 1);
  * same weight format as b2f_gather_qgemm_affine_tcgen05; bits 4,
  * group_size 64, K % 128 == 0, N % 8 == 0.
  * x_plan_order = 0: x row of assignment a is x_row_index[a] (or a/x_row_div),

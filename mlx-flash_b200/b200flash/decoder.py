@@ -217,12 +217,25 @@ class Qwen3MoeDecoder:
         self.attn_ws_bytes = wsb
         self.softmax_scale = 1.0 / math.sqrt(D)
         # dense projections: register GEMV for a few tokens, tcgen05 (split-K
-        # where the matrix has few 128-row blocks) for larger batches
+        # where the matrix has few 128-row blocks) for larger batches.  The
+        # warp-MMA path ("mma": the batch as one 64-token tile) is selectable;
+        # without split-K its few row blocks leave most SMs idle at decode.
+        mma_dense = bits == 4 and gs == 64 and H % 128 == 0 and (Hq * D) % 128 == 0 and B <= 64
         if dense_engine == "auto":
             dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
-        if dense_engine not in ("tc", "gemv"):
+        if dense_engine not in ("tc", "gemv", "mma"):
             raise ValueError(f"unknown dense engine {dense_engine!r}")
+        if dense_engine == "mma" and not mma_dense:
+            dense_engine = "tc" if s.group_size == 64 else "gemv"
         self.dense_engine = dense_engine
+        if dense_engine == "mma":
+            # the batch as slots of one "expert" (a plan over all-zero expert ids)
+            self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 64))
+            self.dplan_ws = torch.empty(self.dplan_bytes, dtype=torch.uint8, device=dev)
+            zeros = torch.zeros(B, dtype=torch.int32, device=dev)
+            call("b2f_moe_plan", ptr(zeros), B, 1, 64, ptr(self.dplan_ws), self.dplan_bytes, 0,
+                 _capi.stream_of(dev))
+            self.oy = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
         self.dense_tile = min(256, max(16, (B + 15) // 16 * 16))
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
@@ -292,7 +305,10 @@ class Qwen3MoeDecoder:
                      ptr(kv["kc"]), ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table),
                      self.max_pages, self.page, s.kv_bits, st)
             else:
-                self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
+                if self.dense_engine == "mma":
+                    self._mma(self.xn, H, w, self.qkv, st)
+                else:
+                    self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
                 call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]),
                      ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]),
                      ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page,
@@ -306,6 +322,11 @@ class Qwen3MoeDecoder:
                 self._partials(self.attn, Hq * D, w, self.ks_o, st)
                 call("b2f_combine_rmsnorm_partials", ptr(self.h), ptr(self.dense_ws), self.ks_o, B,
                      ptr(ly["post_norm"]), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
+            elif self.dense_engine == "mma":
+                # h += o_proj(attn) and the post-attention RMSNorm in one pass
+                self._mma(self.attn, Hq * D, w, self.oy, st)
+                call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.oy), 0, B, 1, ptr(ly["post_norm"]), s.rms_eps, H,
+                     ptr(self.h), ptr(self.xn), st)
             else:
                 self._dense(self.attn, Hq * D, w, self.h, self.h, self.ks_o, st)
                 call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
@@ -365,6 +386,12 @@ class Qwen3MoeDecoder:
             call("b2f_qgemm_affine_tcgen05_splitk", ptr(x), ldx, B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N, w.K,
                  w.bits, w.group_size, ptr(residual) if isinstance(residual, torch.Tensor) else 0, ptr(out), w.N,
                  self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
+
+    def _mma(self, x, ldx, w, out, st):
+        """out = x . W^T on warp MMA, the batch as one planned 64-token tile."""
+        call("b2f_gather_qgemm_affine_mma", ptr(x), ldx, 0, 1, 0, self.B, 1, ptr(w.wq), ptr(w.scales),
+             ptr(w.biases), 0, 0, 0, w.N, w.K, w.bits, w.group_size, 64, ptr(self.dplan_ws), self.dplan_bytes,
+             ptr(out), w.N, 0, st)
 
     def _partials(self, x, ldx, w, ksplit, st):
         """fp32 split-K partials of x . W^T into the dense workspace."""

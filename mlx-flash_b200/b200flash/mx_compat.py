@@ -183,8 +183,9 @@ def gather_qmm_tc_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bias
 def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size, bits,
                            x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None,
                            x_plan_order: bool = False, out_plan_order: bool = False) -> torch.Tensor:
-    """Grouped GEMM over a prepared plan (tile 16) on warp-level tensor-core MMA
-    with the 4-bit codes unpacked in registers (decode-sized expert tiles).
+    """Grouped GEMM over a prepared plan on warp-level tensor-core MMA with the
+    4-bit codes unpacked in registers: tile 16 for decode-sized expert tiles,
+    tile 64 (one matrix) for a dense projection of a whole decode batch.
 
     ``x_plan_order``: ``x_rows`` is in plan order with permuted columns (the
     ``moe_gather_rows`` layout, or this function's ``out_plan_order`` output).
@@ -193,8 +194,10 @@ def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bia
     dev = require_cuda(x_rows, w, scales, biases, x_row_index)
     E, N = w.shape[0], w.shape[1]
     K = w.shape[2] * 32 // bits
-    if bits != 4 or group_size != 64 or K % 128 or N % 8 or plan.tile != 16:
-        raise ValueError("the register-dequant MMA path needs 4-bit, group 64, K % 128 == 0, N % 8 == 0, tile 16")
+    if bits != 4 or group_size != 64 or K % 128 or N % 8 or plan.tile not in (16, 64):
+        raise ValueError("the register-unpack MMA path needs 4-bit, group 64, K % 128 == 0, N % 8 == 0, tile 16/64")
+    if plan.tile == 64 and up is not None:
+        raise ValueError("64-token tiles take one matrix (no fused up projection)")
     xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
     out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
     wu = su = bu = None

@@ -38,15 +38,23 @@ namespace b2f {
 
 constexpr int MMA_CW = 4;         // consumer warps per CTA
 constexpr int MMA_XSTRIDE = 320;  // bytes between token rows of a staged x chunk
-constexpr int MMA_TOK = 16;       // tokens per plan slot (two 8-token MMA n-tiles)
-#ifndef B2F_MMA_WROWS
-#define B2F_MMA_WROWS 64
-#endif
-constexpr int MMA_WROWS = B2F_MMA_WROWS;  // weight rows per consumer warp
-#ifndef B2F_MMA_CTAS_PER_SM
-#define B2F_MMA_CTAS_PER_SM 3
-#endif
-constexpr int MMA_CTAS_PER_SM = B2F_MMA_CTAS_PER_SM;  // resident CTAs per SM the registers are sized for
+
+// Two shapes of the same kernel:
+//   expert tiles (plan tile 16): slots of <= 16 tokens, 64 weight rows per
+//     warp, three CTAs per SM;
+//   wide tiles (plan tile 64, one matrix): slots of <= 64 tokens (a dense
+//     projection of a decode batch is one slot), 16 weight rows per warp so
+//     the rows spread over many CTAs, two CTAs per SM.
+template <int TILE>
+struct MmaShape;
+template <>
+struct MmaShape<16> {
+  static constexpr int NTMAX = 2, WROWS = 64, CTAS = 3;
+};
+template <>
+struct MmaShape<64> {
+  static constexpr int NTMAX = 8, WROWS = 16, CTAS = 2;
+};
 
 struct MmaParams {
   const __nv_bfloat16* x;
@@ -78,18 +86,19 @@ __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_
 __device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
-// The consumer side of one CTA for slots of up to 8*NTA tokens.
-//   MAT 2: rows [wr0, wr0+32) of gate and of up (SwiGLU epilogue); MAT 1: rows
-//   [wr0, wr0+64) of one matrix.  MT = row tiles of 16 per matrix.
-template <int MAT, int NTA, bool XPLAN>
+// The consumer side of one CTA for slots of up to 8*NTA tokens: the warp's
+// WROWS/MAT rows of each matrix (MAT 2: gate and up, SwiGLU epilogue), as
+// MT row tiles of 16.
+template <int MAT, int NTA, bool XPLAN, int WROWS>
 __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
                                             uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
                                             int begin, int cnt, int64_t row_base, int HC, int warp, int lane) {
-  constexpr int MT = MMA_WROWS / 16 / MAT;
+  constexpr int MT = WROWS / 16 / MAT;
+  static_assert(MT >= 1, "at least one 16-row tile per matrix");
   const int S = p.stages;
   const int r = lane >> 2, c = lane & 3;
   const int sw = (r >> 1) & 3;  // 64B swizzle phase of this lane's rows (r and r+8 share it)
-  const int wr0 = warp * (MMA_WROWS / MAT);
+  const int wr0 = warp * (WROWS / MAT);
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
   float acc[MAT][MT][NTA][4];
@@ -256,12 +265,14 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   }
 }
 
-template <int MAT, bool XPLAN>
-__global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
-                                                         const __grid_constant__ CUtensorMap tm1) {
-  constexpr int CTA_ROWS = MMA_CW * MMA_WROWS / MAT;  // weight rows per matrix
+template <int MAT, bool XPLAN, int TILE>
+__global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
+    qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
+                     const __grid_constant__ CUtensorMap tm1) {
+  using SH = MmaShape<TILE>;
+  constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;  // weight rows per matrix
   constexpr int W_BYTES = MAT * CTA_ROWS * 64;
-  constexpr int STAGE = W_BYTES + MMA_TOK * MMA_XSTRIDE;
+  constexpr int STAGE = W_BYTES + TILE * MMA_XSTRIDE;
   static_assert(STAGE % 1024 == 0, "ring stages must stay 1024-byte aligned for the swizzled TMA tiles");
 
   extern __shared__ __align__(1024) uint8_t mma_smem_raw[];
@@ -271,10 +282,15 @@ __global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const M
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
-  if (int(blockIdx.y) >= *p.slot_count) return;
-  const int4 sl = p.slots[blockIdx.y];
-  const int expert = sl.x, begin = sl.y, cnt = min(sl.z, MMA_TOK);
-  const int64_t row_base = int64_t(blockIdx.x) * CTA_ROWS;
+  // expert tiles: x = row block, y = slot (one expert's contiguous rows are
+  // streamed by consecutive CTAs); wide tiles: x = slot, y = row block (the
+  // slots reading one row block run back to back and share it through L2)
+  const int slot_id = TILE == 16 ? int(blockIdx.y) : int(blockIdx.x);
+  const int rblk = TILE == 16 ? int(blockIdx.x) : int(blockIdx.y);
+  if (slot_id >= *p.slot_count) return;
+  const int4 sl = p.slots[slot_id];
+  const int expert = sl.x, begin = sl.y, cnt = min(sl.z, TILE);
+  const int64_t row_base = int64_t(rblk) * CTA_ROWS;
   if (row_base >= p.N || cnt <= 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HC = int(p.K >> 7);
@@ -291,17 +307,23 @@ __global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const M
 
   if (warp == MMA_CW) {
     // ---- producer: weight tiles by TMA, one token row per lane by bulk copy ----
-    const __nv_bfloat16* xrow = nullptr;
-    if (lane < cnt) {
-      const int pos = begin + lane;
-      int64_t row;
-      if constexpr (XPLAN) {
-        row = pos;
-      } else {
-        const int a = p.sorted[pos];
-        row = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
+    constexpr int XPL = (TILE + 31) / 32;  // token rows per producer lane
+    const __nv_bfloat16* xrow[XPL];
+#pragma unroll
+    for (int u = 0; u < XPL; ++u) {
+      xrow[u] = nullptr;
+      const int tk = lane + 32 * u;
+      if (tk < cnt) {
+        const int pos = begin + tk;
+        int64_t row;
+        if constexpr (XPLAN) {
+          row = pos;
+        } else {
+          const int a = p.sorted[pos];
+          row = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
+        }
+        xrow[u] = p.x + row * p.ldx;
       }
-      xrow = p.x + row * p.ldx;
     }
     const int wrow = int(int64_t(expert) * p.N + row_base);
     int h = 0, s = 0;
@@ -324,7 +346,11 @@ __global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const M
         tma_load_2d(st, &tm0, h * 16, wrow, &full[s]);
         if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * 64, &tm1, h * 16, wrow, &full[s]);
       }
-      if (lane < cnt) bulk_g2s(st + W_BYTES + lane * MMA_XSTRIDE, xrow + int64_t(h) * 128, 256u, &full[s]);
+#pragma unroll
+      for (int u = 0; u < XPL; ++u) {
+        const int tk = lane + 32 * u;
+        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * MMA_XSTRIDE, xrow[u] + int64_t(h) * 128, 256u, &full[s]);
+      }
       if (++s == S) {
         s = 0;
         phase ^= 1u;
@@ -337,12 +363,17 @@ __global__ void __launch_bounds__(160, MMA_CTAS_PER_SM) qgemm_mma_kernel(const M
     return;
   }
 
-  if (cnt <= 8) {
-    mma_consume<MAT, 1, XPLAN>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert, begin, cnt,
-                               row_base, HC, warp, lane);
+  if constexpr (SH::NTMAX == 2) {
+    if (cnt <= 8) {
+      mma_consume<MAT, 1, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+                                            begin, cnt, row_base, HC, warp, lane);
+    } else {
+      mma_consume<MAT, 2, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+                                            begin, cnt, row_base, HC, warp, lane);
+    }
   } else {
-    mma_consume<MAT, 2, XPLAN>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert, begin, cnt,
-                               row_base, HC, warp, lane);
+    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
+                                                  expert, begin, cnt, row_base, HC, warp, lane);
   }
   if (lane == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
 }
@@ -361,15 +392,17 @@ static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows
   return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
 }
 
-template <int MAT, bool XPLAN>
+template <int MAT, bool XPLAN, int TILE>
 static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, int64_t E, int64_t slots_grid,
                           cudaStream_t st) {
-  constexpr int CTA_ROWS = MMA_CW * MMA_WROWS / MAT;
-  constexpr int STAGE = MAT * CTA_ROWS * 64 + MMA_TOK * MMA_XSTRIDE;
+  using SH = MmaShape<TILE>;
+  constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
+  constexpr int STAGE = MAT * CTA_ROWS * 64 + TILE * MMA_XSTRIDE;
+  static_assert(STAGE % 1024 == 0, "ring stages must stay 1024-byte aligned");
   // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
   // of it reserved per CTA)
   int S = 8;
-  while (S > 2 && MMA_CTAS_PER_SM * (S * STAGE + 1024 + 256 + 1024) > 228 * 1024) --S;
+  while (S > 2 && SH::CTAS * (S * STAGE + 1024 + 256 + 1024) > 228 * 1024) --S;
   p.stages = S;
   const int smem = S * STAGE + 1024 + 256;
   CUtensorMap m0{}, m1{};
@@ -381,13 +414,16 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   } else {
     m1 = m0;
   }
-  auto kern = qgemm_mma_kernel<MAT, XPLAN>;
+  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     return B2F_ERR_CUDA;
   }
-  const dim3 grid{unsigned((p.N + CTA_ROWS - 1) / CTA_ROWS), unsigned(slots_grid), 1u};
+  const int64_t row_blocks = (p.N + CTA_ROWS - 1) / CTA_ROWS;
+  if ((TILE == 16 ? slots_grid : row_blocks) > 65535) return B2F_ERR_UNSUPPORTED;
+  const dim3 grid = TILE == 16 ? dim3{unsigned(row_blocks), unsigned(slots_grid), 1u}
+                               : dim3{unsigned(slots_grid), unsigned(row_blocks), 1u};
   kern<<<grid, 160, smem, st>>>(p, m0, m1);
   return check_launch();
 }
@@ -409,7 +445,7 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
                                            int out_plan_order, void* stream) {
   if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
-  if (tile != MMA_TOK) return B2F_ERR_UNSUPPORTED;
+  if (!(tile == 16 || (tile == 64 && !w_up))) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0) return B2F_ERR_INVALID;
   if (A == 0) return B2F_OK;
   if (!x || !w_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
@@ -423,7 +459,7 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
   const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
   if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
   const int64_t max_slots = b2f_moe_plan_max_slots(A, E, tile);
-  if (max_slots > 65535) return B2F_ERR_UNSUPPORTED;
+  if (max_slots > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
   int rc = get_encoder();
   if (rc != B2F_OK) return rc;
   char* ws = static_cast<char*>(plan_workspace);
@@ -448,10 +484,13 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
   p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
   cudaStream_t st = as_stream(stream);
   const bool xp = x_plan_order != 0;
+  if (tile == 64)
+    return xp ? launch_mma_cfg<1, true, 64>(p, w_gate, nullptr, E, max_slots, st)
+              : launch_mma_cfg<1, false, 64>(p, w_gate, nullptr, E, max_slots, st);
   if (w_up) {
-    return xp ? launch_mma_cfg<2, true>(p, w_gate, w_up, E, max_slots, st)
-              : launch_mma_cfg<2, false>(p, w_gate, w_up, E, max_slots, st);
+    return xp ? launch_mma_cfg<2, true, 16>(p, w_gate, w_up, E, max_slots, st)
+              : launch_mma_cfg<2, false, 16>(p, w_gate, w_up, E, max_slots, st);
   }
-  return xp ? launch_mma_cfg<1, true>(p, w_gate, nullptr, E, max_slots, st)
-            : launch_mma_cfg<1, false>(p, w_gate, nullptr, E, max_slots, st);
+  return xp ? launch_mma_cfg<1, true, 16>(p, w_gate, nullptr, E, max_slots, st)
+            : launch_mma_cfg<1, false, 16>(p, w_gate, nullptr, E, max_slots, st);
 }

@@ -51,7 +51,8 @@ def _export_cache(dec, ctx):
                                                          (8, "tc", "gemv", 256), (8, "tc_gather", "tc", 256),
                                                          (8, "tc_gather", "tc", 1024), (4, "gemv", "tc", 1024),
                                                          (2, "tc_gather", "gemv", 256), (8, "mma", "gemv", 256),
-                                                         (4, "mma", "tc", 1024)])
+                                                         (4, "mma", "tc", 1024), (8, "mma", "mma", 256),
+                                                         (4, "mma", "mma", 1024)])
 def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
     """dense="tc" runs q/k/v and o through split-K partials summed inside the
     RoPE/KV-append and residual+RMSNorm kernels (K = 1024 splits both)."""

@@ -94,3 +94,17 @@ def test_mma_single_matrix_with_row_index(dev):
     for a in range(A):
         want[a] = deq[eid[a]] @ x[xrow[a]].astype(np.float64)
     assert_close(to_np(y), want, what="mma gather_qmm")
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 5120, 2048), (37, 1000, 1280), (100, 2048, 4096), (1, 256, 128)])
+def test_mma_wide_tile_dense_projection(dev, M, N, K):
+    """64-token tiles over a one-expert plan: mx.quantized_matmul of a decode
+    batch (q/k/v and o projections); M = 100 spans two slots, M = 37 leaves
+    ragged token rows, N = 1000 a partial row block."""
+    rng = np.random.default_rng(M + N)
+    w = _w(rng, (1, N, K))
+    x = round_to(rng.standard_normal((M, K)).astype(np.float32), "bf16")
+    plan = mx_compat.MoEPlan(torch.zeros(M, dtype=torch.int32, device=dev), 1, 64)
+    y = mx_compat.gather_qmm_mma_planned(to_dev(x, "bf16", dev), plan, *_dev3(w, dev), 64, 4, x_row_div=1)
+    want = x.astype(np.float64) @ affine.dequantize_f32(w[0][0], w[1][0], w[2][0], 64, 4).astype(np.float64).T
+    assert_close(to_np(y), want, what=f"mma dense M={M} N={N} K={K}")
