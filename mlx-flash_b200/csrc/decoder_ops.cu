@@ -123,6 +123,8 @@ struct RopeKvParams {
   int Hq, Hkv, PS, bits;
 };
 
+// grid (B, heads / 8): one warp per head of the token, so the (Hq + 2Hkv)
+// heads of a decode batch spread over many SMs instead of queuing on B CTAs.
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams p) {
   constexpr int D = 128;
   const int b = blockIdx.x;
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
     sincosf(float(pos) * inv, &rope_s[threadIdx.x], &rope_c[threadIdx.x]);
   }
   __syncthreads();
-  for (int h = warp; h < NH; h += nw) {
+  for (int h = blockIdx.y * nw + warp; h < min(NH, int(blockIdx.y + 1) * nw); h += nw) {
     float v[4];
     if (p.qkv_partial) {
       // the projection's bf16 output, formed here from its split-K partials
@@ -287,6 +289,87 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* 
     const float v = warp_sum<32>(acc[t]);
     if (lane == 0 && t < nt) logits[int64_t(t0 + t) * E + e] = v + (bias ? bias[e] : 0.f);
   }
+}
+
+// The same logits on warp-level tensor-core MMA (bf16 products, fp32 sums):
+// CTA = 16 tokens x 8 experts, its 8 warps each take 1/8 of H in 32-wide
+// chunks (lane (r, c) holds k in [8c, 8c+8) of a chunk, the nibble-free
+// version of the pair order the expert GEMM uses), and the 8 partial tiles
+// are summed in a fixed order through shared memory.  E % 8 == 0,
+// H % 256 == 0.
+__global__ void __launch_bounds__(256) route_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
+                                                               const __nv_bfloat16* __restrict__ wr,
+                                                               const float* __restrict__ bias, int E,
+                                                               float* __restrict__ logits) {
+  __shared__ float red[8][32][4];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = lane >> 2, c = lane & 3;
+  const int e0 = blockIdx.x * 8, t0 = blockIdx.y * 16;
+  const int kw = H / 8;  // K range of this warp
+  const int k0 = warp * kw;
+  const bool v0 = t0 + r < T, v1 = t0 + r + 8 < T;
+  const __nv_bfloat16* xr0 = x + int64_t(v0 ? t0 + r : 0) * H + k0 + 8 * c;
+  const __nv_bfloat16* xr1 = x + int64_t(v1 ? t0 + r + 8 : 0) * H + k0 + 8 * c;
+  const __nv_bfloat16* wrow = wr + int64_t(e0 + r) * H + k0 + 8 * c;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int U = 4;  // chunks in flight
+  for (int ch = 0; ch < kw / 32; ch += U) {
+    uint4 a0[U], a1[U], bw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool in = ch + u < kw / 32;
+      const int o = 32 * (ch + u);
+      a0[u] = (in && v0) ? *reinterpret_cast<const uint4*>(xr0 + o) : make_uint4(0u, 0u, 0u, 0u);
+      a1[u] = (in && v1) ? *reinterpret_cast<const uint4*>(xr1 + o) : make_uint4(0u, 0u, 0u, 0u);
+      bw[u] = in ? *reinterpret_cast<const uint4*>(wrow + o) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      // pairs (0,4) (1,5) | (2,6) (3,7) of the lane's 8 k values
+      const uint32_t aA[4] = {prmt(a0[u].x, a0[u].z, 0x5410u), prmt(a1[u].x, a1[u].z, 0x5410u),
+                              prmt(a0[u].x, a0[u].z, 0x7632u), prmt(a1[u].x, a1[u].z, 0x7632u)};
+      const uint32_t aB[4] = {prmt(a0[u].y, a0[u].w, 0x5410u), prmt(a1[u].y, a1[u].w, 0x5410u),
+                              prmt(a0[u].y, a0[u].w, 0x7632u), prmt(a1[u].y, a1[u].w, 0x7632u)};
+      const uint32_t bA[2] = {prmt(bw[u].x, bw[u].z, 0x5410u), prmt(bw[u].x, bw[u].z, 0x7632u)};
+      const uint32_t bB[2] = {prmt(bw[u].y, bw[u].w, 0x5410u), prmt(bw[u].y, bw[u].w, 0x7632u)};
+      mma_bf16_16816(acc, aA, bA);
+      mma_bf16_16816(acc, aB, bB);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][lane][i] = acc[i];
+  __syncthreads();
+  if (warp == 0) {
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < 8; ++w)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum[i] += red[w][lane][i];
+    // (token r / r+8, expert 2c / 2c+1)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = t0 + r + 8 * (i >> 1), e = e0 + 2 * c + (i & 1);
+      if (t < T) logits[int64_t(t) * E + e] = sum[i] + (bias ? bias[e] : 0.f);
+    }
+  }
+}
+
+static int launch_route_logits(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                               float* logits, cudaStream_t st) {
+  if (E % 8 == 0 && H % 256 == 0) {
+    const dim3 g{unsigned(E / 8), unsigned((T + 15) / 16), 1u};
+    route_logits_mma_kernel<<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+                                                static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits);
+    return check_launch();
+  }
+  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
+  const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+          cudaSuccess)
+    return check_launch();
+  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
+                                               static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits);
+  return check_launch();
 }
 
 // gates = softmax(logits[t]); top-k by value (ties -> lower id); scores are the
@@ -484,7 +567,8 @@ static int qk_norm_rope_impl(const void* qkv, const float* qkv_partial, int nspl
   p.Hkv = int(Hkv);
   p.PS = int(page_size);
   p.bits = bits;
-  qk_norm_rope_kv_kernel<<<unsigned(B), 256, 0, as_stream(stream)>>>(p);
+  const dim3 grid{unsigned(B), unsigned((Hq + 2 * Hkv + 7) / 8), 1u};
+  qk_norm_rope_kv_kernel<<<grid, 256, 0, as_stream(stream)>>>(p);
   return check_launch();
 }
 
@@ -561,15 +645,7 @@ int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, cons
   if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
   cudaStream_t st = as_stream(stream);
   if (H > 8192) return B2F_ERR_UNSUPPORTED;
-  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
-  const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
-          cudaSuccess)
-    return check_launch();
-  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-                                           static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits_ws);
-  int rc = check_launch();
+  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, st);
   if (rc != B2F_OK) return rc;
   route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds, scores);
   return check_launch();
@@ -588,15 +664,7 @@ int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, cons
   const PlanLayout L = plan_layout(T * k, E, tile);
   if (plan_workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
-  const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
-  const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
-          cudaSuccess)
-    return check_launch();
-  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-                                               static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits_ws);
-  int rc = check_launch();
+  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, st);
   if (rc != B2F_OK) return rc;
   char* ws = static_cast<char*>(plan_workspace);
   if (cudaMemsetAsync(reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2, 0, sizeof(int32_t), st) != cudaSuccess)
