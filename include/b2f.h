@@ -290,6 +290,23 @@ int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int32_t* x_row
                                 void* plan_workspace, int64_t plan_workspace_bytes, void* out,
                                 int64_t ldo, int out_plan_order, void* stream);
 
+/* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
+ * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes
+ * fp32 planes partial[z][a][0:N] for every planned assignment a, to be summed
+ * by the consumer (b2f_qk_norm_rope_kv_append_partials,
+ * b2f_combine_rmsnorm_partials).  A dense projection of B decode tokens is
+ * the plan of b2f_moe_plan over B all-zero expert ids with E = 1.  The plane
+ * count is b2f_mma_splitk_ranges(K, ksplit); partial 16-byte aligned, at
+ * least b2f_mma_splitk_workspace_bytes(A, N, K, ksplit) bytes. */
+int b2f_mma_splitk_ranges(int64_t K, int ksplit);
+int64_t b2f_mma_splitk_workspace_bytes(int64_t A, int64_t N, int64_t K, int ksplit);
+int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                         int64_t x_row_div, int64_t A, int64_t E, const uint32_t* w,
+                                         const void* scales, const void* biases, int64_t N, int64_t K,
+                                         int bits, int group_size, int tile, void* plan_workspace,
+                                         int64_t plan_workspace_bytes, int ksplit, float* partial,
+                                         int64_t partial_bytes, void* stream);
+
 /* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
 
 /* Copies the planned assignments' activation rows into plan order:

@@ -53,6 +53,10 @@ SIGNATURES = {
     "b2f_moe_route_plan": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P, _P, _I, _P, _I64, _P, _P]),
     "b2f_gather_qgemm_affine_mma": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64,
                                          _I, _I, _I, _P, _I64, _P, _I64, _I, _P]),
+    "b2f_mma_splitk_ranges": (_I, [_I64, _I]),
+    "b2f_mma_splitk_workspace_bytes": (_I64, [_I64, _I64, _I64, _I]),
+    "b2f_gather_qgemm_affine_mma_partials": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I,
+                                                  _I, _P, _I64, _I, _P, _I64, _P]),
     "b2f_moe_gather_rows": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _I64, _P]),
     "b2f_sorted_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I,
                                              _P, _I64, _P, _I64, _I, _P]),

@@ -217,10 +217,11 @@ class Qwen3MoeDecoder:
         self.attn_ws_bytes = wsb
         self.softmax_scale = 1.0 / math.sqrt(D)
         # dense projections: register GEMV for a few tokens, tcgen05 (split-K
-        # where the matrix has few 128-row blocks) for larger batches.  The
-        # warp-MMA path ("mma": the batch as one 64-token tile) is selectable;
-        # without split-K its few row blocks leave most SMs idle at decode.
-        mma_dense = bits == 4 and gs == 64 and H % 128 == 0 and (Hq * D) % 128 == 0 and B <= 64
+        # where the matrix has few 128-row blocks) for larger batches; "mma":
+        # the warp-MMA GEMM over the batch as 16-token slots of one expert,
+        # split-K into fp32 planes summed by the RoPE/KV-append and
+        # residual+RMSNorm kernels.
+        mma_dense = bits == 4 and gs == 64 and H % 128 == 0 and (Hq * D) % 128 == 0
         if dense_engine == "auto":
             dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
         if dense_engine not in ("tc", "gemv", "mma"):
@@ -230,12 +231,11 @@ class Qwen3MoeDecoder:
         self.dense_engine = dense_engine
         if dense_engine == "mma":
             # the batch as slots of one "expert" (a plan over all-zero expert ids)
-            self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 64))
+            self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 16))
             self.dplan_ws = torch.empty(self.dplan_bytes, dtype=torch.uint8, device=dev)
             zeros = torch.zeros(B, dtype=torch.int32, device=dev)
-            call("b2f_moe_plan", ptr(zeros), B, 1, 64, ptr(self.dplan_ws), self.dplan_bytes, 0,
+            call("b2f_moe_plan", ptr(zeros), B, 1, 16, ptr(self.dplan_ws), self.dplan_bytes, 0,
                  _capi.stream_of(dev))
-            self.oy = torch.empty(B, H, dtype=torch.bfloat16, device=dev)
         self.dense_tile = min(256, max(16, (B + 15) // 16 * 16))
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
@@ -247,11 +247,23 @@ class Qwen3MoeDecoder:
                 ks *= 2
             return ks
 
+        def mma_ksplit_for(N, K):
+            # about three CTAs per SM: 256-row blocks x 16-token slots x K ranges
+            ctas = ((N + 255) // 256) * ((B + 15) // 16)
+            return max(1, min(K // 256, (3 * sms + ctas - 1) // ctas))
+
         lib = _capi.lib()
         # K ranges actually used (every range non-empty); 1 = no split
-        self.ks_qkv = int(lib.b2f_qgemm_splitk_ranges(H, ksplit_for(self.qkv_rows, H)))
-        self.ks_o = int(lib.b2f_qgemm_splitk_ranges(Hq * D, ksplit_for(H, Hq * D)))
+        if dense_engine == "mma":
+            self.ks_qkv = int(lib.b2f_mma_splitk_ranges(H, mma_ksplit_for(self.qkv_rows, H)))
+            self.ks_o = int(lib.b2f_mma_splitk_ranges(Hq * D, mma_ksplit_for(H, Hq * D)))
+        else:
+            self.ks_qkv = int(lib.b2f_qgemm_splitk_ranges(H, ksplit_for(self.qkv_rows, H)))
+            self.ks_o = int(lib.b2f_qgemm_splitk_ranges(Hq * D, ksplit_for(H, Hq * D)))
         ws = 0
+        if dense_engine == "mma":
+            ws = max(int(lib.b2f_mma_splitk_workspace_bytes(B, self.qkv_rows, H, self.ks_qkv)),
+                     int(lib.b2f_mma_splitk_workspace_bytes(B, H, Hq * D, self.ks_o)))
         if dense_engine == "tc":
             ws = max(int(lib.b2f_qgemm_splitk_workspace_bytes(B, self.qkv_rows, self.ks_qkv)) if self.ks_qkv > 1 else 0,
                      int(lib.b2f_qgemm_splitk_workspace_bytes(B, H, self.ks_o)) if self.ks_o > 1 else 0)
@@ -298,17 +310,14 @@ class Qwen3MoeDecoder:
              0, ptr(self.xn), st)
         for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
             w = ly["wqkv"]
-            if self.dense_engine == "tc" and self.ks_qkv > 1:
+            if self.dense_engine == "mma" or (self.dense_engine == "tc" and self.ks_qkv > 1):
                 self._partials(self.xn, H, w, self.ks_qkv, st)
                 call("b2f_qk_norm_rope_kv_append_partials", ptr(self.dense_ws), self.ks_qkv, B, Hq, Hkv, D,
                      ptr(ly["q_norm"]), ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q),
                      ptr(kv["kc"]), ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table),
                      self.max_pages, self.page, s.kv_bits, st)
             else:
-                if self.dense_engine == "mma":
-                    self._mma(self.xn, H, w, self.qkv, st)
-                else:
-                    self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
+                self._dense(self.xn, H, w, 0, self.qkv, self.ks_qkv, st)
                 call("b2f_qk_norm_rope_kv_append", ptr(self.qkv), B, Hq, Hkv, D, ptr(ly["q_norm"]),
                      ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q), ptr(kv["kc"]),
                      ptr(kv["ks"]), ptr(kv["vc"]), ptr(kv["vs"]), ptr(self.block_table), self.max_pages, self.page,
@@ -318,15 +327,10 @@ class Qwen3MoeDecoder:
                  s.kv_bits, 64, self.softmax_scale, self.n_splits, ptr(self.attn_ws), self.attn_ws_bytes,
                  ptr(self.attn), st)
             w = ly["wo"]
-            if self.dense_engine == "tc" and self.ks_o > 1:
+            if self.dense_engine == "mma" or (self.dense_engine == "tc" and self.ks_o > 1):
                 self._partials(self.attn, Hq * D, w, self.ks_o, st)
                 call("b2f_combine_rmsnorm_partials", ptr(self.h), ptr(self.dense_ws), self.ks_o, B,
                      ptr(ly["post_norm"]), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
-            elif self.dense_engine == "mma":
-                # h += o_proj(attn) and the post-attention RMSNorm in one pass
-                self._mma(self.attn, Hq * D, w, self.oy, st)
-                call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.oy), 0, B, 1, ptr(ly["post_norm"]), s.rms_eps, H,
-                     ptr(self.h), ptr(self.xn), st)
             else:
                 self._dense(self.attn, Hq * D, w, self.h, self.h, self.ks_o, st)
                 call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(ly["post_norm"]), s.rms_eps, H, 0,
@@ -387,14 +391,13 @@ class Qwen3MoeDecoder:
                  w.bits, w.group_size, ptr(residual) if isinstance(residual, torch.Tensor) else 0, ptr(out), w.N,
                  self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
 
-    def _mma(self, x, ldx, w, out, st):
-        """out = x . W^T on warp MMA, the batch as one planned 64-token tile."""
-        call("b2f_gather_qgemm_affine_mma", ptr(x), ldx, 0, 1, 0, self.B, 1, ptr(w.wq), ptr(w.scales),
-             ptr(w.biases), 0, 0, 0, w.N, w.K, w.bits, w.group_size, 64, ptr(self.dplan_ws), self.dplan_bytes,
-             ptr(out), w.N, 0, st)
-
     def _partials(self, x, ldx, w, ksplit, st):
         """fp32 split-K partials of x . W^T into the dense workspace."""
+        if self.dense_engine == "mma":
+            call("b2f_gather_qgemm_affine_mma_partials", ptr(x), ldx, 0, 1, self.B, 1, ptr(w.wq), ptr(w.scales),
+                 ptr(w.biases), w.N, w.K, w.bits, w.group_size, 16, ptr(self.dplan_ws), self.dplan_bytes, ksplit,
+                 ptr(self.dense_ws), self.dense_ws_bytes, st)
+            return
         call("b2f_qgemm_affine_tcgen05_partials", ptr(x), ldx, self.B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N,
              w.K, w.bits, w.group_size, self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
 

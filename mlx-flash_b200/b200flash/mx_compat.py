@@ -211,6 +211,24 @@ def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bia
     return out
 
 
+def gather_qmm_mma_partials(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size, bits,
+                            ksplit: int, x_row_index: torch.Tensor = None, x_row_div: int = 1) -> torch.Tensor:
+    """Split-K form of ``gather_qmm_mma_planned`` (tile 16, one matrix): fp32
+    planes ``[n_ranges, A, N]`` whose sum over the first axis is the product."""
+    dev = require_cuda(x_rows, w, scales, biases, x_row_index)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 32 // bits
+    lib = _capi.lib()
+    nr = int(lib.b2f_mma_splitk_ranges(K, ksplit))
+    out = torch.empty(nr, plan.A, N, dtype=torch.float32, device=dev)
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_gather_qgemm_affine_mma_partials", ptr(xc), K, ptr(xri), int(x_row_div), plan.A, E, ptr(w.contiguous()),
+         ptr(scales.contiguous()), ptr(biases.contiguous()), N, K, bits, group_size, plan.tile, ptr(plan.workspace),
+         plan.workspace.numel(), int(ksplit), ptr(out), out.numel() * 4, stream_of(dev))
+    return out
+
+
 def moe_gather_rows(x_rows: torch.Tensor, plan: "MoEPlan", x_row_index: torch.Tensor = None,
                     x_row_div: int = 1) -> torch.Tensor:
     """Activation rows in the plan's expert-sorted order (``[A, K]``; rows past

@@ -73,6 +73,9 @@ struct MmaParams {
   const int32_t* sorted;
   int32_t* err;
   int stages;
+  int cpk;         // 128-wide K chunks per split (grid z); the whole K when not split
+  float* partial;  // split-K: fp32 planes [gridDim.z][A][N] instead of bf16 out (one matrix)
+  int64_t plane;   // elements per partial plane (A * N)
 };
 
 __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -92,7 +95,8 @@ __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 
 template <int MAT, int NTA, bool XPLAN, int WROWS>
 __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
                                             uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
-                                            int begin, int cnt, int64_t row_base, int HC, int warp, int lane) {
+                                            int begin, int cnt, int64_t row_base, int h0, int h1, int warp,
+                                            int lane) {
   constexpr int MT = WROWS / 16 / MAT;
   static_assert(MT >= 1, "at least one 16-row tile per matrix");
   const int S = p.stages;
@@ -130,11 +134,11 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
         }
       }
   };
-  load_sb(0);
+  load_sb(h0);
 
   int s = 0;
   uint32_t phase = 0;
-  for (int h = 0; h < HC; ++h) {
+  for (int h = h0; h < h1; ++h) {
     const bool ok = !*abort_flag && mbar_wait_bounded(&full[s], phase);
     if (!__all_sync(0xffffffffu, ok)) {
       if (lane == 0) *abort_flag = 1;
@@ -218,13 +222,39 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (h + 1 < HC) load_sb(h + 1);
+    if (h + 1 < h1) load_sb(h + 1);
     if (++s == S) {
       s = 0;
       phase ^= 1u;
     }
   }
   if (*abort_flag) return;
+
+  if (p.partial) {
+    // split-K: fp32 partial plane of this K range, rows = assignments
+    float* plane = p.partial + int64_t(blockIdx.z) * p.plane;
+#pragma unroll
+    for (int nt = 0; nt < NTA; ++nt) {
+      const int t0 = 8 * nt + 2 * c;
+      const int64_t a0 = t0 < cnt ? int64_t(p.sorted[begin + t0]) : 0;
+      const int64_t a1 = t0 + 1 < cnt ? int64_t(p.sorted[begin + t0 + 1]) : 0;
+#pragma unroll
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const float v0 = acc[0][i][nt][2 * hf], v1 = acc[0][i][nt][2 * hf + 1];
+          const int64_t row8 = row_base + wr0 + 16 * i + 8 * hf;
+          const float recv = __shfl_xor_sync(0xffffffffu, (r & 1) ? v0 : v1, 4);
+          const bool odd = r & 1;
+          const int tok = odd ? t0 + 1 : t0;
+          const int64_t col = row8 + (r & ~1);
+          if (tok < cnt && col < p.N)
+            *reinterpret_cast<float2*>(plane + (odd ? a1 : a0) * p.N + col) =
+                odd ? make_float2(recv, v1) : make_float2(v0, recv);
+        }
+    }
+    return;
+  }
 
   // ---- epilogue: values (row R or R+8, tokens 2c and 2c+1) -> bf16 rows ------
 #pragma unroll
@@ -294,6 +324,8 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   if (row_base >= p.N || cnt <= 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HC = int(p.K >> 7);
+  const int h0 = int(blockIdx.z) * p.cpk, h1 = min(HC, h0 + p.cpk);
+  if (h0 >= h1) return;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -326,12 +358,12 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       }
     }
     const int wrow = int(int64_t(expert) * p.N + row_base);
-    int h = 0, s = 0;
+    int h = h0, s = 0;
     uint32_t phase = 0;
-    for (; h < HC; ++h) {
+    for (; h < h1; ++h) {
       int ok = 1;
       if (lane == 0) {
-        if (h >= S && !mbar_wait_bounded_backoff(&empty[s], phase ^ 1u)) ok = 0;
+        if (h - h0 >= S && !mbar_wait_bounded_backoff(&empty[s], phase ^ 1u)) ok = 0;
         if (*abort_flag) ok = 0;
         if (ok) {
           mbar_arrive_expect_tx(&full[s], uint32_t(W_BYTES + cnt * 256));
@@ -357,23 +389,24 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       }
     }
     // copies already issued land before the CTA goes away
+    const int issued = h - h0;
     if (lane == 0)
-      for (int k = 1; k <= S && h - k >= 0; ++k)
-        mbar_wait_bounded(&full[(h - k) % S], uint32_t(((h - k) / S) & 1), 100000000ull);
+      for (int k = 1; k <= S && issued - k >= 0; ++k)
+        mbar_wait_bounded(&full[(issued - k) % S], uint32_t(((issued - k) / S) & 1), 100000000ull);
     return;
   }
 
   if constexpr (SH::NTMAX == 2) {
     if (cnt <= 8) {
       mma_consume<MAT, 1, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, HC, warp, lane);
+                                            begin, cnt, row_base, h0, h1, warp, lane);
     } else {
       mma_consume<MAT, 2, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, HC, warp, lane);
+                                            begin, cnt, row_base, h0, h1, warp, lane);
     }
   } else {
     mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
-                                                  expert, begin, cnt, row_base, HC, warp, lane);
+                                                  expert, begin, cnt, row_base, h0, h1, warp, lane);
   }
   if (lane == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
 }
@@ -394,7 +427,7 @@ static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows
 
 template <int MAT, bool XPLAN, int TILE>
 static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, int64_t E, int64_t slots_grid,
-                          cudaStream_t st) {
+                          int ksplit, cudaStream_t st) {
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
   constexpr int STAGE = MAT * CTA_ROWS * 64 + TILE * MMA_XSTRIDE;
@@ -422,10 +455,19 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   }
   const int64_t row_blocks = (p.N + CTA_ROWS - 1) / CTA_ROWS;
   if ((TILE == 16 ? slots_grid : row_blocks) > 65535) return B2F_ERR_UNSUPPORTED;
-  const dim3 grid = TILE == 16 ? dim3{unsigned(row_blocks), unsigned(slots_grid), 1u}
-                               : dim3{unsigned(slots_grid), unsigned(row_blocks), 1u};
+  const dim3 grid = TILE == 16 ? dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)}
+                               : dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)};
   kern<<<grid, 160, smem, st>>>(p, m0, m1);
   return check_launch();
+}
+
+// K split into ranges of whole 128-wide chunks: the number of non-empty ranges
+static int mma_splitk_ranges(int64_t K, int ksplit, int* cpk) {
+  const int hc = int(K / 128);
+  if (ksplit < 1) ksplit = 1;
+  if (ksplit > hc) ksplit = hc;
+  *cpk = (hc + ksplit - 1) / ksplit;
+  return (hc + *cpk - 1) / *cpk;
 }
 
 // plan layout helpers live in qgemv.cu
@@ -482,15 +524,75 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
   p.err = reinterpret_cast<int32_t*>(ws) + 1;  // the plan header's status word
   p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
   p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
+  p.cpk = int(K / 128);
   cudaStream_t st = as_stream(stream);
   const bool xp = x_plan_order != 0;
   if (tile == 64)
-    return xp ? launch_mma_cfg<1, true, 64>(p, w_gate, nullptr, E, max_slots, st)
-              : launch_mma_cfg<1, false, 64>(p, w_gate, nullptr, E, max_slots, st);
+    return xp ? launch_mma_cfg<1, true, 64>(p, w_gate, nullptr, E, max_slots, 1, st)
+              : launch_mma_cfg<1, false, 64>(p, w_gate, nullptr, E, max_slots, 1, st);
   if (w_up) {
-    return xp ? launch_mma_cfg<2, true, 16>(p, w_gate, w_up, E, max_slots, st)
-              : launch_mma_cfg<2, false, 16>(p, w_gate, w_up, E, max_slots, st);
+    return xp ? launch_mma_cfg<2, true, 16>(p, w_gate, w_up, E, max_slots, 1, st)
+              : launch_mma_cfg<2, false, 16>(p, w_gate, w_up, E, max_slots, 1, st);
   }
-  return xp ? launch_mma_cfg<1, true, 16>(p, w_gate, nullptr, E, max_slots, st)
-            : launch_mma_cfg<1, false, 16>(p, w_gate, nullptr, E, max_slots, st);
+  return xp ? launch_mma_cfg<1, true, 16>(p, w_gate, nullptr, E, max_slots, 1, st)
+            : launch_mma_cfg<1, false, 16>(p, w_gate, nullptr, E, max_slots, 1, st);
+}
+
+extern "C" int b2f_mma_splitk_ranges(int64_t K, int ksplit) {
+  if (K <= 0 || K % 128 != 0) return 0;
+  int cpk = 0;
+  return mma_splitk_ranges(K, ksplit, &cpk);
+}
+
+extern "C" int64_t b2f_mma_splitk_workspace_bytes(int64_t A, int64_t N, int64_t K, int ksplit) {
+  if (A <= 0 || N <= 0 || K <= 0 || K % 128 != 0) return 0;
+  int cpk = 0;
+  return int64_t(mma_splitk_ranges(K, ksplit, &cpk)) * A * N * int64_t(sizeof(float));
+}
+
+extern "C" int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                                    int64_t x_row_div, int64_t A, int64_t E, const uint32_t* w,
+                                                    const void* scales, const void* biases, int64_t N, int64_t K,
+                                                    int bits, int group_size, int tile, void* plan_workspace,
+                                                    int64_t plan_workspace_bytes, int ksplit, float* partial,
+                                                    int64_t partial_bytes, void* stream) {
+  if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
+  if (tile != 16) return B2F_ERR_UNSUPPORTED;
+  if (A < 0 || E <= 0 || ksplit < 1 || ksplit > 65535) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x || !w || !scales || !biases || !partial) return B2F_ERR_INVALID;
+  if (!x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
+  if (ldx < K) return B2F_ERR_INVALID;
+  if (E * N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w, 16) || !aligned(partial, 16) || !aligned(scales, 4) ||
+      !aligned(biases, 4))
+    return B2F_ERR_ALIGN;
+  const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
+  if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
+  if (partial_bytes < b2f_mma_splitk_workspace_bytes(A, N, K, ksplit)) return B2F_ERR_WORKSPACE;
+  const int64_t max_slots = b2f_moe_plan_max_slots(A, E, tile);
+  if (max_slots > 65535) return B2F_ERR_UNSUPPORTED;
+  int rc = get_encoder();
+  if (rc != B2F_OK) return rc;
+  char* ws = static_cast<char*>(plan_workspace);
+  MmaParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.x_row_index = x_row_index;
+  p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  p.s[0] = p.s[1] = static_cast<const __nv_bfloat16*>(scales);
+  p.b[0] = p.b[1] = static_cast<const __nv_bfloat16*>(biases);
+  p.N = N;
+  p.K = K;
+  p.G = int(K / 64);
+  p.ldo = N;
+  p.slot_count = reinterpret_cast<const int32_t*>(ws);
+  p.err = reinterpret_cast<int32_t*>(ws) + 1;
+  p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
+  p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
+  const int ks = mma_splitk_ranges(K, ksplit, &p.cpk);
+  p.partial = partial;
+  p.plane = A * N;
+  return launch_mma_cfg<1, false, 16>(p, w, nullptr, E, max_slots, ks, as_stream(stream));
 }

@@ -108,3 +108,23 @@ def test_mma_wide_tile_dense_projection(dev, M, N, K):
     y = mx_compat.gather_qmm_mma_planned(to_dev(x, "bf16", dev), plan, *_dev3(w, dev), 64, 4, x_row_div=1)
     want = x.astype(np.float64) @ affine.dequantize_f32(w[0][0], w[1][0], w[2][0], 64, 4).astype(np.float64).T
     assert_close(to_np(y), want, what=f"mma dense M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("A,E,N,K,ksplit", [(64, 1, 5120, 2048, 6), (64, 1, 2048, 4096, 11), (300, 24, 1000, 1280, 4),
+                                            (5, 1, 256, 128, 3)])
+def test_mma_splitk_partials(dev, A, E, N, K, ksplit):
+    """K cut into ranges of whole 128-wide chunks: the fp32 planes sum to the
+    product (a one-expert plan is the dense q/k/v or o projection of a decode
+    batch); ksplit beyond the chunk count is clamped."""
+    rng = np.random.default_rng(A + N + ksplit)
+    w = _w(rng, (E, N, K))
+    x = round_to(rng.standard_normal((A, K)).astype(np.float32), "bf16")
+    eid = (rng.integers(0, E, A) if E > 1 else np.zeros(A)).astype(np.int32)
+    plan = mx_compat.MoEPlan(torch.from_numpy(eid).to(dev), E, 16)
+    parts = mx_compat.gather_qmm_mma_partials(to_dev(x, "bf16", dev), plan, *_dev3(w, dev), 64, 4, ksplit)
+    hc = K // 128
+    cpk = -(-hc // min(ksplit, hc))
+    assert parts.shape[0] == -(-hc // cpk)  # non-empty ranges of whole chunks
+    deq = [affine.dequantize_f32(w[0][e], w[1][e], w[2][e], 64, 4).astype(np.float64) for e in range(E)]
+    want = np.stack([deq[eid[a]] @ x[a].astype(np.float64) for a in range(A)])
+    assert_close(to_np(parts.sum(0)), want, what=f"mma split-K A={A} E={E} N={N} K={K} ks={ksplit}")
