@@ -117,20 +117,29 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
 
   // (s, b) pairs of both groups of a chunk for rows R and R+8 of each tile
   uint32_t sr[MAT][MT][2], br[MAT][MT][2];
-  const int64_t srow0 = int64_t(expert) * p.N + row_base + wr0 + r;
+  // the pair of chunk h sits at 32-bit word h of a row (G is even); rows R
+  // and R+8 of tile i are (2i + hf) * 4G words past the lane's first row
+  const int64_t srow0 = (int64_t(expert) * p.N + row_base + wr0 + r) * p.G;
+  const uint32_t* sbase[MAT];
+  const uint32_t* bbase[MAT];
+#pragma unroll
+  for (int m = 0; m < MAT; ++m) {
+    sbase[m] = reinterpret_cast<const uint32_t*>((m == 0 ? p.s[0] : p.s[1]) + srow0);
+    bbase[m] = reinterpret_cast<const uint32_t*>((m == 0 ? p.b[0] : p.b[1]) + srow0);
+  }
+  const int rstep = 4 * p.G;
+  const int64_t rows_left = p.N - (row_base + wr0 + r);  // rows valid at offsets < rows_left
   auto load_sb = [&](int h) {
 #pragma unroll
     for (int i = 0; i < MT; ++i)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const bool rv = row_base + wr0 + 16 * i + 8 * hf + r < p.N;
-        const int64_t o = (srow0 + 16 * i + 8 * hf) * p.G + 2 * h;
+        const bool rv = 16 * i + 8 * hf < rows_left;
+        const int o = (2 * i + hf) * rstep + h;
 #pragma unroll
         for (int m = 0; m < MAT; ++m) {
-          const __nv_bfloat16* sp = m == 0 ? p.s[0] : p.s[1];
-          const __nv_bfloat16* bp = m == 0 ? p.b[0] : p.b[1];
-          sr[m][i][hf] = rv ? *reinterpret_cast<const uint32_t*>(sp + o) : 0u;
-          br[m][i][hf] = rv ? *reinterpret_cast<const uint32_t*>(bp + o) : 0u;
+          sr[m][i][hf] = rv ? sbase[m][o] : 0u;
+          br[m][i][hf] = rv ? bbase[m][o] : 0u;
         }
       }
   };
