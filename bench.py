@@ -58,27 +58,64 @@ def config_dict(args, world):
 
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed
+    region runs: NVML read every 10 ms from a thread (read-only queries), or
+    ``nvidia-smi -lms 100`` when NVML is not importable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, device):
+        self.device = device
         self.proc = None
+        self.thread = None
+        self.samples = []  # (sm_mhz, max_mhz, set of reasons)
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.device)
+        bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            nv, h = self._nvml_handle()
+            self.stop = threading.Event()
+            mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+
+            def run():
+                while not self.stop.is_set():
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    rs = {name for name, attr in self.REASONS if bits & getattr(nv, attr, 0)}
+                    self.samples.append((float(sm), float(mx), rs))
+                    self.stop.wait(0.01)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device.index or 0}",
+                                              f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                              "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                             text=True)
+            except Exception:
+                self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -86,24 +123,23 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+            names = [n for n, _ in self.REASONS]
+            for l in out.splitlines():
+                f = [x.strip() for x in l.split(",")]
+                try:
+                    self.samples.append((float(f[1]), float(f[2]),
+                                         {n for n, v in zip(names, f[5:9]) if v.lower() == "active"}))
+                except (ValueError, IndexError):
+                    continue
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except (ValueError, IndexError):
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = sorted(x[0] for x in self.samples)
+        reasons = set()
+        for x in self.samples:
+            reasons |= x[2]
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": self.samples[-1][1] if self.samples else None, "reasons": sorted(reasons),
+                "samples": len(sm), "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
@@ -249,7 +285,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(dev) as clk:
         if args.profile_window:
             torch.cuda.profiler.start()
         e0.record()
