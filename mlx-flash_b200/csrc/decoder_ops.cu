@@ -27,6 +27,8 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 // One CTA per row; a thread owns chunks of 8 contiguous elements (16-byte loads).
 constexpr int CMB_CHUNKS = 4;
 
+constexpr int CMB_BATCH = 8;  // expert rows / partial planes whose loads are issued together
+
 __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ y,
     const float* __restrict__ scores, int k, const __nv_bfloat16* __restrict__ w, float eps, int H,
@@ -50,28 +52,53 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
       h[2 * i + 1] = __high2float(r2[i]);
     }
     if (partial) {  // split-K fp32 partials of a projection added to the residual
-      for (int j = 0; j < nsplit; ++j) {
-        const float4* pp = reinterpret_cast<const float4*>(partial + (int64_t(j) * M + m) * H) + 2 * v;
-        const float4 a = pp[0], c = pp[1];
-        h[0] += a.x;
-        h[1] += a.y;
-        h[2] += a.z;
-        h[3] += a.w;
-        h[4] += c.x;
-        h[5] += c.y;
-        h[6] += c.z;
-        h[7] += c.w;
+      // all planes' loads in flight before the first add (in plane order)
+      for (int j0 = 0; j0 < nsplit; j0 += CMB_BATCH) {
+        float4 a[CMB_BATCH], c[CMB_BATCH];
+#pragma unroll
+        for (int u = 0; u < CMB_BATCH; ++u) {
+          if (j0 + u < nsplit) {
+            const float4* pp = reinterpret_cast<const float4*>(partial + (int64_t(j0 + u) * M + m) * H) + 2 * v;
+            a[u] = pp[0];
+            c[u] = pp[1];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < CMB_BATCH; ++u) {
+          if (j0 + u < nsplit) {
+            h[0] += a[u].x;
+            h[1] += a[u].y;
+            h[2] += a[u].z;
+            h[3] += a[u].w;
+            h[4] += c[u].x;
+            h[5] += c[u].y;
+            h[6] += c[u].z;
+            h[7] += c[u].w;
+          }
+        }
       }
     }
     if (y) {
-      for (int j = 0; j < k; ++j) {
-        const float sc = scores ? scores[m * k + j] : 1.0f;
-        const uint4 yy = reinterpret_cast<const uint4*>(y + (m * k + j) * H)[v];
-        const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&yy);
+      for (int j0 = 0; j0 < k; j0 += CMB_BATCH) {
+        uint4 yy[CMB_BATCH];
+        float sc[CMB_BATCH];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          h[2 * i] += sc * __low2float(y2[i]);
-          h[2 * i + 1] += sc * __high2float(y2[i]);
+        for (int u = 0; u < CMB_BATCH; ++u) {
+          if (j0 + u < k) {
+            sc[u] = scores ? scores[m * k + j0 + u] : 1.0f;
+            yy[u] = reinterpret_cast<const uint4*>(y + (m * k + j0 + u) * H)[v];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < CMB_BATCH; ++u) {
+          if (j0 + u < k) {
+            const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&yy[u]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              h[2 * i] += sc[u] * __low2float(y2[i]);
+              h[2 * i + 1] += sc[u] * __high2float(y2[i]);
+            }
+          }
         }
       }
     }
@@ -147,12 +174,22 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams
     if (p.qkv_partial) {
       // the projection's bf16 output, formed here from its split-K partials
       const int64_t plane = int64_t(gridDim.x) * NH * D;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      const float* base = p.qkv_partial + int64_t(b) * NH * D + h * D + lane;
+      for (int j0 = 0; j0 < p.nsplit; j0 += 8) {
+        float t[8][4];  // eight planes' loads in flight, summed in plane order
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float a = 0.f;
-        for (int j = 0; j < p.nsplit; ++j) a += p.qkv_partial[j * plane + int64_t(b) * NH * D + h * D + lane + 32 * i];
-        v[i] = __bfloat162float(__float2bfloat16_rn(a));
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) t[u][i] = j0 + u < p.nsplit ? base[(j0 + u) * plane + 32 * i] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (j0 + u < p.nsplit) a[i] += t[u][i];
       }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(a[i]));
     } else {
 #pragma unroll
       for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(row[h * D + lane + 32 * i]);

@@ -124,19 +124,30 @@ struct GatheredExperts {
 };
 
 // The counting sort, run by one whole thread block (any blockDim <= 1024).
+// Per-expert counters live in shared memory (E <= PLAN_SMEM_E) so the
+// count / scan / scatter phases cost shared-memory atomics and block
+// barriers only; larger E falls back to the workspace arrays.
+constexpr int PLAN_SMEM_E = 1024;
+
 template <class Src>
 __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int tile, char* ws, PlanLayout L,
                                                int32_t* status_out) {
   int32_t* hdr = reinterpret_cast<int32_t*>(ws + L.off_hdr);
-  int32_t* counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + L.off_offsets);
-  int32_t* cursor = reinterpret_cast<int32_t*>(ws + L.off_cursor);
-  int32_t* soff = reinterpret_cast<int32_t*>(ws + L.off_soff);
+  int32_t* g_counts = reinterpret_cast<int32_t*>(ws + L.off_counts);
+  int32_t* g_offsets = reinterpret_cast<int32_t*>(ws + L.off_offsets);
+  int32_t* g_cursor = reinterpret_cast<int32_t*>(ws + L.off_cursor);
+  int32_t* g_soff = reinterpret_cast<int32_t*>(ws + L.off_soff);
   int32_t* sorted = reinterpret_cast<int32_t*>(ws + L.off_sorted);
   int4* slots = reinterpret_cast<int4*>(ws + L.off_slots);
   __shared__ int warp_tot[32];
   __shared__ int total;
   __shared__ int bad;
+  __shared__ int s_counts[PLAN_SMEM_E], s_cursor[PLAN_SMEM_E], s_offsets[PLAN_SMEM_E + 1], s_soff[PLAN_SMEM_E + 1];
+  const bool sm = E <= PLAN_SMEM_E;
+  int32_t* counts = sm ? s_counts : g_counts;
+  int32_t* cursor = sm ? s_cursor : g_cursor;
+  int32_t* offsets = sm ? s_offsets : g_offsets;
+  int32_t* soff = sm ? s_soff : g_soff;
   if (threadIdx.x == 0) bad = 0;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     counts[e] = 0;
@@ -188,6 +199,16 @@ __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int
     const int cnt = counts[e];
     for (int j = 0, s = soff[e]; j * tile < cnt; ++j, ++s)
       slots[s] = make_int4(e, offsets[e] + j * tile, min(tile, cnt - j * tile), 0);
+  }
+  if (sm) {  // the per-expert arrays of the workspace layout, for readers of the plan
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+      if (e < E) {
+        g_counts[e] = counts[e];
+        g_cursor[e] = cursor[e];
+      }
+      g_offsets[e] = offsets[e];
+      g_soff[e] = soff[e];
+    }
   }
 }
 
