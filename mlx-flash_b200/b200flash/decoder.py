@@ -229,6 +229,14 @@ class Qwen3MoeDecoder:
         if dense_engine == "mma" and not mma_dense:
             dense_engine = "tc" if s.group_size == 64 else "gemv"
         self.dense_engine = dense_engine
+        # lm_head: warp MMA over a one-expert plan for small batches (measured
+        # ahead of the register GEMV at 8 tokens); tcgen05 from 32 tokens on
+        self.lm_mma = bits == 4 and gs == 64 and H % 128 == 0 and s.vocab % 8 == 0 and B < 32
+        if self.lm_mma:
+            self.lmplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 16))
+            self.lmplan_ws = torch.empty(self.lmplan_bytes, dtype=torch.uint8, device=dev)
+            call("b2f_moe_plan", ptr(torch.zeros(B, dtype=torch.int32, device=dev)), B, 1, 16, ptr(self.lmplan_ws),
+                 self.lmplan_bytes, 0, _capi.stream_of(dev))
         if dense_engine == "mma":
             # the batch as slots of one "expert" (a plan over all-zero expert ids)
             self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 16))
@@ -374,7 +382,15 @@ class Qwen3MoeDecoder:
                      ptr(self.y), H, st)
             call("b2f_combine_rmsnorm", ptr(self.h), ptr(self.y), ptr(self.scores), B, s.top_k, ptr(nxt),
                  s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
-        self._dense(self.xn, H, self.lm_head, 0, self.logits, 1, st)
+        if self.lm_mma:
+            # the vocabulary projection on warp MMA: the batch as 16-token slots
+            # of a one-expert plan, each 64-row block read once from HBM
+            w = self.lm_head
+            call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, 1, 0, B, 1, ptr(w.wq), ptr(w.scales),
+                 ptr(w.biases), 0, 0, 0, w.N, w.K, w.bits, w.group_size, 16, ptr(self.lmplan_ws), self.lmplan_bytes,
+                 ptr(self.logits), w.N, 0, st)
+        else:
+            self._dense(self.xn, H, self.lm_head, 0, self.logits, 1, st)
         call("b2f_argmax_rows", ptr(self.logits), B, s.vocab, ptr(self.next_tokens), st)
         # feed back: next input token and position
         self.tokens.copy_(self.next_tokens)

@@ -76,6 +76,7 @@ struct MmaParams {
   int cpk;         // 128-wide K chunks per split (grid z); the whole K when not split
   float* partial;  // split-K: fp32 planes [gridDim.z][A][N] instead of bf16 out (one matrix)
   int64_t plane;   // elements per partial plane (A * N)
+  int slot_major;  // grid x = slot (the slots sharing a row block run back to back and hit L2)
 };
 
 __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -321,11 +322,11 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
-  // expert tiles: x = row block, y = slot (one expert's contiguous rows are
-  // streamed by consecutive CTAs); wide tiles: x = slot, y = row block (the
-  // slots reading one row block run back to back and share it through L2)
-  const int slot_id = TILE == 16 ? int(blockIdx.y) : int(blockIdx.x);
-  const int rblk = TILE == 16 ? int(blockIdx.x) : int(blockIdx.y);
+  // x = row block, y = slot: one expert's contiguous rows are streamed by
+  // consecutive CTAs; slot-major (wide tiles, one-matrix plans): x = slot,
+  // so the slots reading one row block run back to back and share it in L2
+  const int slot_id = p.slot_major ? int(blockIdx.x) : int(blockIdx.y);
+  const int rblk = p.slot_major ? int(blockIdx.y) : int(blockIdx.x);
   if (slot_id >= *p.slot_count) return;
   const int4 sl = p.slots[slot_id];
   const int expert = sl.x, begin = sl.y, cnt = min(sl.z, TILE);
@@ -463,9 +464,12 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
     return B2F_ERR_CUDA;
   }
   const int64_t row_blocks = (p.N + CTA_ROWS - 1) / CTA_ROWS;
-  if ((TILE == 16 ? slots_grid : row_blocks) > 65535) return B2F_ERR_UNSUPPORTED;
-  const dim3 grid = TILE == 16 ? dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)}
-                               : dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)};
+  // wide tiles, and one-matrix plans whose slots all read the same rows, put
+  // the slots on x; expert tiles keep one expert's row blocks consecutive
+  p.slot_major = (TILE == 64 || E == 1) ? 1 : 0;
+  if ((p.slot_major ? row_blocks : slots_grid) > 65535) return B2F_ERR_UNSUPPORTED;
+  const dim3 grid = p.slot_major ? dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)}
+                                 : dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)};
   kern<<<grid, 160, smem, st>>>(p, m0, m1);
   return check_launch();
 }
