@@ -307,6 +307,21 @@ int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, const int32
                                          int64_t plan_workspace_bytes, int ksplit, float* partial,
                                          int64_t partial_bytes, void* stream);
 
+/* b2f_gather_qgemm_affine_mma for 2-bit codes: w uint32 [E, N, K/16], code k
+ * at bits 2*(k % 16) of word k/16 (LSB first: the byte layout of
+ * requantize_4bit_to_2bit's packed output, mixed_precision.py:173-216, and
+ * of MLX's 2-bit affine format), scales/biases [E, N, K/64] of scale_dtype
+ * (B2F_F16 as requantize_4bit_to_2bit writes them, or B2F_BF16);
+ * w = q*s + b, folded per group as s*sum(q x) + b*sum(x).  x rows x_row(a),
+ * natural column order; out[a, :] natural; plan tile 16; SwiGLU fused when
+ * w_up is given.  K % 128 == 0, N % 8 == 0. */
+int b2f_gather_qgemm_2bit_mma(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div,
+                              int64_t A, int64_t E, const uint32_t* w_gate, const void* s_gate,
+                              const void* b_gate, const uint32_t* w_up, const void* s_up,
+                              const void* b_up, int64_t N, int64_t K, int scale_dtype, int tile,
+                              void* plan_workspace, int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                              void* stream);
+
 /* ---- (c) grouped GEMM over expert-sorted rows (decode and prefill) ------ */
 
 /* Copies the planned assignments' activation rows into plan order:

@@ -57,6 +57,8 @@ SIGNATURES = {
     "b2f_mma_splitk_workspace_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "b2f_gather_qgemm_affine_mma_partials": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I,
                                                   _I, _P, _I64, _I, _P, _I64, _P]),
+    "b2f_gather_qgemm_2bit_mma": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I,
+                                       _P, _I64, _P, _I64, _P]),
     "b2f_moe_gather_rows": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _I64, _P]),
     "b2f_sorted_qgemm_affine_tcgen05": (_I, [_P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64, _I64, _I, _I, _I,
                                              _P, _I64, _P, _I64, _I, _P]),

@@ -229,6 +229,31 @@ def gather_qmm_mma_partials(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bi
     return out
 
 
+def gather_qmm_2bit_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases,
+                            x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None) -> torch.Tensor:
+    """Grouped GEMM over 2-bit codes (``requantize_4bit_to_2bit`` output: packed
+    bytes viewed as uint32 ``[E, N, K/16]``, fp16 or bf16 scales/biases
+    ``[E, N, K/64]``) on warp MMA; plan tile 16; ``up`` fuses SwiGLU."""
+    dev = require_cuda(x_rows, w, scales, biases, x_row_index)
+    E, N = w.shape[0], w.shape[1]
+    K = w.shape[2] * 16
+    if K % 128 or N % 8 or plan.tile != 16:
+        raise ValueError("the 2-bit MMA path needs K % 128 == 0, N % 8 == 0 and a plan with tile 16")
+    if scales.dtype not in (torch.float16, torch.bfloat16) or biases.dtype != scales.dtype:
+        raise ValueError("scales/biases must both be float16 or both bfloat16")
+    sdt = 1 if scales.dtype == torch.float16 else 0
+    xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))
+    out = torch.empty(plan.A, N, dtype=torch.bfloat16, device=dev)
+    wu = su = bu = None
+    if up is not None:
+        wu, su, bu = (t.contiguous() for t in up)
+    xri = None if x_row_index is None else x_row_index.to(torch.int32).contiguous()
+    call("b2f_gather_qgemm_2bit_mma", ptr(xc), K, ptr(xri), int(x_row_div), plan.A, E, ptr(w.contiguous()),
+         ptr(scales.contiguous()), ptr(biases.contiguous()), ptr(wu), ptr(su), ptr(bu), N, K, sdt, plan.tile,
+         ptr(plan.workspace), plan.workspace.numel(), ptr(out), N, stream_of(dev))
+    return out
+
+
 def moe_gather_rows(x_rows: torch.Tensor, plan: "MoEPlan", x_row_index: torch.Tensor = None,
                     x_row_div: int = 1) -> torch.Tensor:
     """Activation rows in the plan's expert-sorted order (``[A, K]``; rows past

@@ -89,11 +89,20 @@ __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_
 
 __device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+// half `hi` of a pair of bf16 (or fp16) scale / bias values as fp32
+template <bool F16>
+__device__ __forceinline__ float sc_half(uint32_t v, int hi) {
+  if constexpr (F16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(hi ? v >> 16 : v & 0xFFFFu)));
+  } else {
+    return hi ? bf_hi(v) : bf_lo(v);
+  }
+}
 
 // The consumer side of one CTA for slots of up to 8*NTA tokens: the warp's
 // WROWS/MAT rows of each matrix (MAT 2: gate and up, SwiGLU epilogue), as
 // MT row tiles of 16.
-template <int MAT, int NTA, bool XPLAN, int WROWS>
+template <int MAT, int NTA, bool XPLAN, int WROWS, int BITS, bool SF16>
 __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
                                             uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
                                             int begin, int cnt, int64_t row_base, int h0, int h1, int warp,
@@ -102,7 +111,11 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   static_assert(MT >= 1, "at least one 16-row tile per matrix");
   const int S = p.stages;
   const int r = lane >> 2, c = lane & 3;
-  const int sw = (r >> 1) & 3;  // 64B swizzle phase of this lane's rows (r and r+8 share it)
+  // swizzle phase of this lane's rows (r and r+8 share it): 64B (4-bit rows
+  // of 64 bytes) or 32B (2-bit rows of 32 bytes)
+  const int sw = BITS == 4 ? (r >> 1) & 3 : (r >> 2) & 1;
+  constexpr int RBY = 16 * BITS;  // code bytes per row per 128-wide chunk
+  constexpr int XS = BITS == 4 ? 320 : 336;
   const int wr0 = warp * (WROWS / MAT);
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
@@ -160,6 +173,52 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
     for (int grp = 0; grp < 2; ++grp) {
       float t[MAT][MT][NTA][4];  // sum over the group of (128+q) x
       float xs[NTA][4];          // sum over the group of x (rows all equal)
+      if constexpr (BITS == 2) {
+        // 2-bit: word c + 4*grp of the row's 8-word chunk, 16 crumbs (LSB
+        // first) covering k in [16(c + 4 grp), +16); crumb pairs (i, i+8)
+        // through k-steps 0..3 as (0,8)(1,9) | (2,10)(3,11) | ...
+        uint32_t bx[NTA][4][2];
+#pragma unroll
+        for (int nt = 0; nt < NTA; ++nt) {
+          const uint8_t* xp = xst + (8 * nt + r) * XS + 32 * (c + 4 * grp);
+          const uint4 u0 = *reinterpret_cast<const uint4*>(xp), u1 = *reinterpret_cast<const uint4*>(xp + 16);
+          const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+          for (int st = 0; st < 4; ++st) {
+            bx[nt][st][0] = prmt(uu[st], uu[st + 4], 0x5410u);  // (x 2st, x 2st+8)
+            bx[nt][st][1] = prmt(uu[st], uu[st + 4], 0x7632u);  // (x 2st+1, x 2st+9)
+            if (st == 0) {
+              mma_bf16_16816_zero(xs[nt], ones, bx[nt][st]);
+            } else {
+              mma_bf16_16816(xs[nt], ones, bx[nt][st]);
+            }
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < MAT; ++m) {
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            const uint8_t* rowp = wst + m * CTA_ROWS * RBY + (wr0 + 16 * i + r) * RBY + 16 * (grp ^ sw) + 4 * c;
+            const uint32_t wl = *reinterpret_cast<const uint32_t*>(rowp);
+            const uint32_t wh = *reinterpret_cast<const uint32_t*>(rowp + 8 * RBY);
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+              const uint32_t a[4] = {and_or(wl >> (4 * st), 0x00030003u, 0x43004300u),
+                                     and_or(wh >> (4 * st), 0x00030003u, 0x43004300u),
+                                     and_or(wl >> (4 * st + 2), 0x00030003u, 0x43004300u),
+                                     and_or(wh >> (4 * st + 2), 0x00030003u, 0x43004300u)};
+#pragma unroll
+              for (int nt = 0; nt < NTA; ++nt) {
+                if (st == 0) {
+                  mma_bf16_16816_zero(t[m][i][nt], a, bx[nt][st]);
+                } else {
+                  mma_bf16_16816(t[m][i][nt], a, bx[nt][st]);
+                }
+              }
+            }
+          }
+        }
+      } else {
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * grp + jj;
@@ -167,7 +226,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
         uint32_t bx[NTA][2][2];
 #pragma unroll
         for (int nt = 0; nt < NTA; ++nt) {
-          const uint4 u = *reinterpret_cast<const uint4*>(xst + (8 * nt + r) * MMA_XSTRIDE + 16 * c + 64 * j);
+          const uint4 u = *reinterpret_cast<const uint4*>(xst + (8 * nt + r) * XS + 16 * c + 64 * j);
           if constexpr (XPLAN) {  // stored as (0,4,1,5,2,6,3,7): the pairs already
             bx[nt][0][0] = u.x;
             bx[nt][0][1] = u.y;
@@ -212,15 +271,15 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
           }
         }
       }
+      }
       // fold the group: y += s*T + (b - 128 s)*X   (rows R: e 0,1; R+8: e 2,3)
 #pragma unroll
       for (int m = 0; m < MAT; ++m)
 #pragma unroll
         for (int i = 0; i < MT; ++i) {
-          const float s0 = grp ? bf_hi(sr[m][i][0]) : bf_lo(sr[m][i][0]);
-          const float s1 = grp ? bf_hi(sr[m][i][1]) : bf_lo(sr[m][i][1]);
-          const float c0 = fmaf(-128.f, s0, grp ? bf_hi(br[m][i][0]) : bf_lo(br[m][i][0]));
-          const float c1 = fmaf(-128.f, s1, grp ? bf_hi(br[m][i][1]) : bf_lo(br[m][i][1]));
+          const float s0 = sc_half<SF16>(sr[m][i][0], grp), s1 = sc_half<SF16>(sr[m][i][1], grp);
+          const float c0 = fmaf(-128.f, s0, sc_half<SF16>(br[m][i][0], grp));
+          const float c1 = fmaf(-128.f, s1, sc_half<SF16>(br[m][i][1], grp));
 #pragma unroll
           for (int nt = 0; nt < NTA; ++nt) {
             acc[m][i][nt][0] = fmaf(s0, t[m][i][nt][0], fmaf(c0, xs[nt][0], acc[m][i][nt][0]));
@@ -305,15 +364,16 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   }
 }
 
-template <int MAT, bool XPLAN, int TILE>
+template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false>
 __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
     qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
                      const __grid_constant__ CUtensorMap tm1) {
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;  // weight rows per matrix
-  constexpr int W_BYTES = MAT * CTA_ROWS * 64;
-  constexpr int STAGE = W_BYTES + TILE * MMA_XSTRIDE;
-  static_assert(STAGE % 1024 == 0, "ring stages must stay 1024-byte aligned for the swizzled TMA tiles");
+  constexpr int RBY = 16 * BITS;                      // code bytes per row per chunk
+  constexpr int XS = BITS == 4 ? 320 : 336;           // token row pitch in a stage
+  constexpr int W_BYTES = MAT * CTA_ROWS * RBY;
+  constexpr int STAGE = (W_BYTES + TILE * XS + 1023) / 1024 * 1024;
 
   extern __shared__ __align__(1024) uint8_t mma_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mma_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -385,13 +445,13 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       if (!ok) break;
       uint8_t* st = smem + s * STAGE;
       if (lane == 0) {
-        tma_load_2d(st, &tm0, h * 16, wrow, &full[s]);
-        if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * 64, &tm1, h * 16, wrow, &full[s]);
+        tma_load_2d(st, &tm0, h * (4 * BITS), wrow, &full[s]);
+        if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, h * (4 * BITS), wrow, &full[s]);
       }
 #pragma unroll
       for (int u = 0; u < XPL; ++u) {
         const int tk = lane + 32 * u;
-        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * MMA_XSTRIDE, xrow[u] + int64_t(h) * 128, 256u, &full[s]);
+        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * XS, xrow[u] + int64_t(h) * 128, 256u, &full[s]);
       }
       if (++s == S) {
         s = 0;
@@ -408,40 +468,41 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
 
   if constexpr (SH::NTMAX == 2) {
     if (cnt <= 8) {
-      mma_consume<MAT, 1, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     } else {
-      mma_consume<MAT, 2, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     }
   } else {
-    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
+    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
                                                   expert, begin, cnt, row_base, h0, h1, warp, lane);
   }
   if (lane == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
 }
 
-// 4-bit code rows as a 2-D uint32 tensor [rows, K/8]; box = one 128-wide K
-// chunk (16 words = 64 bytes) of `box_rows` rows, 64B-swizzled.
-static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int box_rows) {
-  const cuuint64_t words = cuuint64_t(K / 8);
+// Code rows as a 2-D uint32 tensor [rows, K*bits/32]; box = one 128-wide K
+// chunk (4-bit: 16 words = 64 bytes, 64B swizzle; 2-bit: 8 words = 32
+// bytes, 32B swizzle) of `box_rows` rows.
+static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows, int64_t K, int box_rows,
+                               int bits = 4) {
+  const cuuint64_t words = cuuint64_t(K * bits / 32);
   const cuuint64_t dims[2] = {words, cuuint64_t(rows)};
   const cuuint64_t strides[1] = {words * 4};
-  const cuuint32_t box[2] = {16u, cuuint32_t(box_rows)};
+  const cuuint32_t box[2] = {cuuint32_t(4 * bits), cuuint32_t(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(w), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, bits == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
 }
 
-template <int MAT, bool XPLAN, int TILE>
+template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false>
 static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, int64_t E, int64_t slots_grid,
                           int ksplit, cudaStream_t st) {
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
-  constexpr int STAGE = MAT * CTA_ROWS * 64 + TILE * MMA_XSTRIDE;
-  static_assert(STAGE % 1024 == 0, "ring stages must stay 1024-byte aligned");
+  constexpr int STAGE = (MAT * CTA_ROWS * 16 * BITS + TILE * (BITS == 4 ? 320 : 336) + 1023) / 1024 * 1024;
   // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
   // of it reserved per CTA)
   int S = 8;
@@ -449,15 +510,15 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   p.stages = S;
   const int smem = S * STAGE + 1024 + 256;
   CUtensorMap m0{}, m1{};
-  int rc = make_mma_weight_map(&m0, w0, E * p.N, p.K, CTA_ROWS);
+  int rc = make_mma_weight_map(&m0, w0, E * p.N, p.K, CTA_ROWS, BITS);
   if (rc != B2F_OK) return rc;
   if (w1) {
-    rc = make_mma_weight_map(&m1, w1, E * p.N, p.K, CTA_ROWS);
+    rc = make_mma_weight_map(&m1, w1, E * p.N, p.K, CTA_ROWS, BITS);
     if (rc != B2F_OK) return rc;
   } else {
     m1 = m0;
   }
-  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE>;
+  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -608,4 +669,57 @@ extern "C" int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, 
   p.partial = partial;
   p.plane = A * N;
   return launch_mma_cfg<1, false, 16>(p, w, nullptr, E, max_slots, ks, as_stream(stream));
+}
+
+extern "C" int b2f_gather_qgemm_2bit_mma(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div,
+                                         int64_t A, int64_t E, const uint32_t* w_gate, const void* s_gate,
+                                         const void* b_gate, const uint32_t* w_up, const void* s_up,
+                                         const void* b_up, int64_t N, int64_t K, int scale_dtype, int tile,
+                                         void* plan_workspace, int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                         void* stream) {
+  if (!(scale_dtype == B2F_BF16 || scale_dtype == B2F_F16)) return B2F_ERR_UNSUPPORTED;
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0 || tile != 16) return B2F_ERR_UNSUPPORTED;
+  if (A < 0 || E <= 0) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x || !w_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
+  if (w_up && (!s_up || !b_up)) return B2F_ERR_INVALID;
+  if (!x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
+  if (ldx < K || ldo < N) return B2F_ERR_INVALID;
+  if (E * N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(w_gate, 16) || (w_up && !aligned(w_up, 16)) || !aligned(out, 4) ||
+      ldo % 2 != 0 || !aligned(s_gate, 4) || !aligned(b_gate, 4) || (w_up && (!aligned(s_up, 4) || !aligned(b_up, 4))))
+    return B2F_ERR_ALIGN;
+  const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
+  if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
+  const int64_t max_slots = b2f_moe_plan_max_slots(A, E, tile);
+  if (max_slots > 65535) return B2F_ERR_UNSUPPORTED;
+  int rc = get_encoder();
+  if (rc != B2F_OK) return rc;
+  char* ws = static_cast<char*>(plan_workspace);
+  MmaParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.x_row_index = x_row_index;
+  p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
+  p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
+  p.s[1] = static_cast<const __nv_bfloat16*>(s_up);
+  p.b[1] = static_cast<const __nv_bfloat16*>(b_up);
+  p.N = N;
+  p.K = K;
+  p.G = int(K / 64);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.slot_count = reinterpret_cast<const int32_t*>(ws);
+  p.err = reinterpret_cast<int32_t*>(ws) + 1;
+  p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
+  p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
+  p.cpk = int(K / 128);
+  cudaStream_t st = as_stream(stream);
+  const bool f16 = scale_dtype == B2F_F16;
+  if (w_up)
+    return f16 ? launch_mma_cfg<2, false, 16, 2, true>(p, w_gate, w_up, E, max_slots, 1, st)
+               : launch_mma_cfg<2, false, 16, 2, false>(p, w_gate, w_up, E, max_slots, 1, st);
+  return f16 ? launch_mma_cfg<1, false, 16, 2, true>(p, w_gate, nullptr, E, max_slots, 1, st)
+             : launch_mma_cfg<1, false, 16, 2, false>(p, w_gate, nullptr, E, max_slots, 1, st);
 }

@@ -128,3 +128,59 @@ def test_mma_splitk_partials(dev, A, E, N, K, ksplit):
     deq = [affine.dequantize_f32(w[0][e], w[1][e], w[2][e], 64, 4).astype(np.float64) for e in range(E)]
     want = np.stack([deq[eid[a]] @ x[a].astype(np.float64) for a in range(A)])
     assert_close(to_np(parts.sum(0)), want, what=f"mma split-K A={A} E={E} N={N} K={K} ks={ksplit}")
+
+
+def _two_bit(rng, E, N, K):
+    """Experts quantized to 4 bits, then requantized to the 2-bit cold-expert
+    format by the oracle restatement of requantize_4bit_to_2bit."""
+    from oracle import mixed
+    w = round_to(rng.normal(0, 0.02, (E, N, K)).astype(np.float32), "bf16")
+    wq, s, b = affine.quantize(w, 64, 4)
+    packed, s2, b2 = zip(*(mixed.requantize_4bit_to_2bit(wq[e], s[e], b[e]) for e in range(E)))
+    packed, s2, b2 = np.stack(packed), np.stack(s2), np.stack(b2)
+    deq = [mixed.dequantize_2bit(packed[e], s2[e], b2[e], K).astype(np.float64) for e in range(E)]
+    return packed, s2, b2, deq
+
+
+@pytest.mark.parametrize("sdt", ["f16", "bf16"])
+def test_mma_2bit_swiglu_and_down(dev, sdt):
+    """2-bit codes (the requantized cold-expert format): SwitchGLU front half
+    then down, vs float64 products of the oracle's dequantized 2-bit weights
+    (bf16 scale variant: the same codes with bf16-rounded scales/biases)."""
+    from oracle import mixed
+    rng = np.random.default_rng(21)
+    T, k, E, H, I = 24, 4, 8, 1024, 384
+    gp, gs, gb, gdq = _two_bit(rng, E, I, H)
+    up, us, ub, udq = _two_bit(rng, E, I, H)
+    dp, ds, db, ddq = _two_bit(rng, E, H, I)
+    if sdt == "bf16":
+        rd = lambda a: round_to(a.astype(np.float32), "bf16")  # noqa: E731
+        gs, gb, us, ub, ds, db = (rd(a) for a in (gs, gb, us, ub, ds, db))
+        gdq = [mixed.dequantize_2bit(gp[e], gs[e], gb[e], H).astype(np.float64) for e in range(E)]
+        udq = [mixed.dequantize_2bit(up[e], us[e], ub[e], H).astype(np.float64) for e in range(E)]
+        ddq = [mixed.dequantize_2bit(dp[e], ds[e], db[e], I).astype(np.float64) for e in range(E)]
+    tdt = torch.float16 if sdt == "f16" else torch.bfloat16
+
+    def dev3(p, s, b):
+        w = torch.from_numpy(np.ascontiguousarray(p)).to(dev).view(torch.int32).view(torch.uint32)
+        sv = torch.from_numpy(np.asarray(s, np.float32)).to(dev).to(tdt)
+        bv = torch.from_numpy(np.asarray(b, np.float32)).to(dev).to(tdt)
+        return w, sv, bv
+
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    inds = _routing(rng, T, k, E)
+    plan = mx_compat.MoEPlan(torch.from_numpy(inds.reshape(-1)).to(dev), E, 16)
+    h = mx_compat.gather_qmm_2bit_planned(to_dev(x, "bf16", dev), plan, *dev3(gp, gs, gb), x_row_div=k,
+                                          up=dev3(up, us, ub))
+    y = mx_compat.gather_qmm_2bit_planned(h, plan, *dev3(dp, ds, db), x_row_div=1)
+    plan.check()
+    xs = x.astype(np.float64)
+    want_h = np.zeros((T * k, I))
+    for a in range(T * k):
+        e = inds.reshape(-1)[a]
+        g, u = gdq[e] @ xs[a // k], udq[e] @ xs[a // k]
+        want_h[a] = g / (1 + np.exp(-g)) * u
+    assert_close(to_np(h), want_h, what=f"2-bit swiglu ({sdt} scales)")
+    hh = to_np(h).astype(np.float64)
+    want_y = np.stack([ddq[inds.reshape(-1)[a]] @ hh[a] for a in range(T * k)])
+    assert_close(to_np(y), want_y, what=f"2-bit down ({sdt} scales)")
