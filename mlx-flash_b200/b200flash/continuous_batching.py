@@ -1,20 +1,29 @@
-"""Batched continuous decoding over the quantized decode step.
+"""Batched continuous decoding with chunked prefill over the quantized decode step.
 
 The reference engine (``mlx_flash_compress/continuous_batching.py:337-668``:
 ``InferenceRequest``, ``BatchScheduler``, ``ContinuousBatchingEngine``) runs
 every request on its own forward pass (``_batch_step`` loops over the batch,
-``:532-554``).  Here all active requests share one decode step of the
-B-slot decoder (``decoder.Qwen3MoeDecoder``, one CUDA graph per step): each
-slot holds one request; a request in its prompt phase feeds its next prompt
-token through the step (prefill by decode, the KV rows land in its pages),
-one in its generating phase feeds back its sampled token.  Requests join free
-slots and leave at step boundaries; a finished slot's pages are reused from
-position 0 by the next request.  Sampling is greedy (the step's fused
-argmax); ``temperature`` other than 0 is rejected.
+``:532-554``; ``_prefill_step`` pushes a prompt chunk with a causal mask,
+``:556-580``).  Here all active requests share one step of the B-row decoder
+(``decoder.Qwen3MoeDecoder``, one CUDA graph per step).  A row is one query
+token with its own position and its own block-table row, so rows of one step
+can belong to different requests or to the same one:
 
-Per-token results do not depend on the other slots (the MoE plan only groups
+* a generating request takes one row (its last sampled token);
+* a prompting request takes up to ``prefill_chunk`` rows for its next prompt
+  tokens, all pointing at its pages with consecutive positions.  Within a
+  layer the KV rows of every row are appended before attention runs, and the
+  attention of row i reads positions 0..i of its sequence, which is the
+  causal mask of a chunked prefill, with no separate prefill kernel.
+
+Each request owns one region of ``max_pages`` pages (region r = the block
+table row r of the decoder's initial layout) from admission to completion;
+idle rows point at a region no request owns.  Sampling is greedy (the step's
+fused argmax); ``temperature`` other than 0 is rejected.
+
+Per-token results do not depend on the other rows (the MoE plan only groups
 tokens by expert; attention, projections and sampling are per token), so a
-request's tokens are the same alone or batched.
+request's tokens are the same alone or batched, and with any prefill chunk.
 """
 
 import itertools
@@ -50,8 +59,9 @@ class InferenceRequest:
     created_at: float = field(default_factory=time.time)
     first_token_at: Optional[float] = None
     completed_at: Optional[float] = None
-    _slot: int = -1
+    _slot: int = -1  # page region owned while active
     _prefill_pos: int = 0
+    _last: int = 0  # token to feed when generating
 
     @property
     def ttft_ms(self) -> float:
@@ -76,6 +86,7 @@ class InferenceRequest:
 class BatchSchedulerConfig:
     max_batch_size: int = 64
     max_queue_size: int = 1024
+    prefill_chunk_size: int = 16  # prompt tokens a request may push through one step
 
 
 class BatchScheduler:
@@ -123,14 +134,18 @@ class BatchScheduler:
 
 
 class ContinuousBatchingEngine:
-    """Slot-based continuous batching over a ``Qwen3MoeDecoder`` (greedy decoding)."""
+    """Continuous batching with chunked prefill over a ``Qwen3MoeDecoder`` (greedy decoding)."""
 
     def __init__(self, decoder, config: Optional[BatchSchedulerConfig] = None, use_graph: bool = True):
         self.dec = decoder
         self.B = decoder.B
-        self.scheduler = BatchScheduler(config or BatchSchedulerConfig(max_batch_size=decoder.B))
-        self.slots = [None] * self.B
+        self.config = config or BatchSchedulerConfig(max_batch_size=decoder.B)
+        self.scheduler = BatchScheduler(self.config)
+        self.slots = [None] * self.B  # page region -> request
         self.max_context = (decoder.max_pages - 1) * decoder.page
+        mp = decoder.max_pages
+        self._regions = torch.arange(self.B * mp, dtype=torch.int32).reshape(self.B, mp)
+        self._bt = torch.zeros(self.B, mp, dtype=torch.int32).pin_memory()
         self._tok = torch.zeros(self.B, dtype=torch.int32).pin_memory()
         self._pos = torch.zeros(self.B, dtype=torch.int32).pin_memory()
         self._next = torch.zeros(self.B, dtype=torch.int32).pin_memory()
@@ -166,15 +181,14 @@ class ContinuousBatchingEngine:
                     return
                 req._slot = b
                 req.status = RequestStatus.PREFILLING
-                req._prefill_pos = 1
+                req._prefill_pos = 0
                 self.slots[b] = req
-                self._tok[b] = req.prompt_tokens[0]
-                self._pos[b] = 0
 
     def _run_step(self):
         dec = self.dec
         dec.tokens.copy_(self._tok, non_blocking=True)
         dec.positions.copy_(self._pos, non_blocking=True)
+        dec.block_table.copy_(self._bt, non_blocking=True)
         if self._use_graph:
             if self._graph is None:
                 side = torch.cuda.Stream(dec.dev)
@@ -184,6 +198,7 @@ class ContinuousBatchingEngine:
                 torch.cuda.current_stream(dec.dev).wait_stream(side)
                 dec.tokens.copy_(self._tok, non_blocking=True)
                 dec.positions.copy_(self._pos, non_blocking=True)
+                dec.block_table.copy_(self._bt, non_blocking=True)
                 self._graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(self._graph):
                     dec.step()
@@ -194,42 +209,69 @@ class ContinuousBatchingEngine:
         torch.cuda.current_stream(dec.dev).synchronize()
 
     def step(self) -> int:
-        """Admit waiting requests, run one batched decode step, advance every
-        active request.  Returns the number of active requests this step."""
+        """Admit waiting requests, assign this step's rows (one per generating
+        request, then prompt chunks), run one batched step, advance every
+        request that had rows.  Returns the number of rows used."""
         for b, req in enumerate(self.slots):
             if req is not None and req.status == RequestStatus.CANCELLED:
+                req._slot = -1
                 self.slots[b] = None
         self._admit()
-        active = [b for b in range(self.B) if self.slots[b] is not None]
+        active = [r for r in self.slots if r is not None]
         if not active:
             return 0
-        for b in range(self.B):
-            if self.slots[b] is None:  # idle slot: writes its own page 0, output ignored
-                self._tok[b] = 0
-                self._pos[b] = 0
+        rows = []  # (request, first prompt index or -1, count)
+        for req in active:
+            if req.is_prefill_done:
+                rows.append((req, -1, 1))
+        free = self.B - len(rows)
+        for req in active:
+            if not req.is_prefill_done and free > 0:
+                n = min(self.config.prefill_chunk_size, len(req.prompt_tokens) - req._prefill_pos, free)
+                rows.append((req, req._prefill_pos, n))
+                free -= n
+        idle_region = next((b for b in range(self.B) if self.slots[b] is None), None)
+        row = 0
+        owner = []
+        for req, p0, n in rows:
+            for i in range(n):
+                if p0 < 0:
+                    self._tok[row] = req._last
+                    self._pos[row] = len(req.prompt_tokens) + len(req.generated_tokens) - 1
+                else:
+                    self._tok[row] = req.prompt_tokens[p0 + i]
+                    self._pos[row] = p0 + i
+                self._bt[row] = self._regions[req._slot]
+                owner.append(req)
+                row += 1
+        used = row
+        for r in range(used, self.B):  # idle rows: position 0 of a region no request owns
+            self._tok[r] = 0
+            self._pos[r] = 0
+            self._bt[r] = self._regions[idle_region]
         self._run_step()
         self.steps += 1
         now = time.time()
-        for b in active:
-            req = self.slots[b]
-            self._pos[b] += 1
-            if not req.is_prefill_done:
-                self._tok[b] = req.prompt_tokens[req._prefill_pos]
-                req._prefill_pos += 1
-                continue
-            tok = int(self._next[b])
-            if req.status == RequestStatus.PREFILLING:
+        row = 0
+        for req, p0, n in rows:
+            last_row = row + n - 1
+            row += n
+            if p0 >= 0:
+                req._prefill_pos = p0 + n
+                if not req.is_prefill_done:
+                    continue
                 req.status = RequestStatus.GENERATING
                 req.first_token_at = now
+            tok = int(self._next[last_row])
             req.generated_tokens.append(tok)
+            req._last = tok
             self._total_generated += 1
-            self._tok[b] = tok
             if len(req.generated_tokens) >= req.max_tokens or (req.eos_token_id is not None and
                                                                  tok == req.eos_token_id):
                 self.scheduler.mark_completed(req.request_id)
+                self.slots[req._slot] = None
                 req._slot = -1
-                self.slots[b] = None
-        return len(active)
+        return used
 
     def run_until_idle(self, max_steps: int = 1 << 30):
         n = 0

@@ -1,10 +1,11 @@
 """GPU: continuous batching over the decode step -- requests joining and
-leaving slots, prompts fed through the batched step, greedy tokens identical
-to each request decoded alone."""
+leaving, prompts pushed through the batched step in chunks (rows of one
+request share its pages with consecutive positions), greedy tokens identical
+to each request decoded alone and for every chunk size."""
 
 import pytest
 
-from b200flash.continuous_batching import ContinuousBatchingEngine, RequestStatus
+from b200flash.continuous_batching import BatchSchedulerConfig, ContinuousBatchingEngine, RequestStatus
 from b200flash.decoder import Qwen3MoeDecoder, Qwen3MoeShape
 
 pytestmark = pytest.mark.gpu
@@ -16,13 +17,14 @@ def _decoder(dev):
     return Qwen3MoeDecoder(shape, max_batch=4, max_context=96, page_size=16, device=dev, seed=3)
 
 
-@pytest.mark.parametrize("use_graph", [True, False])
-def test_batched_equals_alone(dev, use_graph):
+@pytest.mark.parametrize("use_graph,chunk", [(True, 16), (False, 1), (True, 3)])
+def test_batched_equals_alone(dev, use_graph, chunk):
     dec = _decoder(dev)
     prompts = [[3, 14, 15], [9, 2, 6, 5, 3, 5, 8], [7], [1, 4, 1, 4, 2, 1, 3, 5, 6, 2, 3, 7], [27, 18, 28, 18, 28],
                [31, 41, 59, 26, 53, 58, 97, 93, 23]]
     max_toks = [5, 3, 8, 4, 6, 2]
-    eng = ContinuousBatchingEngine(dec, use_graph=use_graph)
+    cfg = BatchSchedulerConfig(max_batch_size=4, prefill_chunk_size=chunk)
+    eng = ContinuousBatchingEngine(dec, cfg, use_graph=use_graph)
     reqs = [eng.submit(p, max_tokens=m) for p, m in zip(prompts, max_toks)]
     eng.run_until_idle()
     assert all(r.status == RequestStatus.COMPLETED for r in reqs)
@@ -31,7 +33,8 @@ def test_batched_equals_alone(dev, use_graph):
     assert st["completed"] == 6 and st["active"] == 0 and st["total_generated"] == sum(max_toks)
     # six requests through four slots: later requests reused finished slots
     for p, m, r in zip(prompts, max_toks, reqs):
-        alone = ContinuousBatchingEngine(dec, use_graph=use_graph)
+        alone = ContinuousBatchingEngine(dec, BatchSchedulerConfig(max_batch_size=4, prefill_chunk_size=1),
+                                         use_graph=False)
         a = alone.submit(p, max_tokens=m)
         alone.run_until_idle()
         assert a.generated_tokens == r.generated_tokens, (p, a.generated_tokens, r.generated_tokens)
