@@ -6,7 +6,6 @@ import numpy as np
 import pytest
 import torch
 
-from b200flash import mx_compat
 from b200flash.expert_streaming import CachedSwitchLinear, ResidentExpertCache
 from b200flash.kv_cache_backend import HybridKVCache, PlainKVCache, QuantizedKVCache, StreamingKVCache
 from oracle import affine, kv_sym

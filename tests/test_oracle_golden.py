@@ -1,6 +1,5 @@
 """The CPU oracle against the golden vectors generated from the reference's own code."""
 
-import json
 import os
 
 import numpy as np
@@ -9,7 +8,6 @@ import pytest
 from oracle import affine, kv_sym, mixed
 from oracle.fp import round_bf16, round_f16
 
-from conftest import GOLDEN
 
 
 def _kv_cases(golden):
