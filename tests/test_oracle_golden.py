@@ -9,7 +9,6 @@ from oracle import affine, kv_sym, mixed
 from oracle.fp import round_bf16, round_f16
 
 
-
 def _kv_cases(golden):
     z = golden("kv_sym.npz")
     for entry in z["__cases__"]:
