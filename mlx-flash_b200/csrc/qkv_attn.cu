@@ -521,6 +521,346 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
   }
 }
 
+// 8x8 transpose of 16-bit elements across the warp: lane (r, c) holds
+// elements (r, 2c), (r, 2c+1) before and (2c, r), (2c+1, r) after.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(x));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// Token-row form for 8-bit codes, D = 128, G <= 8, head-major pages (the
+// decode shape of the grouped-query models here).  The MMA's M side is 16
+// tokens and its N side the G query heads of the KV head, so with G = 8 no
+// MMA row is padding (the form above fills 8 of its 16 rows):
+//   S^T = K.Q^T    A = K codes as fp16 1024+code (one prmt per two codes),
+//                  B = q^T (fp16, pre-scaled by softmax_scale*log2(e));
+//                  per 64-wide group s = kscale*(acc - (1024+127)*sum(q))
+//   online softmax per head over the 8 lanes sharing its column
+//   P' = P*vscale  per token and group, moved into the B layout of the next
+//                  MMA with one 8x8 transpose per 8 tokens
+//   O^T += V^T.P'^T  A = V codes as fp16 1024+code (two tokens per register),
+//                  plus one MMA of an all-ones A per group that accumulates
+//                  sum(P'); O = acc - (1024+127)*sum(P') at the end.
+// Inside each 8-token half, MMA row i is page row sigma(i) (sigma = 0 6 1 7
+// 4 2 5 3): with the 128B swizzle of the page tiles that makes every K and V
+// fragment read of a warp hit 32 distinct banks.  The page ring, the
+// 4-warp merge and the split partials are those of the kernel above.
+template <int D>
+__global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnParams p,
+                                                                    const __grid_constant__ CUtensorMap tmk,
+                                                                    const __grid_constant__ CUtensorMap tmv) {
+  static_assert(D == 128, "token-row form: 128-byte code rows");
+  constexpr int DG = D / 64;  // quantization groups per row
+  constexpr int RB = D;       // bytes per 8-bit code row
+  constexpr float KOFF = 1024.f + 127.f;
+  constexpr uint32_t SIGMA = 0x35247160u;  // nibble i = page row of MMA row i (mod 8)
+
+  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int G = p.G;
+  const int len = p.seq_lens[b];
+  const int n_sub = (len + 15) / 16;
+  const int per_split = (n_sub + p.n_splits - 1) / p.n_splits;
+  const int sub_begin = split * per_split;
+  const int sub_end = min(n_sub, sub_begin + per_split);
+
+  const int sg = (SIGMA >> (4 * g)) & 7;        // page row of MMA rows g (and 8+sg of g+8)
+  const int sv0 = (SIGMA >> (8 * c)) & 7;       // page row of token 2c (B side of P.V)
+  const int sv1 = (SIGMA >> (8 * c + 4)) & 7;   // page row of token 2c+1
+  // byte offsets inside a swizzled code row: K (16 bytes, dims 64grp+16c..)
+  // for rows sg / 8+sg; V (8 bytes, dims 64grp+vdim(g)..) for rows sv0 / sv1
+  const int vdim = 32 * ((g >> 1) & 1) + 16 * (g >> 2) + 8 * (g & 1);
+  int kcol[DG], vcol0[DG], vcol1[DG];
+#pragma unroll
+  for (int grp = 0; grp < DG; ++grp) {
+    kcol[grp] = (((4 * grp) | c) ^ sg) << 4;
+    const int ch = (64 * grp + vdim) >> 4;
+    vcol0[grp] = ((ch ^ sv0) << 4) + 8 * (g & 1);
+    vcol1[grp] = ((ch ^ sv1) << 4) + 8 * (g & 1);
+  }
+
+  // ---- q^T fragments (head g, dims 64grp+16c+[0,16)) and (1024+127)*sum(q)
+  uint32_t qb[DG * 4][2];
+  float kq[2][DG];  // heads 2c, 2c+1
+  {
+    const bool hv = g < G;
+    const __nv_bfloat16* qrow = p.q + (int64_t(b) * p.Hq + int64_t(hkv) * G + g) * D;
+#pragma unroll
+    for (int grp = 0; grp < DG; ++grp) {
+      float v[16];
+      if (hv) {
+        const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * grp + 16 * c);
+        const uint4 a = src[0], bb = src[1];
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+          v[2 * i] = round_f16(__low2float(h) * p.qscale);
+          v[2 * i + 1] = round_f16(__high2float(h) * p.qscale);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = 0.f;
+      }
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) part += v[i];
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+#pragma unroll
+      for (int st = 0; st < 4; ++st) {
+        qb[grp * 4 + st][0] = pack_f16x2(v[4 * st], v[4 * st + 1]);
+        qb[grp * 4 + st][1] = pack_f16x2(v[4 * st + 2], v[4 * st + 3]);
+      }
+      kq[0][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c);
+      kq[1][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c + 4);
+    }
+  }
+
+  float oacc[DG * 4][4];
+  float oone[DG][4];
+#pragma unroll
+  for (int j = 0; j < DG * 4; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oacc[j][i] = 0.f;
+#pragma unroll
+  for (int j = 0; j < DG; ++j)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oone[j][i] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};  // this lane's rows only; summed over the 8 row lanes at the end
+  const uint32_t ONE2 = 0x3C003C00u;
+  const uint32_t ones[4] = {ONE2, ONE2, ONE2, ONE2};
+
+  extern __shared__ __align__(1024) uint8_t attn_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(attn_smem + p.ring_bytes - 128);
+  uint64_t* empty = full + ATTN_RING;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + ATTN_RING);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ATTN_RING; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  const int spp = p.PS / 16;
+  const int pg0 = sub_begin / spp;
+  const int npg = sub_end > sub_begin ? (sub_end + spp - 1) / spp - pg0 : 0;
+  const int code_bytes = p.PS * RB, sc_bytes = p.PS * DG * 4;
+  if (warp == 4) {
+    if (lane == 0) {
+      int jj = 0;
+      for (; jj < npg; ++jj) {
+        const int slot = jj % ATTN_RING;
+        if (jj >= ATTN_RING && !mbar_wait_bounded(&empty[slot], uint32_t(((jj / ATTN_RING) - 1) & 1))) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const int page = p.block_table[int64_t(b) * p.max_pages + pg0 + jj];
+        const int64_t rowbase = (int64_t(page) * p.Hkv + hkv) * p.PS;
+        uint8_t* sb = attn_smem + slot * p.slot_bytes;
+        mbar_arrive_expect_tx(&full[slot], uint32_t(2 * code_bytes + 2 * sc_bytes));
+        tma_load_2d(sb, &tmk, 0, int(rowbase), &full[slot]);
+        tma_load_2d(sb + code_bytes, &tmv, 0, int(rowbase), &full[slot]);
+        bulk_g2s(sb + 2 * code_bytes, p.ks + rowbase * DG, uint32_t(sc_bytes), &full[slot]);
+        bulk_g2s(sb + 2 * code_bytes + sc_bytes, p.vs + rowbase * DG, uint32_t(sc_bytes), &full[slot]);
+      }
+      // copies already issued land before the CTA goes away
+      for (int k = 1; k <= ATTN_RING && jj - k >= 0; ++k)
+        mbar_wait_bounded(&full[(jj - k) % ATTN_RING], uint32_t(((jj - k) / ATTN_RING) & 1), 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    for (int jj = 0; jj < npg; ++jj) {
+      const int slot = jj % ATTN_RING;
+      const bool ok = !*abort_flag && mbar_wait_bounded(&full[slot], uint32_t((jj / ATTN_RING) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      const uint8_t* kb = attn_smem + slot * p.slot_bytes;
+      const uint8_t* vb = kb + code_bytes;
+      const float* ksb = reinterpret_cast<const float*>(kb + 2 * code_bytes);
+      const float* vsb = ksb + p.PS * DG;
+      const int s_lo = max(sub_begin, (pg0 + jj) * spp), s_hi = min(sub_end, (pg0 + jj + 1) * spp);
+      for (int sub = s_lo; sub < s_hi; ++sub) {
+        if (((sub - sub_begin) & 3) != warp) continue;
+        const int t0 = sub * 16;
+        const int lr = t0 % p.PS;  // first page row of the sub-tile (a multiple of 16)
+        const uint8_t* krow = kb + (lr + sg) * RB;
+        uint4 kw[2][DG];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int grp = 0; grp < DG; ++grp)
+            kw[h][grp] = *reinterpret_cast<const uint4*>(krow + h * 8 * RB + kcol[grp]);
+        uint2 vw[4][DG];  // tokens 2c, 2c+1, 2c+8, 2c+9
+#pragma unroll
+        for (int grp = 0; grp < DG; ++grp) {
+          vw[0][grp] = *reinterpret_cast<const uint2*>(vb + (lr + sv0) * RB + vcol0[grp]);
+          vw[1][grp] = *reinterpret_cast<const uint2*>(vb + (lr + sv1) * RB + vcol1[grp]);
+          vw[2][grp] = *reinterpret_cast<const uint2*>(vb + (lr + 8 + sv0) * RB + vcol0[grp]);
+          vw[3][grp] = *reinterpret_cast<const uint2*>(vb + (lr + 8 + sv1) * RB + vcol1[grp]);
+        }
+        bool valid[2];
+        float ksc[2][DG], vsc[2][DG];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = lr + 8 * h + sg;
+          valid[h] = t0 + 8 * h + sg < len;
+          const float2 kk = *reinterpret_cast<const float2*>(ksb + row * DG);
+          const float2 vv = *reinterpret_cast<const float2*>(vsb + row * DG);
+          ksc[h][0] = kk.x;
+          ksc[h][1] = kk.y;
+          vsc[h][0] = valid[h] ? vv.x : 0.f;
+          vsc[h][1] = valid[h] ? vv.y : 0.f;
+        }
+
+        // ---- S^T = K.Q^T ---------------------------------------------------
+        float sacc[DG][4];
+#pragma unroll
+        for (int grp = 0; grp < DG; ++grp) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sacc[grp][i] = 0.f;
+          const uint32_t k0[4] = {kw[0][grp].x, kw[0][grp].y, kw[0][grp].z, kw[0][grp].w};
+          const uint32_t k1[4] = {kw[1][grp].x, kw[1][grp].y, kw[1][grp].z, kw[1][grp].w};
+#pragma unroll
+          for (int st = 0; st < 4; ++st) {
+            const uint32_t a[4] = {prmt(k0[st], 0x64646464u, 0x4140u), prmt(k1[st], 0x64646464u, 0x4140u),
+                                   prmt(k0[st], 0x64646464u, 0x4342u), prmt(k1[st], 0x64646464u, 0x4342u)};
+            mma_f16_16816(sacc[grp], a, qb[grp * 4 + st]);
+          }
+        }
+        float s[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int h = i >> 1, e = i & 1;
+          float v = 0.f;
+#pragma unroll
+          for (int grp = 0; grp < DG; ++grp) v += ksc[h][grp] * (sacc[grp][i] - kq[e][grp]);
+          s[i] = valid[h] ? v : -INFINITY;
+        }
+
+        // ---- online softmax (heads 2c, 2c+1 over the 8 lanes of a column) --
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float mt = fmaxf(s[e], s[2 + e]);
+          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+          const float mnew = fmaxf(m_run[e], mt);
+          const bool none = (mnew == -INFINITY);
+          const float alpha = none ? 1.f : exp2f(m_run[e] - mnew);
+          pr[e] = none ? 0.f : exp2f(s[e] - mnew);
+          pr[2 + e] = none ? 0.f : exp2f(s[2 + e] - mnew);
+          l_run[e] = l_run[e] * alpha + (pr[e] + pr[2 + e]);
+          m_run[e] = mnew;
+#pragma unroll
+          for (int j = 0; j < DG * 4; ++j) {
+            oacc[j][e] *= alpha;
+            oacc[j][2 + e] *= alpha;
+          }
+#pragma unroll
+          for (int j = 0; j < DG; ++j) {
+            oone[j][e] *= alpha;
+            oone[j][2 + e] *= alpha;
+          }
+        }
+
+        // ---- O^T += V^T.P'^T ------------------------------------------------
+#pragma unroll
+        for (int grp = 0; grp < DG; ++grp) {
+          const uint32_t xlo = pack_f16x2(pr[0] * vsc[0][grp], pr[1] * vsc[0][grp]);
+          const uint32_t xhi = pack_f16x2(pr[2] * vsc[1][grp], pr[3] * vsc[1][grp]);
+          const uint32_t bp[2] = {movmatrix_trans(xlo), movmatrix_trans(xhi)};
+          mma_f16_16816(oone[grp], ones, bp);
+#pragma unroll
+          for (int jl = 0; jl < 4; ++jl) {
+            const int bs = 2 * (jl & 1);
+            const uint32_t sel_lo = uint32_t(bs | (bs << 4) | ((4 + bs) << 8) | ((4 + bs) << 12));
+            const uint32_t sel_hi = sel_lo + 0x1111u;
+            const uint32_t w0 = (jl >> 1) ? vw[0][grp].y : vw[0][grp].x;
+            const uint32_t w1 = (jl >> 1) ? vw[1][grp].y : vw[1][grp].x;
+            const uint32_t w2 = (jl >> 1) ? vw[2][grp].y : vw[2][grp].x;
+            const uint32_t w3 = (jl >> 1) ? vw[3][grp].y : vw[3][grp].x;
+            const uint32_t a[4] = {and_or(prmt(w0, w1, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                   and_or(prmt(w0, w1, sel_hi), 0x00FF00FFu, 0x64006400u),
+                                   and_or(prmt(w2, w3, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                   and_or(prmt(w2, w3, sel_hi), 0x00FF00FFu, 0x64006400u)};
+            mma_f16_16816(oacc[grp * 4 + jl], a, bp);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+  }
+
+  // ---- merge the 4 warps through shared memory -----------------------------
+  float* sm = reinterpret_cast<float*>(attn_smem + p.ring_bytes);
+  float* sm_o = sm;               // [4][G][D]
+  float* sm_ml = sm + 4 * G * D;  // [4][G][2]
+  if (warp < 4) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float l = l_run[e];
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      const int head = 2 * c + e;
+      if (head < G) {
+        if (g == 0) {
+          sm_ml[(warp * G + head) * 2 + 0] = m_run[e];
+          sm_ml[(warp * G + head) * 2 + 1] = l;
+        }
+#pragma unroll
+        for (int j = 0; j < DG * 4; ++j) {
+          const int grp = j >> 2, jl = j & 3;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int d = 64 * grp + vdim + 2 * jl + h;
+            sm_o[(warp * G + head) * D + d] = oacc[j][2 * h + e] - KOFF * oone[grp][2 * h + e];
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int hq0 = hkv * G;
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int head = idx / D, d = idx % D;
+    float mstar = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mstar = fmaxf(mstar, sm_ml[(w * G + head) * 2]);
+    float o = 0.f, l = 0.f;
+    if (mstar != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float f = exp2f(sm_ml[(w * G + head) * 2] - mstar);
+        o += f * sm_o[(w * G + head) * D + d];
+        l += f * sm_ml[(w * G + head) * 2 + 1];
+      }
+    }
+    const int64_t bh = int64_t(b) * p.Hq + hq0 + head;
+    if (p.n_splits == 1) {
+      p.out[bh * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+    } else {
+      p.o_part[(bh * p.n_splits + split) * D + d] = o;
+      if (d == 0) {
+        p.ml_part[(bh * p.n_splits + split) * 2 + 0] = mstar;
+        p.ml_part[(bh * p.n_splits + split) * 2 + 1] = l;
+      }
+    }
+  }
+}
+
 __global__ void attn_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part,
                                     int n_splits, int D, __nv_bfloat16* __restrict__ out) {
   const int64_t bh = blockIdx.x;
@@ -580,6 +920,9 @@ static int launch_attn(AttnParams p, cudaStream_t st) {
   auto kern = qkv_decode_attn_kernel<BITS, D, false>;
   if constexpr (RING_OK) {
     if (ring) kern = qkv_decode_attn_kernel<BITS, D, true>;
+  }
+  if constexpr (BITS == 8 && D == 128) {
+    if (ring && p.G <= 8) kern = qkv_decode_attn_t8_kernel<D>;
   }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

@@ -146,7 +146,8 @@ def _paged_case(dev, rng, B, lens, Hq, Hkv, D, bits, page):
 
 
 @pytest.mark.parametrize("bits", [2, 4, 8])
-@pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (32, 4, 128), (8, 8, 64), (16, 2, 256)])
+@pytest.mark.parametrize("Hq,Hkv,D", [(32, 8, 128), (32, 4, 128), (24, 4, 128), (8, 8, 128), (8, 8, 64),
+                                         (16, 2, 256)])
 def test_decode_attention_paged(dev, bits, Hq, Hkv, D):
     rng = np.random.default_rng(bits * 1000 + Hq + D)
     lens = [1, 17, 300, 1000]
