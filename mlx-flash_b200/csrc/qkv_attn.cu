@@ -547,7 +547,17 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 // 4 2 5 3): with the 128B swizzle of the page tiles that makes every K and V
 // fragment read of a warp hit 32 distinct banks.  The page ring, the
 // 4-warp merge and the split partials are those of the kernel above.
-template <int D>
+// ex2.approx.ftz: 2^x (-inf gives +0), the softmax exponential in base 2
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// NT = 16-token tiles a warp takes per step (2 when the pages hold an even
+// number of tiles): the tiles' MMA chains, loads and conversions interleave,
+// and the softmax max and the O rescale are paid once per NT tiles.
+template <int D, int NT>
 __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnParams p,
                                                                     const __grid_constant__ CUtensorMap tmk,
                                                                     const __grid_constant__ CUtensorMap tmv) {
@@ -567,19 +577,19 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
   const int sub_begin = split * per_split;
   const int sub_end = min(n_sub, sub_begin + per_split);
 
-  const int sg = (SIGMA >> (4 * g)) & 7;        // page row of MMA rows g (and 8+sg of g+8)
-  const int sv0 = (SIGMA >> (8 * c)) & 7;       // page row of token 2c (B side of P.V)
-  const int sv1 = (SIGMA >> (8 * c + 4)) & 7;   // page row of token 2c+1
+  const int sg = (SIGMA >> (4 * g)) & 7;       // page row of MMA rows g (and 8+sg of g+8)
+  const int sv0 = (SIGMA >> (8 * c)) & 7;      // page row of token 2c (B side of P.V)
+  const int sv1 = (SIGMA >> (8 * c + 4)) & 7;  // page row of token 2c+1
   // byte offsets inside a swizzled code row: K (16 bytes, dims 64grp+16c..)
   // for rows sg / 8+sg; V (8 bytes, dims 64grp+vdim(g)..) for rows sv0 / sv1
   const int vdim = 32 * ((g >> 1) & 1) + 16 * (g >> 2) + 8 * (g & 1);
   int kcol[DG], vcol0[DG], vcol1[DG];
 #pragma unroll
   for (int grp = 0; grp < DG; ++grp) {
-    kcol[grp] = (((4 * grp) | c) ^ sg) << 4;
+    kcol[grp] = sg * RB + ((((4 * grp) | c) ^ sg) << 4);
     const int ch = (64 * grp + vdim) >> 4;
-    vcol0[grp] = ((ch ^ sv0) << 4) + 8 * (g & 1);
-    vcol1[grp] = ((ch ^ sv1) << 4) + 8 * (g & 1);
+    vcol0[grp] = sv0 * RB + ((ch ^ sv0) << 4) + 8 * (g & 1);
+    vcol1[grp] = sv1 * RB + ((ch ^ sv1) << 4) + 8 * (g & 1);
   }
 
   // ---- q^T fragments (head g, dims 64grp+16c+[0,16)) and (1024+127)*sum(q)
@@ -657,7 +667,8 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
       int jj = 0;
       for (; jj < npg; ++jj) {
         const int slot = jj % ATTN_RING;
-        if (jj >= ATTN_RING && !mbar_wait_bounded(&empty[slot], uint32_t(((jj / ATTN_RING) - 1) & 1))) {
+        if (jj >= ATTN_RING &&
+            !mbar_wait_bounded_backoff(&empty[slot], uint32_t(((jj / ATTN_RING) - 1) & 1))) {
           *abort_flag = 1;
           break;
         }
@@ -689,78 +700,92 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
       const float* ksb = reinterpret_cast<const float*>(kb + 2 * code_bytes);
       const float* vsb = ksb + p.PS * DG;
       const int s_lo = max(sub_begin, (pg0 + jj) * spp), s_hi = min(sub_end, (pg0 + jj + 1) * spp);
-      for (int sub = s_lo; sub < s_hi; ++sub) {
-        if (((sub - sub_begin) & 3) != warp) continue;
-        const int t0 = sub * 16;
-        const int lr = t0 % p.PS;  // first page row of the sub-tile (a multiple of 16)
-        const uint8_t* krow = kb + (lr + sg) * RB;
-        uint4 kw[2][DG];
+      const int nstep = (s_hi - s_lo + NT - 1) / NT;
+      for (int k = 0; k < nstep; ++k) {
+        if (((jj * (spp / NT) + k) & 3) != warp) continue;
+        const int sub0 = s_lo + NT * k;
+        uint4 kw[NT][2][DG];
+        uint2 vw[NT][4][DG];  // tokens 2c, 2c+1, 2c+8, 2c+9
+        bool valid[NT][2];
+        float ksc[NT][2][DG], vsc[NT][2][DG];
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int t = 0; t < NT; ++t) {
+          const bool here = sub0 + t < s_hi;  // warp-uniform
+          const int t0 = (sub0 + t) * 16;
+          const int lr = here ? t0 % p.PS : 0;  // first page row of the tile (a multiple of 16)
+          const uint8_t* kt = kb + lr * RB;
+          const uint8_t* vt = vb + lr * RB;
 #pragma unroll
-          for (int grp = 0; grp < DG; ++grp)
-            kw[h][grp] = *reinterpret_cast<const uint4*>(krow + h * 8 * RB + kcol[grp]);
-        uint2 vw[4][DG];  // tokens 2c, 2c+1, 2c+8, 2c+9
+          for (int grp = 0; grp < DG; ++grp) {
+            kw[t][0][grp] = *reinterpret_cast<const uint4*>(kt + kcol[grp]);
+            kw[t][1][grp] = *reinterpret_cast<const uint4*>(kt + 8 * RB + kcol[grp]);
+            vw[t][0][grp] = *reinterpret_cast<const uint2*>(vt + vcol0[grp]);
+            vw[t][1][grp] = *reinterpret_cast<const uint2*>(vt + vcol1[grp]);
+            vw[t][2][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol0[grp]);
+            vw[t][3][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol1[grp]);
+          }
 #pragma unroll
-        for (int grp = 0; grp < DG; ++grp) {
-          vw[0][grp] = *reinterpret_cast<const uint2*>(vb + (lr + sv0) * RB + vcol0[grp]);
-          vw[1][grp] = *reinterpret_cast<const uint2*>(vb + (lr + sv1) * RB + vcol1[grp]);
-          vw[2][grp] = *reinterpret_cast<const uint2*>(vb + (lr + 8 + sv0) * RB + vcol0[grp]);
-          vw[3][grp] = *reinterpret_cast<const uint2*>(vb + (lr + 8 + sv1) * RB + vcol1[grp]);
-        }
-        bool valid[2];
-        float ksc[2][DG], vsc[2][DG];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int row = lr + 8 * h + sg;
-          valid[h] = t0 + 8 * h + sg < len;
-          const float2 kk = *reinterpret_cast<const float2*>(ksb + row * DG);
-          const float2 vv = *reinterpret_cast<const float2*>(vsb + row * DG);
-          ksc[h][0] = kk.x;
-          ksc[h][1] = kk.y;
-          vsc[h][0] = valid[h] ? vv.x : 0.f;
-          vsc[h][1] = valid[h] ? vv.y : 0.f;
+          for (int h = 0; h < 2; ++h) {
+            const int row = lr + 8 * h + sg;
+            valid[t][h] = here && t0 + 8 * h + sg < len;
+            const float2 kk = *reinterpret_cast<const float2*>(ksb + row * DG);
+            const float2 vv = *reinterpret_cast<const float2*>(vsb + row * DG);
+            ksc[t][h][0] = kk.x;
+            ksc[t][h][1] = kk.y;
+            vsc[t][h][0] = valid[t][h] ? vv.x : 0.f;
+            vsc[t][h][1] = valid[t][h] ? vv.y : 0.f;
+          }
         }
 
         // ---- S^T = K.Q^T ---------------------------------------------------
-        float sacc[DG][4];
+        float s[NT][4];
 #pragma unroll
-        for (int grp = 0; grp < DG; ++grp) {
+        for (int t = 0; t < NT; ++t) {
+          float sacc[DG][4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) sacc[grp][i] = 0.f;
-          const uint32_t k0[4] = {kw[0][grp].x, kw[0][grp].y, kw[0][grp].z, kw[0][grp].w};
-          const uint32_t k1[4] = {kw[1][grp].x, kw[1][grp].y, kw[1][grp].z, kw[1][grp].w};
+          for (int grp = 0; grp < DG; ++grp) {
 #pragma unroll
-          for (int st = 0; st < 4; ++st) {
-            const uint32_t a[4] = {prmt(k0[st], 0x64646464u, 0x4140u), prmt(k1[st], 0x64646464u, 0x4140u),
-                                   prmt(k0[st], 0x64646464u, 0x4342u), prmt(k1[st], 0x64646464u, 0x4342u)};
-            mma_f16_16816(sacc[grp], a, qb[grp * 4 + st]);
+            for (int i = 0; i < 4; ++i) sacc[grp][i] = 0.f;
+            const uint32_t k0[4] = {kw[t][0][grp].x, kw[t][0][grp].y, kw[t][0][grp].z, kw[t][0][grp].w};
+            const uint32_t k1[4] = {kw[t][1][grp].x, kw[t][1][grp].y, kw[t][1][grp].z, kw[t][1][grp].w};
+#pragma unroll
+            for (int st = 0; st < 4; ++st) {
+              const uint32_t a[4] = {prmt(k0[st], 0x64646464u, 0x4140u), prmt(k1[st], 0x64646464u, 0x4140u),
+                                     prmt(k0[st], 0x64646464u, 0x4342u), prmt(k1[st], 0x64646464u, 0x4342u)};
+              mma_f16_16816(sacc[grp], a, qb[grp * 4 + st]);
+            }
           }
-        }
-        float s[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int h = i >> 1, e = i & 1;
-          float v = 0.f;
+          for (int i = 0; i < 4; ++i) {
+            const int h = i >> 1, e = i & 1;
+            float v = 0.f;
 #pragma unroll
-          for (int grp = 0; grp < DG; ++grp) v += ksc[h][grp] * (sacc[grp][i] - kq[e][grp]);
-          s[i] = valid[h] ? v : -INFINITY;
+            for (int grp = 0; grp < DG; ++grp) v += ksc[t][h][grp] * (sacc[grp][i] - kq[e][grp]);
+            s[t][i] = valid[t][h] ? v : -INFINITY;
+          }
         }
 
         // ---- online softmax (heads 2c, 2c+1 over the 8 lanes of a column) --
-        float pr[4];
+        float pr[NT][4];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          float mt = fmaxf(s[e], s[2 + e]);
+          float mt = fmaxf(s[0][e], s[0][2 + e]);
+#pragma unroll
+          for (int t = 1; t < NT; ++t) mt = fmaxf(mt, fmaxf(s[t][e], s[t][2 + e]));
           mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
           mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
           mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
           const float mnew = fmaxf(m_run[e], mt);
           const bool none = (mnew == -INFINITY);
-          const float alpha = none ? 1.f : exp2f(m_run[e] - mnew);
-          pr[e] = none ? 0.f : exp2f(s[e] - mnew);
-          pr[2 + e] = none ? 0.f : exp2f(s[2 + e] - mnew);
-          l_run[e] = l_run[e] * alpha + (pr[e] + pr[2 + e]);
+          const float alpha = none ? 1.f : fast_exp2(m_run[e] - mnew);
+          float lsum = 0.f;
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            pr[t][e] = none ? 0.f : fast_exp2(s[t][e] - mnew);
+            pr[t][2 + e] = none ? 0.f : fast_exp2(s[t][2 + e] - mnew);
+            lsum += pr[t][e] + pr[t][2 + e];
+          }
+          l_run[e] = l_run[e] * alpha + lsum;
           m_run[e] = mnew;
 #pragma unroll
           for (int j = 0; j < DG * 4; ++j) {
@@ -776,25 +801,28 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
 
         // ---- O^T += V^T.P'^T ------------------------------------------------
 #pragma unroll
-        for (int grp = 0; grp < DG; ++grp) {
-          const uint32_t xlo = pack_f16x2(pr[0] * vsc[0][grp], pr[1] * vsc[0][grp]);
-          const uint32_t xhi = pack_f16x2(pr[2] * vsc[1][grp], pr[3] * vsc[1][grp]);
-          const uint32_t bp[2] = {movmatrix_trans(xlo), movmatrix_trans(xhi)};
-          mma_f16_16816(oone[grp], ones, bp);
+        for (int t = 0; t < NT; ++t) {
 #pragma unroll
-          for (int jl = 0; jl < 4; ++jl) {
-            const int bs = 2 * (jl & 1);
-            const uint32_t sel_lo = uint32_t(bs | (bs << 4) | ((4 + bs) << 8) | ((4 + bs) << 12));
-            const uint32_t sel_hi = sel_lo + 0x1111u;
-            const uint32_t w0 = (jl >> 1) ? vw[0][grp].y : vw[0][grp].x;
-            const uint32_t w1 = (jl >> 1) ? vw[1][grp].y : vw[1][grp].x;
-            const uint32_t w2 = (jl >> 1) ? vw[2][grp].y : vw[2][grp].x;
-            const uint32_t w3 = (jl >> 1) ? vw[3][grp].y : vw[3][grp].x;
-            const uint32_t a[4] = {and_or(prmt(w0, w1, sel_lo), 0x00FF00FFu, 0x64006400u),
-                                   and_or(prmt(w0, w1, sel_hi), 0x00FF00FFu, 0x64006400u),
-                                   and_or(prmt(w2, w3, sel_lo), 0x00FF00FFu, 0x64006400u),
-                                   and_or(prmt(w2, w3, sel_hi), 0x00FF00FFu, 0x64006400u)};
-            mma_f16_16816(oacc[grp * 4 + jl], a, bp);
+          for (int grp = 0; grp < DG; ++grp) {
+            const uint32_t xlo = pack_f16x2(pr[t][0] * vsc[t][0][grp], pr[t][1] * vsc[t][0][grp]);
+            const uint32_t xhi = pack_f16x2(pr[t][2] * vsc[t][1][grp], pr[t][3] * vsc[t][1][grp]);
+            const uint32_t bp[2] = {movmatrix_trans(xlo), movmatrix_trans(xhi)};
+            mma_f16_16816(oone[grp], ones, bp);
+#pragma unroll
+            for (int jl = 0; jl < 4; ++jl) {
+              const int bs = 2 * (jl & 1);
+              const uint32_t sel_lo = uint32_t(bs | (bs << 4) | ((4 + bs) << 8) | ((4 + bs) << 12));
+              const uint32_t sel_hi = sel_lo + 0x1111u;
+              const uint32_t w0 = (jl >> 1) ? vw[t][0][grp].y : vw[t][0][grp].x;
+              const uint32_t w1 = (jl >> 1) ? vw[t][1][grp].y : vw[t][1][grp].x;
+              const uint32_t w2 = (jl >> 1) ? vw[t][2][grp].y : vw[t][2][grp].x;
+              const uint32_t w3 = (jl >> 1) ? vw[t][3][grp].y : vw[t][3][grp].x;
+              const uint32_t a[4] = {and_or(prmt(w0, w1, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                     and_or(prmt(w0, w1, sel_hi), 0x00FF00FFu, 0x64006400u),
+                                     and_or(prmt(w2, w3, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                     and_or(prmt(w2, w3, sel_hi), 0x00FF00FFu, 0x64006400u)};
+              mma_f16_16816(oacc[grp * 4 + jl], a, bp);
+            }
           }
         }
       }
@@ -922,7 +950,7 @@ static int launch_attn(AttnParams p, cudaStream_t st) {
     if (ring) kern = qkv_decode_attn_kernel<BITS, D, true>;
   }
   if constexpr (BITS == 8 && D == 128) {
-    if (ring && p.G <= 8) kern = qkv_decode_attn_t8_kernel<D>;
+    if (ring && p.G <= 8) kern = (p.PS / 16) % 2 == 0 ? qkv_decode_attn_t8_kernel<D, 2> : qkv_decode_attn_t8_kernel<D, 1>;
   }
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
