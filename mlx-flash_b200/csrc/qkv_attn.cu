@@ -933,15 +933,18 @@ static int launch_attn(AttnParams p, cudaStream_t st) {
   const int merge = (4 * p.G * D + 4 * p.G * 2) * int(sizeof(float));
   // page ring: head-major pages whose code rows fit one swizzled TMA box row
   constexpr bool RING_OK = D <= 128 && RB <= 128 && RB % 32 == 0;  // D = 256 would spill registers
-  const bool ring = RING_OK && p.head_stride == p.PS && p.slot_stride == 1 && p.PS <= 256 && aligned(p.ks, 16) &&
+  // (and whose ATTN_RING pages fit the 227 KB of shared memory of one CTA;
+  // larger pages take the direct-load form)
+  const int slot_bytes = (2 * p.PS * RB + 2 * p.PS * DG * 4 + 1023) / 1024 * 1024;
+  const bool ring = RING_OK && p.head_stride == p.PS && p.slot_stride == 1 && p.PS <= 256 &&
+                    ATTN_RING * slot_bytes + 128 + merge <= 227 * 1024 && aligned(p.ks, 16) &&
                     aligned(p.vs, 16) && get_encoder() == B2F_OK;
   CUtensorMap mk{}, mv{};
   int smem = merge;
   if (ring) {
     if (make_kv_map(&mk, p.kp, RB, p.PS) != B2F_OK || make_kv_map(&mv, p.vp, RB, p.PS) != B2F_OK)
       return B2F_ERR_INVALID;
-    const int raw = 2 * p.PS * RB + 2 * p.PS * DG * 4;
-    p.slot_bytes = (raw + 1023) / 1024 * 1024;
+    p.slot_bytes = slot_bytes;
     p.ring_bytes = ATTN_RING * p.slot_bytes + 128;
     smem = p.ring_bytes + merge;
   }

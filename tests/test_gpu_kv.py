@@ -158,6 +158,19 @@ def test_decode_attention_paged(dev, bits, Hq, Hkv, D):
         assert_close(to_np(out), want, what=f"attn bits={bits} splits={n_splits}")
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+def test_decode_attention_256_token_pages(dev, bits):
+    """Pages too large for the shared-memory page ring (256 tokens of 8-bit
+    d128 codes) go through the direct-load kernel."""
+    rng = np.random.default_rng(bits + 256)
+    lens = [5, 256, 700]
+    args, (q, keys, vals) = _paged_case(dev, rng, 3, lens, 32, 4, 128, bits, 256)
+    want, _ = attn.decode_attention(q, keys, vals)
+    for n_splits in (1, 2):
+        out = decode_attention(*args, bits=bits, page_size=256, num_kv_heads=4, n_splits=n_splits)
+        assert_close(to_np(out), want, what=f"attn 256-token pages bits={bits} splits={n_splits}")
+
+
 def test_decode_attention_config2_shape(dev):
     """Llama-3-8B heads (32q/8kv, d128), batch 16, context 8192, 8-, 4- and 2-bit KV."""
     rng = np.random.default_rng(2)
