@@ -225,7 +225,7 @@ def profile_kernels(dec, torch):
 # profiles/qkv_decode_attn_b64_ctx2048.txt).  The per-layer shapes are those
 # of the 48-layer step, so traffic scales with the units a launch processes.
 NCU_TRAFFIC_RATIO = {"moe_gate_up": 95.547392 / 73.596928, "moe_down": 46.04288 / 39.15776,
-                     "attention": 148.952064 / 144.142336}
+                     "attention": (147.63648 + 4.275712) / 144.142336}
 
 
 def attention_bytes(dec, ctx):
