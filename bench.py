@@ -259,7 +259,7 @@ def run_ours(args):
     exchange = EPExchange() if world > 1 else None
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
-                          dense_engine=args.dense_engine)
+                          dense_engine=args.dense_engine, moe_tile=args.moe_tile)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -498,6 +498,8 @@ def main():
                     help="routed-expert GEMM engine (auto: the decoder's choice for this batch)")
     ap.add_argument("--dense-engine", default="auto", choices=["auto", "mma", "tc", "gemv"],
                     help="q/k/v and o projection engine (auto: the decoder's choice for this batch)")
+    ap.add_argument("--moe-tile", type=int, default=16, choices=[16, 32],
+                    help="tokens per expert tile of the warp-MMA expert GEMM")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")
     ap.add_argument("--profile-window", action="store_true",

@@ -99,7 +99,7 @@ class Qwen3MoeDecoder:
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
                  device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
-                 dense_engine: str = "auto"):
+                 dense_engine: str = "auto", moe_tile: int = 16):
         self.s = s = shape
         self.dev = dev = torch.device(device)
         self.B = max_batch
@@ -197,7 +197,9 @@ class Qwen3MoeDecoder:
             if moe_engine == "tc_gather":
                 self.tile = 32
             elif moe_engine == "mma":
-                self.tile = 16
+                if moe_tile not in (16, 32):
+                    raise ValueError("the warp-MMA expert GEMM takes 16- or 32-token tiles")
+                self.tile = moe_tile
             else:
                 self.tile = min(256, max(16, (B + 15) // 16 * 16)) if moe_engine != "gemv" else 16
             self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, E, self.tile))

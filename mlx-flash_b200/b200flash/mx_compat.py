@@ -184,7 +184,8 @@ def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bia
                            x_row_index: torch.Tensor = None, x_row_div: int = 1, up=None,
                            x_plan_order: bool = False, out_plan_order: bool = False) -> torch.Tensor:
     """Grouped GEMM over a prepared plan on warp-level tensor-core MMA with the
-    4-bit codes unpacked in registers: tile 16 for decode-sized expert tiles,
+    4-bit codes unpacked in registers: tile 16 or 32 for decode-sized expert
+    tiles (32 unpacks an expert routed 17-32 tokens once instead of twice),
     tile 64 (one matrix) for a dense projection of a whole decode batch.
 
     ``x_plan_order``: ``x_rows`` is in plan order with permuted columns (the
@@ -194,8 +195,9 @@ def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bia
     dev = require_cuda(x_rows, w, scales, biases, x_row_index)
     E, N = w.shape[0], w.shape[1]
     K = w.shape[2] * 32 // bits
-    if bits != 4 or group_size != 64 or K % 128 or N % 8 or plan.tile not in (16, 64):
-        raise ValueError("the register-unpack MMA path needs 4-bit, group 64, K % 128 == 0, N % 8 == 0, tile 16/64")
+    if bits != 4 or group_size != 64 or K % 128 or N % 8 or plan.tile not in (16, 32, 64):
+        raise ValueError("the register-unpack MMA path needs 4-bit, group 64, K % 128 == 0, N % 8 == 0, "
+                         "tile 16/32/64")
     if plan.tile == 64 and up is not None:
         raise ValueError("64-token tiles take one matrix (no fused up projection)")
     xc = _capi.aligned_contiguous(x_rows.reshape(-1, K))

@@ -42,6 +42,10 @@ constexpr int MMA_XSTRIDE = 320;  // bytes between token rows of a staged x chun
 // Two shapes of the same kernel:
 //   expert tiles (plan tile 16): slots of <= 16 tokens, 64 weight rows per
 //     warp, three CTAs per SM;
+//   expert tiles (plan tile 32): slots of <= 32 tokens, 32 weight rows per
+//     warp, two CTAs per SM (168 registers): an expert routed 17-32 tokens
+//     unpacks its codes once instead of twice (hot experts under skewed
+//     routing);
 //   wide tiles (plan tile 64, one matrix): slots of <= 64 tokens (a dense
 //     projection of a decode batch is one slot), 16 weight rows per warp so
 //     the rows spread over many CTAs, two CTAs per SM.
@@ -50,6 +54,10 @@ struct MmaShape;
 template <>
 struct MmaShape<16> {
   static constexpr int NTMAX = 2, WROWS = 64, CTAS = 3;
+};
+template <>
+struct MmaShape<32> {
+  static constexpr int NTMAX = 4, WROWS = 32, CTAS = 2;
 };
 template <>
 struct MmaShape<64> {
@@ -474,6 +482,17 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     }
+  } else if constexpr (SH::NTMAX == 4) {
+    if (cnt <= 8) {
+      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+                                            begin, cnt, row_base, h0, h1, warp, lane);
+    } else if (cnt <= 16) {
+      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+                                            begin, cnt, row_base, h0, h1, warp, lane);
+    } else {
+      mma_consume<MAT, 4, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+                                            begin, cnt, row_base, h0, h1, warp, lane);
+    }
   } else {
     mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
                                                   expert, begin, cnt, row_base, h0, h1, warp, lane);
@@ -561,7 +580,7 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
                                            int out_plan_order, void* stream) {
   if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
-  if (!(tile == 16 || (tile == 64 && !w_up))) return B2F_ERR_UNSUPPORTED;
+  if (!(tile == 16 || tile == 32 || (tile == 64 && !w_up))) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0) return B2F_ERR_INVALID;
   if (A == 0) return B2F_OK;
   if (!x || !w_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
@@ -604,6 +623,13 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
   if (tile == 64)
     return xp ? launch_mma_cfg<1, true, 64>(p, w_gate, nullptr, E, max_slots, 1, st)
               : launch_mma_cfg<1, false, 64>(p, w_gate, nullptr, E, max_slots, 1, st);
+  if (tile == 32) {
+    if (w_up)
+      return xp ? launch_mma_cfg<2, true, 32>(p, w_gate, w_up, E, max_slots, 1, st)
+                : launch_mma_cfg<2, false, 32>(p, w_gate, w_up, E, max_slots, 1, st);
+    return xp ? launch_mma_cfg<1, true, 32>(p, w_gate, nullptr, E, max_slots, 1, st)
+              : launch_mma_cfg<1, false, 32>(p, w_gate, nullptr, E, max_slots, 1, st);
+  }
   if (w_up) {
     return xp ? launch_mma_cfg<2, true, 16>(p, w_gate, w_up, E, max_slots, 1, st)
               : launch_mma_cfg<2, false, 16>(p, w_gate, w_up, E, max_slots, 1, st);

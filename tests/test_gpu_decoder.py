@@ -89,6 +89,22 @@ def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
     assert to_np(dec.positions).tolist() == (positions + 1).tolist()
 
 
+def test_decode_step_expert_tile32_equals_tile16(dev):
+    """The warp-MMA expert GEMM with 32-token tiles gives bit-identical logits
+    to 16-token tiles (64 tokens over 8 experts: experts hold 17-32 tokens)."""
+    shape = Qwen3MoeShape(hidden=256, layers=2, n_heads=8, n_kv_heads=2, head_dim=128, moe_inter=128,
+                          n_experts=8, top_k=2, vocab=1000, kv_bits=8)
+    logits = []
+    for tile in (16, 32):
+        dec = Qwen3MoeDecoder(shape, max_batch=64, max_context=128, page_size=16, device=dev, seed=9,
+                              moe_engine="mma", dense_engine="gemv", moe_tile=tile)
+        dec.fill_random_context(40)
+        dec.step()
+        torch.cuda.synchronize()
+        logits.append(dec.logits.clone())
+    assert torch.equal(logits[0].view(torch.int16), logits[1].view(torch.int16))
+
+
 def test_decode_step_cuda_graph_replay(dev):
     """The step captured in a CUDA graph gives the same tokens as eager execution."""
     shape = Qwen3MoeShape(hidden=256, layers=2, n_heads=8, n_kv_heads=2, head_dim=128, moe_inter=128,

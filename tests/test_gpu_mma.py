@@ -31,15 +31,16 @@ def _routing(rng, T, k, E):
     return np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
 
 
+@pytest.mark.parametrize("tile", [16, 32])
 @pytest.mark.parametrize("T,k,E,H,I", [(64, 8, 128, 2048, 768), (64, 8, 32, 2048, 768), (7, 2, 4, 640, 384),
                                        (512, 8, 128, 2048, 768), (33, 4, 16, 1024, 512), (3, 1, 4, 256, 128)])
-def test_mma_swiglu_then_down(dev, T, k, E, H, I):
+def test_mma_swiglu_then_down(dev, T, k, E, H, I, tile):
     """SwitchGLU front half then down projection (Qwen3-MoE expert shapes and
     ragged ones: H = 640 leaves a partial CTA and idle warps in the down GEMM;
     512 tokens put up to ~200 tokens on one expert, i.e. many slots; slots of
-    1-8 tokens take the one-n-tile path, 9-16 the two-n-tile path)."""
+    1-8 tokens take the one-n-tile path, 9-16 the two-n-tile path, and with
+    32-token tiles 17-32 the four-n-tile path)."""
     rng = np.random.default_rng(T * 3 + E + H)
-    tile = 16
     g, u, d = _w(rng, (E, I, H)), _w(rng, (E, I, H)), _w(rng, (E, H, I))
     x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
     inds = _routing(rng, T, k, E)
@@ -52,18 +53,20 @@ def test_mma_swiglu_then_down(dev, T, k, E, H, I):
     assert_close(to_np(h), hw.reshape(T * k, I), what="mma swiglu")
     hh = to_np(h).astype(np.float64)
     want = np.zeros((T * k, H))
-    for a in range(T * k):
-        e = inds.reshape(-1)[a]
-        want[a] = affine.dequantize_f32(d[0][e], d[1][e], d[2][e], 64, 4).astype(np.float64) @ hh[a]
+    flat = inds.reshape(-1)
+    for e in np.unique(flat):
+        rows = np.nonzero(flat == e)[0]
+        want[rows] = hh[rows] @ affine.dequantize_f32(d[0][e], d[1][e], d[2][e], 64, 4).astype(np.float64).T
     assert_close(to_np(y), want, what="mma down")
 
 
-def test_mma_plan_order_chain_is_exact(dev):
+@pytest.mark.parametrize("tile", [16, 32])
+def test_mma_plan_order_chain_is_exact(dev, tile):
     """gate/up written in plan order with permuted columns equals the gathered,
     permuted natural-order output bit for bit, and the down projection reading
     it gives bit-identical rows to the natural-order chain."""
     rng = np.random.default_rng(11)
-    T, k, E, H, I, tile = 64, 8, 64, 1024, 768, 16
+    T, k, E, H, I = 64, 8, 64, 1024, 768
     g, u, d = _w(rng, (E, I, H)), _w(rng, (E, I, H)), _w(rng, (E, H, I))
     x = to_dev(round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16"), "bf16", dev)
     inds = _routing(rng, T, k, E)
@@ -76,6 +79,28 @@ def test_mma_plan_order_chain_is_exact(dev):
     y_nat = mx_compat.gather_qmm_mma_planned(h_nat, plan, *_dev3(d, dev), 64, 4, x_row_div=1)
     y_pln = mx_compat.gather_qmm_mma_planned(h_pln, plan, *_dev3(d, dev), 64, 4, x_plan_order=True)
     assert torch.equal(y_nat.view(torch.int16), y_pln.view(torch.int16))
+
+
+def test_mma_tile32_equals_tile16_bitwise(dev):
+    """Each (row, token) value is accumulated the same way whatever number of
+    tokens shares its tile, so 32-token tiles reproduce 16-token tiles bit for
+    bit (skewed routing: hot experts hold 17-64 tokens)."""
+    rng = np.random.default_rng(21)
+    T, k, E, H, I = 64, 8, 128, 2048, 768
+    g, u, d = _w(rng, (E, I, H)), _w(rng, (E, I, H)), _w(rng, (E, H, I))
+    x = to_dev(round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16"), "bf16", dev)
+    inds = torch.from_numpy(_routing(rng, T, k, E).reshape(-1)).to(dev)
+    outs = []
+    for tile in (16, 32):
+        # the expert-sorted (plan) order is the same for both tile sizes
+        plan = mx_compat.MoEPlan(inds, E, tile)
+        h = mx_compat.gather_qmm_mma_planned(x, plan, *_dev3(g, dev), 64, 4, x_row_div=k, up=_dev3(u, dev),
+                                             out_plan_order=True)
+        y = mx_compat.gather_qmm_mma_planned(h, plan, *_dev3(d, dev), 64, 4, x_plan_order=True)
+        plan.check()
+        outs.append((h, y))
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
 
 
 def test_mma_single_matrix_with_row_index(dev):
