@@ -268,7 +268,8 @@ int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, cons
  * 16 weight rows x 8 tokens), each 64-wide group folded as
  * s*sum(q x) + b*sum(x) in fp32 (the order MLX's quantized kernels use).
  * Plan from b2f_moe_plan / b2f_moe_route_plan / b2f_ep_plan with tile = 16
- * (expert tiles), or tile = 64 without w_up (wide tiles: a dense projection
+ * or 32 (expert tiles; 32 unpacks an expert routed 17-32 tokens once instead
+ * of twice), or tile = 64 without w_up (wide tiles: a dense projection
  * of up to 64 decode tokens is b2f_moe_plan over all-zero expert ids, E = 1);
  * same weight format as b2f_gather_qgemm_affine_tcgen05; bits 4,
  * group_size 64, K % 128 == 0, N % 8 == 0.
