@@ -37,7 +37,10 @@
 namespace b2f {
 
 constexpr int MMA_CW = 4;         // consumer warps per CTA
-constexpr int MMA_XSTRIDE = 320;  // bytes between token rows of a staged x chunk
+// bytes between token rows of a staged x chunk (4-bit / 2-bit weights): 256
+// bytes of a row plus padding that keeps the fragment reads conflict free
+template <int BITS>
+constexpr int mma_xstride() { return BITS == 4 ? 320 : 336; }
 
 // Two shapes of the same kernel:
 //   expert tiles (plan tile 16): slots of <= 16 tokens, 64 weight rows per
@@ -123,7 +126,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   // of 64 bytes) or 32B (2-bit rows of 32 bytes)
   const int sw = BITS == 4 ? (r >> 1) & 3 : (r >> 2) & 1;
   constexpr int RBY = 16 * BITS;  // code bytes per row per 128-wide chunk
-  constexpr int XS = BITS == 4 ? 320 : 336;
+  constexpr int XS = mma_xstride<BITS>();
   const int wr0 = warp * (WROWS / MAT);
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;  // weight rows per matrix
   constexpr int RBY = 16 * BITS;                      // code bytes per row per chunk
-  constexpr int XS = BITS == 4 ? 320 : 336;           // token row pitch in a stage
+  constexpr int XS = mma_xstride<BITS>();             // token row pitch in a stage
   constexpr int W_BYTES = MAT * CTA_ROWS * RBY;
   constexpr int STAGE = (W_BYTES + TILE * XS + 1023) / 1024 * 1024;
 
@@ -521,7 +524,7 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
                           int ksplit, cudaStream_t st) {
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
-  constexpr int STAGE = (MAT * CTA_ROWS * 16 * BITS + TILE * (BITS == 4 ? 320 : 336) + 1023) / 1024 * 1024;
+  constexpr int STAGE = (MAT * CTA_ROWS * 16 * BITS + TILE * mma_xstride<BITS>() + 1023) / 1024 * 1024;
   // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
   // of it reserved per CTA)
   int S = 8;
