@@ -218,14 +218,15 @@ def profile_kernels(dec, torch):
     return timings, distinct
 
 
-# DRAM bytes moved per algorithmic byte, from ncu captures of each kernel on
-# the 2-layer copy of this decode step (dram__bytes_read.sum +
+# DRAM bytes moved per algorithmic byte, from an ncu capture of the kernel the
+# step runs, on the 2-layer copy of this decode step (dram__bytes_read.sum +
 # dram__bytes_write.sum over the launch's algorithmic bytes; see
-# profiles/qgemm_tc_moe_b64_2layer.txt and
 # profiles/qkv_decode_attn_b64_ctx2048.txt).  The per-layer shapes are those
 # of the 48-layer step, so traffic scales with the units a launch processes.
-NCU_TRAFFIC_RATIO = {"moe_gate_up": 95.547392 / 73.596928, "moe_down": 46.04288 / 39.15776,
-                     "attention": (147.63648 + 4.275712) / 144.142336}
+# The warp-MMA expert GEMMs have no capture with both counters (their summary,
+# profiles/qgemm_mma_moe_b64_2layer_ncu.txt, holds DRAM reads only), so their
+# traffic is reported as null.
+NCU_TRAFFIC_RATIO = {"attention": (147.63648 + 4.275712) / 144.142336}
 
 
 def attention_bytes(dec, ctx):
@@ -349,7 +350,8 @@ def run_ours(args):
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
                 "traffic": (int(d["bytes_per_launch"] * NCU_TRAFFIC_RATIO[dom]) if dom in NCU_TRAFFIC_RATIO
                             else None),
-                "traffic_source": "ncu DRAM bytes / algorithmic bytes on the 2-layer capture, times this launch's bytes",
+                "traffic_source": ("ncu DRAM bytes / algorithmic bytes on the 2-layer capture, times this launch's bytes"
+                                   if dom in NCU_TRAFFIC_RATIO else "no ncu capture with read and write bytes"),
                 "bytes_per_launch": int(d["bytes_per_launch"]),
                 "avg_launch_us": round(d["avg_us"], 2),
                 "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / max(1, len(distinct)), 1)}
