@@ -18,7 +18,6 @@ One JSON line on rank 0.
 
 import argparse
 import json
-import math
 import os
 import subprocess
 import sys

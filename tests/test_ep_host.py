@@ -4,7 +4,6 @@ dispatch/combine decomposition (sum over ranks of owner-masked partials
 equals the single-process MoE), with the oracle standing in for the expert
 kernels on each rank."""
 
-import os
 import socket
 
 import numpy as np

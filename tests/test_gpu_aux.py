@@ -9,8 +9,8 @@ import pytest
 import torch
 
 from b200flash import kernels, mixed_precision
-from b200flash.layer_quantization import (LayerQuantConfig, LayerQuantizer, LayerSensitivityProfile,
-                                          QuantizedLinear, apply_layer_quantization, fake_quantize_sym)
+from b200flash.layer_quantization import (LayerQuantConfig, LayerSensitivityProfile, QuantizedLinear,
+                                          apply_layer_quantization, fake_quantize_sym)
 from oracle import affine, mixed, q4_0, sensitivity
 from oracle.fp import round_to
 

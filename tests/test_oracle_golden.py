@@ -1,7 +1,5 @@
 """The CPU oracle against the golden vectors generated from the reference's own code."""
 
-import os
-
 import numpy as np
 import pytest
 

@@ -13,7 +13,6 @@ The file name sorts last so that a run stopping at the first failure has
 already run every other test; it also passes alone in a fresh process.
 """
 
-import numpy as np
 import pytest
 import torch
 
