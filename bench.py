@@ -9,9 +9,11 @@ A step is one decode step of all ``--batch`` sequences through all 48 layers
 lm_head, greedy argmax), captured once in a CUDA graph.  ``value`` is device
 time with inputs resident in HBM; ``e2e`` adds, every step, the pinned-host
 ->device copy of the step's token ids and the device->host read of the next
-tokens.  Weights (~17 GB) and KV (~7 GB) exceed the 126 MB L2, so no flush
+tokens, with the host waiting for each step's tokens before it sends the next
+(``pipelined_value``: the same copies queued without that wait).  Weights (~17 GB) and KV (~7 GB) exceed the 126 MB L2, so no flush
 is needed between steps.  Under torchrun (N > 1) every rank runs its own
-batch (independent replicas, weak scaling) and the slowest rank's time is used.
+batch of sequences and holds 1/N of every layer's experts (expert parallel,
+weak scaling); the slowest rank's time is used.
 
 One JSON line on rank 0.
 """
@@ -49,7 +51,8 @@ def workload_name(args):
 def config_dict(args, world):
     return {"workload": workload_name(args), "batch_per_gpu": args.batch, "global_batch": args.batch * world,
             "context": args.ctx, "layers": args.layers, "weights": "4-bit affine g64 (N(0,0.02) random init)",
-            "kv_cache": "8-bit sym g64, paged (64-token pages)", "routing": "softmax top-8, Zipf(1.1) popularity",
+            "kv_cache": "8-bit sym g64, paged (64-token pages)", "routing": ("softmax top-8 over x.Wr + a fitted per-expert bias: each token's experts as if "
+                        "drawn without replacement from Zipf(1.1) popularity (see routing_fit)"),
             "l2_policy": "inputs larger than L2 (weights ~17 GB, KV ~7 GB), no flush",
             "parallelism": (f"ep{world} experts (NCCL all-gather dispatch / reduce-scatter combine), "
                             f"dp{world} attention") if world > 1 else "1 GPU"}
@@ -75,13 +78,17 @@ class ClockSampler:
         self.thread = None
         self.samples = []  # (sm_mhz, max_mhz, set of reasons)
 
+    def _bus_id(self):
+        """PCI bus id of the CUDA device (NVML and nvidia-smi number devices
+        without regard to CUDA_VISIBLE_DEVICES, so the ordinal is not used)."""
+        import torch
+        pr = torch.cuda.get_device_properties(self.device)
+        return f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+
     def _nvml_handle(self):
         import pynvml
-        import torch
         pynvml.nvmlInit()
-        pr = torch.cuda.get_device_properties(self.device)
-        bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
-        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(self._bus_id())
 
     def __enter__(self):
         import threading
@@ -103,7 +110,7 @@ class ClockSampler:
         except Exception:
             self.thread = None
             try:
-                self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device.index or 0}",
+                self.proc = subprocess.Popen(["nvidia-smi", f"--id={self._bus_id()}",
                                               f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                                               "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
                                              text=True)
@@ -187,6 +194,7 @@ def profile_kernels(dec, torch):
     import b200flash.decoder as dmod
 
     routed = []
+    chosen = []
     dmod.call = timed_call
     try:
         # record the routing of every layer for the algorithmic byte count
@@ -194,6 +202,8 @@ def profile_kernels(dec, torch):
 
         def route_and_keep(name, *args):
             rc = orig_route(name, *args)
+            if name in ("b2f_moe_route_topk", "b2f_moe_route_plan"):
+                chosen.append(dec.inds.clone())
             if name in ("b2f_moe_route_topk", "b2f_moe_route_plan") and dec.ep is None:
                 routed.append(dec.inds.clone())
             elif name == "b2f_ep_plan":
@@ -214,7 +224,42 @@ def profile_kernels(dec, torch):
         timings[tag].append(e0.elapsed_time(e1) * 1e-3)
     # per layer: distinct experts this rank computes, and its assignments
     distinct = [(int(torch.unique(r).numel()), int(r.numel())) for r in routed]
-    return timings, distinct
+    return timings, distinct, chosen
+
+
+def routing_fit(dec, chosen):
+    """Realised routing of one step against the Zipf(s) target: per layer the
+    distinct experts the batch hit and the selection frequency of each
+    popularity rank; mean over layers."""
+    import numpy as np
+
+    from b200flash.decoder import expected_distinct_experts, zipf_selection_frequency
+
+    s = dec.s
+    target = zipf_selection_frequency(s.n_experts, s.top_k, s.zipf_s)
+    freq = np.zeros(s.n_experts)
+    distinct = []
+    for ly, inds in zip(dec.layers, chosen):
+        rank = ly["zipf_rank"].to(inds.device)[inds.long()].reshape(-1)
+        freq += np.bincount(rank.cpu().numpy(), minlength=s.n_experts) / inds.shape[0]
+        distinct.append(int(torch_unique_count(inds)))
+    freq /= max(1, len(chosen))
+    B = chosen[0].shape[0] if chosen else 0
+    return {"target": f"each token's top-{s.top_k} drawn without replacement from p_r ~ r^-{s.zipf_s} "
+                      f"over {s.n_experts} experts",
+            "tokens_per_layer": B,
+            "distinct_experts_per_layer": round(float(np.mean(distinct)), 1) if distinct else None,
+            "distinct_experts_expected": round(expected_distinct_experts(target, B), 1),
+            "freq_max_abs_dev": round(float(np.abs(freq - target).max()), 4),
+            "freq_top4": [round(float(v), 3) for v in freq[:4]],
+            "freq_top4_target": [round(float(v), 3) for v in target[:4]],
+            "layers": len(chosen)}
+
+
+def torch_unique_count(t):
+    import torch
+
+    return torch.unique(t).numel()
 
 
 # DRAM bytes moved per algorithmic byte, from an ncu capture of the kernel the
@@ -313,6 +358,20 @@ def run_ours(args):
     torch.cuda.synchronize()
     f0 = torch.cuda.Event(enable_timing=True)
     f1 = torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    # a decode loop: every step's next tokens are on the host (sampling, EOS
+    # checks) before the next step's ids go up, so the host waits each step
+    f0.record()
+    for _ in range(args.steps):
+        dec.tokens.copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(dec.next_tokens, non_blocking=True)
+        stream.synchronize()
+        host_in.copy_(host_out)
+    f1.record()
+    torch.cuda.synchronize()
+    te = f0.elapsed_time(f1) * 1e-3
+    # the same copies queued back to back (no host wait between steps)
     f0.record()
     for _ in range(args.steps):
         dec.tokens.copy_(host_in, non_blocking=True)
@@ -320,15 +379,17 @@ def run_ours(args):
         host_out.copy_(dec.next_tokens, non_blocking=True)
     f1.record()
     torch.cuda.synchronize()
-    te = f0.elapsed_time(f1) * 1e-3
+    tp = f0.elapsed_time(f1) * 1e-3
     if world > 1:
-        tt = torch.tensor([te], device=dev)
+        tt = torch.tensor([te, tp], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        te = float(tt.item())
+        te, tp = float(tt[0].item()), float(tt[1].item())
     e2e = tokens_total / te
+    e2e_pipelined = tokens_total / tp
 
     # live per-kernel timing (eager step, events on the launching stream)
-    timings, distinct = profile_kernels(dec, torch)
+    timings, distinct, chosen = profile_kernels(dec, torch)
+    rfit = routing_fit(dec, chosen)
     peak, peak_kind = load_peaks()
     per_exp = moe_bytes_per_expert(shape)
     gu_bytes = [2 * u * per_exp + a * shape.hidden * 2 + a * shape.moe_inter * 2 for u, a in distinct]
@@ -360,12 +421,14 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random weights, random context, seeded)",
         "config": config_dict(args, world),
         "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": args.batch * 4,
-                "d2h_bytes_per_step": args.batch * 4},
+                "d2h_bytes_per_step": args.batch * 4, "host_sync_per_step": True,
+                "pipelined_value": round(e2e_pipelined, 2)},
         "gpu_launches": dec.launches_per_step() * args.steps,
         "roofline": roofline,
         "kernels": {k: {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()}
                     for k, v in kernels.items()},
         "clocks": clk.summary(),
+        "routing_fit": rfit,
         "weight_bytes": dec.weight_bytes(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -437,7 +500,7 @@ def _oracle_sample(args, shape, n_seq, layers_sampled, seed=0):
     _ = np.asarray(x, np.float64) @ affine.dequantize_f32(*lm, 64, 4).astype(np.float64).T
     t_lm = (time.perf_counter() - t1) * 32
     t_step = t_layers / layers_sampled * 48 + t_lm
-    return n_seq / t_step, t_layers + t_lm / 32, t_step
+    return n_seq / t_step, t_layers + t_lm / 32, t_step, t_layers / layers_sampled, t_lm / 32
 
 
 def cpu_threads():
@@ -451,12 +514,13 @@ def cpu_threads():
 
 def cpu_baseline(args, shape):
     n_seq = 4
-    tps, wall, t_step = _oracle_sample(args, shape, n_seq=n_seq, layers_sampled=1)
+    tps, wall, t_step, t_layer, t_lm32 = _oracle_sample(args, shape, n_seq=n_seq, layers_sampled=1)
     return {"value": round(tps, 4), "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
-            "sample": (f"NumPy oracle (fp64) decode of {n_seq} sequences at context {args.ctx}: 1 of 48 layers "
-                       f"(qkv, 8-bit KV attention, o_proj, router, routed experts) + 1/32 of lm_head, "
-                       f"scaled to the full 48-layer step; {wall:.1f} s measured"),
-            "host_cpus": os.cpu_count()}
+            "sample": (f"NumPy oracle (fp64) decode of {n_seq} sequences at context {args.ctx} (not the GPU's "
+                       f"{args.batch}): 1 of 48 layers (qkv, 8-bit KV attention, o_proj, router, routed experts) "
+                       f"measured at {t_layer:.2f} s, 1/32 of lm_head at {t_lm32:.2f} s; step = 48 x layer + "
+                       f"32 x lm slice = {t_step:.1f} s (extrapolated), tok/s = {n_seq} / step"),
+            "measured_s": round(wall, 2), "host_cpus": os.cpu_count()}
 
 
 def run_reference(args):
@@ -467,16 +531,25 @@ def run_reference(args):
 
     shape = Qwen3MoeShape()
     per_step = []
+    per_layer = []
+    walls = []
     n_seq = 2
+    t_start = time.perf_counter()
     for i in range(args.warmup + args.steps):
-        tps, wall, t_step = _oracle_sample(args, shape, n_seq=n_seq, layers_sampled=1, seed=i)
+        tps, wall, t_step, t_layer, t_lm32 = _oracle_sample(args, shape, n_seq=n_seq, layers_sampled=1, seed=i)
         if i >= args.warmup:
             per_step.append(t_step)
+            per_layer.append(t_layer)
+            walls.append(wall)
     t = sum(per_step)
     value = n_seq * len(per_step) / t
     world = int(os.environ.get("WORLD_SIZE", "1"))
     cb = {"value": round(value, 4), "unit": "tok/s", "kind": "port", "cores": cpu_threads(),
-          "sample": f"NumPy oracle decode, {n_seq} sequences at context {args.ctx}, 1 of 48 layers + 1/32 lm_head per step, scaled to 48 layers"}
+          "sample": (f"NumPy oracle (fp64) decode, {n_seq} sequences at context {args.ctx}; each step times 1 of 48 "
+                     f"layers (mean {sum(per_layer) / len(per_layer):.2f} s measured) + 1/32 of lm_head and "
+                     f"extrapolates to 48 layers + the whole lm_head; ms_per_step is that extrapolated step, "
+                     f"measured_s the CPU time actually spent in the timed steps"),
+          "measured_s": round(sum(walls), 2), "wall_s": round(time.perf_counter() - t_start, 2)}
     print(json.dumps({"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
                       "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                       "ms_per_step": round(1e3 * t / len(per_step), 2), "higher_is_better": True,

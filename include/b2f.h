@@ -56,12 +56,23 @@ const char* b2f_last_error_string(void);
 
 /* mx.quantize(w, group_size, bits) as called through
  * nn.QuantizedLinear.from_linear (mlx_flash_compress/layer_quantization.py:254)
- * and nn.quantize (mlx_flash_compress/dflash_model.py:300).
+ * and nn.quantize (mlx_flash_compress/dflash_model.py:300), with MLX's
+ * per-group rule: scale = max((max-min)/(2^bits-1), 1e-7), the edge (the
+ * larger-magnitude end) becomes the bias and an exact code (scale = edge/q0,
+ * negative when the edge is the max), q from the f32 scale and bias.
  * w: [rows, K] of `dtype`; wq: uint32 [rows, K*bits/32]; scales, biases:
  * [rows, K/group_size] of `dtype`.  bits in {2,4,8}; group_size in {32,64,128}. */
 int b2f_quantize_affine(const void* w, int dtype, int64_t rows, int64_t K, int bits,
                         int group_size, uint32_t* wq, void* scales, void* biases,
                         void* stream);
+
+/* The same packing with the min/max rule: scale = (max-min)/(2^bits-1)
+ * rounded to `dtype`, bias = min, q from the rounded scale (q = 0 where it is
+ * 0).  No MLX call corresponds to it; it is the rule stated for the
+ * single-linear workload (W[4096,4096], 4-bit, group 64). */
+int b2f_quantize_affine_minmax(const void* w, int dtype, int64_t rows, int64_t K, int bits,
+                               int group_size, uint32_t* wq, void* scales, void* biases,
+                               void* stream);
 
 /* mx.dequantize (the unpack restated at mlx_flash_compress/mixed_precision.py:150-171).
  * If row_index is non-NULL, output row i is source row row_index[i] (an

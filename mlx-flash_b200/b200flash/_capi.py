@@ -33,6 +33,7 @@ SIGNATURES = {
     "b2f_status_string": (ctypes.c_char_p, [_I]),
     "b2f_last_error_string": (ctypes.c_char_p, []),
     "b2f_quantize_affine": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),
+    "b2f_quantize_affine_minmax": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),
     "b2f_dequantize_affine": (_I, [_P, _P, _P, _I, _I64, _I64, _I, _I, _P, _P, _P]),
     "b2f_qgemv_affine": (_I, [_P, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I, _P, _P, _I64, _P]),
     "b2f_moe_plan_workspace_bytes": (_I64, [_I64, _I64, _I]),

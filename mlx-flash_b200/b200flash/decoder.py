@@ -26,12 +26,18 @@ b2f_ep_combine_partial -> reduce-scatter -> b2f_combine_rmsnorm (k = 1).
 
 Every buffer is allocated once, so ``step()`` can be captured in a CUDA graph.
 Weights are random (N(0, 0.02) before 4-bit quantization) with the model's
-shapes; the router adds a per-expert logit bias log(p_e) with p Zipf(s) so
-expert popularity is skewed like real traffic.
+shapes.  Expert popularity follows Zipf(s): the router weight is Gaussian,
+so for a unit-RMS hidden row the logits x.Wr are iid N(0, tau^2) over the
+experts, and a per-expert logit bias (``zipf_router_bias``) is fitted so that
+the top-k of ``x.Wr + bias`` picks each expert as often as drawing k experts
+per token without replacement from p_r ~ r^-s does.
 """
 
+import functools
 import math
 from dataclasses import dataclass
+
+import numpy as np
 
 import torch
 
@@ -60,6 +66,53 @@ class Qwen3MoeShape:
     kv_bits: int = 8
     norm_topk: bool = True
     zipf_s: float = 1.1
+    # std of the router logits x.Wr for a unit-RMS hidden row (sets Wr's std)
+    router_tau: float = 1.3
+
+
+@functools.lru_cache(maxsize=8)
+def zipf_selection_frequency(E: int, k: int, s: float, samples: int = 100_000, seed: int = 0) -> np.ndarray:
+    """Per-token probability that the expert of popularity rank r (0-based) is
+    among a token's k experts when the k are drawn without replacement from
+    p_r ~ (r+1)^-s (Gumbel top-k sampling), estimated from ``samples`` draws
+    with a fixed seed.  For E=128, k=8, s=1.1: 0.90, 0.68, 0.52, ... 0.011."""
+    p = np.arange(1, E + 1, dtype=np.float64) ** (-s)
+    lp = np.log(p / p.sum())
+    g = np.random.default_rng(seed)
+    f = np.zeros(E)
+    chunk = 10_000
+    for i in range(0, samples, chunk):
+        n = min(chunk, samples - i)
+        top = np.argpartition(-(lp[None] + g.gumbel(size=(n, E))), k, axis=1)[:, :k]
+        f += np.bincount(top.ravel(), minlength=E)
+    f /= samples
+    f.setflags(write=False)
+    return f
+
+
+@functools.lru_cache(maxsize=8)
+def zipf_router_bias(E: int, k: int, s: float, tau: float, samples: int = 16384, iters: int = 60,
+                     seed: int = 1) -> np.ndarray:
+    """Per-rank logit bias beta (float32 [E]) such that the top-k of
+    ``beta + tau * z`` (z iid N(0, 1) per expert, the router logits of a
+    Gaussian Wr) selects rank r with frequency ``zipf_selection_frequency``.
+    Fixed-point fit on ``samples`` fixed noise draws: beta += 0.7 log(f/h)."""
+    f = zipf_selection_frequency(E, k, s)
+    z = (tau * np.random.default_rng(seed).standard_normal((samples, E))).astype(np.float32)
+    beta = np.log(f).astype(np.float32)
+    for _ in range(iters):
+        top = np.argpartition(-(beta[None] + z), k, axis=1)[:, :k]
+        h = np.bincount(top.ravel(), minlength=E) / samples
+        beta += (0.7 * np.log(np.maximum(f, 1e-6) / np.maximum(h, 1e-6))).astype(np.float32)
+        beta -= beta.max()
+    beta.setflags(write=False)
+    return beta
+
+
+def expected_distinct_experts(freq: np.ndarray, tokens: int) -> float:
+    """Expected number of distinct experts hit by ``tokens`` independent
+    tokens whose per-token selection frequencies are ``freq``."""
+    return float(np.sum(1.0 - (1.0 - np.asarray(freq, np.float64)) ** tokens))
 
 
 class QWeight:
@@ -125,17 +178,19 @@ class Qwen3MoeDecoder:
 
         self.embed = random_qweight((s.vocab, H), bits, gs, dev, gen, std=1.0)
         self.layers = []
-        ranks = torch.arange(1, E + 1, dtype=torch.float64, device=dev)
-        zipf = ranks ** (-s.zipf_s)
-        zipf = (zipf / zipf.sum()).log().to(torch.float32)
+        # router: x.Wr has std router_tau for a unit-RMS row scaled by the
+        # post-attention norm weight (mean square 1.01); the fitted bias gives
+        # the Zipf(s) selection frequencies, rank perm[e] for expert e
+        zbias = torch.from_numpy(np.array(zipf_router_bias(E, s.top_k, s.zipf_s, s.router_tau))).to(dev)
+        wr_std = s.router_tau / math.sqrt(H * 1.01)
         for _ in range(self.L):
             perm = torch.randperm(E, device=dev, generator=gen)
             self.layers.append({
                 "in_norm": norm_w(H), "post_norm": norm_w(H), "q_norm": norm_w(D), "k_norm": norm_w(D),
                 "wqkv": random_qweight((self.qkv_rows, H), bits, gs, dev, gen),
                 "wo": random_qweight((H, Hq * D), bits, gs, dev, gen),
-                "wr": (torch.randn(E, H, device=dev, generator=gen) * 0.02).to(torch.bfloat16),
-                "rbias": zipf[perm].contiguous(),
+                "wr": (torch.randn(E, H, device=dev, generator=gen) * wr_std).to(torch.bfloat16),
+                "rbias": zbias[perm].contiguous(), "zipf_rank": perm,
                 "gate": random_qweight((E_loc, I, H), bits, gs, dev, egen),
                 "up": random_qweight((E_loc, I, H), bits, gs, dev, egen),
                 "down": random_qweight((E_loc, H, I), bits, gs, dev, egen),

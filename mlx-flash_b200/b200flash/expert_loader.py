@@ -120,6 +120,20 @@ class SafetensorsMap:
                 return torch.stack(slices)
         return None
 
+    def present_experts(self, key, expert_ids):
+        """The ids among ``expert_ids`` whose tensors exist for ``key`` (every
+        id for a stacked key, the ids with their own key in the per-expert and
+        Mixtral layouts)."""
+        expert_ids = [int(e) for e in expert_ids]
+        if key in self._tensors:
+            shape = self._tensors[key][2]
+            return [e for e in expert_ids if len(shape) >= 3 and 0 <= e < shape[0]]
+        per_expert = key.replace(".switch_mlp.", ".experts.0.")
+        if per_expert not in self._tensors:
+            for mlx_name, st_name in _MIXTRAL_MAP.items():
+                per_expert = per_expert.replace(f".{mlx_name}.", f".{st_name}.")
+        return [e for e in expert_ids if per_expert.replace(".experts.0.", f".experts.{e}.") in self._tensors]
+
     def close(self):
         for m in self._mmaps.values():
             m.close()
@@ -152,9 +166,16 @@ def load_moe_layer_shard(smap: SafetensorsMap, layer_idx: int, shard: ExpertShar
     for proj in ("gate_proj", "up_proj", "down_proj"):
         parts = []
         for suffix in ("weight", "scales", "biases"):
-            t = smap.get_expert_slice(expert_weight_key(layer_idx, proj, suffix, mixtral), owned, device)
+            key = expert_weight_key(layer_idx, proj, suffix, mixtral)
+            t = smap.get_expert_slice(key, owned, device)
             if t is None:
                 raise KeyError(f"layer {layer_idx} {proj}.{suffix} not found")
+            if t.shape[0] != len(owned):
+                # a per-expert layout with some experts' keys absent: every later
+                # expert's local index would shift, so refuse the shard
+                have = set(smap.present_experts(key, owned))
+                missing = [e for e in owned if e not in have]
+                raise KeyError(f"layer {layer_idx} {proj}.{suffix}: experts {missing} not found")
             parts.append(t)
         out[proj] = tuple(parts)
     return out

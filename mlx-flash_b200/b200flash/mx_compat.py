@@ -33,10 +33,19 @@ def _check_format(bits, group_size, allowed=SUPPORTED_BITS):
         raise ValueError(f"group_size must be one of {GROUP_SIZES}, got {group_size}")
 
 
-def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine"):
-    """Affine-quantize ``w[..., K]`` -> ``(wq uint32[..., K*bits/32], scales, biases)``."""
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine", rule: str = "mlx"):
+    """Affine-quantize ``w[..., K]`` -> ``(wq uint32[..., K*bits/32], scales, biases)``.
+
+    ``rule="mlx"`` (default): MLX's per-group rule -- the larger-magnitude end
+    of the group is the bias and lies exactly on the code grid (the scale is
+    negative when that end is the maximum); codes from the f32 scale and bias.
+    ``rule="minmax"``: ``scale = (max - min) / (2**bits - 1)``, ``bias = min``
+    (the rule stated for the single-linear W[4096, 4096] workload).
+    """
     if mode != "affine":
         raise ValueError(f"only mode='affine' is supported, got {mode!r}")
+    if rule not in ("mlx", "minmax"):
+        raise ValueError(f"rule must be 'mlx' or 'minmax', got {rule!r}")
     _check_format(bits, group_size)
     if w.dtype not in DTYPE_CODES:
         raise ValueError(f"unsupported dtype {w.dtype}")
@@ -50,8 +59,9 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "
     wq = torch.empty(*lead, K * bits // 32, dtype=torch.uint32, device=dev)
     scales = torch.empty(*lead, K // group_size, dtype=w.dtype, device=dev)
     biases = torch.empty_like(scales)
-    call("b2f_quantize_affine", ptr(wc), DTYPE_CODES[w.dtype], rows, K, bits, group_size, ptr(wq),
-         ptr(scales), ptr(biases), stream_of(dev))
+    fn = "b2f_quantize_affine" if rule == "mlx" else "b2f_quantize_affine_minmax"
+    call(fn, ptr(wc), DTYPE_CODES[w.dtype], rows, K, bits, group_size, ptr(wq), ptr(scales), ptr(biases),
+         stream_of(dev))
     return wq, scales, biases
 
 
@@ -87,12 +97,46 @@ def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, grou
     return out
 
 
+def _sm_count(dev) -> int:
+    return torch.cuda.get_device_properties(dev).multi_processor_count
+
+
+def tc_ksplit(N: int, K: int, sms: int) -> int:
+    """K ranges for the tcgen05 GEMM of a decode-sized batch: double the split
+    while the 128-row blocks x ranges stay within two CTAs per SM and each
+    range keeps at least four 64-wide chunks."""
+    blocks = (N + 127) // 128
+    chunks = K // 64
+    ks = 1
+    while blocks * ks * 2 <= 2 * sms and ks * 2 <= chunks // 4:
+        ks *= 2
+    return ks
+
+
+def quantized_matmul_engine(M: int, N: int, K: int, bits: int, group_size: int, residual: bool = False) -> str:
+    """Kernel ``quantized_matmul`` runs for an ``[M, K] x [N, K]^T`` product:
+
+    * ``"gemv"`` -- the register GEMV (``b2f_qgemv_affine``) for up to 16 rows
+      when K has at most 64 groups;
+    * ``"tc"`` -- the tcgen05 GEMM (``b2f_qgemm_affine_tcgen05_splitk``) for
+      group 64: any K (multiple of 64), K split over the SMs for decode-sized M;
+    * ``"gemv_k"`` -- group 32 / 128 with more than 64 groups: the GEMV over K
+      ranges of 64 groups, each range adding the previous ones as its residual.
+    """
+    if group_size == 64 and K % 64 == 0 and (M > 16 or K // group_size > 64 or bits == 8):
+        return "tc"
+    if K // group_size <= 64:
+        return "gemv"
+    return "gemv_k"
+
+
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      transpose: bool = True, group_size: int = 64, bits: int = 4,
-                     mode: str = "affine", residual: torch.Tensor = None) -> torch.Tensor:
+                     mode: str = "affine", residual: torch.Tensor = None, engine: str = "auto") -> torch.Tensor:
     """``x @ dequantize(w).T`` for ``x[..., K]`` (bf16) -> ``[..., N]`` bf16.
 
     ``residual`` (optional, ``[..., N]`` bf16) is added in the same kernel.
+    ``engine`` picks the kernel (``quantized_matmul_engine`` for ``"auto"``).
     """
     if not transpose:
         raise ValueError("only transpose=True is supported on this path")
@@ -110,13 +154,40 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
         raise ValueError("w must be [N, K*bits/32] with scales/biases [N, K/group_size]")
     lead = tuple(x.shape[:-1])
     M = x.numel() // K
+    if engine == "auto":
+        engine = quantized_matmul_engine(M, N, K, bits, group_size, residual is not None)
+    if engine not in ("gemv", "tc", "gemv_k"):
+        raise ValueError(f"unknown engine {engine!r}")
+    if engine == "tc":
+        if not tc_supported(K, group_size, bits):
+            raise ValueError("the tcgen05 GEMM needs group_size 64 and K % 64 == 0")
+        ks = tc_ksplit(N, K, _sm_count(dev)) if M <= 64 else 1
+        tile = min(128, max(16, (M + 15) // 16 * 16))
+        return quantized_matmul_tc(x, w, scales, biases, group_size, bits, residual, tile=tile, ksplit=ks)
     xc = _capi.aligned_contiguous(x.reshape(M, K))
     out = torch.empty(*lead, N, dtype=torch.bfloat16, device=dev)
     res = None
     if residual is not None:
         res = residual.reshape(M, N).contiguous()
-    call("b2f_qgemv_affine", ptr(xc), K, M, ptr(w.contiguous()), ptr(scales.contiguous()),
-         ptr(biases.contiguous()), N, K, bits, group_size, ptr(res), ptr(out), N, stream_of(dev))
+    wc, sc, bc = w.contiguous(), scales.contiguous(), biases.contiguous()
+    if engine == "gemv":
+        if K // group_size > 64:
+            raise ValueError("the register GEMV takes at most 64 groups per row")
+        call("b2f_qgemv_affine", ptr(xc), K, M, ptr(wc), ptr(sc), ptr(bc), N, K, bits, group_size, ptr(res),
+             ptr(out), N, stream_of(dev))
+        return out
+    # K ranges of 64 groups: each range's product adds the running sum (bf16)
+    kr = 64 * group_size
+    out2 = out.reshape(M, N)
+    for k0 in range(0, K, kr):
+        k1 = min(K, k0 + kr)
+        wr = wc[:, k0 * bits // 32: k1 * bits // 32].contiguous()
+        sr = sc[:, k0 // group_size: k1 // group_size].contiguous()
+        br = bc[:, k0 // group_size: k1 // group_size].contiguous()
+        xr = _capi.aligned_contiguous(xc[:, k0:k1])
+        prev = res if k0 == 0 else out2.clone()
+        call("b2f_qgemv_affine", ptr(xr), k1 - k0, M, ptr(wr), ptr(sr), ptr(br), N, k1 - k0, bits, group_size,
+             ptr(prev), ptr(out2), N, stream_of(dev))
     return out
 
 
@@ -342,12 +413,13 @@ def gather_qmv_planned(x_rows: torch.Tensor, plan: MoEPlan, w, scales, biases, g
 def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                lhs_indices: torch.Tensor = None, rhs_indices: torch.Tensor = None, transpose: bool = True,
                group_size: int = 64, bits: int = 4, mode: str = "affine",
-               sorted_indices: bool = False) -> torch.Tensor:
+               sorted_indices: bool = False, engine: str = "auto") -> torch.Tensor:
     """``mx.gather_qmm``: per batch element ``x[lhs] @ dequantize(w[rhs]).T``.
 
     ``x``: ``[..., M, K]`` bf16; ``w``: ``[E, N, K*bits/32]``; result
     ``[*broadcast(batch), M, N]`` bf16.  ``sorted_indices`` is accepted for
-    signature compatibility; the kernel always groups rows by expert itself.
+    signature compatibility; the kernels always group rows by expert
+    themselves.  ``engine`` picks the kernel (``gather_qmm_engine`` for "auto").
     """
     if not transpose:
         raise ValueError("only transpose=True is supported on this path")
@@ -380,8 +452,45 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     m_idx = torch.arange(M, device=dev)
     x_row = (lhs_f[:, None] * M + m_idx[None, :]).reshape(-1).to(torch.int32)
     expert_of = rhs_f[:, None].expand(-1, M).reshape(-1).to(torch.int32)
-    tile = _moe_tile(K, group_size)
-    plan = MoEPlan(expert_of, E, tile)
-    out = gather_qmv_planned(x.reshape(nx * M, K), plan, w, scales, biases, group_size, bits,
-                             x_row_index=x_row)
+    A = expert_of.numel()
+    if engine == "auto":
+        engine = gather_qmm_engine(A, E, N, K, bits, group_size)
+    x2 = x.reshape(nx * M, K)
+    if engine == "mma":
+        plan = MoEPlan(expert_of, E, 16)
+        out = gather_qmm_mma_planned(x2, plan, w, scales, biases, group_size, bits, x_row_index=x_row)
+    elif engine == "tc_sorted":
+        plan = MoEPlan(expert_of, E, 64 if A >= 64 * E else 32)
+        xs = moe_gather_rows(x2, plan, x_row_index=x_row)
+        out = sorted_qmm_tc(xs, plan, w, scales, biases, group_size, bits)
+    elif engine == "tc":
+        plan = MoEPlan(expert_of, E, 32)
+        out = gather_qmm_tc_planned(x2, plan, w, scales, biases, group_size, bits, x_row_index=x_row)
+    elif engine == "gemv":
+        if K // group_size > 64:
+            raise ValueError("the register GEMV takes at most 64 groups per row; use group_size 64")
+        plan = MoEPlan(expert_of, E, _moe_tile(K, group_size))
+        out = gather_qmv_planned(x2, plan, w, scales, biases, group_size, bits, x_row_index=x_row)
+    else:
+        raise ValueError(f"unknown engine {engine!r}")
     return out.reshape(*batch, M, N)
+
+
+def gather_qmm_engine(A: int, E: int, N: int, K: int, bits: int, group_size: int) -> str:
+    """Kernel ``gather_qmm`` runs for ``A`` (token, expert) assignments over
+    ``E`` stacked ``[N, K]`` experts:
+
+    * ``"mma"`` -- warp-level MMA with the 4-bit codes unpacked in registers
+      (``b2f_gather_qgemm_affine_mma``) while experts average at most 32
+      assignments (decode): 4-bit, group 64, K % 128 == 0, N % 8 == 0;
+    * ``"tc_sorted"`` -- rows gathered into expert order, then the tcgen05
+      grouped GEMM (``b2f_sorted_qgemm_affine_tcgen05``) for prefill-sized
+      batches: group 64 with an even group count;
+    * ``"tc"`` -- the per-slot tcgen05 GEMM for other group-64 shapes;
+    * ``"gemv"`` -- the register GEMV (group 32 / 128, at most 64 groups).
+    """
+    if bits == 4 and group_size == 64 and K % 128 == 0 and N % 8 == 0 and A <= 32 * E:
+        return "mma"
+    if group_size == 64 and K % 64 == 0:
+        return "tc_sorted" if (K // 64) % 2 == 0 else "tc"
+    return "gemv"

@@ -14,11 +14,21 @@ void set_last_cuda_error(cudaError_t e) { g_last_error = cudaGetErrorString(e); 
 // ------------------------------------------------------------------------
 // (a) affine quantize.  One thread owns EPT consecutive elements of one
 // group; TPG = GS/EPT neighbouring lanes reduce min/max with shuffles.
-// Rounding follows oracle/affine.py: range = max-min (f32), scale =
-// round_T(range / n_bins), q = clip(rint((w - min) / scale), 0, n_bins),
-// q = 0 for a group whose rounded scale is 0.
+// Two per-group rules, f32 arithmetic with one IEEE rounding per step
+// (n = 2^bits - 1):
+//   kRuleMlx (mx.quantize): scale = max((max-min)/n, 1e-7); the edge is the
+//     larger-magnitude end (min, positive scale, if |min| > |max|; else max
+//     with the scale negated); q0 = rint(edge/scale); if q0 != 0 then
+//     scale = edge/q0 and bias = edge, else bias = 0; q = clip(rint((w-bias)
+//     /scale), 0, n) with the f32 scale and bias, which are rounded into the
+//     weight dtype only when stored.
+//   kRuleMinMax (the single-linear workload's stated rule): scale =
+//     round_T((max-min)/n), bias = min, q = clip(rint((w-min)/scale), 0, n)
+//     with the rounded scale; q = 0 for a group whose rounded scale is 0.
 // ------------------------------------------------------------------------
-template <class Tag, int BITS, int GS>
+enum QuantRule { kRuleMlx = 0, kRuleMinMax = 1 };
+
+template <class Tag, int BITS, int GS, int RULE>
 __global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag::T* __restrict__ w,
                                                               int64_t n_threads,
                                                               uint32_t* __restrict__ wq,
@@ -57,15 +67,32 @@ __global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag
     }
     mx = warp_max<TPG>(mx);
     mn = warp_min<TPG>(mn);
-    const float scale = Tag::round(__fdiv_rn(__fsub_rn(mx, mn), NBINS));
+    float scale, bias;
+    bool zero_q = false;
+    if constexpr (RULE == kRuleMlx) {
+      scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), NBINS), 1e-7f);
+      const bool side = fabsf(mn) > fabsf(mx);
+      if (!side) scale = -scale;
+      const float edge = side ? mn : mx;
+      const float q0 = rintf(__fdiv_rn(edge, scale));
+      bias = 0.f;
+      if (q0 != 0.f) {
+        scale = __fdiv_rn(edge, q0);
+        bias = edge;
+      }
+    } else {
+      scale = Tag::round(__fdiv_rn(__fsub_rn(mx, mn), NBINS));
+      bias = mn;
+      zero_q = scale == 0.f;
+    }
     uint32_t words[WPT];
 #pragma unroll
     for (int j = 0; j < WPT; ++j) words[j] = 0u;
 #pragma unroll
     for (int i = 0; i < EPT; ++i) {
       uint32_t q = 0u;
-      if (scale != 0.f) {
-        float r = rintf(__fdiv_rn(__fsub_rn(v[i], mn), scale));
+      if (!zero_q) {
+        float r = rintf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
         r = fminf(fmaxf(r, 0.f), NBINS);
         q = uint32_t(r);
       }
@@ -81,13 +108,13 @@ __global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag
       if ((threadIdx.x % TPG) == 0) {
         const int64_t g = (t * EPT) / GS;
         scales[g] = Tag::from_f(scale);
-        biases[g] = Tag::from_f(mn);
+        biases[g] = Tag::from_f(bias);
       }
     }
   }
 }
 
-template <class Tag, int BITS>
+template <class Tag, int BITS, int RULE>
 static int launch_quantize_bits(const void* w, int64_t rows, int64_t K, int gs, uint32_t* wq,
                                 void* s, void* b, cudaStream_t st) {
   using T = typename Tag::T;
@@ -102,13 +129,13 @@ static int launch_quantize_bits(const void* w, int64_t rows, int64_t K, int gs, 
   auto Bi = static_cast<T*>(b);
   switch (gs) {
     case 32:
-      quantize_affine_kernel<Tag, BITS, 32><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      quantize_affine_kernel<Tag, BITS, 32, RULE><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
       break;
     case 64:
-      quantize_affine_kernel<Tag, BITS, 64><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      quantize_affine_kernel<Tag, BITS, 64, RULE><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
       break;
     case 128:
-      quantize_affine_kernel<Tag, BITS, 128><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
+      quantize_affine_kernel<Tag, BITS, 128, RULE><<<grid, block, 0, st>>>(W, n_threads, wq, S, Bi);
       break;
     default:
       return B2F_ERR_UNSUPPORTED;
@@ -116,13 +143,32 @@ static int launch_quantize_bits(const void* w, int64_t rows, int64_t K, int gs, 
   return check_launch();
 }
 
-template <class Tag>
+template <class Tag, int RULE>
 static int launch_quantize(const void* w, int64_t rows, int64_t K, int bits, int gs, uint32_t* wq,
                            void* s, void* b, cudaStream_t st) {
   switch (bits) {
-    case 2: return launch_quantize_bits<Tag, 2>(w, rows, K, gs, wq, s, b, st);
-    case 4: return launch_quantize_bits<Tag, 4>(w, rows, K, gs, wq, s, b, st);
-    case 8: return launch_quantize_bits<Tag, 8>(w, rows, K, gs, wq, s, b, st);
+    case 2: return launch_quantize_bits<Tag, 2, RULE>(w, rows, K, gs, wq, s, b, st);
+    case 4: return launch_quantize_bits<Tag, 4, RULE>(w, rows, K, gs, wq, s, b, st);
+    case 8: return launch_quantize_bits<Tag, 8, RULE>(w, rows, K, gs, wq, s, b, st);
+    default: return B2F_ERR_UNSUPPORTED;
+  }
+}
+
+template <int RULE>
+static int quantize_entry(const void* w, int dtype, int64_t rows, int64_t K, int bits, int group_size, uint32_t* wq,
+                          void* scales, void* biases, void* stream) {
+  if (rows < 0 || K < 0) return B2F_ERR_INVALID;
+  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
+  if (!(group_size == 32 || group_size == 64 || group_size == 128)) return B2F_ERR_UNSUPPORTED;
+  if (K % group_size != 0) return B2F_ERR_INVALID;
+  if (rows * K == 0) return B2F_OK;
+  if (!w || !wq || !scales || !biases) return B2F_ERR_INVALID;
+  if (!aligned(w, 16) || !aligned(wq, 8)) return B2F_ERR_ALIGN;
+  cudaStream_t st = as_stream(stream);
+  switch (dtype) {
+    case B2F_BF16: return launch_quantize<TagBF16, RULE>(w, rows, K, bits, group_size, wq, scales, biases, st);
+    case B2F_F16: return launch_quantize<TagF16, RULE>(w, rows, K, bits, group_size, wq, scales, biases, st);
+    case B2F_F32: return launch_quantize<TagF32, RULE>(w, rows, K, bits, group_size, wq, scales, biases, st);
     default: return B2F_ERR_UNSUPPORTED;
   }
 }
@@ -329,20 +375,12 @@ const char* b2f_last_error_string(void) { return g_last_error.c_str(); }
 
 int b2f_quantize_affine(const void* w, int dtype, int64_t rows, int64_t K, int bits,
                         int group_size, uint32_t* wq, void* scales, void* biases, void* stream) {
-  if (rows < 0 || K < 0) return B2F_ERR_INVALID;
-  if (!(bits == 2 || bits == 4 || bits == 8)) return B2F_ERR_UNSUPPORTED;
-  if (!(group_size == 32 || group_size == 64 || group_size == 128)) return B2F_ERR_UNSUPPORTED;
-  if (K % group_size != 0) return B2F_ERR_INVALID;
-  if (rows * K == 0) return B2F_OK;
-  if (!w || !wq || !scales || !biases) return B2F_ERR_INVALID;
-  if (!aligned(w, 16) || !aligned(wq, 8)) return B2F_ERR_ALIGN;
-  cudaStream_t st = as_stream(stream);
-  switch (dtype) {
-    case B2F_BF16: return launch_quantize<TagBF16>(w, rows, K, bits, group_size, wq, scales, biases, st);
-    case B2F_F16: return launch_quantize<TagF16>(w, rows, K, bits, group_size, wq, scales, biases, st);
-    case B2F_F32: return launch_quantize<TagF32>(w, rows, K, bits, group_size, wq, scales, biases, st);
-    default: return B2F_ERR_UNSUPPORTED;
-  }
+  return quantize_entry<kRuleMlx>(w, dtype, rows, K, bits, group_size, wq, scales, biases, stream);
+}
+
+int b2f_quantize_affine_minmax(const void* w, int dtype, int64_t rows, int64_t K, int bits, int group_size,
+                               uint32_t* wq, void* scales, void* biases, void* stream) {
+  return quantize_entry<kRuleMinMax>(w, dtype, rows, K, bits, group_size, wq, scales, biases, stream);
 }
 
 int b2f_dequantize_affine(const uint32_t* wq, const void* scales, const void* biases, int dtype,

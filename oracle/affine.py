@@ -1,15 +1,14 @@
 """Oracle: MLX-style affine group quantization of weights (test infrastructure only).
 
+Nothing in the product path imports this module; tests, the smoke check and
+the benchmark's CPU baseline use it as the checker.
+
 Format (the one ``mx.quantize`` produces and ``mx.quantized_matmul`` /
 ``mx.gather_qmm`` consume, as called at
 ``mlx_flash_compress/layer_quantization.py:254`` and
 ``mlx_flash_compress/expert_streaming.py:230-241``):
 
 * ``W[..., K]`` is split along its last axis into groups of ``group_size``.
-* per group: ``scale = (max - min) / (2**bits - 1)`` rounded to the weight
-  dtype, ``bias = min``; ``q = clip(rint((w - bias) / scale), 0, 2**bits-1)``
-  (round half to even); a group whose rounded scale is 0 (constant group) gets
-  ``q = 0`` so that it dequantizes to exactly ``bias``.
 * ``q`` is packed little-end first into uint32 words: element ``k`` sits at bit
   ``bits * (k % (32 // bits))`` of word ``k // (32 // bits)``.  This is the
   unpack order restated in NumPy at ``mixed_precision.py:150-171`` (view the
@@ -17,11 +16,33 @@ Format (the one ``mx.quantize`` produces and ``mx.quantized_matmul`` /
 * dequantize: ``w = q * scale + bias`` (float32 multiply, then float32 add,
   then one rounding into the weight dtype) -- ``mixed_precision.py:161-171``.
 
-The scale/bias rule is the one stated for this workload (scale=(max-min)/15,
-bias=min for 4-bit); MLX's own quantizer is not available here, so parity
-against real MLX is unpinned.  Arithmetic is written with float32 NumPy
-operations so that each step is one IEEE-754 rounding, matching the CUDA
-kernels' ``__fsub_rn``/``__fdiv_rn``/``rintf``.
+Two per-group scale/bias rules (float32 arithmetic, n = 2**bits - 1):
+
+``rule="mlx"`` (default) -- MLX's ``affine_quantize``, restated from the
+published source of ml-explore/mlx (``mlx/ops.cpp`` ``affine_quantize`` and
+its CPU kernel in ``mlx/backend/cpu/quantized.cpp``, releases 0.24-0.26; the
+reference pins ``mlx>=0.24.0``, ``pyproject.toml:26``).  MLX is not
+installable here, so the restatement is checked against hand-derived known
+answers, not against MLX output:
+  1. ``scale = max((max - min) / n, 1e-7)``;
+  2. the edge is the group's larger-magnitude end: if ``|min| > |max|`` the
+     edge is ``min`` and the scale stays positive, else the edge is ``max``
+     and the scale is negated;
+  3. ``q0 = rint(edge / scale)``; if ``q0 != 0`` then ``scale = edge / q0``
+     and ``bias = edge`` (the edge, and zero, land exactly on the code grid),
+     else ``bias = 0``;
+  4. ``q = clip(rint((w - bias) / scale), 0, n)`` with the float32 scale and
+     bias; only then are scale and bias rounded into the weight dtype.
+  ``rint`` rounds half to even (MLX's ``round`` and ``std::rint``).
+
+``rule="minmax"`` -- the rule the single-linear workload states: ``scale =
+(max - min) / n`` rounded to the weight dtype, ``bias = min``, ``q`` computed
+with the rounded scale; a group whose rounded scale is 0 gets ``q = 0`` so
+that it dequantizes to exactly ``bias``.
+
+Arithmetic is written with float32 NumPy operations so that each step is one
+IEEE-754 rounding, matching the CUDA kernels' ``__fsub_rn``/``__fdiv_rn``/
+``rintf``.
 """
 
 import numpy as np
@@ -38,23 +59,39 @@ def _check(bits, group_size, K):
         raise ValueError(f"last dimension {K} must be divisible by group_size {group_size}")
 
 
-def quantize(w, group_size: int = 64, bits: int = 4, dtype: str = "bf16"):
+def quantize(w, group_size: int = 64, bits: int = 4, dtype: str = "bf16", rule: str = "mlx"):
     """Return ``(wq uint32, scales f32, biases f32)``; scales/biases hold ``dtype`` values."""
     w = np.asarray(w, dtype=np.float32)
     K = w.shape[-1]
     _check(bits, group_size, K)
+    if rule not in ("mlx", "minmax"):
+        raise ValueError(f"rule must be 'mlx' or 'minmax', got {rule!r}")
     lead = w.shape[:-1]
     g = w.reshape(*lead, K // group_size, group_size)
     n_bins = np.float32((1 << bits) - 1)
-    wmax = g.max(axis=-1)
-    wmin = g.min(axis=-1)
-    scale = round_to(np.float32(wmax - wmin) / n_bins, dtype).astype(np.float32)
-    bias = wmin.astype(np.float32)
-    safe = np.where(scale == 0, np.float32(1), scale).astype(np.float32)
+    wmax = g.max(axis=-1).astype(np.float32)
+    wmin = g.min(axis=-1).astype(np.float32)
     with np.errstate(invalid="ignore", divide="ignore"):
-        t = (g - bias[..., None]).astype(np.float32) / safe[..., None]
-    q = np.clip(np.rint(t), 0, n_bins)
-    q = np.where((scale == 0)[..., None], 0, q).astype(np.uint32)
+        if rule == "mlx":
+            scale = np.maximum((wmax - wmin).astype(np.float32) / n_bins, np.float32(1e-7)).astype(np.float32)
+            side = np.abs(wmin) > np.abs(wmax)
+            scale = np.where(side, scale, -scale).astype(np.float32)
+            edge = np.where(side, wmin, wmax).astype(np.float32)
+            q0 = np.rint(edge / scale).astype(np.float32)
+            nz = q0 != 0
+            scale = np.where(nz, edge / np.where(nz, q0, np.float32(1)), scale).astype(np.float32)
+            bias = np.where(nz, edge, np.float32(0)).astype(np.float32)
+            t = (g - bias[..., None]).astype(np.float32) / scale[..., None]
+            q = np.clip(np.rint(t), 0, n_bins).astype(np.uint32)
+            scale = round_to(scale, dtype).astype(np.float32)
+            bias = round_to(bias, dtype).astype(np.float32)
+        else:
+            scale = round_to((wmax - wmin).astype(np.float32) / n_bins, dtype).astype(np.float32)
+            bias = wmin.astype(np.float32)
+            safe = np.where(scale == 0, np.float32(1), scale).astype(np.float32)
+            t = (g - bias[..., None]).astype(np.float32) / safe[..., None]
+            q = np.clip(np.rint(t), 0, n_bins)
+            q = np.where((scale == 0)[..., None], 0, q).astype(np.uint32)
     q = q.reshape(*lead, K)
     per = 32 // bits
     qw = q.reshape(*lead, K // per, per)

@@ -1,9 +1,11 @@
 """Generate the committed golden vectors under ``tests/golden/``.
 
-Run from the repository root, in a checkout that has the reference tree
-(szibis/MLX-Flash 0.8.0) at ``/root/reference`` or at ``$MLXFLASH_REF``:
+Run from the repository root with the reference tree (szibis/MLX-Flash
+0.8.0) named by ``$MLXFLASH_REF`` or by the first argument:
 
-    python tests/golden/gen_golden.py
+    MLXFLASH_REF=/path/to/MLX-Flash python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py /path/to/MLX-Flash
+    python tests/golden/gen_golden.py --affine-only     # affine.npz alone
 
 What each fixture pins:
 
@@ -17,8 +19,9 @@ What each fixture pins:
   NumPy, executed unmodified) on weights packed by ``oracle.affine``.  The
   script checks that ``oracle.mixed`` (which unpacks with ``oracle.affine``)
   matches them bit for bit, which pins the affine unpack order and dequant.
-* ``affine.npz`` -- oracle-derived vectors for the affine quantizer and
-  quantized matmul (the quantizer rule lives inside MLX; see ``oracle/affine.py``).
+* ``affine.npz`` -- oracle-derived vectors for the affine quantizer (MLX's
+  edge rule under ``mlx/``, restated from ml-explore/mlx's ``affine_quantize``;
+  the min/max rule elsewhere) and quantized matmul (see ``oracle/affine.py``).
 * ``ep_shard.json`` -- ``ExpertShard`` ownership and ``owner_of`` from
   ``mlx_flash_compress/distributed_experts.py:36-80`` executed unmodified.
 * ``moe_dispatch.npz`` -- ``moe_dispatch_numpy`` (``kernels/ops.py:138-148``).
@@ -39,7 +42,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MLXFLASH_REF", "/root/reference")
+_ARGS = [a for a in sys.argv[1:] if not a.startswith("--")]
+REF = _ARGS[0] if _ARGS else os.environ.get("MLXFLASH_REF")
 sys.path.insert(0, ROOT)
 
 from oracle import affine, kv_sym, mixed  # noqa: E402
@@ -47,6 +51,8 @@ from oracle.fp import round_to  # noqa: E402
 
 
 def _load_ref_module(name, relpath, extra_path=None):
+    if not REF or not os.path.isdir(REF):
+        sys.exit("gen_golden.py needs the reference tree: set MLXFLASH_REF or pass its path as the first argument")
     if extra_path:
         sys.path.insert(0, extra_path)
     path = os.path.join(REF, relpath)
@@ -119,7 +125,7 @@ def gen_mixed(out):
     arrays = {}
     for i, (rows, K, gs) in enumerate([(16, 256, 64), (8, 512, 128), (4, 64, 64)]):
         w = round_to(rng.normal(0, 0.02, (rows, K)).astype(np.float32), "bf16")
-        wq, s, b = affine.quantize(w, gs, 4, "bf16")
+        wq, s, b = affine.quantize(w, gs, 4, "bf16", rule="minmax")
         p2, s2, b2, meta = ref.requantize_4bit_to_2bit(wq, s, b)
         d2 = ref.dequantize_2bit(p2, s2, b2, K)
         op2, os2, ob2 = mixed.requantize_4bit_to_2bit(wq, s, b, gs)
@@ -140,6 +146,9 @@ def gen_mixed(out):
 
 
 def gen_affine(out):
+    """Keys ``b{bits}_g{gs}/*`` and ``f16/*``, ``f32/*``: the min/max rule;
+    ``mlx/b{bits}_g{gs}/*``: MLX's edge rule on the same weights (both rules
+    restated in ``oracle/affine.py``; neither needs the reference tree)."""
     rng = np.random.default_rng(0)
     arrays = {}
     for bits in (2, 4, 8):
@@ -147,7 +156,14 @@ def gen_affine(out):
             w = round_to(rng.normal(0, 0.02, (48, 256)).astype(np.float32), "bf16")
             w[3, :gs] = np.float32(0.015625)  # constant group -> scale 0, exact bias
             w[5, gs:2 * gs] = 0.0
-            wq, s, b = affine.quantize(w, gs, bits, "bf16")
+            w[6, :gs] = -np.abs(w[6, :gs])  # all-negative group: the edge is the min
+            w[7, :gs] = np.abs(w[7, :gs])  # all-positive group: the edge is the max
+            mq, ms, mb = affine.quantize(w, gs, bits, "bf16", rule="mlx")
+            arrays[f"mlx/b{bits}_g{gs}/wq"] = mq
+            arrays[f"mlx/b{bits}_g{gs}/scales"] = ms
+            arrays[f"mlx/b{bits}_g{gs}/biases"] = mb
+            arrays[f"mlx/b{bits}_g{gs}/deq"] = affine.dequantize(mq, ms, mb, gs, bits)
+            wq, s, b = affine.quantize(w, gs, bits, "bf16", rule="minmax")
             x = round_to(rng.standard_normal((8, 256)).astype(np.float32), "bf16")
             y = affine.quantized_matmul(x, wq, s, b, True, gs, bits)
             key = f"b{bits}_g{gs}"
@@ -160,7 +176,10 @@ def gen_affine(out):
             arrays[f"{key}/y"] = y
     for dtype in ("f16", "f32"):
         w = round_to(rng.normal(0, 0.02, (16, 128)).astype(np.float32), dtype)
-        wq, s, b = affine.quantize(w, 64, 4, dtype)
+        wq, s, b = affine.quantize(w, 64, 4, dtype, rule="minmax")
+        mq, ms, mb = affine.quantize(w, 64, 4, dtype, rule="mlx")
+        arrays[f"mlx/{dtype}/wq"], arrays[f"mlx/{dtype}/scales"], arrays[f"mlx/{dtype}/biases"] = mq, ms, mb
+        arrays[f"mlx/{dtype}/deq"] = affine.dequantize(mq, ms, mb, 64, 4, dtype)
         arrays[f"{dtype}/w"] = w
         arrays[f"{dtype}/wq"] = wq
         arrays[f"{dtype}/scales"] = s
@@ -268,6 +287,10 @@ def gen_evict(out):
 
 def main():
     out = HERE
+    if "--affine-only" in sys.argv:
+        gen_affine(out)
+        print("golden vectors written: affine")
+        return
     n = gen_kv(out)
     gen_mixed(out)
     gen_affine(out)

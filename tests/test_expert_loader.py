@@ -85,6 +85,25 @@ def test_per_expert_layouts(tmp_path, mixtral):
     smap.close()
 
 
+def test_per_expert_layout_missing_expert_is_refused(tmp_path):
+    """An expert whose per-expert keys are absent must not shift the local
+    indices of the experts after it: the shard load names the missing ids."""
+    rng = np.random.default_rng(2)
+    E, N, K = 4, 16, 128
+    data = {p: _layer(rng, E, N, K) for p in ("gate_proj", "up_proj", "down_proj")}
+    tensors = {f"model.layers.0.mlp.experts.{e}.{p}.{s}": data[p][s][e]
+               for p in data for s in data[p] for e in range(E) if e != 2}
+    path = str(tmp_path / "gap.safetensors")
+    _write(path, tensors)
+    smap = SafetensorsMap([path])
+    with pytest.raises(KeyError, match=r"experts \[2\]"):
+        load_moe_layer_shard(smap, 0, ExpertShard(rank=0, world_size=1, total_experts=E), None)
+    # a shard that does not own the gap still loads
+    got = load_moe_layer_shard(smap, 0, ExpertShard(rank=0, world_size=2, total_experts=E), None)
+    assert got["up_proj"][0].shape[0] == 2
+    smap.close()
+
+
 @pytest.mark.gpu
 def test_loaded_shard_drives_the_expert_kernels(tmp_path, dev):
     """Quantized experts written as MLX safetensors, loaded to HBM for one

@@ -13,46 +13,54 @@ from helpers import assert_close, to_dev, to_np, u32_to_dev
 pytestmark = pytest.mark.gpu
 
 
-def test_quantize_matches_golden_bit_exact(golden, dev):
+@pytest.mark.parametrize("rule", ["mlx", "minmax"])
+def test_quantize_matches_golden_bit_exact(golden, dev, rule):
     z = golden("affine.npz")
+    pre = "mlx/" if rule == "mlx" else ""
     for bits in (2, 4, 8):
         for gs in (32, 64, 128):
             k = f"b{bits}_g{gs}"
-            wq, s, b = mx_compat.quantize(to_dev(z[f"{k}/w"], "bf16", dev), gs, bits)
+            wq, s, b = mx_compat.quantize(to_dev(z[f"{k}/w"], "bf16", dev), gs, bits, rule=rule)
             assert wq.dtype == torch.uint32
-            assert np.array_equal(to_np(wq), z[f"{k}/wq"]), k
-            assert np.array_equal(to_np(s), z[f"{k}/scales"]), k
-            assert np.array_equal(to_np(b), z[f"{k}/biases"]), k
+            assert np.array_equal(to_np(wq), z[f"{pre}{k}/wq"]), k
+            assert np.array_equal(to_np(s), z[f"{pre}{k}/scales"]), k
+            assert np.array_equal(to_np(b), z[f"{pre}{k}/biases"]), k
             d = mx_compat.dequantize(wq, s, b, gs, bits)
-            assert np.array_equal(to_np(d), z[f"{k}/deq"]), k
+            assert np.array_equal(to_np(d), z[f"{pre}{k}/deq"]), k
     for dt in ("f16", "f32"):
-        wq, s, b = mx_compat.quantize(to_dev(z[f"{dt}/w"], dt, dev), 64, 4)
-        assert np.array_equal(to_np(wq), z[f"{dt}/wq"]) and np.array_equal(to_np(s), z[f"{dt}/scales"])
-        assert np.array_equal(to_np(mx_compat.dequantize(wq, s, b, 64, 4)), z[f"{dt}/deq"])
+        wq, s, b = mx_compat.quantize(to_dev(z[f"{dt}/w"], dt, dev), 64, 4, rule=rule)
+        assert np.array_equal(to_np(wq), z[f"{pre}{dt}/wq"]) and np.array_equal(to_np(s), z[f"{pre}{dt}/scales"])
+        assert np.array_equal(to_np(mx_compat.dequantize(wq, s, b, 64, 4)), z[f"{pre}{dt}/deq"])
 
 
-@pytest.mark.parametrize("bits", [4, 8])
-def test_quantize_config1_full_size_bit_exact(dev, bits):
-    """W[4096, 4096] ~ N(0, 0.02) bf16, group 64: packed words, scales, biases bit-exact."""
+@pytest.mark.parametrize("bits,rule", [(4, "minmax"), (8, "minmax"), (4, "mlx"), (8, "mlx")])
+def test_quantize_config1_full_size_bit_exact(dev, bits, rule):
+    """W[4096, 4096] ~ N(0, 0.02) bf16, group 64: packed words, scales, biases
+    bit-exact (the workload's min/max rule and MLX's edge rule)."""
     rng = np.random.default_rng(0)
     w = round_to(rng.normal(0, 0.02, (4096, 4096)).astype(np.float32), "bf16")
-    wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits)
-    owq, os_, ob = affine.quantize(w, 64, bits)
+    wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits, rule=rule)
+    owq, os_, ob = affine.quantize(w, 64, bits, rule=rule)
     assert np.array_equal(to_np(wq), owq)
     assert np.array_equal(to_np(s), os_) and np.array_equal(to_np(b), ob)
     d = to_np(mx_compat.dequantize(wq, s, b, 64, bits))
     assert np.array_equal(d, affine.dequantize(owq, os_, ob, 64, bits))
 
 
-def test_quantize_edge_groups(dev):
-    w = np.zeros((4, 128), np.float32)
+@pytest.mark.parametrize("rule", ["mlx", "minmax"])
+def test_quantize_edge_groups(dev, rule):
+    w = np.zeros((7, 128), np.float32)
     w[1] = 3.0                      # constant group
     w[2, :64] = np.linspace(-1, 1, 64)
     w[3] = round_to(np.float32(1e-30) * np.arange(128), "bf16")  # tiny range
+    w[4, :64] = -np.linspace(0.1, 1, 64)  # all negative
+    w[4, 64:] = np.linspace(0.1, 1, 64)  # all positive
+    w[5, :2] = [-0.875, 1.0]  # exact q0 (= -8)
+    w[6, :2] = [-1.0, 0.5]  # edge is the min
     w = round_to(w, "bf16")
     for bits in (2, 4, 8):
-        wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits)
-        owq, os_, ob = affine.quantize(w, 64, bits)
+        wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits, rule=rule)
+        owq, os_, ob = affine.quantize(w, 64, bits, rule=rule)
         assert np.array_equal(to_np(wq), owq) and np.array_equal(to_np(s), os_) and np.array_equal(to_np(b), ob)
 
 

@@ -71,7 +71,11 @@ def test_affine_oracle_vectors(golden):
     for bits in (2, 4, 8):
         for gs in (32, 64, 128):
             k = f"b{bits}_g{gs}"
-            wq, s, b = affine.quantize(z[f"{k}/w"], gs, bits)
+            mq, ms, mb = affine.quantize(z[f"{k}/w"], gs, bits)  # MLX's rule is the default
+            assert np.array_equal(mq, z[f"mlx/{k}/wq"])
+            assert np.array_equal(ms, z[f"mlx/{k}/scales"]) and np.array_equal(mb, z[f"mlx/{k}/biases"])
+            assert np.array_equal(affine.dequantize(mq, ms, mb, gs, bits), z[f"mlx/{k}/deq"])
+            wq, s, b = affine.quantize(z[f"{k}/w"], gs, bits, rule="minmax")
             assert np.array_equal(wq, z[f"{k}/wq"])
             assert np.array_equal(s, z[f"{k}/scales"]) and np.array_equal(b, z[f"{k}/biases"])
             assert np.array_equal(affine.dequantize(wq, s, b, gs, bits), z[f"{k}/deq"])
@@ -81,6 +85,51 @@ def test_affine_oracle_vectors(golden):
             assert np.array_equal(y, z[f"{k}/y"])
 
 
+def _group(vals, gs=64):
+    g = np.zeros((1, gs), np.float32)
+    g[0, :len(vals)] = vals
+    return g
+
+
+def test_affine_mlx_rule_known_answers():
+    """MLX's affine_quantize rule, worked by hand (4-bit, n = 15, f32 steps).
+
+    min -1, max 0.5: |min| > |max| so the edge is -1 with a positive scale
+    1.5/15 = 0.1f; q0 = rint(-1/0.1f) = -10, scale = -1/-10 = 0.1f, bias = -1.
+    Codes: -1 -> 0, 0.5 -> rint(1.5/0.1f) = 15, 0 -> rint(1/0.1f) = 10.
+    Stored scale bf16(0.1) = 0.10009765625."""
+    wq, s, b = affine.quantize(_group([-1.0, 0.5]), 64, 4)
+    assert affine.unpack(wq, 4)[0, :3].tolist() == [0, 15, 10]
+    assert s[0, 0] == np.float32(0.10009765625) and b[0, 0] == -1.0
+    # min -0.5, max 1: the edge is the max, the scale negative: -0.1f, bias 1
+    wq, s, b = affine.quantize(_group([-0.5, 1.0]), 64, 4)
+    assert affine.unpack(wq, 4)[0, :3].tolist() == [15, 0, 10]
+    assert s[0, 0] == np.float32(-0.10009765625) and b[0, 0] == 1.0
+    # all zero: range 0 -> scale -1e-7 (|min| > |max| is false), q0 = 0 -> bias 0
+    wq, s, b = affine.quantize(_group([]), 64, 4)
+    assert not wq.any() and b[0, 0] == 0 and s[0, 0] == round_bf16(np.float32(-1e-7))
+    # constant 0.5: scale -1e-7, edge 0.5, q0 = rint(-5e6) -> scale 0.5/q0, bias 0.5, codes 0
+    wq, s, b = affine.quantize(np.full((1, 64), 0.5, np.float32), 64, 4)
+    assert not wq.any() and b[0, 0] == 0.5 and s[0, 0] < 0
+    assert np.all(affine.dequantize(wq, s, b, 64, 4) == 0.5)
+    # equal magnitudes: the edge is the max, scale = -(2/15 in f32 = 0.13333334);
+    # 1/0.13333334 = 7.4999996 so q0 = -7, scale = 1/-7, bias 1: min -1 -> 14, 0 -> 7
+    wq, s, b = affine.quantize(_group([-1.0, 1.0]), 64, 4)
+    assert affine.unpack(wq, 4)[0, :3].tolist() == [14, 0, 7]
+    assert s[0, 0] == round_bf16(np.float32(1) / np.float32(-7)) and b[0, 0] == 1.0
+    # an exact tie in q0 rounds half to even: edge 0.75, range 0.75 + 0.5 = 1.25 -> 1.25/15
+    # = 0.083333336f, 0.75 / 0.083333336f = 8.9999996 -> -9 (no tie); edge 1, min -0.875
+    # range 1.875/15 = 0.125 exactly, 1/0.125 = 8 -> q0 = -8, scale = -0.125, min -> 15
+    wq, s, b = affine.quantize(_group([-0.875, 1.0]), 64, 4)
+    assert affine.unpack(wq, 4)[0, :3].tolist() == [15, 0, 8]
+    assert s[0, 0] == -0.125 and b[0, 0] == 1.0
+    # 8-bit: min -1, max 0.25: scale 1.25/255, q0 = rint(-204.0) -> bias -1 and 0 is code 204
+    wq, s, b = affine.quantize(_group([-1.0, 0.25]), 64, 8)
+    assert affine.unpack(wq, 8)[0, :3].tolist() == [0, 255, 204]
+    with pytest.raises(ValueError, match="rule"):
+        affine.quantize(_group([]), 64, 4, rule="other")
+
+
 def test_affine_unpack_order_and_roundtrip():
     # element k sits at bits 4*(k%8) of word k//8 (mixed_precision.py:150-171)
     words = affine.unpack(np.array([[0x76543210, 0xFEDCBA98]], np.uint32), 4)
@@ -88,9 +137,14 @@ def test_affine_unpack_order_and_roundtrip():
     rng = np.random.default_rng(1)
     w = round_bf16(rng.normal(0, 0.02, (8, 128)).astype(np.float32))
     for bits in (4, 8):
-        wq, s, b = affine.quantize(w, 64, bits)
+        wq, s, b = affine.quantize(w, 64, bits, rule="minmax")
         err = np.abs(affine.dequantize(wq, s, b, 64, bits) - w)
         assert np.all(err <= (s.repeat(64, axis=1) * 0.5 + 1e-6) * 1.01 + np.abs(w) * 2 ** -8)
+        # MLX's rule moves the grid so the edge is exact: at most one step off
+        # (the far end may clip), plus the bf16 rounding of scale and bias
+        wq, s, b = affine.quantize(w, 64, bits)
+        err = np.abs(affine.dequantize(wq, s, b, 64, bits) - w)
+        assert np.all(err <= np.abs(s.repeat(64, axis=1)) * 1.02 + np.abs(w) * 2 ** -7)
 
 
 def test_round_helpers():
