@@ -442,6 +442,342 @@ def run_ours(args):
 
 
 # ---------------------------------------------------------------------------
+# Per-op workloads (single linear, quantized-KV decode attention, one MoE
+# layer): each prints its own JSON line; the default run is the decode step.
+def _graph_time(launch, reps, iters, dev):
+    """Seconds per call of ``launch(i)``: ``reps`` calls on rotating buffers
+    captured in one CUDA graph, replayed ``iters`` times after 3 warm-ups
+    (CUDA events on the replaying stream)."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(reps):
+            launch(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            launch(i)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    del g
+    return e0.elapsed_time(e1) * 1e-3 / (iters * reps)
+
+
+def _op_line(args, metric, value, unit, config, extra, peak, peak_kind, kernels, cpu=None, higher=True):
+    line = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": higher, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded random weights / activations)", "config": config,
+            "kernels": kernels, "peak": {"hbm_gbs": peak, "kind": peak_kind}}
+    line.update(extra)
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_linear(args):
+    """Single 4-bit affine linear W[4096, 4096], x[8, 4096]: quantize (the
+    workload's min/max rule), quantized_matmul, dequantize."""
+    import numpy as np
+    import torch
+
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+    from b200flash.mx_compat import tc_ksplit
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    st = _capi.stream_of(dev)
+    N = K = 4096
+    M, gs, bits = 8, 64, 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    peak, peak_kind = load_peaks()
+    nq = 8  # 8 x 32 MB of bf16 weights per rotation: beyond the 126 MB L2
+    Ws = [(torch.randn(N, K, device=dev, generator=gen) * 0.02).to(torch.bfloat16) for _ in range(nq)]
+    wq = [torch.empty(N, K * bits // 32, dtype=torch.uint32, device=dev) for _ in range(16)]
+    sc = [torch.empty(N, K // gs, dtype=torch.bfloat16, device=dev) for _ in range(16)]
+    bi = [torch.empty(N, K // gs, dtype=torch.bfloat16, device=dev) for _ in range(16)]
+    for i in range(16):
+        call("b2f_quantize_affine_minmax", ptr(Ws[i % nq]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+    x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    deq = [torch.empty(N, K, dtype=torch.bfloat16, device=dev) for _ in range(nq)]
+    q_bytes = N * K * 2 + N * K * bits // 8 + 2 * N * (K // gs) * 2
+    mm_bytes = N * K * bits // 8 + 2 * N * (K // gs) * 2 + M * K * 2 + M * N * 2
+    it = max(args.steps, 20)
+
+    def quant(i):
+        call("b2f_quantize_affine_minmax", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+
+    def quant_mlx(i):
+        call("b2f_quantize_affine", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+
+    def dequant(i):
+        call("b2f_dequantize_affine", ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), 0, N, K, bits, gs, 0, ptr(deq[i]), st)
+
+    def gemv(i):
+        call("b2f_qgemv_affine", ptr(x), K, M, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), N, K, bits, gs, 0, ptr(y), N, st)
+
+    ks = tc_ksplit(N, K, torch.cuda.get_device_properties(dev).multi_processor_count)
+    wsb = int(_capi.lib().b2f_qgemm_splitk_workspace_bytes(M, N, ks))
+    tws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+
+    def tcsplit(i):
+        call("b2f_qgemm_affine_tcgen05_splitk", ptr(x), K, M, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), N, K, bits, gs, 0,
+             ptr(y), N, 16, ks, ptr(tws), wsb, st)
+
+    t = {"quantize_minmax": _graph_time(quant, nq, it, dev), "quantize_mlx": _graph_time(quant_mlx, nq, it, dev),
+         "dequantize": _graph_time(dequant, nq, it, dev), "qmm_gemv": _graph_time(gemv, 16, it * 4, dev),
+         "qmm_tc_splitk": _graph_time(tcsplit, 16, it * 4, dev)}
+    byts = {"quantize_minmax": q_bytes, "quantize_mlx": q_bytes, "dequantize": q_bytes, "qmm_gemv": mm_bytes,
+            "qmm_tc_splitk": mm_bytes}
+    kernels = {k: {"us": round(v * 1e6, 2), "bytes": byts[k], "gbs": round(byts[k] / v / 1e9, 1),
+                   "frac": round(byts[k] / v / 1e9 / peak, 4)} for k, v in t.items()}
+    best = min(("qmm_gemv", "qmm_tc_splitk"), key=lambda k: t[k])
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import affine
+        from oracle.fp import round_bf16
+
+        w = round_bf16(np.random.default_rng(0).normal(0, 0.02, (N, K)).astype(np.float32))
+        xx = round_bf16(np.random.default_rng(1).standard_normal((M, K)).astype(np.float32))
+        c0 = time.perf_counter()
+        owq, osc, obi = affine.quantize(w, gs, bits, rule="minmax")
+        c1 = time.perf_counter()
+        affine.quantized_matmul(xx, owq, osc, obi, True, gs, bits)
+        c2 = time.perf_counter()
+        affine.dequantize(owq, osc, obi, gs, bits)
+        c3 = time.perf_counter()
+        cpu = {"value": round(mm_bytes / (c2 - c1) / 1e9, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+               "sample": (f"NumPy oracle on the full shape: quantize {c1 - c0:.2f} s, quantized_matmul "
+                          f"{c2 - c1:.2f} s, dequantize {c3 - c2:.2f} s")}
+    _op_line(args, "single 4-bit linear: quantized_matmul HBM GB/s (W 4096x4096 g64, x[8,4096])",
+             kernels[best]["gbs"], "GB/s",
+             {"workload": "single 4-bit affine linear W[4096,4096] ~N(0,0.02) bf16, group 64, x[8,4096] ~N(0,1)",
+              "l2_policy": "8 weight copies (quantize / dequantize) and 16 packed copies (qmm) rotated per graph"},
+             {"roofline": {"kernel": best, "bound": "hbm", "achieved": kernels[best]["gbs"], "peak": peak,
+                           "unit": "GB/s", "frac": kernels[best]["frac"], "traffic": None},
+              "ms_per_step": round(t[best] * 1e3, 5)}, peak, peak_kind, kernels, cpu)
+
+
+def run_kv_attention(args):
+    """Quantized-KV decode attention, Llama-3-8B heads (32q / 8kv, d 128),
+    batch 16 x context 8192, 8- and 4-bit KV in 64-token head-major pages;
+    plus the pack of a 512-token prefill chunk of all 16 sequences."""
+    import torch
+
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+    from b200flash.quantized_kv_cache import packed_len, pick_splits
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    st = _capi.stream_of(dev)
+    B, ctx, Hq, Hkv, D, page = 16, 8192, 32, 8, 128, 64
+    peak, peak_kind = load_peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    npg = ctx // page
+    bt = torch.arange(B * npg, dtype=torch.int32, device=dev).reshape(B, npg)
+    sl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, Hq, D, device=dev, generator=gen).to(torch.bfloat16)
+    out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+    ns = pick_splits(B, Hkv, ctx)
+    wsb = int(_capi.lib().b2f_qkv_decode_attn_workspace_bytes(B, Hq, D, ns))
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+    kernels = {}
+    it = max(args.steps, 20)
+    for bits in (8, 4):
+        rb = packed_len(D, bits, 64)
+        pools = []
+        for _ in range(2):  # two pools alternate: each step reads KV the previous step did not
+            kc = torch.randint(0, 256, (B * npg, Hkv, page, rb), dtype=torch.uint8, device=dev, generator=gen)
+            vc = torch.randint(0, 256, (B * npg, Hkv, page, rb), dtype=torch.uint8, device=dev, generator=gen)
+            ks = torch.empty(B * npg, Hkv, page, D // 64, device=dev).uniform_(0.015, 0.03, generator=gen)
+            vs = torch.empty_like(ks).uniform_(0.015, 0.03, generator=gen)
+            pools.append((kc, ks, vc, vs))
+
+        def attn(i, bits=bits, pools=pools):
+            kc, ks, vc, vs = pools[i]
+            call("b2f_qkv_decode_attn", ptr(q), ptr(kc), ptr(ks), ptr(vc), ptr(vs), ptr(bt), npg, ptr(sl), B, Hq, Hkv,
+                 D, page, page, 1, bits, 64, D ** -0.5, ns, ptr(ws), wsb, ptr(out), st)
+
+        tt = _graph_time(attn, 2, it, dev)
+        byts = B * ctx * Hkv * 2 * (rb + 4 * (D // 64)) + 2 * B * Hq * D * 2
+        kernels[f"attention_{bits}bit"] = {"us": round(tt * 1e6, 2), "bytes": byts, "gbs": round(byts / tt / 1e9, 1),
+                                           "frac": round(byts / tt / 1e9 / peak, 4),
+                                           "frac_of_8tbs": round(byts / tt / 8e12, 4)}
+        del pools
+        # the pack of a 512-token chunk of K and V (16 sequences x 8 heads rows)
+        rows = B * 512 * Hkv
+        xs = [torch.randn(rows, D, device=dev, generator=gen).to(torch.bfloat16) for _ in range(8)]
+        pk = torch.empty(rows, rb, dtype=torch.uint8, device=dev)
+        psc = torch.empty(rows, D // 64, dtype=torch.float32, device=dev)
+
+        def pack(i, bits=bits, rb=rb):
+            call("b2f_kv_quantize_sym", ptr(xs[i]), 0, rows, D, bits, 64, 0, ptr(pk), rb, ptr(psc), 0, D // 64, st)
+
+        tp = _graph_time(pack, 8, it, dev) * 2  # K and V
+        pb = 2 * (rows * D * 2 + rows * rb + rows * (D // 64) * 4)
+        kernels[f"pack512_{bits}bit"] = {"us": round(tp * 1e6, 2), "bytes": pb, "gbs": round(pb / tp / 1e9, 1),
+                                         "frac": round(pb / tp / 1e9 / peak, 4)}
+        del xs
+    cpu = None
+    if not args.no_cpu_baseline:
+        import numpy as np
+
+        from oracle import attn as oattn
+        from oracle import kv_sym
+
+        rng = np.random.default_rng(0)
+        kc = rng.integers(0, 255, (ctx, Hkv, D), dtype=np.uint8)
+        ks = rng.uniform(0.015, 0.03, (ctx, Hkv, 2)).astype(np.float32)
+        qq = rng.standard_normal((1, Hq, D)).astype(np.float32)
+        c0 = time.perf_counter()
+        kd = kv_sym.dequantize_tensor(kc, ks, 0 * ks, 8, (ctx, Hkv, D), 64)
+        vd = kv_sym.dequantize_tensor(kc[::-1].copy(), ks, 0 * ks, 8, (ctx, Hkv, D), 64)
+        oattn.decode_attention(qq, [kd], [vd])
+        c1 = time.perf_counter()
+        byts8 = kernels["attention_8bit"]["bytes"]
+        cpu = {"value": round(byts8 / (16 * (c1 - c0)) / 1e9, 3), "unit": "GB/s", "cores": cpu_threads(),
+               "kind": "port", "sample": f"NumPy oracle, 8-bit, 1 of 16 sequences at context {ctx}: {c1 - c0:.2f} s, x16"}
+    k8 = kernels["attention_8bit"]
+    _op_line(args, "quantized-KV decode attention HBM GB/s (8-bit KV, B16 x ctx 8192, 32q/8kv d128)", k8["gbs"], "GB/s",
+             {"workload": "decode attention over 8-bit (and 4-bit) g64 KV, batch 16, context 8192, 32 query / 8 KV "
+                          "heads, head_dim 128, 64-token pages; pack of a 512-token chunk",
+              "l2_policy": "two KV pools alternate (each > 126 MB); 8 pack inputs rotate"},
+             {"roofline": {"kernel": "attention_8bit", "bound": "hbm", "achieved": k8["gbs"], "peak": peak,
+                           "unit": "GB/s", "frac": k8["frac"], "traffic": None},
+              "ms_per_step": round(k8["us"] / 1e3, 5), "context_splits": ns}, peak, peak_kind, kernels, cpu)
+
+
+def run_moe_layer(args):
+    """One Qwen3-30B-A3B-shaped MoE layer (128 experts, top-8, H 2048, I 768,
+    4-bit g64) with Zipf(1.1) routing at 1, 32 and 512 tokens: router + plan,
+    SwiGLU gate/up, down, weighted combine."""
+    import numpy as np
+    import torch
+
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+    from b200flash.decoder import random_qweight, zipf_router_bias
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    st = _capi.stream_of(dev)
+    E, k, H, I, bits, gs = 128, 8, 2048, 768, 4, 64
+    tau = 1.3
+    peak, peak_kind = load_peaks()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    L = 8  # layer copies rotated per graph: 8 x 340 MB of experts
+    beta = torch.from_numpy(np.array(zipf_router_bias(E, k, 1.1, tau))).to(dev)
+    layers = []
+    for _ in range(L):
+        perm = torch.randperm(E, device=dev, generator=gen)
+        layers.append({"g": random_qweight((E, I, H), bits, gs, dev, gen), "u": random_qweight((E, I, H), bits, gs, dev, gen),
+                       "d": random_qweight((E, H, I), bits, gs, dev, gen),
+                       "wr": (torch.randn(E, H, device=dev, generator=gen) * (tau / H ** 0.5)).to(torch.bfloat16),
+                       "rb": beta[perm].contiguous()})
+    per_exp = 3 * (I * H * bits // 8 + 2 * I * (H // gs) * 2)
+    ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    results = {}
+    lib = _capi.lib()
+    for T in (1, 32, 512):
+        A = T * k
+        x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+        zeros = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        gates = torch.empty(T, E, dtype=torch.float32, device=dev)
+        inds = [torch.empty(T, k, dtype=torch.int32, device=dev) for _ in range(L)]
+        scores = torch.empty(T, k, dtype=torch.float32, device=dev)
+        hh = torch.empty(A, I, dtype=torch.bfloat16, device=dev)
+        xs = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(A, H, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        scratch = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        engines = ["mma"] + (["tc_sorted"] if T >= 32 else [])
+        for eng in engines:
+            tile = 16 if eng == "mma" else (64 if A >= 64 * E else 32)
+            pb = int(lib.b2f_moe_plan_workspace_bytes(A, E, tile))
+            pws = torch.empty(pb, dtype=torch.uint8, device=dev)
+
+            def layer(i, eng=eng, tile=tile, pws=pws, pb=pb):
+                ly = layers[i]
+                g, u, d = ly["g"], ly["u"], ly["d"]
+                call("b2f_moe_route_plan", ptr(x), T, H, ptr(ly["wr"]), ptr(ly["rb"]), E, k, 1, ptr(gates),
+                     ptr(inds[i]), ptr(scores), tile, ptr(pws), pb, ptr(status), st)
+                if eng == "mma":
+                    call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
+                         ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
+                         ptr(hh), I, 1, st)
+                    call("b2f_gather_qgemm_affine_mma", ptr(hh), I, 0, 1, 1, A, E, ptr(d.wq), ptr(d.scales),
+                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, st)
+                else:
+                    call("b2f_moe_gather_rows", ptr(x), H, 0, k, A, E, tile, ptr(pws), pb, H, ptr(xs), H, st)
+                    call("b2f_sorted_qgemm_affine_tcgen05", ptr(xs), H, A, E, ptr(g.wq), ptr(g.scales), ptr(g.biases),
+                         ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1,
+                         st)
+                    call("b2f_sorted_qgemm_affine_tcgen05", ptr(hh), I, A, E, ptr(d.wq), ptr(d.scales),
+                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, st)
+                call("b2f_combine_rmsnorm", ptr(zeros), ptr(y), ptr(scores), T, k, ptr(ones), 1e-6, H, ptr(out),
+                     ptr(scratch), st)
+
+            tt = _graph_time(layer, L, max(args.steps, 10), dev)
+            U = float(np.mean([torch.unique(inds[i]).numel() for i in range(L)]))
+            byts = U * per_exp + E * H * 2 + 2 * T * H * 2
+            flops = 2.0 * A * 3 * H * I
+            results[f"T{T}_{eng}"] = {"us": round(tt * 1e6, 2), "distinct_experts": round(U, 1),
+                                      "bytes": int(byts), "gbs": round(byts / tt / 1e9, 1),
+                                      "frac": round(byts / tt / 1e9 / peak, 4), "tflops": round(flops / tt / 1e12, 2)}
+    best = {T: min((v for kk, v in results.items() if kk.startswith(f"T{T}_")), key=lambda v: v["us"])
+            for T in (1, 32, 512)}
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import affine
+        from oracle import moe as omoe
+
+        rng = np.random.default_rng(0)
+        xx = rng.standard_normal((32, H)).astype(np.float32)
+        wrn = rng.normal(0, tau / H ** 0.5, (E, H)).astype(np.float32)
+        oi, os_ = omoe.route(xx, wrn.T, k, bias=np.array(zipf_router_bias(E, k, 1.1, tau)))
+        used = sorted(set(oi.ravel().tolist()))
+        mk = {e: tuple(affine.quantize(rng.normal(0, 0.02, shp).astype(np.float32), gs, bits)
+                       for shp in ((I, H), (I, H), (H, I))) for e in used}
+        c0 = time.perf_counter()
+        dq = {e: tuple(affine.dequantize_f32(*m, gs, bits).astype(np.float64) for m in mk[e]) for e in used}
+        for t in range(32):
+            for j in range(k):
+                g_, u_, d_ = dq[int(oi[t, j])]
+                hv = omoe.silu(g_ @ xx[t]) * (u_ @ xx[t])
+                _ = d_ @ hv
+        c1 = time.perf_counter()
+        cpu = {"value": round(32 / (c1 - c0), 3), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"NumPy oracle MoE layer at 32 tokens ({len(used)} experts): {c1 - c0:.2f} s"}
+    b32 = best[32]
+    _op_line(args, "Qwen3-30B-A3B-shaped MoE layer (4-bit g64, Zipf(1.1) top-8): HBM GB/s at 32 tokens",
+             b32["gbs"], "GB/s",
+             {"workload": "one MoE layer: 128 experts top-8, H 2048, I 768, SwiGLU, 4-bit g64 N(0,0.02); router "
+                          "x.Wr + fitted Zipf(1.1) bias; 1 / 32 / 512 tokens x ~N(0,1)",
+              "l2_policy": f"{L} layer copies (340 MB of experts each) rotated per graph"},
+             {"roofline": {"kernel": "moe_layer_T32", "bound": "hbm", "achieved": b32["gbs"], "peak": peak,
+                           "unit": "GB/s", "frac": b32["frac"], "traffic": None},
+              "ms_per_step": round(b32["us"] / 1e3, 5), "per_tokens": results}, peak, peak_kind, results, cpu)
+
+
+# ---------------------------------------------------------------------------
 def _oracle_sample(args, shape, n_seq, layers_sampled, seed=0):
     """Time the CPU oracle on a bounded sample of the decode step and scale it
     to tok/s: ``layers_sampled`` decoder layers for ``n_seq`` sequences at
@@ -567,6 +903,9 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="decode", choices=["decode", "linear", "kv-attention", "moe-layer"],
+                    help="decode: the 48-layer decode step (the benchmark line); linear / kv-attention / "
+                         "moe-layer: the single-op workloads, one JSON line each")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--moe-engine", default="auto", choices=["auto", "mma", "tc_gather", "tc", "gemv"],
                     help="routed-expert GEMM engine (auto: the decoder's choice for this batch)")
@@ -584,6 +923,12 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "linear":
+        run_linear(args)
+    elif args.workload == "kv-attention":
+        run_kv_attention(args)
+    elif args.workload == "moe-layer":
+        run_moe_layer(args)
     else:
         run_ours(args)
 

@@ -558,6 +558,35 @@ int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, cons
                        int64_t E, int64_t k, int renorm, float* logits_ws, int32_t* inds,
                        float* scores, void* stream);
 
+/* Gate kinds of the _ex routers. */
+#define B2F_GATE_SOFTMAX 0 /* gates = softmax over the experts (expert_streaming.py:440) */
+#define B2F_GATE_SIGMOID 1 /* gates = sigmoid per expert (DeepSeek-V3-style routing) */
+
+/* b2f_moe_route_topk with the gate kind and the LExI skip of the reference's
+ * skip-fallback forward (enable_skip_fallback, expert_streaming.py:439-462):
+ * with skip_threshold > 0, slot 0 (the largest gate) is kept and slot j >= 1
+ * gets score 0 when top1 > skip_threshold * score_j; renorm then divides the
+ * scores by their sum when that sum is positive (:459-460).  The reference
+ * takes top1 from an argpartition whose order inside the top-k MLX does not
+ * define; here slots are in descending gate order, so slot 0 is the largest. */
+int b2f_moe_route_topk_ex(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
+                          int64_t E, int64_t k, int renorm, int gating, float skip_threshold,
+                          float* logits_ws, int32_t* inds, float* scores, void* stream);
+
+/* b2f_moe_route_plan with the gate kind and skip of b2f_moe_route_topk_ex. */
+int b2f_moe_route_plan_ex(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
+                          int64_t E, int64_t k, int renorm, int gating, float skip_threshold,
+                          float* logits_ws, int32_t* inds, float* scores, int tile,
+                          void* plan_workspace, int64_t plan_workspace_bytes, int32_t* status_out,
+                          void* stream);
+
+/* out[t, e] = x[t].wr[e] + bias[e] in f32, then sigmoid if apply_sigmoid: the
+ * shared expert's gate sigmoid(shared_expert_gate(x)) of expert_streaming.py:466-470
+ * (E = 1), or raw router logits.  x bf16 [T,H] (H % 8 == 0, H <= 8192), wr bf16
+ * [E,H] (E <= 256), bias f32 [E] or NULL. */
+int b2f_router_logits(const void* x, int64_t T, int64_t H, const void* wr, const float* bias,
+                      int64_t E, int apply_sigmoid, float* out, void* stream);
+
 /* Greedy next token: out[m] = argmax_v x[m, v] (ties to the lower index). */
 int b2f_argmax_rows(const void* x, int64_t M, int64_t V, int32_t* out, void* stream);
 

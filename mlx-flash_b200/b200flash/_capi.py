@@ -95,6 +95,10 @@ SIGNATURES = {
     "b2f_qk_norm_rope_kv_append": (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P,
                                         _P, _I64, _I64, _I, _P]),
     "b2f_moe_route_topk": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),
+    "b2f_moe_route_topk_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _P]),
+    "b2f_moe_route_plan_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _I, _P, _I64, _P,
+                                   _P]),
+    "b2f_router_logits": (_I, [_P, _I64, _I64, _P, _P, _I64, _I, _P, _P]),
     "b2f_argmax_rows": (_I, [_P, _I64, _I64, _P, _P]),
 }
 

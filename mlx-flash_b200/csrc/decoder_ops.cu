@@ -409,14 +409,20 @@ static int launch_route_logits(const void* x, int64_t T, int64_t H, const void* 
   return check_launch();
 }
 
-// gates = softmax(logits[t]); top-k by value (ties -> lower id); scores are the
-// gates of the top-k, optionally renormalised to sum 1.  One warp per token;
+// gates = softmax(logits[t]) (or sigmoid(logits[t]) per expert); top-k by
+// gate value (ties -> lower id); scores are the gates of the top-k.  With
+// skip > 0 the LExI confidence mask of the reference's skip-fallback forward
+// (expert_streaming.py:451-457) follows: slot 0 (the largest gate) is kept,
+// slot j >= 1 is zeroed when top1 > skip * score_j.  renorm divides the kept
+// scores by their sum when it is positive (:459-460).  One warp per token;
 // the E <= 256 logits live in registers (8 per lane).
 constexpr int TOPK_PER_LANE = 8;
+enum Gating { kGateSoftmax = 0, kGateSigmoid = 1 };
 
-// One warp: softmax and top-k of token t's logits.
+// One warp: gates and top-k of token t's logits.
 __device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int t, int E, int k, int renorm,
-                                                 int32_t* __restrict__ inds, float* __restrict__ scores) {
+                                                 int gating, float skip, int32_t* __restrict__ inds,
+                                                 float* __restrict__ scores) {
   const int lane = threadIdx.x & 31;
   float* lg = logits + int64_t(t) * E;
   float v[TOPK_PER_LANE];
@@ -427,21 +433,31 @@ __device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int
     v[i] = e < E ? lg[e] : -INFINITY;
     mx = fmaxf(mx, v[i]);
   }
-  mx = warp_max<32>(mx);
-  float sum = 0.f;
+  if (gating == kGateSigmoid) {
 #pragma unroll
-  for (int i = 0; i < TOPK_PER_LANE; ++i) {
-    const int e = lane + 32 * i;
-    v[i] = e < E ? expf(v[i] - mx) : -1.f;
-    sum += e < E ? v[i] : 0.f;
-  }
-  sum = warp_sum<32>(sum);
+    for (int i = 0; i < TOPK_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? 1.f / (1.f + expf(-v[i])) : -1.f;
+      if (e < E) lg[e] = v[i];  // leave the gates in the workspace
+    }
+  } else {
+    mx = warp_max<32>(mx);
+    float sum = 0.f;
 #pragma unroll
-  for (int i = 0; i < TOPK_PER_LANE; ++i) {
-    const int e = lane + 32 * i;
-    if (e < E) lg[e] = v[i] / sum;  // leave the gates in the workspace
+    for (int i = 0; i < TOPK_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? expf(v[i] - mx) : 0.f;
+      sum += v[i];
+    }
+    sum = warp_sum<32>(sum);
+#pragma unroll
+    for (int i = 0; i < TOPK_PER_LANE; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? v[i] / sum : -1.f;
+      if (e < E) lg[e] = v[i];
+    }
   }
-  float picked = 0.f, my_score = 0.f;
+  float my_score = 0.f;
   int my_ind = 0;
   for (int j = 0; j < k; ++j) {
     float bv = -1.f;
@@ -463,9 +479,8 @@ __device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int
         bi = oi;
       }
     }
-    const float sc = bv / sum;
     if (lane == j) {
-      my_score = sc;
+      my_score = bv;
       my_ind = bi;
     }
     // the owner lane drops the winner from its candidates
@@ -474,30 +489,35 @@ __device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int
       for (int i = 0; i < TOPK_PER_LANE; ++i)
         if (lane + 32 * i == bi) v[i] = -2.f;
     }
-    picked += sc;
   }
+  if (skip > 0.f && k > 1) {
+    const float top1 = __shfl_sync(0xffffffffu, my_score, 0);
+    if (lane > 0 && lane < k && top1 > skip * my_score) my_score = 0.f;
+  }
+  const float picked = warp_sum<32>(lane < k ? my_score : 0.f);
   if (lane < k) {
     inds[int64_t(t) * k + lane] = my_ind;
-    scores[int64_t(t) * k + lane] = renorm ? my_score / picked : my_score;
+    scores[int64_t(t) * k + lane] = (renorm && picked > 0.f) ? my_score / picked : my_score;
   }
 }
 
 __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
-                                                         int renorm, int32_t* __restrict__ inds,
-                                                         float* __restrict__ scores) {
+                                                         int renorm, int gating, float skip,
+                                                         int32_t* __restrict__ inds, float* __restrict__ scores) {
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (t < T) route_topk_token(logits, t, E, k, renorm, inds, scores);
+  if (t < T) route_topk_token(logits, t, E, k, renorm, gating, skip, inds, scores);
 }
 
 // Top-k of every token, then -- in the last thread block to finish, found
 // with an arrival counter -- the counting sort of the T*k assignments by
 // expert (the MoE plan), so routing and planning take one launch.
 __global__ void __launch_bounds__(256) route_topk_plan_kernel(float* __restrict__ logits, int T, int E, int k,
-                                                              int renorm, int32_t* __restrict__ inds,
+                                                              int renorm, int gating, float skip,
+                                                              int32_t* __restrict__ inds,
                                                               float* __restrict__ scores, int tile, char* ws,
                                                               PlanLayout L, int32_t* status_out) {
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (t < T) route_topk_token(logits, t, E, k, renorm, inds, scores);
+  if (t < T) route_topk_token(logits, t, E, k, renorm, gating, skip, inds, scores);
   __shared__ int is_last;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -509,6 +529,12 @@ __global__ void __launch_bounds__(256) route_topk_plan_kernel(float* __restrict_
   if (!is_last) return;
   __threadfence();
   moe_plan_block(DenseExperts{inds}, T * k, E, tile, ws, L, status_out);
+}
+
+// sigmoid of every element (the shared expert's gate logits, [T, E])
+__global__ void __launch_bounds__(256) sigmoid_inplace_kernel(float* __restrict__ v, int64_t n) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    v[i] = 1.f / (1.f + expf(-v[i]));
 }
 
 __global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
@@ -672,9 +698,11 @@ int b2f_qk_norm_rope_kv_append(const void* qkv, int64_t B, int64_t Hq, int64_t H
                            k_codes, k_scales, v_codes, v_scales, block_table, max_pages, page_size, bits, stream);
 }
 
-int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
-                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, void* stream) {
+int b2f_moe_route_topk_ex(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                          int64_t k, int renorm, int gating, float skip_threshold, float* logits_ws, int32_t* inds,
+                          float* scores, void* stream) {
   if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+  if (!(gating == kGateSoftmax || gating == kGateSigmoid) || !(skip_threshold >= 0.f)) return B2F_ERR_INVALID;
   if (E > 32 * TOPK_PER_LANE) return B2F_ERR_UNSUPPORTED;
   if (H % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (T == 0) return B2F_OK;
@@ -684,14 +712,22 @@ int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, cons
   if (H > 8192) return B2F_ERR_UNSUPPORTED;
   int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, st);
   if (rc != B2F_OK) return rc;
-  route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds, scores);
+  route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, gating,
+                                                           skip_threshold, inds, scores);
   return check_launch();
 }
 
-int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
-                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, int tile,
-                       void* plan_workspace, int64_t plan_workspace_bytes, int32_t* status_out, void* stream) {
+int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, void* stream) {
+  return b2f_moe_route_topk_ex(x, T, H, wr, bias, E, k, renorm, kGateSoftmax, 0.f, logits_ws, inds, scores, stream);
+}
+
+int b2f_moe_route_plan_ex(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                          int64_t k, int renorm, int gating, float skip_threshold, float* logits_ws, int32_t* inds,
+                          float* scores, int tile, void* plan_workspace, int64_t plan_workspace_bytes,
+                          int32_t* status_out, void* stream) {
   if (T < 0 || H <= 0 || E <= 0 || k <= 0 || k > E || k > 32) return B2F_ERR_INVALID;
+  if (!(gating == kGateSoftmax || gating == kGateSigmoid) || !(skip_threshold >= 0.f)) return B2F_ERR_INVALID;
   if (E > 32 * TOPK_PER_LANE || H % 8 != 0 || H > 8192) return B2F_ERR_UNSUPPORTED;
   if (tile < 8 || tile > 256 || tile % 8 != 0) return B2F_ERR_INVALID;
   if (T * k > 0x3fffffff) return B2F_ERR_UNSUPPORTED;
@@ -706,8 +742,31 @@ int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, cons
   char* ws = static_cast<char*>(plan_workspace);
   if (cudaMemsetAsync(reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2, 0, sizeof(int32_t), st) != cudaSuccess)
     return check_launch();
-  route_topk_plan_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, inds,
-                                                                scores, tile, ws, L, status_out);
+  route_topk_plan_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, gating,
+                                                                skip_threshold, inds, scores, tile, ws, L,
+                                                                status_out);
+  return check_launch();
+}
+
+int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                       int64_t k, int renorm, float* logits_ws, int32_t* inds, float* scores, int tile,
+                       void* plan_workspace, int64_t plan_workspace_bytes, int32_t* status_out, void* stream) {
+  return b2f_moe_route_plan_ex(x, T, H, wr, bias, E, k, renorm, kGateSoftmax, 0.f, logits_ws, inds, scores, tile,
+                               plan_workspace, plan_workspace_bytes, status_out, stream);
+}
+
+int b2f_router_logits(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
+                      int apply_sigmoid, float* out, void* stream) {
+  if (T < 0 || H <= 0 || E <= 0) return B2F_ERR_INVALID;
+  if (E > 32 * TOPK_PER_LANE || H % 8 != 0 || H > 8192) return B2F_ERR_UNSUPPORTED;
+  if (T == 0) return B2F_OK;
+  if (!x || !wr || !out) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
+  cudaStream_t st = as_stream(stream);
+  int rc = launch_route_logits(x, T, H, wr, bias, E, out, st);
+  if (rc != B2F_OK || !apply_sigmoid) return rc;
+  const int64_t n = T * E;
+  sigmoid_inplace_kernel<<<unsigned(n < 148 * 8 * 256 ? (n + 255) / 256 : 148 * 8), 256, 0, st>>>(out, n);
   return check_launch();
 }
 

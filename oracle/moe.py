@@ -13,21 +13,48 @@ import numpy as np
 from . import affine
 
 
-def route(x, wr, top_k, renorm=True):
-    """Softmax top-k routing; ``wr`` is [H, E].  Returns (inds [T,k], scores [T,k]).
+def route(x, wr, top_k, renorm=True, bias=None, gating="softmax", skip_threshold=0.0):
+    """Top-k routing; ``wr`` is [H, E].  Returns (inds [T,k], scores [T,k]).
 
-    Ties in the gate value are broken by the lower expert id.
+    ``gating="softmax"``: ``softmax(x.wr + bias)`` (``expert_streaming.py:440``);
+    ``"sigmoid"``: ``sigmoid`` per expert.  Ties in the gate value are broken
+    by the lower expert id; slots are in descending gate order.  With
+    ``skip_threshold > 0``, the LExI mask (``expert_streaming.py:451-457``):
+    slot 0 is kept, slot j >= 1 is zeroed where ``top1 > skip * score_j``;
+    then ``renorm`` divides by the sum where it is positive (``:459-460``).
     """
     logits = np.asarray(x, np.float64) @ np.asarray(wr, np.float64)
-    logits = logits - logits.max(axis=-1, keepdims=True)
-    g = np.exp(logits)
-    g /= g.sum(axis=-1, keepdims=True)
+    if bias is not None:
+        logits = logits + np.asarray(bias, np.float64)
+    if gating == "sigmoid":
+        g = 1.0 / (1.0 + np.exp(-logits))
+    else:
+        logits = logits - logits.max(axis=-1, keepdims=True)
+        g = np.exp(logits)
+        g /= g.sum(axis=-1, keepdims=True)
     order = np.lexsort((np.broadcast_to(np.arange(g.shape[-1]), g.shape), -g), axis=-1)
     inds = order[..., :top_k]
     scores = np.take_along_axis(g, inds, axis=-1)
+    if skip_threshold > 0 and top_k > 1:
+        keep = ~(scores[..., :1] > skip_threshold * scores)
+        keep[..., 0] = True
+        scores = scores * keep
     if renorm:
-        scores = scores / scores.sum(axis=-1, keepdims=True)
+        tot = scores.sum(axis=-1, keepdims=True)
+        scores = np.where(tot > 0, scores / np.where(tot > 0, tot, 1), scores)
     return inds.astype(np.int32), scores
+
+
+def shared_expert(x, gate, up, down, gate_weight=None, group_size=64, bits=4):
+    """``sigmoid(x . gate_weight) * down(silu(gate x) * up x)`` for one dense
+    SwiGLU expert (``expert_streaming.py:466-470``); ``gate``/``up``/``down``
+    are (wq, scales, biases) of single matrices.  Returns [T, H] float64."""
+    x = np.asarray(x, np.float64)
+    Wg, Wu, Wd = (affine.dequantize_f32(*t, group_size, bits).astype(np.float64) for t in (gate, up, down))
+    y = (silu(x @ Wg.T) * (x @ Wu.T)) @ Wd.T
+    if gate_weight is not None:
+        y = y / (1.0 + np.exp(-(x @ np.asarray(gate_weight, np.float64).reshape(-1, 1))))
+    return y
 
 
 def silu(v):

@@ -108,3 +108,36 @@ def test_qmm_shapes(dev, bits, gs, K, N):
 
 def test_qmm_residual(dev):
     _qmm_case(dev, 4, 256, 1024, 4, 64, resid=True)
+
+
+@pytest.mark.parametrize("M,K,bits", [(1, 7168, 4), (8, 7168, 4), (64, 7168, 8), (200, 7168, 4), (8, 14336, 4),
+                                      (3, 14336, 8)])
+def test_qmm_large_k_group64(dev, M, K, bits):
+    """K beyond 64 groups (the DeepSeek-V3 hidden size 7168, 14336) through
+    quantized_matmul's dispatch (tcgen05, split over K at decode sizes)."""
+    assert mx_compat.quantized_matmul_engine(M, 256, K, bits, 64) == "tc"
+    _qmm_case(dev, M, 256, K, bits, 64, seed=M + K)
+
+
+@pytest.mark.parametrize("engine,M,K,gs", [("gemv", 8, 2048, 64), ("tc", 8, 2048, 64), ("tc", 130, 2048, 64),
+                                           ("gemv_k", 5, 4096, 32), ("gemv_k", 9, 2304, 32)])
+def test_qmm_each_engine(dev, engine, M, K, gs):
+    rng = np.random.default_rng(M * 7 + K)
+    N = 192
+    w = round_to(rng.normal(0, 0.02, (N, K)).astype(np.float32), "bf16")
+    x = round_to(rng.standard_normal((M, K)).astype(np.float32), "bf16")
+    r = round_to(rng.standard_normal((M, N)).astype(np.float32), "bf16")
+    wq, s, b = affine.quantize(w, gs, 4)
+    y = mx_compat.quantized_matmul(to_dev(x, "bf16", dev), u32_to_dev(wq, dev), to_dev(s, "bf16", dev),
+                                   to_dev(b, "bf16", dev), True, gs, 4, residual=to_dev(r, "bf16", dev),
+                                   engine=engine)
+    want = affine.quantized_matmul(x, wq, s, b, True, gs, 4, out_dtype="f32") + r
+    assert_close(to_np(y), want, what=f"qmm engine {engine} M={M} K={K} gs={gs}")
+
+
+def test_qmm_gemv_refuses_too_many_groups(dev):
+    x = torch.zeros(2, 4160, dtype=torch.bfloat16, device=dev)
+    wq = torch.zeros(16, 4160 // 8, dtype=torch.uint32, device=dev)
+    s = torch.zeros(16, 65, dtype=torch.bfloat16, device=dev)
+    with pytest.raises(ValueError, match="64 groups"):
+        mx_compat.quantized_matmul(x, wq, s, s, True, 64, 4, engine="gemv")

@@ -172,3 +172,98 @@ def test_fused_route_plan_matches_separate_calls(dev, T, E, k, tile):
         want = affine.gather_qmm(to_np(x)[:, None, None, :], wq, s, b, rhs_indices=to_np(inds),
                                  group_size=64, bits=4, out_dtype="f32")
         assert_close(to_np(out).reshape(want.shape), want, what="grouped GEMM over the fused plan")
+
+
+@pytest.mark.parametrize("engine,T,k,E,N,K,bits", [
+    ("mma", 1, 8, 128, 768, 2048, 4),         # Qwen3-30B-A3B gate/up at one token
+    ("mma", 32, 8, 128, 768, 2048, 4),
+    ("tc_sorted", 512, 8, 16, 768, 2048, 4),  # prefill density: many tokens per expert
+    ("mma", 512, 8, 16, 768, 2048, 4),
+    ("tc", 40, 4, 8, 128, 576, 4),            # odd group count: per-slot tcgen05
+    ("gemv", 6, 2, 8, 128, 1024, 4),
+    ("mma", 9, 8, 16, 256, 7168, 4),          # DeepSeek-V3 hidden size
+    ("tc_sorted", 300, 8, 8, 256, 7168, 4),
+    ("tc_sorted", 70, 4, 8, 128, 2048, 8),
+])
+def test_gather_qmm_each_engine(dev, engine, T, k, E, N, K, bits):
+    """gather_qmm through each kernel it dispatches to, Zipf-skewed routing."""
+    rng = np.random.default_rng(T + E + K)
+    wq, s, b = _experts(rng, E, N, K, bits, 64)
+    x = round_to(rng.standard_normal((T, 1, 1, K)).astype(np.float32), "bf16")
+    p = np.arange(1, E + 1, dtype=np.float64) ** -1.1
+    p /= p.sum()
+    inds = np.stack([rng.choice(E, size=k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
+    out = mx_compat.gather_qmm(to_dev(x, "bf16", dev), *_dev3((wq, s, b), dev),
+                               rhs_indices=torch.from_numpy(inds).to(dev), group_size=64, bits=bits, engine=engine)
+    want = affine.gather_qmm(x, wq, s, b, rhs_indices=inds, group_size=64, bits=bits, out_dtype="f32")
+    assert_close(to_np(out), want, what=f"gather_qmm engine {engine}")
+
+
+@pytest.mark.parametrize("T,E,want", [(1, 128, "mma"), (32, 128, "mma"), (512, 128, "mma"), (512, 16, "tc_sorted")])
+def test_gather_qmm_engine_choice(T, E, want):
+    assert mx_compat.gather_qmm_engine(T * 8, E, 768, 2048, 4, 64) == want
+
+
+@pytest.mark.parametrize("gating,skip,renorm", [("softmax", 3.0, True), ("sigmoid", 0.0, True),
+                                                ("sigmoid", 2.0, False), ("softmax", 1.5, False)])
+def test_router_gating_and_lexi_skip(dev, gating, skip, renorm):
+    """Sigmoid gates and the LExI skip mask (expert_streaming.py:451-460) vs the oracle."""
+    from b200flash.moe import route_topk
+
+    rng = np.random.default_rng(int(skip * 10) + len(gating))
+    T, E, H, k = 96, 64, 1024, 8
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    wr = round_to(rng.normal(0, 0.06, (E, H)).astype(np.float32), "bf16")
+    bias = (-0.8 * np.log(np.arange(1, E + 1))).astype(np.float32)
+    inds, scores = route_topk(to_dev(x, "bf16", dev), to_dev(wr, "bf16", dev), k, torch.from_numpy(bias).to(dev),
+                              renorm, gating=gating, skip_threshold=skip)
+    oi, os_ = moe.route(x, wr.T, k, renorm, bias=bias, gating=gating, skip_threshold=skip)
+    assert np.array_equal(to_np(inds), oi)
+    got = to_np(scores)
+    if skip > 0:
+        # the mask must agree wherever the decision is not within rounding of the threshold
+        assert np.array_equal(got == 0, os_ == 0) or np.abs(got - os_).max() < 1e-3
+        assert (os_ == 0).any(), "the threshold never fired; the case tests nothing"
+    assert_close(got, os_, rtol=1e-4, atol=1e-5, what=f"router {gating} skip {skip}")
+
+
+@pytest.mark.parametrize("engine", ["mma", "tc_sorted", "tc", "gemv"])
+def test_switch_glu_engines(dev, engine):
+    """The routed SwiGLU experts through every engine switch_glu dispatches to."""
+    from b200flash.moe import switch_glu
+
+    rng = np.random.default_rng(len(engine))
+    T, E, H, I, k = 40, 8, 512, 256, 4
+    g, u, d = (_experts(rng, E, n, kk, 4, 64) for n, kk in ((I, H), (I, H), (H, I)))
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    inds = np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+    y = switch_glu(to_dev(x, "bf16", dev), torch.from_numpy(inds).to(dev), _dev3(g, dev), _dev3(u, dev),
+                   _dev3(d, dev), engine=engine)
+    _, _, yk = moe.expert_mlp(x, inds, np.ones(inds.shape), g, u, d)
+    assert_close(to_np(y), yk, what=f"switch_glu {engine}")
+
+
+@pytest.mark.parametrize("gating,skip", [("softmax", 0.0), ("softmax", 2.5), ("sigmoid", 0.0)])
+def test_moe_block_shared_expert(dev, gating, skip):
+    """Routed experts + LExI skip + the sigmoid-gated shared expert
+    (expert_streaming.py:439-472) against the oracle, end to end."""
+    from b200flash.moe import moe_block
+
+    rng = np.random.default_rng(31 + int(skip))
+    T, E, H, I, Is, k = 24, 16, 512, 256, 384, 4
+    g, u, d = (_experts(rng, E, n, kk, 4, 64) for n, kk in ((I, H), (I, H), (H, I)))
+    sg, su, sd = (affine.quantize(round_to(rng.normal(0, 0.02, shp).astype(np.float32), "bf16"), 64, 4)
+                  for shp in ((Is, H), (Is, H), (H, Is)))
+    sw = round_to(rng.normal(0, 0.05, (1, H)).astype(np.float32), "bf16")
+    x = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    wr = round_to(rng.normal(0, 0.05, (E, H)).astype(np.float32), "bf16")
+    res = round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16")
+    out, inds, scores = moe_block(to_dev(x, "bf16", dev), to_dev(wr, "bf16", dev), _dev3(g, dev), _dev3(u, dev),
+                                  _dev3(d, dev), k, residual=to_dev(res, "bf16", dev), gating=gating,
+                                  skip_threshold=skip,
+                                  shared=(_dev3(sg, dev), _dev3(su, dev), _dev3(sd, dev), to_dev(sw, "bf16", dev)))
+    oi, os_ = moe.route(x, wr.T, k, gating=gating, skip_threshold=skip)
+    assert np.array_equal(to_np(inds), oi)
+    y, _, _ = moe.expert_mlp(x, oi, os_, g, u, d)
+    want = y + moe.shared_expert(x, sg, su, sd, sw) + res
+    assert_close(to_np(out), want, what=f"moe block + shared ({gating}, skip {skip})")
