@@ -169,11 +169,11 @@ def profile_kernels(dec, torch):
 
     def timed_call(name, *args):
         tag = None
-        if name == "b2f_gather_qgemm_affine_mma" and args[6] == 1:
+        if name in ("b2f_gather_qgemm_affine_mma", "b2f_gather_qgemm_affine_mma_packed") and args[6] == 1:
             # one-expert plan: the dense q/k/v (or o) projection of the batch
             tag = "qkv_proj" if args[13] == dec.qkv_rows else None
         elif name in ("b2f_gather_qgemv_affine", "b2f_gather_qgemm_affine_tcgen05", "b2f_sorted_qgemm_affine_tcgen05",
-                      "b2f_gather_qgemm_affine_mma"):
+                      "b2f_gather_qgemm_affine_mma", "b2f_gather_qgemm_affine_mma_packed"):
             tag = "moe_gate_up" if state["gather"] % 2 == 0 else "moe_down"
             state["gather"] += 1
         elif name == "b2f_qkv_decode_attn":
@@ -304,7 +304,8 @@ def run_ours(args):
     exchange = EPExchange() if world > 1 else None
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
-                          dense_engine=args.dense_engine, moe_tile=args.moe_tile)
+                          dense_engine=args.dense_engine, moe_tile=args.moe_tile,
+                          moe_packed=not args.moe_unpacked)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -434,6 +435,11 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args, shape)
     del graph
+    if world > 1 and args.strong_batch:
+        # strong scaling: the same global batch spread over the N ranks
+        del dec
+        torch.cuda.empty_cache()
+        result["strong_scaling"] = strong_scaling(args, shape, world, dev, exchange, max_ctx)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -498,7 +504,6 @@ def run_linear(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    st = _capi.stream_of(dev)
     N = K = 4096
     M, gs, bits = 8, 64, 4
     gen = torch.Generator(device=dev)
@@ -510,7 +515,7 @@ def run_linear(args):
     sc = [torch.empty(N, K // gs, dtype=torch.bfloat16, device=dev) for _ in range(16)]
     bi = [torch.empty(N, K // gs, dtype=torch.bfloat16, device=dev) for _ in range(16)]
     for i in range(16):
-        call("b2f_quantize_affine_minmax", ptr(Ws[i % nq]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+        call("b2f_quantize_affine_minmax", ptr(Ws[i % nq]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), _capi.stream_of(dev))
     x = torch.randn(M, K, device=dev, generator=gen).to(torch.bfloat16)
     y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     deq = [torch.empty(N, K, dtype=torch.bfloat16, device=dev) for _ in range(nq)]
@@ -519,16 +524,16 @@ def run_linear(args):
     it = max(args.steps, 20)
 
     def quant(i):
-        call("b2f_quantize_affine_minmax", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+        call("b2f_quantize_affine_minmax", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), _capi.stream_of(dev))
 
     def quant_mlx(i):
-        call("b2f_quantize_affine", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), st)
+        call("b2f_quantize_affine", ptr(Ws[i]), 0, N, K, bits, gs, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), _capi.stream_of(dev))
 
     def dequant(i):
-        call("b2f_dequantize_affine", ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), 0, N, K, bits, gs, 0, ptr(deq[i]), st)
+        call("b2f_dequantize_affine", ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), 0, N, K, bits, gs, 0, ptr(deq[i]), _capi.stream_of(dev))
 
     def gemv(i):
-        call("b2f_qgemv_affine", ptr(x), K, M, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), N, K, bits, gs, 0, ptr(y), N, st)
+        call("b2f_qgemv_affine", ptr(x), K, M, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), N, K, bits, gs, 0, ptr(y), N, _capi.stream_of(dev))
 
     ks = tc_ksplit(N, K, torch.cuda.get_device_properties(dev).multi_processor_count)
     wsb = int(_capi.lib().b2f_qgemm_splitk_workspace_bytes(M, N, ks))
@@ -536,7 +541,7 @@ def run_linear(args):
 
     def tcsplit(i):
         call("b2f_qgemm_affine_tcgen05_splitk", ptr(x), K, M, ptr(wq[i]), ptr(sc[i]), ptr(bi[i]), N, K, bits, gs, 0,
-             ptr(y), N, 16, ks, ptr(tws), wsb, st)
+             ptr(y), N, 16, ks, ptr(tws), wsb, _capi.stream_of(dev))
 
     t = {"quantize_minmax": _graph_time(quant, nq, it, dev), "quantize_mlx": _graph_time(quant_mlx, nq, it, dev),
          "dequantize": _graph_time(dequant, nq, it, dev), "qmm_gemv": _graph_time(gemv, 16, it * 4, dev),
@@ -584,7 +589,6 @@ def run_kv_attention(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    st = _capi.stream_of(dev)
     B, ctx, Hq, Hkv, D, page = 16, 8192, 32, 8, 128, 64
     peak, peak_kind = load_peaks()
     gen = torch.Generator(device=dev)
@@ -612,7 +616,7 @@ def run_kv_attention(args):
         def attn(i, bits=bits, pools=pools):
             kc, ks, vc, vs = pools[i]
             call("b2f_qkv_decode_attn", ptr(q), ptr(kc), ptr(ks), ptr(vc), ptr(vs), ptr(bt), npg, ptr(sl), B, Hq, Hkv,
-                 D, page, page, 1, bits, 64, D ** -0.5, ns, ptr(ws), wsb, ptr(out), st)
+                 D, page, page, 1, bits, 64, D ** -0.5, ns, ptr(ws), wsb, ptr(out), _capi.stream_of(dev))
 
         tt = _graph_time(attn, 2, it, dev)
         byts = B * ctx * Hkv * 2 * (rb + 4 * (D // 64)) + 2 * B * Hq * D * 2
@@ -627,7 +631,7 @@ def run_kv_attention(args):
         psc = torch.empty(rows, D // 64, dtype=torch.float32, device=dev)
 
         def pack(i, bits=bits, rb=rb):
-            call("b2f_kv_quantize_sym", ptr(xs[i]), 0, rows, D, bits, 64, 0, ptr(pk), rb, ptr(psc), 0, D // 64, st)
+            call("b2f_kv_quantize_sym", ptr(xs[i]), 0, rows, D, bits, 64, 0, ptr(pk), rb, ptr(psc), 0, D // 64, _capi.stream_of(dev))
 
         tp = _graph_time(pack, 8, it, dev) * 2  # K and V
         pb = 2 * (rows * D * 2 + rows * rb + rows * (D // 64) * 4)
@@ -676,7 +680,6 @@ def run_moe_layer(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    st = _capi.stream_of(dev)
     E, k, H, I, bits, gs = 128, 8, 2048, 768, 4, 64
     tau = 1.3
     peak, peak_kind = load_peaks()
@@ -718,22 +721,22 @@ def run_moe_layer(args):
                 ly = layers[i]
                 g, u, d = ly["g"], ly["u"], ly["d"]
                 call("b2f_moe_route_plan", ptr(x), T, H, ptr(ly["wr"]), ptr(ly["rb"]), E, k, 1, ptr(gates),
-                     ptr(inds[i]), ptr(scores), tile, ptr(pws), pb, ptr(status), st)
+                     ptr(inds[i]), ptr(scores), tile, ptr(pws), pb, ptr(status), _capi.stream_of(dev))
                 if eng == "mma":
                     call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
                          ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
-                         ptr(hh), I, 1, st)
+                         ptr(hh), I, 1, _capi.stream_of(dev))
                     call("b2f_gather_qgemm_affine_mma", ptr(hh), I, 0, 1, 1, A, E, ptr(d.wq), ptr(d.scales),
-                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, st)
+                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, _capi.stream_of(dev))
                 else:
-                    call("b2f_moe_gather_rows", ptr(x), H, 0, k, A, E, tile, ptr(pws), pb, H, ptr(xs), H, st)
+                    call("b2f_moe_gather_rows", ptr(x), H, 0, k, A, E, tile, ptr(pws), pb, H, ptr(xs), H, _capi.stream_of(dev))
                     call("b2f_sorted_qgemm_affine_tcgen05", ptr(xs), H, A, E, ptr(g.wq), ptr(g.scales), ptr(g.biases),
                          ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1,
-                         st)
+                         _capi.stream_of(dev))
                     call("b2f_sorted_qgemm_affine_tcgen05", ptr(hh), I, A, E, ptr(d.wq), ptr(d.scales),
-                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, st)
+                         ptr(d.biases), 0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, _capi.stream_of(dev))
                 call("b2f_combine_rmsnorm", ptr(zeros), ptr(y), ptr(scores), T, k, ptr(ones), 1e-6, H, ptr(out),
-                     ptr(scratch), st)
+                     ptr(scratch), _capi.stream_of(dev))
 
             tt = _graph_time(layer, L, max(args.steps, 10), dev)
             U = float(np.mean([torch.unique(inds[i]).numel() for i in range(L)]))
@@ -775,6 +778,221 @@ def run_moe_layer(args):
              {"roofline": {"kernel": "moe_layer_T32", "bound": "hbm", "achieved": b32["gbs"], "peak": peak,
                            "unit": "GB/s", "frac": b32["frac"], "traffic": None},
               "ms_per_step": round(b32["us"] / 1e3, 5), "per_tokens": results}, peak, peak_kind, results, cpu)
+
+
+def run_ds_prefill(args):
+    """DeepSeek-V3-shaped MoE layer at prefill: 256 routed experts (top-8,
+    sigmoid gates, the hottest 10% taking 40% of assignments) + 1 shared
+    expert, H 7168, I 2048, SwiGLU, 4-bit g64; 4096 tokens over N ranks
+    (4096/N each), experts sharded in ExpertShard blocks, tokens moved by the
+    counts-then-rows NCCL all-to-all (b200flash.ep_a2a).  One step = router,
+    dispatch, local experts, return, combine and the shared expert."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+    from b200flash.decoder import fit_router_bias, hot_set_frequency, random_qweight
+    from b200flash.distributed_experts import ExpertShard
+    from b200flash.ep import EPExchange
+    from b200flash.ep_a2a import ExpertParallelA2A
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    E, k, H, I, bits, gs = args.experts, 8, 7168, 2048, 4, 64
+    T_all = args.tokens
+    T = T_all // world
+    tau = 1.3
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(100 + rank)
+    shard = ExpertShard(rank=rank, world_size=world, total_experts=E)
+    E_loc = len(shard.owned_experts)
+    g = random_qweight((E_loc, I, H), bits, gs, dev, gen)
+    u = random_qweight((E_loc, I, H), bits, gs, dev, gen)
+    dn = random_qweight((E_loc, H, I), bits, gs, dev, gen)
+    sg = random_qweight((1, I, H), bits, gs, dev, gen)
+    su = random_qweight((1, I, H), bits, gs, dev, gen)
+    sd = random_qweight((1, H, I), bits, gs, dev, gen)
+    rgen = torch.Generator(device=dev)
+    rgen.manual_seed(7)  # the router is the same on every rank
+    perm = torch.randperm(E, device=dev, generator=rgen)
+    beta = torch.from_numpy(np.array(fit_router_bias(hot_set_frequency(E, k, 0.1, 0.4), k, tau))).to(dev)
+    rbias = torch.empty_like(beta)
+    rbias[perm] = beta  # expert perm[i] takes the i-th frequency (the hot set first)
+    wr = (torch.randn(E, H, device=dev, generator=rgen) * (tau / H ** 0.5)).to(torch.bfloat16)
+    x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+    gates = torch.empty(T, E, dtype=torch.float32, device=dev)
+    inds = torch.empty(T, k, dtype=torch.int32, device=dev)
+    scores = torch.empty(T, k, dtype=torch.float32, device=dev)
+    ex = EPExchange() if world > 1 else None
+    ep = ExpertParallelA2A(shard, T, H, I, k, dev, bits, gs, exchange=ex, engine="tc", tile=args.ds_tile)
+    # shared expert: a one-expert plan over this rank's tokens, rows gathered
+    # into the sorted GEMM's layout, SwiGLU fused, then down
+    lib = _capi.lib()
+    sp_bytes = int(lib.b2f_moe_plan_workspace_bytes(T, 1, 128))
+    sp_ws = torch.empty(sp_bytes, dtype=torch.uint8, device=dev)
+    call("b2f_moe_plan", ptr(torch.zeros(T, dtype=torch.int32, device=dev)), T, 1, 128, ptr(sp_ws), sp_bytes, 0,
+         _capi.stream_of(dev))
+    sxs = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    shh = torch.empty(T, I, dtype=torch.bfloat16, device=dev)
+    sy = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    routed = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    scratch = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    ones_h = torch.ones(H, dtype=torch.bfloat16, device=dev)
+    ones_t = torch.ones(T, 1, dtype=torch.float32, device=dev)
+    ev = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for n in ("route", "dispatch", "experts", "return", "shared")}
+
+    def step(record=False):
+        st = _capi.stream_of(dev)
+
+        def mark(n, i):
+            if record:
+                ev[n][i].record()
+
+        mark("route", 0)
+        call("b2f_moe_route_topk_ex", ptr(x), T, H, ptr(wr), ptr(rbias), E, k, 1, 1, 0.0, ptr(gates), ptr(inds),
+             ptr(scores), st)
+        mark("route", 1)
+        mark("dispatch", 0)
+        sc, rc = ep.dispatch(x, inds, scores)
+        mark("dispatch", 1)
+        mark("experts", 0)
+        ep.compute(sum(rc), (g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases), (dn.wq, dn.scales, dn.biases))
+        mark("experts", 1)
+        mark("return", 0)
+        ep.combine(T, sc, rc, out=routed)
+        mark("return", 1)
+        mark("shared", 0)
+        call("b2f_moe_gather_rows", ptr(x), H, 0, 1, T, 1, 128, ptr(sp_ws), sp_bytes, H, ptr(sxs), H, st)
+        call("b2f_sorted_qgemm_affine_tcgen05", ptr(sxs), H, T, 1, ptr(sg.wq), ptr(sg.scales), ptr(sg.biases),
+             ptr(su.wq), ptr(su.scales), ptr(su.biases), I, H, bits, gs, 128, ptr(sp_ws), sp_bytes, ptr(shh), I, 1, st)
+        call("b2f_sorted_qgemm_affine_tcgen05", ptr(shh), I, T, 1, ptr(sd.wq), ptr(sd.scales), ptr(sd.biases), 0, 0, 0,
+             H, I, bits, gs, 128, ptr(sp_ws), sp_bytes, ptr(sy), H, 0, st)
+        call("b2f_combine_rmsnorm", ptr(routed), ptr(sy), ptr(ones_t), T, 1, ptr(ones_h), 1e-6, H, ptr(out),
+             ptr(scratch), st)
+        mark("shared", 1)
+        return sc, rc
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    ep.check()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            sc, rc = step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    t = e0.elapsed_time(e1) * 1e-3 / args.steps
+    sc, rc = step(record=True)
+    torch.cuda.synchronize()
+    phases = {n: ev[n][0].elapsed_time(ev[n][1]) * 1e3 for n in ev}
+    A_here = int((ep.local[: sum(rc) * k] >= 0).sum().item()) if sum(rc) else 0
+    routed_ids = inds.reshape(-1)
+    hot_ids = perm[: max(1, int(round(0.1 * E)))]
+    hot = float(torch.isin(routed_ids, hot_ids).float().mean().item())
+    vals = torch.tensor([t, float(A_here), hot] + [phases[n] for n in ev], device=dev, dtype=torch.float64)
+    if world > 1:
+        tmax = vals[:1].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        allv = [torch.empty_like(vals) for _ in range(world)]
+        dist.all_gather(allv, vals)
+        t = float(tmax.item())
+        per_rank = [v.tolist() for v in allv]
+    else:
+        per_rank = [vals.tolist()]
+    flops = 2.0 * T_all * k * 3 * H * I + 2.0 * T_all * 3 * H * I
+    peak = None
+    try:
+        with open(PEAKS_FILE) as f:
+            pk = json.load(f)
+        peak = float(pk["bf16_tflops"])
+    except Exception:
+        peak = 1590.0
+    if rank == 0:
+        line = {"metric": "DeepSeek-V3-shaped prefill MoE layer TFLOP/s (4-bit g64, 256 experts top-8 + shared)",
+                "value": round(flops / t / 1e12, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": round(t * 1e3, 4), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random)",
+                "config": {"workload": f"MoE layer, {E} routed experts top-{k} (sigmoid gates, hottest 10% take 40% "
+                                       f"of assignments) + 1 shared, H {H}, I {I}, 4-bit g64, {T_all} tokens "
+                                       f"({T} per rank)", "parallelism": f"ep{world} (NCCL all-to-all)",
+                           "expert_tile": args.ds_tile},
+                "roofline": {"kernel": "whole MoE layer", "bound": "tensor", "achieved": round(flops / t / 1e12, 2),
+                             "peak": peak, "unit": "TFLOP/s", "frac": round(flops / t / 1e12 / peak / world, 4),
+                             "traffic": None},
+                "phases_us_rank0": {n: round(phases[n], 1) for n in ev},
+                "per_rank": [{"ms": round(v[0] * 1e3, 3), "assignments": int(v[1]), "hot_share": round(v[2], 3),
+                              "experts_us": round(v[6], 1)} for v in per_rank],
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    del ep
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def strong_scaling(args, shape, world, dev, exchange, max_ctx):
+    """Decode step with ``--strong-batch`` sequences in total (that number / N
+    per rank), timed like the main line (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from b200flash.decoder import Qwen3MoeDecoder
+
+    b = max(1, args.strong_batch // world)
+    dec = Qwen3MoeDecoder(shape, max_batch=b, max_context=max_ctx, page_size=64, device=dev, seed=1234,
+                          layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
+                          dense_engine=args.dense_engine, moe_tile=args.moe_tile, moe_packed=not args.moe_unpacked)
+    dec.fill_random_context(args.ctx)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        dec.step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        dec.step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    tt = torch.tensor([e0.elapsed_time(e1) * 1e-3], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t = float(tt.item())
+    del graph
+    del dec
+    torch.cuda.empty_cache()
+    return {"global_batch": b * world, "batch_per_gpu": b, "value": round(b * world * args.steps / t, 2),
+            "unit": "tok/s", "ms_per_step": round(1e3 * t / args.steps, 4)}
 
 
 # ---------------------------------------------------------------------------
@@ -903,7 +1121,13 @@ def main():
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="decode", choices=["decode", "linear", "kv-attention", "moe-layer"],
+    ap.add_argument("--strong-batch", type=int, default=64,
+                    help="N > 1: also time this global batch spread over the N ranks (0: skip)")
+    ap.add_argument("--experts", type=int, default=256, help="ds-prefill: routed experts")
+    ap.add_argument("--tokens", type=int, default=4096, help="ds-prefill: tokens over all ranks")
+    ap.add_argument("--ds-tile", type=int, default=128, help="ds-prefill: tokens per expert tile")
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "linear", "kv-attention", "moe-layer", "ds-prefill"],
                     help="decode: the 48-layer decode step (the benchmark line); linear / kv-attention / "
                          "moe-layer: the single-op workloads, one JSON line each")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -913,6 +1137,8 @@ def main():
                     help="q/k/v and o projection engine (auto: the decoder's choice for this batch)")
     ap.add_argument("--moe-tile", type=int, default=16, choices=[16, 32],
                     help="tokens per expert tile of the warp-MMA expert GEMM")
+    ap.add_argument("--moe-unpacked", action="store_true",
+                    help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")
     ap.add_argument("--profile-window", action="store_true",
@@ -929,6 +1155,8 @@ def main():
         run_kv_attention(args)
     elif args.workload == "moe-layer":
         run_moe_layer(args)
+    elif args.workload == "ds-prefill":
+        run_ds_prefill(args)
     else:
         run_ours(args)
 

@@ -52,6 +52,23 @@ const char* b2f_status_string(int status);
 /* text of the last CUDA error seen by this thread (or "") */
 const char* b2f_last_error_string(void);
 
+/* Bounded device waits.  Every kernel that waits on a copy or on another warp
+ * (the expert GEMMs, the GEMV, the paged decode attention) gives up after a
+ * time limit instead of spinning forever, skips its remaining work and
+ * records B2F_ERR_TIMEOUT in its call's status word (the MoE plan header, for
+ * the plan-driven GEMMs) and in a library-wide sticky status.
+ * b2f_device_status synchronises the device and reads that sticky status
+ * (B2F_OK or B2F_ERR_TIMEOUT) into *status_out, clearing it if `clear`. */
+int b2f_device_status(int32_t* status_out, int clear);
+
+/* The wait limit in ns for all later launches (0: the default, 2 s). */
+int b2f_set_wait_limit_ns(int64_t ns);
+
+/* Test control: non-zero makes the kernels' producer warps issue no copies,
+ * so their consumers' bounded waits run out (how the tests drive the timeout
+ * path without any fault); 0 (the default) is normal operation. */
+int b2f_set_producer_stall(int on);
+
 /* ---- (a) affine quantize / (a') dequantize ---------------------------- */
 
 /* mx.quantize(w, group_size, bits) as called through
@@ -302,6 +319,30 @@ int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int32_t* x_row
                                 void* plan_workspace, int64_t plan_workspace_bytes, void* out,
                                 int64_t ldo, int out_plan_order, void* stream);
 
+/* Packed expert weights for b2f_gather_qgemm_affine_mma_packed: the 4-bit
+ * codes of E stacked [N, K] matrices (MLX layout, uint32 [E*N, K/8]) re-laid
+ * as one tile per (expert, block of 128 rows for a gate/up matrix (mat 2) or
+ * 256 rows for a down matrix (mat 1), 128-wide K chunk), each tile the exact
+ * shared-memory image the GEMM consumes (64-byte rows, 16-byte word groups
+ * XOR-swizzled by (row / 2) % 4), rows past N zero-filled.  No MLX call
+ * corresponds: an internal layout of HBM-resident experts so each staged tile
+ * is one contiguous bulk copy.  out must hold b2f_mma_packed_bytes. */
+int64_t b2f_mma_packed_bytes(int64_t E, int64_t N, int64_t K, int mat);
+int b2f_mma_repack(const uint32_t* wq, int64_t E, int64_t N, int64_t K, int mat, void* out,
+                   int64_t out_bytes, void* stream);
+
+/* b2f_gather_qgemm_affine_mma (plan tile 16) reading b2f_mma_repack tiles
+ * (mat 2 for pw_gate / pw_up with SwiGLU fused, mat 1 for a single matrix)
+ * instead of the MLX-layout codes; scales and biases stay in MLX layout.
+ * Same results, bit for bit, as the unpacked call. */
+int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                       int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
+                                       const void* pw_gate, const void* s_gate, const void* b_gate,
+                                       const void* pw_up, const void* s_up, const void* b_up,
+                                       int64_t N, int64_t K, int bits, int group_size, int tile,
+                                       void* plan_workspace, int64_t plan_workspace_bytes, void* out,
+                                       int64_t ldo, int out_plan_order, void* stream);
+
 /* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
  * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes
  * fp32 planes partial[z][a][0:N] for every planned assignment a, to be summed
@@ -454,6 +495,39 @@ int b2f_ep_plan(const void* recv, int64_t seg_bytes, int64_t row_bytes, int64_t 
  * output.  bf16 y [G*k, ldy], out [G, ldo]; H % 8 == 0. */
 int b2f_ep_combine_partial(const void* y, int64_t ldy, const float* wts, const int32_t* local,
                            int64_t G, int64_t k, int64_t H, void* out, int64_t ldo, void* stream);
+
+/* ---- (e) expert parallelism over a variable-split all-to-all ---------- */
+/* The dispatch / combine halves of distributed_experts.py:36-150's expert
+ * partition for prefill-sized batches (one NCCL all_to_all_single of counts,
+ * then one of rows, each way).  A dispatched row is [bf16 hidden row H][int32
+ * local expert ids k (-1: another rank's)][float32 scores k], padded to
+ * b2f_ep_a2a_row_pitch(H, k) bytes (a multiple of 16). */
+int64_t b2f_ep_a2a_row_pitch(int64_t H, int64_t k);
+
+/* Pack this rank's T tokens for W ranks: token t goes once to every rank d
+ * owning one of its experts (ExpertShard blocks of floor(E/W), the last rank
+ * the remainder), at row pos[t*W + d] of `send` (rows grouped by d, token order
+ * within d; -1 = not sent); send_counts[d] = rows for d.  x bf16 [T, ldx];
+ * inds int32 / scores f32 [T, k] (global ids in [0, e_total), else
+ * B2F_ERR_INVALID in status_out).  send holds T*min(W,k) rows. */
+int b2f_ep_a2a_dispatch(const void* x, int64_t ldx, const int32_t* inds, const float* scores,
+                        int64_t T, int64_t k, int64_t W, int64_t e_total, int64_t H, void* send,
+                        int64_t send_bytes, int32_t* pos, int32_t* send_counts,
+                        int32_t* status_out, void* stream);
+
+/* MoE plan (as b2f_moe_plan, A = R*k) over R received rows: assignment
+ * a = r*k + j of local expert id j of row r, skipped when -1; per assignment
+ * x_row[a] = r, wts[a] = its score (0 if skipped), local[a] = the id or -1.
+ * The received rows are a bf16 matrix of leading dimension pitch/2 for the
+ * expert kernels' x-row index. */
+int b2f_ep_a2a_plan(const void* recv, int64_t R, int64_t H, int64_t k, int64_t e_count, int tile,
+                    int32_t* x_row, float* wts, int32_t* local, void* workspace,
+                    int64_t workspace_bytes, int32_t* status_out, void* stream);
+
+/* out[t] = resid[t] (if non-NULL) + sum over d = 0..W-1 of ret[pos[t*W + d]]
+ * (rows the owner ranks returned), f32 accumulation, bf16 out [T, ldo]. */
+int b2f_ep_a2a_combine(const void* ret, int64_t ldr, const int32_t* pos, int64_t T, int64_t W,
+                       int64_t H, const void* resid, void* out, int64_t ldo, void* stream);
 
 /* ---- smaller ops: Q4_0 GEMV, kernels/ops.py drop-ins, 2-bit requant,
  *      sensitivity fake quantization ------------------------------------- */

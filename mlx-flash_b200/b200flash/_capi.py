@@ -99,6 +99,17 @@ SIGNATURES = {
     "b2f_moe_route_plan_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _F, _P, _P, _P, _I, _P, _I64, _P,
                                    _P]),
     "b2f_router_logits": (_I, [_P, _I64, _I64, _P, _P, _I64, _I, _P, _P]),
+    "b2f_device_status": (_I, [_P, _I]),
+    "b2f_set_wait_limit_ns": (_I, [_I64]),
+    "b2f_set_producer_stall": (_I, [_I]),
+    "b2f_mma_packed_bytes": (_I64, [_I64, _I64, _I64, _I]),
+    "b2f_mma_repack": (_I, [_P, _I64, _I64, _I64, _I, _P, _I64, _P]),
+    "b2f_gather_qgemm_affine_mma_packed": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _P, _P, _P, _P, _I64,
+                                                _I64, _I, _I, _I, _P, _I64, _P, _I64, _I, _P]),
+    "b2f_ep_a2a_row_pitch": (_I64, [_I64, _I64]),
+    "b2f_ep_a2a_dispatch": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P]),
+    "b2f_ep_a2a_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P, _P]),
+    "b2f_ep_a2a_combine": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P, _P, _I64, _P]),
     "b2f_argmax_rows": (_I, [_P, _I64, _I64, _P, _P]),
 }
 
@@ -168,6 +179,16 @@ def require_cuda(*tensors) -> torch.device:
 
 def ptr(t) -> int:
     return 0 if t is None else t.data_ptr()
+
+
+def device_status(clear: bool = True) -> int:
+    """The library's sticky device status (0, or B2F_ERR_TIMEOUT after a
+    bounded wait gave up); synchronises the device."""
+    st = ctypes.c_int32(0)
+    rc = lib().b2f_device_status(ctypes.byref(st), int(clear))
+    if rc != 0:
+        raise RuntimeError(f"b2f_device_status failed: {rc}")
+    return int(st.value)
 
 
 def stream_of(device) -> int:

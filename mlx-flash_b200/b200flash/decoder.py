@@ -95,9 +95,29 @@ def zipf_router_bias(E: int, k: int, s: float, tau: float, samples: int = 16384,
                      seed: int = 1) -> np.ndarray:
     """Per-rank logit bias beta (float32 [E]) such that the top-k of
     ``beta + tau * z`` (z iid N(0, 1) per expert, the router logits of a
-    Gaussian Wr) selects rank r with frequency ``zipf_selection_frequency``.
-    Fixed-point fit on ``samples`` fixed noise draws: beta += 0.7 log(f/h)."""
-    f = zipf_selection_frequency(E, k, s)
+    Gaussian Wr) selects rank r with frequency ``zipf_selection_frequency``."""
+    return fit_router_bias(tuple(zipf_selection_frequency(E, k, s)), k, tau, samples, iters, seed)
+
+
+def hot_set_frequency(E: int, k: int, hot_frac: float, hot_share: float) -> tuple:
+    """Per-token selection frequency when the hottest ``round(hot_frac * E)``
+    experts take ``hot_share`` of the T*k assignments, evenly within the hot
+    and the cold set (hot first)."""
+    nh = max(1, int(round(hot_frac * E)))
+    fh = hot_share * k / nh
+    fc = (1.0 - hot_share) * k / (E - nh)
+    return tuple([fh] * nh + [fc] * (E - nh))
+
+
+@functools.lru_cache(maxsize=8)
+def fit_router_bias(freq: tuple, k: int, tau: float, samples: int = 16384, iters: int = 60,
+                    seed: int = 1) -> np.ndarray:
+    """Per-expert logit bias beta (float32 [E]) such that the top-k of
+    ``beta + tau * z`` (z iid N(0, 1)) selects expert e with per-token
+    frequency ``freq[e]`` (sum k).  Fixed-point fit on ``samples`` fixed
+    noise draws: beta += 0.7 log(f / h)."""
+    f = np.asarray(freq, np.float64)
+    E = f.size
     z = (tau * np.random.default_rng(seed).standard_normal((samples, E))).astype(np.float32)
     beta = np.log(f).astype(np.float32)
     for _ in range(iters):
@@ -152,7 +172,7 @@ class Qwen3MoeDecoder:
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
                  device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
-                 dense_engine: str = "auto", moe_tile: int = 16):
+                 dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True):
         self.s = s = shape
         self.dev = dev = torch.device(device)
         self.B = max_batch
@@ -266,6 +286,20 @@ class Qwen3MoeDecoder:
             self.xs = torch.empty(A, H, dtype=torch.bfloat16, device=dev) if moe_engine == "tc" else None
         else:
             self.tile = self.ep.tile
+        # warp-MMA experts read their codes as packed tiles (b2f_mma_repack:
+        # one contiguous bulk copy per staged tile); the MLX-layout codes stay
+        # for export and the expert-parallel path
+        self.moe_packed = bool(moe_packed) and self.ep is None and self.moe_engine == "mma" and self.tile == 16
+        if self.moe_packed:
+            lib = _capi.lib()
+            st = _capi.stream_of(dev)
+            for ly in self.layers:
+                for name, mat in (("gate", 2), ("up", 2), ("down", 1)):
+                    w = ly[name]
+                    nbytes = int(lib.b2f_mma_packed_bytes(E_loc, w.N, w.K, mat))
+                    pk = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+                    call("b2f_mma_repack", ptr(w.wq), E_loc, w.N, w.K, mat, ptr(pk), nbytes, st)
+                    ly[name + "_packed"] = pk
         self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
         self.next_tokens = torch.empty(B, dtype=torch.int32, device=dev)
         self.n_splits = pick_splits(B, Hkv, max_context)
@@ -412,7 +446,15 @@ class Qwen3MoeDecoder:
             call("b2f_moe_route_plan", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
                  self.plan_bytes, ptr(self.plan_status), st)
-            if self.moe_engine == "mma":
+            if self.moe_packed:
+                # gate/up rows land in plan order (the down GEMM's input layout)
+                call("b2f_gather_qgemm_affine_mma_packed", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(ly["gate_packed"]),
+                     ptr(g.scales), ptr(g.biases), ptr(ly["up_packed"]), ptr(u.scales), ptr(u.biases), I, H, g.bits,
+                     g.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, 1, st)
+                call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), I, 0, 1, 1, A, E, ptr(ly["down_packed"]),
+                     ptr(d.scales), ptr(d.biases), 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws),
+                     self.plan_bytes, ptr(self.y), H, 0, st)
+            elif self.moe_engine == "mma":
                 # gate/up rows land in plan order (the down GEMM's input layout)
                 call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(g.wq), ptr(g.scales),
                      ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, g.bits, g.group_size, self.tile,

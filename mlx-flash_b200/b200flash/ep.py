@@ -86,6 +86,11 @@ class EPExchange:
     def all_gather(self, recv: torch.Tensor, send: torch.Tensor):
         dist.all_gather_into_tensor(recv, send, group=self.group)
 
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits=None, in_splits=None):
+        """``all_to_all_single`` over the group's first dimension (splits in rows)."""
+        dist.all_to_all_single(out, inp, output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=self.group)
+
     def reduce_scatter(self, out: torch.Tensor, inp: torch.Tensor):
         if self.backend == "nccl":
             dist.reduce_scatter_tensor(out, inp, op=dist.ReduceOp.SUM, group=self.group)

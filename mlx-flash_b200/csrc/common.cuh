@@ -157,11 +157,35 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// ---- bounded waits: limit, sticky timeout status, test control ----------
+// One copy per translation unit (the library is built without relocatable
+// device code); the host reaches every unit's copy through b2f_device_status,
+// b2f_set_wait_limit_ns and b2f_set_producer_stall.
+//   b2f_tu_status   B2F_ERR_TIMEOUT once any kernel of the unit had a bounded
+//                   wait give up (sticky until read with clear)
+//   b2f_tu_wait_ns  the default wait limit (2 s)
+//   b2f_tu_stall    test control, 0 in normal operation: non-zero makes the
+//                   producer warps issue no copies, so the consumers' waits
+//                   run out (how the tests exercise the timeout paths)
+static __device__ int32_t b2f_tu_status = 0;
+static __device__ unsigned long long b2f_tu_wait_ns = 2000000000ull;
+static __device__ int32_t b2f_tu_stall = 0;
+
+__device__ __forceinline__ bool producers_stalled() { return *const_cast<volatile int32_t*>(&b2f_tu_stall) != 0; }
+
+// A kernel whose bounded wait gave up: the call's own status word (if any)
+// and the unit's sticky status both get B2F_ERR_TIMEOUT.
+__device__ __forceinline__ void report_timeout(int32_t* err) {
+  if (err) atomicExch(err, B2F_ERR_TIMEOUT);
+  atomicExch(&b2f_tu_status, B2F_ERR_TIMEOUT);
+}
+
 // Waits for the phase with the given parity; gives up after `limit_ns`
-// (returns false) instead of spinning forever.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
-                                                  uint64_t limit_ns = 2000000000ull) {
+// (0: the unit's limit, 2 s by default) and returns false instead of
+// spinning forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (limit_ns == 0) limit_ns = *const_cast<volatile unsigned long long*>(&b2f_tu_wait_ns);
   const uint64_t t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
     if (global_ns() - t0 > limit_ns) return false;
@@ -171,9 +195,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // mbar_wait_bounded for a thread that has nothing else to do while it waits
 // (a producer whose ring is full): backs off between polls so the spinning
 // thread leaves the issue slots to the warps doing the work.
-__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_t parity,
-                                                          uint64_t limit_ns = 2000000000ull) {
+__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (limit_ns == 0) limit_ns = *const_cast<volatile unsigned long long*>(&b2f_tu_wait_ns);
   const uint64_t t0 = global_ns();
   uint32_t ns = 32;
   while (!mbar_try_wait(bar, parity)) {
@@ -183,6 +207,30 @@ __device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_
   }
   return true;
 }
+// Host accessor of this unit's controls (one per .cu file with bounded
+// waits): op 0 reads the status into *v, 1 reads and clears it, 2 sets the
+// wait limit to *v ns, 3 sets the producer stall to *v.
+#define B2F_DEFINE_WAIT_CONTROLS(NAME)                                                            \
+  int b2f_wait_controls_##NAME(int op, long long* v) {                                           \
+    cudaError_t e = cudaSuccess;                                                                  \
+    if (op == 0 || op == 1) {                                                                     \
+      int32_t st = 0;                                                                             \
+      e = cudaMemcpyFromSymbol(&st, b2f_tu_status, sizeof(st));                                   \
+      *v = st;                                                                                    \
+      if (e == cudaSuccess && op == 1) {                                                          \
+        const int32_t z = 0;                                                                      \
+        e = cudaMemcpyToSymbol(b2f_tu_status, &z, sizeof(z));                                     \
+      }                                                                                           \
+    } else if (op == 2) {                                                                         \
+      const unsigned long long ns = (unsigned long long)(*v);                                     \
+      e = cudaMemcpyToSymbol(b2f_tu_wait_ns, &ns, sizeof(ns));                                    \
+    } else if (op == 3) {                                                                         \
+      const int32_t on = int32_t(*v);                                                             \
+      e = cudaMemcpyToSymbol(b2f_tu_stall, &on, sizeof(on));                                      \
+    }                                                                                             \
+    return e == cudaSuccess ? 0 : -1;                                                             \
+  }
+
 // named barrier over the first `nthreads` threads of the CTA (id 1)
 __device__ __forceinline__ void named_sync(int nthreads) {
   asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");

@@ -123,6 +123,32 @@ struct GatheredExperts {
   }
 };
 
+// Expert ids carried in the rows an all-to-all dispatch delivered: received
+// row r (pitch `pitch` bytes) holds the token's bf16 hidden row (H values),
+// then int32 local expert ids [k] (-1 where that slot's expert lives on
+// another rank) at meta_off, then float32 scores [k] at meta_off + 4k.
+// Assignment a = r*k + j.  Side outputs as for GatheredExperts.
+struct A2AExperts {
+  const char* recv;
+  int64_t pitch, meta_off;
+  int k;
+  int32_t* x_row;
+  float* wts;
+  int32_t* local;
+  __device__ __forceinline__ int expert(int a) const {
+    const int r = a / k, j = a - r * k;
+    return reinterpret_cast<const int32_t*>(recv + int64_t(r) * pitch + meta_off)[j];
+  }
+  __device__ __forceinline__ bool invalid(int a, int e, int E) const { return e < -1 || e >= E; }
+  __device__ __forceinline__ void side(int a, int e, int E) const {
+    const int r = a / k, j = a - r * k;
+    const bool mine = e >= 0 && e < E;
+    x_row[a] = r;
+    wts[a] = mine ? reinterpret_cast<const float*>(recv + int64_t(r) * pitch + meta_off + 4 * k)[j] : 0.0f;
+    local[a] = mine ? e : -1;
+  }
+};
+
 // The counting sort, run by one whole thread block (any blockDim <= 1024).
 // Per-expert counters live in shared memory (E <= PLAN_SMEM_E) so the
 // count / scan / scatter phases cost shared-memory atomics and block

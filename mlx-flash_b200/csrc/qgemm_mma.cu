@@ -88,6 +88,10 @@ struct MmaParams {
   float* partial;  // split-K: fp32 planes [gridDim.z][A][N] instead of bf16 out (one matrix)
   int64_t plane;   // elements per partial plane (A * N)
   int slot_major;  // grid x = slot (the slots sharing a row block run back to back and hit L2)
+  // packed weights (b2f_mma_repack): tile (expert, row block, chunk) at byte
+  // ((expert * nb + row block) * (K/128) + chunk) * tile_bytes of pw[m]
+  const uint8_t* pw[2];
+  int64_t nb;
 };
 
 __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
@@ -375,7 +379,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   }
 }
 
-template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false>
+template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false, bool PACKED = false>
 __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
     qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
                      const __grid_constant__ CUtensorMap tm1) {
@@ -420,6 +424,7 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
 
   if (warp == MMA_CW) {
     // ---- producer: weight tiles by TMA, one token row per lane by bulk copy ----
+    if (producers_stalled()) return;  // test control: nothing is issued, the consumers' waits run out
     constexpr int XPL = (TILE + 31) / 32;  // token rows per producer lane
     const __nv_bfloat16* xrow[XPL];
 #pragma unroll
@@ -456,8 +461,16 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       if (!ok) break;
       uint8_t* st = smem + s * STAGE;
       if (lane == 0) {
-        tma_load_2d(st, &tm0, h * (4 * BITS), wrow, &full[s]);
-        if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, h * (4 * BITS), wrow, &full[s]);
+        if constexpr (PACKED) {
+          // the tile is stored as its shared-memory image: one contiguous copy per matrix
+          constexpr uint32_t TB = uint32_t(CTA_ROWS * RBY);
+          const int64_t off = ((int64_t(expert) * p.nb + rblk) * (p.K >> 7) + h) * int64_t(TB);
+          bulk_g2s(st, p.pw[0] + off, TB, &full[s]);
+          if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, TB, &full[s]);
+        } else {
+          tma_load_2d(st, &tm0, h * (4 * BITS), wrow, &full[s]);
+          if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, h * (4 * BITS), wrow, &full[s]);
+        }
       }
 #pragma unroll
       for (int u = 0; u < XPL; ++u) {
@@ -500,7 +513,7 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
     mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
                                                   expert, begin, cnt, row_base, h0, h1, warp, lane);
   }
-  if (lane == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+  if (lane == 0 && *abort_flag) report_timeout(p.err);
 }
 
 // Code rows as a 2-D uint32 tensor [rows, K*bits/32]; box = one 128-wide K
@@ -519,7 +532,7 @@ static int make_mma_weight_map(CUtensorMap* map, const uint32_t* w, int64_t rows
   return r == CUDA_SUCCESS ? B2F_OK : B2F_ERR_INVALID;
 }
 
-template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false>
+template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false, bool PACKED = false>
 static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, int64_t E, int64_t slots_grid,
                           int ksplit, cudaStream_t st) {
   using SH = MmaShape<TILE>;
@@ -532,15 +545,17 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   p.stages = S;
   const int smem = S * STAGE + 1024 + 256;
   CUtensorMap m0{}, m1{};
-  int rc = make_mma_weight_map(&m0, w0, E * p.N, p.K, CTA_ROWS, BITS);
-  if (rc != B2F_OK) return rc;
-  if (w1) {
-    rc = make_mma_weight_map(&m1, w1, E * p.N, p.K, CTA_ROWS, BITS);
+  if constexpr (!PACKED) {
+    int rc = make_mma_weight_map(&m0, w0, E * p.N, p.K, CTA_ROWS, BITS);
     if (rc != B2F_OK) return rc;
-  } else {
-    m1 = m0;
+    if (w1) {
+      rc = make_mma_weight_map(&m1, w1, E * p.N, p.K, CTA_ROWS, BITS);
+      if (rc != B2F_OK) return rc;
+    } else {
+      m1 = m0;
+    }
   }
-  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16>;
+  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16, PACKED>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -557,6 +572,34 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   return check_launch();
 }
 
+// Packed expert weights for the warp-MMA GEMM: 4-bit codes [E*N rows, K/8
+// words] (MLX layout) -> per (expert, row block of `cr` rows, 128-wide K chunk)
+// one 64*cr-byte tile holding exactly the shared-memory image a 64B-swizzled
+// TMA box of that tile would give: row r of the tile at byte 64r, its 16-byte
+// word group j at position j ^ ((r >> 1) & 3).  Rows past N are zero.  The
+// producer then fetches each tile with one contiguous bulk copy.
+__global__ void __launch_bounds__(256) mma_repack_kernel(const uint32_t* __restrict__ wq, int64_t E, int64_t N,
+                                                         int64_t K, int cr, int64_t nb, uint4* __restrict__ out) {
+  const int hc = int(K >> 7);
+  const int64_t groups = E * nb * hc * cr * 4;  // 16-byte word groups of the output
+  for (int64_t o = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; o < groups;
+       o += int64_t(gridDim.x) * blockDim.x) {
+    const int pos = int(o & 3);
+    int64_t t = o >> 2;
+    const int rr = int(t % cr);
+    t /= cr;
+    const int h = int(t % hc);
+    t /= hc;
+    const int64_t rb = t % nb;
+    const int64_t e = t / nb;
+    const int64_t row = rb * cr + rr;
+    const int jj = pos ^ ((rr >> 1) & 3);
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < N) v = reinterpret_cast<const uint4*>(wq + (e * N + row) * (K / 8) + int64_t(h) * 16)[jj];
+    out[o] = v;
+  }
+}
+
 // K split into ranges of whole 128-wide chunks: the number of non-empty ranges
 static int mma_splitk_ranges(int64_t K, int ksplit, int* cpk) {
   const int hc = int(K / 128);
@@ -569,6 +612,8 @@ static int mma_splitk_ranges(int64_t K, int ksplit, int* cpk) {
 // plan layout helpers live in qgemv.cu
 int64_t plan_slots_offset(int64_t A, int64_t E, int tile);
 int64_t plan_sorted_offset(int64_t A, int64_t E, int tile);
+
+B2F_DEFINE_WAIT_CONTROLS(mma)
 
 }  // namespace b2f
 
@@ -639,6 +684,89 @@ extern "C" int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int
   }
   return xp ? launch_mma_cfg<1, true, 16>(p, w_gate, nullptr, E, max_slots, 1, st)
             : launch_mma_cfg<1, false, 16>(p, w_gate, nullptr, E, max_slots, 1, st);
+}
+
+// rows per packed tile: the CTA rows of one matrix at plan tile 16
+static int mma_packed_rows(int mat) { return mat == 2 ? MMA_CW * MmaShape<16>::WROWS / 2 : MMA_CW * MmaShape<16>::WROWS; }
+
+extern "C" int64_t b2f_mma_packed_bytes(int64_t E, int64_t N, int64_t K, int mat) {
+  if (E <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || !(mat == 1 || mat == 2)) return 0;
+  const int cr = mma_packed_rows(mat);
+  const int64_t nb = (N + cr - 1) / cr;
+  return E * nb * (K / 128) * int64_t(cr) * 64;
+}
+
+extern "C" int b2f_mma_repack(const uint32_t* wq, int64_t E, int64_t N, int64_t K, int mat, void* out,
+                              int64_t out_bytes, void* stream) {
+  if (E <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || !(mat == 1 || mat == 2)) return B2F_ERR_INVALID;
+  if (!wq || !out) return B2F_ERR_INVALID;
+  if (out_bytes < b2f_mma_packed_bytes(E, N, K, mat)) return B2F_ERR_WORKSPACE;
+  if (!aligned(wq, 16) || !aligned(out, 16)) return B2F_ERR_ALIGN;
+  const int cr = mma_packed_rows(mat);
+  const int64_t nb = (N + cr - 1) / cr;
+  const int64_t groups = E * nb * (K / 128) * cr * 4;
+  int64_t grid = (groups + 255) / 256;
+  if (grid > 148 * 32) grid = 148 * 32;
+  mma_repack_kernel<<<unsigned(grid), 256, 0, as_stream(stream)>>>(wq, E, N, K, cr, nb, static_cast<uint4*>(out));
+  return check_launch();
+}
+
+extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
+                                                  int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
+                                                  const void* pw_gate, const void* s_gate, const void* b_gate,
+                                                  const void* pw_up, const void* s_up, const void* b_up, int64_t N,
+                                                  int64_t K, int bits, int group_size, int tile,
+                                                  void* plan_workspace, int64_t plan_workspace_bytes, void* out,
+                                                  int64_t ldo, int out_plan_order, void* stream) {
+  if (bits != 4 || group_size != 64 || tile != 16) return B2F_ERR_UNSUPPORTED;
+  if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
+  if (A < 0 || E <= 0) return B2F_ERR_INVALID;
+  if (A == 0) return B2F_OK;
+  if (!x || !pw_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
+  if (pw_up && (!s_up || !b_up)) return B2F_ERR_INVALID;
+  if (!x_plan_order && !x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
+  if (ldx < K || ldo < N) return B2F_ERR_INVALID;
+  if (E * N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(pw_gate, 16) || (pw_up && !aligned(pw_up, 16)) ||
+      !aligned(out, 4) || ldo % 2 != 0 || !aligned(s_gate, 4) || !aligned(b_gate, 4) ||
+      (pw_up && (!aligned(s_up, 4) || !aligned(b_up, 4))))
+    return B2F_ERR_ALIGN;
+  const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
+  if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
+  const int64_t max_slots = b2f_moe_plan_max_slots(A, E, tile);
+  if (max_slots > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  char* ws = static_cast<char*>(plan_workspace);
+  MmaParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.x_row_index = x_row_index;
+  p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
+  p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
+  p.s[1] = static_cast<const __nv_bfloat16*>(s_up);
+  p.b[1] = static_cast<const __nv_bfloat16*>(b_up);
+  p.pw[0] = static_cast<const uint8_t*>(pw_gate);
+  p.pw[1] = static_cast<const uint8_t*>(pw_up);
+  const int mat = pw_up ? 2 : 1;
+  p.nb = (N + mma_packed_rows(mat) - 1) / mma_packed_rows(mat);
+  p.N = N;
+  p.K = K;
+  p.G = int(K / 64);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.out_plan = out_plan_order ? 1 : 0;
+  p.slot_count = reinterpret_cast<const int32_t*>(ws);
+  p.err = reinterpret_cast<int32_t*>(ws) + 1;
+  p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
+  p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
+  p.cpk = int(K / 128);
+  cudaStream_t st = as_stream(stream);
+  const bool xp = x_plan_order != 0;
+  if (pw_up)
+    return xp ? launch_mma_cfg<2, true, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st)
+              : launch_mma_cfg<2, false, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st);
+  return xp ? launch_mma_cfg<1, true, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st)
+            : launch_mma_cfg<1, false, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st);
 }
 
 extern "C" int b2f_mma_splitk_ranges(int64_t K, int ksplit) {

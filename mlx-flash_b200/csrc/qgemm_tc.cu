@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
 
   if (warp == 0) {
     // =========================== TMA producer ================================
-    if (lane == 0) {
+    if (lane == 0 && !producers_stalled()) {
       const int row0 = int(int64_t(expert) * p.N + m0);
       for (int c = 0; c < n_chunks; ++c) {
         const int s = c % PS;
@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
-  if (tid == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+  if (tid == 0 && *abort_flag) report_timeout(p.err);
 }
 
 // split-K: out[m, n] = bf16(sum_k partial[k, m, n] + residual[m, n])
@@ -474,6 +474,8 @@ static int check_tc_shape(int64_t N, int64_t K, int bits, int gs) {
 // plan layout helpers live in qgemv.cu
 int64_t plan_slots_offset(int64_t A, int64_t E, int tile);
 int64_t plan_sorted_offset(int64_t A, int64_t E, int tile);
+
+B2F_DEFINE_WAIT_CONTROLS(tc)
 
 }  // namespace b2f
 

@@ -125,7 +125,8 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     // Control flow stays warp-uniform: lane 0 waits, the verdict is broadcast.
     int gsx = 0;  // stage sequence number
     bool stop = __shfl_sync(0xffffffffu, *abort_flag, 0) != 0;
-    for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+    const bool stall = producers_stalled();  // test control: nothing is issued
+    for (int u = blockIdx.x; u < n_units && !stop && !stall; u += gridDim.x) {
       const int4 sl = p.slots[u / p.n_rb];
       const int64_t m0 = int64_t(u % p.n_rb) * TC_M;
       const int row0 = int(int64_t(sl.x) * p.N + m0);
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(TC2_THREADS, 1) qgemm_tc2_kernel(const Tc2Para
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
   }
-  if (tid == 0 && *abort_flag && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+  if (tid == 0 && *abort_flag) report_timeout(p.err);
 }
 
 // out[i, :] = x[row(sorted[i]), :] for every planned assignment i, each group
@@ -503,6 +504,8 @@ static int launch_tc2_bits(const Tc2Params& p, const Tc2Maps& maps, int tile, cu
   if (tile <= 128) return launch_tc2_tile<BITS, MAT, 128>(p, maps, st);
   return launch_tc2_tile<BITS, MAT, 256>(p, maps, st);
 }
+
+B2F_DEFINE_WAIT_CONTROLS(tc2)
 
 }  // namespace b2f
 

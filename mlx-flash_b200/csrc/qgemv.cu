@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(288, 1) qgemv_kernel(const GemvParams p, const
 
   // =========================== producer warp ================================
   if (warp == NW) {
-    if (lane == 0) {
+    if (lane == 0 && !producers_stalled()) {  // test control: stalled producers issue nothing
       for (int it = 0; it < n_iter; ++it) {
         const int s = it % L.stages;
         if (it >= L.stages) {
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(288, 1) qgemv_kernel(const GemvParams p, const
       }
     }
   }
-  if (timed_out && lane == 0 && p.err) atomicExch(p.err, B2F_ERR_TIMEOUT);
+  if (timed_out && lane == 0) report_timeout(p.err);
 }
 
 int64_t plan_slots_offset(int64_t A, int64_t E, int tile) { return plan_layout(A, E, tile).off_slots; }
@@ -539,6 +539,8 @@ static int check_gemv_shape(int64_t N, int64_t K, int bits, int gs) {
   if (K / gs > 64) return B2F_ERR_UNSUPPORTED;
   return B2F_OK;
 }
+
+B2F_DEFINE_WAIT_CONTROLS(gemv)
 
 }  // namespace b2f
 

@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
     constexpr int RB_ = D * BITS / 8;
     const int code_bytes = p.PS * RB_, sc_bytes = p.PS * DG * 4;
     if (warp == 4) {
-      if (lane == 0) {
+      if (lane == 0 && !producers_stalled()) {  // test control: stalled producers issue nothing
         int jj = 0;
         for (; jj < npg; ++jj) {
           const int slot = jj % ATTN_RING;
@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const
     }
   }
   __syncthreads();
+  if (aborted && (threadIdx.x & 31) == 0) report_timeout(nullptr);  // a page wait gave up
   const int hq0 = hkv * G;
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int head = idx / D, d = idx % D;
@@ -663,7 +664,7 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
   const int npg = sub_end > sub_begin ? (sub_end + spp - 1) / spp - pg0 : 0;
   const int code_bytes = p.PS * RB, sc_bytes = p.PS * DG * 4;
   if (warp == 4) {
-    if (lane == 0) {
+    if (lane == 0 && !producers_stalled()) {  // test control: stalled producers issue nothing
       int jj = 0;
       for (; jj < npg; ++jj) {
         const int slot = jj % ATTN_RING;
@@ -861,6 +862,7 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
     }
   }
   __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) report_timeout(nullptr);  // a page wait gave up
   const int hq0 = hkv * G;
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int head = idx / D, d = idx % D;
@@ -969,6 +971,8 @@ static int launch_attn(AttnParams p, cudaStream_t st) {
   attn_combine_kernel<<<unsigned(int64_t(p.B) * p.Hq), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, D, p.out);
   return check_launch();
 }
+
+B2F_DEFINE_WAIT_CONTROLS(attn)
 
 }  // namespace b2f
 

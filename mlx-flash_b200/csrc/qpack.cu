@@ -28,6 +28,18 @@ void set_last_cuda_error(cudaError_t e) { g_last_error = cudaGetErrorString(e); 
 // ------------------------------------------------------------------------
 enum QuantRule { kRuleMlx = 0, kRuleMinMax = 1 };
 
+// rint(d / s) with d / s the IEEE round-to-nearest quotient, for |d / s| < 2^12.
+// d * rcp(s) (rcp correctly rounded) is within 2 ulp of that quotient, so the
+// two round to the same integer unless the product lies within 2^-10 of a
+// half-integer; only then is the exact division taken.
+__device__ __forceinline__ float rint_div(float d, float s, float rs) {
+  if (!isfinite(rs)) return rintf(__fdiv_rn(d, s));  // subnormal s: divide exactly
+  const float qa = __fmul_rn(d, rs);
+  const float fr = fabsf(qa - truncf(qa));
+  if (fabsf(fr - 0.5f) < 0.0009765625f) return rintf(__fdiv_rn(d, s));
+  return rintf(qa);
+}
+
 template <class Tag, int BITS, int GS, int RULE>
 __global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag::T* __restrict__ w,
                                                               int64_t n_threads,
@@ -88,11 +100,12 @@ __global__ void __launch_bounds__(256) quantize_affine_kernel(const typename Tag
     uint32_t words[WPT];
 #pragma unroll
     for (int j = 0; j < WPT; ++j) words[j] = 0u;
+    const float rs = zero_q ? 0.f : __frcp_rn(scale);
 #pragma unroll
     for (int i = 0; i < EPT; ++i) {
       uint32_t q = 0u;
       if (!zero_q) {
-        float r = rintf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
+        float r = rint_div(__fsub_rn(v[i], bias), scale, rs);
         r = fminf(fmaxf(r, 0.f), NBINS);
         q = uint32_t(r);
       }
@@ -174,45 +187,67 @@ static int quantize_entry(const void* w, int dtype, int64_t rows, int64_t K, int
 }
 
 // ------------------------------------------------------------------------
-// (a') affine dequantize: one thread per packed word; optional row gather.
+// (a') affine dequantize: one thread per 16-byte vector of packed words (4
+// words), rows on the grid's y axis; optional row gather.
 // w = round_T(q*scale + bias) with an f32 multiply then an f32 add.
 // ------------------------------------------------------------------------
 template <class Tag, int BITS>
 __global__ void __launch_bounds__(256) dequantize_affine_kernel(
     const uint32_t* __restrict__ wq, const typename Tag::T* __restrict__ scales,
-    const typename Tag::T* __restrict__ biases, int64_t out_rows, int64_t K, int gs,
+    const typename Tag::T* __restrict__ biases, int64_t out_rows, int64_t K, int gs_log2,
     const int32_t* __restrict__ row_index, typename Tag::T* __restrict__ out) {
   using T = typename Tag::T;
   constexpr int PER = 32 / BITS;
   constexpr uint32_t MASK = (1u << BITS) - 1u;
-  const int64_t wpr = K / PER;
-  const int64_t n = out_rows * wpr;
-  const int64_t groups = K / gs;
-  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < n;
-       t += int64_t(gridDim.x) * blockDim.x) {
-    const int64_t r = t / wpr, j = t - r * wpr;
+  const int wpr = int(K / PER);
+  const int nv = (wpr + 3) / 4;
+  const int groups = int(K >> gs_log2);
+  // 16-byte word vectors when every row starts 16-byte aligned, else words one by one
+  const bool vec = (reinterpret_cast<uintptr_t>(wq) & 15) == 0 && (wpr & 3) == 0;
+  for (int64_t r = blockIdx.y; r < out_rows; r += gridDim.y) {
     const int64_t src = row_index ? int64_t(row_index[r]) : r;
-    const uint32_t word = wq[src * wpr + j];
-    const int64_t g = (j * PER) / gs;
-    const float s = Tag::to_f(scales[src * groups + g]);
-    const float b = Tag::to_f(biases[src * groups + g]);
-    T vals[PER];
+    const uint32_t* wrow = wq + src * wpr;
+    const T* srow = scales + src * groups;
+    const T* brow = biases + src * groups;
+    T* orow = out + r * K;
+    for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += gridDim.x * blockDim.x) {
+      uint32_t ws[4];
+      if (vec) {
+        const uint4 w4 = reinterpret_cast<const uint4*>(wrow)[v];
+        ws[0] = w4.x;
+        ws[1] = w4.y;
+        ws[2] = w4.z;
+        ws[3] = w4.w;
+      } else {
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const float q = float((word >> (BITS * i)) & MASK);
-      vals[i] = Tag::from_f(__fadd_rn(__fmul_rn(q, s), b));
-    }
-    T* dst = out + r * K + j * PER;
-    constexpr int BYTES = PER * int(sizeof(T));
-    if constexpr (BYTES % 16 == 0) {
+        for (int u = 0; u < 4; ++u) ws[u] = 4 * v + u < wpr ? wrow[4 * v + u] : 0u;
+      }
 #pragma unroll
-      for (int i = 0; i < BYTES / 16; ++i)
-        reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(vals)[i];
-    } else if constexpr (BYTES == 8) {
-      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(vals);
-    } else {
+      for (int u = 0; u < 4; ++u) {
+        if (4 * v + u >= wpr) break;
+        const int k0 = (4 * v + u) * PER;
+        const int g = k0 >> gs_log2;
+        const float s = Tag::to_f(srow[g]);
+        const float b = Tag::to_f(brow[g]);
+        T vals[PER];
 #pragma unroll
-      for (int i = 0; i < PER; ++i) dst[i] = vals[i];
+        for (int i = 0; i < PER; ++i) {
+          const float q = float((ws[u] >> (BITS * i)) & MASK);
+          vals[i] = Tag::from_f(__fadd_rn(__fmul_rn(q, s), b));
+        }
+        T* dst = orow + k0;
+        constexpr int BYTES = PER * int(sizeof(T));
+        if constexpr (BYTES % 16 == 0) {
+#pragma unroll
+          for (int i = 0; i < BYTES / 16; ++i)
+            reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(vals)[i];
+        } else if constexpr (BYTES == 8) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(vals);
+        } else {
+#pragma unroll
+          for (int i = 0; i < PER; ++i) dst[i] = vals[i];
+        }
+      }
     }
   }
 }
@@ -222,18 +257,22 @@ static int launch_dequantize(const uint32_t* wq, const void* s, const void* b, i
                              int64_t K, int bits, int gs, const int32_t* ridx, void* out,
                              cudaStream_t st) {
   using T = typename Tag::T;
-  const int64_t n = rows * K * bits / 32;
-  if (n == 0) return B2F_OK;
-  const int block = 256;
-  int64_t grid = (n + block - 1) / block;
-  if (grid > 148 * 64) grid = 148 * 64;
+  if (rows * K == 0) return B2F_OK;
+  const int64_t wpr = K * bits / 32;
+  const int64_t nv = (wpr + 3) / 4;
+  const int block = nv >= 256 ? 256 : int((nv + 31) / 32 * 32);
+  int64_t gx = (nv + block - 1) / block;
+  if (gx > 65535) gx = 65535;
+  const int64_t gy = rows < 65535 ? rows : 65535;
+  const dim3 grid{unsigned(gx), unsigned(gy), 1u};
+  const int gl = gs == 32 ? 5 : (gs == 64 ? 6 : 7);
   auto S = static_cast<const T*>(s);
   auto Bi = static_cast<const T*>(b);
   auto O = static_cast<T*>(out);
   switch (bits) {
-    case 2: dequantize_affine_kernel<Tag, 2><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
-    case 4: dequantize_affine_kernel<Tag, 4><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
-    case 8: dequantize_affine_kernel<Tag, 8><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gs, ridx, O); break;
+    case 2: dequantize_affine_kernel<Tag, 2><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
+    case 4: dequantize_affine_kernel<Tag, 4><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
+    case 8: dequantize_affine_kernel<Tag, 8><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
     default: return B2F_ERR_UNSUPPORTED;
   }
   return check_launch();
@@ -260,6 +299,91 @@ static KvGeom kv_geom(int64_t D, int bits, int group_size) {
   g.bits = bits;
   g.max_int = (1 << (bits - 1)) - 1;
   return g;
+}
+
+// Fast path of the same quantizer for bf16 rows in whole 64-wide groups (the
+// cache's K/V rows, D % 64 == 0): 8 lanes per group, each lane one 16-byte
+// load of 8 values, the absmax over the group by shuffles, the codes packed
+// in registers and stored as 8 / 4 / 2 bytes.  The per-element arithmetic is
+// kv_quantize_kernel's, so the bytes and scales are identical.
+template <int BITS>
+__global__ void __launch_bounds__(256) kv_quantize_g64_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
+                                                              int64_t D, const int64_t* __restrict__ dst_row,
+                                                              uint8_t* __restrict__ packed, int64_t packed_ld,
+                                                              float* __restrict__ scales, float* __restrict__ zeros,
+                                                              int64_t scales_ld) {
+  constexpr float MI = float((1 << (BITS - 1)) - 1);
+  const int64_t ng = D / 64;
+  const int64_t total = rows * ng * 8;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  const int64_t iters = (total + stride - 1) / stride;
+  int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int64_t it = 0; it < iters; ++it, t += stride) {
+    const bool valid = t < total;
+    const int64_t row = valid ? t / (ng * 8) : 0;
+    const int64_t rem = t - row * ng * 8;
+    const int64_t grp = rem >> 3;
+    const int part = int(rem & 7);
+    float v[8];
+    if (valid) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(x + row * D + grp * 64 + part * 8);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[2 * i] = __low2float(h2[i]);
+        v[2 * i + 1] = __high2float(h2[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(v[i]));
+    m = warp_max<8>(m);
+    float scale = TagBF16::round(__fdiv_rn(m, MI));
+    if (scale == 0.f) scale = 1.f;
+    const float rs = __frcp_rn(scale);
+    uint32_t c[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // bf16(v / scale): the product with the reciprocal is within 2 ulp of the
+      // IEEE quotient, so both round to the same bf16 unless the product's low
+      // 16 bits sit within 8 of the bf16 rounding midpoint (then divide exactly)
+      float qa = __fmul_rn(v[i], rs);
+      const uint32_t lo = __float_as_uint(qa) & 0xFFFFu;
+      if (lo - 0x7FF8u <= 0x10u || !isfinite(rs)) qa = __fdiv_rn(v[i], scale);
+      const float xs = TagBF16::round(qa);
+      float xq = TagBF16::round(rintf(xs));
+      xq = fminf(fmaxf(xq, -MI), MI);
+      c[i] = uint32_t(int(TagBF16::round(xq + MI)));
+    }
+    if (!valid) continue;
+    const int64_t orow = dst_row ? dst_row[row] : row;
+    uint8_t* pr = packed + orow * packed_ld;
+    if constexpr (BITS == 8) {
+      const uint2 o = make_uint2(c[0] | (c[1] << 8) | (c[2] << 16) | (c[3] << 24),
+                                 c[4] | (c[5] << 8) | (c[6] << 16) | (c[7] << 24));
+      *reinterpret_cast<uint2*>(pr + grp * 64 + part * 8) = o;
+    } else if constexpr (BITS == 4) {
+      uint32_t o = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o |= (((c[2 * i] << 4) | (c[2 * i + 1] & 0xFu)) & 0xFFu) << (8 * i);
+      *reinterpret_cast<uint32_t*>(pr + grp * 32 + part * 4) = o;
+    } else {
+      uint32_t o = 0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        o |= (((c[4 * i] << 6) | ((c[4 * i + 1] & 3u) << 4) | ((c[4 * i + 2] & 3u) << 2) | (c[4 * i + 3] & 3u)) &
+              0xFFu)
+             << (8 * i);
+      *reinterpret_cast<uint16_t*>(pr + grp * 16 + part * 2) = uint16_t(o);
+    }
+    if (part == 0) {
+      scales[orow * scales_ld + grp] = scale;
+      if (zeros) zeros[orow * scales_ld + grp] = 0.f;
+    }
+  }
 }
 
 template <class Tag>
@@ -373,6 +497,48 @@ const char* b2f_status_string(int s) {
 
 const char* b2f_last_error_string(void) { return g_last_error.c_str(); }
 
+}  // extern "C"
+
+namespace b2f {
+int b2f_wait_controls_mma(int op, long long* v);
+int b2f_wait_controls_tc(int op, long long* v);
+int b2f_wait_controls_tc2(int op, long long* v);
+int b2f_wait_controls_gemv(int op, long long* v);
+int b2f_wait_controls_attn(int op, long long* v);
+static int (*const k_wait_units[])(int, long long*) = {b2f_wait_controls_mma, b2f_wait_controls_tc,
+                                                        b2f_wait_controls_tc2, b2f_wait_controls_gemv,
+                                                        b2f_wait_controls_attn};
+}  // namespace b2f
+
+extern "C" {
+
+int b2f_device_status(int32_t* status_out, int clear) {
+  if (!status_out) return B2F_ERR_INVALID;
+  int32_t st = B2F_OK;
+  for (auto f : k_wait_units) {
+    long long v = 0;
+    if (f(clear ? 1 : 0, &v) != 0) return B2F_ERR_CUDA;
+    if (v != 0 && st == B2F_OK) st = int32_t(v);
+  }
+  *status_out = st;
+  return B2F_OK;
+}
+
+int b2f_set_wait_limit_ns(int64_t ns) {
+  if (ns < 0) return B2F_ERR_INVALID;
+  long long v = ns == 0 ? 2000000000ll : (long long)ns;
+  for (auto f : k_wait_units)
+    if (f(2, &v) != 0) return B2F_ERR_CUDA;
+  return B2F_OK;
+}
+
+int b2f_set_producer_stall(int on) {
+  long long v = on ? 1 : 0;
+  for (auto f : k_wait_units)
+    if (f(3, &v) != 0) return B2F_ERR_CUDA;
+  return B2F_OK;
+}
+
 int b2f_quantize_affine(const void* w, int dtype, int64_t rows, int64_t K, int bits,
                         int group_size, uint32_t* wq, void* scales, void* biases, void* stream) {
   return quantize_entry<kRuleMlx>(w, dtype, rows, K, bits, group_size, wq, scales, biases, stream);
@@ -422,6 +588,22 @@ int b2f_kv_quantize_sym(const void* x, int dtype, int64_t rows, int64_t D, int b
   if (!x || !packed || !scales) return B2F_ERR_INVALID;
   KvGeom g = kv_geom(D, bits, group_size);
   if (packed_ld < g.pl || scales_ld < g.ng) return B2F_ERR_INVALID;
+  const int64_t store_align = bits == 8 ? 8 : (bits == 4 ? 4 : 2);
+  if (dtype == B2F_BF16 && g.gs == 64 && D % 64 == 0 && aligned(x, 16) && aligned(packed, 16) &&
+      packed_ld % store_align == 0) {
+    const int64_t threads = rows * (D / 64) * 8;
+    int64_t grid = (threads + 255) / 256;
+    if (grid > 148 * 16) grid = 148 * 16;
+    cudaStream_t st = as_stream(stream);
+    auto xx = static_cast<const __nv_bfloat16*>(x);
+    if (bits == 8)
+      kv_quantize_g64_kernel<8><<<grid, 256, 0, st>>>(xx, rows, D, dst_row, packed, packed_ld, scales, zeros, scales_ld);
+    else if (bits == 4)
+      kv_quantize_g64_kernel<4><<<grid, 256, 0, st>>>(xx, rows, D, dst_row, packed, packed_ld, scales, zeros, scales_ld);
+    else
+      kv_quantize_g64_kernel<2><<<grid, 256, 0, st>>>(xx, rows, D, dst_row, packed, packed_ld, scales, zeros, scales_ld);
+    return check_launch();
+  }
   const int64_t buf = (g.dp + 15) & ~int64_t(15);
   if (buf > 200 * 1024) return B2F_ERR_UNSUPPORTED;
   int wpb = int(buf <= 48 * 1024 / 8 ? 8 : (48 * 1024 / buf > 0 ? 48 * 1024 / buf : 1));

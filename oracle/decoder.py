@@ -45,11 +45,17 @@ def rope(v, pos, theta, D):
     return out
 
 
-def decode_step(model, cache, tokens, positions):
+def decode_step(model, cache, tokens, positions, route_override=None, route_log=None):
     """``model``: dict of numpy weights (see b200flash.decoder for names);
     ``cache``: per layer list of (K codes+scales, V codes+scales) per sequence
     as dicts {"k": [S,Hkv,D] float32 dequantized, "v": ...} that this call
     extends with the new token.  Returns (logits [B, V] float32, next tokens).
+
+    ``route_override``: per layer the expert ids [B, k] to use instead of the
+    oracle's own top-k (their scores are still the oracle's gates, renormalised
+    over the given ids) -- to compare the rest of the step on the routing a
+    kernel chose where two gates are within rounding of each other.
+    ``route_log``: a list that receives per layer (own ids, gates [B, E]).
     """
     cfg = model["cfg"]
     H, D, Hq, Hkv = cfg["hidden"], cfg["head_dim"], cfg["n_heads"], cfg["n_kv_heads"]
@@ -83,16 +89,28 @@ def decode_step(model, cache, tokens, positions):
         xn = rmsnorm(h, ly["post_norm"], eps).astype(np.float64)
         logits_r = xn @ np.asarray(ly["wr"], np.float64).T + ly["rbias"]
         inds, scores = _route_from_logits(logits_r, cfg["top_k"], cfg["norm_topk"])
+        if route_log is not None:
+            z = logits_r - logits_r.max(axis=-1, keepdims=True)
+            gates = np.exp(z) / np.exp(z).sum(axis=-1, keepdims=True)
+            route_log.append((inds.copy(), gates))
+        if route_override is not None:
+            z = logits_r - logits_r.max(axis=-1, keepdims=True)
+            gates = np.exp(z) / np.exp(z).sum(axis=-1, keepdims=True)
+            inds = np.asarray(route_override[li], np.int64)
+            scores = np.take_along_axis(gates, inds, axis=-1)
+            if cfg["norm_topk"]:
+                scores = scores / scores.sum(axis=-1, keepdims=True)
         E = len(ly["gate"][0])
         y = np.zeros((B, H))
-        for bi in range(B):
-            for j in range(cfg["top_k"]):
-                e = int(inds[bi, j])
-                g = qmm(xn[bi], tuple(t[e] for t in ly["gate"]), gs, bits)
-                u = qmm(xn[bi], tuple(t[e] for t in ly["up"]), gs, bits)
-                hh = round_bf16((moe.silu(g) * u).astype(np.float32)).astype(np.float64)
-                yk = round_bf16(qmm(hh, tuple(t[e] for t in ly["down"]), gs, bits).astype(np.float32))
-                y[bi] += scores[bi, j] * yk
+        # each routed expert dequantized once, applied to all of its tokens
+        for e in np.unique(inds):
+            bi, j = np.nonzero(inds == e)
+            g = qmm(xn[bi], tuple(t[e] for t in ly["gate"]), gs, bits)
+            u = qmm(xn[bi], tuple(t[e] for t in ly["up"]), gs, bits)
+            hh = round_bf16((moe.silu(g) * u).astype(np.float32)).astype(np.float64)
+            yk = round_bf16(qmm(hh, tuple(t[e] for t in ly["down"]), gs, bits).astype(np.float32))
+            for r in range(len(bi)):
+                y[bi[r]] += scores[bi[r], j[r]] * yk[r]
         assert E > 0
         h = round_bf16((h + y).astype(np.float32)).astype(np.float64)
         nxt = layers[li + 1]["in_norm"] if li + 1 < len(layers) else model["final_norm"]

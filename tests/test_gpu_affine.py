@@ -141,3 +141,22 @@ def test_qmm_gemv_refuses_too_many_groups(dev):
     s = torch.zeros(16, 65, dtype=torch.bfloat16, device=dev)
     with pytest.raises(ValueError, match="64 groups"):
         mx_compat.quantized_matmul(x, wq, s, s, True, 64, 4, engine="gemv")
+
+
+@pytest.mark.parametrize("rule", ["mlx", "minmax"])
+def test_quantize_exact_ties(dev, rule):
+    """Groups whose codes land exactly on half-integers ((w - bias) / scale =
+    k + 0.5): rounding half to even must match the oracle bit for bit."""
+    g = np.zeros((4, 64), np.float32)
+    g[0, :32] = np.arange(32) * 0.5  # min 0, max 15.5: ties at every odd half
+    g[1, :31] = np.arange(31) * 0.5 - 7.5
+    g[2, :16] = np.arange(16) + 0.5
+    g[2, 16] = 0.0
+    g[2, 17] = 15.0
+    g[3, :64] = (np.arange(64) % 31) * 0.25 - 3.75
+    w = round_to(np.tile(g, (32, 2)), "bf16")
+    for bits in (2, 4, 8):
+        wq, s, b = mx_compat.quantize(to_dev(w, "bf16", dev), 64, bits, rule=rule)
+        owq, os_, ob = affine.quantize(w, 64, bits, rule=rule)
+        assert np.array_equal(to_np(wq), owq), bits
+        assert np.array_equal(to_np(s), os_) and np.array_equal(to_np(b), ob), bits
