@@ -711,9 +711,9 @@ def run_moe_layer(args):
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         scratch = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        engines = ["mma"] + (["tc_sorted"] if T >= 32 else [])
+        engines = ["mma"] + (["tc_sorted"] if T >= 32 else []) + (["gemv"] if T <= 32 else [])
         for eng in engines:
-            tile = 16 if eng == "mma" else (64 if A >= 64 * E else 32)
+            tile = 16 if eng in ("mma", "gemv") else (64 if A >= 64 * E else 32)
             pb = int(lib.b2f_moe_plan_workspace_bytes(A, E, tile))
             pws = torch.empty(pb, dtype=torch.uint8, device=dev)
 
@@ -722,7 +722,13 @@ def run_moe_layer(args):
                 g, u, d = ly["g"], ly["u"], ly["d"]
                 call("b2f_moe_route_plan", ptr(x), T, H, ptr(ly["wr"]), ptr(ly["rb"]), E, k, 1, ptr(gates),
                      ptr(inds[i]), ptr(scores), tile, ptr(pws), pb, ptr(status), _capi.stream_of(dev))
-                if eng == "mma":
+                if eng == "gemv":
+                    call("b2f_gather_qgemv_affine", ptr(x), H, 0, k, A, E, ptr(g.wq), ptr(g.scales), ptr(g.biases),
+                         ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I,
+                         _capi.stream_of(dev))
+                    call("b2f_gather_qgemv_affine", ptr(hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
+                         0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, _capi.stream_of(dev))
+                elif eng == "mma":
                     call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
                          ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
                          ptr(hh), I, 1, _capi.stream_of(dev))

@@ -635,6 +635,8 @@ int b2f_gather_qgemm_affine_tcgen05(const void* x, int64_t ldx, const int32_t* x
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   p.slot_count = reinterpret_cast<const int32_t*>(ws);
+  // a bounded wait that gives up records B2F_ERR_TIMEOUT in the plan header's status word
+  p.err = const_cast<int32_t*>(reinterpret_cast<const int32_t*>(ws)) + 1;
   p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
   p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
   p.tile = tile;

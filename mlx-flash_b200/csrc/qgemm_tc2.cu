@@ -562,6 +562,8 @@ int b2f_sorted_qgemm_affine_tcgen05(const void* x_sorted, int64_t ldx, int64_t A
   const char* ws = static_cast<const char*>(plan_workspace);
   Tc2Params p{};
   p.slot_count = reinterpret_cast<const int32_t*>(ws + L.off_hdr);
+  // a bounded wait that gives up records B2F_ERR_TIMEOUT in the plan header's status word
+  p.err = const_cast<int32_t*>(reinterpret_cast<const int32_t*>(ws + L.off_hdr)) + 1;
   p.slots = reinterpret_cast<const int4*>(ws + L.off_slots);
   p.sorted = reinterpret_cast<const int32_t*>(ws + L.off_sorted);
   p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);

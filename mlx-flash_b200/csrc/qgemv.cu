@@ -640,6 +640,8 @@ int b2f_gather_qgemv_affine(const void* x, int64_t ldx, const int32_t* x_row_ind
   p.out = static_cast<__nv_bfloat16*>(out);
   p.ldo = ldo;
   p.slot_count = reinterpret_cast<const int32_t*>(ws + L.off_hdr);
+  // a bounded wait that gives up records B2F_ERR_TIMEOUT in the plan header's status word
+  p.err = const_cast<int32_t*>(reinterpret_cast<const int32_t*>(ws + L.off_hdr)) + 1;
   p.slots = reinterpret_cast<const int4*>(ws + L.off_slots);
   p.sorted = reinterpret_cast<const int32_t*>(ws + L.off_sorted);
   p.tile = tile;
