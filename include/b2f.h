@@ -320,28 +320,31 @@ int b2f_gather_qgemm_affine_mma(const void* x, int64_t ldx, const int32_t* x_row
                                 int64_t ldo, int out_plan_order, void* stream);
 
 /* Packed expert weights for b2f_gather_qgemm_affine_mma_packed: the 4-bit
- * codes of E stacked [N, K] matrices (MLX layout, uint32 [E*N, K/8]) re-laid
- * as one tile per (expert, block of 128 rows for a gate/up matrix (mat 2) or
- * 256 rows for a down matrix (mat 1), 128-wide K chunk), each tile the exact
- * shared-memory image the GEMM consumes (64-byte rows, 16-byte word groups
- * XOR-swizzled by (row / 2) % 4), rows past N zero-filled.  No MLX call
- * corresponds: an internal layout of HBM-resident experts so each staged tile
- * is one contiguous bulk copy.  out must hold b2f_mma_packed_bytes. */
+ * codes of E stacked [N, K] matrices (MLX layout, uint32 [E*N, K/8]) and
+ * their bf16 scales / biases [E*N, K/64], re-laid as one tile per (expert,
+ * block of 128 rows for a gate/up matrix (mat 2) or 256 rows for a down
+ * matrix (mat 1), 128-wide K chunk).  A tile is the exact shared-memory
+ * image the GEMM consumes: the codes (64-byte rows, 16-byte word groups
+ * XOR-swizzled by (row / 2) % 4), then per row 8 bytes of scale and bias for
+ * the chunk's two groups; rows past N zero-filled.  No MLX call corresponds:
+ * an internal layout of HBM-resident experts, so each staged tile is one
+ * contiguous bulk copy and no scale is fetched from global memory in the
+ * inner loop.  out must hold b2f_mma_packed_bytes (72 bytes per row and
+ * 128-wide chunk). */
 int64_t b2f_mma_packed_bytes(int64_t E, int64_t N, int64_t K, int mat);
-int b2f_mma_repack(const uint32_t* wq, int64_t E, int64_t N, int64_t K, int mat, void* out,
-                   int64_t out_bytes, void* stream);
+int b2f_mma_repack(const uint32_t* wq, const void* scales, const void* biases, int64_t E, int64_t N,
+                   int64_t K, int mat, void* out, int64_t out_bytes, void* stream);
 
 /* b2f_gather_qgemm_affine_mma (plan tile 16) reading b2f_mma_repack tiles
- * (mat 2 for pw_gate / pw_up with SwiGLU fused, mat 1 for a single matrix)
- * instead of the MLX-layout codes; scales and biases stay in MLX layout.
- * Same results, bit for bit, as the unpacked call. */
+ * (mat 2 for pw_gate / pw_up with SwiGLU fused, mat 1 for pw_gate alone)
+ * instead of the MLX-layout codes, scales and biases.  Same results, bit
+ * for bit, as the unpacked call. */
 int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
                                        int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
-                                       const void* pw_gate, const void* s_gate, const void* b_gate,
-                                       const void* pw_up, const void* s_up, const void* b_up,
-                                       int64_t N, int64_t K, int bits, int group_size, int tile,
-                                       void* plan_workspace, int64_t plan_workspace_bytes, void* out,
-                                       int64_t ldo, int out_plan_order, void* stream);
+                                       const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
+                                       int bits, int group_size, int tile, void* plan_workspace,
+                                       int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                       int out_plan_order, void* stream);
 
 /* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
  * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes

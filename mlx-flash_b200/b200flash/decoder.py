@@ -298,7 +298,8 @@ class Qwen3MoeDecoder:
                     w = ly[name]
                     nbytes = int(lib.b2f_mma_packed_bytes(E_loc, w.N, w.K, mat))
                     pk = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-                    call("b2f_mma_repack", ptr(w.wq), E_loc, w.N, w.K, mat, ptr(pk), nbytes, st)
+                    call("b2f_mma_repack", ptr(w.wq), ptr(w.scales), ptr(w.biases), E_loc, w.N, w.K, mat, ptr(pk),
+                         nbytes, st)
                     ly[name + "_packed"] = pk
         self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
         self.next_tokens = torch.empty(B, dtype=torch.int32, device=dev)
@@ -449,11 +450,10 @@ class Qwen3MoeDecoder:
             if self.moe_packed:
                 # gate/up rows land in plan order (the down GEMM's input layout)
                 call("b2f_gather_qgemm_affine_mma_packed", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(ly["gate_packed"]),
-                     ptr(g.scales), ptr(g.biases), ptr(ly["up_packed"]), ptr(u.scales), ptr(u.biases), I, H, g.bits,
-                     g.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), I, 1, st)
-                call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), I, 0, 1, 1, A, E, ptr(ly["down_packed"]),
-                     ptr(d.scales), ptr(d.biases), 0, 0, 0, H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws),
-                     self.plan_bytes, ptr(self.y), H, 0, st)
+                     ptr(ly["up_packed"]), I, H, g.bits, g.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes,
+                     ptr(self.hh), I, 1, st)
+                call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), I, 0, 1, 1, A, E, ptr(ly["down_packed"]), 0,
+                     H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), H, 0, st)
             elif self.moe_engine == "mma":
                 # gate/up rows land in plan order (the down GEMM's input layout)
                 call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(g.wq), ptr(g.scales),

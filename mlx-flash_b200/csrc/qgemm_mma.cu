@@ -67,6 +67,7 @@ struct MmaShape<64> {
   static constexpr int NTMAX = 8, WROWS = 16, CTAS = 2;
 };
 
+
 struct MmaParams {
   const __nv_bfloat16* x;
   int64_t ldx;
@@ -117,7 +118,7 @@ __device__ __forceinline__ float sc_half(uint32_t v, int hi) {
 // The consumer side of one CTA for slots of up to 8*NTA tokens: the warp's
 // WROWS/MAT rows of each matrix (MAT 2: gate and up, SwiGLU epilogue), as
 // MT row tiles of 16.
-template <int MAT, int NTA, bool XPLAN, int WROWS, int BITS, bool SF16>
+template <int MAT, int NTA, bool XPLAN, int WROWS, int BITS, bool SF16, bool PACKED = false>
 __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
                                             uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
                                             int begin, int cnt, int64_t row_base, int h0, int h1, int warp,
@@ -158,7 +159,11 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   }
   const int rstep = 4 * p.G;
   const int64_t rows_left = p.N - (row_base + wr0 + r);  // rows valid at offsets < rows_left
+  // matrix m's tile in a stage: codes (CTA_ROWS rows of RBY bytes), then for
+  // packed tiles each row's 8 bytes of (s, s, b, b) for the chunk's 2 groups
+  const int TB = CTA_ROWS * (RBY + (PACKED ? 8 : 0));
   auto load_sb = [&](int h) {
+    if constexpr (PACKED) return;  // read from the stage once it has landed
 #pragma unroll
     for (int i = 0; i < MT; ++i)
 #pragma unroll
@@ -184,6 +189,19 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
     }
     const uint8_t* wst = smem + s * STAGE;
     const uint8_t* xst = wst + W_BYTES;
+    if constexpr (PACKED) {
+#pragma unroll
+      for (int m = 0; m < MAT; ++m)
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const uint2 v = *reinterpret_cast<const uint2*>(wst + m * TB + CTA_ROWS * RBY +
+                                                            (wr0 + 16 * i + 8 * hf + r) * 8);
+            sr[m][i][hf] = v.x;
+            br[m][i][hf] = v.y;
+          }
+    }
 #pragma unroll
     for (int grp = 0; grp < 2; ++grp) {
       float t[MAT][MT][NTA][4];  // sum over the group of (128+q) x
@@ -213,7 +231,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
         for (int m = 0; m < MAT; ++m) {
 #pragma unroll
           for (int i = 0; i < MT; ++i) {
-            const uint8_t* rowp = wst + m * CTA_ROWS * RBY + (wr0 + 16 * i + r) * RBY + 16 * (grp ^ sw) + 4 * c;
+            const uint8_t* rowp = wst + m * TB + (wr0 + 16 * i + r) * RBY + 16 * (grp ^ sw) + 4 * c;
             const uint32_t wl = *reinterpret_cast<const uint32_t*>(rowp);
             const uint32_t wh = *reinterpret_cast<const uint32_t*>(rowp + 8 * RBY);
 #pragma unroll
@@ -264,7 +282,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
         for (int m = 0; m < MAT; ++m) {
 #pragma unroll
           for (int i = 0; i < MT; ++i) {
-            const uint8_t* rowp = wst + m * CTA_ROWS * 64 + (wr0 + 16 * i + r) * 64 + 16 * (j ^ sw) + 4 * c;
+            const uint8_t* rowp = wst + m * TB + (wr0 + 16 * i + r) * 64 + 16 * (j ^ sw) + 4 * c;
             const uint32_t wl = *reinterpret_cast<const uint32_t*>(rowp);
             const uint32_t wh = *reinterpret_cast<const uint32_t*>(rowp + 8 * 64);
             const uint32_t a0[4] = {and_or(wl, 0x000F000Fu, 0x43004300u), and_or(wh, 0x000F000Fu, 0x43004300u),
@@ -387,7 +405,8 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;  // weight rows per matrix
   constexpr int RBY = 16 * BITS;                      // code bytes per row per chunk
   constexpr int XS = mma_xstride<BITS>();             // token row pitch in a stage
-  constexpr int W_BYTES = MAT * CTA_ROWS * RBY;
+  constexpr int TB = CTA_ROWS * (RBY + (PACKED ? 8 : 0));  // one matrix's tile (packed: + scales)
+  constexpr int W_BYTES = MAT * TB;
   constexpr int STAGE = (W_BYTES + TILE * XS + 1023) / 1024 * 1024;
 
   extern __shared__ __align__(1024) uint8_t mma_smem_raw[];
@@ -463,10 +482,9 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       if (lane == 0) {
         if constexpr (PACKED) {
           // the tile is stored as its shared-memory image: one contiguous copy per matrix
-          constexpr uint32_t TB = uint32_t(CTA_ROWS * RBY);
           const int64_t off = ((int64_t(expert) * p.nb + rblk) * (p.K >> 7) + h) * int64_t(TB);
-          bulk_g2s(st, p.pw[0] + off, TB, &full[s]);
-          if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, TB, &full[s]);
+          bulk_g2s(st, p.pw[0] + off, uint32_t(TB), &full[s]);
+          if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, uint32_t(TB), &full[s]);
         } else {
           tma_load_2d(st, &tm0, h * (4 * BITS), wrow, &full[s]);
           if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, h * (4 * BITS), wrow, &full[s]);
@@ -492,25 +510,25 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
 
   if constexpr (SH::NTMAX == 2) {
     if (cnt <= 8) {
-      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     } else {
-      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     }
   } else if constexpr (SH::NTMAX == 4) {
     if (cnt <= 8) {
-      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     } else if (cnt <= 16) {
-      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     } else {
-      mma_consume<MAT, 4, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
+      mma_consume<MAT, 4, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
                                             begin, cnt, row_base, h0, h1, warp, lane);
     }
   } else {
-    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
+    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
                                                   expert, begin, cnt, row_base, h0, h1, warp, lane);
   }
   if (lane == 0 && *abort_flag) report_timeout(p.err);
@@ -537,7 +555,7 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
                           int ksplit, cudaStream_t st) {
   using SH = MmaShape<TILE>;
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
-  constexpr int STAGE = (MAT * CTA_ROWS * 16 * BITS + TILE * mma_xstride<BITS>() + 1023) / 1024 * 1024;
+  constexpr int STAGE = (MAT * CTA_ROWS * (16 * BITS + (PACKED ? 8 : 0)) + TILE * mma_xstride<BITS>() + 1023) / 1024 * 1024;
   // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
   // of it reserved per CTA)
   int S = 8;
@@ -573,29 +591,49 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
 }
 
 // Packed expert weights for the warp-MMA GEMM: 4-bit codes [E*N rows, K/8
-// words] (MLX layout) -> per (expert, row block of `cr` rows, 128-wide K chunk)
-// one 64*cr-byte tile holding exactly the shared-memory image a 64B-swizzled
-// TMA box of that tile would give: row r of the tile at byte 64r, its 16-byte
-// word group j at position j ^ ((r >> 1) & 3).  Rows past N are zero.  The
-// producer then fetches each tile with one contiguous bulk copy.
-__global__ void __launch_bounds__(256) mma_repack_kernel(const uint32_t* __restrict__ wq, int64_t E, int64_t N,
+// words] (MLX layout) with their bf16 scales / biases [E*N, K/64] -> per
+// (expert, row block of `cr` rows, 128-wide K chunk) one tile of 72*cr bytes
+// holding exactly the stage image the consumers read: first the codes as a
+// 64B-swizzled TMA box of the tile would give them (row r at byte 64r, its
+// 16-byte word group j at position j ^ ((r >> 1) & 3)), then per row 8 bytes
+// (s[2h], s[2h+1], b[2h], b[2h+1]) for the chunk's two groups.  Rows past N
+// are zero.  The producer fetches a whole tile with one contiguous bulk copy
+// and the consumers take scales and biases from shared memory.
+__global__ void __launch_bounds__(256) mma_repack_kernel(const uint32_t* __restrict__ wq,
+                                                         const uint16_t* __restrict__ sc,
+                                                         const uint16_t* __restrict__ bi, int64_t E, int64_t N,
                                                          int64_t K, int cr, int64_t nb, uint4* __restrict__ out) {
   const int hc = int(K >> 7);
-  const int64_t groups = E * nb * hc * cr * 4;  // 16-byte word groups of the output
+  const int G = int(K >> 6);
+  const int per_tile = cr * 4 + cr / 2;  // 16-byte groups: codes, then scales/biases (2 rows per group)
+  const int64_t groups = E * nb * hc * per_tile;
   for (int64_t o = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; o < groups;
        o += int64_t(gridDim.x) * blockDim.x) {
-    const int pos = int(o & 3);
-    int64_t t = o >> 2;
-    const int rr = int(t % cr);
-    t /= cr;
+    const int q = int(o % per_tile);
+    int64_t t = o / per_tile;
     const int h = int(t % hc);
     t /= hc;
     const int64_t rb = t % nb;
     const int64_t e = t / nb;
-    const int64_t row = rb * cr + rr;
-    const int jj = pos ^ ((rr >> 1) & 3);
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (row < N) v = reinterpret_cast<const uint4*>(wq + (e * N + row) * (K / 8) + int64_t(h) * 16)[jj];
+    if (q < cr * 4) {
+      const int rr = q >> 2, pos = q & 3;
+      const int64_t row = rb * cr + rr;
+      const int jj = pos ^ ((rr >> 1) & 3);
+      if (row < N) v = reinterpret_cast<const uint4*>(wq + (e * N + row) * (K / 8) + int64_t(h) * 16)[jj];
+    } else {
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t row = rb * cr + 2 * (q - cr * 4) + u;
+        if (row < N) {
+          const int64_t g0 = (e * N + row) * G + 2 * h;
+          w[2 * u] = uint32_t(sc[g0]) | (uint32_t(sc[g0 + 1]) << 16);
+          w[2 * u + 1] = uint32_t(bi[g0]) | (uint32_t(bi[g0 + 1]) << 16);
+        }
+      }
+      v = make_uint4(w[0], w[1], w[2], w[3]);
+    }
     out[o] = v;
   }
 }
@@ -693,43 +731,42 @@ extern "C" int64_t b2f_mma_packed_bytes(int64_t E, int64_t N, int64_t K, int mat
   if (E <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || !(mat == 1 || mat == 2)) return 0;
   const int cr = mma_packed_rows(mat);
   const int64_t nb = (N + cr - 1) / cr;
-  return E * nb * (K / 128) * int64_t(cr) * 64;
+  return E * nb * (K / 128) * int64_t(cr) * 72;
 }
 
-extern "C" int b2f_mma_repack(const uint32_t* wq, int64_t E, int64_t N, int64_t K, int mat, void* out,
-                              int64_t out_bytes, void* stream) {
+extern "C" int b2f_mma_repack(const uint32_t* wq, const void* scales, const void* biases, int64_t E, int64_t N,
+                              int64_t K, int mat, void* out, int64_t out_bytes, void* stream) {
   if (E <= 0 || N <= 0 || K <= 0 || K % 128 != 0 || !(mat == 1 || mat == 2)) return B2F_ERR_INVALID;
-  if (!wq || !out) return B2F_ERR_INVALID;
+  if (!wq || !scales || !biases || !out) return B2F_ERR_INVALID;
   if (out_bytes < b2f_mma_packed_bytes(E, N, K, mat)) return B2F_ERR_WORKSPACE;
-  if (!aligned(wq, 16) || !aligned(out, 16)) return B2F_ERR_ALIGN;
+  if (!aligned(wq, 16) || !aligned(out, 16) || !aligned(scales, 4) || !aligned(biases, 4)) return B2F_ERR_ALIGN;
   const int cr = mma_packed_rows(mat);
   const int64_t nb = (N + cr - 1) / cr;
-  const int64_t groups = E * nb * (K / 128) * cr * 4;
+  const int64_t groups = E * nb * (K / 128) * (cr * 4 + cr / 2);
   int64_t grid = (groups + 255) / 256;
   if (grid > 148 * 32) grid = 148 * 32;
-  mma_repack_kernel<<<unsigned(grid), 256, 0, as_stream(stream)>>>(wq, E, N, K, cr, nb, static_cast<uint4*>(out));
+  mma_repack_kernel<<<unsigned(grid), 256, 0, as_stream(stream)>>>(
+      wq, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases), E, N, K, cr, nb,
+      static_cast<uint4*>(out));
   return check_launch();
 }
 
 extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
                                                   int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
-                                                  const void* pw_gate, const void* s_gate, const void* b_gate,
-                                                  const void* pw_up, const void* s_up, const void* b_up, int64_t N,
-                                                  int64_t K, int bits, int group_size, int tile,
-                                                  void* plan_workspace, int64_t plan_workspace_bytes, void* out,
-                                                  int64_t ldo, int out_plan_order, void* stream) {
+                                                  const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
+                                                  int bits, int group_size, int tile, void* plan_workspace,
+                                                  int64_t plan_workspace_bytes, void* out, int64_t ldo,
+                                                  int out_plan_order, void* stream) {
   if (bits != 4 || group_size != 64 || tile != 16) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0) return B2F_ERR_INVALID;
   if (A == 0) return B2F_OK;
-  if (!x || !pw_gate || !s_gate || !b_gate || !out) return B2F_ERR_INVALID;
-  if (pw_up && (!s_up || !b_up)) return B2F_ERR_INVALID;
+  if (!x || !pw_gate || !out) return B2F_ERR_INVALID;
   if (!x_plan_order && !x_row_index && x_row_div <= 0) return B2F_ERR_INVALID;
   if (ldx < K || ldo < N) return B2F_ERR_INVALID;
   if (E * N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
   if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(pw_gate, 16) || (pw_up && !aligned(pw_up, 16)) ||
-      !aligned(out, 4) || ldo % 2 != 0 || !aligned(s_gate, 4) || !aligned(b_gate, 4) ||
-      (pw_up && (!aligned(s_up, 4) || !aligned(b_up, 4))))
+      !aligned(out, 4) || ldo % 2 != 0)
     return B2F_ERR_ALIGN;
   const int64_t need = b2f_moe_plan_workspace_bytes(A, E, tile);
   if (!plan_workspace || plan_workspace_bytes < need) return B2F_ERR_WORKSPACE;
@@ -741,10 +778,6 @@ extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, co
   p.ldx = ldx;
   p.x_row_index = x_row_index;
   p.x_row_div = x_row_div > 0 ? x_row_div : 1;
-  p.s[0] = static_cast<const __nv_bfloat16*>(s_gate);
-  p.b[0] = static_cast<const __nv_bfloat16*>(b_gate);
-  p.s[1] = static_cast<const __nv_bfloat16*>(s_up);
-  p.b[1] = static_cast<const __nv_bfloat16*>(b_up);
   p.pw[0] = static_cast<const uint8_t*>(pw_gate);
   p.pw[1] = static_cast<const uint8_t*>(pw_up);
   const int mat = pw_up ? 2 : 1;

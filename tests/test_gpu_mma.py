@@ -215,9 +215,9 @@ def test_mma_2bit_swiglu_and_down(dev, sdt):
 
 @pytest.mark.parametrize("E,N,K,T,k", [(8, 768, 2048, 64, 8), (5, 384, 640, 9, 2), (3, 256, 384, 40, 3)])
 def test_packed_tiles_equal_unpacked(dev, E, N, K, T, k):
-    """b2f_mma_repack + the bulk-copy producer: gate/up (SwiGLU, plan-order
-    rows) and down outputs bit-identical to the TMA path over MLX-layout codes,
-    including row blocks past N (zero-filled tiles)."""
+    """b2f_mma_repack (codes + in-tile scales/biases) + the bulk-copy producer:
+    gate/up (SwiGLU, plan-order rows) and down outputs bit-identical to the TMA
+    path over MLX-layout codes, including row blocks past N (zero-filled)."""
     from b200flash import _capi
     from b200flash._capi import call, ptr
 
@@ -234,19 +234,19 @@ def test_packed_tiles_equal_unpacked(dev, E, N, K, T, k):
     def pack(w, NN, KK, mat):
         nb = int(lib.b2f_mma_packed_bytes(E, NN, KK, mat))
         out = torch.empty(nb, dtype=torch.uint8, device=dev)
-        call("b2f_mma_repack", ptr(w), E, NN, KK, mat, ptr(out), nb, st)
+        call("b2f_mma_repack", ptr(w[0]), ptr(w[1]), ptr(w[2]), E, NN, KK, mat, ptr(out), nb, st)
         return out
 
-    pg, pu, pd = pack(G[0], N, K, 2), pack(U[0], N, K, 2), pack(D[0], K, N, 1)
+    pg, pu, pd = pack(G, N, K, 2), pack(U, N, K, 2), pack(D, K, N, 1)
     A = plan.A
     h_ref = mx_compat.gather_qmm_mma_planned(x, plan, *G, 64, 4, x_row_div=k, up=U, out_plan_order=True)
     y_ref = mx_compat.gather_qmm_mma_planned(h_ref, plan, *D, 64, 4, x_plan_order=True)
     h = torch.empty(A, N, dtype=torch.bfloat16, device=dev)
     y = torch.empty(A, K, dtype=torch.bfloat16, device=dev)
-    call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(G[1]), ptr(G[2]), ptr(pu),
-         ptr(U[1]), ptr(U[2]), N, K, 4, 64, 16, ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, st)
-    call("b2f_gather_qgemm_affine_mma_packed", ptr(h), N, 0, 1, 1, A, E, ptr(pd), ptr(D[1]), ptr(D[2]), 0, 0, 0,
-         K, N, 4, 64, 16, ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, st)
+    call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
+         ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, st)
+    call("b2f_gather_qgemm_affine_mma_packed", ptr(h), N, 0, 1, 1, A, E, ptr(pd), 0, K, N, 4, 64, 16,
+         ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, st)
     torch.cuda.synchronize()
     # rows the plan wrote (plan order, all A assignments) compare bitwise
     assert torch.equal(h.view(torch.int16), h_ref.view(torch.int16))
