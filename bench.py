@@ -694,6 +694,13 @@ def run_moe_layer(args):
                        "d": random_qweight((E, H, I), bits, gs, dev, gen),
                        "wr": (torch.randn(E, H, device=dev, generator=gen) * (tau / H ** 0.5)).to(torch.bfloat16),
                        "rb": beta[perm].contiguous()})
+        ly = layers[-1]
+        for name, mat in (("g", 2), ("u", 2), ("d", 1)):
+            w = ly[name]
+            nbytes = int(_capi.lib().b2f_mma_packed_bytes(E, w.N, w.K, mat))
+            ly[name + "_packed"] = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            call("b2f_mma_repack", ptr(w.wq), ptr(w.scales), ptr(w.biases), E, w.N, w.K, mat,
+                 ptr(ly[name + "_packed"]), nbytes, _capi.stream_of(dev))
     per_exp = 3 * (I * H * bits // 8 + 2 * I * (H // gs) * 2)
     ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
     results = {}
@@ -711,9 +718,9 @@ def run_moe_layer(args):
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         scratch = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         status = torch.zeros(1, dtype=torch.int32, device=dev)
-        engines = ["mma"] + (["tc_sorted"] if T >= 32 else []) + (["gemv"] if T <= 32 else [])
+        engines = ["mma", "mma_mlx"] + (["tc_sorted"] if T >= 32 else []) + (["gemv"] if T <= 32 else [])
         for eng in engines:
-            tile = 16 if eng in ("mma", "gemv") else (64 if A >= 64 * E else 32)
+            tile = 16 if eng in ("mma", "mma_mlx", "gemv") else (64 if A >= 64 * E else 32)
             pb = int(lib.b2f_moe_plan_workspace_bytes(A, E, tile))
             pws = torch.empty(pb, dtype=torch.uint8, device=dev)
 
@@ -729,6 +736,12 @@ def run_moe_layer(args):
                     call("b2f_gather_qgemv_affine", ptr(hh), I, 0, 1, A, E, ptr(d.wq), ptr(d.scales), ptr(d.biases),
                          0, 0, 0, H, I, bits, gs, tile, ptr(pws), pb, ptr(y), H, _capi.stream_of(dev))
                 elif eng == "mma":
+                    # packed tiles (the decoder's layout): codes + scales in one copy per tile
+                    call("b2f_gather_qgemm_affine_mma_packed", ptr(x), H, 0, k, 0, A, E, ptr(ly["g_packed"]),
+                         ptr(ly["u_packed"]), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1, _capi.stream_of(dev))
+                    call("b2f_gather_qgemm_affine_mma_packed", ptr(hh), I, 0, 1, 1, A, E, ptr(ly["d_packed"]), 0, H,
+                         I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, _capi.stream_of(dev))
+                elif eng == "mma_mlx":
                     call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
                          ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
                          ptr(hh), I, 1, _capi.stream_of(dev))

@@ -141,12 +141,14 @@ def decode_attention(q: torch.Tensor, k_pages: torch.Tensor, k_scales: torch.Ten
 
 
 def pick_splits(B: int, Hkv: int, max_len: int, sms: int = 148) -> int:
-    """Context splits: about two CTAs per SM, at least 1024 tokens per split
-    (longer per-warp streams beat more, shorter CTAs on B200)."""
+    """Context splits: about two CTAs per SM, at least 256 tokens per split.
+    Measured on B200 (8-bit KV, 32q/4kv heads of 128, context 2048): batch 1
+    24.4 us unsplit -> 10.3 us with 8 splits; batch 8 24.9 -> 12.3 us; batch
+    64 fastest unsplit (34.9 us; 2 splits 43.5)."""
     if max_len <= 0:
         return 1
     want = max(1, (2 * sms) // max(1, B * Hkv))
-    cap = max(1, max_len // 1024)
+    cap = max(1, max_len // 256)
     return int(min(want, cap, 64))
 
 

@@ -557,9 +557,20 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   constexpr int CTA_ROWS = MMA_CW * SH::WROWS / MAT;
   constexpr int STAGE = (MAT * CTA_ROWS * (16 * BITS + (PACKED ? 8 : 0)) + TILE * mma_xstride<BITS>() + 1023) / 1024 * 1024;
   // as many ring stages as fit in the CTA's share of the SM's 228 KB (1 KB
-  // of it reserved per CTA)
+  // of it reserved per CTA); a grid that fits one CTA per SM (a decode step
+  // of a few tokens) gives each CTA the whole SM's shared memory, so more
+  // bytes are in flight per CTA
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                    cudaSuccess)
+      sms = 148;
+  }
+  const int64_t row_blocks_all = (p.N + CTA_ROWS - 1) / CTA_ROWS;
+  const int per_sm = slots_grid * row_blocks_all * ksplit <= sms ? 1 : SH::CTAS;
   int S = 8;
-  while (S > 2 && SH::CTAS * (S * STAGE + 1024 + 256 + 1024) > 228 * 1024) --S;
+  while (S > 2 && per_sm * (S * STAGE + 1024 + 256 + 1024) > 228 * 1024) --S;
   p.stages = S;
   const int smem = S * STAGE + 1024 + 256;
   CUtensorMap m0{}, m1{};
