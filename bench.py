@@ -961,7 +961,7 @@ def run_ds_prefill(args):
                              "traffic": None},
                 "phases_us_rank0": {n: round(phases[n], 1) for n in ev},
                 "per_rank": [{"ms": round(v[0] * 1e3, 3), "assignments": int(v[1]), "hot_share": round(v[2], 3),
-                              "experts_us": round(v[6], 1)} for v in per_rank],
+                              "experts_us": round(v[3 + list(ev).index("experts")], 1)} for v in per_rank],
                 "clocks": clk.summary()}
         print(json.dumps(line), flush=True)
     del ep
@@ -1144,7 +1144,8 @@ def main():
                     help="N > 1: also time this global batch spread over the N ranks (0: skip)")
     ap.add_argument("--experts", type=int, default=256, help="ds-prefill: routed experts")
     ap.add_argument("--tokens", type=int, default=4096, help="ds-prefill: tokens over all ranks")
-    ap.add_argument("--ds-tile", type=int, default=128, help="ds-prefill: tokens per expert tile")
+    ap.add_argument("--ds-tile", type=int, default=256,
+                    help="ds-prefill: tokens per expert tile (measured 64 / 128 / 256: 185 / 300 / 336 TFLOP/s)")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "linear", "kv-attention", "moe-layer", "ds-prefill"],
                     help="decode: the 48-layer decode step (the benchmark line); linear / kv-attention / "
