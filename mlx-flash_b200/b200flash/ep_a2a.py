@@ -95,7 +95,7 @@ class ExpertParallelA2A:
             # to 256 tokens (the dequantizing warps bound this GEMM; measured
             # on the DeepSeek-V3-shaped layer: tiles 64 / 128 / 256 give
             # 185 / 300 / 336 TFLOP/s)
-            tile = 16 if engine == "mma" else (256 if A >= 256 * self.e_count else 128)
+            tile = 16 if engine == "mma" else (256 if A >= 64 * self.e_count else 128)
         self.tile = int(tile)
         self.plan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(A, self.e_count, self.tile))
         self.plan_ws = torch.empty(max(self.plan_bytes, 16), dtype=torch.uint8, device=dev)
