@@ -262,15 +262,17 @@ def torch_unique_count(t):
     return torch.unique(t).numel()
 
 
-# DRAM bytes moved per algorithmic byte, from an ncu capture of the kernel the
+# DRAM bytes moved per algorithmic byte, from ncu captures of the kernels the
 # step runs, on the 2-layer copy of this decode step (dram__bytes_read.sum +
 # dram__bytes_write.sum over the launch's algorithmic bytes; see
-# profiles/qkv_decode_attn_b64_ctx2048.txt).  The per-layer shapes are those
-# of the 48-layer step, so traffic scales with the units a launch processes.
-# The warp-MMA expert GEMMs have no capture with both counters (their summary,
-# profiles/qgemm_mma_moe_b64_2layer_ncu.txt, holds DRAM reads only), so their
-# traffic is reported as null.
-NCU_TRAFFIC_RATIO = {"attention": (147.63648 + 4.275712) / 144.142336}
+# profiles/qgemm_mma_packed_moe_b64_2layer_zipf_ncu.txt and
+# profiles/qkv_decode_attn_b64_ctx2048.txt).  The per-layer shapes are those of
+# the 48-layer step, so traffic scales with the units a launch processes.  The
+# expert GEMMs' algorithmic bytes are the 2-layer run's mean per launch (the
+# capture is layer 0's launch).
+NCU_TRAFFIC_RATIO = {"attention": (147.63648 + 4.275712) / 144.142336,
+                     "moe_gate_up": (168.513024 + 4.78976) / 178.946048,
+                     "moe_down": (84.907008 + 2.450176) / 90.914816}
 
 
 def attention_bytes(dec, ctx):
@@ -411,8 +413,9 @@ def run_ours(args):
                 "peak_kind": peak_kind, "unit": "GB/s", "frac": round(d["gbs"] / peak, 4),
                 "traffic": (int(d["bytes_per_launch"] * NCU_TRAFFIC_RATIO[dom]) if dom in NCU_TRAFFIC_RATIO
                             else None),
-                "traffic_source": ("ncu DRAM bytes / algorithmic bytes on the 2-layer capture, times this launch's bytes"
-                                   if dom in NCU_TRAFFIC_RATIO else "no ncu capture with read and write bytes"),
+                "traffic_source": ("ncu DRAM read + write bytes / algorithmic bytes on the 2-layer capture, times this "
+                                   "launch's algorithmic bytes" if dom in NCU_TRAFFIC_RATIO
+                                   else "no ncu capture with read and write bytes"),
                 "bytes_per_launch": int(d["bytes_per_launch"]),
                 "avg_launch_us": round(d["avg_us"], 2),
                 "distinct_experts_per_layer": round(sum(u for u, _ in distinct) / max(1, len(distinct)), 1)}
