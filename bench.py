@@ -307,7 +307,7 @@ def run_ours(args):
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile,
-                          moe_packed=not args.moe_unpacked)
+                          moe_packed=not args.moe_unpacked, pdl=not args.no_pdl)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -741,9 +741,9 @@ def run_moe_layer(args):
                 elif eng == "mma":
                     # packed tiles (the decoder's layout): codes + scales in one copy per tile
                     call("b2f_gather_qgemm_affine_mma_packed", ptr(x), H, 0, k, 0, A, E, ptr(ly["g_packed"]),
-                         ptr(ly["u_packed"]), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1, _capi.stream_of(dev))
+                         ptr(ly["u_packed"]), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1, 0, _capi.stream_of(dev))
                     call("b2f_gather_qgemm_affine_mma_packed", ptr(hh), I, 0, 1, 1, A, E, ptr(ly["d_packed"]), 0, H,
-                         I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, _capi.stream_of(dev))
+                         I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, 0, _capi.stream_of(dev))
                 elif eng == "mma_mlx":
                     call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
                          ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
@@ -984,7 +984,8 @@ def strong_scaling(args, shape, world, dev, exchange, max_ctx):
     b = max(1, args.strong_batch // world)
     dec = Qwen3MoeDecoder(shape, max_batch=b, max_context=max_ctx, page_size=64, device=dev, seed=1234,
                           layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
-                          dense_engine=args.dense_engine, moe_tile=args.moe_tile, moe_packed=not args.moe_unpacked)
+                          dense_engine=args.dense_engine, moe_tile=args.moe_tile, moe_packed=not args.moe_unpacked,
+                          pdl=not args.no_pdl)
     dec.fill_random_context(args.ctx)
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
@@ -1160,6 +1161,8 @@ def main():
                     help="q/k/v and o projection engine (auto: the decoder's choice for this batch)")
     ap.add_argument("--moe-tile", type=int, default=16, choices=[16, 32],
                     help="tokens per expert tile of the warp-MMA expert GEMM")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch the expert down GEMM in plain stream order (no programmatic dependent launch)")
     ap.add_argument("--moe-unpacked", action="store_true",
                     help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
     ap.add_argument("--layers", type=int, default=48,

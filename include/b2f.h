@@ -338,13 +338,18 @@ int b2f_mma_repack(const uint32_t* wq, const void* scales, const void* biases, i
 /* b2f_gather_qgemm_affine_mma (plan tile 16) reading b2f_mma_repack tiles
  * (mat 2 for pw_gate / pw_up with SwiGLU fused, mat 1 for pw_gate alone)
  * instead of the MLX-layout codes, scales and biases.  Same results, bit
- * for bit, as the unpacked call. */
+ * for bit, as the unpacked call.  launch_flags (programmatic dependent
+ * launch; 0 = ordinary stream order): bit 0 -- this call may start while
+ * the previous kernel in the stream finishes: it stages its first weight
+ * tiles, then waits for that kernel before copying x (so x may be that
+ * kernel's output); bit 1 -- let the next kernel start once every CTA of
+ * this one has started (pair it with bit 0 on the next call). */
 int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
                                        int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
                                        const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
                                        int bits, int group_size, int tile, void* plan_workspace,
                                        int64_t plan_workspace_bytes, void* out, int64_t ldo,
-                                       int out_plan_order, void* stream);
+                                       int out_plan_order, int launch_flags, void* stream);
 
 /* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
  * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes

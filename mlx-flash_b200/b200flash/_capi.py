@@ -105,7 +105,7 @@ SIGNATURES = {
     "b2f_mma_packed_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "b2f_mma_repack": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _I64, _P]),
     "b2f_gather_qgemm_affine_mma_packed": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _I,
-                                                _P, _I64, _P, _I64, _I, _P]),
+                                                _P, _I64, _P, _I64, _I, _I, _P]),
     "b2f_ep_a2a_row_pitch": (_I64, [_I64, _I64]),
     "b2f_ep_a2a_dispatch": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P]),
     "b2f_ep_a2a_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P, _P]),

@@ -172,8 +172,9 @@ class Qwen3MoeDecoder:
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
                  device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
-                 dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True):
+                 dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True, pdl: bool = True):
         self.s = s = shape
+        self.pdl = bool(pdl)
         self.dev = dev = torch.device(device)
         self.B = max_batch
         self.page = page_size
@@ -449,11 +450,15 @@ class Qwen3MoeDecoder:
                  self.plan_bytes, ptr(self.plan_status), st)
             if self.moe_packed:
                 # gate/up rows land in plan order (the down GEMM's input layout)
+                # the down GEMM is a programmatic dependent launch: its first weight
+                # tiles stream while the gate/up GEMM's last wave finishes
+                pdl = 1 if self.pdl else 0
                 call("b2f_gather_qgemm_affine_mma_packed", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(ly["gate_packed"]),
                      ptr(ly["up_packed"]), I, H, g.bits, g.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes,
-                     ptr(self.hh), I, 1, st)
+                     ptr(self.hh), I, 1, 2 * pdl, st)
                 call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), I, 0, 1, 1, A, E, ptr(ly["down_packed"]), 0,
-                     H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), H, 0, st)
+                     H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), H, 0, pdl,
+                     st)
             elif self.moe_engine == "mma":
                 # gate/up rows land in plan order (the down GEMM's input layout)
                 call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(g.wq), ptr(g.scales),

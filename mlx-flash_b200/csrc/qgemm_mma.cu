@@ -93,7 +93,15 @@ struct MmaParams {
   // ((expert * nb + row block) * (K/128) + chunk) * tile_bytes of pw[m]
   const uint8_t* pw[2];
   int64_t nb;
+  // programmatic dependent launch: bit 0 = this launch depends on the kernel
+  // before it in the stream (weights of the first ring stages are fetched,
+  // then griddepcontrol.wait, then the activation rows); bit 1 = let the next
+  // kernel launch as soon as every CTA of this one has started
+  int flags;
 };
+
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
   asm volatile(
@@ -419,6 +427,7 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   // x = row block, y = slot: one expert's contiguous rows are streamed by
   // consecutive CTAs; slot-major (wide tiles, one-matrix plans): x = slot,
   // so the slots reading one row block run back to back and share it in L2
+  if ((p.flags & 2) && threadIdx.x == 0) griddep_launch_dependents();
   const int slot_id = p.slot_major ? int(blockIdx.x) : int(blockIdx.y);
   const int rblk = p.slot_major ? int(blockIdx.y) : int(blockIdx.x);
   if (slot_id >= *p.slot_count) return;
@@ -463,8 +472,43 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       }
     }
     const int wrow = int(int64_t(expert) * p.N + row_base);
+    auto issue_weights = [&](int hh, uint8_t* st, uint64_t* bar) {
+      if constexpr (PACKED) {
+        // the tile is stored as its shared-memory image: one contiguous copy per matrix
+        const int64_t off = ((int64_t(expert) * p.nb + rblk) * (p.K >> 7) + hh) * int64_t(TB);
+        bulk_g2s(st, p.pw[0] + off, uint32_t(TB), bar);
+        if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, uint32_t(TB), bar);
+      } else {
+        tma_load_2d(st, &tm0, hh * (4 * BITS), wrow, bar);
+        if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, hh * (4 * BITS), wrow, bar);
+      }
+    };
+    auto issue_x = [&](int hh, uint8_t* st, uint64_t* bar) {
+#pragma unroll
+      for (int u = 0; u < XPL; ++u) {
+        const int tk = lane + 32 * u;
+        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * XS, xrow[u] + int64_t(hh) * 128, 256u, bar);
+      }
+    };
     int h = h0, s = 0;
     uint32_t phase = 0;
+    if (p.flags & 1) {
+      // dependent launch: the first stages' weights need nothing from the kernel
+      // before this one, so they are in flight before the wait; the activation
+      // rows (that kernel's output) are copied after it
+      const int pre = min(S, h1 - h0);
+      if (lane == 0)
+        for (int u = 0; u < pre; ++u) {
+          mbar_arrive_expect_tx(&full[u], uint32_t(W_BYTES + cnt * 256));
+          issue_weights(h0 + u, smem + u * STAGE, &full[u]);
+        }
+      __syncwarp();
+      griddep_wait();
+      for (int u = 0; u < pre; ++u) issue_x(h0 + u, smem + u * STAGE, &full[u]);
+      h = h0 + pre;
+      s = pre % S;
+      phase = pre == S ? 1u : 0u;
+    }
     for (; h < h1; ++h) {
       int ok = 1;
       if (lane == 0) {
@@ -479,22 +523,8 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       uint8_t* st = smem + s * STAGE;
-      if (lane == 0) {
-        if constexpr (PACKED) {
-          // the tile is stored as its shared-memory image: one contiguous copy per matrix
-          const int64_t off = ((int64_t(expert) * p.nb + rblk) * (p.K >> 7) + h) * int64_t(TB);
-          bulk_g2s(st, p.pw[0] + off, uint32_t(TB), &full[s]);
-          if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, uint32_t(TB), &full[s]);
-        } else {
-          tma_load_2d(st, &tm0, h * (4 * BITS), wrow, &full[s]);
-          if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, h * (4 * BITS), wrow, &full[s]);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < XPL; ++u) {
-        const int tk = lane + 32 * u;
-        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * XS, xrow[u] + int64_t(h) * 128, 256u, &full[s]);
-      }
+      if (lane == 0) issue_weights(h, st, &full[s]);
+      issue_x(h, st, &full[s]);
       if (++s == S) {
         s = 0;
         phase ^= 1u;
@@ -597,6 +627,27 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   if ((p.slot_major ? row_blocks : slots_grid) > 65535) return B2F_ERR_UNSUPPORTED;
   const dim3 grid = p.slot_major ? dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)}
                                  : dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)};
+  if (p.flags & 1) {
+    // programmatic dependent launch: may start while the previous kernel in
+    // the stream finishes; the kernel waits (griddepcontrol.wait) before it
+    // reads that kernel's output
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3{160, 1, 1};
+    cfg.dynamicSmemBytes = size_t(smem);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, p, m0, m1);
+    if (le != cudaSuccess) {
+      set_last_cuda_error(le);
+      return B2F_ERR_CUDA;
+    }
+    return check_launch();
+  }
   kern<<<grid, 160, smem, st>>>(p, m0, m1);
   return check_launch();
 }
@@ -767,7 +818,7 @@ extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, co
                                                   const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
                                                   int bits, int group_size, int tile, void* plan_workspace,
                                                   int64_t plan_workspace_bytes, void* out, int64_t ldo,
-                                                  int out_plan_order, void* stream) {
+                                                  int out_plan_order, int launch_flags, void* stream) {
   if (bits != 4 || group_size != 64 || tile != 16) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0) return B2F_ERR_INVALID;
@@ -789,6 +840,8 @@ extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, co
   p.ldx = ldx;
   p.x_row_index = x_row_index;
   p.x_row_div = x_row_div > 0 ? x_row_div : 1;
+  if (launch_flags & ~3) return B2F_ERR_INVALID;
+  p.flags = launch_flags;
   p.pw[0] = static_cast<const uint8_t*>(pw_gate);
   p.pw[1] = static_cast<const uint8_t*>(pw_up);
   const int mat = pw_up ? 2 : 1;

@@ -244,10 +244,20 @@ def test_packed_tiles_equal_unpacked(dev, E, N, K, T, k):
     h = torch.empty(A, N, dtype=torch.bfloat16, device=dev)
     y = torch.empty(A, K, dtype=torch.bfloat16, device=dev)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, 0, st)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(h), N, 0, 1, 1, A, E, ptr(pd), 0, K, N, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, 0, st)
     torch.cuda.synchronize()
     # rows the plan wrote (plan order, all A assignments) compare bitwise
     assert torch.equal(h.view(torch.int16), h_ref.view(torch.int16))
     assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    # programmatic dependent launch (gate/up lets the down GEMM start early, the
+    # down GEMM waits before copying its input rows): the same bits
+    h2, y2 = torch.empty_like(h), torch.empty_like(y)
+    call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
+         ptr(plan.workspace), plan.workspace.numel(), ptr(h2), N, 1, 2, st)
+    call("b2f_gather_qgemm_affine_mma_packed", ptr(h2), N, 0, 1, 1, A, E, ptr(pd), 0, K, N, 4, 64, 16,
+         ptr(plan.workspace), plan.workspace.numel(), ptr(y2), K, 0, 1, st)
+    torch.cuda.synchronize()
+    assert torch.equal(h2.view(torch.int16), h_ref.view(torch.int16))
+    assert torch.equal(y2.view(torch.int16), y_ref.view(torch.int16))
