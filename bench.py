@@ -307,7 +307,8 @@ def run_ours(args):
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile,
-                          moe_packed=not args.moe_unpacked, pdl=not args.no_pdl)
+                          moe_packed=not args.moe_unpacked, pdl=not args.no_pdl,
+                          moe_streamk=args.streamk)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -708,6 +709,10 @@ def run_moe_layer(args):
     ones = torch.ones(H, dtype=torch.bfloat16, device=dev)
     results = {}
     lib = _capi.lib()
+    # stream-K workspace of the packed expert GEMM (zeroed once; left zeroed)
+    skb = int(lib.b2f_mma_streamk_workspace_bytes())
+    skw_t = torch.zeros(skb, dtype=torch.uint8, device=dev)
+    skw = ptr(skw_t) if args.streamk else 0
     for T in (1, 32, 512):
         A = T * k
         x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
@@ -741,9 +746,10 @@ def run_moe_layer(args):
                 elif eng == "mma":
                     # packed tiles (the decoder's layout): codes + scales in one copy per tile
                     call("b2f_gather_qgemm_affine_mma_packed", ptr(x), H, 0, k, 0, A, E, ptr(ly["g_packed"]),
-                         ptr(ly["u_packed"]), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1, 0, _capi.stream_of(dev))
+                         ptr(ly["u_packed"]), I, H, bits, gs, tile, ptr(pws), pb, ptr(hh), I, 1, skw, skb, 0,
+                         _capi.stream_of(dev))
                     call("b2f_gather_qgemm_affine_mma_packed", ptr(hh), I, 0, 1, 1, A, E, ptr(ly["d_packed"]), 0, H,
-                         I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, 0, _capi.stream_of(dev))
+                         I, bits, gs, tile, ptr(pws), pb, ptr(y), H, 0, skw, skb, 0, _capi.stream_of(dev))
                 elif eng == "mma_mlx":
                     call("b2f_gather_qgemm_affine_mma", ptr(x), H, 0, k, 0, A, E, ptr(g.wq), ptr(g.scales),
                          ptr(g.biases), ptr(u.wq), ptr(u.scales), ptr(u.biases), I, H, bits, gs, tile, ptr(pws), pb,
@@ -985,7 +991,7 @@ def strong_scaling(args, shape, world, dev, exchange, max_ctx):
     dec = Qwen3MoeDecoder(shape, max_batch=b, max_context=max_ctx, page_size=64, device=dev, seed=1234,
                           layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile, moe_packed=not args.moe_unpacked,
-                          pdl=not args.no_pdl)
+                          pdl=not args.no_pdl, moe_streamk=args.streamk)
     dec.fill_random_context(args.ctx)
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
@@ -1162,7 +1168,9 @@ def main():
     ap.add_argument("--moe-tile", type=int, default=16, choices=[16, 32],
                     help="tokens per expert tile of the warp-MMA expert GEMM")
     ap.add_argument("--no-pdl", action="store_true",
-                    help="launch the expert down GEMM in plain stream order (no programmatic dependent launch)")
+                    help="launch the decode-step kernels in plain stream order (no programmatic dependent launch)")
+    ap.add_argument("--streamk", action="store_true",
+                    help="stream-K ranges in the packed expert GEMM instead of one CTA per (slot, row block) item")
     ap.add_argument("--moe-unpacked", action="store_true",
                     help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
     ap.add_argument("--layers", type=int, default=48,

@@ -10,8 +10,9 @@
  *     available from b2f_last_error_string();
  *   - the library never allocates: outputs and workspaces are owned by the
  *     caller (the Python layer allocates them as torch tensors);
- *   - entry points are stream-ordered and hold no global mutable state, so
- *     different threads may drive different streams concurrently.
+ *   - entry points are stream-ordered and hold no global mutable state (the
+ *     launch policy of b2f_set_launch_pdl is per thread), so different
+ *     threads may drive different streams concurrently.
  *
  * Data formats:
  *   AFFINE (weights): W[rows, K] -> wq uint32[rows, K*bits/32] packed
@@ -68,6 +69,14 @@ int b2f_set_wait_limit_ns(int64_t ns);
  * so their consumers' bounded waits run out (how the tests drive the timeout
  * path without any fault); 0 (the default) is normal operation. */
 int b2f_set_producer_stall(int on);
+
+/* Launch policy of the calling thread (default 0).  Non-zero: the decode-step
+ * kernels are launched as programmatic dependent launches, so each may be
+ * scheduled while the kernel before it in the stream runs its last wave; each
+ * waits for that kernel's completion before touching memory and only then
+ * lets the next one be scheduled.  Results are identical either way; a CUDA
+ * graph captured under the policy keeps it.  Returns the previous value. */
+int b2f_set_launch_pdl(int on);
 
 /* ---- (a) affine quantize / (a') dequantize ---------------------------- */
 
@@ -338,18 +347,34 @@ int b2f_mma_repack(const uint32_t* wq, const void* scales, const void* biases, i
 /* b2f_gather_qgemm_affine_mma (plan tile 16) reading b2f_mma_repack tiles
  * (mat 2 for pw_gate / pw_up with SwiGLU fused, mat 1 for pw_gate alone)
  * instead of the MLX-layout codes, scales and biases.  Same results, bit
- * for bit, as the unpacked call.  launch_flags (programmatic dependent
- * launch; 0 = ordinary stream order): bit 0 -- this call may start while
- * the previous kernel in the stream finishes: it stages its first weight
- * tiles, then waits for that kernel before copying x (so x may be that
- * kernel's output); bit 1 -- let the next kernel start once every CTA of
- * this one has started (pair it with bit 0 on the next call). */
+ * for bit, as the unpacked call when sk_workspace is null.
+ *
+ * sk_workspace (optional, 256-byte aligned, b2f_mma_streamk_workspace_bytes
+ * long): stream-K scheduling.  The live (slot, 128/256-row block) items
+ * times their 128-wide K chunks are cut into one equal range per resident
+ * CTA, so every SM streams the same number of weight tiles; an item cut
+ * between two CTAs is summed in fp32 by the second to finish (results
+ * deterministic, within fp32 rounding of the whole-item sum).  Layout: one
+ * int32 arrival counter per resident CTA (SMs x 3, padded to 256 bytes),
+ * then two 4096-float partials per CTA.  The counters must be ZERO before
+ * the first use; each launch that completes leaves them zero (after a
+ * B2F_ERR_TIMEOUT zero them again).  One workspace serves calls in stream
+ * order.
+ *
+ * launch_flags (programmatic dependent launch; 0 = ordinary stream order):
+ * bit 0 -- this call may start while the previous kernel in the stream
+ * finishes: it stages its first weight tiles, then waits for that kernel
+ * before copying x (so x may be that kernel's output, but the plan must be
+ * older); bit 1 -- let the next kernel start once every CTA of this one has
+ * passed that wait (pair it with bit 0 on the next call). */
+int64_t b2f_mma_streamk_workspace_bytes(void);
 int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
                                        int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
                                        const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
                                        int bits, int group_size, int tile, void* plan_workspace,
                                        int64_t plan_workspace_bytes, void* out, int64_t ldo,
-                                       int out_plan_order, int launch_flags, void* stream);
+                                       int out_plan_order, void* sk_workspace, int64_t sk_workspace_bytes,
+                                       int launch_flags, void* stream);
 
 /* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
  * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes

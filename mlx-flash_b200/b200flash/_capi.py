@@ -5,6 +5,7 @@ CPU or framework fallback: if the library is missing or no CUDA device is
 present, every compute entry point raises.
 """
 
+import contextlib
 import ctypes
 import os
 
@@ -102,10 +103,12 @@ SIGNATURES = {
     "b2f_device_status": (_I, [_P, _I]),
     "b2f_set_wait_limit_ns": (_I, [_I64]),
     "b2f_set_producer_stall": (_I, [_I]),
+    "b2f_set_launch_pdl": (_I, [_I]),
     "b2f_mma_packed_bytes": (_I64, [_I64, _I64, _I64, _I]),
     "b2f_mma_repack": (_I, [_P, _P, _P, _I64, _I64, _I64, _I, _P, _I64, _P]),
     "b2f_gather_qgemm_affine_mma_packed": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _I,
-                                                _P, _I64, _P, _I64, _I, _I, _P]),
+                                                _P, _I64, _P, _I64, _I, _P, _I64, _I, _P]),
+    "b2f_mma_streamk_workspace_bytes": (_I64, []),
     "b2f_ep_a2a_row_pitch": (_I64, [_I64, _I64]),
     "b2f_ep_a2a_dispatch": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P]),
     "b2f_ep_a2a_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P, _I64, _P, _P]),
@@ -189,6 +192,19 @@ def device_status(clear: bool = True) -> int:
     if rc != 0:
         raise RuntimeError(f"b2f_device_status failed: {rc}")
     return int(st.value)
+
+
+@contextlib.contextmanager
+def dependent_launches(on: bool = True):
+    """Launch this thread's library kernels as programmatic dependent
+    launches inside the block (each may be scheduled while its predecessor in
+    the stream finishes; results are unchanged); a CUDA graph captured inside
+    keeps the dependent edges."""
+    prev = int(lib().b2f_set_launch_pdl(int(bool(on))))
+    try:
+        yield
+    finally:
+        lib().b2f_set_launch_pdl(prev)
 
 
 def stream_of(device) -> int:

@@ -172,7 +172,8 @@ class Qwen3MoeDecoder:
 
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
                  device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
-                 dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True, pdl: bool = True):
+                 dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True, pdl: bool = True,
+                 moe_streamk: bool = False):
         self.s = s = shape
         self.pdl = bool(pdl)
         self.dev = dev = torch.device(device)
@@ -289,8 +290,8 @@ class Qwen3MoeDecoder:
             self.tile = self.ep.tile
         # warp-MMA experts read their codes as packed tiles (b2f_mma_repack:
         # one contiguous bulk copy per staged tile); the MLX-layout codes stay
-        # for export and the expert-parallel path
-        self.moe_packed = bool(moe_packed) and self.ep is None and self.moe_engine == "mma" and self.tile == 16
+        # for export
+        self.moe_packed = bool(moe_packed) and self.moe_engine == "mma" and self.tile == 16
         if self.moe_packed:
             lib = _capi.lib()
             st = _capi.stream_of(dev)
@@ -302,6 +303,13 @@ class Qwen3MoeDecoder:
                     call("b2f_mma_repack", ptr(w.wq), ptr(w.scales), ptr(w.biases), E_loc, w.N, w.K, mat, ptr(pk),
                          nbytes, st)
                     ly[name + "_packed"] = pk
+            # stream-K: every SM streams the same number of weight tiles (the
+            # counters and partials start zeroed; each launch leaves them zeroed)
+            if self.ep is None:
+                self.sk_bytes = int(lib.b2f_mma_streamk_workspace_bytes()) if moe_streamk else 0
+                self.sk_ws = torch.zeros(max(self.sk_bytes, 256), dtype=torch.uint8, device=dev)
+            elif not moe_streamk:
+                self.ep.sk_bytes = 0
         self.logits = torch.empty(B, s.vocab, dtype=torch.bfloat16, device=dev)
         self.next_tokens = torch.empty(B, dtype=torch.int32, device=dev)
         self.n_splits = pick_splits(B, Hkv, max_context)
@@ -397,16 +405,22 @@ class Qwen3MoeDecoder:
 
     # ------------------------------------------------------------------
     def step(self):
-        """One decode step for all B sequences (graph-capturable)."""
+        """One decode step for all B sequences (graph-capturable).  With
+        `pdl` the library kernels are programmatic dependent launches: each is
+        scheduled while its predecessor finishes (identical results)."""
+        with _capi.dependent_launches(self.pdl and self.ep is None):
+            self._step()
+
+    def _step(self):
         s, B = self.s, self.B
         H, D, Hq, Hkv, E, I = s.hidden, s.head_dim, s.n_heads, s.n_kv_heads, s.n_experts, s.moe_inter
         A = B * s.top_k
         st = _capi.stream_of(self.dev)
         # embedding gather (dequantize selected rows) and first norm
         e = self.embed
+        torch.add(self.positions, 1, out=self.seq_lens)
         call("b2f_dequantize_affine", ptr(e.wq), ptr(e.scales), ptr(e.biases), 0, B, H, e.bits, e.group_size,
              ptr(self.tokens), ptr(self.h), st)
-        torch.add(self.positions, 1, out=self.seq_lens)
         call("b2f_combine_rmsnorm", ptr(self.h), 0, 0, B, 0, ptr(self.layers[0]["in_norm"]), s.rms_eps, H,
              0, ptr(self.xn), st)
         for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
@@ -441,7 +455,8 @@ class Qwen3MoeDecoder:
             if self.ep is not None:
                 self.ep.route(ly["wr"], ly["rbias"], s.norm_topk)
                 y = self.ep.forward((g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases),
-                                    (d.wq, d.scales, d.biases))
+                                    (d.wq, d.scales, d.biases),
+                                    (ly["gate_packed"], ly["up_packed"], ly["down_packed"]) if self.moe_packed else None)
                 call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), 0, B, 1, ptr(nxt), s.rms_eps, H, ptr(self.h),
                      ptr(self.xn), st)
                 continue
@@ -449,16 +464,16 @@ class Qwen3MoeDecoder:
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
                  self.plan_bytes, ptr(self.plan_status), st)
             if self.moe_packed:
-                # gate/up rows land in plan order (the down GEMM's input layout)
-                # the down GEMM is a programmatic dependent launch: its first weight
-                # tiles stream while the gate/up GEMM's last wave finishes
+                # gate/up rows land in plan order (the down GEMM's input layout);
+                # the down GEMM's first weight tiles stream while the gate/up
+                # GEMM's last wave finishes (its plan is two launches old)
                 pdl = 1 if self.pdl else 0
                 call("b2f_gather_qgemm_affine_mma_packed", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(ly["gate_packed"]),
                      ptr(ly["up_packed"]), I, H, g.bits, g.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes,
-                     ptr(self.hh), I, 1, 2 * pdl, st)
+                     ptr(self.hh), I, 1, ptr(self.sk_ws) if self.sk_bytes else 0, self.sk_bytes, 2 * pdl, st)
                 call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), I, 0, 1, 1, A, E, ptr(ly["down_packed"]), 0,
-                     H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), H, 0, pdl,
-                     st)
+                     H, I, d.bits, d.group_size, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), H, 0,
+                     ptr(self.sk_ws) if self.sk_bytes else 0, self.sk_bytes, pdl, st)
             elif self.moe_engine == "mma":
                 # gate/up rows land in plan order (the down GEMM's input layout)
                 call("b2f_gather_qgemm_affine_mma", ptr(self.xn), H, 0, s.top_k, 0, A, E, ptr(g.wq), ptr(g.scales),

@@ -168,6 +168,9 @@ class ExpertParallelMoE:
         self.xs = torch.empty(A, hidden, dtype=torch.bfloat16, device=dev) if engine == "tc" else None
         self.y = torch.empty(A, hidden, dtype=torch.bfloat16, device=dev)
         self.part = torch.empty(self.G, hidden, dtype=torch.bfloat16, device=dev)
+        # stream-K workspace of the packed expert GEMM (zeroed once; left zeroed)
+        self.sk_bytes = int(_capi.lib().b2f_mma_streamk_workspace_bytes()) if engine == "mma" else 0
+        self.sk_ws = torch.zeros(max(self.sk_bytes, 256), dtype=torch.uint8, device=dev)
         self.out = self.part if self.W == 1 else torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
 
     # -- phases (the single-GPU multi-rank emulation in the tests drives them one by one)
@@ -180,8 +183,11 @@ class ExpertParallelMoE:
         if self.W > 1:
             self.exchange.all_gather(self.recv, self.send)
 
-    def compute(self, gate, up, down):
-        """Plan over the gathered assignments, local experts, weighted partial sums."""
+    def compute(self, gate, up, down, packed=None):
+        """Plan over the gathered assignments, local experts, weighted partial
+        sums.  ``packed``: (gate/up tiles of mat 2 each, down tiles of mat 1)
+        from b2f_mma_repack of the local experts, for the warp-MMA engine with
+        16-token tiles: one bulk copy per staged tile, stream-K ranges."""
         seg, st = self.seg, stream_of(self.dev)
         call("b2f_ep_plan", ptr(self.recv), seg.seg_bytes, seg.row_bytes, seg.inds_off, seg.scores_off, self.W,
              self.T, self.k, self.e_begin, self.e_count, self.e_total, self.tile, ptr(self.x_row), ptr(self.wts),
@@ -189,7 +195,18 @@ class ExpertParallelMoE:
         gw, gs_, gb = gate
         uw, us, ub = up
         dw, ds, db = down
-        if self.engine == "mma":
+        if packed is not None:
+            if self.engine != "mma" or self.tile != 16:
+                raise ValueError("packed expert tiles run on the warp-MMA engine with 16-token tiles")
+            pg, pu, pd = packed
+            sk = ptr(self.sk_ws) if self.sk_bytes else 0
+            call("b2f_gather_qgemm_affine_mma_packed", ptr(self.recv), self.H, ptr(self.x_row), 1, 0, self.A,
+                 self.e_count, ptr(pg), ptr(pu), self.I, self.H, self.bits, self.gs, self.tile, ptr(self.plan_ws),
+                 self.plan_bytes, ptr(self.hh), self.I, 1, sk, self.sk_bytes, 0, st)
+            call("b2f_gather_qgemm_affine_mma_packed", ptr(self.hh), self.I, 0, 1, 1, self.A, self.e_count,
+                 ptr(pd), 0, self.H, self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws), self.plan_bytes,
+                 ptr(self.y), self.H, 0, sk, self.sk_bytes, 0, st)
+        elif self.engine == "mma":
             call("b2f_gather_qgemm_affine_mma", ptr(self.recv), self.H, ptr(self.x_row), 1, 0, self.A, self.e_count,
                  ptr(gw), ptr(gs_), ptr(gb), ptr(uw), ptr(us), ptr(ub), self.I, self.H, self.bits, self.gs, self.tile,
                  ptr(self.plan_ws), self.plan_bytes, ptr(self.hh), self.I, 1, st)
@@ -219,9 +236,9 @@ class ExpertParallelMoE:
         if self.W > 1:
             self.exchange.reduce_scatter(self.out, self.part)
 
-    def forward(self, gate, up, down) -> torch.Tensor:
+    def forward(self, gate, up, down, packed=None) -> torch.Tensor:
         self.dispatch()
-        self.compute(gate, up, down)
+        self.compute(gate, up, down, packed)
         self.combine()
         return self.out
 

@@ -24,6 +24,50 @@ inline int check_launch() {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// ---- programmatic dependent launch --------------------------------------
+// With the calling thread's launch policy on (b2f_set_launch_pdl), kernels
+// are launched with programmatic stream serialization: a kernel may be
+// scheduled while the one before it in the stream finishes its last wave.
+// Every kernel so launched calls pdl_enter() before it touches global
+// memory: griddepcontrol.wait returns once the previous kernel has completed
+// and its writes are visible, then griddepcontrol.launch_dependents lets
+// the next kernel be scheduled.  Waiting before triggering keeps the chain
+// transitive -- when kernel n may start, kernel n-2 has completed -- so a
+// kernel may read data written two or more launches back before its wait.
+// Both instructions do nothing in a normal launch.
+int& launch_pdl_policy();
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_trigger();
+}
+
+// kern<<<grid, block, smem, st>>>(args...) under the launch policy; B2F_OK or
+// B2F_ERR_CUDA (with the CUDA error text recorded)
+template <typename... P, typename... A>
+inline int launch_kernel(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (launch_pdl_policy()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<A&&>(args)...);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  return check_launch();
+}
+
 inline bool aligned(const void* p, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

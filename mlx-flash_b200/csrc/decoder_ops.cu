@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
     const float* __restrict__ scores, int k, const __nv_bfloat16* __restrict__ w, float eps, int H,
     __nv_bfloat16* __restrict__ resid_out, __nv_bfloat16* __restrict__ norm_out,
     const float* __restrict__ partial = nullptr, int nsplit = 0, int64_t M = 0) {
+  pdl_enter();
   __shared__ float sh[8];
   const int64_t m = blockIdx.x;
   const int nvec = H / 8;
@@ -153,6 +154,7 @@ struct RopeKvParams {
 // grid (B, heads / 8): one warp per head of the token, so the (Hq + 2Hkv)
 // heads of a decode batch spread over many SMs instead of queuing on B CTAs.
 __global__ void __launch_bounds__(256) qk_norm_rope_kv_kernel(const RopeKvParams p) {
+  pdl_enter();
   constexpr int D = 128;
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -276,7 +278,10 @@ constexpr int RL_MAXV = 4;  // router-row vectors per lane per pass (1024 elemen
 __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                            const __nv_bfloat16* __restrict__ wr,
                                                            const float* __restrict__ bias, int E,
-                                                           float* __restrict__ logits) {
+                                                           float* __restrict__ logits, int32_t* __restrict__ counter) {
+  pdl_enter();
+  // the MoE plan's arrival counter, read by the routing kernel that follows
+  if (counter && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *counter = 0;
   extern __shared__ __align__(16) uint4 xs[];  // [RL_TOK][H/8]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int e = blockIdx.x * 8 + warp;
@@ -337,7 +342,10 @@ __global__ void __launch_bounds__(256) route_logits_kernel(const __nv_bfloat16* 
 __global__ void __launch_bounds__(256) route_logits_mma_kernel(const __nv_bfloat16* __restrict__ x, int T, int H,
                                                                const __nv_bfloat16* __restrict__ wr,
                                                                const float* __restrict__ bias, int E,
-                                                               float* __restrict__ logits) {
+                                                               float* __restrict__ logits, int32_t* __restrict__ counter) {
+  pdl_enter();
+  // the MoE plan's arrival counter, read by the routing kernel that follows
+  if (counter && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *counter = 0;
   __shared__ float red[8][32][4];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int r = lane >> 2, c = lane & 3;
@@ -390,13 +398,13 @@ __global__ void __launch_bounds__(256) route_logits_mma_kernel(const __nv_bfloat
   }
 }
 
+// counter (optional): zeroed by the kernel, for the routing kernel after it
 static int launch_route_logits(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
-                               float* logits, cudaStream_t st) {
+                               float* logits, int32_t* counter, cudaStream_t st) {
   if (E % 8 == 0 && H % 256 == 0) {
     const dim3 g{unsigned(E / 8), unsigned((T + 15) / 16), 1u};
-    route_logits_mma_kernel<<<g, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-                                                static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits);
-    return check_launch();
+    return launch_kernel(route_logits_mma_kernel, g, dim3{256}, 0, st, static_cast<const __nv_bfloat16*>(x),
+                         int(T), int(H), static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits, counter);
   }
   const dim3 g1{unsigned((E + 7) / 8), unsigned((T + RL_TOK - 1) / RL_TOK), 1u};
   const size_t smem = size_t(RL_TOK) * size_t(H) * 2;
@@ -404,9 +412,8 @@ static int launch_route_logits(const void* x, int64_t T, int64_t H, const void* 
       cudaFuncSetAttribute(route_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
           cudaSuccess)
     return check_launch();
-  route_logits_kernel<<<g1, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), int(T), int(H),
-                                               static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits);
-  return check_launch();
+  return launch_kernel(route_logits_kernel, g1, dim3{256}, smem, st, static_cast<const __nv_bfloat16*>(x), int(T),
+                       int(H), static_cast<const __nv_bfloat16*>(wr), bias, int(E), logits, counter);
 }
 
 // gates = softmax(logits[t]) (or sigmoid(logits[t]) per expert); top-k by
@@ -504,6 +511,7 @@ __device__ __forceinline__ void route_topk_token(float* __restrict__ logits, int
 __global__ void __launch_bounds__(256) route_topk_kernel(float* __restrict__ logits, int T, int E, int k,
                                                          int renorm, int gating, float skip,
                                                          int32_t* __restrict__ inds, float* __restrict__ scores) {
+  pdl_enter();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t < T) route_topk_token(logits, t, E, k, renorm, gating, skip, inds, scores);
 }
@@ -516,6 +524,7 @@ __global__ void __launch_bounds__(256) route_topk_plan_kernel(float* __restrict_
                                                               int32_t* __restrict__ inds,
                                                               float* __restrict__ scores, int tile, char* ws,
                                                               PlanLayout L, int32_t* status_out) {
+  pdl_enter();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t < T) route_topk_token(logits, t, E, k, renorm, gating, skip, inds, scores);
   __shared__ int is_last;
@@ -533,12 +542,14 @@ __global__ void __launch_bounds__(256) route_topk_plan_kernel(float* __restrict_
 
 // sigmoid of every element (the shared expert's gate logits, [T, E])
 __global__ void __launch_bounds__(256) sigmoid_inplace_kernel(float* __restrict__ v, int64_t n) {
+  pdl_enter();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
     v[i] = 1.f / (1.f + expf(-v[i]));
 }
 
 __global__ void __launch_bounds__(1024) argmax_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t V,
                                                            int32_t* __restrict__ out) {
+  pdl_enter();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int64_t m = blockIdx.x;
@@ -631,8 +642,7 @@ static int qk_norm_rope_impl(const void* qkv, const float* qkv_partial, int nspl
   p.PS = int(page_size);
   p.bits = bits;
   const dim3 grid{unsigned(B), unsigned((Hq + 2 * Hkv + 7) / 8), 1u};
-  qk_norm_rope_kv_kernel<<<grid, 256, 0, as_stream(stream)>>>(p);
-  return check_launch();
+  return launch_kernel(qk_norm_rope_kv_kernel, grid, dim3{256}, 0, as_stream(stream), p);
 }
 
 }  // namespace b2f
@@ -652,11 +662,11 @@ int b2f_combine_rmsnorm(const void* resid, const void* y, const float* scores, i
       (resid_out && !aligned(resid_out, 16)))
     return B2F_ERR_ALIGN;
   const int threads = int(H / 8) < 256 ? int(((H / 8) + 31) / 32 * 32) : 256;
-  combine_rmsnorm_kernel<<<unsigned(M), threads, 0, as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(resid), static_cast<const __nv_bfloat16*>(y), scores, int(k),
-      static_cast<const __nv_bfloat16*>(weight), eps, int(H), static_cast<__nv_bfloat16*>(resid_out),
-      static_cast<__nv_bfloat16*>(norm_out));
-  return check_launch();
+  return launch_kernel(combine_rmsnorm_kernel, dim3{unsigned(M)}, dim3{unsigned(threads)}, 0, as_stream(stream),
+                       static_cast<const __nv_bfloat16*>(resid), static_cast<const __nv_bfloat16*>(y), scores,
+                       int(k), static_cast<const __nv_bfloat16*>(weight), eps, int(H),
+                       static_cast<__nv_bfloat16*>(resid_out), static_cast<__nv_bfloat16*>(norm_out),
+                       static_cast<const float*>(nullptr), 0, int64_t(0));
 }
 
 int b2f_combine_rmsnorm_partials(const void* resid, const float* partial, int nsplit, int64_t M,
@@ -670,10 +680,11 @@ int b2f_combine_rmsnorm_partials(const void* resid, const float* partial, int ns
       (resid_out && !aligned(resid_out, 16)))
     return B2F_ERR_ALIGN;
   const int threads = int(H / 8) < 256 ? int(((H / 8) + 31) / 32 * 32) : 256;
-  combine_rmsnorm_kernel<<<unsigned(M), threads, 0, as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(resid), nullptr, nullptr, 0, static_cast<const __nv_bfloat16*>(weight),
-      eps, int(H), static_cast<__nv_bfloat16*>(resid_out), static_cast<__nv_bfloat16*>(norm_out), partial, nsplit, M);
-  return check_launch();
+  return launch_kernel(combine_rmsnorm_kernel, dim3{unsigned(M)}, dim3{unsigned(threads)}, 0, as_stream(stream),
+                       static_cast<const __nv_bfloat16*>(resid), static_cast<const __nv_bfloat16*>(nullptr),
+                       static_cast<const float*>(nullptr), 0, static_cast<const __nv_bfloat16*>(weight), eps,
+                       int(H), static_cast<__nv_bfloat16*>(resid_out), static_cast<__nv_bfloat16*>(norm_out),
+                       partial, nsplit, M);
 }
 
 int b2f_qk_norm_rope_kv_append_partials(const float* qkv_partial, int nsplit, int64_t B, int64_t Hq, int64_t Hkv,
@@ -710,11 +721,10 @@ int b2f_moe_route_topk_ex(const void* x, int64_t T, int64_t H, const void* wr, c
   if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
   cudaStream_t st = as_stream(stream);
   if (H > 8192) return B2F_ERR_UNSUPPORTED;
-  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, st);
+  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, nullptr, st);
   if (rc != B2F_OK) return rc;
-  route_topk_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, gating,
-                                                           skip_threshold, inds, scores);
-  return check_launch();
+  return launch_kernel(route_topk_kernel, dim3{unsigned((T + 7) / 8)}, dim3{256}, 0, st, logits_ws, int(T), int(E),
+                       int(k), renorm, gating, skip_threshold, inds, scores);
 }
 
 int b2f_moe_route_topk(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
@@ -737,15 +747,11 @@ int b2f_moe_route_plan_ex(const void* x, int64_t T, int64_t H, const void* wr, c
   const PlanLayout L = plan_layout(T * k, E, tile);
   if (plan_workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
   cudaStream_t st = as_stream(stream);
-  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, st);
-  if (rc != B2F_OK) return rc;
   char* ws = static_cast<char*>(plan_workspace);
-  if (cudaMemsetAsync(reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2, 0, sizeof(int32_t), st) != cudaSuccess)
-    return check_launch();
-  route_topk_plan_kernel<<<unsigned((T + 7) / 8), 256, 0, st>>>(logits_ws, int(T), int(E), int(k), renorm, gating,
-                                                                skip_threshold, inds, scores, tile, ws, L,
-                                                                status_out);
-  return check_launch();
+  int rc = launch_route_logits(x, T, H, wr, bias, E, logits_ws, reinterpret_cast<int32_t*>(ws + L.off_hdr) + 2, st);
+  if (rc != B2F_OK) return rc;
+  return launch_kernel(route_topk_plan_kernel, dim3{unsigned((T + 7) / 8)}, dim3{256}, 0, st, logits_ws, int(T),
+                       int(E), int(k), renorm, gating, skip_threshold, inds, scores, tile, ws, L, status_out);
 }
 
 int b2f_moe_route_plan(const void* x, int64_t T, int64_t H, const void* wr, const float* bias, int64_t E,
@@ -763,19 +769,19 @@ int b2f_router_logits(const void* x, int64_t T, int64_t H, const void* wr, const
   if (!x || !wr || !out) return B2F_ERR_INVALID;
   if (!aligned(x, 16) || !aligned(wr, 16)) return B2F_ERR_ALIGN;
   cudaStream_t st = as_stream(stream);
-  int rc = launch_route_logits(x, T, H, wr, bias, E, out, st);
+  int rc = launch_route_logits(x, T, H, wr, bias, E, out, nullptr, st);
   if (rc != B2F_OK || !apply_sigmoid) return rc;
   const int64_t n = T * E;
-  sigmoid_inplace_kernel<<<unsigned(n < 148 * 8 * 256 ? (n + 255) / 256 : 148 * 8), 256, 0, st>>>(out, n);
-  return check_launch();
+  return launch_kernel(sigmoid_inplace_kernel, dim3{unsigned(n < 148 * 8 * 256 ? (n + 255) / 256 : 148 * 8)},
+                       dim3{256}, 0, st, out, n);
 }
 
 int b2f_argmax_rows(const void* x, int64_t M, int64_t V, int32_t* out, void* stream) {
   if (M < 0 || V <= 0 || V > 0x7fffffff) return B2F_ERR_INVALID;
   if (M == 0) return B2F_OK;
   if (!x || !out) return B2F_ERR_INVALID;
-  argmax_rows_kernel<<<unsigned(M), 1024, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16*>(x), V, out);
-  return check_launch();
+  return launch_kernel(argmax_rows_kernel, dim3{unsigned(M)}, dim3{1024}, 0, as_stream(stream),
+                       static_cast<const __nv_bfloat16*>(x), V, out);
 }
 
 }  // extern "C"

@@ -241,6 +241,7 @@ __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int
 template <class Src>
 __global__ void __launch_bounds__(1024) moe_plan_kernel(const Src src, int A, int E, int tile, char* ws,
                                                         PlanLayout L, int32_t* status_out) {
+  pdl_enter();
   moe_plan_block(src, A, E, tile, ws, L, status_out);
 }
 

@@ -94,14 +94,21 @@ struct MmaParams {
   const uint8_t* pw[2];
   int64_t nb;
   // programmatic dependent launch: bit 0 = this launch depends on the kernel
-  // before it in the stream (weights of the first ring stages are fetched,
-  // then griddepcontrol.wait, then the activation rows); bit 1 = let the next
-  // kernel launch as soon as every CTA of this one has started
+  // before it in the stream, whose output is only the activation rows
+  // (weights of the first ring stages are fetched, then griddepcontrol.wait,
+  // then the activation rows; the plan is two or more launches old); bit 2 =
+  // a programmatic launch that waits before anything else; bit 1 = let the
+  // next kernel launch once every CTA of this one has waited (or, in a
+  // normal launch, has started)
   int flags;
+  // stream-K (packed tiles, one K range): fp32 partials, 2 x 4096 floats per
+  // CTA, and one arrival counter per CTA (zero before the first launch; every
+  // launch that completes leaves them zero); rb = row blocks per slot
+  float* sk_part;
+  int32_t* sk_cnt;
+  int rb;
 };
 
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
   asm volatile(
@@ -123,14 +130,47 @@ __device__ __forceinline__ float sc_half(uint32_t v, int hi) {
   }
 }
 
+// Named barrier 1 over the MMA_CW consumer warps (the producer warp never
+// takes it); consumers_or also returns whether any consumer passed non-zero.
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MMA_CW * 32) : "memory"); }
+__device__ __forceinline__ int consumers_or(int v) {
+  int r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(v), "n"(MMA_CW * 32)
+      : "memory");
+  return r;
+}
+
+// Stream-K cut of one item between two CTAs: each stores its fp32
+// accumulators (thread-private layout, 4096 floats per partial) and counts
+// itself in; the second to arrive adds the other's partial (fp32 addition
+// commutes, so the sum does not depend on which arrives second), leaves the
+// counter zero and runs the epilogue.
+struct MmaCut {
+  float* mine;
+  const float* other;
+  int32_t* counter;
+};
+// kind 1: the item's first chunks, this CTA's last item (its partial slot 1;
+// the next CTA's slot 0, counter of this CTA); kind 2: the item's last
+// chunks, this CTA's first item (slot 0; the previous CTA's slot 1 and counter)
+__device__ __forceinline__ MmaCut mma_cut(const MmaParams& p, int kind) {
+  const int64_t g = blockIdx.x;
+  if (kind == 1) return {p.sk_part + (2 * g + 1) * 4096, p.sk_part + (2 * g + 2) * 4096, p.sk_cnt + g};
+  return {p.sk_part + 2 * g * 4096, p.sk_part + (2 * g - 1) * 4096, p.sk_cnt + (g - 1)};
+}
+
 // The consumer side of one CTA for slots of up to 8*NTA tokens: the warp's
 // WROWS/MAT rows of each matrix (MAT 2: gate and up, SwiGLU epilogue), as
 // MT row tiles of 16.
 template <int MAT, int NTA, bool XPLAN, int WROWS, int BITS, bool SF16, bool PACKED = false>
-__device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
+__device__ __forceinline__ int mma_consume(const MmaParams& p, uint8_t* smem, int STAGE, int W_BYTES, int CTA_ROWS,
                                             uint64_t* full, uint64_t* empty, volatile int* abort_flag, int expert,
                                             int begin, int cnt, int64_t row_base, int h0, int h1, int warp,
-                                            int lane) {
+                                            int lane, int& s, uint32_t& phase, bool walk, int cut_kind,
+                                            volatile int* sk_flag) {
   constexpr int MT = WROWS / 16 / MAT;
   static_assert(MT >= 1, "at least one 16-row tile per matrix");
   const int S = p.stages;
@@ -187,8 +227,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
   };
   load_sb(h0);
 
-  int s = 0;
-  uint32_t phase = 0;
+  // ring position (s, phase) carries over from the CTA's previous item
   for (int h = h0; h < h1; ++h) {
     const bool ok = !*abort_flag && mbar_wait_bounded(&full[s], phase);
     if (!__all_sync(0xffffffffu, ok)) {
@@ -338,7 +377,45 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
       phase ^= 1u;
     }
   }
-  if (*abort_flag) return;
+  if (!walk) {
+    if (*abort_flag) return 1;
+  } else {
+    // a CTA walking several items: every consumer warp takes the same path
+    // (the next item's barriers need all of them)
+    if (consumers_or(*abort_flag)) return 1;
+    if (cut_kind) {
+      const MmaCut cut = mma_cut(p, cut_kind);
+      const int tid = threadIdx.x;  // consumer threads are 0 .. 32*MMA_CW-1
+      int k = 0;
+#pragma unroll
+      for (int m = 0; m < MAT; ++m)
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+#pragma unroll
+          for (int nt = 0; nt < NTA; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) __stcg(cut.mine + (k++) * (32 * MMA_CW) + tid, acc[m][i][nt][e]);
+      consumers_sync();
+      if (tid == 0) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const int old = atomicAdd(cut.counter, 1);
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        if (old) *cut.counter = 0;
+        *sk_flag = old;
+      }
+      consumers_sync();
+      if (*sk_flag == 0) return 0;  // the other CTA finishes the item
+      k = 0;
+#pragma unroll
+      for (int m = 0; m < MAT; ++m)
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+#pragma unroll
+          for (int nt = 0; nt < NTA; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[m][i][nt][e] += __ldcg(cut.other + (k++) * (32 * MMA_CW) + tid);
+    }
+  }
 
   if (p.partial) {
     // split-K: fp32 partial plane of this K range, rows = assignments
@@ -363,7 +440,7 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
                 odd ? make_float2(recv, v1) : make_float2(v0, recv);
         }
     }
-    return;
+    return 0;
   }
 
   // ---- epilogue: values (row R or R+8, tokens 2c and 2c+1) -> bf16 rows ------
@@ -403,9 +480,10 @@ __device__ __forceinline__ void mma_consume(const MmaParams& p, uint8_t* smem, i
         }
       }
   }
+  return 0;
 }
 
-template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false, bool PACKED = false>
+template <int MAT, bool XPLAN, int TILE, int BITS = 4, bool SF16 = false, bool PACKED = false, bool WALK = false>
 __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
     qgemm_mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap tm0,
                      const __grid_constant__ CUtensorMap tm1) {
@@ -424,21 +502,84 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
   uint64_t* empty = full + S;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
 
-  // x = row block, y = slot: one expert's contiguous rows are streamed by
-  // consecutive CTAs; slot-major (wide tiles, one-matrix plans): x = slot,
-  // so the slots reading one row block run back to back and share it in L2
-  if ((p.flags & 2) && threadIdx.x == 0) griddep_launch_dependents();
-  const int slot_id = p.slot_major ? int(blockIdx.x) : int(blockIdx.y);
-  const int rblk = p.slot_major ? int(blockIdx.y) : int(blockIdx.x);
-  if (slot_id >= *p.slot_count) return;
-  const int4 sl = p.slots[slot_id];
-  const int expert = sl.x, begin = sl.y, cnt = min(sl.z, TILE);
-  const int64_t row_base = int64_t(rblk) * CTA_ROWS;
-  if (row_base >= p.N || cnt <= 0) return;
+  volatile int* sk_flag = abort_flag + 1;
+  int64_t* sk_range = reinterpret_cast<int64_t*>(const_cast<int*>(abort_flag + 2));  // stream-K [u0, u1)
+
+  if (p.flags & 4) pdl_wait();
+  if ((p.flags & 2) && !(p.flags & 1) && threadIdx.x == 0) pdl_trigger();
+  // bit 0: a CTA without work still waits, so the grid never completes
+  // before the kernel it depends on
+  const bool idle_wait = (p.flags & 1) != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int HC = int(p.K >> 7);
-  const int h0 = int(blockIdx.z) * p.cpk, h1 = min(HC, h0 + p.cpk);
-  if (h0 >= h1) return;
+
+  // The CTA's items: (slot, row block) pairs, each with a K chunk range.
+  // Per-item grid: x = row block, y = slot (one expert's contiguous rows are
+  // streamed by consecutive CTAs; slot-major -- wide tiles, one-matrix plans
+  // -- x = slot, so the slots reading one row block run back to back and
+  // share it in L2), z = K range.  Stream-K (p.sk_part): the live items in
+  // (slot, row block) order times their HC chunks are cut into G equal unit
+  // ranges, G = min(grid, live items), so a range spans >= HC units and an
+  // item is cut between at most two CTAs.
+  constexpr bool walk = WALK;  // stream-K: p.sk_part is set
+  int n_it = 1;
+  int one_slot = 0, one_rblk = 0, one_h0 = 0, one_h1 = 0;
+  if (walk) {
+    const int64_t n_items = int64_t(*p.slot_count) * p.rb;
+    const int64_t G = min(int64_t(gridDim.x), n_items);
+    if (int64_t(blockIdx.x) >= G) {
+      if (idle_wait) pdl_wait();
+      return;
+    }
+    const int64_t U = n_items * HC;
+    const int64_t u0 = int64_t(blockIdx.x) * U / G, u1 = (int64_t(blockIdx.x) + 1) * U / G;
+    n_it = int((u1 - 1) / HC - u0 / HC + 1);
+    if (threadIdx.x == 0) {
+      sk_range[0] = u0;
+      sk_range[1] = u1;
+    }
+  } else {
+    one_slot = p.slot_major ? int(blockIdx.x) : int(blockIdx.y);
+    one_rblk = p.slot_major ? int(blockIdx.y) : int(blockIdx.x);
+    one_h0 = int(blockIdx.z) * p.cpk;
+    one_h1 = min(HC, one_h0 + p.cpk);
+    bool idle = one_slot >= *p.slot_count || int64_t(one_rblk) * CTA_ROWS >= p.N || one_h0 >= one_h1;
+    if (!idle) idle = p.slots[one_slot].z <= 0;
+    if (idle) {
+      if (idle_wait) pdl_wait();
+      return;
+    }
+  }
+  struct Item {
+    int expert, begin, cnt, rblk, h0, h1;
+    int64_t row_base;
+    int cut;  // 0 whole; 1 its first chunks (this CTA's last item); 2 its last chunks (this CTA's first item)
+  };
+  auto item_at = [&](int ii) {
+    Item w;
+    int slot;
+    if (walk) {
+      const int64_t u0 = sk_range[0], u1 = sk_range[1];
+      const int64_t i = u0 / HC + ii;
+      slot = int(i / p.rb);
+      w.rblk = int(i - int64_t(slot) * p.rb);
+      w.h0 = int(max(u0 - i * HC, int64_t(0)));
+      w.h1 = int(min(u1 - i * HC, int64_t(HC)));
+      w.cut = w.h0 > 0 ? 2 : (w.h1 < HC ? 1 : 0);
+    } else {
+      slot = one_slot;
+      w.rblk = one_rblk;
+      w.h0 = one_h0;
+      w.h1 = one_h1;
+      w.cut = 0;
+    }
+    const int4 sl = p.slots[slot];
+    w.expert = sl.x;
+    w.begin = sl.y;
+    w.cnt = min(sl.z, TILE);
+    w.row_base = int64_t(w.rblk) * CTA_ROWS;
+    return w;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -452,114 +593,125 @@ __global__ void __launch_bounds__(160, MmaShape<TILE>::CTAS)
 
   if (warp == MMA_CW) {
     // ---- producer: weight tiles by TMA, one token row per lane by bulk copy ----
-    if (producers_stalled()) return;  // test control: nothing is issued, the consumers' waits run out
+    if (producers_stalled()) {  // test control: nothing is issued, the consumers' waits run out
+      if (idle_wait) pdl_wait();
+      return;
+    }
     constexpr int XPL = (TILE + 31) / 32;  // token rows per producer lane
     const __nv_bfloat16* xrow[XPL];
-#pragma unroll
-    for (int u = 0; u < XPL; ++u) {
-      xrow[u] = nullptr;
-      const int tk = lane + 32 * u;
-      if (tk < cnt) {
-        const int pos = begin + tk;
-        int64_t row;
-        if constexpr (XPLAN) {
-          row = pos;
-        } else {
-          const int a = p.sorted[pos];
-          row = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
-        }
-        xrow[u] = p.x + row * p.ldx;
-      }
-    }
-    const int wrow = int(int64_t(expert) * p.N + row_base);
-    auto issue_weights = [&](int hh, uint8_t* st, uint64_t* bar) {
+    auto issue_weights = [&](const Item& w, int hh, uint8_t* st, uint64_t* bar) {
       if constexpr (PACKED) {
         // the tile is stored as its shared-memory image: one contiguous copy per matrix
-        const int64_t off = ((int64_t(expert) * p.nb + rblk) * (p.K >> 7) + hh) * int64_t(TB);
+        const int64_t off = ((int64_t(w.expert) * p.nb + w.rblk) * (p.K >> 7) + hh) * int64_t(TB);
         bulk_g2s(st, p.pw[0] + off, uint32_t(TB), bar);
         if constexpr (MAT == 2) bulk_g2s(st + TB, p.pw[1] + off, uint32_t(TB), bar);
       } else {
+        const int wrow = int(int64_t(w.expert) * p.N + w.row_base);
         tma_load_2d(st, &tm0, hh * (4 * BITS), wrow, bar);
         if constexpr (MAT == 2) tma_load_2d(st + CTA_ROWS * RBY, &tm1, hh * (4 * BITS), wrow, bar);
       }
     };
-    auto issue_x = [&](int hh, uint8_t* st, uint64_t* bar) {
+    auto issue_x = [&](const Item& w, int hh, uint8_t* st, uint64_t* bar) {
 #pragma unroll
       for (int u = 0; u < XPL; ++u) {
         const int tk = lane + 32 * u;
-        if (tk < cnt) bulk_g2s(st + W_BYTES + tk * XS, xrow[u] + int64_t(hh) * 128, 256u, bar);
+        if (tk < w.cnt) bulk_g2s(st + W_BYTES + tk * XS, xrow[u] + int64_t(hh) * 128, 256u, bar);
       }
     };
-    int h = h0, s = 0;
+    int s = 0;
     uint32_t phase = 0;
-    if (p.flags & 1) {
-      // dependent launch: the first stages' weights need nothing from the kernel
-      // before this one, so they are in flight before the wait; the activation
-      // rows (that kernel's output) are copied after it
-      const int pre = min(S, h1 - h0);
-      if (lane == 0)
-        for (int u = 0; u < pre; ++u) {
-          mbar_arrive_expect_tx(&full[u], uint32_t(W_BYTES + cnt * 256));
-          issue_weights(h0 + u, smem + u * STAGE, &full[u]);
-        }
-      __syncwarp();
-      griddep_wait();
-      for (int u = 0; u < pre; ++u) issue_x(h0 + u, smem + u * STAGE, &full[u]);
-      h = h0 + pre;
-      s = pre % S;
-      phase = pre == S ? 1u : 0u;
-    }
-    for (; h < h1; ++h) {
-      int ok = 1;
-      if (lane == 0) {
-        if (h - h0 >= S && !mbar_wait_bounded_backoff(&empty[s], phase ^ 1u)) ok = 0;
-        if (*abort_flag) ok = 0;
-        if (ok) {
-          mbar_arrive_expect_tx(&full[s], uint32_t(W_BYTES + cnt * 256));
-        } else {
-          *abort_flag = 1;
+    int64_t issued = 0;
+    bool stop = false;
+    for (int ii = 0; ii < n_it && !stop; ++ii) {
+      const Item w = item_at(ii);
+#pragma unroll
+      for (int u = 0; u < XPL; ++u) {
+        xrow[u] = nullptr;
+        const int tk = lane + 32 * u;
+        if (tk < w.cnt) {
+          const int pos = w.begin + tk;
+          int64_t row;
+          if constexpr (XPLAN) {
+            row = pos;
+          } else {
+            const int a = p.sorted[pos];
+            row = p.x_row_index ? int64_t(p.x_row_index[a]) : int64_t(a) / p.x_row_div;
+          }
+          xrow[u] = p.x + row * p.ldx;
         }
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      uint8_t* st = smem + s * STAGE;
-      if (lane == 0) issue_weights(h, st, &full[s]);
-      issue_x(h, st, &full[s]);
-      if (++s == S) {
-        s = 0;
-        phase ^= 1u;
+      const uint32_t tx = uint32_t(W_BYTES + w.cnt * 256);
+      int h = w.h0;
+      if (ii == 0 && (p.flags & 1)) {
+        // dependent launch: the first stages' weights need nothing from the kernel
+        // before this one, so they are in flight before the wait; the activation
+        // rows (that kernel's output) are copied after it
+        const int pre = min(S, w.h1 - w.h0);
+        if (lane == 0)
+          for (int u = 0; u < pre; ++u) {
+            mbar_arrive_expect_tx(&full[u], tx);
+            issue_weights(w, w.h0 + u, smem + u * STAGE, &full[u]);
+          }
+        __syncwarp();
+        pdl_wait();
+        if ((p.flags & 2) && lane == 0) pdl_trigger();
+        for (int u = 0; u < pre; ++u) issue_x(w, w.h0 + u, smem + u * STAGE, &full[u]);
+        h += pre;
+        issued = pre;
+        s = pre % S;
+        phase = pre == S ? 1u : 0u;
+      }
+      for (; h < w.h1; ++h) {
+        int ok = 1;
+        if (lane == 0) {
+          if (issued >= S && !mbar_wait_bounded_backoff(&empty[s], phase ^ 1u)) ok = 0;
+          if (*abort_flag) ok = 0;
+          if (ok) {
+            mbar_arrive_expect_tx(&full[s], tx);
+          } else {
+            *abort_flag = 1;
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          stop = true;
+          break;
+        }
+        uint8_t* st = smem + s * STAGE;
+        if (lane == 0) issue_weights(w, h, st, &full[s]);
+        issue_x(w, h, st, &full[s]);
+        ++issued;
+        if (++s == S) {
+          s = 0;
+          phase ^= 1u;
+        }
       }
     }
     // copies already issued land before the CTA goes away
-    const int issued = h - h0;
     if (lane == 0)
-      for (int k = 1; k <= S && issued - k >= 0; ++k)
+      for (int64_t k = 1; k <= S && issued - k >= 0; ++k)
         mbar_wait_bounded(&full[(issued - k) % S], uint32_t(((issued - k) / S) & 1), 100000000ull);
     return;
   }
 
-  if constexpr (SH::NTMAX == 2) {
-    if (cnt <= 8) {
-      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, h0, h1, warp, lane);
+  int s = 0;
+  uint32_t phase = 0;
+  for (int ii = 0; ii < n_it; ++ii) {
+    const Item w = item_at(ii);
+    int ab;
+#define B2F_MMA_CONSUME(NT)                                                                                         \
+  mma_consume<MAT, NT, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty,       \
+                                                             abort_flag, w.expert, w.begin, w.cnt, w.row_base,    \
+                                                             w.h0, w.h1, warp, lane, s, phase, walk, w.cut, sk_flag)
+    if constexpr (SH::NTMAX == 2) {
+      ab = w.cnt <= 8 ? B2F_MMA_CONSUME(1) : B2F_MMA_CONSUME(2);
+    } else if constexpr (SH::NTMAX == 4) {
+      ab = w.cnt <= 8 ? B2F_MMA_CONSUME(1) : (w.cnt <= 16 ? B2F_MMA_CONSUME(2) : B2F_MMA_CONSUME(4));
     } else {
-      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, h0, h1, warp, lane);
+      ab = B2F_MMA_CONSUME(SH::NTMAX);
     }
-  } else if constexpr (SH::NTMAX == 4) {
-    if (cnt <= 8) {
-      mma_consume<MAT, 1, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, h0, h1, warp, lane);
-    } else if (cnt <= 16) {
-      mma_consume<MAT, 2, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, h0, h1, warp, lane);
-    } else {
-      mma_consume<MAT, 4, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag, expert,
-                                            begin, cnt, row_base, h0, h1, warp, lane);
-    }
-  } else {
-    mma_consume<MAT, SH::NTMAX, XPLAN, SH::WROWS, BITS, SF16, PACKED>(p, smem, STAGE, W_BYTES, CTA_ROWS, full, empty, abort_flag,
-                                                  expert, begin, cnt, row_base, h0, h1, warp, lane);
+#undef B2F_MMA_CONSUME
+    if (ab) break;
   }
   if (lane == 0 && *abort_flag) report_timeout(p.err);
 }
@@ -614,7 +766,10 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
       m1 = m0;
     }
   }
-  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16, PACKED>;
+  auto kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16, PACKED, false>;
+  if constexpr (PACKED) {
+    if (p.sk_part) kern = qgemm_mma_kernel<MAT, XPLAN, TILE, BITS, SF16, PACKED, true>;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
@@ -625,12 +780,24 @@ static int launch_mma_cfg(MmaParams p, const uint32_t* w0, const uint32_t* w1, i
   // the slots on x; expert tiles keep one expert's row blocks consecutive
   p.slot_major = (TILE == 64 || E == 1) ? 1 : 0;
   if ((p.slot_major ? row_blocks : slots_grid) > 65535) return B2F_ERR_UNSUPPORTED;
-  const dim3 grid = p.slot_major ? dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)}
-                                 : dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)};
-  if (p.flags & 1) {
-    // programmatic dependent launch: may start while the previous kernel in
-    // the stream finishes; the kernel waits (griddepcontrol.wait) before it
-    // reads that kernel's output
+  dim3 grid = p.slot_major ? dim3{unsigned(slots_grid), unsigned(row_blocks), unsigned(ksplit)}
+                           : dim3{unsigned(row_blocks), unsigned(slots_grid), unsigned(ksplit)};
+  if (p.sk_part) {
+    // stream-K: one CTA per resident slot (at most the items of the plan's
+    // largest slot count); the workspace holds sms * CTAS CTAs' partials
+    if (ksplit != 1 || p.partial) return B2F_ERR_INVALID;
+    p.rb = int(row_blocks);
+    const int64_t items = slots_grid * row_blocks;
+    grid = dim3{unsigned(min(int64_t(sms) * per_sm, items)), 1u, 1u};
+  }
+  // programmatic dependent launch (bit 0, or the thread's launch policy):
+  // the grid may start while the previous kernel in the stream finishes.
+  // Bit 0 prefetches weights before griddepcontrol.wait; otherwise every
+  // thread waits first (bit 2).  Under the policy the next kernel may be
+  // scheduled once every CTA has waited (bit 1).
+  if (launch_pdl_policy()) p.flags |= 2;
+  if (launch_pdl_policy() && !(p.flags & 1)) p.flags |= 4;
+  if (p.flags & 5) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3{160, 1, 1};
@@ -813,12 +980,30 @@ extern "C" int b2f_mma_repack(const uint32_t* wq, const void* scales, const void
   return check_launch();
 }
 
+// stream-K workspace: arrival counters for sms * CTAS CTAs (256-byte
+// padded), then two 4096-float partials per CTA
+static int mma_sk_ctas() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                  cudaSuccess)
+    return 0;
+  return sms * MmaShape<16>::CTAS;
+}
+static int64_t mma_sk_counter_bytes() { return (int64_t(mma_sk_ctas()) * 4 + 255) / 256 * 256; }
+
+extern "C" int64_t b2f_mma_streamk_workspace_bytes() {
+  const int64_t g = mma_sk_ctas();
+  if (g <= 0) return 0;
+  return mma_sk_counter_bytes() + g * 2 * 4096 * int64_t(sizeof(float));
+}
+
 extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t* x_row_index,
                                                   int64_t x_row_div, int x_plan_order, int64_t A, int64_t E,
                                                   const void* pw_gate, const void* pw_up, int64_t N, int64_t K,
                                                   int bits, int group_size, int tile, void* plan_workspace,
                                                   int64_t plan_workspace_bytes, void* out, int64_t ldo,
-                                                  int out_plan_order, int launch_flags, void* stream) {
+                                                  int out_plan_order, void* sk_workspace,
+                                                  int64_t sk_workspace_bytes, int launch_flags, void* stream) {
   if (bits != 4 || group_size != 64 || tile != 16) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0) return B2F_ERR_INVALID;
@@ -857,6 +1042,13 @@ extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, co
   p.slots = reinterpret_cast<const int4*>(ws + plan_slots_offset(A, E, tile));
   p.sorted = reinterpret_cast<const int32_t*>(ws + plan_sorted_offset(A, E, tile));
   p.cpk = int(K / 128);
+  if (sk_workspace) {
+    const int64_t skb = b2f_mma_streamk_workspace_bytes();
+    if (skb <= 0 || sk_workspace_bytes < skb) return B2F_ERR_WORKSPACE;
+    if (!aligned(sk_workspace, 256)) return B2F_ERR_ALIGN;
+    p.sk_cnt = static_cast<int32_t*>(sk_workspace);
+    p.sk_part = reinterpret_cast<float*>(static_cast<char*>(sk_workspace) + mma_sk_counter_bytes());
+  }
   cudaStream_t st = as_stream(stream);
   const bool xp = x_plan_order != 0;
   if (pw_up)

@@ -58,6 +58,7 @@ struct TcParams {
 template <int BITS, int MAT, int TILE_N>
 __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tm0,
                                                          const __grid_constant__ CUtensorMap tm1) {
+  pdl_enter();
   constexpr int PKB = TC_KC * BITS / 8;         // packed bytes per row per chunk (32 or 64)
   constexpr int PK_TILE = TC_M * PKB;           // per matrix
   constexpr int A_TILE = TC_M * TC_KC * 2;      // 16 KB per matrix
@@ -367,6 +368,7 @@ __global__ void __launch_bounds__(256, 2) qgemm_tc_kernel(const TcParams p, cons
 __global__ void __launch_bounds__(256) splitk_finalize_kernel(const float* __restrict__ partial, int ksplit, int64_t M,
                                                               int64_t N, const __nv_bfloat16* __restrict__ residual,
                                                               __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  pdl_enter();
   const int64_t total = M * N;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t m = i / N, n = i - m * N;
@@ -434,8 +436,7 @@ static int launch_tc_cfg(TcParams p, const CUtensorMap& m0, const CUtensorMap& m
     return B2F_ERR_CUDA;
   }
   const dim3 grid{unsigned((p.N + TC_M - 1) / TC_M), unsigned(slots_grid), unsigned(p.ksplit)};
-  kern<<<grid, 256, smem, st>>>(p, m0, m1);
-  return check_launch();
+  return launch_kernel(kern, grid, dim3{256}, size_t(smem), st, p, m0, m1);
 }
 
 template <int BITS, int MAT>
@@ -595,9 +596,9 @@ int b2f_qgemm_affine_tcgen05_splitk(const void* x, int64_t ldx, int64_t M, const
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int64_t blocks = (total + 255) / 256;
-  splitk_finalize_kernel<<<unsigned(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8), 256, 0, st>>>(
-      p.partial, ksplit, M, N, static_cast<const __nv_bfloat16*>(residual), p.out, ldy);
-  return check_launch();
+  return launch_kernel(splitk_finalize_kernel, dim3{unsigned(blocks < int64_t(sms) * 8 ? blocks : int64_t(sms) * 8)},
+                       dim3{256}, 0, st, static_cast<const float*>(p.partial), int(ksplit), int64_t(M), int64_t(N),
+                       static_cast<const __nv_bfloat16*>(residual), p.out, int64_t(ldy));
 }
 
 int b2f_gather_qgemm_affine_tcgen05(const void* x, int64_t ldx, const int32_t* x_row_index, int64_t x_row_div,

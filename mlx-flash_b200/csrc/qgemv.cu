@@ -73,6 +73,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + 
 
 template <int BITS, int GS, int NT, int GW, int MAT>
 __global__ void __launch_bounds__(288, 1) qgemv_kernel(const GemvParams p, const SmemPlan L) {
+  pdl_enter();
   constexpr int STEPS = GS / 16;           // MMA k-steps per group
   constexpr int CHUNK_K = GS / 4;          // k values per thread per group
   constexpr int CW = CHUNK_K * BITS / 32;  // packed words per thread per group per row
@@ -481,8 +482,7 @@ static int launch_gemv_cfg(const GemvParams& p, int64_t max_work, int NW, cudaSt
   int64_t grid = int64_t(num_sms()) * per_sm;
   if (grid > max_work) grid = max_work;
   if (grid < 1) grid = 1;
-  kern<<<unsigned(grid), threads, smem, st>>>(p, L);
-  return check_launch();
+  return launch_kernel(kern, dim3{unsigned(grid)}, dim3{unsigned(threads)}, size_t(smem), st, p, L);
 }
 
 // Groups per warp: the smallest GW that keeps <= 8 consumer warps while the
@@ -596,9 +596,8 @@ int b2f_moe_plan(const int32_t* expert_of, int64_t A, int64_t E, int tile, void*
   if (!workspace || workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
   if (A > 0 && !expert_of) return B2F_ERR_INVALID;
   if (!aligned(workspace, 16)) return B2F_ERR_ALIGN;
-  moe_plan_kernel<<<1, 1024, 0, as_stream(stream)>>>(DenseExperts{expert_of}, int(A), int(E), tile,
-                                                     static_cast<char*>(workspace), L, status_out);
-  return check_launch();
+  return launch_kernel(moe_plan_kernel<DenseExperts>, dim3{1}, dim3{1024}, 0, as_stream(stream),
+                       DenseExperts{expert_of}, int(A), int(E), tile, static_cast<char*>(workspace), L, status_out);
 }
 
 int b2f_gather_qgemv_affine(const void* x, int64_t ldx, const int32_t* x_row_index,

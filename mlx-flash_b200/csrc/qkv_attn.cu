@@ -65,6 +65,7 @@ template <int BITS, int D, bool RING>
 __global__ void __launch_bounds__(RING ? 160 : 128) qkv_decode_attn_kernel(const AttnParams p,
                                                                          const __grid_constant__ CUtensorMap tmk,
                                                                          const __grid_constant__ CUtensorMap tmv) {
+  pdl_enter();
   constexpr int DG = D / 64;      // quantization groups per row
   constexpr int KSTEPS = D / 16;  // MMA k-steps for Q.K^T
   constexpr int NTD = D / 8;      // 8-wide output column tiles
@@ -562,6 +563,7 @@ template <int D, int NT>
 __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnParams p,
                                                                     const __grid_constant__ CUtensorMap tmk,
                                                                     const __grid_constant__ CUtensorMap tmv) {
+  pdl_enter();
   static_assert(D == 128, "token-row form: 128-byte code rows");
   constexpr int DG = D / 64;  // quantization groups per row
   constexpr int RB = D;       // bytes per 8-bit code row
@@ -893,6 +895,7 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
 
 __global__ void attn_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part,
                                     int n_splits, int D, __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
   const int64_t bh = blockIdx.x;
   const float* ml = ml_part + bh * n_splits * 2;
   float mstar = -INFINITY;
@@ -965,11 +968,11 @@ static int launch_attn(AttnParams p, cudaStream_t st) {
     }
   }
   const dim3 grid{unsigned(p.n_splits), unsigned(p.Hkv), unsigned(p.B)};
-  kern<<<grid, ring ? 160 : 128, smem, st>>>(p, mk, mv);
-  int rc = check_launch();
+  int rc = launch_kernel(kern, grid, dim3{ring ? 160u : 128u}, size_t(smem), st, p, mk, mv);
   if (rc != B2F_OK || p.n_splits == 1) return rc;
-  attn_combine_kernel<<<unsigned(int64_t(p.B) * p.Hq), 128, 0, st>>>(p.o_part, p.ml_part, p.n_splits, D, p.out);
-  return check_launch();
+  return launch_kernel(attn_combine_kernel, dim3{unsigned(int64_t(p.B) * p.Hq)}, dim3{128}, 0, st,
+                       static_cast<const float*>(p.o_part), static_cast<const float*>(p.ml_part), p.n_splits, D,
+                       p.out);
 }
 
 B2F_DEFINE_WAIT_CONTROLS(attn)

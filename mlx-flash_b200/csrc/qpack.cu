@@ -11,6 +11,11 @@ namespace b2f {
 static thread_local std::string g_last_error;
 void set_last_cuda_error(cudaError_t e) { g_last_error = cudaGetErrorString(e); }
 
+int& launch_pdl_policy() {
+  static thread_local int on = 0;
+  return on;
+}
+
 // ------------------------------------------------------------------------
 // (a) affine quantize.  One thread owns EPT consecutive elements of one
 // group; TPG = GS/EPT neighbouring lanes reduce min/max with shuffles.
@@ -196,6 +201,7 @@ __global__ void __launch_bounds__(256) dequantize_affine_kernel(
     const uint32_t* __restrict__ wq, const typename Tag::T* __restrict__ scales,
     const typename Tag::T* __restrict__ biases, int64_t out_rows, int64_t K, int gs_log2,
     const int32_t* __restrict__ row_index, typename Tag::T* __restrict__ out) {
+  pdl_enter();
   using T = typename Tag::T;
   constexpr int PER = 32 / BITS;
   constexpr uint32_t MASK = (1u << BITS) - 1u;
@@ -269,13 +275,14 @@ static int launch_dequantize(const uint32_t* wq, const void* s, const void* b, i
   auto S = static_cast<const T*>(s);
   auto Bi = static_cast<const T*>(b);
   auto O = static_cast<T*>(out);
+  auto kern = dequantize_affine_kernel<Tag, 4>;
   switch (bits) {
-    case 2: dequantize_affine_kernel<Tag, 2><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
-    case 4: dequantize_affine_kernel<Tag, 4><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
-    case 8: dequantize_affine_kernel<Tag, 8><<<grid, block, 0, st>>>(wq, S, Bi, rows, K, gl, ridx, O); break;
+    case 2: kern = dequantize_affine_kernel<Tag, 2>; break;
+    case 4: break;
+    case 8: kern = dequantize_affine_kernel<Tag, 8>; break;
     default: return B2F_ERR_UNSUPPORTED;
   }
-  return check_launch();
+  return launch_kernel(kern, grid, dim3{unsigned(block)}, 0, st, wq, S, Bi, rows, K, gl, ridx, O);
 }
 
 // ------------------------------------------------------------------------
@@ -530,6 +537,12 @@ int b2f_set_wait_limit_ns(int64_t ns) {
   for (auto f : k_wait_units)
     if (f(2, &v) != 0) return B2F_ERR_CUDA;
   return B2F_OK;
+}
+
+int b2f_set_launch_pdl(int on) {
+  const int prev = launch_pdl_policy();
+  launch_pdl_policy() = on ? 1 : 0;
+  return prev;
 }
 
 int b2f_set_producer_stall(int on) {

@@ -58,3 +58,48 @@ def test_eos_and_cancel(dev):
         eng.submit([1], temperature=0.7)
     with pytest.raises(ValueError):
         eng.submit([1] * 90, max_tokens=10)
+
+
+@pytest.mark.parametrize("chunk", [1, 5, 16])
+def test_chunked_prefill_matches_oracle(dev, chunk):
+    """Prompts pushed through the batched step in chunks of `chunk` rows (the
+    rows of one request attend causally over pages they fill in the same
+    step), then greedy decoding: the oracle runs each request alone, one token
+    per step from an empty cache, on the engine's own token sequence (prompt,
+    then the engine's generated tokens as inputs).  Every generated token must
+    carry the oracle's largest logit up to 0.05 (a near tie), and the oracle's
+    clear winners must be the engine's tokens."""
+    import numpy as np
+
+    from oracle import decoder as odec
+    from test_gpu_decoder import _export
+
+    dec = _decoder(dev)
+    model = _export(dec)
+    s = dec.s
+    prompts = [[3, 14, 15, 92, 65, 35, 89, 79], [9, 2, 6, 5, 3, 5, 8, 9, 7, 9, 3, 2, 3, 8, 4, 6, 2, 6], [7],
+               [1, 4, 1, 4, 2, 1, 3, 5, 6, 2, 3, 7]]
+    max_toks = [6, 4, 7, 5]
+    eng = ContinuousBatchingEngine(dec, BatchSchedulerConfig(max_batch_size=4, prefill_chunk_size=chunk),
+                                   use_graph=True)
+    reqs = [eng.submit(p, max_tokens=m) for p, m in zip(prompts, max_toks)]
+    eng.run_until_idle()
+    exact = 0
+    for p, r in zip(prompts, reqs):
+        assert r.status == RequestStatus.COMPLETED
+        seq = list(p) + list(r.generated_tokens)
+        cache = [[{"k": np.zeros((0, s.n_kv_heads, s.head_dim), np.float32),
+                   "v": np.zeros((0, s.n_kv_heads, s.head_dim), np.float32)}] for _ in range(dec.L)]
+        for i in range(len(seq) - 1):
+            logits, _, _ = odec.decode_step(model, cache, np.array([seq[i]], np.int64), np.array([i], np.int32))
+            if i < len(p) - 1:
+                continue  # prompt positions: the engine keeps no token there
+            got = seq[i + 1]
+            row = logits[0]
+            top = float(row.max())
+            assert row[got] >= top - 0.05, (p, i, got, int(row.argmax()), top - float(row[got]))
+            second = float(np.sort(row)[-2])
+            if top - second > 0.05:
+                assert got == int(row.argmax())
+            exact += int(got == int(row.argmax()))
+    assert exact >= sum(max_toks) - 2

@@ -209,3 +209,44 @@ def test_decode_step_packed_experts_equal_unpacked(dev):
         torch.cuda.synchronize()
         logits.append(dec.logits.clone())
     assert torch.equal(logits[0].view(torch.int16), logits[1].view(torch.int16))
+
+
+@pytest.mark.parametrize("engine,dense,batch", [("mma", "tc", 64), ("mma", "gemv", 8), ("mma", "mma", 24),
+                                                ("tc_gather", "tc", 48), ("gemv", "gemv", 3), ("tc", "tc", 40)])
+def test_decode_step_dependent_launches_bit_identical(dev, engine, dense, batch):
+    """Programmatic dependent launches (each kernel scheduled while its
+    predecessor finishes, waiting for it before touching memory) give
+    bit-identical tokens and logits to plain launches, eagerly and replayed
+    from a CUDA graph, over several steps (each step's KV append read by the
+    next step's attention)."""
+    shape = Qwen3MoeShape(hidden=512, layers=3, n_heads=8, n_kv_heads=2, head_dim=128, moe_inter=256,
+                          n_experts=16, top_k=4, vocab=1000, kv_bits=8)
+    runs = []
+    for pdl in (False, True):
+        for graph in (False, True):
+            dec = Qwen3MoeDecoder(shape, max_batch=batch, max_context=128, page_size=16, device=dev, seed=21,
+                                  moe_engine=engine, dense_engine=dense, pdl=pdl)
+            dec.fill_random_context(33)
+            if graph:
+                s = torch.cuda.Stream(dev)
+                s.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(s):
+                    dec.step()  # warm-up outside capture
+                torch.cuda.current_stream(dev).wait_stream(s)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    dec.step()
+                steps = [g.replay for _ in range(3)]
+            else:
+                dec.step()  # the same warm-up step as the graph run
+                steps = [dec.step for _ in range(3)]
+            toks = []
+            for f in steps:
+                f()
+                toks.append(dec.next_tokens.clone())
+            torch.cuda.synchronize()
+            runs.append((torch.stack(toks), dec.logits.clone(), dec.h.clone()))
+    for toks, logits, h in runs[1:]:
+        assert torch.equal(toks, runs[0][0])
+        assert torch.equal(logits.view(torch.int16), runs[0][1].view(torch.int16))
+        assert torch.equal(h.view(torch.int16), runs[0][2].view(torch.int16))

@@ -32,6 +32,21 @@ def _dev3(t, dev):
     return u32_to_dev(wq, dev), to_dev(s, "bf16", dev), to_dev(b, "bf16", dev)
 
 
+def _repack(loc, m, dev):
+    """b2f_mma_repack tiles of a rank's local experts: (gate, up, down)."""
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+
+    out = []
+    for (wq, s, b), (N, K, mat) in zip(loc, ((m.I, m.H, 2), (m.I, m.H, 2), (m.H, m.I, 1))):
+        nb = int(_capi.lib().b2f_mma_packed_bytes(m.e_count, N, K, mat))
+        t = torch.empty(nb, dtype=torch.uint8, device=dev)
+        call("b2f_mma_repack", ptr(wq.contiguous()), ptr(s.contiguous()), ptr(b.contiguous()), m.e_count, N, K, mat,
+             ptr(t), nb, _capi.stream_of(dev))
+        out.append(t)
+    return tuple(out)
+
+
 def _emulate(dev, W, T, E, k, H, I, bits, engine, seed):
     rng = np.random.default_rng(seed)
     g = _experts(rng, E, I, H, bits)
@@ -42,7 +57,8 @@ def _emulate(dev, W, T, E, k, H, I, bits, engine, seed):
     gd, ud, dd = _dev3(g, dev), _dev3(u, dev), _dev3(d, dev)
     wr_d = to_dev(wr, "bf16", dev)
     shards = [ExpertShard(rank=r, world_size=W, total_experts=E) for r in range(W)]
-    ranks = [ExpertParallelMoE(sh, T, H, I, k, dev, bits=bits, engine=engine) for sh in shards]
+    packed = engine == "mma_packed"
+    ranks = [ExpertParallelMoE(sh, T, H, I, k, dev, bits=bits, engine="mma" if packed else engine) for sh in shards]
     for r, m in enumerate(ranks):
         m.x.copy_(to_dev(xs[r], "bf16", dev))
         m.route(wr_d)
@@ -52,7 +68,7 @@ def _emulate(dev, W, T, E, k, H, I, bits, engine, seed):
         if W > 1:
             m.recv.copy_(gathered)
         loc = [tuple(local_expert_slice(t, shards[r]) for t in w) for w in (gd, ud, dd)]
-        m.compute(*loc)
+        m.compute(*loc, _repack(loc, m, dev) if packed else None)
         parts.append(m.part.float())
     torch.cuda.synchronize()
     total = torch.stack(parts).sum(0)  # the reduce-scatter (before slicing)
@@ -70,6 +86,8 @@ def _emulate(dev, W, T, E, k, H, I, bits, engine, seed):
     (8, 4, 16, 8, 256, 128, 4, "gemv"),
     (4, 16, 32, 8, 512, 256, 4, "mma"),
     (3, 7, 16, 4, 256, 128, 4, "mma"),
+    (4, 16, 32, 8, 512, 256, 4, "mma_packed"),
+    (2, 24, 16, 4, 256, 384, 4, "mma_packed"),
 ])
 def test_ep_block_matches_oracle(dev, W, T, E, k, H, I, bits, engine):
     ranks, shards, xs, wr, (g, u, d), total = _emulate(dev, W, T, E, k, H, I, bits, engine, seed=W * 100 + T)

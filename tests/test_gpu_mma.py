@@ -244,9 +244,9 @@ def test_packed_tiles_equal_unpacked(dev, E, N, K, T, k):
     h = torch.empty(A, N, dtype=torch.bfloat16, device=dev)
     y = torch.empty(A, K, dtype=torch.bfloat16, device=dev)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, 0, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, 0, 0, 0, st)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(h), N, 0, 1, 1, A, E, ptr(pd), 0, K, N, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, 0, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, 0, 0, 0, st)
     torch.cuda.synchronize()
     # rows the plan wrote (plan order, all A assignments) compare bitwise
     assert torch.equal(h.view(torch.int16), h_ref.view(torch.int16))
@@ -255,9 +255,77 @@ def test_packed_tiles_equal_unpacked(dev, E, N, K, T, k):
     # down GEMM waits before copying its input rows): the same bits
     h2, y2 = torch.empty_like(h), torch.empty_like(y)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(h2), N, 1, 2, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(h2), N, 1, 0, 0, 2, st)
     call("b2f_gather_qgemm_affine_mma_packed", ptr(h2), N, 0, 1, 1, A, E, ptr(pd), 0, K, N, 4, 64, 16,
-         ptr(plan.workspace), plan.workspace.numel(), ptr(y2), K, 0, 1, st)
+         ptr(plan.workspace), plan.workspace.numel(), ptr(y2), K, 0, 0, 0, 1, st)
     torch.cuda.synchronize()
     assert torch.equal(h2.view(torch.int16), h_ref.view(torch.int16))
     assert torch.equal(y2.view(torch.int16), y_ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("E,N,K,T,k", [(128, 768, 2048, 64, 8), (96, 2048, 768, 64, 8), (8, 768, 2048, 64, 8),
+                                       (5, 384, 640, 9, 2)])
+def test_packed_streamk_ranges(dev, E, N, K, T, k):
+    """Stream-K scheduling of the packed expert GEMM (every resident CTA
+    streams an equal range of (item, K chunk) units; an item cut between two
+    CTAs is summed by the second to finish).  The first two shapes have more
+    live items than resident CTAs, so items are cut.  Outputs equal the
+    whole-item grid up to the fp32 re-association of the cut items' sums (at
+    most one bf16 rounding step), are bit-identical from launch to launch,
+    and the arrival counters are zero again after every launch."""
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+    from b200flash.decoder import random_qweight
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(E + N)
+    rng = np.random.default_rng(E * 7 + K)
+    G, U, D = (random_qweight(shape, 4, 64, dev, gen) for shape in ((E, N, K), (E, N, K), (E, K, N)))
+    x = torch.randn(T, K, device=dev, generator=gen).to(torch.bfloat16)
+    inds = torch.from_numpy(_routing(rng, T, k, E) if E > 8 else
+                            np.stack([rng.choice(E, size=k, replace=False) for _ in range(T)]).astype(np.int32))
+    plan = mx_compat.MoEPlan(inds.reshape(-1).to(dev), E, 16)
+    lib = _capi.lib()
+    st = _capi.stream_of(dev)
+
+    def pack(w, NN, KK, mat):
+        nb = int(lib.b2f_mma_packed_bytes(E, NN, KK, mat))
+        out = torch.empty(nb, dtype=torch.uint8, device=dev)
+        call("b2f_mma_repack", ptr(w.wq), ptr(w.scales), ptr(w.biases), E, NN, KK, mat, ptr(out), nb, st)
+        return out
+
+    pg, pu, pd = pack(G, N, K, 2), pack(U, N, K, 2), pack(D, K, N, 1)
+    A = plan.A
+    skb = int(lib.b2f_mma_streamk_workspace_bytes())
+    assert skb > 0
+    ws = torch.zeros(skb, dtype=torch.uint8, device=dev)
+
+    def run(sk, h_in=None):
+        # gate/up, then down on h_in (default: this call's own gate/up rows)
+        h = torch.empty(A, N, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(A, K, dtype=torch.bfloat16, device=dev)
+        p, n = (ptr(ws), skb) if sk else (0, 0)
+        call("b2f_gather_qgemm_affine_mma_packed", ptr(x), K, 0, k, 0, A, E, ptr(pg), ptr(pu), N, K, 4, 64, 16,
+             ptr(plan.workspace), plan.workspace.numel(), ptr(h), N, 1, p, n, 0, st)
+        call("b2f_gather_qgemm_affine_mma_packed", ptr(h if h_in is None else h_in), N, 0, 1, 1, A, E, ptr(pd), 0,
+             K, N, 4, 64, 16, ptr(plan.workspace), plan.workspace.numel(), ptr(y), K, 0, p, n, 0, st)
+        torch.cuda.synchronize()
+        return h, y
+
+    # the arrival counters (one int32 per resident CTA, 256-byte padded, ahead
+    # of the partials) start zero and every completed launch leaves them zero
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    counters = ws[:(sms * 3 * 4 + 255) // 256 * 256]
+    assert skb == counters.numel() + sms * 3 * 2 * 4096 * 4
+    h0, y0 = run(False)
+    h1, y1 = run(True, h0)
+    assert int(counters.count_nonzero()) == 0
+    h2, y2 = run(True, h0)
+    assert int(counters.count_nonzero()) == 0
+    plan.check()
+    assert torch.equal(h1.view(torch.int16), h2.view(torch.int16))
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    for got, want, what in ((h1, h0, "gate/up"), (y1, y0, "down")):
+        g, w = got.float(), want.float()
+        assert torch.all((g - w).abs() <= w.abs() * 2.0 ** -7 + 1e-6), what
+        assert float((got.view(torch.int16) == want.view(torch.int16)).float().mean()) > 0.98, what
