@@ -54,8 +54,11 @@ def config_dict(args, world):
             "kv_cache": "8-bit sym g64, paged (64-token pages)", "routing": ("softmax top-8 over x.Wr + a fitted per-expert bias: each token's experts as if "
                         "drawn without replacement from Zipf(1.1) popularity (see routing_fit)"),
             "l2_policy": "inputs larger than L2 (weights ~17 GB, KV ~7 GB), no flush",
-            "parallelism": (f"ep{world} experts (NCCL all-gather dispatch / reduce-scatter combine), "
-                            f"dp{world} attention") if world > 1 else "1 GPU"}
+            "parallelism": (f"ep{world} experts ("
+                            + ("dispatch / combine by the library's NVLink peer-memory kernels"
+                               if getattr(args, "ep_exchange", "nccl") == "p2p"
+                               else "NCCL all-gather dispatch / reduce-scatter combine")
+                            + f"), dp{world} attention") if world > 1 else "1 GPU"}
 
 
 # ---------------------------------------------------------------------------
@@ -297,13 +300,15 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
 
     from b200flash.decoder import Qwen3MoeDecoder, Qwen3MoeShape
-    from b200flash.ep import EPExchange
+    from b200flash.ep import EPExchange, PeerExchange
 
     shape = Qwen3MoeShape()
     max_ctx = args.ctx + args.warmup * 3 + args.steps * 3 + 8
     # N > 1: experts sharded expert-parallel (ExpertShard blocks), attention,
     # router and lm_head data-parallel over each rank's own batch
-    exchange = EPExchange() if world > 1 else None
+    # N > 1: the decode exchange runs on the library's peer-memory kernels
+    # (--ep-exchange p2p) or on NCCL all-gather / reduce-scatter (nccl)
+    exchange = (PeerExchange() if args.ep_exchange == "p2p" else EPExchange()) if world > 1 else None
     dec = Qwen3MoeDecoder(shape, max_batch=args.batch, max_context=max_ctx, page_size=64, device=dev,
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile,
@@ -1173,6 +1178,8 @@ def main():
                     help="stream-K ranges in the packed expert GEMM instead of one CTA per (slot, row block) item")
     ap.add_argument("--moe-unpacked", action="store_true",
                     help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
+    ap.add_argument("--ep-exchange", default="nccl", choices=["p2p", "nccl"],
+                    help="decode expert-parallel exchange for N > 1: peer-memory kernels or NCCL collectives")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")
     ap.add_argument("--profile-window", action="store_true",

@@ -376,8 +376,10 @@ int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t
                                        int out_plan_order, void* sk_workspace, int64_t sk_workspace_bytes,
                                        int launch_flags, void* stream);
 
-/* b2f_gather_qgemm_affine_mma (tile 16, one matrix, x rows x_row(a)) with K
- * cut into ksplit ranges of whole 128-wide chunks (grid z): range z writes
+/* b2f_gather_qgemm_affine_mma (tile 16, or 64: slots of up to 64 tokens,
+ * one unpack of each weight for a whole decode batch; one matrix, x rows
+ * x_row(a)) with K cut into ksplit ranges of whole 128-wide chunks (grid z):
+ * range z writes
  * fp32 planes partial[z][a][0:N] for every planned assignment a, to be summed
  * by the consumer (b2f_qk_norm_rope_kv_append_partials,
  * b2f_combine_rmsnorm_partials).  A dense projection of B decode tokens is
@@ -528,6 +530,44 @@ int b2f_ep_plan(const void* recv, int64_t seg_bytes, int64_t row_bytes, int64_t 
  * output.  bf16 y [G*k, ldy], out [G, ldo]; H % 8 == 0. */
 int b2f_ep_combine_partial(const void* y, int64_t ldy, const float* wts, const int32_t* local,
                            int64_t G, int64_t k, int64_t H, void* out, int64_t ldo, void* stream);
+
+/* ---- (e) expert-parallel decode exchange over NVLink peer memory -------- */
+/* The dispatch / combine of distributed_experts.py:36-150's expert partition
+ * done by this library's kernels storing into the other GPUs' memory (CUDA
+ * IPC mappings of each rank's shared region), in place of the NCCL
+ * all-gather / reduce-scatter above.  Region layout (identical on every rank):
+ * uint32 flags at flags_off (dispatch [64], combine [64]), W routing segments
+ * of seg_bytes at *seg_off (the all-gather's layout, so b2f_ep_plan runs on
+ * it unchanged), bf16 combine rows [T][W][H] at *comb_off.  Returns the
+ * region's bytes (0 for invalid sizes); the region and the caller's int32
+ * control words ctl[4] must be ZERO before the first exchange.  `peers` is a
+ * device array of the W regions' base addresses as mapped in this process
+ * (entry `rank` = the own region). */
+int64_t b2f_ep_p2p_region_bytes(int64_t W, int64_t T, int64_t H, int64_t seg_bytes, int64_t* seg_off,
+                                int64_t* comb_off);
+/* Dispatch: copies this rank's segment `seg` into slot `rank` of every peer's
+ * segment area, writes mask[T][W] (1.0 where rank d owns one of token m's
+ * experts under the ExpertShard block partition, else 0) and, once every
+ * copy is visible system-wide, raises this rank's dispatch flag in every
+ * region with the next exchange number (ctl[0] + 1).  An expert id outside
+ * [0, e_total) records B2F_ERR_INVALID in *status_out. */
+int b2f_ep_p2p_dispatch(const void* seg, int64_t seg_bytes, const int64_t* peers, int64_t seg_off,
+                        int64_t flags_off, int rank, int W, const int32_t* inds, int64_t T, int64_t k,
+                        int64_t e_total, float* mask, int32_t* ctl, int32_t* status_out, void* stream);
+/* Waits until all W flags of `kind` (0 dispatch, 1 combine) in this rank's
+ * region carry the current exchange number ctl[0]; a wait that runs past the
+ * wait limit (b2f_set_wait_limit_ns, 2 s by default) records
+ * B2F_ERR_TIMEOUT in *status_out and the device status and returns. */
+int b2f_ep_p2p_wait(const void* region, int64_t flags_off, int kind, int W, const int32_t* ctl,
+                    int32_t* status_out, void* stream);
+/* Combine: b2f_ep_combine_partial's weighted sums for the W*T gathered tokens,
+ * each stored into the owning rank's combine row (token * W + rank) -- only
+ * tokens with a local expert -- then this rank's combine flag is raised in
+ * every region.  The owner completes the MoE output with
+ * b2f_combine_rmsnorm(resid, rows, mask, T, W, ...). */
+int b2f_ep_p2p_combine(const void* y, int64_t ldy, const float* wts, const int32_t* local, int64_t T, int64_t k,
+                       int64_t H, const int64_t* peers, int64_t comb_off, int64_t flags_off, int rank, int W,
+                       int32_t* ctl, void* stream);
 
 /* ---- (e) expert parallelism over a variable-split all-to-all ---------- */
 /* The dispatch / combine halves of distributed_experts.py:36-150's expert

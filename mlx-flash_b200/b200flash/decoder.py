@@ -339,11 +339,13 @@ class Qwen3MoeDecoder:
             call("b2f_moe_plan", ptr(torch.zeros(B, dtype=torch.int32, device=dev)), B, 1, 16, ptr(self.lmplan_ws),
                  self.lmplan_bytes, 0, _capi.stream_of(dev))
         if dense_engine == "mma":
-            # the batch as slots of one "expert" (a plan over all-zero expert ids)
-            self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, 16))
+            # the batch as 16-token slots of one "expert" (a plan over all-zero
+            # expert ids); 64-token slots measured slower at batch 64
+            self.dmma_tile = 16
+            self.dplan_bytes = int(_capi.lib().b2f_moe_plan_workspace_bytes(B, 1, self.dmma_tile))
             self.dplan_ws = torch.empty(self.dplan_bytes, dtype=torch.uint8, device=dev)
             zeros = torch.zeros(B, dtype=torch.int32, device=dev)
-            call("b2f_moe_plan", ptr(zeros), B, 1, 16, ptr(self.dplan_ws), self.dplan_bytes, 0,
+            call("b2f_moe_plan", ptr(zeros), B, 1, self.dmma_tile, ptr(self.dplan_ws), self.dplan_bytes, 0,
                  _capi.stream_of(dev))
         self.dense_tile = min(256, max(16, (B + 15) // 16 * 16))
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -457,8 +459,10 @@ class Qwen3MoeDecoder:
                 y = self.ep.forward((g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases),
                                     (d.wq, d.scales, d.biases),
                                     (ly["gate_packed"], ly["up_packed"], ly["down_packed"]) if self.moe_packed else None)
-                call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), 0, B, 1, ptr(nxt), s.rms_eps, H, ptr(self.h),
-                     ptr(self.xn), st)
+                # peer exchange: W rows per token weighted by the ownership mask
+                kc = self.ep.combine_k
+                call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), ptr(self.ep.mask) if kc > 1 else 0, B, kc,
+                     ptr(nxt), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
                 continue
             call("b2f_moe_route_plan", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
@@ -530,8 +534,8 @@ class Qwen3MoeDecoder:
         """fp32 split-K partials of x . W^T into the dense workspace."""
         if self.dense_engine == "mma":
             call("b2f_gather_qgemm_affine_mma_partials", ptr(x), ldx, 0, 1, self.B, 1, ptr(w.wq), ptr(w.scales),
-                 ptr(w.biases), w.N, w.K, w.bits, w.group_size, 16, ptr(self.dplan_ws), self.dplan_bytes, ksplit,
-                 ptr(self.dense_ws), self.dense_ws_bytes, st)
+                 ptr(w.biases), w.N, w.K, w.bits, w.group_size, self.dmma_tile, ptr(self.dplan_ws), self.dplan_bytes,
+                 ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
             return
         call("b2f_qgemm_affine_tcgen05_partials", ptr(x), ldx, self.B, ptr(w.wq), ptr(w.scales), ptr(w.biases), w.N,
              w.K, w.bits, w.group_size, self.dense_tile, ksplit, ptr(self.dense_ws), self.dense_ws_bytes, st)
@@ -545,5 +549,7 @@ class Qwen3MoeDecoder:
         if self.moe_engine == "tc":
             per_layer += 1  # the row gather into expert-sorted order
         if self.ep is not None:
-            per_layer += 1  # the partial-sum kernel before the reduce-scatter
+            per_layer += 1  # the partial-sum kernel before the reduce-scatter (or the peer combine)
+            if self.ep.p2p:
+                per_layer += 3  # peer dispatch and the two waits
         return 2 + self.L * per_layer + 2

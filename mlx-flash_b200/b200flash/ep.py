@@ -28,6 +28,8 @@ All buffers are allocated once, so the block (collectives included) can be
 captured in a CUDA graph.  No TMA multicast is used anywhere on this path.
 """
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -100,6 +102,75 @@ class EPExchange:
             out.copy_(tmp.view(self.world, *out.shape)[self.rank])
 
 
+class PeerExchange:
+    """The two exchanges of the expert-parallel MoE done by this library's
+    kernels over NVLink peer memory (``b2f_ep_p2p_*``) instead of NCCL
+    collectives: every rank holds one shared region (routing segments of all
+    ranks, the combine rows of its own tokens, the exchange flags), mapped
+    into every other rank's process by CUDA IPC.  The process group only
+    carries the one-time exchange of the IPC handles; no NCCL call runs in a
+    decode step.  One process per GPU on one node, peer access between every
+    pair of GPUs (NVSwitch)."""
+
+    kind = "p2p"
+
+    def __init__(self, group=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def map_region(self, nbytes: int, device):
+        """A zeroed region of ``nbytes`` on this rank, mapped on every rank.
+        Returns (own region, int64 device table of the W regions' addresses in
+        this process, the mapped peer tensors -- keep them alive)."""
+        from torch.multiprocessing.reductions import reduce_tensor
+
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)
+        rebuild, args = reduce_tensor(buf)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, args, group=self.group)
+        views = [buf if r == self.rank else rebuild(*a) for r, a in enumerate(handles)]
+        peers = torch.tensor([v.data_ptr() for v in views], dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        # every region is zeroed and mapped before any rank's first exchange
+        dist.barrier(group=self.group)
+        return buf, peers, views
+
+
+class LocalPeerGroup:
+    """W ranks' shared regions on ONE device (the single-GPU emulation the
+    tests use): ``exchange(r)`` is rank r's view.  Each rank's kernels store
+    into the other emulated ranks' regions exactly as into a peer GPU's;
+    the caller runs the phases so that every wait finds its flags raised
+    (all dispatches before any dispatch wait, all combines before any
+    combine wait)."""
+
+    def __init__(self, W: int, device):
+        self.W = W
+        self.device = torch.device(device)
+        self.bufs = None
+        self.peers = None
+
+    def exchange(self, rank: int):
+        grp = self
+
+        class _Ex:
+            kind = "p2p"
+            world = grp.W
+
+            def __init__(self):
+                self.rank = rank
+
+            def map_region(self, nbytes, device):
+                if grp.bufs is None:
+                    grp.bufs = [torch.zeros(nbytes, dtype=torch.uint8, device=grp.device) for _ in range(grp.W)]
+                    grp.peers = torch.tensor([b.data_ptr() for b in grp.bufs], dtype=torch.int64, device=grp.device)
+                return grp.bufs[rank], grp.peers, grp.bufs
+
+        return _Ex()
+
+
 class ExpertParallelMoE:
     """Buffers and launches of the expert-parallel MoE block for one rank.
 
@@ -130,9 +201,28 @@ class ExpertParallelMoE:
             raise ValueError("exchange world size differs from the shard's")
         self.exchange = exchange
         self.seg = seg = RoutingSegment(T, hidden, top_k)
-        self.send = torch.zeros(seg.seg_bytes, dtype=torch.uint8, device=dev)
-        self.recv = self.send if self.W == 1 else torch.zeros(self.W * seg.seg_bytes, dtype=torch.uint8,
-                                                              device=dev)
+        self.p2p = getattr(exchange, "kind", None) == "p2p"
+        if self.p2p:
+            so, co = ctypes.c_int64(0), ctypes.c_int64(0)
+            nbytes = int(_capi.lib().b2f_ep_p2p_region_bytes(self.W, T, hidden, seg.seg_bytes,
+                                                              ctypes.addressof(so), ctypes.addressof(co)))
+            if nbytes <= 0:
+                raise ValueError("peer exchange: unsupported sizes")
+            self.region, self.peers, self._mapped = exchange.map_region(nbytes, dev)
+            self.seg_off, self.comb_off, self.flags_off = so.value, co.value, 0
+            self.recv = self.region[so.value: so.value + self.W * seg.seg_bytes]
+            self.send = self.recv[self.rank * seg.seg_bytes: (self.rank + 1) * seg.seg_bytes]
+            # combine rows [T][W][H] and their weights (1 where rank d owns one
+            # of token m's experts): b2f_combine_rmsnorm with k = W sums them
+            self.comb = self.region[co.value: co.value + T * self.W * hidden * 2].view(torch.bfloat16).view(
+                T * self.W, hidden)
+            self.mask = torch.zeros(T, self.W, dtype=torch.float32, device=dev)
+            self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)
+            self.p2p_status = torch.zeros(1, dtype=torch.int32, device=dev)
+        else:
+            self.send = torch.zeros(seg.seg_bytes, dtype=torch.uint8, device=dev)
+            self.recv = self.send if self.W == 1 else torch.zeros(self.W * seg.seg_bytes, dtype=torch.uint8,
+                                                                  device=dev)
         self.x, self.inds, self.scores = seg.views(self.send)
         self.G = self.W * T
         self.A = self.G * top_k
@@ -171,7 +261,10 @@ class ExpertParallelMoE:
         # stream-K workspace of the packed expert GEMM (zeroed once; left zeroed)
         self.sk_bytes = int(_capi.lib().b2f_mma_streamk_workspace_bytes()) if engine == "mma" else 0
         self.sk_ws = torch.zeros(max(self.sk_bytes, 256), dtype=torch.uint8, device=dev)
-        self.out = self.part if self.W == 1 else torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
+        if self.p2p:
+            self.out = self.comb
+        else:
+            self.out = self.part if self.W == 1 else torch.empty(T, hidden, dtype=torch.bfloat16, device=dev)
 
     # -- phases (the single-GPU multi-rank emulation in the tests drives them one by one)
     def route(self, wr: torch.Tensor, bias: torch.Tensor = None, renorm: bool = True):
@@ -180,8 +273,33 @@ class ExpertParallelMoE:
              int(renorm), ptr(self.gates), ptr(self.inds), ptr(self.scores), stream_of(self.dev))
 
     def dispatch(self):
-        if self.W > 1:
+        if self.p2p:
+            self.dispatch_send()
+            self.dispatch_wait()
+        elif self.W > 1:
             self.exchange.all_gather(self.recv, self.send)
+
+    # peer exchange phases (forward() runs them in order; the one-GPU
+    # emulation runs every rank's send before any rank's wait)
+    def dispatch_send(self):
+        st = stream_of(self.dev)
+        call("b2f_ep_p2p_dispatch", ptr(self.send), self.seg.seg_bytes, ptr(self.peers), self.seg_off,
+             self.flags_off, self.rank, self.W, ptr(self.inds), self.T, self.k, self.e_total, ptr(self.mask),
+             ptr(self.ctl), ptr(self.p2p_status), st)
+
+    def dispatch_wait(self):
+        call("b2f_ep_p2p_wait", ptr(self.region), self.flags_off, 0, self.W, ptr(self.ctl), ptr(self.p2p_status),
+             stream_of(self.dev))
+
+    def combine_wait(self):
+        call("b2f_ep_p2p_wait", ptr(self.region), self.flags_off, 1, self.W, ptr(self.ctl), ptr(self.p2p_status),
+             stream_of(self.dev))
+
+    @property
+    def combine_k(self) -> int:
+        """Rows per token of ``out`` (W with the peer exchange: sum them
+        weighted by ``mask``; else 1, already summed)."""
+        return self.W if self.p2p else 1
 
     def compute(self, gate, up, down, packed=None):
         """Plan over the gathered assignments, local experts, weighted partial
@@ -229,11 +347,17 @@ class ExpertParallelMoE:
                  self.plan_bytes, ptr(self.hh), self.I, st)
             call(fn, ptr(self.hh), self.I, 0, 1, self.A, self.e_count, ptr(dw), ptr(ds), ptr(db), 0, 0, 0, self.H,
                  self.I, self.bits, self.gs, self.tile, ptr(self.plan_ws), self.plan_bytes, ptr(self.y), self.H, st)
+        if self.p2p:
+            call("b2f_ep_p2p_combine", ptr(self.y), self.H, ptr(self.wts), ptr(self.local), self.T, self.k, self.H,
+                 ptr(self.peers), self.comb_off, self.flags_off, self.rank, self.W, ptr(self.ctl), st)
+            return
         call("b2f_ep_combine_partial", ptr(self.y), self.H, ptr(self.wts), ptr(self.local), self.G, self.k,
              self.H, ptr(self.part), self.H, st)
 
     def combine(self):
-        if self.W > 1:
+        if self.p2p:
+            self.combine_wait()
+        elif self.W > 1:
             self.exchange.reduce_scatter(self.out, self.part)
 
     def forward(self, gate, up, down, packed=None) -> torch.Tensor:
@@ -243,14 +367,22 @@ class ExpertParallelMoE:
         return self.out
 
     def check(self):
-        """Synchronising check that every gathered expert id was in range."""
+        """Synchronising check that every gathered expert id was in range (and,
+        with the peer exchange, that no wait ran out)."""
         if int(self.plan_status.item()):
             raise IndexError("expert index out of range in the gathered routing")
+        if self.p2p:
+            st = int(self.p2p_status.item())
+            if st == _capi.B2F_ERR_TIMEOUT:
+                raise TimeoutError("peer exchange: a rank's flags did not arrive within the wait limit")
+            if st:
+                raise IndexError("expert index out of range in this rank's routing")
 
     @property
     def launches_per_block(self) -> int:
-        """route, plan, (row gather), gate/up, down, partial; the collectives are NCCL's."""
-        return 6 if self.engine == "tc" else 5
+        """route, plan, (row gather), gate/up, down, partial; the collectives
+        are NCCL's, or with the peer exchange dispatch + two waits."""
+        return (6 if self.engine == "tc" else 5) + (3 if self.p2p else 0)
 
 
 def local_expert_slice(w: torch.Tensor, shard: ExpertShard) -> torch.Tensor:

@@ -286,8 +286,9 @@ def gather_qmm_mma_planned(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, bia
 
 def gather_qmm_mma_partials(x_rows: torch.Tensor, plan: "MoEPlan", w, scales, biases, group_size, bits,
                             ksplit: int, x_row_index: torch.Tensor = None, x_row_div: int = 1) -> torch.Tensor:
-    """Split-K form of ``gather_qmm_mma_planned`` (tile 16, one matrix): fp32
-    planes ``[n_ranges, A, N]`` whose sum over the first axis is the product."""
+    """Split-K form of ``gather_qmm_mma_planned`` (plan tile 16 or 64, one
+    matrix): fp32 planes ``[n_ranges, A, N]`` whose sum over the first axis is
+    the product."""
     dev = require_cuda(x_rows, w, scales, biases, x_row_index)
     E, N = w.shape[0], w.shape[1]
     K = w.shape[2] * 32 // bits

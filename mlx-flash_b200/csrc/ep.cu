@@ -205,8 +205,8 @@ int64_t b2f_ep_a2a_row_pitch(int64_t H, int64_t k) {
 int b2f_ep_a2a_dispatch(const void* x, int64_t ldx, const int32_t* inds, const float* scores, int64_t T, int64_t k,
                         int64_t W, int64_t e_total, int64_t H, void* send, int64_t send_bytes, int32_t* pos,
                         int32_t* send_counts, int32_t* status_out, void* stream) {
-  if (T < 0 || k <= 0 || k > 32 || W <= 0 || W > 64 || H <= 0 || H % 8 != 0 || ldx < H || ldx % 8 != 0)
-    return B2F_ERR_INVALID;
+  if (T < 0 || k <= 0 || k > 32 || W <= 0 || W > 64 || H <= 0 || H % 8 != 0) return B2F_ERR_INVALID;
+  if (T > 0 && (ldx < H || ldx % 8 != 0)) return B2F_ERR_INVALID;  // a rank without tokens reads no row
   if (e_total < W) return B2F_ERR_INVALID;  // every rank owns at least one expert
   if (T * W > 0x7fffffff) return B2F_ERR_UNSUPPORTED;
   if (!pos || !send_counts) return B2F_ERR_INVALID;

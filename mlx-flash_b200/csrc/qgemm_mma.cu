@@ -1078,7 +1078,7 @@ extern "C" int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, 
                                                     int64_t partial_bytes, void* stream) {
   if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
   if (K <= 0 || K % 128 != 0 || N <= 0 || N % 8 != 0) return B2F_ERR_UNSUPPORTED;
-  if (tile != 16) return B2F_ERR_UNSUPPORTED;
+  if (tile != 16 && tile != 64) return B2F_ERR_UNSUPPORTED;
   if (A < 0 || E <= 0 || ksplit < 1 || ksplit > 65535) return B2F_ERR_INVALID;
   if (A == 0) return B2F_OK;
   if (!x || !w || !scales || !biases || !partial) return B2F_ERR_INVALID;
@@ -1114,6 +1114,8 @@ extern "C" int b2f_gather_qgemm_affine_mma_partials(const void* x, int64_t ldx, 
   const int ks = mma_splitk_ranges(K, ksplit, &p.cpk);
   p.partial = partial;
   p.plane = A * N;
+  // 64-token tiles: one unpack of each weight serves a whole decode batch
+  if (tile == 64) return launch_mma_cfg<1, false, 64>(p, w, nullptr, E, max_slots, ks, as_stream(stream));
   return launch_mma_cfg<1, false, 16>(p, w, nullptr, E, max_slots, ks, as_stream(stream));
 }
 

@@ -512,9 +512,10 @@ int b2f_wait_controls_tc(int op, long long* v);
 int b2f_wait_controls_tc2(int op, long long* v);
 int b2f_wait_controls_gemv(int op, long long* v);
 int b2f_wait_controls_attn(int op, long long* v);
+int b2f_wait_controls_p2p(int op, long long* v);
 static int (*const k_wait_units[])(int, long long*) = {b2f_wait_controls_mma, b2f_wait_controls_tc,
                                                         b2f_wait_controls_tc2, b2f_wait_controls_gemv,
-                                                        b2f_wait_controls_attn};
+                                                        b2f_wait_controls_attn, b2f_wait_controls_p2p};
 }  // namespace b2f
 
 extern "C" {

@@ -131,16 +131,20 @@ def test_decode_step_cuda_graph_replay(dev):
     assert torch.equal(dec_a.logits, dec_b.logits)
 
 
-def test_decode_step_bench_shape_matches_oracle(dev):
+@pytest.mark.parametrize("dense", ["tc", "mma"])
+def test_decode_step_bench_shape_matches_oracle(dev, dense):
     """The benchmark's decoder configuration with 2 of its 48 layers: hidden
     2048, 32 query / 4 KV heads of 128, 128 experts top-8 (I 768) with the
     Zipf(1.1) router, 151936-token vocabulary, batch 64, 64-token pages,
-    8-bit KV, the engines the bench uses at batch 64 (warp-MMA experts,
-    tcgen05 split-K dense projections): one step vs the oracle."""
+    8-bit KV, warp-MMA experts over packed tiles and either dense engine
+    (tcgen05 split-K, or warp MMA over 64-token tiles split along K): one step
+    vs the oracle."""
     shape = Qwen3MoeShape(layers=2)
     B, ctx = 64, 256
-    dec = Qwen3MoeDecoder(shape, max_batch=B, max_context=ctx + 8, page_size=64, device=dev, seed=1234)
-    assert dec.moe_engine == "mma" and dec.dense_engine == "tc" and dec.tile == 16
+    dec = Qwen3MoeDecoder(shape, max_batch=B, max_context=ctx + 8, page_size=64, device=dev, seed=1234,
+                          dense_engine=dense)
+    assert dec.moe_engine == "mma" and dec.dense_engine == dense and dec.tile == 16
+    assert dec.moe_packed
     dec.fill_random_context(ctx)
     model = _export(dec)
     cache = _export_cache(dec, ctx)

@@ -1,8 +1,10 @@
-"""The expert-parallel MoE block over real NCCL collectives, one process per
-GPU (needs at least two visible GPUs; skipped otherwise).  Each rank checks
-its tokens' MoE output against the oracle, eagerly and again from a CUDA
-graph that holds the whole block (route, all-gather, plan, experts,
-partials, reduce-scatter) replayed on new inputs."""
+"""The expert-parallel MoE block over real NCCL collectives, and over the
+library's own NVLink peer-memory exchange, one process per GPU (needs at
+least two visible GPUs; skipped otherwise).  Each rank checks its tokens'
+MoE output against the oracle, eagerly and again from a CUDA graph that
+holds the whole block (route, dispatch, plan, experts, partials, combine)
+replayed on new inputs, twice (the peer exchange's flags carry the exchange
+number across replays)."""
 
 import os
 import socket
@@ -20,13 +22,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_path):
+def _rank_main(rank, world, port, out_path, kind="nccl"):
     from datetime import timedelta
 
     import torch.distributed as dist
 
     from b200flash.distributed_experts import ExpertShard
-    from b200flash.ep import EPExchange, ExpertParallelMoE, local_expert_slice
+    from b200flash.ep import EPExchange, ExpertParallelMoE, PeerExchange, local_expert_slice
     from helpers import RTOL, ATOL, to_dev, u32_to_dev
     from oracle import affine, moe
     from oracle.fp import round_to
@@ -48,9 +50,10 @@ def _rank_main(rank, world, port, out_path):
         (g, gd), (u, ud), (d, dd) = experts(I, H), experts(I, H), experts(H, I)
         wr = round_to(rng.normal(0, 0.05, (E, H)).astype(np.float32), "bf16")
         xs = [[round_to(rng.standard_normal((T, H)).astype(np.float32), "bf16") for _ in range(world)]
-              for _ in range(2)]
+              for _ in range(3)]
         shard = ExpertShard(rank=rank, world_size=world, total_experts=E)
-        m = ExpertParallelMoE(shard, T, H, I, k, dev, exchange=EPExchange(), engine="tc")
+        ex = PeerExchange() if kind == "p2p" else EPExchange()
+        m = ExpertParallelMoE(shard, T, H, I, k, dev, exchange=ex, engine="tc")
         loc = [tuple(local_expert_slice(t, shard) for t in w) for w in (gd, ud, dd)]
         wr_d = to_dev(wr, "bf16", dev)
 
@@ -64,7 +67,12 @@ def _rank_main(rank, world, port, out_path):
             # records instead of raising, so every rank takes the same collective steps
             oi, osc = moe.route(x, wr.T, k)
             want, _, _ = moe.expert_mlp(x, oi, osc, g, u, d)
-            got = m.out.float().cpu().numpy()
+            if m.p2p:  # W rows per token, weighted by the ownership mask
+                got = (m.out.float().view(T, world, H) * m.mask[:, :, None]).sum(1).cpu().numpy()
+                if int(m.p2p_status.item()):
+                    errors.append(f"{tag}: peer exchange status {int(m.p2p_status.item())}")
+            else:
+                got = m.out.float().cpu().numpy()
             bad = np.abs(got - want) > ATOL + RTOL * np.abs(want)
             if bad.any():
                 errors.append(f"{tag}: {int(bad.sum())} outside tolerance")
@@ -78,10 +86,11 @@ def _rank_main(rank, world, port, out_path):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             block()
-        m.x.copy_(to_dev(xs[1][rank], "bf16", dev))
-        graph.replay()
-        torch.cuda.synchronize()
-        check(xs[1][rank], "graph replay")
+        for it in (1, 2):
+            m.x.copy_(to_dev(xs[it][rank], "bf16", dev))
+            graph.replay()
+            torch.cuda.synchronize()
+            check(xs[it][rank], f"graph replay {it}")
         del graph
         if errors:
             msg = f"rank {rank}: " + "; ".join(errors)
@@ -96,14 +105,15 @@ def _rank_main(rank, world, port, out_path):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_ep_block_over_nccl(tmp_path):
+@pytest.mark.parametrize("kind", ["nccl", "p2p"])
+def test_ep_block_over_nccl(tmp_path, kind):
     import torch.multiprocessing as mp
 
     world = 2
     port = _free_port()
     ctx = mp.get_context("spawn")
     outs = [str(tmp_path / f"rank{r}.txt") for r in range(world)]
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r])) for r in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, outs[r], kind)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -139,15 +139,17 @@ def test_mma_wide_tile_dense_projection(dev, M, N, K):
 
 @pytest.mark.parametrize("A,E,N,K,ksplit", [(64, 1, 5120, 2048, 6), (64, 1, 2048, 4096, 11), (300, 24, 1000, 1280, 4),
                                             (5, 1, 256, 128, 3)])
-def test_mma_splitk_partials(dev, A, E, N, K, ksplit):
+@pytest.mark.parametrize("tile", [16, 64])
+def test_mma_splitk_partials(dev, A, E, N, K, ksplit, tile):
     """K cut into ranges of whole 128-wide chunks: the fp32 planes sum to the
     product (a one-expert plan is the dense q/k/v or o projection of a decode
-    batch); ksplit beyond the chunk count is clamped."""
+    batch); ksplit beyond the chunk count is clamped.  64-token tiles: one
+    unpack of each weight serves up to 64 tokens (A = 300 spans 5 slots)."""
     rng = np.random.default_rng(A + N + ksplit)
     w = _w(rng, (E, N, K))
     x = round_to(rng.standard_normal((A, K)).astype(np.float32), "bf16")
     eid = (rng.integers(0, E, A) if E > 1 else np.zeros(A)).astype(np.int32)
-    plan = mx_compat.MoEPlan(torch.from_numpy(eid).to(dev), E, 16)
+    plan = mx_compat.MoEPlan(torch.from_numpy(eid).to(dev), E, tile)
     parts = mx_compat.gather_qmm_mma_partials(to_dev(x, "bf16", dev), plan, *_dev3(w, dev), 64, 4, ksplit)
     hc = K // 128
     cpk = -(-hc // min(ksplit, hc))
