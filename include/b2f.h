@@ -376,6 +376,23 @@ int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, const int32_t
                                        int out_plan_order, void* sk_workspace, int64_t sk_workspace_bytes,
                                        int launch_flags, void* stream);
 
+/* Dense projection of a decode batch (the QuantizedLinear forward of
+ * layer_quantization.py:240-256 for M <= 64 token rows: the q/k/v and o
+ * projections of a decode step): fp32 planes partial[P][M][N] whose sum in
+ * plane order is x . dequant(W)^T, P = b2f_qgemm_decode_planes(M, N, K)
+ * (0 for unsupported sizes).  The (128-row block, 128-wide K chunk) units
+ * are cut into equal contiguous ranges, one per SM (stream-K), so every SM
+ * streams the same weight bytes; weights are dequantized to bf16 in
+ * registers (one rounding of q*s + b, as the tcgen05 kernels) and multiplied
+ * on warp MMA.  4-bit, group 64, K % 128 == 0, N % 8 == 0; x bf16 16-byte
+ * aligned with ldx % 8 == 0; partial 8-byte aligned, at least P*M*N floats.
+ * Consumers: b2f_qk_norm_rope_kv_append_partials, b2f_combine_rmsnorm_partials
+ * with nsplit = P. */
+int b2f_qgemm_decode_planes(int64_t M, int64_t N, int64_t K);
+int b2f_qgemm_affine_decode_partials(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                                     const void* scales, const void* biases, int64_t N, int64_t K, int bits,
+                                     int group_size, float* partial, int64_t partial_bytes, void* stream);
+
 /* b2f_gather_qgemm_affine_mma (tile 16, or 64: slots of up to 64 tokens,
  * one unpack of each weight for a whole decode batch; one matrix, x rows
  * x_row(a)) with K cut into ksplit ranges of whole 128-wide chunks (grid z):
@@ -545,6 +562,14 @@ int b2f_ep_combine_partial(const void* y, int64_t ldy, const float* wts, const i
  * (entry `rank` = the own region). */
 int64_t b2f_ep_p2p_region_bytes(int64_t W, int64_t T, int64_t H, int64_t seg_bytes, int64_t* seg_off,
                                 int64_t* comb_off);
+/* CUDA IPC of a region for the peer exchange (one process per GPU): export
+ * writes the 64-byte handle of the device allocation holding `ptr` and ptr's
+ * byte offset in it; import (with the importing rank's device current) maps a
+ * peer's allocation into this process for the CURRENT device, enabling peer
+ * access, and returns its base (add the exporter's offset); close unmaps. */
+int b2f_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int b2f_ipc_import(const void* handle, void** base_out);
+int b2f_ipc_close(void* base);
 /* Dispatch: copies this rank's segment `seg` into slot `rank` of every peer's
  * segment area, writes mask[T][W] (1.0 where rank d owns one of token m's
  * experts under the ExpertShard block partition, else 0) and, once every

@@ -109,6 +109,11 @@ SIGNATURES = {
     "b2f_gather_qgemm_affine_mma_packed": (_I, [_P, _I64, _P, _I64, _I, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _I,
                                                 _P, _I64, _P, _I64, _I, _P, _I64, _I, _P]),
     "b2f_mma_streamk_workspace_bytes": (_I64, []),
+    "b2f_qgemm_decode_planes": (_I, [_I64, _I64, _I64]),
+    "b2f_qgemm_affine_decode_partials": (_I, [_P, _I64, _I64, _P, _P, _P, _I64, _I64, _I, _I, _P, _I64, _P]),
+    "b2f_ipc_export": (_I, [_P, _P, _P]),
+    "b2f_ipc_import": (_I, [_P, _P]),
+    "b2f_ipc_close": (_I, [_P]),
     "b2f_ep_p2p_region_bytes": (_I64, [_I64, _I64, _I64, _I64, _P, _P]),
     "b2f_ep_p2p_dispatch": (_I, [_P, _I64, _P, _I64, _I64, _I, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "b2f_ep_p2p_wait": (_I, [_P, _I64, _I, _I, _P, _P, _P]),

@@ -323,11 +323,14 @@ class Qwen3MoeDecoder:
         # split-K into fp32 planes summed by the RoPE/KV-append and
         # residual+RMSNorm kernels.
         mma_dense = bits == 4 and gs == 64 and H % 128 == 0 and (Hq * D) % 128 == 0
+        dec_dense = mma_dense and B <= 64 and H % 8 == 0
         if dense_engine == "auto":
             dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
-        if dense_engine not in ("tc", "gemv", "mma"):
+        if dense_engine not in ("tc", "gemv", "mma", "dec"):
             raise ValueError(f"unknown dense engine {dense_engine!r}")
         if dense_engine == "mma" and not mma_dense:
+            dense_engine = "tc" if s.group_size == 64 else "gemv"
+        if dense_engine == "dec" and not dec_dense:
             dense_engine = "tc" if s.group_size == 64 else "gemv"
         self.dense_engine = dense_engine
         # lm_head: warp MMA over a one-expert plan for small batches (measured
@@ -365,13 +368,19 @@ class Qwen3MoeDecoder:
 
         lib = _capi.lib()
         # K ranges actually used (every range non-empty); 1 = no split
-        if dense_engine == "mma":
+        if dense_engine == "dec":
+            # stream-K decode GEMM: its plane counts
+            self.ks_qkv = int(lib.b2f_qgemm_decode_planes(B, self.qkv_rows, H))
+            self.ks_o = int(lib.b2f_qgemm_decode_planes(B, H, Hq * D))
+        elif dense_engine == "mma":
             self.ks_qkv = int(lib.b2f_mma_splitk_ranges(H, mma_ksplit_for(self.qkv_rows, H)))
             self.ks_o = int(lib.b2f_mma_splitk_ranges(Hq * D, mma_ksplit_for(H, Hq * D)))
         else:
             self.ks_qkv = int(lib.b2f_qgemm_splitk_ranges(H, ksplit_for(self.qkv_rows, H)))
             self.ks_o = int(lib.b2f_qgemm_splitk_ranges(Hq * D, ksplit_for(H, Hq * D)))
         ws = 0
+        if dense_engine == "dec":
+            ws = 4 * B * max(self.ks_qkv * self.qkv_rows, self.ks_o * H)
         if dense_engine == "mma":
             ws = max(int(lib.b2f_mma_splitk_workspace_bytes(B, self.qkv_rows, H, self.ks_qkv)),
                      int(lib.b2f_mma_splitk_workspace_bytes(B, H, Hq * D, self.ks_o)))
@@ -427,7 +436,7 @@ class Qwen3MoeDecoder:
              0, ptr(self.xn), st)
         for li, (ly, kv) in enumerate(zip(self.layers, self.kv)):
             w = ly["wqkv"]
-            if self.dense_engine == "mma" or (self.dense_engine == "tc" and self.ks_qkv > 1):
+            if self.dense_engine in ("mma", "dec") or (self.dense_engine == "tc" and self.ks_qkv > 1):
                 self._partials(self.xn, H, w, self.ks_qkv, st)
                 call("b2f_qk_norm_rope_kv_append_partials", ptr(self.dense_ws), self.ks_qkv, B, Hq, Hkv, D,
                      ptr(ly["q_norm"]), ptr(ly["k_norm"]), s.rms_eps, s.rope_theta, ptr(self.positions), ptr(self.q),
@@ -444,7 +453,7 @@ class Qwen3MoeDecoder:
                  s.kv_bits, 64, self.softmax_scale, self.n_splits, ptr(self.attn_ws), self.attn_ws_bytes,
                  ptr(self.attn), st)
             w = ly["wo"]
-            if self.dense_engine == "mma" or (self.dense_engine == "tc" and self.ks_o > 1):
+            if self.dense_engine in ("mma", "dec") or (self.dense_engine == "tc" and self.ks_o > 1):
                 self._partials(self.attn, Hq * D, w, self.ks_o, st)
                 call("b2f_combine_rmsnorm_partials", ptr(self.h), ptr(self.dense_ws), self.ks_o, B,
                      ptr(ly["post_norm"]), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
@@ -532,6 +541,10 @@ class Qwen3MoeDecoder:
 
     def _partials(self, x, ldx, w, ksplit, st):
         """fp32 split-K partials of x . W^T into the dense workspace."""
+        if self.dense_engine == "dec":
+            call("b2f_qgemm_affine_decode_partials", ptr(x), ldx, self.B, ptr(w.wq), ptr(w.scales), ptr(w.biases),
+                 w.N, w.K, w.bits, w.group_size, ptr(self.dense_ws), self.dense_ws_bytes, st)
+            return
         if self.dense_engine == "mma":
             call("b2f_gather_qgemm_affine_mma_partials", ptr(x), ldx, 0, 1, self.B, 1, ptr(w.wq), ptr(w.scales),
                  ptr(w.biases), w.N, w.K, w.bits, w.group_size, self.dmma_tile, ptr(self.dplan_ws), self.dplan_bytes,

@@ -122,20 +122,56 @@ class PeerExchange:
     def map_region(self, nbytes: int, device):
         """A zeroed region of ``nbytes`` on this rank, mapped on every rank.
         Returns (own region, int64 device table of the W regions' addresses in
-        this process, the mapped peer tensors -- keep them alive)."""
-        from torch.multiprocessing.reductions import reduce_tensor
+        this process, a handle that unmaps the peers' regions when released).
 
+        Each peer region is opened by ``b2f_ipc_import`` with THIS rank's
+        device current, so the mapping belongs to the device whose kernels
+        store into it (with peer access enabled); a mapping opened under the
+        owner's device index would leave this device without peer access."""
+        device = torch.device(device)
+        for r in range(torch.cuda.device_count()):
+            if r != device.index and not torch.cuda.can_device_access_peer(device, r):
+                raise RuntimeError(f"peer exchange: GPU {device.index} cannot access GPU {r}")
         buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         torch.cuda.synchronize(device)
-        rebuild, args = reduce_tensor(buf)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, args, group=self.group)
-        views = [buf if r == self.rank else rebuild(*a) for r, a in enumerate(handles)]
-        peers = torch.tensor([v.data_ptr() for v in views], dtype=torch.int64, device=device)
+        lib = _capi.lib()
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_int64(0)
+        _capi.check(lib.b2f_ipc_export(ptr(buf), handle, ctypes.addressof(off)), "b2f_ipc_export")
+        shared = [None] * self.world
+        dist.all_gather_object(shared, (handle.raw, off.value), group=self.group)
+        addrs, mapped = [], _PeerMappings()
+        with torch.cuda.device(device):
+            for r, (h, o) in enumerate(shared):
+                if r == self.rank:
+                    addrs.append(buf.data_ptr())
+                    continue
+                base = ctypes.c_void_p(0)
+                _capi.check(lib.b2f_ipc_import(ctypes.create_string_buffer(h, 64), ctypes.addressof(base)),
+                            "b2f_ipc_import")
+                mapped.bases.append(base.value)
+                addrs.append(base.value + o)
+        peers = torch.tensor(addrs, dtype=torch.int64, device=device)
         torch.cuda.synchronize(device)
         # every region is zeroed and mapped before any rank's first exchange
         dist.barrier(group=self.group)
-        return buf, peers, views
+        return buf, peers, mapped
+
+
+class _PeerMappings:
+    """Peer regions opened by b2f_ipc_import; unmapped when released."""
+
+    def __init__(self):
+        self.bases = []
+
+    def __del__(self):
+        try:
+            lib = _capi.lib()
+            for b in self.bases:
+                lib.b2f_ipc_close(ctypes.c_void_p(b))
+        except Exception:
+            pass
+        self.bases = []
 
 
 class LocalPeerGroup:

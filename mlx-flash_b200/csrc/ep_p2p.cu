@@ -41,6 +41,12 @@
 // the slot (row), so one region serves every layer.  Every wait gives up
 // after the unit's wait limit and reports B2F_ERR_TIMEOUT instead of
 // spinning forever.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "common.cuh"
 #include "plan.cuh"
 
@@ -218,7 +224,68 @@ B2F_DEFINE_WAIT_CONTROLS(p2p)
 
 using namespace b2f;
 
+namespace b2f {
+// cuMemGetAddressRange through the runtime's driver entry point: the base of
+// the device allocation that holds a pointer (the unit of CUDA IPC)
+static std::mutex g_range_mu;
+static PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
+static int get_range_fn() {
+  std::lock_guard<std::mutex> lock(g_range_mu);
+  if (g_range) return B2F_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  const cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+    set_last_cuda_error(e == cudaSuccess ? cudaErrorNotSupported : e);
+    return B2F_ERR_CUDA;
+  }
+  g_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  return B2F_OK;
+}
+}  // namespace b2f
+
 extern "C" {
+
+int b2f_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  if (!ptr || !handle_out || !offset_out) return B2F_ERR_INVALID;
+  int rc = get_range_fn();
+  if (rc != B2F_OK) return rc;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (g_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return B2F_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<uintptr_t>(ptr) - uintptr_t(base));
+  return B2F_OK;
+}
+
+int b2f_ipc_import(const void* handle, void** base_out) {
+  if (!handle || !base_out) return B2F_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  return B2F_OK;
+}
+
+int b2f_ipc_close(void* base) {
+  if (!base) return B2F_ERR_INVALID;
+  const cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  return B2F_OK;
+}
 
 int64_t b2f_ep_p2p_region_bytes(int64_t W, int64_t T, int64_t H, int64_t seg_bytes, int64_t* seg_off,
                                 int64_t* comb_off) {

@@ -880,6 +880,252 @@ static int mma_splitk_ranges(int64_t K, int ksplit, int* cpk) {
 int64_t plan_slots_offset(int64_t A, int64_t E, int tile);
 int64_t plan_sorted_offset(int64_t A, int64_t E, int tile);
 
+
+// ---------------------------------------------------------------------------
+// Dense projection of a decode batch: mx.quantized_matmul of M <= 64 token
+// rows (the QuantizedLinear forward, layer_quantization.py:240-256 -- the
+// q/k/v and o projections of a decode step) on warp MMA with the weights
+// dequantized in registers.
+//
+// Work: units (128-row block, 128-wide K chunk) in row-block-major order,
+// cut into G equal contiguous ranges (stream-K), G = the SM count or the unit
+// count if smaller, so every SM streams the same number of weight tiles
+// whatever N and K are.  A range ends in at most a few row blocks; each
+// (row block, range) piece is summed in registers and stored as fp32 into
+// plane `piece` of the output planes [P][M][N] -- piece = the range's index
+// among the ranges covering that row block -- and the range that finishes a
+// row block writes zeros into its remaining planes, so the P planes summed
+// in plane order give the product with no atomics.
+//
+// CTA = 8 consumer warps (16 weight rows each) + 1 producer warp, one CTA
+// per SM.  Per unit the producer TMA-loads the 128 rows' codes (64 bytes per
+// row, 64B swizzle)
+// and the token rows' 128 columns of x as one box of 160 columns x 64 rows
+// (rows past M and columns past K arrive as zeros) into a ring stage -- two
+// copies per unit, not one per token row; the 32 extra columns give the
+// staged rows a 320-byte pitch, so the 16-byte fragment reads of 8 rows hit
+// distinct banks.  Consumer lane (r, c) reads code word 4j + c of rows r and r+8 (k in [32j + 8c, +8)),
+// turns each nibble pair (i, i+4) into the exact bf16 q as (128 + q) - 128,
+// dequantizes w = q*s + b with one bf16 rounding (as the tcgen05 kernels do:
+// no per-group fold, so the accumulators of all 64 tokens fit in registers)
+// and multiplies with the token fragments of the same pairs.
+constexpr int DEC_CW = 8;      // consumer warps per CTA (16 weight rows each)
+constexpr int DEC_ROWS = 16 * DEC_CW;  // weight rows per CTA
+constexpr int DEC_W = DEC_ROWS * 64;
+constexpr int DEC_XS = 320;       // bytes between staged token rows (a 160-column box row)
+constexpr int DEC_STAGE = DEC_W + 64 * DEC_XS;  // 24 KB
+constexpr int DEC_CTAS = 1;     // CTAs per SM
+constexpr int DEC_STAGES = 6;
+
+struct DecParams {
+  const __nv_bfloat16* x;
+  int64_t ldx;
+  int M;
+  const uint32_t* sc;  // bf16 scales [N][G] as 32-bit words (groups 2h, 2h+1)
+  const uint32_t* bi;
+  int64_t N;
+  int G;    // groups per row
+  int C;    // 128-wide chunks per row
+  int64_t U;  // units = row blocks * C
+  int P;    // planes
+  float* partial;  // [P][M][N]
+  int stages;
+};
+
+// the CTA whose range holds unit u (ranges [g*U/G, (g+1)*U/G))
+__host__ __device__ __forceinline__ int64_t dec_range_of(int64_t u, int64_t U, int64_t G) {
+  return ((u + 1) * G - 1) / U;
+}
+
+template <int NT>
+__device__ __forceinline__ void dec_store(const DecParams& p, float (&acc)[8][4], int plane, int64_t row_base,
+                                          int warp, int r, int c, bool zero) {
+  float* out = p.partial + int64_t(plane) * p.M * p.N;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int t0 = 8 * nt + 2 * c;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const float v0 = zero ? 0.f : acc[nt][2 * hf], v1 = zero ? 0.f : acc[nt][2 * hf + 1];
+      // lanes r and r^1 trade so each holds two adjacent rows of one token
+      const float recv = __shfl_xor_sync(0xffffffffu, (r & 1) ? v0 : v1, 4);
+      const bool odd = r & 1;
+      const int tok = odd ? t0 + 1 : t0;
+      const int64_t col = row_base + 16 * warp + 8 * hf + (r & ~1);
+      if (tok < p.M && col < p.N)
+        *reinterpret_cast<float2*>(out + int64_t(tok) * p.N + col) =
+            odd ? make_float2(recv, v1) : make_float2(v0, recv);
+    }
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(32 * (DEC_CW + 1), DEC_CTAS) qgemm_decode_kernel(const DecParams p,
+                                                                     const __grid_constant__ CUtensorMap tm,
+                                                                     const __grid_constant__ CUtensorMap tmx) {
+  extern __shared__ __align__(1024) uint8_t dec_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dec_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * DEC_STAGE);
+  uint64_t* empty = full + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t G = gridDim.x, g = blockIdx.x;
+  const int64_t u0 = g * p.U / G, u1 = (g + 1) * p.U / G;
+  const int n_units = int(u1 - u0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], DEC_CW);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  const uint32_t tx = uint32_t(DEC_STAGE);  // the x boxes always carry 64 rows (zeros past M)
+
+  if (warp == DEC_CW) {
+    // ---- producer: the first stages' weights before waiting for the kernel
+    // that writes x, then x rows and the rest of the ring ----
+    const bool stalled = producers_stalled();  // test control: nothing is issued
+    const int pre = min(S, n_units);
+    if (lane == 0 && !stalled)
+      for (int i = 0; i < pre; ++i) {
+        const int64_t u = u0 + i;
+        mbar_arrive_expect_tx(&full[i], tx);
+        tma_load_2d(smem + i * DEC_STAGE, &tm, int(u % p.C) * 16, int((u / p.C) * DEC_ROWS), &full[i]);
+      }
+    pdl_wait();
+    pdl_trigger();
+    if (stalled) return;
+    int issued = 0;
+    for (int i = 0; i < n_units; ++i) {
+      const int st = i % S;
+      const int64_t u = u0 + i;
+      const int h = int(u % p.C);
+      if (i >= pre) {
+        int ok = 1;
+        if (lane == 0) {
+          if (!mbar_wait_bounded_backoff(&empty[st], uint32_t(((i / S) - 1) & 1)) || *abort_flag) {
+            *abort_flag = 1;
+            ok = 0;
+          } else {
+            mbar_arrive_expect_tx(&full[st], tx);
+            tma_load_2d(smem + st * DEC_STAGE, &tm, h * 16, int((u / p.C) * DEC_ROWS), &full[st]);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      if (lane == 0) tma_load_2d(smem + st * DEC_STAGE + DEC_W, &tmx, h * 128, 0, &full[st]);
+      __syncwarp();
+      issued = i + 1;
+    }
+    // copies already issued land before the CTA goes away
+    if (lane == 0)
+      for (int k = 1; k <= S && issued - k >= 0; ++k)
+        mbar_wait_bounded(&full[(issued - k) % S], uint32_t(((issued - k) / S) & 1), 100000000ull);
+    return;
+  }
+
+  pdl_wait();
+  pdl_trigger();
+  const int r = lane >> 2, c = lane & 3;
+  const int sw = (r >> 1) & 3;  // 64B swizzle phase of rows r and r+8
+  float acc[8][4];
+  int64_t u = u0;
+  int i = 0;
+  bool aborted = false;
+  while (u < u1 && !aborted) {
+    const int64_t blk = u / p.C;
+    const int64_t seg_end = min(u1, (blk + 1) * p.C);
+    const int64_t row_base = blk * DEC_ROWS;
+    const int64_t R0 = row_base + 16 * warp + r, R1 = R0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+    // this segment's (s, b) of rows R0 and R1 for chunk h (groups 2h, 2h+1),
+    // loaded one unit ahead of their use
+    auto load_sb = [&](int64_t uu, uint32_t (&v)[4]) {
+      const int hh = int(uu % p.C);
+      v[0] = R0 < p.N ? p.sc[R0 * (p.G / 2) + hh] : 0u;
+      v[1] = R0 < p.N ? p.bi[R0 * (p.G / 2) + hh] : 0u;
+      v[2] = R1 < p.N ? p.sc[R1 * (p.G / 2) + hh] : 0u;
+      v[3] = R1 < p.N ? p.bi[R1 * (p.G / 2) + hh] : 0u;
+    };
+    uint32_t sbn[4];
+    load_sb(u, sbn);
+    for (; u < seg_end; ++u, ++i) {
+      const uint32_t s0 = sbn[0], b0 = sbn[1], s1 = sbn[2], b1 = sbn[3];
+      if (u + 1 < seg_end) load_sb(u + 1, sbn);
+      const int st = i % S;
+      const bool ok = !*abort_flag && mbar_wait_bounded(&full[st], uint32_t((i / S) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) *abort_flag = 1;
+        aborted = true;
+        break;
+      }
+      const uint8_t* wst = smem + st * DEC_STAGE;
+      const uint8_t* xst = wst + DEC_W;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t sel = (j >> 1) ? 0x3232u : 0x1010u;  // group 2h + j/2 as a (v, v) pair
+        const uint32_t S0 = prmt(s0, s0, sel), B0 = prmt(b0, b0, sel);
+        const uint32_t S1 = prmt(s1, s1, sel), B1 = prmt(b1, b1, sel);
+        const uint8_t* rowp = wst + (16 * warp + r) * 64 + 16 * (j ^ sw) + 4 * c;
+        const uint32_t wl = *reinterpret_cast<const uint32_t*>(rowp);
+        const uint32_t wh = *reinterpret_cast<const uint32_t*>(rowp + 8 * 64);
+        uint32_t al[4], ah[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          al[q] = hfma2_bf(hsub2_bf(and_or(wl >> (4 * q), 0x000F000Fu, 0x43004300u), 0x43004300u), S0, B0);
+          ah[q] = hfma2_bf(hsub2_bf(and_or(wh >> (4 * q), 0x000F000Fu, 0x43004300u), 0x43004300u), S1, B1);
+        }
+        const uint32_t a0[4] = {al[0], ah[0], al[1], ah[1]};  // k-step 2j: pairs (0,4) (1,5)
+        const uint32_t a1[4] = {al[2], ah[2], al[3], ah[3]};  // k-step 2j+1: pairs (2,6) (3,7)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xst + (8 * nt + r) * DEC_XS + 16 * c + 64 * j);
+          const uint32_t bx0[2] = {prmt(xv.x, xv.z, 0x5410u), prmt(xv.x, xv.z, 0x7632u)};
+          const uint32_t bx1[2] = {prmt(xv.y, xv.w, 0x5410u), prmt(xv.y, xv.w, 0x7632u)};
+          mma_bf16_16816(acc[nt], a0, bx0);
+          mma_bf16_16816(acc[nt], a1, bx1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (aborted) break;
+    const int piece = int(g - dec_range_of(blk * p.C, p.U, G));
+    dec_store<NT>(p, acc, piece, row_base, warp, r, c, false);
+    if (seg_end == (blk + 1) * p.C)  // this range finishes the row block: its unused planes are zero
+      for (int q = piece + 1; q < p.P; ++q) dec_store<NT>(p, acc, q, row_base, warp, r, c, true);
+  }
+  if (lane == 0 && *abort_flag) report_timeout(nullptr);
+}
+
+// Planes of b2f_qgemm_affine_decode_partials: the most ranges covering one
+// row block, for G ranges over U units of C chunks.
+static int dec_planes(int64_t NB, int64_t C, int64_t G) {
+  const int64_t U = NB * C;
+  int P = 1;
+  for (int64_t b = 0; b < NB; ++b) {
+    const int64_t n = dec_range_of((b + 1) * C - 1, U, G) - dec_range_of(b * C, U, G) + 1;
+    if (n > P) P = int(n);
+  }
+  return P;
+}
+static int64_t dec_grid(int64_t NB, int64_t C) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                    cudaSuccess)
+      sms = 148;
+  }
+  return std::min<int64_t>(NB * C, int64_t(sms) * DEC_CTAS);
+}
+
 B2F_DEFINE_WAIT_CONTROLS(mma)
 
 }  // namespace b2f
@@ -1056,6 +1302,69 @@ extern "C" int b2f_gather_qgemm_affine_mma_packed(const void* x, int64_t ldx, co
               : launch_mma_cfg<2, false, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st);
   return xp ? launch_mma_cfg<1, true, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st)
             : launch_mma_cfg<1, false, 16, 4, false, true>(p, nullptr, nullptr, E, max_slots, 1, st);
+}
+
+extern "C" int b2f_qgemm_decode_planes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || M > 64 || N <= 0 || K <= 0 || K % 128 != 0) return 0;
+  const int64_t NB = (N + DEC_ROWS - 1) / DEC_ROWS, C = K / 128;
+  return dec_planes(NB, C, dec_grid(NB, C));
+}
+
+extern "C" int b2f_qgemm_affine_decode_partials(const void* x, int64_t ldx, int64_t M, const uint32_t* wq,
+                                                const void* scales, const void* biases, int64_t N, int64_t K,
+                                                int bits, int group_size, float* partial, int64_t partial_bytes,
+                                                void* stream) {
+  if (bits != 4 || group_size != 64) return B2F_ERR_UNSUPPORTED;
+  if (M < 0 || N <= 0 || K <= 0) return B2F_ERR_INVALID;
+  if (M > 64 || K % 128 != 0 || N % 8 != 0 || N > 0x7fffffffLL) return B2F_ERR_UNSUPPORTED;
+  if (M == 0) return B2F_OK;
+  if (!x || !wq || !scales || !biases || !partial) return B2F_ERR_INVALID;
+  if (ldx < K) return B2F_ERR_INVALID;
+  if (!aligned(x, 16) || ldx % 8 != 0 || !aligned(wq, 16) || !aligned(partial, 8) || !aligned(scales, 4) ||
+      !aligned(biases, 4))
+    return B2F_ERR_ALIGN;
+  const int64_t NB = (N + DEC_ROWS - 1) / DEC_ROWS, C = K / 128;
+  const int64_t G = dec_grid(NB, C);
+  DecParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.ldx = ldx;
+  p.M = int(M);
+  p.sc = static_cast<const uint32_t*>(scales);
+  p.bi = static_cast<const uint32_t*>(biases);
+  p.N = N;
+  p.G = int(K / 64);
+  p.C = int(C);
+  p.U = NB * C;
+  p.P = dec_planes(NB, C, G);
+  p.partial = partial;
+  if (partial_bytes < int64_t(p.P) * M * N * int64_t(sizeof(float))) return B2F_ERR_WORKSPACE;
+  int rc = get_encoder();
+  if (rc != B2F_OK) return rc;
+  CUtensorMap tm{}, tmx{};
+  rc = make_mma_weight_map(&tm, wq, N, K, DEC_ROWS, 4);
+  if (rc != B2F_OK) return rc;
+  {
+    // x as bf16 [M rows, K columns]; box 160 columns x 64 rows, no swizzle
+    const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(M)};
+    const cuuint64_t strides[1] = {cuuint64_t(ldx) * 2};
+    const cuuint32_t box[2] = {uint32_t(DEC_XS / 2), 64u};
+    const cuuint32_t estr[2] = {1, 1};
+    if (g_encode(&tmx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return B2F_ERR_INVALID;
+  }
+  const int S = DEC_STAGES;
+  const int smem = S * DEC_STAGE + 1024 + 256;
+  auto kern = M <= 16 ? qgemm_decode_kernel<2> : (M <= 32 ? qgemm_decode_kernel<4> : qgemm_decode_kernel<8>);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) {
+    set_last_cuda_error(e);
+    return B2F_ERR_CUDA;
+  }
+  p.stages = S;
+  return launch_kernel(kern, dim3{unsigned(G)}, dim3{unsigned(32 * (DEC_CW + 1))}, size_t(smem), as_stream(stream),
+                       p, tm, tmx);
 }
 
 extern "C" int b2f_mma_splitk_ranges(int64_t K, int ksplit) {

@@ -159,6 +159,43 @@ def test_mma_splitk_partials(dev, A, E, N, K, ksplit, tile):
     assert_close(to_np(parts.sum(0)), want, what=f"mma split-K A={A} E={E} N={N} K={K} ks={ksplit}")
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 5120, 2048), (64, 2048, 4096), (37, 1000, 1280), (16, 384, 640),
+                                   (8, 256, 128), (1, 512, 256), (64, 151936 // 16, 2048)])
+def test_decode_partials_stream_k(dev, M, N, K):
+    """The stream-K decode GEMM (the q/k/v and o shapes of a batch-64 decode
+    step, ragged token counts, a partial last row block at N = 1000, one
+    chunk per row at K = 128): its planes, summed in plane order, against the
+    oracle's bf16-dequantized weights (the kernel rounds q*s + b to bf16 once,
+    as the tcgen05 kernels do); the plane count is the one the C ABI
+    reports, and a second launch gives the same bits."""
+    from b200flash import _capi
+    from b200flash._capi import call, ptr
+
+    rng = np.random.default_rng(M * 7 + N + K)
+    w = _w(rng, (1, N, K))
+    x = round_to(rng.standard_normal((M, K)).astype(np.float32), "bf16")
+    wq, sc, bi = _dev3(w, dev)
+    P = int(_capi.lib().b2f_qgemm_decode_planes(M, N, K))
+    assert P >= 1
+    st = _capi.stream_of(dev)
+    outs = []
+    for _ in range(2):
+        part = torch.full((P, M, N), float("nan"), dtype=torch.float32, device=dev)
+        call("b2f_qgemm_affine_decode_partials", ptr(to_dev(x, "bf16", dev)), K, M, ptr(wq[0]), ptr(sc[0]),
+             ptr(bi[0]), N, K, 4, 64, ptr(part), part.numel() * 4, st)
+        torch.cuda.synchronize()
+        outs.append(part)
+    # every plane element is written (a zero where a row block has fewer pieces)
+    assert not torch.isnan(outs[0]).any()
+    assert torch.equal(outs[0], outs[1])
+    total = outs[0][0].clone()
+    for q in range(1, P):
+        total += outs[0][q]
+    deq = affine.dequantize(w[0][0], w[1][0], w[2][0], 64, 4, "bf16").astype(np.float64)
+    want = x.astype(np.float64) @ deq.T
+    assert_close(to_np(total), want, what=f"decode GEMM M={M} N={N} K={K} P={P}")
+
+
 def _two_bit(rng, E, N, K):
     """Experts quantized to 4 bits, then requantized to the 2-bit cold-expert
     format by the oracle restatement of requantize_4bit_to_2bit."""
