@@ -56,7 +56,7 @@ def config_dict(args, world):
             "l2_policy": "inputs larger than L2 (weights ~17 GB, KV ~7 GB), no flush",
             "parallelism": (f"ep{world} experts ("
                             + ("dispatch / combine by the library's NVLink peer-memory kernels"
-                               if getattr(args, "ep_exchange", "nccl") == "p2p"
+                               if getattr(args, "ep_exchange", "p2p") == "p2p"
                                else "NCCL all-gather dispatch / reduce-scatter combine")
                             + f"), dp{world} attention") if world > 1 else "1 GPU"}
 
@@ -1168,7 +1168,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--moe-engine", default="auto", choices=["auto", "mma", "tc_gather", "tc", "gemv"],
                     help="routed-expert GEMM engine (auto: the decoder's choice for this batch)")
-    ap.add_argument("--dense-engine", default="auto", choices=["auto", "mma", "tc", "gemv"],
+    ap.add_argument("--dense-engine", default="auto", choices=["auto", "mma", "tc", "gemv", "dec"],
                     help="q/k/v and o projection engine (auto: the decoder's choice for this batch)")
     ap.add_argument("--moe-tile", type=int, default=16, choices=[16, 32],
                     help="tokens per expert tile of the warp-MMA expert GEMM")
@@ -1178,7 +1178,7 @@ def main():
                     help="stream-K ranges in the packed expert GEMM instead of one CTA per (slot, row block) item")
     ap.add_argument("--moe-unpacked", action="store_true",
                     help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
-    ap.add_argument("--ep-exchange", default="nccl", choices=["p2p", "nccl"],
+    ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
                     help="decode expert-parallel exchange for N > 1: peer-memory kernels or NCCL collectives")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")

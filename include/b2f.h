@@ -585,6 +585,23 @@ int b2f_ep_p2p_dispatch(const void* seg, int64_t seg_bytes, const int64_t* peers
  * B2F_ERR_TIMEOUT in *status_out and the device status and returns. */
 int b2f_ep_p2p_wait(const void* region, int64_t flags_off, int kind, int W, const int32_t* ctl,
                     int32_t* status_out, void* stream);
+/* b2f_ep_plan over the segment area of this rank's region (region + seg_off)
+ * that first waits, like b2f_ep_p2p_wait, for the W dispatch flags of the
+ * current exchange (one launch instead of two; a wait that runs out records
+ * B2F_ERR_TIMEOUT in *wait_status). */
+int b2f_ep_p2p_plan(const void* region, int64_t seg_off, int64_t flags_off, int64_t seg_bytes, int64_t row_bytes,
+                    int64_t inds_off, int64_t scores_off, int W, int64_t T, int64_t k, int64_t e_begin,
+                    int64_t e_count, int64_t e_total, int tile, int32_t* x_row, float* wts, int32_t* local,
+                    void* workspace, int64_t workspace_bytes, int32_t* status_out, const int32_t* ctl,
+                    int32_t* wait_status, void* stream);
+/* The owner's completion of the combine once the W combine flags carry the
+ * current exchange's number: h = resid + sum_d mask[m,d] * rows[m*W + d]
+ * (the combine rows at region + comb_off), resid_out = bf16(h), norm_out =
+ * RMSNorm(h) -- b2f_combine_rmsnorm with k = W and the wait folded in. */
+int b2f_ep_p2p_combine_rmsnorm(const void* resid, const void* region, int64_t comb_off, int64_t flags_off,
+                               const float* mask, int64_t M, int W, const void* weight, float eps, int64_t H,
+                               void* resid_out, void* norm_out, const int32_t* ctl, int32_t* wait_status,
+                               void* stream);
 /* Combine: b2f_ep_combine_partial's weighted sums for the W*T gathered tokens,
  * each stored into the owning rank's combine row (token * W + rank) -- only
  * tokens with a local expert -- then this rank's combine flag is raised in

@@ -117,6 +117,9 @@ SIGNATURES = {
     "b2f_ep_p2p_region_bytes": (_I64, [_I64, _I64, _I64, _I64, _P, _P]),
     "b2f_ep_p2p_dispatch": (_I, [_P, _I64, _P, _I64, _I64, _I, _I, _P, _I64, _I64, _I64, _P, _P, _P, _P]),
     "b2f_ep_p2p_wait": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "b2f_ep_p2p_plan": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _I64, _I64, _I64, _I64, _I64, _I, _P, _P,
+                             _P, _P, _I64, _P, _P, _P, _P]),
+    "b2f_ep_p2p_combine_rmsnorm": (_I, [_P, _P, _I64, _I64, _P, _I64, _I, _P, _F, _I64, _P, _P, _P, _P, _P]),
     "b2f_ep_p2p_combine": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _I, _I, _P, _P]),
     "b2f_ep_a2a_row_pitch": (_I64, [_I64, _I64]),
     "b2f_ep_a2a_dispatch": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P]),

@@ -325,7 +325,13 @@ class Qwen3MoeDecoder:
         mma_dense = bits == 4 and gs == 64 and H % 128 == 0 and (Hq * D) % 128 == 0
         dec_dense = mma_dense and B <= 64 and H % 8 == 0
         if dense_engine == "auto":
-            dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
+            # 32-64 tokens: the stream-K decode GEMM (every SM streams the same
+            # weight bytes; measured ahead of tcgen05 split-K at batch 64:
+            # 7244 against 6960 tok/s for the whole step)
+            if dec_dense and B >= 32:
+                dense_engine = "dec"
+            else:
+                dense_engine = "tc" if B >= 32 and s.group_size == 64 else "gemv"
         if dense_engine not in ("tc", "gemv", "mma", "dec"):
             raise ValueError(f"unknown dense engine {dense_engine!r}")
         if dense_engine == "mma" and not mma_dense:
@@ -419,7 +425,9 @@ class Qwen3MoeDecoder:
         """One decode step for all B sequences (graph-capturable).  With
         `pdl` the library kernels are programmatic dependent launches: each is
         scheduled while its predecessor finishes (identical results)."""
-        with _capi.dependent_launches(self.pdl and self.ep is None):
+        # NCCL's kernels take no part in programmatic dependent launch; with
+        # the peer exchange every kernel of the step is this library's
+        with _capi.dependent_launches(self.pdl and (self.ep is None or self.ep.p2p)):
             self._step()
 
     def _step(self):
@@ -465,13 +473,10 @@ class Qwen3MoeDecoder:
             g, u, d = ly["gate"], ly["up"], ly["down"]
             if self.ep is not None:
                 self.ep.route(ly["wr"], ly["rbias"], s.norm_topk)
-                y = self.ep.forward((g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases),
-                                    (d.wq, d.scales, d.biases),
-                                    (ly["gate_packed"], ly["up_packed"], ly["down_packed"]) if self.moe_packed else None)
-                # peer exchange: W rows per token weighted by the ownership mask
-                kc = self.ep.combine_k
-                call("b2f_combine_rmsnorm", ptr(self.h), ptr(y), ptr(self.ep.mask) if kc > 1 else 0, B, kc,
-                     ptr(nxt), s.rms_eps, H, ptr(self.h), ptr(self.xn), st)
+                self.ep.forward((g.wq, g.scales, g.biases), (u.wq, u.scales, u.biases), (d.wq, d.scales, d.biases),
+                                (ly["gate_packed"], ly["up_packed"], ly["down_packed"]) if self.moe_packed else None,
+                                wait_combine=False)
+                self.ep.combine_rmsnorm(self.h, nxt, s.rms_eps, self.h, self.xn)
                 continue
             call("b2f_moe_route_plan", ptr(self.xn), B, H, ptr(ly["wr"]), ptr(ly["rbias"]), E, s.top_k,
                  int(s.norm_topk), ptr(self.gates), ptr(self.inds), ptr(self.scores), self.tile, ptr(self.plan_ws),
@@ -564,5 +569,5 @@ class Qwen3MoeDecoder:
         if self.ep is not None:
             per_layer += 1  # the partial-sum kernel before the reduce-scatter (or the peer combine)
             if self.ep.p2p:
-                per_layer += 3  # peer dispatch and the two waits
+                per_layer += 1  # the peer dispatch
         return 2 + self.L * per_layer + 2

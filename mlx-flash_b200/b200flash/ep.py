@@ -310,8 +310,7 @@ class ExpertParallelMoE:
 
     def dispatch(self):
         if self.p2p:
-            self.dispatch_send()
-            self.dispatch_wait()
+            self.dispatch_send()  # the plan in compute() waits for every rank's dispatch
         elif self.W > 1:
             self.exchange.all_gather(self.recv, self.send)
 
@@ -343,9 +342,16 @@ class ExpertParallelMoE:
         from b2f_mma_repack of the local experts, for the warp-MMA engine with
         16-token tiles: one bulk copy per staged tile, stream-K ranges."""
         seg, st = self.seg, stream_of(self.dev)
-        call("b2f_ep_plan", ptr(self.recv), seg.seg_bytes, seg.row_bytes, seg.inds_off, seg.scores_off, self.W,
-             self.T, self.k, self.e_begin, self.e_count, self.e_total, self.tile, ptr(self.x_row), ptr(self.wts),
-             ptr(self.local), ptr(self.plan_ws), self.plan_bytes, ptr(self.plan_status), st)
+        if self.p2p:
+            # the plan first waits for the W dispatch flags of this exchange
+            call("b2f_ep_p2p_plan", ptr(self.region), self.seg_off, self.flags_off, seg.seg_bytes, seg.row_bytes,
+                 seg.inds_off, seg.scores_off, self.W, self.T, self.k, self.e_begin, self.e_count, self.e_total,
+                 self.tile, ptr(self.x_row), ptr(self.wts), ptr(self.local), ptr(self.plan_ws), self.plan_bytes,
+                 ptr(self.plan_status), ptr(self.ctl), ptr(self.p2p_status), st)
+        else:
+            call("b2f_ep_plan", ptr(self.recv), seg.seg_bytes, seg.row_bytes, seg.inds_off, seg.scores_off, self.W,
+                 self.T, self.k, self.e_begin, self.e_count, self.e_total, self.tile, ptr(self.x_row),
+                 ptr(self.wts), ptr(self.local), ptr(self.plan_ws), self.plan_bytes, ptr(self.plan_status), st)
         gw, gs_, gb = gate
         uw, us, ub = up
         dw, ds, db = down
@@ -396,11 +402,27 @@ class ExpertParallelMoE:
         elif self.W > 1:
             self.exchange.reduce_scatter(self.out, self.part)
 
-    def forward(self, gate, up, down, packed=None) -> torch.Tensor:
+    def forward(self, gate, up, down, packed=None, wait_combine: bool = True) -> torch.Tensor:
+        """``wait_combine=False`` (peer exchange): the caller completes the
+        combine with :meth:`combine_rmsnorm`, which waits for the rows itself."""
         self.dispatch()
         self.compute(gate, up, down, packed)
-        self.combine()
+        if wait_combine or not self.p2p:
+            self.combine()
         return self.out
+
+    def combine_rmsnorm(self, resid, weight, eps, resid_out, norm_out):
+        """Peer exchange: once every rank's combine rows have arrived,
+        ``resid_out = resid + sum_d mask * rows`` and ``norm_out = RMSNorm`` (one
+        launch); the NCCL form: b2f_combine_rmsnorm over the summed output."""
+        st = stream_of(self.dev)
+        if self.p2p:
+            call("b2f_ep_p2p_combine_rmsnorm", ptr(resid), ptr(self.region), self.comb_off, self.flags_off,
+                 ptr(self.mask), self.T, self.W, ptr(weight), eps, self.H, ptr(resid_out), ptr(norm_out),
+                 ptr(self.ctl), ptr(self.p2p_status), st)
+        else:
+            call("b2f_combine_rmsnorm", ptr(resid), ptr(self.out), 0, self.T, 1, ptr(weight), eps, self.H,
+                 ptr(resid_out), ptr(norm_out), st)
 
     def check(self):
         """Synchronising check that every gathered expert id was in range (and,
@@ -417,8 +439,9 @@ class ExpertParallelMoE:
     @property
     def launches_per_block(self) -> int:
         """route, plan, (row gather), gate/up, down, partial; the collectives
-        are NCCL's, or with the peer exchange dispatch + two waits."""
-        return (6 if self.engine == "tc" else 5) + (3 if self.p2p else 0)
+        are NCCL's, or with the peer exchange the dispatch (the plan and the
+        owner's combine + RMSNorm wait for the flags themselves)."""
+        return (6 if self.engine == "tc" else 5) + (1 if self.p2p else 0)
 
 
 def local_expert_slice(w: torch.Tensor, shard: ExpertShard) -> torch.Tensor:

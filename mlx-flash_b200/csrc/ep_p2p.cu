@@ -48,6 +48,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "norm.cuh"
 #include "plan.cuh"
 
 namespace b2f {
@@ -130,6 +131,55 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(const P2PDispatch 
     }
   }
   p2p_arrive_and_signal(p.peers, p.flags_off, 0, p.rank, p.W, p.ctl, true);
+}
+
+// Threads s < W of the block wait (bounded) for flag s to reach the current
+// exchange number ctl[0]; then the whole block passes a barrier.  Called at
+// the start of the kernels that read what the exchange delivered.
+__device__ __forceinline__ void p2p_block_wait(const uint32_t* flags, int W, const int32_t* ctl, int32_t* status) {
+  const int s = threadIdx.x;
+  if (s < W) {
+    const uint32_t seq = uint32_t(*const_cast<const volatile int32_t*>(ctl));
+    if (int32_t(ld_acquire_sys(flags + s) - seq) < 0) {
+      const uint64_t limit = *const_cast<volatile unsigned long long*>(&b2f_tu_wait_ns);
+      const uint64_t t0 = global_ns();
+      uint32_t ns = 32;
+      while (int32_t(ld_acquire_sys(flags + s) - seq) < 0) {
+        if (global_ns() - t0 > limit) {
+          report_timeout(status);
+          break;
+        }
+        __nanosleep(ns);
+        if (ns < 512) ns <<= 1;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// The MoE plan over the W routing segments once the dispatch flags of every
+// rank carry this exchange's number (b2f_ep_plan with the wait folded in).
+__global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(const GatheredExperts src, int A, int E, int tile,
+                                                           char* ws, PlanLayout L, int32_t* status_out,
+                                                           const uint32_t* flags, int W, const int32_t* ctl,
+                                                           int32_t* wait_status) {
+  pdl_wait();
+  p2p_block_wait(flags, W, ctl, wait_status);
+  pdl_trigger();
+  moe_plan_block(src, A, E, tile, ws, L, status_out);
+}
+
+// The owner's completion of the combine once every rank's combine flag
+// carries this exchange's number: h = resid + sum_d mask[m,d] * rows[m*W+d],
+// then RMSNorm (b2f_combine_rmsnorm with k = W and the wait folded in).
+__global__ void __launch_bounds__(256) ep_p2p_combine_rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ resid, const __nv_bfloat16* __restrict__ rows, const float* __restrict__ mask,
+    int W, const __nv_bfloat16* __restrict__ w, float eps, int H, __nv_bfloat16* __restrict__ resid_out,
+    __nv_bfloat16* __restrict__ norm_out, const uint32_t* flags, const int32_t* ctl, int32_t* wait_status) {
+  pdl_wait();
+  p2p_block_wait(flags, W, ctl, wait_status);
+  pdl_trigger();
+  combine_rmsnorm_block(resid, rows, mask, W, w, eps, H, resid_out, norm_out, nullptr, 0, 0);
 }
 
 // One CTA of up to 64 threads: thread s waits for flag s of `kind` to reach
@@ -340,6 +390,68 @@ int b2f_ep_p2p_wait(const void* region, int64_t flags_off, int kind, int W, cons
                           kind * P2P_MAX_W;
   ep_p2p_wait_kernel<<<1, 64, 0, as_stream(stream)>>>(flags, W, ctl, status_out);
   return check_launch();
+}
+
+int b2f_ep_p2p_plan(const void* region, int64_t seg_off, int64_t flags_off, int64_t seg_bytes, int64_t row_bytes,
+                    int64_t inds_off, int64_t scores_off, int W, int64_t T, int64_t k, int64_t e_begin,
+                    int64_t e_count, int64_t e_total, int tile, int32_t* x_row, float* wts, int32_t* local,
+                    void* workspace, int64_t workspace_bytes, int32_t* status_out, const int32_t* ctl,
+                    int32_t* wait_status, void* stream) {
+  if (W <= 0 || W > P2P_MAX_W || T < 0 || k <= 0 || k > 32 || e_count <= 0 || e_begin < 0 ||
+      e_begin + e_count > e_total)
+    return B2F_ERR_INVALID;
+  if (tile < 8 || tile > 256 || tile % 8 != 0) return B2F_ERR_INVALID;
+  if (row_bytes <= 0 || seg_bytes <= 0 || seg_bytes % row_bytes != 0) return B2F_ERR_INVALID;
+  if (inds_off < 0 || scores_off < 0 || inds_off % 4 || scores_off % 4 || flags_off < 0 || flags_off % 4)
+    return B2F_ERR_ALIGN;
+  if (inds_off + 4 * T * k > seg_bytes || scores_off + 4 * T * k > seg_bytes || T * row_bytes > inds_off)
+    return B2F_ERR_INVALID;
+  const int64_t A = int64_t(W) * T * k;
+  if (A > 0x3fffffff || e_count > 65535 || W * (seg_bytes / row_bytes) > 0x7fffffff) return B2F_ERR_UNSUPPORTED;
+  PlanLayout L = plan_layout(A, e_count, tile);
+  if (!workspace || workspace_bytes < L.total) return B2F_ERR_WORKSPACE;
+  if (!region || !ctl || (A > 0 && (!x_row || !wts || !local))) return B2F_ERR_INVALID;
+  const char* recv = static_cast<const char*>(region) + seg_off;
+  if (!aligned(workspace, 16) || !aligned(recv, 16)) return B2F_ERR_ALIGN;
+  GatheredExperts src;
+  src.recv = recv;
+  src.seg_bytes = seg_bytes;
+  src.inds_off = inds_off;
+  src.scores_off = scores_off;
+  src.seg_rows = seg_bytes / row_bytes;
+  src.T = int(T);
+  src.k = int(k);
+  src.e_begin = int(e_begin);
+  src.e_total = int(e_total);
+  src.x_row = x_row;
+  src.wts = wts;
+  src.local = local;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(static_cast<const char*>(region) + flags_off);
+  return launch_kernel(ep_p2p_plan_kernel, dim3{1}, dim3{1024}, 0, as_stream(stream), src, int(A), int(e_count),
+                       tile, static_cast<char*>(workspace), L, status_out, flags, W, ctl, wait_status);
+}
+
+int b2f_ep_p2p_combine_rmsnorm(const void* resid, const void* region, int64_t comb_off, int64_t flags_off,
+                               const float* mask, int64_t M, int W, const void* weight, float eps, int64_t H,
+                               void* resid_out, void* norm_out, const int32_t* ctl, int32_t* wait_status,
+                               void* stream) {
+  if (M < 0 || H <= 0 || W <= 0 || W > P2P_MAX_W) return B2F_ERR_INVALID;
+  if (H % 8 != 0 || H > CMB_CHUNKS * 8 * 256) return B2F_ERR_UNSUPPORTED;
+  if (M == 0) return B2F_OK;
+  if (!resid || !region || !mask || !weight || !norm_out || !ctl) return B2F_ERR_INVALID;
+  const char* rows = static_cast<const char*>(region) + comb_off;
+  if (comb_off % 16 != 0 || flags_off < 0 || flags_off % 4 != 0 || !aligned(resid, 16) || !aligned(rows, 16) ||
+      !aligned(weight, 16) || !aligned(norm_out, 16) || (resid_out && !aligned(resid_out, 16)))
+    return B2F_ERR_ALIGN;
+  const int threads = int(H / 8) < 256 ? int(((H / 8) + 31) / 32 * 32) : 256;
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(static_cast<const char*>(region) + flags_off) +
+                          P2P_MAX_W;  // the combine flags
+  return launch_kernel(ep_p2p_combine_rmsnorm_kernel, dim3{unsigned(M)}, dim3{unsigned(threads < 64 ? 64 : threads)},
+                       0, as_stream(stream), static_cast<const __nv_bfloat16*>(resid),
+                       reinterpret_cast<const __nv_bfloat16*>(rows), mask, W,
+                       static_cast<const __nv_bfloat16*>(weight), eps, int(H),
+                       static_cast<__nv_bfloat16*>(resid_out), static_cast<__nv_bfloat16*>(norm_out), flags, ctl,
+                       wait_status);
 }
 
 int b2f_ep_p2p_combine(const void* y, int64_t ldy, const float* wts, const int32_t* local, int64_t T, int64_t k,

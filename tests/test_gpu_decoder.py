@@ -53,7 +53,8 @@ def _export_cache(dec, ctx):
                                                          (8, "tc_gather", "tc", 1024), (4, "gemv", "tc", 1024),
                                                          (2, "tc_gather", "gemv", 256), (8, "mma", "gemv", 256),
                                                          (4, "mma", "tc", 1024), (8, "mma", "mma", 256),
-                                                         (4, "mma", "mma", 1024)])
+                                                         (4, "mma", "mma", 1024), (8, "mma", "dec", 256),
+                                                         (4, "gemv", "dec", 1024)])
 def test_decode_step_matches_oracle(dev, kv_bits, engine, dense, hidden):
     """dense="tc" runs q/k/v and o through split-K partials summed inside the
     RoPE/KV-append and residual+RMSNorm kernels (K = 1024 splits both)."""
@@ -131,14 +132,14 @@ def test_decode_step_cuda_graph_replay(dev):
     assert torch.equal(dec_a.logits, dec_b.logits)
 
 
-@pytest.mark.parametrize("dense", ["tc", "mma"])
+@pytest.mark.parametrize("dense", ["dec", "tc", "mma"])
 def test_decode_step_bench_shape_matches_oracle(dev, dense):
     """The benchmark's decoder configuration with 2 of its 48 layers: hidden
     2048, 32 query / 4 KV heads of 128, 128 experts top-8 (I 768) with the
     Zipf(1.1) router, 151936-token vocabulary, batch 64, 64-token pages,
-    8-bit KV, warp-MMA experts over packed tiles and either dense engine
-    (tcgen05 split-K, or warp MMA over 64-token tiles split along K): one step
-    vs the oracle."""
+    8-bit KV, warp-MMA experts over packed tiles and each dense engine (the
+    stream-K decode GEMM the bench uses, tcgen05 split-K, warp MMA split
+    along K): one step vs the oracle."""
     shape = Qwen3MoeShape(layers=2)
     B, ctx = 64, 256
     dec = Qwen3MoeDecoder(shape, max_batch=B, max_context=ctx + 8, page_size=64, device=dev, seed=1234,
@@ -216,7 +217,8 @@ def test_decode_step_packed_experts_equal_unpacked(dev):
 
 
 @pytest.mark.parametrize("engine,dense,batch", [("mma", "tc", 64), ("mma", "gemv", 8), ("mma", "mma", 24),
-                                                ("tc_gather", "tc", 48), ("gemv", "gemv", 3), ("tc", "tc", 40)])
+                                                ("tc_gather", "tc", 48), ("gemv", "gemv", 3), ("tc", "tc", 40),
+                                                ("mma", "dec", 64), ("mma", "dec", 37)])
 def test_decode_step_dependent_launches_bit_identical(dev, engine, dense, batch):
     """Programmatic dependent launches (each kernel scheduled while its
     predecessor finishes, waiting for it before touching memory) give

@@ -133,8 +133,14 @@ def test_p2p_combine_rmsnorm_consumes_rows(dev):
     xn = torch.empty_like(resid)
     call("b2f_combine_rmsnorm", ptr(resid), ptr(m.out), ptr(m.mask), T, W, ptr(nw), 1e-6, H, ptr(h_out), ptr(xn),
          _capi.stream_of(dev))
+    # the decoder's form: the owner's combine + RMSNorm with the combine wait
+    # folded in gives the same bits
+    h2, xn2 = torch.empty_like(resid), torch.empty_like(resid)
+    m.combine_rmsnorm(resid, nw, 1e-6, h2, xn2)
     torch.cuda.synchronize()
     m.check()
+    assert torch.equal(h2.view(torch.int16), h_out.view(torch.int16))
+    assert torch.equal(xn2.view(torch.int16), xn.view(torch.int16))
     h = resid.float() + (m.out.float().view(T, W, H) * m.mask[:, :, None]).sum(1)
     hb = h.to(torch.bfloat16).float()
     want = nw.float() * hb * torch.rsqrt((hb * hb).mean(-1, keepdim=True) + 1e-6)
@@ -169,6 +175,12 @@ def test_p2p_wait_times_out_without_flags(dev):
         assert _capi.device_status(clear=True) == _capi.B2F_ERR_TIMEOUT
         with pytest.raises(TimeoutError):
             ranks[0].check()
+        # the plan's own wait (the form the decoder uses) gives up the same way
+        ranks[0].p2p_status.zero_()
+        ranks[0].compute(*[tuple(local_expert_slice(t, shards[0]) for t in w) for w in (gd, ud, dd)])
+        torch.cuda.synchronize()
+        assert int(ranks[0].p2p_status.item()) == _capi.B2F_ERR_TIMEOUT
+        assert _capi.device_status(clear=True) == _capi.B2F_ERR_TIMEOUT
     finally:
         call("b2f_set_wait_limit_ns", 0)
     # rank 1 catches up; both ranks' second waits find every flag raised
