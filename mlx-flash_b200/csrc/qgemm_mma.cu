@@ -118,6 +118,17 @@ __device__ __forceinline__ void mma_bf16_16816_zero(float (&d)[4], const uint32_
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(0.f));
 }
 
+// (d0, d1) = (a0*b0 + c0, a1*b1 + c1), one packed fp32x2 FMA (two round-to-nearest FMAs)
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                      float c1) {
+  unsigned long long a, b, c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+
 __device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 // half `hi` of a pair of bf16 (or fp16) scale / bias values as fp32
@@ -362,10 +373,13 @@ __device__ __forceinline__ int mma_consume(const MmaParams& p, uint8_t* smem, in
           const float c1 = fmaf(-128.f, s1, sc_half<SF16>(br[m][i][1], grp));
 #pragma unroll
           for (int nt = 0; nt < NTA; ++nt) {
-            acc[m][i][nt][0] = fmaf(s0, t[m][i][nt][0], fmaf(c0, xs[nt][0], acc[m][i][nt][0]));
-            acc[m][i][nt][1] = fmaf(s0, t[m][i][nt][1], fmaf(c0, xs[nt][1], acc[m][i][nt][1]));
-            acc[m][i][nt][2] = fmaf(s1, t[m][i][nt][2], fmaf(c1, xs[nt][0], acc[m][i][nt][2]));
-            acc[m][i][nt][3] = fmaf(s1, t[m][i][nt][3], fmaf(c1, xs[nt][1], acc[m][i][nt][3]));
+            // (rows R, R+8) x (tokens 2c, 2c+1) as two packed pairs: the same
+            // round-to-nearest FMAs as one scalar FMA per element
+            float* a = acc[m][i][nt];
+            ffma2(a[0], a[1], c0, c0, xs[nt][0], xs[nt][1], a[0], a[1]);
+            ffma2(a[0], a[1], s0, s0, t[m][i][nt][0], t[m][i][nt][1], a[0], a[1]);
+            ffma2(a[2], a[3], c1, c1, xs[nt][0], xs[nt][1], a[2], a[3]);
+            ffma2(a[2], a[3], s1, s1, t[m][i][nt][2], t[m][i][nt][3], a[2], a[3]);
           }
         }
     }
