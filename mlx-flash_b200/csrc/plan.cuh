@@ -12,9 +12,14 @@
 //   counts  int32[E]    assignments per expert
 //   offsets int32[E+1]  exclusive scan of counts
 //   cursor  int32[E]    scatter cursors
-//   soff    int32[E+1]  first slot of each expert
+//   soff    int32[E+1]  slots of the experts before each expert (exclusive scan)
 //   sorted  int32[A]    assignment ids grouped by expert
-//   slots   int4[S]     {expert, begin in sorted, count <= tile, 0}
+//   slots   int4[S]     {expert, begin in sorted, count <= tile, 0}: the slots
+//                       holding more than tile/2 assignments first, then the
+//                       rest, each part in expert order (E <= 1024; else all
+//                       in expert order) -- grids launched over the slots then
+//                       start their longest CTAs first, so the last wave holds
+//                       short ones
 #pragma once
 #include "common.cuh"
 
@@ -169,6 +174,8 @@ __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int
   __shared__ int total;
   __shared__ int bad;
   __shared__ int s_counts[PLAN_SMEM_E], s_cursor[PLAN_SMEM_E], s_offsets[PLAN_SMEM_E + 1], s_soff[PLAN_SMEM_E + 1];
+  __shared__ int s_hoff[PLAN_SMEM_E];  // first heavy slot of each expert
+  __shared__ int heavy_total;
   const bool sm = E <= PLAN_SMEM_E;
   int32_t* counts = sm ? s_counts : g_counts;
   int32_t* cursor = sm ? s_cursor : g_cursor;
@@ -187,25 +194,35 @@ __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int
     if (e >= 0 && e < E) atomicAdd(&counts[e], 1);
   }
   __syncthreads();
-  // exclusive scans over experts (chunks of blockDim.x)
-  int run = 0, srun = 0;
+  // exclusive scans over experts (chunks of blockDim.x): assignments, slots,
+  // heavy slots (more than tile/2 assignments: every full slot and a last
+  // slot past half a tile)
+  int run = 0, srun = 0, hrun = 0;
   for (int base = 0; base < E; base += blockDim.x) {
     const int e = base + threadIdx.x;
     const int cnt = e < E ? counts[e] : 0;
     const int ns = (cnt + tile - 1) / tile;
+    const int nfull = cnt / tile;
+    const int nh = nfull + (cnt - nfull * tile > tile / 2 ? 1 : 0);
     const int ex = block_exclusive_scan(cnt, warp_tot, &total);
     const int t1 = total;
     __syncthreads();
     const int sx = block_exclusive_scan(ns, warp_tot, &total);
     const int t2 = total;
+    __syncthreads();
+    const int hx = block_exclusive_scan(nh, warp_tot, &total);
+    const int t3 = total;
     if (e < E) {
       offsets[e] = run + ex;
       soff[e] = srun + sx;
+      if (sm) s_hoff[e] = hrun + hx;
     }
     run += t1;
     srun += t2;
+    hrun += t3;
     __syncthreads();
   }
+  if (threadIdx.x == 0) heavy_total = hrun;
   if (threadIdx.x == 0) {
     offsets[E] = run;
     soff[E] = srun;
@@ -223,8 +240,15 @@ __device__ __forceinline__ void moe_plan_block(const Src& src, int A, int E, int
   }
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int cnt = counts[e];
-    for (int j = 0, s = soff[e]; j * tile < cnt; ++j, ++s)
-      slots[s] = make_int4(e, offsets[e] + j * tile, min(tile, cnt - j * tile), 0);
+    for (int j = 0; j * tile < cnt; ++j) {
+      const int c = min(tile, cnt - j * tile);
+      // heavy slots of expert e are its first ones (j < its heavy count); its
+      // light slot (at most one, the last) follows all heavy slots, after
+      // the light slots of the experts before it (soff[e] - s_hoff[e])
+      int s = soff[e] + j;
+      if (sm) s = c > tile / 2 ? s_hoff[e] + j : heavy_total + soff[e] - s_hoff[e];
+      slots[s] = make_int4(e, offsets[e] + j * tile, c, 0);
+    }
   }
   if (sm) {  // the per-expert arrays of the workspace layout, for readers of the plan
     for (int e = threadIdx.x; e <= E; e += blockDim.x) {

@@ -309,8 +309,9 @@ def test_packed_streamk_ranges(dev, E, N, K, T, k):
     streams an equal range of (item, K chunk) units; an item cut between two
     CTAs is summed by the second to finish).  The first two shapes have more
     live items than resident CTAs, so items are cut.  Outputs equal the
-    whole-item grid up to the fp32 re-association of the cut items' sums (at
-    most one bf16 rounding step), are bit-identical from launch to launch,
+    whole-item grid up to the fp32 re-association of the cut items' sums (one
+    bf16 rounding step, or 2^-16 of the output rms where a sum cancels to
+    about zero), are bit-identical from launch to launch,
     and the arrival counters are zero again after every launch."""
     from b200flash import _capi
     from b200flash._capi import call, ptr
@@ -366,5 +367,9 @@ def test_packed_streamk_ranges(dev, E, N, K, T, k):
     assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
     for got, want, what in ((h1, h0, "gate/up"), (y1, y0, "down")):
         g, w = got.float(), want.float()
-        assert torch.all((g - w).abs() <= w.abs() * 2.0 ** -7 + 1e-6), what
+        # one bf16 step, plus the re-association error of a cut item's fp32
+        # sum, which is absolute (a few fp32 ulps of partial sums of the
+        # output's rms size) and so dominates where the sum cancels to ~0
+        floor = float(w.pow(2).mean().sqrt()) * 2.0 ** -16
+        assert torch.all((g - w).abs() <= w.abs() * 2.0 ** -7 + floor), what
         assert float((got.view(torch.int16) == want.view(torch.int16)).float().mean()) > 0.98, what

@@ -64,6 +64,60 @@ def test_gather_qmm_skewed_routing_and_empty_experts(dev):
     assert_close(to_np(out), want, what="skewed gather_qmm")
 
 
+def _plan_arrays(plan):
+    """hdr, sorted and slots of a plan workspace, at the offsets of the
+    documented layout (hdr 64 B, counts, offsets, cursor, soff, sorted,
+    slots; each array 16-byte aligned)."""
+    A, E = plan.A, plan.E
+    up = lambda v, a: (v + a - 1) // a * a  # noqa: E731
+    o = 64
+    o = up(o + 4 * E, 16)
+    o = up(o + 4 * (E + 1), 16)
+    o = up(o + 4 * E, 16)
+    o = up(o + 4 * (E + 1), 16)
+    off_sorted = o
+    off_slots = up(o + 4 * max(A, 1), 16)
+    ws = plan.workspace.cpu().numpy()
+    hdr = ws[:64].view(np.int32)
+    S = int(hdr[0])
+    return hdr, ws[off_sorted:off_sorted + 4 * A].view(np.int32), ws[off_slots:off_slots + 16 * S].view(np.int32).reshape(S, 4)
+
+
+@pytest.mark.parametrize("A,E,tile,skew", [(512, 128, 16, 1.1), (512, 128, 32, 1.1), (4096, 64, 16, 0.5),
+                                           (300, 1500, 16, 1.1), (0, 8, 16, 0.0), (7, 1, 16, 0.0)])
+def test_moe_plan_slot_order(dev, A, E, tile, skew):
+    """The plan's slots: every assignment in exactly one slot of its expert;
+    slots holding more than tile/2 assignments come first, then the rest,
+    each part in expert order, so grids over the slots start their longest
+    CTAs first.  E > 1024 keeps plain expert order (global-memory counters)."""
+    rng = np.random.default_rng(A + E + tile)
+    p = np.arange(1, E + 1, dtype=np.float64) ** -skew
+    ids = rng.choice(E, size=A, p=p / p.sum()).astype(np.int32)
+    plan = mx_compat.MoEPlan(torch.from_numpy(ids).to(dev), E, tile)
+    plan.check()
+    hdr, srt, slots = _plan_arrays(plan)
+    cnt = np.bincount(ids, minlength=E)
+    assert hdr[0] == int(((cnt + tile - 1) // tile).sum())
+    assert np.array_equal(np.sort(srt), np.arange(A))
+    seen = np.zeros(A, np.int64)
+    for e, begin, c, _ in slots:
+        assert 1 <= c <= tile
+        assert np.all(ids[srt[begin:begin + c]] == e)
+        seen[begin:begin + c] += 1
+    assert np.all(seen == 1)
+    heavy = slots[:, 2] > tile // 2
+    key = np.stack([slots[:, 0], slots[:, 1]], 1)
+    if E <= 1024:
+        nh = int(heavy.sum())
+        assert heavy[:nh].all() and not heavy[nh:].any()
+        parts = (key[:nh], key[nh:])
+    else:
+        parts = (key,)
+    for part in parts:  # expert order, chunks of one expert in sorted order
+        order = np.lexsort((part[:, 1], part[:, 0]))
+        assert np.array_equal(order, np.arange(len(part)))
+
+
 def test_moe_plan_rejects_out_of_range_expert(dev):
     plan = mx_compat.MoEPlan(torch.tensor([0, 1, 9], dtype=torch.int32, device=dev), 4, 16)
     with pytest.raises(IndexError):
