@@ -40,6 +40,11 @@ struct AttnParams {
   int slot_bytes;  // ring path: bytes of one ring slot
 };
 
+// Named barrier `id` over the first `n` threads of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 constexpr int ATTN_RING = 4;  // pages in flight per CTA on the ring path
 
 // Byte offset of `byte` of K/V code row `row` inside a TMA tile of rows of
@@ -547,8 +552,10 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
 //                  sum(P'); O = acc - (1024+127)*sum(P') at the end.
 // Inside each 8-token half, MMA row i is page row sigma(i) (sigma = 0 6 1 7
 // 4 2 5 3): with the 128B swizzle of the page tiles that makes every K and V
-// fragment read of a warp hit 32 distinct banks.  The page ring, the
-// 4-warp merge and the split partials are those of the kernel above.
+// fragment read of a warp hit 32 distinct banks.  The page ring and the
+// split partials are those of the kernel above; the producer warp leaves once
+// its copies have landed, and the 4 compute warps merge through shared memory
+// behind a named barrier of their own.
 // ex2.approx.ftz: 2^x (-inf gives +0), the softmax exponential in base 2
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -570,15 +577,9 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
   constexpr float KOFF = 1024.f + 127.f;
   constexpr uint32_t SIGMA = 0x35247160u;  // nibble i = page row of MMA row i (mod 8)
 
-  const int split = blockIdx.x, hkv = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int G = p.G;
-  const int len = p.seq_lens[b];
-  const int n_sub = (len + 15) / 16;
-  const int per_split = (n_sub + p.n_splits - 1) / p.n_splits;
-  const int sub_begin = split * per_split;
-  const int sub_end = min(n_sub, sub_begin + per_split);
 
   const int sg = (SIGMA >> (4 * g)) & 7;       // page row of MMA rows g (and 8+sg of g+8)
   const int sv0 = (SIGMA >> (8 * c)) & 7;      // page row of token 2c (B side of P.V)
@@ -595,63 +596,13 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
     vcol1[grp] = sv1 * RB + ((ch ^ sv1) << 4) + 8 * (g & 1);
   }
 
-  // ---- q^T fragments (head g, dims 64grp+16c+[0,16)) and (1024+127)*sum(q)
-  uint32_t qb[DG * 4][2];
-  float kq[2][DG];  // heads 2c, 2c+1
-  {
-    const bool hv = g < G;
-    const __nv_bfloat16* qrow = p.q + (int64_t(b) * p.Hq + int64_t(hkv) * G + g) * D;
-#pragma unroll
-    for (int grp = 0; grp < DG; ++grp) {
-      float v[16];
-      if (hv) {
-        const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * grp + 16 * c);
-        const uint4 a = src[0], bb = src[1];
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-          v[2 * i] = round_f16(__low2float(h) * p.qscale);
-          v[2 * i + 1] = round_f16(__high2float(h) * p.qscale);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.f;
-      }
-      float part = 0.f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) part += v[i];
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-#pragma unroll
-      for (int st = 0; st < 4; ++st) {
-        qb[grp * 4 + st][0] = pack_f16x2(v[4 * st], v[4 * st + 1]);
-        qb[grp * 4 + st][1] = pack_f16x2(v[4 * st + 2], v[4 * st + 3]);
-      }
-      kq[0][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c);
-      kq[1][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c + 4);
-    }
-  }
-
-  float oacc[DG * 4][4];
-  float oone[DG][4];
-#pragma unroll
-  for (int j = 0; j < DG * 4; ++j)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) oacc[j][i] = 0.f;
-#pragma unroll
-  for (int j = 0; j < DG; ++j)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) oone[j][i] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_run[2] = {0.f, 0.f};  // this lane's rows only; summed over the 8 row lanes at the end
-  const uint32_t ONE2 = 0x3C003C00u;
-  const uint32_t ones[4] = {ONE2, ONE2, ONE2, ONE2};
-
   extern __shared__ __align__(1024) uint8_t attn_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(attn_smem + p.ring_bytes - 128);
   uint64_t* empty = full + ATTN_RING;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + ATTN_RING);
+  float* sm = reinterpret_cast<float*>(attn_smem + p.ring_bytes);
+  float* sm_o = sm;               // [4][G][D]
+  float* sm_ml = sm + 4 * G * D;  // [4][G][2]
   if (threadIdx.x == 0) {
     for (int i = 0; i < ATTN_RING; ++i) {
       mbar_init(&full[i], 1);
@@ -661,22 +612,29 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
     fence_mbarrier_init();
   }
   __syncthreads();
+  // the CTA's pages: pair (blockIdx.z, blockIdx.y), context split blockIdx.x
+  const int b = blockIdx.z, hkv = blockIdx.y;
+  const int len = p.seq_lens[b];
+  const int n_sub = (len + 15) / 16;
+  const int per_split = (n_sub + p.n_splits - 1) / p.n_splits;
+  const int sub_begin = int(blockIdx.x) * per_split;
+  const int sub_end = min(n_sub, sub_begin + per_split);
+
   const int spp = p.PS / 16;
   const int pg0 = sub_begin / spp;
   const int npg = sub_end > sub_begin ? (sub_end + spp - 1) / spp - pg0 : 0;
   const int code_bytes = p.PS * RB, sc_bytes = p.PS * DG * 4;
   if (warp == 4) {
     if (lane == 0 && !producers_stalled()) {  // test control: stalled producers issue nothing
-      int jj = 0;
-      for (; jj < npg; ++jj) {
-        const int slot = jj % ATTN_RING;
-        if (jj >= ATTN_RING &&
-            !mbar_wait_bounded_backoff(&empty[slot], uint32_t(((jj / ATTN_RING) - 1) & 1))) {
+      int it = 0;  // pages issued (ring position)
+      for (; it < npg; ++it) {
+        const int slot = it % ATTN_RING;
+        if (it >= ATTN_RING && !mbar_wait_bounded_backoff(&empty[slot], uint32_t(((it / ATTN_RING) - 1) & 1))) {
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
-        const int page = p.block_table[int64_t(b) * p.max_pages + pg0 + jj];
+        const int page = p.block_table[int64_t(b) * p.max_pages + pg0 + it];
         const int64_t rowbase = (int64_t(page) * p.Hkv + hkv) * p.PS;
         uint8_t* sb = attn_smem + slot * p.slot_bytes;
         mbar_arrive_expect_tx(&full[slot], uint32_t(2 * code_bytes + 2 * sc_bytes));
@@ -686,14 +644,70 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
         bulk_g2s(sb + 2 * code_bytes + sc_bytes, p.vs + rowbase * DG, uint32_t(sc_bytes), &full[slot]);
       }
       // copies already issued land before the CTA goes away
-      for (int k = 1; k <= ATTN_RING && jj - k >= 0; ++k)
-        mbar_wait_bounded(&full[(jj - k) % ATTN_RING], uint32_t(((jj - k) / ATTN_RING) & 1), 100000000ull);
+      for (int k = 1; k <= ATTN_RING && it - k >= 0; ++k)
+        mbar_wait_bounded(&full[(it - k) % ATTN_RING], uint32_t(((it - k) / ATTN_RING) & 1), 100000000ull);
     }
     __syncwarp();
-  } else {
-    for (int jj = 0; jj < npg; ++jj) {
-      const int slot = jj % ATTN_RING;
-      const bool ok = !*abort_flag && mbar_wait_bounded(&full[slot], uint32_t((jj / ATTN_RING) & 1));
+    return;
+  }
+
+  // ---- consumer warps 0..3 ---------------------------------------------------
+  const uint32_t ONE2 = 0x3C003C00u;
+  const uint32_t ones[4] = {ONE2, ONE2, ONE2, ONE2};
+  {
+    uint32_t qb[DG * 4][2];
+    float kq[2][DG];  // heads 2c, 2c+1
+    // ---- q^T fragments (head g, dims 64grp+16c+[0,16)) and (1024+127)*sum(q)
+    {
+      const bool hv = g < G;
+      const __nv_bfloat16* qrow = p.q + (int64_t(b) * p.Hq + int64_t(hkv) * G + g) * D;
+#pragma unroll
+      for (int grp = 0; grp < DG; ++grp) {
+        float v[16];
+        if (hv) {
+          const uint4* src = reinterpret_cast<const uint4*>(qrow + 64 * grp + 16 * c);
+          const uint4 a = src[0], bb = src[1];
+          const uint32_t w[8] = {a.x, a.y, a.z, a.w, bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+            v[2 * i] = round_f16(__low2float(h) * p.qscale);
+            v[2 * i + 1] = round_f16(__high2float(h) * p.qscale);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = 0.f;
+        }
+        float part = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) part += v[i];
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+#pragma unroll
+        for (int st = 0; st < 4; ++st) {
+          qb[grp * 4 + st][0] = pack_f16x2(v[4 * st], v[4 * st + 1]);
+          qb[grp * 4 + st][1] = pack_f16x2(v[4 * st + 2], v[4 * st + 3]);
+        }
+        kq[0][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c);
+        kq[1][grp] = KOFF * __shfl_sync(0xffffffffu, part, 8 * c + 4);
+      }
+    }
+
+    float oacc[DG * 4][4];
+    float oone[DG][4];
+#pragma unroll
+    for (int j = 0; j < DG * 4; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) oacc[j][i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < DG; ++j)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) oone[j][i] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_run[2] = {0.f, 0.f};  // this lane's rows only; summed over the 8 row lanes at the end
+    for (int it = 0; it < npg; ++it) {
+      const int slot = it % ATTN_RING;
+      const bool ok = !*abort_flag && mbar_wait_bounded(&full[slot], uint32_t((it / ATTN_RING) & 1));
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) *abort_flag = 1;
         break;
@@ -702,143 +716,138 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
       const uint8_t* vb = kb + code_bytes;
       const float* ksb = reinterpret_cast<const float*>(kb + 2 * code_bytes);
       const float* vsb = ksb + p.PS * DG;
-      const int s_lo = max(sub_begin, (pg0 + jj) * spp), s_hi = min(sub_end, (pg0 + jj + 1) * spp);
+      const int s_lo = max(sub_begin, (pg0 + it) * spp), s_hi = min(sub_end, (pg0 + it + 1) * spp);
       const int nstep = (s_hi - s_lo + NT - 1) / NT;
       for (int k = 0; k < nstep; ++k) {
-        if (((jj * (spp / NT) + k) & 3) != warp) continue;
+        if (((it * (spp / NT) + k) & 3) != warp) continue;
         const int sub0 = s_lo + NT * k;
-        uint4 kw[NT][2][DG];
-        uint2 vw[NT][4][DG];  // tokens 2c, 2c+1, 2c+8, 2c+9
-        bool valid[NT][2];
-        float ksc[NT][2][DG], vsc[NT][2][DG];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const bool here = sub0 + t < s_hi;  // warp-uniform
-          const int t0 = (sub0 + t) * 16;
-          const int lr = here ? t0 % p.PS : 0;  // first page row of the tile (a multiple of 16)
-          const uint8_t* kt = kb + lr * RB;
-          const uint8_t* vt = vb + lr * RB;
-#pragma unroll
-          for (int grp = 0; grp < DG; ++grp) {
-            kw[t][0][grp] = *reinterpret_cast<const uint4*>(kt + kcol[grp]);
-            kw[t][1][grp] = *reinterpret_cast<const uint4*>(kt + 8 * RB + kcol[grp]);
-            vw[t][0][grp] = *reinterpret_cast<const uint2*>(vt + vcol0[grp]);
-            vw[t][1][grp] = *reinterpret_cast<const uint2*>(vt + vcol1[grp]);
-            vw[t][2][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol0[grp]);
-            vw[t][3][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol1[grp]);
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = lr + 8 * h + sg;
-            valid[t][h] = here && t0 + 8 * h + sg < len;
-            const float2 kk = *reinterpret_cast<const float2*>(ksb + row * DG);
-            const float2 vv = *reinterpret_cast<const float2*>(vsb + row * DG);
-            ksc[t][h][0] = kk.x;
-            ksc[t][h][1] = kk.y;
-            vsc[t][h][0] = valid[t][h] ? vv.x : 0.f;
-            vsc[t][h][1] = valid[t][h] ? vv.y : 0.f;
-          }
-        }
+            uint4 kw[NT][2][DG];
+            uint2 vw[NT][4][DG];  // tokens 2c, 2c+1, 2c+8, 2c+9
+            bool valid[NT][2];
+            float ksc[NT][2][DG], vsc[NT][2][DG];
+    #pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              const bool here = sub0 + t < s_hi;  // warp-uniform
+              const int t0 = (sub0 + t) * 16;
+              const int lr = here ? t0 % p.PS : 0;  // first page row of the tile (a multiple of 16)
+              const uint8_t* kt = kb + lr * RB;
+              const uint8_t* vt = vb + lr * RB;
+    #pragma unroll
+              for (int grp = 0; grp < DG; ++grp) {
+                kw[t][0][grp] = *reinterpret_cast<const uint4*>(kt + kcol[grp]);
+                kw[t][1][grp] = *reinterpret_cast<const uint4*>(kt + 8 * RB + kcol[grp]);
+                vw[t][0][grp] = *reinterpret_cast<const uint2*>(vt + vcol0[grp]);
+                vw[t][1][grp] = *reinterpret_cast<const uint2*>(vt + vcol1[grp]);
+                vw[t][2][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol0[grp]);
+                vw[t][3][grp] = *reinterpret_cast<const uint2*>(vt + 8 * RB + vcol1[grp]);
+              }
+    #pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int row = lr + 8 * h + sg;
+                valid[t][h] = here && t0 + 8 * h + sg < len;
+                const float2 kk = *reinterpret_cast<const float2*>(ksb + row * DG);
+                const float2 vv = *reinterpret_cast<const float2*>(vsb + row * DG);
+                ksc[t][h][0] = kk.x;
+                ksc[t][h][1] = kk.y;
+                vsc[t][h][0] = valid[t][h] ? vv.x : 0.f;
+                vsc[t][h][1] = valid[t][h] ? vv.y : 0.f;
+              }
+            }
 
-        // ---- S^T = K.Q^T ---------------------------------------------------
-        float s[NT][4];
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          float sacc[DG][4];
-#pragma unroll
-          for (int grp = 0; grp < DG; ++grp) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) sacc[grp][i] = 0.f;
-            const uint32_t k0[4] = {kw[t][0][grp].x, kw[t][0][grp].y, kw[t][0][grp].z, kw[t][0][grp].w};
-            const uint32_t k1[4] = {kw[t][1][grp].x, kw[t][1][grp].y, kw[t][1][grp].z, kw[t][1][grp].w};
-#pragma unroll
-            for (int st = 0; st < 4; ++st) {
-              const uint32_t a[4] = {prmt(k0[st], 0x64646464u, 0x4140u), prmt(k1[st], 0x64646464u, 0x4140u),
-                                     prmt(k0[st], 0x64646464u, 0x4342u), prmt(k1[st], 0x64646464u, 0x4342u)};
-              mma_f16_16816(sacc[grp], a, qb[grp * 4 + st]);
+            // ---- S^T = K.Q^T ---------------------------------------------------
+            float s[NT][4];
+    #pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              float sacc[DG][4];
+    #pragma unroll
+              for (int grp = 0; grp < DG; ++grp) {
+    #pragma unroll
+                for (int i = 0; i < 4; ++i) sacc[grp][i] = 0.f;
+                const uint32_t k0[4] = {kw[t][0][grp].x, kw[t][0][grp].y, kw[t][0][grp].z, kw[t][0][grp].w};
+                const uint32_t k1[4] = {kw[t][1][grp].x, kw[t][1][grp].y, kw[t][1][grp].z, kw[t][1][grp].w};
+    #pragma unroll
+                for (int st = 0; st < 4; ++st) {
+                  const uint32_t a[4] = {prmt(k0[st], 0x64646464u, 0x4140u), prmt(k1[st], 0x64646464u, 0x4140u),
+                                         prmt(k0[st], 0x64646464u, 0x4342u), prmt(k1[st], 0x64646464u, 0x4342u)};
+                  mma_f16_16816(sacc[grp], a, qb[grp * 4 + st]);
+                }
+              }
+    #pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int h = i >> 1, e = i & 1;
+                float v = 0.f;
+    #pragma unroll
+                for (int grp = 0; grp < DG; ++grp) v += ksc[t][h][grp] * (sacc[grp][i] - kq[e][grp]);
+                s[t][i] = valid[t][h] ? v : -INFINITY;
+              }
+            }
+
+            // ---- online softmax (heads 2c, 2c+1 over the 8 lanes of a column) --
+            float pr[NT][4];
+    #pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float mt = fmaxf(s[0][e], s[0][2 + e]);
+    #pragma unroll
+              for (int t = 1; t < NT; ++t) mt = fmaxf(mt, fmaxf(s[t][e], s[t][2 + e]));
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+              mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+              const float mnew = fmaxf(m_run[e], mt);
+              const bool none = (mnew == -INFINITY);
+              const float alpha = none ? 1.f : fast_exp2(m_run[e] - mnew);
+              float lsum = 0.f;
+    #pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                pr[t][e] = none ? 0.f : fast_exp2(s[t][e] - mnew);
+                pr[t][2 + e] = none ? 0.f : fast_exp2(s[t][2 + e] - mnew);
+                lsum += pr[t][e] + pr[t][2 + e];
+              }
+              l_run[e] = l_run[e] * alpha + lsum;
+              m_run[e] = mnew;
+    #pragma unroll
+              for (int j = 0; j < DG * 4; ++j) {
+                oacc[j][e] *= alpha;
+                oacc[j][2 + e] *= alpha;
+              }
+    #pragma unroll
+              for (int j = 0; j < DG; ++j) {
+                oone[j][e] *= alpha;
+                oone[j][2 + e] *= alpha;
+              }
+            }
+
+            // ---- O^T += V^T.P'^T ------------------------------------------------
+    #pragma unroll
+            for (int t = 0; t < NT; ++t) {
+    #pragma unroll
+              for (int grp = 0; grp < DG; ++grp) {
+                const uint32_t xlo = pack_f16x2(pr[t][0] * vsc[t][0][grp], pr[t][1] * vsc[t][0][grp]);
+                const uint32_t xhi = pack_f16x2(pr[t][2] * vsc[t][1][grp], pr[t][3] * vsc[t][1][grp]);
+                const uint32_t bp[2] = {movmatrix_trans(xlo), movmatrix_trans(xhi)};
+                mma_f16_16816(oone[grp], ones, bp);
+    #pragma unroll
+                for (int jl = 0; jl < 4; ++jl) {
+                  const int bs = 2 * (jl & 1);
+                  const uint32_t sel_lo = uint32_t(bs | (bs << 4) | ((4 + bs) << 8) | ((4 + bs) << 12));
+                  const uint32_t sel_hi = sel_lo + 0x1111u;
+                  const uint32_t w0 = (jl >> 1) ? vw[t][0][grp].y : vw[t][0][grp].x;
+                  const uint32_t w1 = (jl >> 1) ? vw[t][1][grp].y : vw[t][1][grp].x;
+                  const uint32_t w2 = (jl >> 1) ? vw[t][2][grp].y : vw[t][2][grp].x;
+                  const uint32_t w3 = (jl >> 1) ? vw[t][3][grp].y : vw[t][3][grp].x;
+                  const uint32_t a[4] = {and_or(prmt(w0, w1, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                         and_or(prmt(w0, w1, sel_hi), 0x00FF00FFu, 0x64006400u),
+                                         and_or(prmt(w2, w3, sel_lo), 0x00FF00FFu, 0x64006400u),
+                                         and_or(prmt(w2, w3, sel_hi), 0x00FF00FFu, 0x64006400u)};
+                  mma_f16_16816(oacc[grp * 4 + jl], a, bp);
+                }
+              }
             }
           }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int h = i >> 1, e = i & 1;
-            float v = 0.f;
-#pragma unroll
-            for (int grp = 0; grp < DG; ++grp) v += ksc[t][h][grp] * (sacc[grp][i] - kq[e][grp]);
-            s[t][i] = valid[t][h] ? v : -INFINITY;
-          }
-        }
-
-        // ---- online softmax (heads 2c, 2c+1 over the 8 lanes of a column) --
-        float pr[NT][4];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float mt = fmaxf(s[0][e], s[0][2 + e]);
-#pragma unroll
-          for (int t = 1; t < NT; ++t) mt = fmaxf(mt, fmaxf(s[t][e], s[t][2 + e]));
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-          mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-          const float mnew = fmaxf(m_run[e], mt);
-          const bool none = (mnew == -INFINITY);
-          const float alpha = none ? 1.f : fast_exp2(m_run[e] - mnew);
-          float lsum = 0.f;
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            pr[t][e] = none ? 0.f : fast_exp2(s[t][e] - mnew);
-            pr[t][2 + e] = none ? 0.f : fast_exp2(s[t][2 + e] - mnew);
-            lsum += pr[t][e] + pr[t][2 + e];
-          }
-          l_run[e] = l_run[e] * alpha + lsum;
-          m_run[e] = mnew;
-#pragma unroll
-          for (int j = 0; j < DG * 4; ++j) {
-            oacc[j][e] *= alpha;
-            oacc[j][2 + e] *= alpha;
-          }
-#pragma unroll
-          for (int j = 0; j < DG; ++j) {
-            oone[j][e] *= alpha;
-            oone[j][2 + e] *= alpha;
-          }
-        }
-
-        // ---- O^T += V^T.P'^T ------------------------------------------------
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-#pragma unroll
-          for (int grp = 0; grp < DG; ++grp) {
-            const uint32_t xlo = pack_f16x2(pr[t][0] * vsc[t][0][grp], pr[t][1] * vsc[t][0][grp]);
-            const uint32_t xhi = pack_f16x2(pr[t][2] * vsc[t][1][grp], pr[t][3] * vsc[t][1][grp]);
-            const uint32_t bp[2] = {movmatrix_trans(xlo), movmatrix_trans(xhi)};
-            mma_f16_16816(oone[grp], ones, bp);
-#pragma unroll
-            for (int jl = 0; jl < 4; ++jl) {
-              const int bs = 2 * (jl & 1);
-              const uint32_t sel_lo = uint32_t(bs | (bs << 4) | ((4 + bs) << 8) | ((4 + bs) << 12));
-              const uint32_t sel_hi = sel_lo + 0x1111u;
-              const uint32_t w0 = (jl >> 1) ? vw[t][0][grp].y : vw[t][0][grp].x;
-              const uint32_t w1 = (jl >> 1) ? vw[t][1][grp].y : vw[t][1][grp].x;
-              const uint32_t w2 = (jl >> 1) ? vw[t][2][grp].y : vw[t][2][grp].x;
-              const uint32_t w3 = (jl >> 1) ? vw[t][3][grp].y : vw[t][3][grp].x;
-              const uint32_t a[4] = {and_or(prmt(w0, w1, sel_lo), 0x00FF00FFu, 0x64006400u),
-                                     and_or(prmt(w0, w1, sel_hi), 0x00FF00FFu, 0x64006400u),
-                                     and_or(prmt(w2, w3, sel_lo), 0x00FF00FFu, 0x64006400u),
-                                     and_or(prmt(w2, w3, sel_hi), 0x00FF00FFu, 0x64006400u)};
-              mma_f16_16816(oacc[grp * 4 + jl], a, bp);
-            }
-          }
-        }
-      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
-  }
 
-  // ---- merge the 4 warps through shared memory -----------------------------
-  float* sm = reinterpret_cast<float*>(attn_smem + p.ring_bytes);
-  float* sm_o = sm;               // [4][G][D]
-  float* sm_ml = sm + 4 * G * D;  // [4][G][2]
-  if (warp < 4) {
+    // ---- merge the 4 warps through shared memory (the producer warp has left)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float l = l_run[e];
@@ -862,32 +871,33 @@ __global__ void __launch_bounds__(160, 2) qkv_decode_attn_t8_kernel(const AttnPa
         }
       }
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && *abort_flag) report_timeout(nullptr);  // a page wait gave up
-  const int hq0 = hkv * G;
-  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    const int head = idx / D, d = idx % D;
-    float mstar = -INFINITY;
+    named_bar_sync(1, 128);
+    if (threadIdx.x == 0 && *abort_flag) report_timeout(nullptr);  // a page wait gave up
+    const int hq0 = hkv * G;
+    for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+      const int head = idx / D, d = idx % D;
+      float mstar = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mstar = fmaxf(mstar, sm_ml[(w * G + head) * 2]);
-    float o = 0.f, l = 0.f;
-    if (mstar != -INFINITY) {
+      for (int w = 0; w < 4; ++w) mstar = fmaxf(mstar, sm_ml[(w * G + head) * 2]);
+      float o = 0.f, l = 0.f;
+      if (mstar != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float f = exp2f(sm_ml[(w * G + head) * 2] - mstar);
-        o += f * sm_o[(w * G + head) * D + d];
-        l += f * sm_ml[(w * G + head) * 2 + 1];
+        for (int w = 0; w < 4; ++w) {
+          const float f = exp2f(sm_ml[(w * G + head) * 2] - mstar);
+          o += f * sm_o[(w * G + head) * D + d];
+          l += f * sm_ml[(w * G + head) * 2 + 1];
+        }
       }
-    }
-    const int64_t bh = int64_t(b) * p.Hq + hq0 + head;
-    if (p.n_splits == 1) {
-      p.out[bh * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
-    } else {
-      p.o_part[(bh * p.n_splits + split) * D + d] = o;
-      if (d == 0) {
-        p.ml_part[(bh * p.n_splits + split) * 2 + 0] = mstar;
-        p.ml_part[(bh * p.n_splits + split) * 2 + 1] = l;
+      const int64_t bh = int64_t(b) * p.Hq + hq0 + head;
+      if (p.n_splits == 1) {
+        p.out[bh * D + d] = __float2bfloat16_rn(l > 0.f ? o / l : 0.f);
+      } else {
+        const int split = blockIdx.x;
+        p.o_part[(bh * p.n_splits + split) * D + d] = o;
+        if (d == 0) {
+          p.ml_part[(bh * p.n_splits + split) * 2 + 0] = mstar;
+          p.ml_part[(bh * p.n_splits + split) * 2 + 1] = l;
+        }
       }
     }
   }

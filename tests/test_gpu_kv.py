@@ -158,6 +158,25 @@ def test_decode_attention_paged(dev, bits, Hq, Hkv, D):
         assert_close(to_np(out), want, what=f"attn bits={bits} splits={n_splits}")
 
 
+@pytest.mark.parametrize("B,Hkv,maxlen,page", [(40, 4, 700, 64), (64, 4, 2048, 64), (9, 8, 90, 64), (3, 4, 40, 16),
+                                               (24, 2, 1500, 128)])
+def test_decode_attention_ragged_batch(dev, B, Hkv, maxlen, page):
+    """8-bit token-row form over ragged batches: empty sequences (zero
+    output), lengths off the 16-token tiles, context splits longer than some
+    sequences, 16- to 128-token pages."""
+    rng = np.random.default_rng(B * 7 + maxlen)
+    lens = [int(v) for v in rng.integers(0, maxlen + 1, B)]
+    lens[0], lens[-1] = 0, maxlen
+    if B > 4:
+        lens[1], lens[2] = 1, 16
+    args, (q, keys, vals) = _paged_case(dev, rng, B, lens, 8 * Hkv, Hkv, 128, 8, page)
+    want, _ = attn.decode_attention(q, keys, vals)
+    for n_splits in (1, 2, None):
+        out = to_np(decode_attention(*args, bits=8, page_size=page, num_kv_heads=Hkv, n_splits=n_splits))
+        assert_close(out, want, what=f"ragged batch B={B} splits={n_splits}")
+        assert np.all(out[[i for i, n in enumerate(lens) if n == 0]] == 0)
+
+
 @pytest.mark.parametrize("bits", [4, 8])
 def test_decode_attention_256_token_pages(dev, bits):
     """Pages too large for the shared-memory page ring (256 tokens of 8-bit
@@ -176,9 +195,9 @@ def test_decode_attention_config2_shape(dev):
     rng = np.random.default_rng(2)
     for bits in (8, 4, 2):
         args, (q, keys, vals) = _paged_case(dev, rng, 16, [8192] * 16, 32, 8, 128, bits, 128)
-        out = to_np(decode_attention(*args, bits=bits, page_size=128, num_kv_heads=8))
         sel = [0, 7, 15]
         want, _ = attn.decode_attention(q[sel], [keys[i] for i in sel], [vals[i] for i in sel])
+        out = to_np(decode_attention(*args, bits=bits, page_size=128, num_kv_heads=8))
         assert_close(out[sel], want, what=f"config2 bits={bits}")
 
 
