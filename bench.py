@@ -58,7 +58,11 @@ def config_dict(args, world):
                             + ("dispatch / combine by the library's NVLink peer-memory kernels"
                                if getattr(args, "ep_exchange", "p2p") == "p2p"
                                else "NCCL all-gather dispatch / reduce-scatter combine")
-                            + f"), dp{world} attention") if world > 1 else "1 GPU"}
+                            + f"), dp{world} attention") if world > 1 else "1 GPU",
+            "expert_placement": (("balanced: each layer's experts relabelled so the ExpertShard blocks carry even "
+                                  "expected routing load (greedy longest-first)")
+                                 if getattr(args, "ep_placement", "balanced") == "balanced"
+                                 else "ExpertShard id blocks over the shuffled popularity") if world > 1 else None}
 
 
 # ---------------------------------------------------------------------------
@@ -313,7 +317,7 @@ def run_ours(args):
                           seed=1234, layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile,
                           moe_packed=not args.moe_unpacked, pdl=not args.no_pdl,
-                          moe_streamk=args.streamk)
+                          moe_streamk=args.streamk, expert_placement=args.ep_placement)
     dec.fill_random_context(args.ctx)
     torch.cuda.synchronize()
 
@@ -996,7 +1000,7 @@ def strong_scaling(args, shape, world, dev, exchange, max_ctx):
     dec = Qwen3MoeDecoder(shape, max_batch=b, max_context=max_ctx, page_size=64, device=dev, seed=1234,
                           layers=args.layers, exchange=exchange, moe_engine=args.moe_engine,
                           dense_engine=args.dense_engine, moe_tile=args.moe_tile, moe_packed=not args.moe_unpacked,
-                          pdl=not args.no_pdl, moe_streamk=args.streamk)
+                          pdl=not args.no_pdl, moe_streamk=args.streamk, expert_placement=args.ep_placement)
     dec.fill_random_context(args.ctx)
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
@@ -1180,6 +1184,9 @@ def main():
                     help="stream the experts' MLX-layout codes by 2-D TMA instead of the packed tiles")
     ap.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
                     help="decode expert-parallel exchange for N > 1: peer-memory kernels or NCCL collectives")
+    ap.add_argument("--ep-placement", default="balanced", choices=["balanced", "contiguous"],
+                    help="N > 1: relabel each layer's experts so the rank blocks carry even expected load, "
+                         "or keep the id blocks")
     ap.add_argument("--layers", type=int, default=48,
                     help="decoder depth; anything but 48 is a profiling case, not a bench line")
     ap.add_argument("--profile-window", action="store_true",

@@ -43,7 +43,7 @@ import torch
 
 from . import _capi
 from ._capi import call, ptr
-from .distributed_experts import ExpertShard
+from .distributed_experts import ExpertShard, balanced_placement
 from .ep import ExpertParallelMoE
 from .quantized_kv_cache import packed_len, pick_splits
 
@@ -173,7 +173,7 @@ class Qwen3MoeDecoder:
     def __init__(self, shape: Qwen3MoeShape, max_batch: int, max_context: int, page_size: int = 64,
                  device="cuda:0", seed: int = 0, layers=None, moe_engine: str = "auto", exchange=None,
                  dense_engine: str = "auto", moe_tile: int = 16, moe_packed: bool = True, pdl: bool = True,
-                 moe_streamk: bool = False):
+                 moe_streamk: bool = False, expert_placement: str = "balanced"):
         self.s = s = shape
         self.pdl = bool(pdl)
         self.dev = dev = torch.device(device)
@@ -205,8 +205,19 @@ class Qwen3MoeDecoder:
         # the Zipf(s) selection frequencies, rank perm[e] for expert e
         zbias = torch.from_numpy(np.array(zipf_router_bias(E, s.top_k, s.zipf_s, s.router_tau))).to(dev)
         wr_std = s.router_tau / math.sqrt(H * 1.01)
+        if expert_placement not in ("balanced", "contiguous"):
+            raise ValueError("expert_placement is 'balanced' or 'contiguous'")
+        # expert parallelism: "balanced" relabels each layer's experts so the
+        # ExpertShard blocks carry even expected loads (balanced_placement over
+        # the experts' selection frequencies); "contiguous" keeps the shuffled
+        # popularity of the single-GPU model on the id blocks as they are
+        self.expert_placement = expert_placement if self.world > 1 else "contiguous"
+        sel_freq = np.array(zipf_selection_frequency(E, s.top_k, s.zipf_s))
         for _ in range(self.L):
             perm = torch.randperm(E, device=dev, generator=gen)
+            if self.expert_placement == "balanced":
+                order = balanced_placement(sel_freq[perm.cpu().numpy()], self.world)
+                perm = perm[torch.tensor(order, device=dev)]
             self.layers.append({
                 "in_norm": norm_w(H), "post_norm": norm_w(H), "q_norm": norm_w(D), "k_norm": norm_w(D),
                 "wqkv": random_qweight((self.qkv_rows, H), bits, gs, dev, gen),

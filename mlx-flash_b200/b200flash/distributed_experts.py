@@ -110,3 +110,35 @@ def plan_expert_distribution(num_experts: int, num_layers: int, world_size: int,
         "comm_latency_ms": round(latency_ms, 3),
         "nodes": nodes,
     }
+
+
+def balanced_placement(loads, world_size: int) -> list:
+    """Expert placement that evens the expected load of the contiguous
+    ExpertShard blocks: returns ``order`` with ``order[s]`` = the expert
+    stored at position ``s``, so rank ``r`` holds the experts at positions
+    ``[r*floor(E/W), ...)`` exactly as ``ExpertShard`` partitions ids.
+
+    ``loads[e]`` is expert e's expected load (e.g. its routing frequency).
+    Longest first: experts in decreasing load, each to the rank with the
+    least load so far among those whose block still has room (blocks keep
+    the ExpertShard sizes; ties go to the lower rank), so the rank holding
+    the hottest expert fills up with the coldest ones.  The reference
+    partitions by id only (distributed_experts.py:36-80); relabelling experts
+    by this order (router columns and expert weights together) leaves the
+    model's outputs unchanged and only moves work between ranks.
+    """
+    E = len(loads)
+    W = int(world_size)
+    if W <= 1 or E < W:
+        return list(range(E))
+    per = E // W
+    room = [per] * W
+    room[-1] += E - per * W
+    total = [0.0] * W
+    blocks = [[] for _ in range(W)]
+    for e in sorted(range(E), key=lambda e: (-float(loads[e]), e)):
+        r = min((r for r in range(W) if room[r] > 0), key=lambda r: (total[r], r))
+        blocks[r].append(e)
+        total[r] += float(loads[e])
+        room[r] -= 1
+    return [e for b in blocks for e in b]

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from b200flash.distributed_experts import ExpertShard
+from b200flash.distributed_experts import ExpertShard, balanced_placement
 from b200flash.ep import RoutingSegment
 
 
@@ -18,6 +18,28 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("E,W", [(128, 1), (128, 2), (128, 4), (128, 8), (60, 7), (5, 8)])
+def test_balanced_placement(E, W):
+    """Expert placement over the ExpertShard blocks: a permutation of the
+    experts whose blocks keep the ExpertShard sizes (the last rank takes the
+    remainder), each rank's expected load within the largest single load of
+    the mean, and a load spread no wider than the id blocks' under Zipf
+    popularity; one rank (or fewer experts than ranks) keeps the identity."""
+    rng = np.random.default_rng(E + W)
+    zipf = np.arange(1, E + 1, dtype=np.float64) ** -1.1
+    loads = zipf[rng.permutation(E)]  # popularity shuffled over the ids, as the decoder's router bias
+    order = balanced_placement(loads, W)
+    assert sorted(order) == list(range(E))
+    if W == 1 or E < W:
+        assert order == list(range(E))
+        return
+    blocks = [ExpertShard(rank=r, world_size=W, total_experts=E).owned_experts for r in range(W)]
+    per_rank = np.array([sum(loads[order[s]] for s in b) for b in blocks])
+    assert per_rank.max() - per_rank.mean() <= loads.max() + 1e-12
+    ids = np.array([sum(loads[s] for s in b) for b in blocks])
+    assert per_rank.max() - per_rank.min() <= ids.max() - ids.min()
 
 
 def test_routing_segment_layout():
